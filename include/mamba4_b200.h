@@ -1,0 +1,153 @@
+/*
+ * mamba4_b200 - C ABI of the B200 (sm_100a) FlashMamba hot path.
+ *
+ * Two operators of tasmaikeni13/mamba4's `lm/kernels` surface, each a
+ * forward/backward pair:
+ *
+ *   - the selective conjugate memory read
+ *       (reference: selective_memory_fused, lm/kernels/mamba4_fused.py:372-454,
+ *        contract of selective_gaussian_memory, lm/kernels/mamba4.py:228-338)
+ *   - the Mamba-3 SISO chunked scan in the projection layout
+ *       (reference: mamba3_fused, lm/kernels/flashmamba.py:1114-1162,
+ *        fused_scan custom_vjp, :859-1102)
+ *
+ * Conventions
+ *   - All pointers are device pointers (cudaMalloc'd or framework-owned).
+ *     The library never allocates: the caller sizes residual and workspace
+ *     buffers with the *_bytes queries and passes them in.
+ *   - `stream` is a cudaStream_t passed as void*; every call is asynchronous
+ *     on it and reentrant (no global mutable state).
+ *   - Tensors are dense, row-major, in the layouts stated per argument.
+ *   - Every entry point returns an M4Status; nonzero means nothing was
+ *     launched (argument errors) or a launch failed (M4_ERR_LAUNCH).
+ *     m4_status_string() names a code. No entry point traps or asserts.
+ *   - Results are deterministic: fixed reduction orders, no float atomics.
+ */
+#ifndef MAMBA4_B200_H
+#define MAMBA4_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  M4_OK = 0,
+  M4_ERR_DIMS = 1,        /* a dimension is non-positive or inconsistent */
+  M4_ERR_UNSUPPORTED = 2, /* a dimension this build does not implement */
+  M4_ERR_NULL = 3,        /* a required pointer is NULL */
+  M4_ERR_ALIGN = 4,       /* a pointer is not 16-byte aligned */
+  M4_ERR_LAUNCH = 5,      /* a CUDA launch reported an error */
+  M4_ERR_WORKSPACE = 6    /* residual/workspace buffer too small */
+} M4Status;
+
+/* Memory-read problem size. key_dim must be 64 and value_dim 64 or 128
+ * (the host adapter pads smaller dimensions with an identity block, as the
+ * reference's batched_solve pads to 8, lm/kernels/mamba4_fused.py:289-297). */
+typedef struct {
+  int batch;      /* B */
+  int time;       /* T, any length >= 1 (padded internally) */
+  int heads;      /* H */
+  int key_dim;    /* D = 64 */
+  int value_dim;  /* P = 64 or 128 */
+} M4MemDims;
+
+/* Bytes of the forward residual (stored Cholesky factors, solutions and
+ * chunk-start statistics) that m4_memread_bwd consumes. The reference keeps
+ * the same residuals under the remat name "memory_solve"
+ * (lm/kernels/mamba4_fused.py:329-337). */
+size_t m4_memread_residual_bytes(const M4MemDims* dims);
+
+/* Bytes of scratch the backward needs. */
+size_t m4_memread_workspace_bytes(const M4MemDims* dims);
+
+/* Forward read. Replaces selective_memory_fused's forward
+ * (lm/kernels/mamba4_fused.py:372-454; custom-VJP forward :329-337).
+ *   keys, queries [B,T,H,D]; values [B,T,H,P]; beta, log_decay [B,T,H];
+ *   floor [H,D]; init_evidence [B,H,D,D] and init_cross [B,H,P,D] or NULL
+ *   (zero state, lm/kernels/mamba4.py:221-225).
+ * Outputs: output [B,T,H,P], variance [B,T,H], final_evidence [B,H,D,D],
+ *   final_cross [B,H,P,D]; residual as sized above. */
+int m4_memread_fwd(const M4MemDims* dims, const float* keys, const float* values,
+                   const float* queries, const float* beta, const float* log_decay,
+                   const float* floor, const float* init_evidence,
+                   const float* init_cross, float* output, float* variance,
+                   float* final_evidence, float* final_cross, void* residual,
+                   size_t residual_bytes, void* stream);
+
+/* Backward of the read. Replaces _chunk_solve_backward
+ * (lm/kernels/mamba4_fused.py:340-366) together with the JAX autodiff of the
+ * surrounding chunk algebra (:402-447). Inputs as m4_memread_fwd plus the
+ * residual it wrote and the cotangents d_output [B,T,H,P],
+ * d_variance [B,T,H], d_final_evidence [B,H,D,D] / d_final_cross [B,H,P,D]
+ * (either may be NULL = zero). Writes every input gradient; d_init_evidence
+ * and d_init_cross may be NULL when no initial state is differentiated. */
+int m4_memread_bwd(const M4MemDims* dims, const float* keys, const float* values,
+                   const float* queries, const float* beta, const float* log_decay,
+                   const float* floor, const float* init_evidence,
+                   const float* init_cross, const void* residual,
+                   size_t residual_bytes, const float* d_output,
+                   const float* d_variance, const float* d_final_evidence,
+                   const float* d_final_cross, float* d_keys, float* d_values,
+                   float* d_queries, float* d_beta, float* d_log_decay,
+                   float* d_floor, float* d_init_evidence, float* d_init_cross,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scan problem size (projection layout of mamba3_fused). */
+typedef struct {
+  int batch;        /* B */
+  int time;         /* T, any length >= 1 */
+  int heads;        /* H */
+  int head_dim;     /* P = 64 */
+  int state_dim;    /* N = 64 */
+  int angle_count;  /* A <= N/2 rotation pairs */
+  int chunk;        /* chunk length: 64 */
+  int bf16;         /* 1: c, b, x, y, d_y, dc, db, dx are bfloat16; 0: float32 */
+  int per_head;     /* 1: q/k [B,T,H,N] and angles [B,T,H,A] per head
+                       (mamba3_flash_heads, lm/kernels/flashmamba.py:467-502);
+                       0: shared c/b [B,T,N] and angles [B,T,A] (mamba3_fused) */
+} M4ScanDims;
+
+size_t m4_scan_residual_bytes(const M4ScanDims* dims);
+size_t m4_scan_workspace_bytes(const M4ScanDims* dims);
+
+/* Forward scan. Replaces mamba3_fused's forward
+ * (lm/kernels/flashmamba.py:1114-1162 -> _fused_forward_pass :901-959).
+ *   c (queries C), b (keys B): [B,T,N] (per_head: [B,T,H,N]); x [B,T,H*P];
+ *   adt, dt, trap_logits [B,T,H] float32; angles [B,T,A] (per_head [B,T,H,A])
+ *   float32 rates; q_bias, k_bias [H,N] float32 (may be NULL = zero).
+ * Outputs: y [B,T,H*P] (dtype of x), final_state [B,H,N,P] float32;
+ *   residual: chunk-start states and phases (remat name "ssd_scan"). */
+int m4_scan_fwd(const M4ScanDims* dims, const void* c, const void* b, const void* x,
+                const float* adt, const float* dt, const float* trap_logits,
+                const float* angles, const float* q_bias, const float* k_bias,
+                void* y, float* final_state, void* residual, size_t residual_bytes,
+                void* stream);
+
+/* Backward scan. Replaces _fused_backward (lm/kernels/flashmamba.py:996-1099)
+ * and the JAX autodiff of mamba3_fused's preprocessing (:1142-1147,
+ * angle_rates :1105-1111). d_final may be NULL (zero). Writes dc, db
+ * (dtype of c/b; shared layouts sum over heads in a fixed order), dx,
+ * d_adt, d_dt, d_trap_logits [B,T,H], d_angles (shape of angles),
+ * d_q_bias, d_k_bias [H,N] (may be NULL). */
+int m4_scan_bwd(const M4ScanDims* dims, const void* c, const void* b, const void* x,
+                const float* adt, const float* dt, const float* trap_logits,
+                const float* angles, const float* q_bias, const float* k_bias,
+                const void* residual, size_t residual_bytes, const void* d_y,
+                const float* d_final, void* dc, void* db, void* dx, float* d_adt,
+                float* d_dt, float* d_trap_logits, float* d_angles,
+                float* d_q_bias, float* d_k_bias, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+/* Name of a status code (static string). */
+const char* m4_status_string(int status);
+
+/* Library version string, e.g. "mamba4_b200 0.1 sm_100a". */
+const char* m4_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA4_B200_H */

@@ -1,0 +1,20 @@
+"""mamba4_b200: the Mamba 4 FlashMamba hot path, native on B200 (sm_100a).
+
+Operators (reference `lm/kernels` surface):
+  memory:      selective_memory_fused, selective_gaussian_memory,
+               SelectiveState, SelectiveResult, selective_initial_state
+  flashmamba:  mamba3_fused, mamba3_flash, mamba3_flash_heads, angle_rates
+Compute runs in the in-tree CUDA library `libmamba4_b200.so` (C ABI in
+include/mamba4_b200.h); importing the package does not need a GPU.
+"""
+
+from .memory import (  # noqa: F401
+    SelectiveResult,
+    SelectiveState,
+    selective_gaussian_memory,
+    selective_initial_state,
+    selective_memory_fused,
+)
+from .flashmamba import angle_rates, mamba3_flash, mamba3_flash_heads, mamba3_fused  # noqa: F401
+
+__version__ = "0.1"

@@ -1,0 +1,82 @@
+"""ctypes binding of the C ABI declared in include/mamba4_b200.h.
+
+The shared library is built in-tree by `mamba4_b200.build`. There is no
+fallback: if the library is missing or a call returns a nonzero status, the
+caller gets an exception.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIBRARY_PATH = _HERE / "libmamba4_b200.so"
+
+_c_int = ctypes.c_int
+_p = ctypes.c_void_p
+_size = ctypes.c_size_t
+
+
+class MemDims(ctypes.Structure):
+    """M4MemDims."""
+
+    _fields_ = [("batch", _c_int), ("time", _c_int), ("heads", _c_int),
+                ("key_dim", _c_int), ("value_dim", _c_int)]
+
+
+class ScanDims(ctypes.Structure):
+    """M4ScanDims."""
+
+    _fields_ = [("batch", _c_int), ("time", _c_int), ("heads", _c_int),
+                ("head_dim", _c_int), ("state_dim", _c_int), ("angle_count", _c_int),
+                ("chunk", _c_int), ("bf16", _c_int), ("per_head", _c_int)]
+
+
+# Exported symbols and their signatures (argtypes, restype).
+SIGNATURES = {
+    "m4_memread_residual_bytes": ([ctypes.POINTER(MemDims)], _size),
+    "m4_memread_workspace_bytes": ([ctypes.POINTER(MemDims)], _size),
+    "m4_memread_fwd": ([ctypes.POINTER(MemDims)] + [_p] * 12 + [_p, _size, _p], _c_int),
+    "m4_memread_bwd": ([ctypes.POINTER(MemDims)] + [_p] * 9 + [_size] + [_p] * 12
+                       + [_p, _size, _p], _c_int),
+    "m4_scan_residual_bytes": ([ctypes.POINTER(ScanDims)], _size),
+    "m4_scan_workspace_bytes": ([ctypes.POINTER(ScanDims)], _size),
+    "m4_scan_fwd": ([ctypes.POINTER(ScanDims)] + [_p] * 11 + [_p, _size, _p], _c_int),
+    "m4_scan_bwd": ([ctypes.POINTER(ScanDims)] + [_p] * 10 + [_size] + [_p] * 11
+                    + [_p, _size, _p], _c_int),
+    "m4_status_string": ([_c_int], ctypes.c_char_p),
+    "m4_version": ([], ctypes.c_char_p),
+}
+
+_lib = None
+
+
+def load():
+    """Load (once) and return the ctypes library handle; raise if absent."""
+    global _lib
+    if _lib is None:
+        if not LIBRARY_PATH.exists():
+            raise RuntimeError(
+                f"mamba4_b200 CUDA library not found at {LIBRARY_PATH}; build it with "
+                "`python -c 'import __graft_entry__ as g; g.build()'` or "
+                "`python -m mamba4_b200.build`"
+            )
+        lib = ctypes.CDLL(str(LIBRARY_PATH))
+        for name, (argtypes, restype) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        message = load().m4_status_string(status).decode()
+        raise RuntimeError(f"{what} failed: {message} (status {status})")
+
+
+def ptr(tensor) -> int | None:
+    """Device pointer of a tensor (None -> NULL)."""
+    return None if tensor is None else tensor.data_ptr()

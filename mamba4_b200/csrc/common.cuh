@@ -1,0 +1,58 @@
+// Shared device helpers for the mamba4_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/mamba4_b200.h"
+
+#define M4_DEV __device__ __forceinline__
+
+namespace m4 {
+
+constexpr int kWarp = 32;
+
+M4_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Inclusive prefix sum over a warp (Kogge-Stone).
+M4_DEV float warp_inclusive_scan(float v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    float n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
+M4_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+M4_DEV void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+// Streaming (evict-first) 128-bit global store for write-once residuals.
+M4_DEV void st4_stream(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
+
+// Load a scalar that may be float or bfloat16.
+template <typename T> M4_DEV float to_f(T v);
+template <> M4_DEV float to_f<float>(float v) { return v; }
+template <> M4_DEV float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> M4_DEV T from_f(float v);
+template <> M4_DEV float from_f<float>(float v) { return v; }
+template <> M4_DEV __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Round to the model dtype and back (identity for float).
+template <typename T> M4_DEV float round_to(float v) { return to_f<T>(from_f<T>(v)); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+inline int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? M4_OK : M4_ERR_LAUNCH;
+}
+
+}  // namespace m4

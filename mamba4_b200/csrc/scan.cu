@@ -1,0 +1,841 @@
+// Mamba-3 SISO chunked scan (rotation, phase and trapezoidal weights fused),
+// forward and backward, for sm_100a.
+//
+// Reference operator: mamba3_fused (lm/kernels/flashmamba.py:1114-1162) ->
+// fused_scan custom VJP (:859-1102) with kernels _fused_forward_kernel
+// (:589-660) and _fused_backward_kernel (:663-786). Per head h and chunk of
+// `chunk` tokens, with p = chunk-local prefix of adt, the phase
+// theta_t = phase0 + sum_{s<=t} rate_s dt_s, Q/K = rotated, biased C/B:
+//   W[t,s] = e^(p_t-p_s) scale_s (s < t), gamma_t (s = t)
+//   y      = ((Q K^T) o W) V + e^(p_t) Q state
+//   state  = e^(p_L) state + K^T (V o scale o tail)
+// Model-dtype (bf16) rounding points follow the reference kernel: bias add,
+// rotation, masked scores, carried-state read, weighted values, output, and
+// in the backward the score/value cotangent products (:734-751).
+//
+// This version: one CTA (4 warps) per (batch, head), chunks in sequence, the
+// chunk products on bf16 mma.sync tensor-core tiles with fp32 accumulation
+// (fp32 inputs use an exact CUDA-core path with the same fragment ownership).
+#include "common.cuh"
+
+namespace m4 {
+namespace scan {
+
+constexpr int C = 64;      // chunk length
+constexpr int NS = 64;     // state dim N
+constexpr int HP = 64;     // head dim P
+constexpr int LDS = 68;    // smem tile stride (floats)
+constexpr int THREADS = 128;
+
+M4_DEV uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+M4_DEV void mma16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// Warp tile: rows row0 + g and row0 + g + 8 (g = lane/4), columns
+// nt*8 + 2c, 2c+1 (c = lane%4) for nt < 8: acc[nt][0..1] row g, [2..3] row g+8.
+// C[16 x 64] += A[16 x K] B[K x 64] with element accessors fa(row, k), fb(k, col).
+template <bool BF, int K, class FA, class FB>
+M4_DEV void warp_gemm(float (&acc)[8][4], int row0, FA fa, FB fb) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  if constexpr (BF) {
+#pragma unroll
+    for (int k0 = 0; k0 < K; k0 += 16) {
+      uint32_t a[4];
+      a[0] = pack_bf16(fa(row0 + g, k0 + 2 * c), fa(row0 + g, k0 + 2 * c + 1));
+      a[1] = pack_bf16(fa(row0 + g + 8, k0 + 2 * c), fa(row0 + g + 8, k0 + 2 * c + 1));
+      a[2] = pack_bf16(fa(row0 + g, k0 + 2 * c + 8), fa(row0 + g, k0 + 2 * c + 9));
+      a[3] = pack_bf16(fa(row0 + g + 8, k0 + 2 * c + 8), fa(row0 + g + 8, k0 + 2 * c + 9));
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        uint32_t b[2];
+        b[0] = pack_bf16(fb(k0 + 2 * c, nt * 8 + g), fb(k0 + 2 * c + 1, nt * 8 + g));
+        b[1] = pack_bf16(fb(k0 + 2 * c + 8, nt * 8 + g), fb(k0 + 2 * c + 9, nt * 8 + g));
+        mma16816(acc[nt], a, b);
+      }
+    }
+  } else {
+#pragma unroll 4
+    for (int k = 0; k < K; ++k) {
+      const float a0 = fa(row0 + g, k), a1 = fa(row0 + g + 8, k);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float b0 = fb(k, nt * 8 + 2 * c), b1 = fb(k, nt * 8 + 2 * c + 1);
+        acc[nt][0] = fmaf(a0, b0, acc[nt][0]);
+        acc[nt][1] = fmaf(a0, b1, acc[nt][1]);
+        acc[nt][2] = fmaf(a1, b0, acc[nt][2]);
+        acc[nt][3] = fmaf(a1, b1, acc[nt][3]);
+      }
+    }
+  }
+}
+
+M4_DEV void zero8(float (&acc)[8][4]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+}
+
+// Visit the warp tile's elements: f(row, col, value).
+template <class F>
+M4_DEV void for_tile(const float (&acc)[8][4], int row0, F f) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    f(row0 + g, nt * 8 + 2 * c, acc[nt][0]);
+    f(row0 + g, nt * 8 + 2 * c + 1, acc[nt][1]);
+    f(row0 + g + 8, nt * 8 + 2 * c, acc[nt][2]);
+    f(row0 + g + 8, nt * 8 + 2 * c + 1, acc[nt][3]);
+  }
+}
+
+struct Dims {
+  int B, T, H, A, nch;
+  bool per_head;
+};
+
+// Per-token chunk scalars shared by the forward and backward kernels.
+struct Rows {
+  float p[C], gam[C], scl[C], tail[C], dt[C], trap[C];
+};
+
+// Fill Rows for chunk t0 of (b, h) (threads 0..63; warp 0 does the prefix).
+M4_DEV void chunk_rows(const Dims& d, int b, int h, int t0, const float* adt, const float* dt,
+                       const float* trap_logits, Rows& r, float* scratch) {
+  const int tid = threadIdx.x;
+  if (tid < C) {
+    const int t = t0 + tid;
+    const bool live = t < d.T;
+    const size_t i = (size_t(b) * d.T + t) * d.H + h;
+    const float dtv = live ? dt[i] : 0.f;
+    const float tr = live ? 1.f / (1.f + expf(-trap_logits[i])) : 0.f;
+    float next = 0.f;
+    if (t + 1 < d.T) {
+      const size_t j = (size_t(b) * d.T + t + 1) * d.H + h;
+      const float trn = 1.f / (1.f + expf(-trap_logits[j]));
+      next = dt[j] * (1.f - trn);
+    }
+    r.dt[tid] = dtv;
+    r.trap[tid] = tr;
+    r.gam[tid] = dtv * tr;
+    r.scl[tid] = dtv * tr + next;
+    scratch[tid] = live ? adt[i] : 0.f;
+  }
+  __syncthreads();
+  if (tid < 32) {
+    const float v0 = warp_inclusive_scan(scratch[tid], tid);
+    const float tot = __shfl_sync(0xffffffffu, v0, 31);
+    const float v1 = warp_inclusive_scan(scratch[32 + tid], tid) + tot;
+    r.p[tid] = v0;
+    r.p[32 + tid] = v1;
+  }
+  __syncthreads();
+  if (tid < C) r.tail[tid] = expf(r.p[C - 1] - r.p[tid]);
+}
+
+// Phase theta[t][i] = phase0[i] + sum_{s<=t} rate_s[i] dt_s for pairs i < A.
+M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles, const Rows& r,
+                        const float* phase0, float* theta) {
+  const int tid = threadIdx.x;
+  if (tid < d.A) {
+    float acc = phase0[tid];
+    for (int tt = 0; tt < C; ++tt) {
+      const int t = t0 + tt;
+      float rate = 0.f;
+      if (t < d.T)
+        rate = d.per_head ? angles[((size_t(b) * d.T + t) * d.H + h) * d.A + tid]
+                          : angles[(size_t(b) * d.T + t) * d.A + tid];
+      acc = fmaf(rate, r.dt[tt], acc);
+      theta[tt * 33 + tid] = acc;
+    }
+  }
+}
+
+// Build rotated, rounded Q and K tiles (and optionally the fp32 rotated
+// values and cos/sin for the backward).
+template <typename T>
+M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const T* cq, const T* bk, const float* qb,
+                     const float* kb, const float* theta, float* Qs, float* Ks, float* Qf, float* Kf,
+                     float* cosv, float* sinv) {
+  for (int idx = threadIdx.x; idx < C * (NS / 2); idx += THREADS) {
+    const int tt = idx / (NS / 2), i = idx % (NS / 2), t = t0 + tt;
+    const int n0 = 2 * i, n1 = 2 * i + 1;
+    float c0 = 0.f, c1 = 0.f, b0 = 0.f, b1 = 0.f;
+    if (t < d.T) {
+      const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * NS : (size_t(b) * d.T + t) * NS;
+      c0 = to_f(cq[base + n0]); c1 = to_f(cq[base + n1]);
+      b0 = to_f(bk[base + n0]); b1 = to_f(bk[base + n1]);
+    }
+    const float q0 = round_to<T>(c0 + (qb ? qb[h * NS + n0] : 0.f));
+    const float q1 = round_to<T>(c1 + (qb ? qb[h * NS + n1] : 0.f));
+    const float k0 = round_to<T>(b0 + (kb ? kb[h * NS + n0] : 0.f));
+    const float k1 = round_to<T>(b1 + (kb ? kb[h * NS + n1] : 0.f));
+    float cs = 1.f, sn = 0.f;
+    if (i < d.A) sincosf(theta[tt * 33 + i], &sn, &cs);
+    const float qr0 = q0 * cs - q1 * sn, qr1 = q1 * cs + q0 * sn;
+    const float kr0 = k0 * cs - k1 * sn, kr1 = k1 * cs + k0 * sn;
+    Qs[tt * LDS + n0] = round_to<T>(qr0);
+    Qs[tt * LDS + n1] = round_to<T>(qr1);
+    Ks[tt * LDS + n0] = round_to<T>(kr0);
+    Ks[tt * LDS + n1] = round_to<T>(kr1);
+    if (Qf) {
+      Qf[tt * LDS + n0] = qr0; Qf[tt * LDS + n1] = qr1;
+      Kf[tt * LDS + n0] = kr0; Kf[tt * LDS + n1] = kr1;
+      cosv[tt * 33 + i] = cs; sinv[tt * 33 + i] = sn;
+    }
+  }
+}
+
+template <typename T>
+M4_DEV void load_values(const Dims& d, int b, int h, int t0, const T* x, float* Vs) {
+  for (int idx = threadIdx.x; idx < C * HP; idx += THREADS) {
+    const int tt = idx / HP, p = idx % HP, t = t0 + tt;
+    Vs[tt * LDS + p] = t < d.T ? to_f(x[(size_t(b) * d.T + t) * d.H * HP + h * HP + p]) : 0.f;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Forward.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(THREADS) fwd_kernel(
+    Dims d, const T* __restrict__ cq, const T* __restrict__ bk, const T* __restrict__ x,
+    const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
+    const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
+    T* __restrict__ y, float* __restrict__ final_state, float* __restrict__ starts,
+    float* __restrict__ phases) {
+  constexpr bool BF = sizeof(T) == 2;
+  extern __shared__ __align__(16) float sh[];
+  float* Qs = sh;
+  float* Ks = Qs + C * LDS;
+  float* Vs = Ks + C * LDS;
+  float* Ms = Vs + C * LDS;
+  float* St = Ms + C * LDS;           // [N][P] fp32 state
+  float* theta = St + NS * LDS;       // [C][33]
+  float* phase = theta + C * 33;      // [32]
+  float* scratch = phase + 32;        // [64]
+  Rows& r = *reinterpret_cast<Rows*>(scratch + C);
+  const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row0 = warp * 16;
+  for (int i = tid; i < NS * LDS; i += THREADS) St[i] = 0.f;
+  if (tid < 32) phase[tid] = 0.f;
+  __syncthreads();
+  for (int ch = 0; ch < d.nch; ++ch) {
+    const int t0 = ch * C;
+    // Residuals: chunk-start state and phase.
+    {
+      float* sd = starts + (size_t(bh) * d.nch + ch) * NS * HP;
+      for (int i = tid; i < NS * HP; i += THREADS) sd[i] = St[(i / HP) * LDS + i % HP];
+      if (tid < 32) phases[(size_t(bh) * d.nch + ch) * 32 + tid] = phase[tid];
+    }
+    chunk_rows(d, b, h, t0, adt, dt, trap_logits, r, scratch);
+    __syncthreads();
+    chunk_theta(d, b, h, t0, angles, r, phase, theta);
+    __syncthreads();
+    build_qk<T>(d, b, h, t0, cq, bk, qb, kb, theta, Qs, Ks, nullptr, nullptr, nullptr, nullptr);
+    load_values<T>(d, b, h, t0, x, Vs);
+    if (tid < d.A) phase[tid] = theta[(C - 1) * 33 + tid];
+    __syncthreads();
+    // Masked, weighted scores.
+    {
+      float acc[8][4];
+      zero8(acc);
+      warp_gemm<BF, NS>(acc, row0, [&](int i, int k) { return Qs[i * LDS + k]; },
+                        [&](int k, int j) { return Ks[j * LDS + k]; });
+      for_tile(acc, row0, [&](int t, int s, float v) {
+        float w = 0.f;
+        if (s < t) w = expf(r.p[t] - r.p[s]) * r.scl[s];
+        else if (s == t) w = r.gam[t];
+        Ms[t * LDS + s] = round_to<T>(v * w);
+      });
+    }
+    __syncthreads();
+    // y = mixed V + e^p Q state.
+    {
+      float acc[8][4], inh[8][4];
+      zero8(acc);
+      zero8(inh);
+      warp_gemm<BF, C>(acc, row0, [&](int i, int k) { return Ms[i * LDS + k]; },
+                       [&](int k, int j) { return Vs[k * LDS + j]; });
+      warp_gemm<BF, NS>(inh, row0, [&](int i, int k) { return Qs[i * LDS + k]; },
+                        [&](int k, int j) { return round_to<T>(St[k * LDS + j]); });
+      const int lane = tid & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int tt = row0 + g + 8 * half, t = t0 + tt;
+        if (t >= d.T) continue;
+        const float e = expf(r.p[tt]);
+        T* yrow = y + (size_t(b) * d.T + t) * d.H * HP + h * HP;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int col = nt * 8 + 2 * c;
+          yrow[col] = from_f<T>(fmaf(e, inh[nt][2 * half], acc[nt][2 * half]));
+          yrow[col + 1] = from_f<T>(fmaf(e, inh[nt][2 * half + 1], acc[nt][2 * half + 1]));
+        }
+      }
+    }
+    __syncthreads();
+    // state = e^(p_L) state + K^T (V o scale o tail)
+    {
+      float acc[8][4];
+      zero8(acc);
+      warp_gemm<BF, C>(acc, row0, [&](int n, int t) { return Ks[t * LDS + n]; },
+                       [&](int t, int p) { return round_to<T>(Vs[t * LDS + p] * (r.scl[t] * r.tail[t])); });
+      const float end = expf(r.p[C - 1]);
+      for_tile(acc, row0, [&](int n, int p, float v) { St[n * LDS + p] = fmaf(end, St[n * LDS + p], v); });
+    }
+    __syncthreads();
+  }
+  float* fd = final_state + size_t(bh) * NS * HP;
+  for (int i = tid; i < NS * HP; i += THREADS) fd[i] = St[(i / HP) * LDS + i % HP];
+}
+
+// ---------------------------------------------------------------------------
+// Backward: reverse chunks, state cotangent carried in shared memory.
+// Per-head partial outputs go to workspace; head/batch reductions and the
+// trapezoid/gate chain rule run in small follow-up kernels.
+// ---------------------------------------------------------------------------
+struct BwdOut {
+  float* dq;      // [B,T,H,N] rotation-backed query gradient (per head)
+  float* dk;      // [B,T,H,N]
+  float* drate;   // [B,T,H,A] angle-rate gradient (per head)
+  float* dgam;    // [B,T,H] d gamma
+  float* dscl;    // [B,T,H] d scale
+  float* dlog;    // [B,T,H] d adt
+  float* ddtp;    // [B,T,H] d dt through the phase
+  float* dqb;     // [B,H,N] bias partials
+  float* dkb;     // [B,H,N]
+};
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS) bwd_kernel(
+    Dims d, const T* __restrict__ cq, const T* __restrict__ bk, const T* __restrict__ x,
+    const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
+    const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
+    const float* __restrict__ starts, const float* __restrict__ phases, const T* __restrict__ dy,
+    const float* __restrict__ d_final, T* __restrict__ dx, BwdOut o) {
+  constexpr bool BF = sizeof(T) == 2;
+  extern __shared__ __align__(16) float sh[];
+  float* Qs = sh;                     // rounded rotated queries
+  float* Ks = Qs + C * LDS;
+  float* Vs = Ks + C * LDS;
+  float* Dy = Vs + C * LDS;           // dY (model dtype values)
+  float* Sc = Dy + C * LDS;           // scores  Q K^T
+  float* Dm = Sc + C * LDS;           // d_mixed dY V^T
+  float* St = Dm + C * LDS;           // chunk-start state [N][P]
+  float* Cy = St + NS * LDS;          // carry: cotangent of chunk-end state [N][P]
+  float* Qf = Cy + NS * LDS;          // fp32 rotated (pre-rounding) queries
+  float* Kf = Qf + C * LDS;
+  float* theta = Kf + C * LDS;        // [C][33]
+  float* cosv = theta + C * 33;       // [C][33]
+  float* sinv = cosv + C * 33;        // [C][33]
+  float* later = sinv + C * 33;       // [32] phase-gradient carry per pair
+  float* scratch = later + 32;        // [64]
+  float* vec = scratch + C;           // [8][64] per-token accumulators
+  Rows& r = *reinterpret_cast<Rows*>(vec + 8 * C);
+  float* dq_t = Qf;                   // reuse after use: dQ tile
+  float* dk_t = Kf;                   // dK tile
+  const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = warp * 16;
+  for (int i = tid; i < NS * HP; i += THREADS)
+    Cy[(i / HP) * LDS + i % HP] = d_final ? d_final[size_t(bh) * NS * HP + i] : 0.f;
+  if (tid < 32) later[tid] = 0.f;
+  float qbs = 0.f, kbs = 0.f;  // bias partial sums for column tid (tid < N)
+  __syncthreads();
+  for (int ch = d.nch - 1; ch >= 0; --ch) {
+    const int t0 = ch * C;
+    chunk_rows(d, b, h, t0, adt, dt, trap_logits, r, scratch);
+    __syncthreads();
+    chunk_theta(d, b, h, t0, angles, r, phases + (size_t(bh) * d.nch + ch) * 32, theta);
+    {
+      const float* sd = starts + (size_t(bh) * d.nch + ch) * NS * HP;
+      for (int i = tid; i < NS * HP; i += THREADS) St[(i / HP) * LDS + i % HP] = sd[i];
+    }
+    __syncthreads();
+    build_qk<T>(d, b, h, t0, cq, bk, qb, kb, theta, Qs, Ks, Qf, Kf, cosv, sinv);
+    load_values<T>(d, b, h, t0, x, Vs);
+    load_values<T>(d, b, h, t0, dy, Dy);
+    for (int i = tid; i < 8 * C; i += THREADS) vec[i] = 0.f;
+    __syncthreads();
+    // Scores and d_mixed.
+    {
+      float acc[8][4];
+      zero8(acc);
+      warp_gemm<BF, NS>(acc, row0, [&](int i, int k) { return Qs[i * LDS + k]; },
+                        [&](int k, int j) { return Ks[j * LDS + k]; });
+      for_tile(acc, row0, [&](int t, int s, float v) { Sc[t * LDS + s] = v; });
+      zero8(acc);
+      warp_gemm<BF, HP>(acc, row0, [&](int i, int k) { return Dy[i * LDS + k]; },
+                        [&](int k, int j) { return Vs[j * LDS + k]; });
+      for_tile(acc, row0, [&](int t, int s, float v) { Dm[t * LDS + s] = v; });
+    }
+    __syncthreads();
+    auto wgt = [&](int t, int s) -> float {
+      if (s < t) return expf(r.p[t] - r.p[s]) * r.scl[s];
+      return s == t ? r.gam[t] : 0.f;
+    };
+    const float end = expf(r.p[C - 1]);
+    // dV = rd(mixed)^T dY + src o (K rd(carry)) ; write dx.
+    {
+      float acc[8][4], ve[8][4];
+      zero8(acc);
+      zero8(ve);
+      warp_gemm<BF, C>(acc, row0, [&](int s, int t) { return round_to<T>(Sc[t * LDS + s] * wgt(t, s)); },
+                       [&](int t, int p) { return Dy[t * LDS + p]; });
+      warp_gemm<BF, NS>(ve, row0, [&](int s, int n) { return Ks[s * LDS + n]; },
+                        [&](int n, int p) { return round_to<T>(Cy[n * LDS + p]); });
+      const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int s = row0 + g + 8 * half, t = t0 + s;
+        if (t >= d.T) continue;
+        const float src = r.scl[s] * r.tail[s];
+        T* row = dx + (size_t(b) * d.T + t) * d.H * HP + h * HP;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int col = nt * 8 + 2 * c;
+          row[col] = from_f<T>(fmaf(src, ve[nt][2 * half], acc[nt][2 * half]));
+          row[col + 1] = from_f<T>(fmaf(src, ve[nt][2 * half + 1], acc[nt][2 * half + 1]));
+        }
+      }
+    }
+    // dQ = rd(Dm o W) K + rd(dY e^p) rd(start)^T  ; inherited for dp.
+    {
+      float acc[8][4];
+      zero8(acc);
+      warp_gemm<BF, C>(acc, row0, [&](int t, int s) { return round_to<T>(Dm[t * LDS + s] * wgt(t, s)); },
+                       [&](int s, int n) { return Ks[s * LDS + n]; });
+      warp_gemm<BF, HP>(acc, row0, [&](int t, int p) { return round_to<T>(Dy[t * LDS + p] * expf(r.p[t])); },
+                        [&](int p, int n) { return round_to<T>(St[n * LDS + p]); });
+      for_tile(acc, row0, [&](int t, int n, float v) { dq_t[t * LDS + n] = v; });
+    }
+    // dK = rd(Dm o W)^T Q + src o (V rd(carry)^T)  ; d_source.
+    {
+      float acc[8][4], ve[8][4];
+      zero8(acc);
+      zero8(ve);
+      warp_gemm<BF, C>(acc, row0, [&](int s, int t) { return round_to<T>(Dm[t * LDS + s] * wgt(t, s)); },
+                       [&](int t, int n) { return Qs[t * LDS + n]; });
+      warp_gemm<BF, HP>(ve, row0, [&](int s, int p) { return Vs[s * LDS + p]; },
+                        [&](int p, int n) { return round_to<T>(Cy[n * LDS + p]); });
+      float dsrc[2] = {0.f, 0.f};
+      const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int s = row0 + g + 8 * half;
+        const float src = r.scl[s] * r.tail[s];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int n = nt * 8 + 2 * c + e;
+            dsrc[half] = fmaf(Ks[s * LDS + n], ve[nt][2 * half + e], dsrc[half]);
+            dk_t[s * LDS + n] = fmaf(src, ve[nt][2 * half + e], acc[nt][2 * half + e]);
+          }
+        // reduce over the 4 lanes sharing the row
+        float v = dsrc[half];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (c == 0) vec[0 * C + s] = v;  // d_source
+      }
+    }
+    // inherited . dY (dp term) : rows t, e^(p_t) sum_p dY[t,p] (Q rd(start))[t,p]
+    {
+      float acc[8][4];
+      zero8(acc);
+      warp_gemm<BF, NS>(acc, row0, [&](int t, int n) { return Qs[t * LDS + n]; },
+                        [&](int n, int p) { return round_to<T>(St[n * LDS + p]); });
+      const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int t = row0 + g + 8 * half;
+        float v = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) v = fmaf(Dy[t * LDS + nt * 8 + 2 * c + e], acc[nt][2 * half + e], v);
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (c == 0) vec[1 * C + t] = v * expf(r.p[t]);
+      }
+    }
+    __syncthreads();
+    // Per-token scalar gradients from d_weights = Dm o Sc.
+    if (tid < C) {
+      const int t = tid;
+      float rowoff = 0.f, coloff = 0.f, cdec = 0.f;
+      for (int s = 0; s < t; ++s) {
+        const float dw = Dm[t * LDS + s] * Sc[t * LDS + s];
+        rowoff = fmaf(dw, expf(r.p[t] - r.p[s]) * r.scl[s], rowoff);
+      }
+      for (int u = t + 1; u < C; ++u) {
+        const float dw = Dm[u * LDS + t] * Sc[u * LDS + t];
+        const float dec = expf(r.p[u] - r.p[t]);
+        coloff = fmaf(dw, dec * r.scl[t], coloff);
+        cdec = fmaf(dw, dec, cdec);
+      }
+      const float flow = vec[0 * C + t] * r.scl[t] * r.tail[t];
+      vec[2 * C + t] = rowoff - coloff - flow + vec[1 * C + t];        // dp
+      vec[3 * C + t] = Dm[t * LDS + t] * Sc[t * LDS + t];                // d gamma
+      vec[4 * C + t] = vec[0 * C + t] * r.tail[t] + cdec;                // d scale
+      vec[5 * C + t] = flow;
+    }
+    // <carry, start> for the chunk-end decay.
+    {
+      float part = 0.f;
+      for (int i = tid; i < NS * HP; i += THREADS) part = fmaf(Cy[(i / HP) * LDS + i % HP], St[(i / HP) * LDS + i % HP], part);
+      part = warp_sum(part);
+      if (lane == 0) scratch[warp] = part;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // d_log_decay = suffix sum of dp (+ chunk-end terms at the last position)
+      float fl = vec[5 * C + tid] + vec[5 * C + 32 + tid];
+      fl = warp_sum(fl);
+      const float extra = fl + end * (scratch[0] + scratch[1] + scratch[2] + scratch[3]);
+      float hi = vec[2 * C + 63 - tid] + (tid == 0 ? extra : 0.f);
+      const float shi = warp_inclusive_scan(hi, tid);
+      const float tot = __shfl_sync(0xffffffffu, shi, 31);
+      const float slo = warp_inclusive_scan(vec[2 * C + 31 - tid], tid) + tot;
+      vec[6 * C + 63 - tid] = shi;
+      vec[6 * C + 31 - tid] = slo;
+    }
+    __syncthreads();
+    // New carry: d_start = Q^T rd(dY e^p) + e^(p_L) carry.
+    {
+      float acc[8][4];
+      zero8(acc);
+      warp_gemm<BF, C>(acc, row0, [&](int n, int t) { return Qs[t * LDS + n]; },
+                       [&](int t, int p) { return round_to<T>(Dy[t * LDS + p] * expf(r.p[t])); });
+      __syncthreads();
+      for_tile(acc, row0, [&](int n, int p, float v) { Cy[n * LDS + p] = fmaf(end, Cy[n * LDS + p], v); });
+    }
+    // Rotation backward: dq_pre = R^T dQ, d_theta = dQ.J q_rot + dK.J k_rot.
+    // Per-token, per-pair: write dq/dk pre-rotation and d_theta per pair.
+    for (int idx = tid; idx < C * (NS / 2); idx += THREADS) {
+      const int tt = idx / (NS / 2), i = idx % (NS / 2), t = t0 + tt;
+      const int n0 = 2 * i, n1 = 2 * i + 1;
+      const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
+      const float gq0 = dq_t[tt * LDS + n0], gq1 = dq_t[tt * LDS + n1];
+      const float gk0 = dk_t[tt * LDS + n0], gk1 = dk_t[tt * LDS + n1];
+      const float pq0 = gq0 * cs + gq1 * sn, pq1 = gq1 * cs - gq0 * sn;
+      const float pk0 = gk0 * cs + gk1 * sn, pk1 = gk1 * cs - gk0 * sn;
+      if (t < d.T) {
+        const size_t base = ((size_t(b) * d.T + t) * d.H + h) * NS;
+        o.dq[base + n0] = pq0; o.dq[base + n1] = pq1;
+        o.dk[base + n0] = pk0; o.dk[base + n1] = pk1;
+      }
+      // Pre-rotation gradients kept for the bias sums.
+      Sc[tt * LDS + n0] = pq0; Sc[tt * LDS + n1] = pq1;
+      Dm[tt * LDS + n0] = pk0; Dm[tt * LDS + n1] = pk1;
+    }
+    __syncthreads();
+    // d_theta per pair from the fp32 rotated values before rounding
+    // (flashmamba.py:776), recomputed since Qf/Kf now hold dQ/dK.
+    for (int idx = tid; idx < C * (NS / 2); idx += THREADS) {
+      const int tt = idx / (NS / 2), i = idx % (NS / 2), t = t0 + tt;
+      const int n0 = 2 * i, n1 = 2 * i + 1;
+      float c0 = 0.f, c1 = 0.f, b0 = 0.f, b1 = 0.f;
+      if (t < d.T) {
+        const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * NS : (size_t(b) * d.T + t) * NS;
+        c0 = to_f(cq[base + n0]); c1 = to_f(cq[base + n1]);
+        b0 = to_f(bk[base + n0]); b1 = to_f(bk[base + n1]);
+      }
+      const float q0 = round_to<T>(c0 + (qb ? qb[h * NS + n0] : 0.f));
+      const float q1 = round_to<T>(c1 + (qb ? qb[h * NS + n1] : 0.f));
+      const float k0 = round_to<T>(b0 + (kb ? kb[h * NS + n0] : 0.f));
+      const float k1 = round_to<T>(b1 + (kb ? kb[h * NS + n1] : 0.f));
+      const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
+      const float qr0 = q0 * cs - q1 * sn, qr1 = q1 * cs + q0 * sn;
+      const float kr0 = k0 * cs - k1 * sn, kr1 = k1 * cs + k0 * sn;
+      const float gq0 = dq_t[tt * LDS + n0], gq1 = dq_t[tt * LDS + n1];
+      const float gk0 = dk_t[tt * LDS + n0], gk1 = dk_t[tt * LDS + n1];
+      // partner(q_rot) = (-qr1, qr0)
+      const float dth = gq0 * (-qr1) + gq1 * qr0 + gk0 * (-kr1) + gk1 * kr0;
+      theta[tt * 33 + i] = i < d.A ? dth : 0.f;
+    }
+    __syncthreads();
+    // Suffix sums of d_theta per pair -> rate and dt gradients.
+    if (tid < d.A) {
+      const int i = tid;
+      float acc = later[i];
+      for (int tt = C - 1; tt >= 0; --tt) {
+        acc += theta[tt * 33 + i];
+        theta[tt * 33 + i] = acc;  // d_increment (pair) at tt
+      }
+      later[i] = acc;
+    }
+    __syncthreads();
+    if (tid < C) {
+      const int tt = tid, t = t0 + tt;
+      if (t < d.T) {
+        float ddt = 0.f;
+        for (int i = 0; i < d.A; ++i) {
+          const float rate = d.per_head ? angles[((size_t(b) * d.T + t) * d.H + h) * d.A + i]
+                                        : angles[(size_t(b) * d.T + t) * d.A + i];
+          const float inc = theta[tt * 33 + i];
+          o.drate[((size_t(b) * d.T + t) * d.H + h) * d.A + i] = inc * r.dt[tt];
+          ddt = fmaf(inc, rate, ddt);
+        }
+        const size_t si = (size_t(b) * d.T + t) * d.H + h;
+        o.ddtp[si] = ddt;
+        o.dgam[si] = vec[3 * C + tt];
+        o.dscl[si] = vec[4 * C + tt];
+        o.dlog[si] = vec[6 * C + tt];
+      }
+    }
+    // Bias partial sums over this chunk's tokens (column tid).
+    if (tid < NS) {
+      float sq = 0.f, sk = 0.f;
+      for (int tt = 0; tt < C; ++tt) {
+        if (t0 + tt < d.T) { sq += Sc[tt * LDS + tid]; sk += Dm[tt * LDS + tid]; }
+      }
+      qbs += sq;
+      kbs += sk;
+    }
+    __syncthreads();
+  }
+  if (tid < NS) {
+    o.dqb[size_t(bh) * NS + tid] = qbs;
+    o.dkb[size_t(bh) * NS + tid] = kbs;
+  }
+}
+
+// dc/db: sum the per-head pre-rotation gradients over heads (fixed order),
+// or copy them for per-head layouts; cast to the model dtype.
+template <typename T>
+__global__ void reduce_heads_kernel(Dims d, const float* __restrict__ dq, const float* __restrict__ dk,
+                                    T* __restrict__ dc, T* __restrict__ db) {
+  const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (d.per_head) {
+    const size_t total = size_t(d.B) * d.T * d.H * NS;
+    if (idx >= total) return;
+    dc[idx] = from_f<T>(dq[idx]);
+    db[idx] = from_f<T>(dk[idx]);
+    return;
+  }
+  const size_t total = size_t(d.B) * d.T * NS;
+  if (idx >= total) return;
+  const size_t bt = idx / NS, n = idx % NS;
+  float sq = 0.f, sk = 0.f;
+  for (int h = 0; h < d.H; ++h) {
+    sq += dq[(bt * d.H + h) * NS + n];
+    sk += dk[(bt * d.H + h) * NS + n];
+  }
+  dc[idx] = from_f<T>(sq);
+  db[idx] = from_f<T>(sk);
+}
+
+// Gate chain rule (mamba3_fused preprocessing, flashmamba.py:1142-1147):
+// gamma = dt s, prev = dt (1 - s), scale_t = gamma_t + prev_(t+1), s = sigmoid(trap).
+__global__ void gates_kernel(Dims d, const float* __restrict__ dt, const float* __restrict__ trap_logits,
+                             const float* __restrict__ dgam, const float* __restrict__ dscl,
+                             const float* __restrict__ dlog, const float* __restrict__ ddtp,
+                             const float* __restrict__ drate, float* __restrict__ d_adt,
+                             float* __restrict__ d_dt, float* __restrict__ d_trap,
+                             float* __restrict__ d_angles) {
+  const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t total = size_t(d.B) * d.T * d.H;
+  if (idx < total) {
+    const size_t bt = idx / d.H;
+    const int t = int(bt % d.T);
+    const float s = 1.f / (1.f + expf(-trap_logits[idx]));
+    const float g = dgam[idx] + dscl[idx];
+    const float pv = t > 0 ? dscl[idx - d.H] : 0.f;
+    d_dt[idx] = fmaf(g, s, pv * (1.f - s)) + ddtp[idx];
+    d_trap[idx] = (g - pv) * dt[idx] * s * (1.f - s);
+    d_adt[idx] = dlog[idx];
+  }
+  // Angle-rate gradients: per head, or summed over heads for shared angles.
+  if (d.per_head) {
+    const size_t ta = size_t(d.B) * d.T * d.H * d.A;
+    if (idx < ta) d_angles[idx] = drate[idx];
+  } else {
+    const size_t ta = size_t(d.B) * d.T * d.A;
+    if (idx < ta) {
+      const size_t bt = idx / d.A, i = idx % d.A;
+      float acc = 0.f;
+      for (int h = 0; h < d.H; ++h) acc += drate[(bt * d.H + h) * d.A + i];
+      d_angles[idx] = acc;
+    }
+  }
+}
+
+__global__ void bias_kernel(Dims d, const float* __restrict__ dqb, const float* __restrict__ dkb,
+                            float* __restrict__ d_qb, float* __restrict__ d_kb) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= d.H * NS) return;
+  float sq = 0.f, sk = 0.f;
+  for (int b = 0; b < d.B; ++b) {
+    sq += dqb[size_t(b) * d.H * NS + idx];
+    sk += dkb[size_t(b) * d.H * NS + idx];
+  }
+  if (d_qb) d_qb[idx] = sq;
+  if (d_kb) d_kb[idx] = sk;
+}
+
+struct Layout {
+  size_t starts, phases, resid;
+  size_t dq, dk, drate, dgam, dscl, dlog, ddtp, dqb, dkb, work;
+};
+
+inline Layout layout(const M4ScanDims& s) {
+  Layout l;
+  const int nch = (s.time + C - 1) / C;
+  const size_t bh = size_t(s.batch) * s.heads, bth = size_t(s.batch) * s.time * s.heads;
+  size_t off = 0;
+  l.starts = off; off += align256(bh * nch * NS * HP * sizeof(float));
+  l.phases = off; off += align256(bh * nch * 32 * sizeof(float));
+  l.resid = off;
+  off = 0;
+  l.dq = off; off += align256(bth * NS * sizeof(float));
+  l.dk = off; off += align256(bth * NS * sizeof(float));
+  l.drate = off; off += align256(bth * 32 * sizeof(float));
+  l.dgam = off; off += align256(bth * sizeof(float));
+  l.dscl = off; off += align256(bth * sizeof(float));
+  l.dlog = off; off += align256(bth * sizeof(float));
+  l.ddtp = off; off += align256(bth * sizeof(float));
+  l.dqb = off; off += align256(bh * NS * sizeof(float));
+  l.dkb = off; off += align256(bh * NS * sizeof(float));
+  l.work = off;
+  return l;
+}
+
+inline size_t fwd_smem() { return (5 * C * LDS + C * 33 + 32 + C + sizeof(Rows) / 4) * sizeof(float); }
+inline size_t bwd_smem() {
+  return (10 * C * LDS + 3 * C * 33 + 32 + C + 8 * C + sizeof(Rows) / 4) * sizeof(float);
+}
+
+inline Dims make_dims(const M4ScanDims& s) {
+  Dims d;
+  d.B = s.batch; d.T = s.time; d.H = s.heads; d.A = s.angle_count;
+  d.nch = (s.time + C - 1) / C;
+  d.per_head = s.per_head != 0;
+  return d;
+}
+
+inline int check(const M4ScanDims* s) {
+  if (!s) return M4_ERR_NULL;
+  if (s->batch <= 0 || s->time <= 0 || s->heads <= 0 || s->head_dim <= 0 || s->state_dim <= 0 ||
+      s->angle_count < 0 || s->chunk <= 0)
+    return M4_ERR_DIMS;
+  if (s->head_dim != HP || s->state_dim != NS || s->chunk != C || s->angle_count > NS / 2)
+    return M4_ERR_UNSUPPORTED;
+  return M4_OK;
+}
+
+template <typename T>
+int forward(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+            const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
+            void* y, float* fin, char* resid, cudaStream_t st) {
+  const Dims d = make_dims(s);
+  const Layout l = layout(s);
+  const size_t sm = fwd_smem();
+  cudaFuncSetAttribute(fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  fwd_kernel<T><<<s.batch * s.heads, THREADS, sm, st>>>(
+      d, static_cast<const T*>(c), static_cast<const T*>(b), static_cast<const T*>(x), adt, dt, trap,
+      angles, qb, kb, static_cast<T*>(y), fin, reinterpret_cast<float*>(resid + l.starts),
+      reinterpret_cast<float*>(resid + l.phases));
+  return launch_status();
+}
+
+template <typename T>
+int backward(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+             const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
+             const char* resid, const void* dy, const float* d_final, void* dc, void* db, void* dx,
+             float* d_adt, float* d_dt, float* d_trap, float* d_angles, float* d_qb, float* d_kb,
+             char* work, cudaStream_t st) {
+  const Dims d = make_dims(s);
+  const Layout l = layout(s);
+  BwdOut o;
+  o.dq = reinterpret_cast<float*>(work + l.dq);
+  o.dk = reinterpret_cast<float*>(work + l.dk);
+  o.drate = reinterpret_cast<float*>(work + l.drate);
+  o.dgam = reinterpret_cast<float*>(work + l.dgam);
+  o.dscl = reinterpret_cast<float*>(work + l.dscl);
+  o.dlog = reinterpret_cast<float*>(work + l.dlog);
+  o.ddtp = reinterpret_cast<float*>(work + l.ddtp);
+  o.dqb = reinterpret_cast<float*>(work + l.dqb);
+  o.dkb = reinterpret_cast<float*>(work + l.dkb);
+  const size_t sm = bwd_smem();
+  cudaFuncSetAttribute(bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  bwd_kernel<T><<<s.batch * s.heads, THREADS, sm, st>>>(
+      d, static_cast<const T*>(c), static_cast<const T*>(b), static_cast<const T*>(x), adt, dt, trap,
+      angles, qb, kb, reinterpret_cast<const float*>(resid + l.starts),
+      reinterpret_cast<const float*>(resid + l.phases), static_cast<const T*>(dy), d_final,
+      static_cast<T*>(dx), o);
+  const size_t n1 = s.per_head ? size_t(s.batch) * s.time * s.heads * NS : size_t(s.batch) * s.time * NS;
+  reduce_heads_kernel<T><<<unsigned((n1 + 255) / 256), 256, 0, st>>>(d, o.dq, o.dk, static_cast<T*>(dc),
+                                                                      static_cast<T*>(db));
+  size_t n2 = size_t(s.batch) * s.time * s.heads;
+  const size_t na = s.per_head ? n2 * s.angle_count : size_t(s.batch) * s.time * s.angle_count;
+  if (na > n2) n2 = na;
+  gates_kernel<<<unsigned((n2 + 255) / 256), 256, 0, st>>>(d, dt, trap, o.dgam, o.dscl, o.dlog, o.ddtp,
+                                                            o.drate, d_adt, d_dt, d_trap, d_angles);
+  if (d_qb || d_kb)
+    bias_kernel<<<(s.heads * NS + 255) / 256, 256, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
+  return launch_status();
+}
+
+}  // namespace scan
+}  // namespace m4
+
+using namespace m4;
+
+extern "C" size_t m4_scan_residual_bytes(const M4ScanDims* s) {
+  return scan::check(s) == M4_OK ? scan::layout(*s).resid : 0;
+}
+
+extern "C" size_t m4_scan_workspace_bytes(const M4ScanDims* s) {
+  return scan::check(s) == M4_OK ? scan::layout(*s).work : 0;
+}
+
+extern "C" int m4_scan_fwd(const M4ScanDims* s, const void* c, const void* b, const void* x,
+                           const float* adt, const float* dt, const float* trap, const float* angles,
+                           const float* qb, const float* kb, void* y, float* fin, void* resid,
+                           size_t resid_bytes, void* stream) {
+  int st = scan::check(s);
+  if (st) return st;
+  if (!c || !b || !x || !adt || !dt || !trap || !y || !fin || !resid) return M4_ERR_NULL;
+  if (s->angle_count > 0 && !angles) return M4_ERR_NULL;
+  if (resid_bytes < scan::layout(*s).resid) return M4_ERR_WORKSPACE;
+  cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  if (s->bf16)
+    return scan::forward<__nv_bfloat16>(*s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin,
+                                        static_cast<char*>(resid), strm);
+  return scan::forward<float>(*s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin,
+                              static_cast<char*>(resid), strm);
+}
+
+extern "C" int m4_scan_bwd(const M4ScanDims* s, const void* c, const void* b, const void* x,
+                           const float* adt, const float* dt, const float* trap, const float* angles,
+                           const float* qb, const float* kb, const void* resid, size_t resid_bytes,
+                           const void* dy, const float* d_final, void* dc, void* db, void* dx,
+                           float* d_adt, float* d_dt, float* d_trap, float* d_angles, float* d_qb,
+                           float* d_kb, void* work, size_t work_bytes, void* stream) {
+  int st = scan::check(s);
+  if (st) return st;
+  if (!c || !b || !x || !adt || !dt || !trap || !resid || !dy || !dc || !db || !dx || !d_adt ||
+      !d_dt || !d_trap || !work)
+    return M4_ERR_NULL;
+  if (s->angle_count > 0 && (!angles || !d_angles)) return M4_ERR_NULL;
+  const scan::Layout l = scan::layout(*s);
+  if (resid_bytes < l.resid || work_bytes < l.work) return M4_ERR_WORKSPACE;
+  cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  if (s->bf16)
+    return scan::backward<__nv_bfloat16>(*s, c, b, x, adt, dt, trap, angles, qb, kb,
+                                         static_cast<const char*>(resid), dy, d_final, dc, db, dx, d_adt,
+                                         d_dt, d_trap, d_angles, d_qb, d_kb, static_cast<char*>(work), strm);
+  return scan::backward<float>(*s, c, b, x, adt, dt, trap, angles, qb, kb, static_cast<const char*>(resid),
+                               dy, d_final, dc, db, dx, d_adt, d_dt, d_trap, d_angles, d_qb, d_kb,
+                               static_cast<char*>(work), strm);
+}

@@ -1,0 +1,166 @@
+"""Mamba-3 SISO chunked scan on B200: the reference's FlashMamba surface.
+
+Mirrors `lm/kernels/flashmamba.py`: `mamba3_fused` (projection layout,
+:1114-1162), `mamba3_flash_heads` / `mamba3_flash` (per-head layout,
+:467-540) and `angle_rates` (:1105-1111), with the same argument meaning,
+shapes and ValueError messages. The scan runs in the CUDA library through the
+C ABI (`m4_scan_fwd/bwd`); the trapezoid gates, the angle duplication and
+their derivatives are folded into those kernels. No CPU path exists.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+STATE_DIM = 64
+HEAD_DIM = 64
+CHUNK = 64
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+class _Scan(torch.autograd.Function):
+    """Forward/backward over padded operands (N = P = 64, chunk 64)."""
+
+    @staticmethod
+    def forward(ctx, c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
+        lib = _lib.load()
+        batch, time = c.shape[:2]
+        heads = dt.shape[-1]
+        bf16 = x.dtype == torch.bfloat16
+        dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, angles.shape[-1], CHUNK,
+                             int(bf16), int(per_head))
+        y = torch.empty_like(x)
+        final = torch.empty(batch, heads, STATE_DIM, HEAD_DIM, device=x.device)
+        nbytes = lib.m4_scan_residual_bytes(ctypes.byref(dims))
+        resid = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        _lib.check(
+            lib.m4_scan_fwd(ctypes.byref(dims), *map(_lib.ptr, (c, b, x, adt, dt, trap, angles, q_bias,
+                                                                 k_bias, y, final, resid)),
+                            nbytes, _stream()),
+            "m4_scan_fwd")
+        ctx.save_for_backward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, resid)
+        ctx.dims = (batch, time, heads, angles.shape[-1], bf16, per_head)
+        return y, final
+
+    @staticmethod
+    def backward(ctx, d_y, d_final):
+        lib = _lib.load()
+        c, b, x, adt, dt, trap, angles, q_bias, k_bias, resid = ctx.saved_tensors
+        batch, time, heads, count, bf16, per_head = ctx.dims
+        dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, count, CHUNK, int(bf16),
+                             int(per_head))
+        d_y = torch.zeros_like(x) if d_y is None else d_y.to(x.dtype).contiguous()
+        d_final = None if d_final is None else d_final.float().contiguous()
+        dc, db, dx = torch.empty_like(c), torch.empty_like(b), torch.empty_like(x)
+        dadt, ddt, dtrap = torch.empty_like(adt), torch.empty_like(dt), torch.empty_like(trap)
+        dang = torch.empty_like(angles)
+        dqb = torch.empty_like(q_bias) if q_bias is not None else None
+        dkb = torch.empty_like(k_bias) if k_bias is not None else None
+        wbytes = lib.m4_scan_workspace_bytes(ctypes.byref(dims))
+        work = torch.empty(wbytes, dtype=torch.uint8, device=x.device)
+        _lib.check(
+            lib.m4_scan_bwd(ctypes.byref(dims), *map(_lib.ptr, (c, b, x, adt, dt, trap, angles, q_bias,
+                                                                 k_bias, resid)),
+                            resid.numel(),
+                            *map(_lib.ptr, (d_y, d_final, dc, db, dx, dadt, ddt, dtrap, dang, dqb, dkb,
+                                            work)),
+                            wbytes, _stream()),
+            "m4_scan_bwd")
+        return dc, db, dx, dadt, ddt, dtrap, dang, dqb, dkb, None
+
+
+def _prepare(c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, per_head):
+    """Pad N and P to 64 (zero coordinates do not interact) and fix dtypes."""
+    state_dim = c.shape[-1]
+    value_dim = x.shape[-1] // heads
+    if state_dim % 2 or angles.shape[-1] > state_dim // 2:
+        # Message of lm/kernels/mamba3.py:23-24.
+        raise ValueError("Mamba-3 state dimension must be even and contain angles")
+    if state_dim > STATE_DIM or value_dim > HEAD_DIM:
+        raise ValueError(f"Scan supports state and head dims up to {STATE_DIM}")
+    model = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
+    c = F.pad(c.to(model), (0, STATE_DIM - state_dim)).contiguous()
+    b = F.pad(b.to(model), (0, STATE_DIM - state_dim)).contiguous()
+    lead = x.shape[:-1]
+    x = F.pad(x.to(model).reshape(*lead, heads, value_dim), (0, HEAD_DIM - value_dim))
+    x = x.reshape(*lead, heads * HEAD_DIM).contiguous()
+    f32 = lambda a: a.float().contiguous()  # noqa: E731
+    qb = None if q_bias is None else F.pad(f32(q_bias).reshape(heads, state_dim), (0, STATE_DIM - state_dim)).contiguous()
+    kb = None if k_bias is None else F.pad(f32(k_bias).reshape(heads, state_dim), (0, STATE_DIM - state_dim)).contiguous()
+    return c, b, x, f32(adt), f32(dt), f32(trap_logits), f32(angles), qb, kb, value_dim, state_dim
+
+
+def mamba3_fused(
+    c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias, chunk_size=CHUNK,
+    interpret=None, heads_per_step=None,
+):
+    """SISO Mamba-3 with one shared query and key per token (one group).
+
+    c, b [B,T,N]; x [B,T,H*P] (bfloat16 or float32); adt, dt, trap_logits
+    [B,T,H]; angles [B,T,A] shared rates; q_bias, k_bias [H,1,N]. Returns
+    y [B,T,H*P] and the final state [B,H,N,P] (`flashmamba.py:1129-1135`).
+    `chunk_size`, `interpret` and `heads_per_step` are accepted for signature
+    compatibility (TPU tiling knobs); the kernels tile by 64.
+    """
+    del chunk_size, interpret, heads_per_step
+    if not x.is_cuda:
+        raise RuntimeError("mamba3_fused runs on CUDA tensors only (no CPU path)")
+    heads = dt.shape[-1]
+    c, b, x, adt, dt, trap, ang, qb, kb, value_dim, state_dim = _prepare(
+        c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, False)
+    y, final = _Scan.apply(c, b, x, adt, dt, trap, ang, qb, kb, False)
+    lead = y.shape[:-1]
+    y = y.reshape(*lead, heads, HEAD_DIM)[..., :value_dim].reshape(*lead, heads * value_dim)
+    return y, final[:, :, :state_dim, :value_dim]
+
+
+def mamba3_flash_heads(
+    q, k, v, adt, dt, trap_logits, angles, *, q_bias=None, k_bias=None, chunk_size=CHUNK,
+    interpret=None, heads_per_step=None,
+):
+    """Per-head layout (`flashmamba.py:467-502`): q, k [B,T,H,N], v [B,T,H,P],
+    angles [B,T,H,A], biases [H,N]. Returns [B,T,H,P] and [B,H,N,P]."""
+    del chunk_size, interpret, heads_per_step
+    if not v.is_cuda:
+        raise RuntimeError("mamba3_flash_heads runs on CUDA tensors only (no CPU path)")
+    batch, time, heads, value_dim = v.shape
+    x = v.reshape(batch, time, heads * value_dim)
+    c, b, x, adt, dt, trap, ang, qb, kb, value_dim, state_dim = _prepare(
+        q, k, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, True)
+    y, final = _Scan.apply(c, b, x, adt, dt, trap, ang, qb, kb, True)
+    y = y.reshape(batch, time, heads, HEAD_DIM)[..., :value_dim]
+    return y, final[:, :, :state_dim, :value_dim]
+
+
+def mamba3_flash(
+    q, k, v, adt, dt, trap_logits, angles, *, chunk_size=CHUNK, q_bias=None, k_bias=None,
+    pairwise=True, interpret=None, heads_per_step=None,
+):
+    """Drop-in for `mamba3_chunked` with rank-one heads (`flashmamba.py:505-540`)."""
+    if q.shape[3] != 1:
+        raise ValueError("mamba3_flash supports SISO (rank-one) heads only")
+    if not pairwise:
+        raise ValueError("mamba3_flash implements pairwise rotation")
+    output, final = mamba3_flash_heads(
+        q[..., 0, :], k[..., 0, :], v[..., 0, :], adt, dt, trap_logits, angles,
+        q_bias=None if q_bias is None else q_bias[:, 0],
+        k_bias=None if k_bias is None else k_bias[:, 0],
+        chunk_size=chunk_size, interpret=interpret, heads_per_step=heads_per_step,
+    )
+    return output[..., None, :], final
+
+
+def angle_rates(angles, state_dim):
+    """[B,T,A] rates on both coordinates of their pair, zero on fixed ones
+    (`flashmamba.py:1105-1111`). The kernels duplicate internally; this is the
+    explicit form for callers that need it."""
+    rates = torch.repeat_interleave(angles.float(), 2, dim=-1)
+    return F.pad(rates, (0, state_dim - rates.shape[-1]))

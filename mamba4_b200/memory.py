@@ -1,0 +1,194 @@
+"""Selective conjugate memory read: the reference operator surface on B200.
+
+Mirrors `lm/kernels/mamba4.py` (SelectiveState, SelectiveResult,
+selective_initial_state, selective_gaussian_memory) and
+`lm/kernels/mamba4_fused.py:372-454` (selective_memory_fused) with the same
+argument meaning, shapes, broadcasting and ValueError messages. The compute
+runs in the CUDA library through the C ABI (`m4_memread_fwd/bwd`); there is
+no CPU path. Gradients come from the library's backward, wrapped as a
+torch.autograd.Function (the reference's jax.custom_vjp).
+"""
+
+from __future__ import annotations
+
+from typing import NamedTuple
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+
+KEY_DIM = 64
+VALUE_DIMS = (64, 128)
+
+
+class SelectiveState(NamedTuple):
+    """Evidence-only sufficient statistics (`lm/kernels/mamba4.py:18-22`)."""
+
+    evidence: torch.Tensor
+    cross: torch.Tensor
+
+
+class SelectiveResult(NamedTuple):
+    """Reads, variances and final state (`lm/kernels/mamba4.py:25-28`)."""
+
+    output: torch.Tensor
+    variance: torch.Tensor
+    state: SelectiveState
+
+
+def selective_initial_state(batch, heads, key_dim, value_dim, device=None):
+    """Zero state (`lm/kernels/mamba4.py:221-225`)."""
+    return SelectiveState(
+        torch.zeros(batch, heads, key_dim, key_dim, dtype=torch.float32, device=device),
+        torch.zeros(batch, heads, value_dim, key_dim, dtype=torch.float32, device=device),
+    )
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dims(batch, time, heads, value_dim):
+    return _lib.MemDims(batch, time, heads, KEY_DIM, value_dim)
+
+
+class _MemoryRead(torch.autograd.Function):
+    """Forward/backward pair over padded operands (D = 64, P in {64, 128})."""
+
+    @staticmethod
+    def forward(ctx, keys, values, queries, beta, log_decay, floor, init_s, init_c):
+        lib = _lib.load()
+        batch, time, heads, _ = keys.shape
+        value_dim = values.shape[-1]
+        dims = _dims(batch, time, heads, value_dim)
+        dev = keys.device
+        out = torch.empty(batch, time, heads, value_dim, device=dev)
+        var = torch.empty(batch, time, heads, device=dev)
+        s_fin = torch.empty(batch, heads, KEY_DIM, KEY_DIM, device=dev)
+        c_fin = torch.empty(batch, heads, value_dim, KEY_DIM, device=dev)
+        nbytes = lib.m4_memread_residual_bytes(ctypes_ref(dims))
+        resid = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _lib.check(
+            lib.m4_memread_fwd(
+                ctypes_ref(dims), *map(_lib.ptr, (keys, values, queries, beta, log_decay, floor,
+                                                   init_s, init_c, out, var, s_fin, c_fin, resid)),
+                nbytes, _stream()),
+            "m4_memread_fwd")
+        ctx.save_for_backward(keys, values, queries, beta, log_decay, floor, init_s, init_c, resid)
+        ctx.has_initial = init_s is not None
+        return out, var, s_fin, c_fin
+
+    @staticmethod
+    def backward(ctx, d_out, d_var, d_s, d_c):
+        lib = _lib.load()
+        keys, values, queries, beta, log_decay, floor, init_s, init_c, resid = ctx.saved_tensors
+        batch, time, heads, _ = keys.shape
+        value_dim = values.shape[-1]
+        dims = _dims(batch, time, heads, value_dim)
+        dev = keys.device
+        d_out = torch.zeros_like(values) if d_out is None else d_out.float().contiguous()
+        d_var = torch.zeros_like(beta) if d_var is None else d_var.float().contiguous()
+        d_s = None if d_s is None else d_s.float().contiguous()
+        d_c = None if d_c is None else d_c.float().contiguous()
+        dk, dv, dq = torch.empty_like(keys), torch.empty_like(values), torch.empty_like(queries)
+        dbeta, dlog = torch.empty_like(beta), torch.empty_like(log_decay)
+        dfloor = torch.empty_like(floor)
+        dis = torch.empty_like(init_s) if ctx.has_initial else None
+        dic = torch.empty_like(init_c) if ctx.has_initial else None
+        wbytes = lib.m4_memread_workspace_bytes(ctypes_ref(dims))
+        work = torch.empty(wbytes, dtype=torch.uint8, device=dev)
+        _lib.check(
+            lib.m4_memread_bwd(
+                ctypes_ref(dims), *map(_lib.ptr, (keys, values, queries, beta, log_decay, floor,
+                                                   init_s, init_c, resid)),
+                resid.numel(),
+                *map(_lib.ptr, (d_out, d_var, d_s, d_c, dk, dv, dq, dbeta, dlog, dfloor, dis, dic,
+                                work)),
+                wbytes, _stream()),
+            "m4_memread_bwd")
+        return dk, dv, dq, dbeta, dlog, dfloor, dis, dic
+
+
+def ctypes_ref(dims):
+    import ctypes
+
+    return ctypes.byref(dims)
+
+
+def _pad_last(x, size, value=0.0):
+    extra = size - x.shape[-1]
+    return x if extra == 0 else F.pad(x, (0, extra), value=value)
+
+
+def selective_memory_fused(
+    keys, values, queries, beta, log_decay, floor, *, chunk_size=64, initial=None
+):
+    """Exact chunked reads of the fixed-floor selective Gaussian memory.
+
+    Same contract as `selective_memory_fused` / `selective_gaussian_memory`
+    (`lm/kernels/mamba4.py:240-248`): keys/queries [B,T,H,D], values [B,T,H,P],
+    beta and log_decay [B,T,H] (log_decay <= 0), floor [H,D] positive,
+    optional initial SelectiveState. Returns SelectiveResult(output [B,T,H,P],
+    variance [B,T,H], final SelectiveState). `chunk_size` is accepted for
+    signature compatibility; the kernels use their own tiling and results are
+    chunk-independent up to float32 rounding.
+
+    Key dims D < 64 are padded with an identity block (zero keys and queries,
+    unit floor), which solves to zero and leaves the true coordinates
+    unchanged, as `batched_solve` pads to 8 (`mamba4_fused.py:289-297`).
+    """
+    del chunk_size
+    keys, values, queries = (torch.as_tensor(a).float() for a in (keys, values, queries))
+    if not keys.is_cuda:
+        raise RuntimeError("selective_memory_fused runs on CUDA tensors only (no CPU path)")
+    batch, time, heads, dim = keys.shape
+    value_dim = values.shape[-1]
+    if queries.shape != keys.shape or values.shape[:3] != keys.shape[:3]:
+        raise ValueError("Selective memory keys, values and queries disagree")
+    if dim > KEY_DIM:
+        raise ValueError(f"Selective memory key dimension {dim} exceeds {KEY_DIM}")
+    if value_dim > VALUE_DIMS[-1]:
+        raise ValueError(f"Selective memory value dimension {value_dim} exceeds {VALUE_DIMS[-1]}")
+    shape = (batch, time, heads)
+    dev = keys.device
+    beta = torch.broadcast_to(torch.as_tensor(beta, dtype=torch.float32, device=dev), shape)
+    log_decay = torch.broadcast_to(torch.as_tensor(log_decay, dtype=torch.float32, device=dev), shape)
+    floor = torch.broadcast_to(torch.as_tensor(floor, dtype=torch.float32, device=dev), (heads, dim))
+    pv = VALUE_DIMS[0] if value_dim <= VALUE_DIMS[0] else VALUE_DIMS[1]
+    k = _pad_last(keys, KEY_DIM).contiguous()
+    q = _pad_last(queries, KEY_DIM).contiguous()
+    v = _pad_last(values, pv).contiguous()
+    f = _pad_last(floor, KEY_DIM, 1.0).contiguous()
+    init_s = init_c = None
+    if initial is not None:
+        s0 = torch.as_tensor(initial.evidence, dtype=torch.float32, device=dev)
+        c0 = torch.as_tensor(initial.cross, dtype=torch.float32, device=dev)
+        init_s = F.pad(s0, (0, KEY_DIM - dim, 0, KEY_DIM - dim)).contiguous()
+        init_c = F.pad(c0, (0, KEY_DIM - dim, 0, pv - value_dim)).contiguous()
+    out, var, s_fin, c_fin = _MemoryRead.apply(
+        k, v, q, beta.contiguous(), log_decay.contiguous(), f, init_s, init_c
+    )
+    state = SelectiveState(s_fin[..., :dim, :dim], c_fin[..., :value_dim, :dim])
+    return SelectiveResult(out[..., :value_dim], var, state)
+
+
+SOLVERS = ("cuda", "fused")
+
+
+def selective_gaussian_memory(
+    keys, values, queries, beta, log_decay, floor, *, chunk_size=64, initial=None, solver="cuda"
+):
+    """`lm/kernels/mamba4.py:228-338` dispatcher with the B200 solver.
+
+    `solver` "cuda" (and the reference's "fused", which this build maps to
+    the same kernel) selects the sm_100a path; the reference's XLA solvers
+    (loop, blocked, unrolled, auto) are not part of this library.
+    """
+    if solver is None:
+        solver = "cuda"
+    if solver not in SOLVERS:
+        raise ValueError(f"Unknown SPD solve backend {solver}")
+    return selective_memory_fused(
+        keys, values, queries, beta, log_decay, floor, chunk_size=chunk_size, initial=initial
+    )
