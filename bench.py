@@ -1,0 +1,462 @@
+"""Benchmark of the Mamba 4 FlashMamba hot path on B200.
+
+Default workload ("hotpath", BASELINE configs[1] + configs[2]): one step is
+  * one Mamba-3 SISO scan layer forward+backward on config 1
+    (batch 16 x seq 1024, 16 heads, P = N = 64, chunk 64, bf16 operands), and
+  * one memory-read layer forward+backward on config 2
+    (batch 128 x seq 1024, 8 heads, D = P = 64, fp32, factors stored),
+on seeded synthetic inputs already resident in HBM. The metric is the
+baseline's "memory-read+scan tokens/s fwd+bwd": tokens through the two layers
+(16,384 + 131,072 per GPU per step) per second. Under torchrun every rank
+runs its own batch (no data-path exchange; weak scaling) and the value is the
+job total. `e2e` is the same metric through the public operator API with the
+inputs copied from pinned host memory and every output and gradient copied
+back inside the timed region.
+
+`--impl reference` times the reference's CPU algorithm for the same
+workload (the float64 oracle port; the reference's JAX runtime is not
+installed) on all host cores, on a bounded sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+MEM_CFG = dict(batch=128, time=1024, heads=8, dim=64, value_dim=64)      # configs[2]
+SCAN_CFG = dict(batch=16, time=1024, heads=16, head_dim=64, state_dim=64)  # configs[1]
+SMALL_MEM_CFG = dict(batch=16, time=1024, heads=8, dim=64, value_dim=64)
+# Algorithmic work per unit (per token-head for the memory read, per token for
+# the scan at H = 16, P = N = 64, c = 64): the figures of the hot-path survey.
+MEM_FWD_BYTES, MEM_BWD_BYTES = 9356, 10132
+MEM_FWD_FLOPS, MEM_BWD_FLOPS = 122421, 80160
+SCAN_BYTES, SCAN_FLOPS = 11776, 1835008
+L2_BYTES = 126 * 2**20
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        p = json.loads(path.read_text())
+        return dict(hbm=p["hbm_gbs"], bf16=p["bf16_tflops"], bf16_sust=p["bf16_tflops_sustained"],
+                    source="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sust=1400.0, source="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 8:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[4:]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def setup_dist(n_gpus):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_mem(cfg, seed, device):
+    """Seeded config-2 inputs generated on the device (torch RNG; same
+    distributions as the oracle's config_inputs)."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, T, H, D, P = cfg["batch"], cfg["time"], cfg["heads"], cfg["dim"], cfg["value_dim"]
+    q = torch.randn(B, T, H, D, device=device, generator=g) / 8
+    k = torch.randn(B, T, H, D, device=device, generator=g) / 8
+    v = torch.randn(B, T, H, P, device=device, generator=g)
+    lam = torch.sigmoid(torch.randn(B, T, H, device=device, generator=g) + 2.0)
+    beta = torch.sigmoid(torch.randn(B, T, H, device=device, generator=g))
+    d_out = torch.randn(B, T, H, P, device=device, generator=g)
+    d_var = torch.randn(B, T, H, device=device, generator=g)
+    k = torch.cat((torch.zeros_like(k[:, :1]), k[:, :-1]), 1).contiguous()
+    floor = torch.full((H, D), 0.1, device=device)
+    return dict(keys=k, values=v, queries=q, beta=beta, log_decay=torch.log(lam), floor=floor,
+                d_output=d_out, d_variance=d_var)
+
+
+def make_scan(cfg, seed, device):
+    import math
+
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    B, T, H, P, N = cfg["batch"], cfg["time"], cfg["heads"], cfg["head_dim"], cfg["state_dim"]
+    bf = torch.bfloat16
+    x = (torch.randn(B, T, H * P, device=device, generator=g) / 8).to(bf)
+    b = (torch.randn(B, T, N, device=device, generator=g) / 8).to(bf)
+    c = (torch.randn(B, T, N, device=device, generator=g) / 8).to(bf)
+    dt = torch.nn.functional.softplus(torch.randn(B, T, H, device=device, generator=g) * 0.5 - 3.0)
+    a = -torch.exp(torch.rand(H, device=device, generator=g) * math.log(16.0))
+    adt = a * dt
+    trap = torch.randn(B, T, H, device=device, generator=g)
+    angles = (torch.rand(B, T, N // 2, device=device, generator=g) * 2 - 1) * math.pi
+    ones = torch.ones(H, 1, N, device=device)
+    d_y = torch.randn(B, T, H * P, device=device, generator=g).to(bf)
+    d_final = torch.randn(B, H, N, P, device=device, generator=g)
+    return dict(c=c, b=b, x=x, adt=adt, dt=dt, trap_logits=trap, angles=angles, q_bias=ones,
+                k_bias=ones.clone(), d_y=d_y, d_final=d_final)
+
+
+def memread_step(m, requires=True):
+    import torch
+
+    from mamba4_b200 import selective_memory_fused
+
+    leaves = [m[n].requires_grad_(requires) for n in ("keys", "values", "queries", "beta", "log_decay")]
+    res = selective_memory_fused(*leaves, m["floor"])
+    grads = torch.autograd.grad((res.output, res.variance), leaves,
+                                (m["d_output"], m["d_variance"]))
+    return res, grads
+
+
+def scan_step(s):
+    import torch
+
+    from mamba4_b200 import mamba3_fused
+
+    names = ("c", "b", "x", "adt", "dt", "trap_logits", "angles", "q_bias", "k_bias")
+    leaves = [s[n].requires_grad_(True) for n in names]
+    y, final = mamba3_fused(*leaves[:7], q_bias=leaves[7], k_bias=leaves[8])
+    grads = torch.autograd.grad((y, final), leaves, (s["d_y"], s["d_final"]))
+    return y, final, grads
+
+
+def time_region(fn, steps, warmup, world):
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop)
+
+
+def op_times(fn_fwd, fn_bwd, reps=5):
+    """Average device time (ms) of a forward and a backward call, CUDA events."""
+    import torch
+
+    fwd_ms, bwd_ms = [], []
+    for _ in range(reps):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        ctx = fn_fwd()
+        e1.record()
+        fn_bwd(ctx)
+        e2.record()
+        torch.cuda.synchronize()
+        fwd_ms.append(e0.elapsed_time(e1))
+        bwd_ms.append(e1.elapsed_time(e2))
+    return statistics.median(fwd_ms), statistics.median(bwd_ms)
+
+
+def cpu_baseline_sample(mem_cfg, scan_cfg, threads):
+    """Oracle port on the host: a bounded sample of each layer, extrapolated
+    to the step's token counts. Returns (tokens/s, description)."""
+    import numpy as np
+    import torch
+
+    from oracle import memread as M
+    from oracle import scan as S
+
+    torch.set_num_threads(threads)
+    mt = 256  # memory-read sample: 1 sequence x 256 tokens x all heads
+    cfg = M.config_inputs(1, mt, mem_cfg["heads"], mem_cfg["dim"], mem_cfg["value_dim"], seed=0)
+    names = ("keys", "values", "queries", "beta", "log_decay", "floor")
+    t0 = time.perf_counter()
+    M.chunked_forward(*[cfg[n] for n in names])
+    M.chunked_backward(*[cfg[n] for n in names], None, cfg["d_output"], cfg["d_variance"])
+    t_mem = time.perf_counter() - t0
+    st = 1024
+    sc = S.config_inputs(1, st, scan_cfg["heads"], scan_cfg["head_dim"], scan_cfg["state_dim"], seed=1)
+    keys = ("c", "b", "x", "adt", "dt", "trap_logits", "angles", "q_bias", "k_bias")
+    t0 = time.perf_counter()
+    S.fused_layout_scan(*[torch.tensor(sc[n], dtype=torch.float64) for n in keys])
+    S.fused_layout_grads([sc[n] for n in keys], sc["d_y"], sc["d_final"])
+    t_scan = time.perf_counter() - t0
+    mem_tokens = mem_cfg["batch"] * mem_cfg["time"]
+    scan_tokens = scan_cfg["batch"] * scan_cfg["time"]
+    per_step = t_mem * mem_tokens / mt + t_scan * scan_tokens / st
+    del np
+    return (mem_tokens + scan_tokens) / per_step, (
+        f"oracle port float64: memory read fwd+bwd on 1x{mt} tokens x {mem_cfg['heads']} heads "
+        f"({t_mem:.2f} s) and scan fwd+bwd on 1x{st} tokens x {scan_cfg['heads']} heads "
+        f"({t_scan:.2f} s), extrapolated linearly to the step's token counts")
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = host_threads()
+    tokens = MEM_CFG["batch"] * MEM_CFG["time"] + SCAN_CFG["batch"] * SCAN_CFG["time"]
+    rates, desc = [], ""
+    for i in range(args.warmup + args.steps):
+        rate, desc = cpu_baseline_sample(MEM_CFG, SCAN_CFG, threads)
+        if i >= args.warmup:
+            rates.append(rate)
+    value = statistics.median(rates)
+    line = {
+        "impl": "reference", "metric": "memory-read+scan tokens/s fwd+bwd", "value": value,
+        "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * tokens / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "configs[1]+configs[2] (hotpath)", "tokens_per_step": tokens,
+                   "cpu": "reference CPU algorithm (oracle port; jax not installed)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    del world
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+
+    world, rank, local = setup_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    mem_cfg = SMALL_MEM_CFG if args.workload == "small" else MEM_CFG
+    m = make_mem(mem_cfg, seed=1000 + rank, device=dev)
+    s = make_scan(SCAN_CFG, seed=2000 + rank, device=dev)
+
+    def step():
+        memread_step(m)
+        scan_step(s)
+
+    with ClockSampler(local) as clocks:
+        total_ms = time_region(step, args.steps, args.warmup, world)
+    total_ms = max_over_ranks(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    mem_tokens = mem_cfg["batch"] * mem_cfg["time"]
+    scan_tokens = SCAN_CFG["batch"] * SCAN_CFG["time"]
+    tokens = mem_tokens + scan_tokens
+    value = world * tokens / (ms_per_step / 1000.0)
+
+    # Per-op device times (rank-local) for the roofline and the components.
+    from mamba4_b200 import selective_memory_fused
+
+    mleaves = [m[n].detach().requires_grad_(True) for n in ("keys", "values", "queries", "beta", "log_decay")]
+
+    def mfwd():
+        return selective_memory_fused(*mleaves, m["floor"])
+
+    def mbwd(res):
+        torch.autograd.grad((res.output, res.variance), mleaves, (m["d_output"], m["d_variance"]))
+
+    mem_fwd_ms, mem_bwd_ms = op_times(mfwd, mbwd)
+    from mamba4_b200 import mamba3_fused
+
+    names = ("c", "b", "x", "adt", "dt", "trap_logits", "angles", "q_bias", "k_bias")
+    sleaves = [s[n].detach().requires_grad_(True) for n in names]
+
+    def sfwd():
+        return mamba3_fused(*sleaves[:7], q_bias=sleaves[7], k_bias=sleaves[8])
+
+    def sbwd(out):
+        torch.autograd.grad(out, sleaves, (s["d_y"], s["d_final"]))
+
+    scan_fwd_ms, scan_bwd_ms = op_times(sfwd, sbwd)
+
+    # End to end through the public API with host buffers.
+    e2e = None
+    if not args.no_e2e:
+        pin = {k: v.detach().cpu().pin_memory() for k, v in m.items()}
+        spin = {k: v.detach().cpu().pin_memory() for k, v in s.items()}
+        h2d = sum(t.numel() * t.element_size() for t in list(pin.values()) + list(spin.values()))
+        out_host = {}
+        d2h = 0
+
+        def e2e_step():
+            nonlocal d2h
+            dm = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
+            ds = {k: v.to(dev, non_blocking=True) for k, v in spin.items()}
+            res, mg = memread_step(dm)
+            y, fin, sg = scan_step(ds)
+            outs = [res.output, res.variance, res.state.evidence, res.state.cross, *mg, y, fin, *sg]
+            if not out_host:
+                for i, t in enumerate(outs):
+                    out_host[i] = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                d2h = sum(t.numel() * t.element_size() for t in outs)
+            for i, t in enumerate(outs):
+                out_host[i].copy_(t, non_blocking=True)
+
+        e2e_ms = max_over_ranks(time_region(e2e_step, max(2, args.steps // 2), args.warmup, world), world)
+        e2e_ms /= max(2, args.steps // 2)
+        e2e = {"value": world * tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
+
+    pk = peaks()
+    token_heads = mem_tokens * mem_cfg["heads"]
+    fwd_bytes = MEM_FWD_BYTES * token_heads
+    achieved = fwd_bytes / (mem_fwd_ms / 1000.0) / 1e9
+    mem_total_bytes = (MEM_FWD_BYTES + MEM_BWD_BYTES) * token_heads
+    mem_flops = (MEM_FWD_FLOPS + MEM_BWD_FLOPS) * token_heads
+    scan_ms = scan_fwd_ms + scan_bwd_ms
+    traffic = None
+    tpath = ROOT / "profiles" / "memread_traffic.json"
+    if tpath.exists():
+        traffic = json.loads(tpath.read_text()).get("memread_fwd_bytes_per_launch_c2")
+    roofline = {
+        "bound": "hbm", "kernel": "m4_memread_fwd (states + solve + output kernels)",
+        "achieved": achieved, "peak": pk["hbm"], "unit": "GB/s", "frac": achieved / pk["hbm"],
+        "traffic": traffic, "peak_source": pk["source"],
+        "algorithmic_bytes": fwd_bytes,
+        "fp32": {"tflops": MEM_FWD_FLOPS * token_heads / (mem_fwd_ms / 1000.0) / 1e12,
+                 "nominal_peak_tflops": 74.4},
+    }
+    components = {
+        "memread_c2": {"fwd_ms": mem_fwd_ms, "bwd_ms": mem_bwd_ms,
+                       "tokens_per_s": mem_tokens / ((mem_fwd_ms + mem_bwd_ms) / 1000.0),
+                       "hbm_frac": mem_total_bytes / ((mem_fwd_ms + mem_bwd_ms) / 1000.0) / 1e9 / pk["hbm"],
+                       "fp32_tflops": mem_flops / ((mem_fwd_ms + mem_bwd_ms) / 1000.0) / 1e12},
+        "scan_c1": {"fwd_ms": scan_fwd_ms, "bwd_ms": scan_bwd_ms,
+                    "tokens_per_s": scan_tokens / (scan_ms / 1000.0),
+                    "hbm_frac": SCAN_BYTES * scan_tokens / (scan_ms / 1000.0) / 1e9 / pk["hbm"],
+                    "tensor_tflops": SCAN_FLOPS * scan_tokens / (scan_ms / 1000.0) / 1e12},
+    }
+    line = {
+        "metric": "memory-read+scan tokens/s fwd+bwd", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+bf16",
+        "data": "synthetic",
+        "config": {"workload": "configs[1]+configs[2] (hotpath)" if args.workload == "hotpath"
+                   else "small memory read (16x1024x8) + configs[1] scan",
+                   "memread": mem_cfg, "scan": dict(SCAN_CFG, chunk=64, dtype="bf16"),
+                   "tokens_per_step_per_gpu": tokens, "l2": "inputs larger than L2 (memory-read "
+                   "operands 268 MB each, stored factors 9.7 GB)"},
+        "roofline": roofline, "components": components, "e2e": e2e,
+        "gpu_launches": 13 * args.steps, "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, desc = cpu_baseline_sample(mem_cfg, SCAN_CFG, host_threads())
+        line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": host_threads(),
+                                "kind": "port", "sample": desc}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["hotpath", "small"], default="hotpath")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    args = p.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -266,3 +266,156 @@ def config_inputs(batch, time, heads, head_dim, state_dim, seed=0, per_head_angl
         c=c, b=b, x=x, adt=adt, dt=dt, trap_logits=trap, angles=angles,
         q_bias=ones, k_bias=ones.copy(), d_y=dy, d_final=d_final,
     )
+
+
+def _chunk_weights(p, scl, gam, chunk):
+    """decay [B,t,s,H] (strict lower), W = decay*scale + diag(gamma)."""
+    lower = torch.tril(torch.ones(chunk, chunk, dtype=torch.bool), -1)
+    diag = torch.eye(chunk, dtype=torch.bool)
+    diff = p[:, :, None, :] - p[:, None, :, :]
+    zero = torch.zeros_like(diff)
+    decay = torch.where(lower[None, :, :, None], torch.exp(torch.where(lower[None, :, :, None], diff, zero)), zero)
+    weights = decay * scl[:, None, :, :] + torch.where(diag[None, :, :, None], gam[:, :, None, :], zero)
+    return decay, weights, lower, diag
+
+
+def chunked_scan_backward_emulated(
+    q, k, v, adt, dt, trap_logits, angles, q_bias, k_bias, d_y, d_final, *,
+    chunk=64, model_dtype=torch.bfloat16,
+):
+    """Gradients with the reference backward kernel's own rounding points.
+
+    Restates `_fused_backward_kernel` (`lm/kernels/flashmamba.py:663-786`) and
+    its XLA epilogue (`:1081-1099`) on per-head tensors, in float32 with the
+    model-dtype casts of the reference: the masked scores and their
+    cotangent products (`:734-737`), dY scaled by e^p (`:740`), the chunk-
+    start state (`:742`, `:744`) and the end-state cotangent (`:748`). The
+    trapezoid gates and angle duplication are differentiated exactly (the
+    reference leaves them to JAX autodiff, `:1142-1147`, `:1105-1111`).
+    Inputs as `chunked_scan`; d_y [B,T,H,P], d_final [B,H,N,P]. Returns the
+    9 input gradients (q, k, v, adt, dt, trap_logits, angles, q_bias, k_bias).
+    """
+    cd = torch.float32
+
+    def rd(x):
+        return x.to(model_dtype).to(cd)
+
+    q, k, v = (a.to(cd) for a in (q, k, v))
+    batch, length, heads, state_dim = q.shape
+    value_dim = v.shape[-1]
+    qb = torch.zeros(heads, state_dim, dtype=cd) if q_bias is None else q_bias.to(cd)
+    kb = torch.zeros(heads, state_dim, dtype=cd) if k_bias is None else k_bias.to(cd)
+    q0, k0 = rd(q + qb), rd(k + kb)
+    dt = dt.to(cd)
+    rates = _duplicate(angles.to(cd), state_dim)
+    theta = torch.cumsum(rates * dt[..., None], dim=1)
+    cos, sin = torch.cos(theta), torch.sin(theta)
+    q_rot = q0 * cos + _partner(q0) * sin
+    k_rot = k0 * cos + _partner(k0) * sin
+    qr, kr = rd(q_rot), rd(k_rot)
+    v = rd(v)
+    dy = rd(d_y.to(cd))
+    trap = torch.sigmoid(trap_logits.to(cd))
+    gamma = dt * trap
+    previous = dt * (1 - trap)
+    scale = gamma + torch.cat((previous[:, 1:], torch.zeros_like(previous[:, :1])), 1)
+    padding = (-length) % chunk
+
+    def pad_time(x):
+        return torch.nn.functional.pad(x, [0, 0] * (x.ndim - 2) + [0, padding])
+
+    qc, kc, vc, dyc = (pad_time(a).reshape(batch, -1, chunk, heads, a.shape[-1]) for a in (qr, kr, v, dy))
+    ac, gc, sc = (pad_time(a).reshape(batch, -1, chunk, heads) for a in (adt.to(cd), gamma, scale))
+    count = qc.shape[1]
+    # Forward pass for the chunk-start states (model-dtype rounding points).
+    state = torch.zeros(batch, heads, state_dim, value_dim, dtype=cd)
+    starts = []
+    for n in range(count):
+        starts.append(state)
+        p = torch.cumsum(ac[:, n], dim=1)
+        tail = torch.exp(p[:, -1:, :] - p)
+        weighted = rd(vc[:, n] * (sc[:, n] * tail)[..., None])
+        state = torch.exp(p[:, -1, :])[..., None, None] * state + torch.einsum(
+            "bshn,bshp->bhnp", kc[:, n], weighted)
+    carry = d_final.to(cd).clone()
+    dq = torch.zeros_like(qc)
+    dk = torch.zeros_like(kc)
+    dv = torch.zeros_like(vc)
+    dlog = torch.zeros_like(ac)
+    dgam = torch.zeros_like(ac)
+    dscl = torch.zeros_like(ac)
+    for n in range(count - 1, -1, -1):
+        qn, kn, vn, dyn = qc[:, n], kc[:, n], vc[:, n], dyc[:, n]
+        p = torch.cumsum(ac[:, n], dim=1)
+        tail = torch.exp(p[:, -1:, :] - p)
+        decay, weights, lower, diag = _chunk_weights(p, sc[:, n], gc[:, n], chunk)
+        source = sc[:, n] * tail
+        start = starts[n]
+        end_decay = torch.exp(p[:, -1, :])
+        scores = torch.einsum("bthn,bshn->btsh", qn, kn)
+        d_mixed = torch.einsum("bthp,bshp->btsh", dyn, vn)
+        mixed = scores * weights
+        dvn = torch.einsum("btsh,bthp->bshp", rd(mixed), dyn)
+        d_scores = rd(d_mixed * weights)
+        dqn = torch.einsum("btsh,bshn->bthn", d_scores, kn)
+        dkn = torch.einsum("btsh,bthn->bshn", d_scores, qn)
+        d_weights = d_mixed * scores
+        carried = torch.exp(p)
+        scaled_dy = rd(dyn * carried[..., None])
+        start_low = rd(start)
+        dqn = dqn + torch.einsum("bthp,bhnp->bthn", scaled_dy, start_low)
+        inherited = torch.einsum("bthn,bhnp->bthp", qn, start_low)
+        dp_col = carried * torch.sum(dyn * inherited, -1)
+        d_start = torch.einsum("bthn,bthp->bhnp", qn, scaled_dy) + end_decay[..., None, None] * carry
+        end_low = rd(carry)
+        v_end = torch.einsum("bshp,bhnp->bshn", vn, end_low)
+        dkn = dkn + source[..., None] * v_end
+        dvn = dvn + source[..., None] * torch.einsum("bshn,bhnp->bshp", kn, end_low)
+        d_source = torch.sum(kn * v_end, -1)
+        flow = d_source * source
+        off = torch.where(lower[None, :, :, None], d_weights * weights, torch.zeros_like(weights))
+        dp = dp_col + off.sum(2) - flow - off.sum(1)
+        dgam[:, n] = torch.diagonal(d_weights, dim1=1, dim2=2).permute(0, 2, 1)
+        dscl[:, n] = d_source * tail + (d_weights * decay).sum(1)
+        last = flow.sum(1) + end_decay * torch.sum(carry * start, (-1, -2))
+        dp[:, -1] = dp[:, -1] + last
+        dlog[:, n] = torch.flip(torch.cumsum(torch.flip(dp, [1]), 1), [1])
+        dq[:, n], dk[:, n], dv[:, n] = dqn, dkn, dvn
+        carry = d_start
+
+    def unpad(x):
+        return x.reshape(batch, count * chunk, *x.shape[3:])[:, :length]
+
+    dq, dk, dv = unpad(dq), unpad(dk), rd(unpad(dv))
+    dlog, dgam, dscl = unpad(dlog), unpad(dgam), unpad(dscl)
+    # Rotation backward (fp32): dq_pre = R^T dq, d_theta = dq.J q_rot + dk.J k_rot.
+    dq_pre = dq * cos - _partner(dq) * sin
+    dk_pre = dk * cos - _partner(dk) * sin
+    d_theta = dq * _partner(q_rot) + dk * _partner(k_rot)
+    d_inc = torch.flip(torch.cumsum(torch.flip(d_theta, [1]), 1), [1])
+    d_rates = d_inc * dt[..., None]
+    count_a = angles.shape[-1]
+    d_angles = d_rates[..., : 2 * count_a].reshape(*d_rates.shape[:-1], count_a, 2).sum(-1)
+    d_dt_phase = torch.sum(d_inc * rates, -1)
+    # Gates: gamma = dt s, prev = dt (1 - s), scale_t = gamma_t + prev_(t+1).
+    g_total = dgam + dscl
+    prev_bar = torch.cat((torch.zeros_like(dscl[:, :1]), dscl[:, :-1]), 1)
+    d_dt = g_total * trap + prev_bar * (1 - trap) + d_dt_phase
+    d_trap = (g_total - prev_bar) * dt * trap * (1 - trap)
+    return [dq_pre, dk_pre, dv, dlog, d_dt, d_trap, d_angles,
+            dq_pre.sum((0, 1)), dk_pre.sum((0, 1))]
+
+
+def fused_layout_grads_emulated(args, d_y, d_final, *, chunk=64, model_dtype=torch.bfloat16):
+    """`chunked_scan_backward_emulated` on the projection layout: shared c, b
+    and angles sum their per-head gradients over heads; returns gradients in
+    `mamba3_fused` argument order."""
+    c, b, x, adt, dt, trap, angles, q_bias, k_bias = (torch.as_tensor(a, dtype=torch.float32) for a in args)
+    heads = dt.shape[-1]
+    q, k, v, per_head, qb, kb = fused_to_heads(c, b, x, angles, q_bias, k_bias, heads)
+    dyh = torch.as_tensor(d_y, dtype=torch.float32).reshape(*x.shape[:2], heads, -1)
+    g = chunked_scan_backward_emulated(q, k, v, adt, dt, trap, per_head, qb, kb, dyh,
+                                       torch.as_tensor(d_final, dtype=torch.float32),
+                                       chunk=chunk, model_dtype=model_dtype)
+    return [g[0].sum(2), g[1].sum(2), g[2].reshape(x.shape), g[3], g[4], g[5], g[6].sum(2),
+            g[7].reshape(q_bias.shape), g[8].reshape(k_bias.shape)]

@@ -2,10 +2,13 @@
 
 float32 operands: relative 1e-4 forward, 1e-3 gradients against the float64
 oracle (absolute floor scaled to each tensor's max). bfloat16 operands (the
-benchmark dtype): outputs against the oracle with the reference's bf16
-rounding points, within a few bf16 ulps (rtol 2e-2, atol 2e-2 * max) and a
-relative Frobenius error below 5e-3; gradients against the float64 oracle on
-the same rounded inputs within a relative Frobenius error of 2e-2.
+benchmark dtype): outputs and gradients against the oracle that applies the
+reference kernels' own bf16 rounding points (forward `flashmamba.py:582-653`,
+backward `:734-751`), within a few bf16 ulps elementwise (rtol 2e-2,
+atol 2e-2 * max) and a relative Frobenius error below 5e-3. Against float64
+the reference's bf16 arithmetic itself is up to ~3% off for the angle-rate
+gradient (a suffix sum over the whole sequence), which is why bf16 parity is
+pinned to the rounding-point restatement.
 """
 
 import numpy as np
@@ -88,10 +91,11 @@ def test_scan_bf16_config1_shape_matches_oracle():
     assert rel_fro(y, ey) < 5e-3
     close(final, ef, 2e-2, "final")
     assert rel_fro(final, ef) < 5e-3
-    rounded = [a.double().numpy() for a in args]
-    eg = S.fused_layout_grads(rounded, cfg["d_y"], cfg["d_final"], chunk=64)
+    eg = S.fused_layout_grads_emulated(args, cfg["d_y"], cfg["d_final"], chunk=64,
+                                       model_dtype=torch.bfloat16)
     for name, g, e in zip(NAMES, grads, eg):
-        assert rel_fro(g, e) < 2e-2, (name, rel_fro(g, e))
+        close(g, e, 2e-2, name)
+        assert rel_fro(g, e) < 5e-3, (name, rel_fro(g, e))
 
 
 @pytest.mark.parametrize("length, heads_per_step", [(45, 2), (40, 4), (7, 1)])
