@@ -32,13 +32,12 @@ namespace mem {
 constexpr int KD = 64;         // key dimension
 constexpr int CH = 64;         // chunk (epilogue / backward products)
 constexpr int SUB = 16;        // tokens per solve warp (state stride)
-constexpr int SLOTS = 72;      // L slots per lane: (m, n), m in [2n, 15], n in [0, 7]
-constexpr int LSTRIDE = SLOTS * 32;  // floats of one token's stored factor (2304)
+constexpr int LSTRIDE = 72 * 32;  // floats of one token's stored factor (36 float2 per lane)
 constexpr int WARPS = 4;       // solve warps per CTA
+#ifndef M4_SOLVE_MINB
+#define M4_SOLVE_MINB 3
+#endif
 
-// Slot of lane-local tile entry (m, n): rows a + 4m, columns b + 8n on lane
-// a*8 + b (a in 0..3, b in 0..7). Column groups n are stored contiguously.
-__host__ __device__ constexpr int slot_of(int m, int n) { return 16 * n - n * (n - 1) + (m - 2 * n); }
 
 struct Sizes {
   int B, T, H, P, Tp, nsub, nch;
@@ -153,138 +152,221 @@ __global__ void __launch_bounds__(256) states_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Shared pieces of the per-token solve warps.
+// Per-token solve warps: lane-tile layout of the 64x64 lower factor.
+// Lane l = a*8 + b (a in 0..3, b in 0..7) owns rows a + 4m and columns b + 8n,
+// stored as row pairs (a + 8p, a + 4 + 8p) x column b + 8n for n <= p <= 7:
+// 36 float2 per lane, index pair_of(p, n). The 8x8 diagonal block J is the
+// pair (J, J) on every lane; off-diagonal block (K, J) is pair (K, J).
 // ---------------------------------------------------------------------------
+constexpr int NPAIR = 36;
+__host__ __device__ constexpr int pair_of(int p, int n) { return 8 * n - n * (n - 1) / 2 + (p - n); }
+__host__ __device__ constexpr int tri(int r, int c) { return r * (r + 1) / 2 + c; }
+constexpr int pair_n(int q) { return q < 8 ? 0 : q < 15 ? 1 : q < 21 ? 2 : q < 26 ? 3 : q < 30 ? 4 : q < 33 ? 5 : q < 35 ? 6 : 7; }
+constexpr int pair_p(int q) { return q - pair_of(pair_n(q), pair_n(q)) + pair_n(q); }
 
-// In-place inverse of an 8x8 lower-triangular block whose diagonal holds the
-// reciprocal pivots 1/L_rr (upper part zero). Result X = L_block^-1, row-major.
-M4_DEV void invert_lower8(float* blk) {
-  float T[8][8], X[8][8];
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    float4 lo = ld4(blk + 8 * r), hi = ld4(blk + 8 * r + 4);
-    T[r][0] = lo.x; T[r][1] = lo.y; T[r][2] = lo.z; T[r][3] = lo.w;
-    T[r][4] = hi.x; T[r][5] = hi.y; T[r][6] = hi.z; T[r][7] = hi.w;
-  }
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-#pragma unroll
-    for (int r = 0; r < 8; ++r) X[r][c] = 0.f;
-    X[c][c] = T[c][c];
-#pragma unroll
-    for (int r = c + 1; r < 8; ++r) {
-      float acc = 0.f;
-#pragma unroll
-      for (int k = c; k < r; ++k) acc = fmaf(T[r][k], X[k][c], acc);
-      X[r][c] = -T[r][r] * acc;
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    st4(blk + 8 * r, make_float4(X[r][0], X[r][1], X[r][2], X[r][3]));
-    st4(blk + 8 * r + 4, make_float4(X[r][4], X[r][5], X[r][6], X[r][7]));
-  }
+M4_DEV float2 fma2(float2 a, float b, float2 c) {
+#ifdef M4_FFMA2
+  unsigned long long ar, br, cr, dr;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(ar) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1,%1};" : "=l"(br) : "f"(b));
+  asm("mov.b64 %0, {%1,%2};" : "=l"(cr) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dr) : "l"(ar), "l"(br), "l"(cr));
+  float2 d;
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dr));
+  return d;
+#else
+  return make_float2(fmaf(a.x, b, c.x), fmaf(a.y, b, c.y));
+#endif
 }
 
-// Stage the 8 diagonal 8x8 blocks of the lane-distributed factor into shared
-// memory and invert them (lanes 0..7 one block each).
-M4_DEV void stage_and_invert_blocks(const float (&L)[SLOTS], float* blk, int lane, int a, int b) {
+struct SolveSmem {
+  float4 E[NPAIR / 2][32];       // running evidence (pairs 2q, 2q+1 per lane)
+  float flC[64];                 // floor[b + 8n] at b*8 + n
+  float w[64];                   // w = L^-1 q (forward) / u = L^-1 g (backward)
+  float y[64];                   // solution
+  union {
+    struct {
+      float2 kP[32];             // (k[a + 8p], k[a + 4 + 8p]) at a*8 + p
+      float kC[64];              // k[b + 8n] at b*8 + n
+      float qC[64];              // q[b + 8n] at b*8 + n
+      float2 col[2][32];         // column broadcast, pairs at a*8 + p
+      float colw[2][4];          // bordered-row entry per a
+    } f;
+    struct {
+      float T[8 * 36];           // diagonal blocks, packed lower tri(r, c)
+      float X[8 * 36];           // their inverses
+    } s;
+  } u;
+};
+
+// Stage the diagonal blocks and invert them (lanes 0..7, one block each).
+// Diagonal entries hold reciprocal pivots 1/L_rr; X = L_block^-1.
+M4_DEV void invert_blocks(const float2 (&L)[NPAIR], SolveSmem& sm, int lane, int a, int b) {
   __syncwarp();
 #pragma unroll
   for (int J = 0; J < 8; ++J) {
-    blk[J * 64 + a * 8 + b] = L[slot_of(2 * J, J)];
-    blk[J * 64 + (a + 4) * 8 + b] = L[slot_of(2 * J + 1, J)];
+    const float2 d = L[pair_of(J, J)];
+    if (a >= b) sm.u.s.T[J * 36 + tri(a, b)] = d.x;
+    if (a + 4 >= b) sm.u.s.T[J * 36 + tri(a + 4, b)] = d.y;
   }
   __syncwarp();
-  if (lane < 8) invert_lower8(blk + lane * 64);
+  if (lane < 8) {
+    const float* T = sm.u.s.T + lane * 36;
+    float* X = sm.u.s.X + lane * 36;
+    // In place, column by column: column c of X only overwrites entries that
+    // later columns (k > c) never read; the diagonal is unchanged.
+    float t[36];
+#pragma unroll
+    for (int i = 0; i < 36; ++i) t[i] = T[i];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+#pragma unroll
+      for (int r = c + 1; r < 8; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = c; k < r; ++k) acc = fmaf(t[tri(r, k)], t[tri(k, c)], acc);
+        t[tri(r, c)] = -t[tri(r, r)] * acc;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 36; ++i) X[i] = t[i];
+  }
   __syncwarp();
 }
 
-// Blocked back-substitution y = L^-T w. `w` is a 64-vector in shared memory;
-// result returned distributed: yr[m] = y[a + 4m]; y also written to ysm.
-M4_DEV void back_substitute(const float (&L)[SLOTS], const float* blk, const float* w, float* ysm,
-                            float (&yr)[16], int a, int b) {
+M4_DEV float xblk(const SolveSmem& sm, int J, int r, int c) {
+  return r >= c ? sm.u.s.X[J * 36 + tri(r, c)] : 0.f;
+}
+
+// Blocked back-substitution y = L^-T w (w in smem). yr2[K] = (y[8K+a], y[8K+a+4]);
+// y also written to ysm.
+M4_DEV void back_substitute(const float2 (&L)[NPAIR], const SolveSmem& sm, const float* w, float* ysm,
+                            int a, int b) {
+  float2 yr2[8];
 #pragma unroll
   for (int J = 7; J >= 0; --J) {
     float sp = 0.f;
 #pragma unroll
     for (int K = J + 1; K < 8; ++K) {
-      sp = fmaf(L[slot_of(2 * K, J)], yr[2 * K], sp);
-      sp = fmaf(L[slot_of(2 * K + 1, J)], yr[2 * K + 1], sp);
+      sp = fmaf(L[pair_of(K, J)].x, yr2[K].x, sp);
+      sp = fmaf(L[pair_of(K, J)].y, yr2[K].y, sp);
     }
     sp += __shfl_xor_sync(0xffffffffu, sp, 8);
     sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-    const float x = w[8 * J + b] - sp;                 // x[b] on lanes (., b)
-    const float xa = __shfl_sync(0xffffffffu, x, a);     // x[a]
+    const float x = w[8 * J + b] - sp;                   // x[b] on lanes (., b)
+    const float xa = __shfl_sync(0xffffffffu, x, a);       // x[a]
     const float xa4 = __shfl_sync(0xffffffffu, x, a + 4);  // x[a + 4]
-    float p = blk[J * 64 + a * 8 + b] * xa;
-    p = fmaf(blk[J * 64 + (a + 4) * 8 + b], xa4, p);
+    float p = xblk(sm, J, a, b) * xa;
+    p = fmaf(xblk(sm, J, a + 4, b), xa4, p);
     p += __shfl_xor_sync(0xffffffffu, p, 8);
-    p += __shfl_xor_sync(0xffffffffu, p, 16);          // y[8J + b]
-    yr[2 * J] = __shfl_sync(0xffffffffu, p, a);
-    yr[2 * J + 1] = __shfl_sync(0xffffffffu, p, a + 4);
+    p += __shfl_xor_sync(0xffffffffu, p, 16);            // y[8J + b]
+    yr2[J] = make_float2(__shfl_sync(0xffffffffu, p, a), __shfl_sync(0xffffffffu, p, a + 4));
     if (a == 0) ysm[8 * J + b] = p;
   }
 }
 
-// Blocked forward substitution u = L^-1 g. `g` is a 64-vector in shared
-// memory; u written to usm (64 floats).
-M4_DEV void forward_substitute(const float (&L)[SLOTS], const float* blk, const float* g, float* usm,
+// Blocked forward substitution u = L^-1 g (g in smem); u written to usm.
+M4_DEV void forward_substitute(const float2 (&L)[NPAIR], const SolveSmem& sm, const float* g, float* usm,
                                int a, int b) {
   float ub[8];
+  const int src = (b & 3) * 8;
 #pragma unroll
   for (int J = 0; J < 8; ++J) {
     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
     for (int K = 0; K < J; ++K) {
-      s0 = fmaf(L[slot_of(2 * J, K)], ub[K], s0);
-      s1 = fmaf(L[slot_of(2 * J + 1, K)], ub[K], s1);
+      s0 = fmaf(L[pair_of(J, K)].x, ub[K], s0);
+      s1 = fmaf(L[pair_of(J, K)].y, ub[K], s1);
     }
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
       s0 += __shfl_xor_sync(0xffffffffu, s0, o);
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
     }
-    const float x0 = g[8 * J + a] - s0;      // x[a]     on lanes (a, .)
-    const float x1 = g[8 * J + a + 4] - s1;  // x[a + 4]
-    const int src = (b & 3) * 8;
+    const float x0 = g[8 * J + a] - s0;       // x[a]
+    const float x1 = g[8 * J + a + 4] - s1;   // x[a + 4]
     const float t0 = __shfl_sync(0xffffffffu, x0, src);
     const float t1 = __shfl_sync(0xffffffffu, x1, src);
-    const float xb = b < 4 ? t0 : t1;        // x[b]
-    float p0 = blk[J * 64 + a * 8 + b] * xb;
-    float p1 = blk[J * 64 + (a + 4) * 8 + b] * xb;
+    const float xb = b < 4 ? t0 : t1;         // x[b]
+    float p0 = xblk(sm, J, a, b) * xb;
+    float p1 = xblk(sm, J, a + 4, b) * xb;
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
       p0 += __shfl_xor_sync(0xffffffffu, p0, o);
       p1 += __shfl_xor_sync(0xffffffffu, p1, o);
     }
-    // p0 = u[8J + a], p1 = u[8J + a + 4] on lanes (a, .)
     const float u0 = __shfl_sync(0xffffffffu, p0, src);
     const float u1 = __shfl_sync(0xffffffffu, p1, src);
-    ub[J] = b < 4 ? u0 : u1;                 // u[8J + b]
+    ub[J] = b < 4 ? u0 : u1;                  // u[8J + b]
     if (b == 0) { usm[8 * J + a] = p0; usm[8 * J + a + 4] = p1; }
   }
   __syncwarp();
 }
 
-struct SolveSmem {
-  float E[SLOTS / 4][32][4];   // running evidence, lane slot layout
-  float kR[64];                // k[a + 4m] at a*16 + m
-  float kC[64];                // k[b + 8n] at b*8 + n
-  float qC[64];                // q[b + 8n] at b*8 + n
-  float flC[64];               // floor[b + 8n] at b*8 + n
-  float w[64];                 // w = L^-1 q (or u = L^-1 g)
-  float y[64];                 // solution
-  union {
-    float col[2][144];         // column broadcast: R layout a*20+m, C layout 80+b*8+n
-    float blk[8 * 64];         // diagonal blocks / inverses
-  } u;
-};
+template <int JN>
+M4_DEV void store_column(float2* dst, const float2 (&A)[NPAIR]) {
+  if constexpr (JN & 1) dst[JN] = A[pair_of(JN, JN)];
+  constexpr int S = (JN + 1) & ~1;
+#pragma unroll
+  for (int p = S; p < 8; p += 2) {
+    const float2 u = A[pair_of(p, JN)], v = A[pair_of(p + 1, JN)];
+    *reinterpret_cast<float4*>(dst + p) = make_float4(u.x, u.y, v.x, v.y);
+  }
+}
+
+// One right-looking column step on unscaled columns U (L[:, j] = U[:, j]/sqrt(U_jj)).
+template <int J>
+M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
+  constexpr int JN = J >> 3, JB = J & 7, JH = (J >> 2) & 1, JA = J & 3;
+  float2* cb = sm.u.f.col[J & 1];
+  float* cw = sm.u.f.colw[J & 1];
+  if (b == JB) {
+    store_column<JN>(cb + a * 8, A);
+    cw[a] = wr[JN];
+  }
+  __syncwarp();
+  const float piv = reinterpret_cast<const float*>(cb)[(JA * 8 + JN) * 2 + JH];
+  const float r = rsqrtf(piv);
+  const float r2 = r * r;
+  rc[JN] = (b == JB) ? r : rc[JN];
+  float C[8];
+  {
+    const float2* cs = cb + (b & 3) * 8;
+    if constexpr (JN & 1) C[JN] = (b >= 4 ? cs[JN].y : cs[JN].x) * r2;
+#pragma unroll
+    for (int n = (JN + 1) & ~1; n < 8; n += 2) {
+      const float4 v = *reinterpret_cast<const float4*>(cs + n);
+      C[n] = (b >= 4 ? v.y : v.x) * r2;
+      C[n + 1] = (b >= 4 ? v.w : v.z) * r2;
+    }
+  }
+  C[JN] = (b > JB) ? C[JN] : 0.f;
+  const float rw = cw[a];
+#pragma unroll
+  for (int p = JN; p < 8; ++p) {
+    float2 rv = cb[a * 8 + p];
+    if (p == JN) {
+      rv.x = (a > JB) ? rv.x : 0.f;
+      rv.y = (a + 4 > JB) ? rv.y : 0.f;
+    }
+    const float2 nr = make_float2(-rv.x, -rv.y);
+#pragma unroll
+    for (int n = JN; n <= p; ++n) A[pair_of(p, n)] = fma2(nr, C[n], A[pair_of(p, n)]);
+  }
+#pragma unroll
+  for (int n = JN; n < 8; ++n) wr[n] = fmaf(-rw, C[n], wr[n]);
+}
+
+template <int J>
+M4_DEV void factor_all(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
+  factor_step<J>(A, wr, rc, sm, a, b);
+  if constexpr (J + 1 < KD) factor_all<J + 1>(A, wr, rc, sm, a, b);
+}
 
 // ---------------------------------------------------------------------------
 // memread_solve: per-token Cholesky factor + solve, L stored for backward.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(32 * WARPS) solve_kernel(
+__global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ queries,
     const float* __restrict__ beta, const float* __restrict__ log_decay,
     const float* __restrict__ floor_, const float* __restrict__ s_start,
@@ -299,16 +381,15 @@ __global__ void __launch_bounds__(32 * WARPS) solve_kernel(
   SolveSmem& sm = smem_all[warp];
   const int sub = wid % nsub, bh = wid / nsub, bb = bh / H, h = bh % H;
 
-  // Evidence at the sub-chunk start into the lane slot layout.
   {
     const float* src = s_start + (size_t(bh) * nsub + sub) * KD * KD;
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int m = 2 * n; m < 16; ++m) {
-        const int s = slot_of(m, n);
-        sm.E[s >> 2][lane][s & 3] = src[(a + 4 * m) * KD + b + 8 * n];
-      }
+    for (int q = 0; q < NPAIR; ++q) {
+      const int p = pair_p(q), n = pair_n(q);
+      float* e = reinterpret_cast<float*>(&sm.E[q >> 1][lane]) + 2 * (q & 1);
+      e[0] = src[(a + 8 * p) * KD + b + 8 * n];
+      e[1] = src[(a + 4 + 8 * p) * KD + b + 8 * n];
+    }
     if (a == 0) {
 #pragma unroll
       for (int n = 0; n < 8; ++n) sm.flC[b * 8 + n] = floor_[h * KD + b + 8 * n];
@@ -319,20 +400,19 @@ __global__ void __launch_bounds__(32 * WARPS) solve_kernel(
   for (int tt = 0; tt < SUB; ++tt) {
     const int t = sub * SUB + tt;
     const bool live = t < T;
-    // Stage k (lanes 0..15) and q (lanes 16..31) in permuted layouts.
     {
       const int l = lane & 15;
       const float* src = (lane < 16 ? keys : queries) + ((size_t(bb) * T + t) * H + h) * KD + 4 * l;
-      float4 v4 = live ? ld4(src) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 v4 = live ? ld4(src) : make_float4(0.f, 0.f, 0.f, 0.f);
       const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int i = 4 * l + e;
         if (lane < 16) {
-          sm.kR[(i & 3) * 16 + (i >> 2)] = vv[e];
-          sm.kC[(i & 7) * 8 + (i >> 3)] = vv[e];
+          reinterpret_cast<float*>(sm.u.f.kP)[((i & 3) * 8 + (i >> 3)) * 2 + ((i >> 2) & 1)] = vv[e];
+          sm.u.f.kC[(i & 7) * 8 + (i >> 3)] = vv[e];
         } else {
-          sm.qC[(i & 7) * 8 + (i >> 3)] = vv[e];
+          sm.u.f.qC[(i & 7) * 8 + (i >> 3)] = vv[e];
         }
       }
     }
@@ -340,89 +420,48 @@ __global__ void __launch_bounds__(32 * WARPS) solve_kernel(
     const float lam = live ? expf(log_decay[(size_t(bb) * T + t) * H + h]) : 1.f;
     __syncwarp();
 
-    float A[SLOTS];
+    float2 A[NPAIR];
     float wr[8];
     {
-      float kr[16], kc[8], fl[8];
+      float2 kr[8];
+      float kc[8];
 #pragma unroll
-      for (int m = 0; m < 16; m += 4) {
-        float4 v4 = ld4(&sm.kR[a * 16 + m]);
-        kr[m] = bet * v4.x; kr[m + 1] = bet * v4.y; kr[m + 2] = bet * v4.z; kr[m + 3] = bet * v4.w;
+      for (int p = 0; p < 8; p += 2) {
+        const float4 v = *reinterpret_cast<const float4*>(&sm.u.f.kP[a * 8 + p]);
+        kr[p] = make_float2(bet * v.x, bet * v.y);
+        kr[p + 1] = make_float2(bet * v.z, bet * v.w);
       }
 #pragma unroll
       for (int n = 0; n < 8; n += 4) {
-        float4 v4 = ld4(&sm.kC[b * 8 + n]);
-        kc[n] = v4.x; kc[n + 1] = v4.y; kc[n + 2] = v4.z; kc[n + 3] = v4.w;
-        float4 f4 = ld4(&sm.flC[b * 8 + n]);
-        fl[n] = f4.x; fl[n + 1] = f4.y; fl[n + 2] = f4.z; fl[n + 3] = f4.w;
-        float4 q4 = ld4(&sm.qC[b * 8 + n]);
-        wr[n] = a == 0 ? q4.x : 0.f; wr[n + 1] = a == 0 ? q4.y : 0.f;
-        wr[n + 2] = a == 0 ? q4.z : 0.f; wr[n + 3] = a == 0 ? q4.w : 0.f;
+        const float4 k4 = ld4(&sm.u.f.kC[b * 8 + n]);
+        kc[n] = k4.x; kc[n + 1] = k4.y; kc[n + 2] = k4.z; kc[n + 3] = k4.w;
       }
 #pragma unroll
-      for (int q4 = 0; q4 < SLOTS / 4; ++q4) {
-        float4 e4 = ld4(sm.E[q4][lane]);
-        float ev[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int s = 4 * q4 + e;
-          // decode slot -> (m, n) at compile time
-          int n = 0;
-#pragma unroll
-          for (int nn = 1; nn < 8; ++nn) if (s >= slot_of(2 * nn, nn)) n = nn;
-          const int m = s - slot_of(2 * n, n) + 2 * n;
-          ev[e] = fmaf(kr[m], kc[n], lam * ev[e]);
-          A[s] = ev[e];
-        }
-        st4(sm.E[q4][lane], make_float4(ev[0], ev[1], ev[2], ev[3]));
-      }
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        A[slot_of(2 * n, n)] += (b == a) ? fl[n] : 0.f;
-        A[slot_of(2 * n + 1, n)] += (b == a + 4) ? fl[n] : 0.f;
+      for (int q4 = 0; q4 < NPAIR / 2; ++q4) {
+        const float4 e = sm.E[q4][lane];
+        const int q0 = 2 * q4, q1 = 2 * q4 + 1;
+        const float2 e0 = fma2(kr[pair_p(q0)], kc[pair_n(q0)], make_float2(lam * e.x, lam * e.y));
+        const float2 e1 = fma2(kr[pair_p(q1)], kc[pair_n(q1)], make_float2(lam * e.z, lam * e.w));
+        sm.E[q4][lane] = make_float4(e0.x, e0.y, e1.x, e1.y);
+        A[q0] = e0;
+        A[q1] = e1;
       }
     }
+    // Floor on the diagonal (pair (n, n): .x if b == a, .y if b == a + 4) and
+    // the query as the bordered row (rows 64.., lanes a == 0).
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float f = sm.flC[b * 8 + n];
+      A[pair_of(n, n)].x += (b == a) ? f : 0.f;
+      A[pair_of(n, n)].y += (b == a + 4) ? f : 0.f;
+      wr[n] = a == 0 ? sm.u.f.qC[b * 8 + n] : 0.f;
+    }
 
-    // Right-looking Cholesky on unscaled columns U (L[:, j] = U[:, j] / sqrt(U_jj)).
     float rc[8];
 #pragma unroll
     for (int n = 0; n < 8; ++n) rc[n] = 0.f;
-#pragma unroll
-    for (int j = 0; j < KD; ++j) {
-      const int jn = j >> 3, jb = j & 7, jm = j >> 2, ja = j & 3;
-      float* cb = sm.u.col[j & 1];
-      if (b == jb) {
-#pragma unroll
-        for (int m = 2 * jn; m < 16; ++m) {
-          const float v = A[slot_of(m, jn)];
-          cb[a * 20 + m] = v;
-          const int row = a + 4 * m;
-          cb[80 + (row & 7) * 8 + (row >> 3)] = v;
-        }
-        cb[a * 20 + 16] = wr[jn];
-      }
-      __syncwarp();
-      const float piv = cb[ja * 20 + jm];
-      const float r = rsqrtf(piv);
-      const float r2 = r * r;
-      rc[jn] = (b == jb) ? r : rc[jn];
-      float R[17], C[8];
-#pragma unroll
-      for (int m = jm; m < 17; ++m) R[m] = cb[a * 20 + m];
-      R[jm] = (a > ja) ? R[jm] : 0.f;
-#pragma unroll
-      for (int n = jn; n < 8; ++n) C[n] = cb[80 + b * 8 + n] * r2;
-      C[jn] = (b > jb) ? C[jn] : 0.f;
-#pragma unroll
-      for (int n = jn; n < 8; ++n) {
-#pragma unroll
-        for (int m = (2 * n > jm ? 2 * n : jm); m < 16; ++m)
-          A[slot_of(m, n)] = fmaf(-R[m], C[n], A[slot_of(m, n)]);
-        wr[n] = fmaf(-R[16], C[n], wr[n]);
-      }
-    }
+    factor_all<0>(A, wr, rc, sm, a, b);
 
-    // w = L^-1 q (bordered row), variance = |w|^2.
     float vpart = 0.f;
     if (a == 0) {
 #pragma unroll
@@ -438,23 +477,24 @@ __global__ void __launch_bounds__(32 * WARPS) solve_kernel(
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
 #pragma unroll
-      for (int m = 2 * n; m < 16; ++m) A[slot_of(m, n)] *= rc[n];
-      float& d0 = A[slot_of(2 * n, n)];
-      float& d1 = A[slot_of(2 * n + 1, n)];
-      d0 = (b == a) ? rc[n] : (a < b ? 0.f : d0);
-      d1 = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d1);
+      for (int p = n; p < 8; ++p) {
+        A[pair_of(p, n)].x *= rc[n];
+        A[pair_of(p, n)].y *= rc[n];
+      }
+      float2& d = A[pair_of(n, n)];
+      d.x = (b == a) ? rc[n] : (a < b ? 0.f : d.x);
+      d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
     }
     {
       float* dst = Lst + (size_t(bh) * Tp + t) * LSTRIDE;
 #pragma unroll
-      for (int q4 = 0; q4 < SLOTS / 4; ++q4)
+      for (int q4 = 0; q4 < NPAIR / 2; ++q4)
         st4_stream(dst + (q4 * 32 + lane) * 4,
-                   make_float4(A[4 * q4], A[4 * q4 + 1], A[4 * q4 + 2], A[4 * q4 + 3]));
+                   make_float4(A[2 * q4].x, A[2 * q4].y, A[2 * q4 + 1].x, A[2 * q4 + 1].y));
     }
 
-    stage_and_invert_blocks(A, sm.u.blk, lane, a, b);
-    float yr[16];
-    back_substitute(A, sm.u.blk, sm.w, sm.y, yr, a, b);
+    invert_blocks(A, sm, lane, a, b);
+    back_substitute(A, sm, sm.w, sm.y, a, b);
     __syncwarp();
     if (lane < 16) st4(Y + (size_t(bh) * Tp + t) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
     if (live && lane == 0) variance[(size_t(bb) * T + t) * H + h] = var;
@@ -463,39 +503,77 @@ __global__ void __launch_bounds__(32 * WARPS) solve_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Chunk-product kernels (one CTA of 256 threads per (batch, chunk, head)).
-// Thread t owns rows ty + 16 i (i < 4) and columns tx + 16 j, ty = t/16, tx = t%16.
-// Tiles are stored with odd strides so row and column reads are conflict-free.
+// Chunk-product kernels: one CTA of 8 warps per (batch, 64-token chunk, head)
+// (carry: one per (batch, head)). The products run on tensor cores as m16n8k8
+// TF32 MMAs on a two-term split of every fp32 operand (hi = tf32(x),
+// lo = tf32(x - hi)) with three products per tile (lo*hi + hi*lo + hi*hi):
+// about 2^-22 relative error, inside the float32 tolerance of the reference
+// (whose einsums run at Precision.HIGHEST, lm/kernels/mamba4_fused.py:411-447).
+// Warp w owns rows 16 (w % 4) .. +15 and column half w / 4 of each product.
 // ---------------------------------------------------------------------------
-constexpr int LD = KD + 1;
+constexpr int LD = 68;    // tile stride in floats (conflict-free A fragments)
+constexpr int CT = 256;   // threads per chunk CTA
 
-template <int NJ, int K, class FA, class FB>
-M4_DEV void mm(float (&acc)[4][NJ], int ty, int tx, FA fa, FB fb) {
-#pragma unroll 4
-  for (int k = 0; k < K; ++k) {
-    float av[4], bv[NJ];
+M4_DEV uint32_t to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+M4_DEV void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// acc[nt][e] += sum_k A(row0 + g + 8(e>>1), k) B(k, col0 + 8nt + 2c + (e&1)),
+// g = lane/4, c = lane%4, through element accessors fa(row, k), fb(k, col).
+template <int K, int NT, class FA, class FB>
+M4_DEV void gemm3(float (&acc)[NT][4], int row0, int col0, FA fa, FB fb) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll 2
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    const float av[4] = {fa(row0 + g, k0 + c), fa(row0 + g + 8, k0 + c), fa(row0 + g, k0 + c + 4),
+                         fa(row0 + g + 8, k0 + c + 4)};
+    uint32_t ah[4], al[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) av[i] = fa(ty + 16 * i, k);
+    for (int i = 0; i < 4; ++i) {
+      ah[i] = to_tf32(av[i]);
+      al[i] = to_tf32(av[i] - __uint_as_float(ah[i]));
+    }
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) bv[j] = fb(k, tx + 16 * j);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    for (int nt = 0; nt < NT; ++nt) {
+      const float b0 = fb(k0 + c, col0 + 8 * nt + g), b1 = fb(k0 + c + 4, col0 + 8 * nt + g);
+      const uint32_t bh[2] = {to_tf32(b0), to_tf32(b1)};
+      const uint32_t bl[2] = {to_tf32(b0 - __uint_as_float(bh[0])), to_tf32(b1 - __uint_as_float(bh[1]))};
+      mma_tf32(acc[nt], al, bh);
+      mma_tf32(acc[nt], ah, bl);
+      mma_tf32(acc[nt], ah, bh);
+    }
   }
 }
 
-template <int NJ>
-M4_DEV void zero(float (&acc)[4][NJ]) {
+template <int NT>
+M4_DEV void zero(float (&acc)[NT][4]) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < NJ; ++j) acc[i][j] = 0.f;
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 }
 
-// Chunk-local inclusive prefix of log_decay and the gates, by warp 0.
+// Visit accumulator elements: f(row, col, nt, e).
+template <int NT, class F>
+M4_DEV void each(int row0, int col0, F f) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) f(row0 + g + 8 * (e >> 1), col0 + 8 * nt + 2 * c + (e & 1), nt, e);
+}
+
+// Chunk-local inclusive prefix of log_decay, the gates and e^prefix (warp 0).
 M4_DEV void chunk_gates(int tid, int b, int T, int H, int h, int t0, const float* beta,
-                        const float* log_decay, float* pre, float* bet) {
+                        const float* log_decay, float* pre, float* bet, float* ept) {
   if (tid < 32) {
     float carry = 0.f;
 #pragma unroll
@@ -504,93 +582,85 @@ M4_DEV void chunk_gates(int tid, int b, int T, int H, int h, int t0, const float
       const float g = t < T ? log_decay[(size_t(b) * T + t) * H + h] : 0.f;
       const float inc = warp_inclusive_scan(g, tid) + carry;
       pre[tt] = inc;
+      ept[tt] = expf(inc);
       bet[tt] = t < T ? beta[(size_t(b) * T + t) * H + h] : 0.f;
       carry = __shfl_sync(0xffffffffu, inc, 31);
     }
   }
 }
 
-// Load a [64 tokens][W] chunk of a [B,T,H,W] tensor into a strided tile.
+// Load a [64 tokens][W] chunk of a [B,T,H,W] tensor into a tile of stride ld.
 template <int W>
 M4_DEV void load_tokens(float* tile, int ld, const float* src, int b, int T, int H, int h, int t0, int tid) {
-  for (int idx = tid; idx < CH * W; idx += 256) {
-    const int tt = idx / W, c = idx % W, t = t0 + tt;
-    tile[tt * ld + c] = t < T ? src[((size_t(b) * T + t) * H + h) * W + c] : 0.f;
+  for (int idx = tid; idx < CH * W / 4; idx += CT) {
+    const int tt = idx / (W / 4), c4 = idx % (W / 4), t = t0 + tt;
+    const float4 v = t < T ? ld4(src + ((size_t(b) * T + t) * H + h) * W + 4 * c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    st4(tile + tt * ld + 4 * c4, v);
   }
 }
 
-// Load a dense [R][64] row-major block into a strided tile.
+// Load a dense [rows][64] row-major block into a tile of stride LD.
 M4_DEV void load_block(float* tile, int rows, const float* src, int tid) {
-  for (int idx = tid; idx < rows * KD; idx += 256) tile[(idx / KD) * LD + idx % KD] = src[idx];
+  for (int idx = tid; idx < rows * KD / 4; idx += CT) st4(tile + (idx / 16) * LD + 4 * (idx % 16), ld4(src + 4 * idx));
 }
 
 template <int P>
-__global__ void __launch_bounds__(256) output_kernel(
+__global__ void __launch_bounds__(CT) output_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ values,
     const float* __restrict__ beta, const float* __restrict__ log_decay,
     const float* __restrict__ Y, const float* __restrict__ c_start, float* __restrict__ out) {
-  constexpr int LP = P + 1, NJ = P / 16;
+  constexpr int LP = P + 4, NTP = P / 16;
   extern __shared__ __align__(16) float sh[];
   float* Ys = sh;                 // [64][LD]
   float* Ks = Ys + CH * LD;       // [64][LD]
   float* Ms = Ks + CH * LD;       // [64][LD]
   float* Vs = Ms + CH * LD;       // [64][LP]
   float* C0 = Vs + CH * LP;       // [P][LD]
-  float* pre = C0 + P * LD;       // [64]
-  float* bet = pre + CH;          // [64]
+  float* pre = C0 + P * LD;
+  float* bet = pre + CH;
+  float* ept = bet + CH;
   const int Tp = (T + CH - 1) / CH * CH, nch = Tp / CH;
   const int ch = blockIdx.x % nch, bh = blockIdx.x / nch, b = bh / H, h = bh % H;
-  const int t0 = ch * CH, tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int t0 = ch * CH, tid = threadIdx.x, warp = tid >> 5;
+  const int row0 = 16 * (warp & 3), half = warp >> 2;
   load_block(Ys, CH, Y + (size_t(bh) * Tp + t0) * KD, tid);
   load_tokens<KD>(Ks, LD, keys, b, T, H, h, t0, tid);
   load_tokens<P>(Vs, LP, values, b, T, H, h, t0, tid);
   load_block(C0, P, c_start + (size_t(bh) * nch + ch) * P * KD, tid);
-  chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet);
+  chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
   __syncthreads();
   {
     float acc[4][4];
     zero(acc);
-    mm<4, KD>(acc, ty, tx, [&](int r, int k) { return Ys[r * LD + k]; },
-              [&](int k, int c) { return Ks[c * LD + k]; });
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = ty + 16 * i, c = tx + 16 * j;
-        Ms[r * LD + c] = c <= r ? acc[i][j] * bet[c] * expf(pre[r] - pre[c]) : 0.f;
-      }
+    gemm3<KD, 4>(acc, row0, 32 * half, [&](int r, int k) { return Ys[r * LD + k]; },
+                 [&](int k, int n) { return Ks[n * LD + k]; });
+    each<4>(row0, 32 * half, [&](int r, int n, int nt, int e) {
+      Ms[r * LD + n] = n <= r ? acc[nt][e] * bet[n] * expf(pre[r] - pre[n]) : 0.f;
+    });
   }
   __syncthreads();
-  float acc[4][NJ], inh[4][NJ];
+  float acc[NTP][4], inh[NTP][4];
   zero(acc);
   zero(inh);
-  mm<NJ, CH>(acc, ty, tx, [&](int r, int k) { return Ms[r * LD + k]; },
-             [&](int k, int c) { return Vs[k * LP + c]; });
-  mm<NJ, KD>(inh, ty, tx, [&](int r, int k) { return Ys[r * LD + k]; },
-             [&](int k, int c) { return C0[c * LD + k]; });
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = ty + 16 * i, t = t0 + r;
-    if (t >= T) continue;
-    const float e = expf(pre[r]);
-#pragma unroll
-    for (int j = 0; j < NJ; ++j)
-      out[((size_t(b) * T + t) * H + h) * P + tx + 16 * j] = fmaf(e, inh[i][j], acc[i][j]);
-  }
+  const int c0 = half * (P / 2);
+  gemm3<CH, NTP>(acc, row0, c0, [&](int r, int k) { return Ms[r * LD + k]; },
+                 [&](int k, int p) { return Vs[k * LP + p]; });
+  gemm3<KD, NTP>(inh, row0, c0, [&](int r, int k) { return Ys[r * LD + k]; },
+                 [&](int k, int p) { return C0[p * LD + k]; });
+  each<NTP>(row0, c0, [&](int r, int p, int nt, int e) {
+    const int t = t0 + r;
+    if (t < T) out[((size_t(b) * T + t) * H + h) * P + p] = fmaf(ept[r], inh[nt][e], acc[nt][e]);
+  });
 }
-
-// ---------------------------------------------------------------------------
-// Backward kernels.
-// ---------------------------------------------------------------------------
 
 // rhs_kernel: g_t = e^(P_t) C0^T dO_t + sum_s W[t,s] (dO_t . v_s) k_s + dvar_t q_t.
 template <int P>
-__global__ void __launch_bounds__(256) rhs_kernel(
+__global__ void __launch_bounds__(CT) rhs_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ values,
     const float* __restrict__ queries, const float* __restrict__ beta,
     const float* __restrict__ log_decay, const float* __restrict__ c_start,
     const float* __restrict__ d_out, const float* __restrict__ d_var, float* __restrict__ G) {
-  constexpr int LP = P + 1;
+  constexpr int LP = P + 4;
   extern __shared__ __align__(16) float sh[];
   float* Ks = sh;                 // [64][LD]
   float* Ms = Ks + CH * LD;       // [64][LD]
@@ -599,173 +669,161 @@ __global__ void __launch_bounds__(256) rhs_kernel(
   float* C0 = Vs + CH * LP;       // [P][LD]
   float* pre = C0 + P * LD;
   float* bet = pre + CH;
+  float* ept = bet + CH;
   const int Tp = (T + CH - 1) / CH * CH, nch = Tp / CH;
   const int ch = blockIdx.x % nch, bh = blockIdx.x / nch, b = bh / H, h = bh % H;
-  const int t0 = ch * CH, tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int t0 = ch * CH, tid = threadIdx.x, warp = tid >> 5;
+  const int row0 = 16 * (warp & 3), half = warp >> 2;
   load_tokens<KD>(Ks, LD, keys, b, T, H, h, t0, tid);
   load_tokens<P>(Os, LP, d_out, b, T, H, h, t0, tid);
   load_tokens<P>(Vs, LP, values, b, T, H, h, t0, tid);
   load_block(C0, P, c_start + (size_t(bh) * nch + ch) * P * KD, tid);
-  chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet);
+  chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
   __syncthreads();
   {
     float acc[4][4];
     zero(acc);
-    mm<4, P>(acc, ty, tx, [&](int r, int k) { return Os[r * LP + k]; },
-             [&](int k, int c) { return Vs[c * LP + k]; });
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = ty + 16 * i, c = tx + 16 * j;
-        Ms[r * LD + c] = c <= r ? acc[i][j] * bet[c] * expf(pre[r] - pre[c]) : 0.f;
-      }
+    gemm3<P, 4>(acc, row0, 32 * half, [&](int r, int k) { return Os[r * LP + k]; },
+                [&](int k, int s) { return Vs[s * LP + k]; });
+    each<4>(row0, 32 * half, [&](int r, int s, int nt, int e) {
+      Ms[r * LD + s] = s <= r ? acc[nt][e] * bet[s] * expf(pre[r] - pre[s]) : 0.f;
+    });
   }
   __syncthreads();
   float acc[4][4], inh[4][4];
   zero(acc);
   zero(inh);
-  mm<4, CH>(acc, ty, tx, [&](int r, int k) { return Ms[r * LD + k]; },
-            [&](int k, int c) { return Ks[k * LD + c]; });
-  mm<4, P>(inh, ty, tx, [&](int r, int k) { return Os[r * LP + k]; },
-           [&](int k, int c) { return C0[k * LD + c]; });
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = ty + 16 * i, t = t0 + r;
+  gemm3<CH, 4>(acc, row0, 32 * half, [&](int r, int k) { return Ms[r * LD + k]; },
+               [&](int k, int d) { return Ks[k * LD + d]; });
+  gemm3<P, 4>(inh, row0, 32 * half, [&](int r, int k) { return Os[r * LP + k]; },
+              [&](int k, int d) { return C0[k * LD + d]; });
+  each<4>(row0, 32 * half, [&](int r, int d, int nt, int e) {
+    const int t = t0 + r;
     const bool live = t < T;
-    const float e = expf(pre[r]);
     const float dv = live ? d_var[(size_t(b) * T + t) * H + h] : 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = tx + 16 * j;
-      const float q = live ? queries[((size_t(b) * T + t) * H + h) * KD + c] : 0.f;
-      G[(size_t(bh) * Tp + t) * KD + c] = fmaf(dv, q, fmaf(e, inh[i][j], acc[i][j]));
-    }
-  }
+    const float q = live ? queries[((size_t(b) * T + t) * H + h) * KD + d] : 0.f;
+    G[(size_t(bh) * Tp + t) * KD + d] = fmaf(dv, q, fmaf(ept[r], inh[nt][e], acc[nt][e]));
+  });
 }
 
+// ---------------------------------------------------------------------------
+// Backward kernels.
+// ---------------------------------------------------------------------------
 // zsolve_kernel: z_t = A_t^-1 g_t from the stored factor (one warp per token
 // at a time, 16 tokens per warp).
-__global__ void __launch_bounds__(32 * WARPS) zsolve_kernel(
+__global__ void __launch_bounds__(32 * WARPS, 4) zsolve_kernel(
     int B, int T, int H, const float* __restrict__ Lst, const float* __restrict__ G,
     float* __restrict__ Z) {
-  struct Smem {
-    float g[64];
-    float u[64];
-    float z[64];
-    float blk[8 * 64];
-  };
-  __shared__ Smem smem_all[WARPS];
+  extern __shared__ __align__(16) unsigned char zsolve_raw[];
+  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(zsolve_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int a = lane >> 3, b = lane & 7;
   const int Tp = (T + CH - 1) / CH * CH, nsub = Tp / SUB;
   const int wid = blockIdx.x * WARPS + warp;
   if (wid >= B * H * nsub) return;
-  Smem& sm = smem_all[warp];
+  SolveSmem& sm = smem_all[warp];
   const int sub = wid % nsub, bh = wid / nsub;
   for (int tt = 0; tt < SUB; ++tt) {
     const int t = sub * SUB + tt;
-    float L[SLOTS];
+    float2 L[NPAIR];
     const float* src = Lst + (size_t(bh) * Tp + t) * LSTRIDE;
 #pragma unroll
-    for (int q4 = 0; q4 < SLOTS / 4; ++q4) {
-      float4 v4 = __ldcs(reinterpret_cast<const float4*>(src + (q4 * 32 + lane) * 4));
-      L[4 * q4] = v4.x; L[4 * q4 + 1] = v4.y; L[4 * q4 + 2] = v4.z; L[4 * q4 + 3] = v4.w;
+    for (int q4 = 0; q4 < NPAIR / 2; ++q4) {
+      const float4 v4 = __ldcs(reinterpret_cast<const float4*>(src + (q4 * 32 + lane) * 4));
+      L[2 * q4] = make_float2(v4.x, v4.y);
+      L[2 * q4 + 1] = make_float2(v4.z, v4.w);
     }
-    if (lane < 16) st4(&sm.g[4 * lane], ld4(G + (size_t(bh) * Tp + t) * KD + 4 * lane));
-    stage_and_invert_blocks(L, sm.blk, lane, a, b);
-    forward_substitute(L, sm.blk, sm.g, sm.u, a, b);
-    float zr[16];
-    back_substitute(L, sm.blk, sm.u, sm.z, zr, a, b);
+    if (lane < 16) st4(&sm.y[4 * lane], ld4(G + (size_t(bh) * Tp + t) * KD + 4 * lane));
+    invert_blocks(L, sm, lane, a, b);
+    forward_substitute(L, sm, sm.y, sm.w, a, b);
+    back_substitute(L, sm, sm.w, sm.y, a, b);
     __syncwarp();
-    if (lane < 16) st4(Z + (size_t(bh) * Tp + t) * KD + 4 * lane, ld4(&sm.z[4 * lane]));
+    if (lane < 16) st4(Z + (size_t(bh) * Tp + t) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
     __syncwarp();
   }
 }
+
 
 // carry_kernel: per (batch, head), reverse over chunks:
 //   X_S = -sum_t e^(P_t) z_t y_t^T, X_C = sum_t e^(P_t) dO_t y_t^T,
 //   Sbar_end[n] = carry, carry = X_S[n] + e^(P_L) carry (same for C).
 // The final carries are the gradients of the initial state.
 template <int P>
-__global__ void __launch_bounds__(256) carry_kernel(
+__global__ void __launch_bounds__(CT) carry_kernel(
     int B, int T, int H, const float* __restrict__ beta, const float* __restrict__ log_decay,
     const float* __restrict__ Y, const float* __restrict__ Z, const float* __restrict__ d_out,
     const float* __restrict__ d_sfin, const float* __restrict__ d_cfin,
     float* __restrict__ sbar, float* __restrict__ cbar, float* __restrict__ d_init_s,
     float* __restrict__ d_init_c) {
-  constexpr int LP = P + 1, NJ = P / 16;
+  constexpr int LP = P + 4, NTP = P / 16;
   extern __shared__ __align__(16) float sh[];
   float* Ys = sh;               // [64][LD] rows t
   float* Zs = Ys + CH * LD;     // [64][LD]
   float* Os = Zs + CH * LD;     // [64][LP]
   float* pre = Os + CH * LP;
   float* bet = pre + CH;
+  float* ept = bet + CH;
   const int Tp = (T + CH - 1) / CH * CH, nch = Tp / CH;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
-  // carries: S [64 x 64] rows ty+16i, cols tx+16j; C [P x 64]: rows p = tx + 16 j', cols d = ty + 16 i
-  float cs[4][4], cc[4][NJ];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      cs[i][j] = d_sfin ? d_sfin[(size_t(bh) * KD + ty + 16 * i) * KD + tx + 16 * j] : 0.f;
-#pragma unroll
-    for (int j = 0; j < NJ; ++j)
-      cc[i][j] = d_cfin ? d_cfin[(size_t(bh) * P + tx + 16 * j) * KD + ty + 16 * i] : 0.f;
-  }
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int row0 = 16 * (warp & 3), half = warp >> 2;
+  const int cs0 = 32 * half, cc0 = half * (P / 2);
+  // cs[d][e] rows d, cols e; cc[d][p] = Cbar[p][d] (transposed).
+  float cs[4][4], cc[NTP][4];
+  each<4>(row0, cs0, [&](int d, int e, int nt, int i) {
+    cs[nt][i] = d_sfin ? d_sfin[(size_t(bh) * KD + d) * KD + e] : 0.f;
+  });
+  each<NTP>(row0, cc0, [&](int d, int p, int nt, int i) {
+    cc[nt][i] = d_cfin ? d_cfin[(size_t(bh) * P + p) * KD + d] : 0.f;
+  });
   for (int ch = nch - 1; ch >= 0; --ch) {
     const int t0 = ch * CH;
     float* sb = sbar + (size_t(bh) * nch + ch) * KD * KD;
     float* cbp = cbar + (size_t(bh) * nch + ch) * P * KD;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sb[(ty + 16 * i) * KD + tx + 16 * j] = cs[i][j];
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) cbp[(tx + 16 * j) * KD + ty + 16 * i] = cc[i][j];
-    }
-    __syncthreads();  // previous iteration's readers of Ys/Zs/Os are done
+    each<4>(row0, cs0, [&](int d, int e, int nt, int i) { sb[d * KD + e] = cs[nt][i]; });
+    each<NTP>(row0, cc0, [&](int d, int p, int nt, int i) { cbp[p * KD + d] = cc[nt][i]; });
+    __syncthreads();  // previous iteration's readers of the tiles are done
     load_block(Ys, CH, Y + (size_t(bh) * Tp + t0) * KD, tid);
     load_block(Zs, CH, Z + (size_t(bh) * Tp + t0) * KD, tid);
     load_tokens<P>(Os, LP, d_out, b, T, H, h, t0, tid);
-    chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet);
+    chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
     __syncthreads();
-    const float end = expf(pre[CH - 1]);
-    float xs[4][4], xc[4][NJ];
+    const float end = ept[CH - 1];
+    float xs[4][4], xc[NTP][4];
     zero(xs);
     zero(xc);
-    // xs[d][e] = sum_t e^(P_t) z_t[d] y_t[e]
-    mm<4, CH>(xs, ty, tx, [&](int r, int k) { return Zs[k * LD + r] * expf(pre[k]); },
-              [&](int k, int c) { return Ys[k * LD + c]; });
-    // xc[d][p] (transposed) = sum_t e^(P_t) y_t[d] dO_t[p]
-    mm<NJ, CH>(xc, ty, tx, [&](int r, int k) { return Ys[k * LD + r] * expf(pre[k]); },
-               [&](int k, int c) { return Os[k * LP + c]; });
+    gemm3<CH, 4>(xs, row0, cs0, [&](int d, int t) { return Zs[t * LD + d] * ept[t]; },
+                 [&](int t, int e) { return Ys[t * LD + e]; });
+    gemm3<CH, NTP>(xc, row0, cc0, [&](int d, int t) { return Ys[t * LD + d] * ept[t]; },
+                   [&](int t, int p) { return Os[t * LP + p]; });
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) cs[i][j] = fmaf(end, cs[i][j], -xs[i][j]);
+      for (int i = 0; i < 4; ++i) cs[nt][i] = fmaf(end, cs[nt][i], -xs[nt][i]);
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) cc[i][j] = fmaf(end, cc[i][j], xc[i][j]);
-    }
+    for (int nt = 0; nt < NTP; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cc[nt][i] = fmaf(end, cc[nt][i], xc[nt][i]);
   }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if (d_init_s) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) d_init_s[(size_t(bh) * KD + ty + 16 * i) * KD + tx + 16 * j] = cs[i][j];
-    }
-    if (d_init_c) {
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) d_init_c[(size_t(bh) * P + tx + 16 * j) * KD + ty + 16 * i] = cc[i][j];
-    }
-  }
+  if (d_init_s) each<4>(row0, cs0, [&](int d, int e, int nt, int i) { d_init_s[(size_t(bh) * KD + d) * KD + e] = cs[nt][i]; });
+  if (d_init_c) each<NTP>(row0, cc0, [&](int d, int p, int nt, int i) { d_init_c[(size_t(bh) * P + p) * KD + d] = cc[nt][i]; });
 }
 
-// grads_kernel: every input gradient of one chunk (chunk form, see header).
+// Sum a per-lane, per-row partial (rows r = row0 + g + 8*(e>>1)) over the 4
+// lanes of each row and store it at dst[r] (one writer per row and warp).
+M4_DEV void row_reduce_store(float v0, float v1, float* dst, int row0) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+  v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+  v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+  v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+  if (c == 0) { dst[row0 + g] = v0; dst[row0 + g + 8] = v1; }
+}
+
+// grads_kernel: every input gradient of one chunk (chunk form; the algebra
+// is written out in oracle/memread.py:chunked_backward).
 template <int P>
-__global__ void __launch_bounds__(256) grads_kernel(
+__global__ void __launch_bounds__(CT) grads_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ values,
     const float* __restrict__ beta, const float* __restrict__ log_decay,
     const float* __restrict__ Y, const float* __restrict__ Z, const float* __restrict__ s_start,
@@ -774,28 +832,31 @@ __global__ void __launch_bounds__(256) grads_kernel(
     const float* __restrict__ d_var, float* __restrict__ dk, float* __restrict__ dv,
     float* __restrict__ dq, float* __restrict__ dbeta, float* __restrict__ dlog,
     float* __restrict__ floor_part) {
-  constexpr int LP = P + 1, NJ = P / 16;
+  constexpr int LP = P + 4, NTP = P / 16;
   extern __shared__ __align__(16) float sh[];
   float* Ys = sh;                 // [64][LD]
   float* Zs = Ys + CH * LD;       // [64][LD]
   float* Ks = Zs + CH * LD;       // [64][LD]
   float* M1 = Ks + CH * LD;       // [64][LD]  W o GY
   float* M2 = M1 + CH * LD;       // [64][LD]  W o (OV - GZ)
-  float* Os = M2 + CH * LD;       // [64][LP]
+  float* Sb = M2 + CH * LD;       // [64][LD]  dS_end, later S0
+  float* Os = Sb + CH * LD;       // [64][LP]
   float* Vs = Os + CH * LP;       // [64][LP]
-  float* Sb = Vs + CH * LP;       // [64][LD] dS_end (later: S0)
-  float* Cb = Sb + CH * LD;       // [P][LD]  dC_end (later: C0)
+  float* Cb = Vs + CH * LP;       // [P][LD]   dC_end, later C0
   float* pre = Cb + P * LD;
   float* bet = pre + CH;
-  float* rowA = bet + CH;         // [64] sum_s dW W [t,.]
-  float* colA = rowA + CH;        // [64] sum_t dW W [.,s]  and dW D col sums
-  float* colB = colA + CH;        // [64]
-  float* wbar = colB + CH;        // [64] dw_s
-  float* extra = wbar + CH;       // [64] per-token e^P(-z S0 y + dO C0 y)
-  float* red = extra + CH;        // [64] misc reduction scratch
+  float* ept = bet + CH;
+  float* rowP = ept + CH;         // [2][64] half partials of sum_s dW W [t, s]
+  float* colP = rowP + 2 * CH;    // [4][64] row-block partials of sum_t dW W [t, s]
+  float* decP = colP + 4 * CH;    // [4][64] row-block partials of sum_t dW D [t, s]
+  float* wbP = decP + 4 * CH;     // [2][64] half partials of dw_s
+  float* exP = wbP + 2 * CH;      // [2][64] half partials of the per-token extra term
+  float* red = exP + 2 * CH;      // [64 + 16] scratch
   const int Tp = (T + CH - 1) / CH * CH, nch = Tp / CH, nsub = Tp / SUB;
   const int ch = blockIdx.x % nch, bh = blockIdx.x / nch, b = bh / H, h = bh % H;
-  const int t0 = ch * CH, tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+  const int t0 = ch * CH, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = 16 * (warp & 3), half = warp >> 2, rb = warp & 3;
+  const int c64 = 32 * half, cP = half * (P / 2);
   load_block(Ys, CH, Y + (size_t(bh) * Tp + t0) * KD, tid);
   load_block(Zs, CH, Z + (size_t(bh) * Tp + t0) * KD, tid);
   load_tokens<KD>(Ks, LD, keys, b, T, H, h, t0, tid);
@@ -803,202 +864,160 @@ __global__ void __launch_bounds__(256) grads_kernel(
   load_tokens<P>(Vs, LP, values, b, T, H, h, t0, tid);
   load_block(Sb, KD, sbar + (size_t(bh) * nch + ch) * KD * KD, tid);
   load_block(Cb, P, cbar + (size_t(bh) * nch + ch) * P * KD, tid);
-  chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet);
-  if (tid < CH) { rowA[tid] = 0.f; colA[tid] = 0.f; colB[tid] = 0.f; }
+  chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
   __syncthreads();
   const float pl = pre[CH - 1];
-  // GY, GZ, OV -> M1, M2, dW products.
+  // Phase 1: GY, GZ, OV -> M1, M2 and the dW reductions.
   {
     float gy[4][4], gz[4][4], ov[4][4];
     zero(gy); zero(gz); zero(ov);
-    mm<4, KD>(gy, ty, tx, [&](int r, int k) { return Ys[r * LD + k]; },
-              [&](int k, int c) { return Ks[c * LD + k]; });
-    mm<4, KD>(gz, ty, tx, [&](int r, int k) { return Zs[r * LD + k]; },
-              [&](int k, int c) { return Ks[c * LD + k]; });
-    mm<4, P>(ov, ty, tx, [&](int r, int k) { return Os[r * LP + k]; },
-             [&](int k, int c) { return Vs[c * LP + k]; });
-    float rsum[4] = {0.f, 0.f, 0.f, 0.f}, csum[4] = {0.f, 0.f, 0.f, 0.f}, cdec[4] = {0.f, 0.f, 0.f, 0.f};
+    gemm3<KD, 4>(gy, row0, c64, [&](int r, int k) { return Ys[r * LD + k]; },
+                 [&](int k, int s) { return Ks[s * LD + k]; });
+    gemm3<KD, 4>(gz, row0, c64, [&](int r, int k) { return Zs[r * LD + k]; },
+                 [&](int k, int s) { return Ks[s * LD + k]; });
+    gemm3<P, 4>(ov, row0, c64, [&](int r, int k) { return Os[r * LP + k]; },
+                [&](int k, int s) { return Vs[s * LP + k]; });
+    float r0 = 0.f, r1 = 0.f, cw[4][2], cd[4][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int nt = 0; nt < 4; ++nt) cw[nt][0] = cw[nt][1] = cd[nt][0] = cd[nt][1] = 0.f;
+    each<4>(row0, c64, [&](int t, int s, int nt, int e) {
+      const bool on = s <= t;
+      const float dec = on ? expf(pre[t] - pre[s]) : 0.f;
+      const float w = dec * bet[s];
+      const float diff = ov[nt][e] - gz[nt][e];
+      M1[t * LD + s] = w * gy[nt][e];
+      M2[t * LD + s] = w * diff;
+      const float dw = on ? gy[nt][e] * diff : 0.f;
+      if (e < 2) r0 = fmaf(dw, w, r0); else r1 = fmaf(dw, w, r1);
+      cw[nt][e & 1] = fmaf(dw, w, cw[nt][e & 1]);
+      cd[nt][e & 1] = fmaf(dw, dec, cd[nt][e & 1]);
+    });
+    row_reduce_store(r0, r1, rowP + half * CH, row0);
+    // Column partials: reduce over the 8 row groups g of this warp.
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = ty + 16 * i, c = tx + 16 * j;
-        const bool on = c <= r;
-        const float dec = on ? expf(pre[r] - pre[c]) : 0.f;
-        const float w = dec * bet[c];
-        const float diff = ov[i][j] - gz[i][j];
-        M1[r * LD + c] = w * gy[i][j];
-        M2[r * LD + c] = w * diff;
-        const float dw = on ? gy[i][j] * diff : 0.f;
-        rsum[i] = fmaf(dw, w, rsum[i]);
-        csum[j] = fmaf(dw, w, csum[j]);
-        cdec[j] = fmaf(dw, dec, cdec[j]);
-      }
-    // Reduce over the 16 tx lanes (rows) and 16 ty groups (columns) via smem.
-    // Row sums: lanes with the same ty share a half-warp.
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float v = rsum[i];
+      for (int e = 0; e < 2; ++e) {
+        float a = cw[nt][e], d = cd[nt][e];
 #pragma unroll
-      for (int o = 1; o < 16; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (tx == 0) rowA[ty + 16 * i] = v;
-    }
-    __syncthreads();
-    // Column sums: accumulate deterministically by ty in order.
-    for (int g = 0; g < 16; ++g) {
-      if (ty == g) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          colA[tx + 16 * j] += csum[j];
-          colB[tx + 16 * j] += cdec[j];
+        for (int o = 4; o < 32; o <<= 1) {
+          a += __shfl_xor_sync(0xffffffffu, a, o);
+          d += __shfl_xor_sync(0xffffffffu, d, o);
+        }
+        if (lane < 4) {
+          const int s = c64 + 8 * nt + 2 * lane + e;
+          colP[rb * CH + s] = a;
+          decP[rb * CH + s] = d;
         }
       }
-      __syncthreads();
-    }
-  }
-  // dw_s = k^T Sb k + v^T Cb k ; also (Sb + Sb^T) k and Cb^T v rows for dK, Cb k for dV.
-  float tk[4][4], ck[4][NJ];
-  {
-    zero(tk);
-    // tk[s][d] = sum_e K[s][e] (Sb[d][e] + Sb[e][d]) + sum_p V[s][p] Cb[p][d]
-    mm<4, KD>(tk, ty, tx, [&](int r, int k) { return Ks[r * LD + k]; },
-              [&](int k, int c) { return Sb[c * LD + k] + Sb[k * LD + c]; });
-    mm<4, P>(tk, ty, tx, [&](int r, int k) { return Vs[r * LP + k]; },
-             [&](int k, int c) { return Cb[k * LD + c]; });
-    zero(ck);
-    // ck[s][p] = sum_d Cb[p][d] K[s][d]
-    mm<NJ, KD>(ck, ty, tx, [&](int r, int k) { return Ks[r * LD + k]; },
-               [&](int k, int c) { return Cb[c * LD + k]; });
-    // dw_s = 1/2 k.(Sb+Sb^T)k ... computed as k.(tk_S) needs split: recompute directly.
-    float part[4] = {0.f, 0.f, 0.f, 0.f};
-    // k^T Sb k = 1/2 k^T (Sb + Sb^T) k ; v^T Cb k = sum_p v_p (Cb k)_p
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int s = ty + 16 * i;
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) part[i] = fmaf(Vs[s * LP + tx + 16 * j], ck[i][j], part[i]);
-    }
-    float sk[4][4];
-    zero(sk);
-    mm<4, KD>(sk, ty, tx, [&](int r, int k) { return Ks[r * LD + k]; },
-              [&](int k, int c) { return Sb[c * LD + k]; });  // sk[s][d] = (Sb k_s)[d]
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int s = ty + 16 * i;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) part[i] = fmaf(Ks[s * LD + tx + 16 * j], sk[i][j], part[i]);
-      float v = part[i];
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (tx == 0) wbar[s] = v;
-    }
   }
   __syncthreads();
-  // dK and dV.
+  // Phase 2: dK and dV (rows s) and dw_s.
   {
-    float acc[4][4];
-    zero(acc);
-    // -(M1)^T Z + (M2)^T Y : acc[s][d] = sum_t (-M1[t][s] Z[t][d] + M2[t][s] Y[t][d])
-    mm<4, CH>(acc, ty, tx, [&](int r, int k) { return -M1[k * LD + r]; },
-              [&](int k, int c) { return Zs[k * LD + c]; });
-    mm<4, CH>(acc, ty, tx, [&](int r, int k) { return M2[k * LD + r]; },
-              [&](int k, int c) { return Ys[k * LD + c]; });
-    float accv[4][NJ];
-    zero(accv);
-    mm<NJ, CH>(accv, ty, tx, [&](int r, int k) { return M1[k * LD + r]; },
-               [&](int k, int c) { return Os[k * LP + c]; });
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int s = ty + 16 * i, t = t0 + s;
-      if (t >= T) continue;
-      const float ws = bet[s] * expf(pl - pre[s]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        dk[((size_t(b) * T + t) * H + h) * KD + tx + 16 * j] = fmaf(ws, tk[i][j], acc[i][j]);
-#pragma unroll
-      for (int j = 0; j < NJ; ++j)
-        dv[((size_t(b) * T + t) * H + h) * P + tx + 16 * j] = fmaf(ws, ck[i][j], accv[i][j]);
-    }
+    float acc[4][4], tks[4][4], tkc[4][4];
+    zero(acc); zero(tks); zero(tkc);
+    gemm3<CH, 4>(acc, row0, c64, [&](int s, int t) { return -M1[t * LD + s]; },
+                 [&](int t, int d) { return Zs[t * LD + d]; });
+    gemm3<CH, 4>(acc, row0, c64, [&](int s, int t) { return M2[t * LD + s]; },
+                 [&](int t, int d) { return Ys[t * LD + d]; });
+    gemm3<KD, 4>(tks, row0, c64, [&](int s, int e) { return Ks[s * LD + e]; },
+                 [&](int e, int d) { return Sb[e * LD + d] + Sb[d * LD + e]; });
+    gemm3<P, 4>(tkc, row0, c64, [&](int s, int p) { return Vs[s * LP + p]; },
+                [&](int p, int d) { return Cb[p * LD + d]; });
+    float w0 = 0.f, w1 = 0.f;
+    each<4>(row0, c64, [&](int s, int d, int nt, int e) {
+      const float part = 0.5f * Ks[s * LD + d] * tks[nt][e];
+      if (e < 2) w0 += part; else w1 += part;
+      const int t = t0 + s;
+      if (t < T) {
+        const float ws = bet[s] * expf(pl - pre[s]);
+        dk[((size_t(b) * T + t) * H + h) * KD + d] = fmaf(ws, tks[nt][e] + tkc[nt][e], acc[nt][e]);
+      }
+    });
+    float accv[NTP][4], ck[NTP][4];
+    zero(accv); zero(ck);
+    gemm3<CH, NTP>(accv, row0, cP, [&](int s, int t) { return M1[t * LD + s]; },
+                   [&](int t, int p) { return Os[t * LP + p]; });
+    gemm3<KD, NTP>(ck, row0, cP, [&](int s, int d) { return Ks[s * LD + d]; },
+                   [&](int d, int p) { return Cb[p * LD + d]; });
+    each<NTP>(row0, cP, [&](int s, int p, int nt, int e) {
+      const float part = Vs[s * LP + p] * ck[nt][e];
+      if (e < 2) w0 += part; else w1 += part;
+      const int t = t0 + s;
+      if (t < T) {
+        const float ws = bet[s] * expf(pl - pre[s]);
+        dv[((size_t(b) * T + t) * H + h) * P + p] = fmaf(ws, ck[nt][e], accv[nt][e]);
+      }
+    });
+    row_reduce_store(w0, w1, wbP + half * CH, row0);
   }
-  // <Sb, S0>, <Cb, C0> (before overwriting Sb/Cb with S0/C0).
   __syncthreads();
-  float dot_end = 0.f;
+  // <dS_end, S0> + <dC_end, C0>, then S0 and C0 replace them in the tiles.
+  const float* s0 = s_start + (size_t(bh) * nsub + ch * (CH / SUB)) * KD * KD;
+  const float* c0 = c_start + (size_t(bh) * nch + ch) * P * KD;
   {
-    const float* s0 = s_start + (size_t(bh) * nsub + ch * (CH / SUB)) * KD * KD;
-    const float* c0 = c_start + (size_t(bh) * nch + ch) * P * KD;
     float part = 0.f;
-    for (int idx = tid; idx < KD * KD; idx += 256) part = fmaf(Sb[(idx / KD) * LD + idx % KD], s0[idx], part);
-    for (int idx = tid; idx < P * KD; idx += 256) part = fmaf(Cb[(idx / KD) * LD + idx % KD], c0[idx], part);
+    for (int idx = tid; idx < KD * KD; idx += CT) part = fmaf(Sb[(idx / KD) * LD + idx % KD], s0[idx], part);
+    for (int idx = tid; idx < P * KD; idx += CT) part = fmaf(Cb[(idx / KD) * LD + idx % KD], c0[idx], part);
     part = warp_sum(part);
-    if ((tid & 31) == 0) red[tid >> 5] = part;
-    __syncthreads();
-    if (tid == 0) {
-      float s = 0.f;
-      for (int w = 0; w < 8; ++w) s += red[w];
-      red[32] = s;
-    }
-    __syncthreads();
-    dot_end = red[32];
-    __syncthreads();
-    load_block(Sb, KD, s0, tid);
-    load_block(Cb, P, c0, tid);
+    if (lane == 0) red[CH + warp] = part;
   }
   __syncthreads();
-  // extra_t = e^(P_t) (-z_t . (S0 y_t) + dO_t . (C0 y_t))
+  load_block(Sb, KD, s0, tid);
+  load_block(Cb, P, c0, tid);
+  __syncthreads();
+  // Phase 3: extra_t = e^(P_t) (-z_t . (S0 y_t) + dO_t . (C0 y_t)).
   {
-    float sy[4][4], cy[4][NJ];
-    zero(sy);
-    zero(cy);
-    mm<4, KD>(sy, ty, tx, [&](int r, int k) { return Ys[r * LD + k]; },
-              [&](int k, int c) { return Sb[c * LD + k]; });
-    mm<NJ, KD>(cy, ty, tx, [&](int r, int k) { return Ys[r * LD + k]; },
-               [&](int k, int c) { return Cb[c * LD + k]; });
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = ty + 16 * i;
-      float v = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v = fmaf(-Zs[r * LD + tx + 16 * j], sy[i][j], v);
-#pragma unroll
-      for (int j = 0; j < NJ; ++j) v = fmaf(Os[r * LP + tx + 16 * j], cy[i][j], v);
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (tx == 0) extra[r] = v * expf(pre[r]);
-    }
+    float sy[4][4], cy[NTP][4];
+    zero(sy); zero(cy);
+    gemm3<KD, 4>(sy, row0, c64, [&](int t, int k) { return Ys[t * LD + k]; },
+                 [&](int k, int d) { return Sb[d * LD + k]; });
+    gemm3<KD, NTP>(cy, row0, cP, [&](int t, int k) { return Ys[t * LD + k]; },
+                   [&](int k, int p) { return Cb[p * LD + k]; });
+    float v0 = 0.f, v1 = 0.f;
+    each<4>(row0, c64, [&](int t, int d, int nt, int e) {
+      const float part = -Zs[t * LD + d] * sy[nt][e];
+      if (e < 2) v0 += part; else v1 += part;
+    });
+    each<NTP>(row0, cP, [&](int t, int p, int nt, int e) {
+      const float part = Os[t * LP + p] * cy[nt][e];
+      if (e < 2) v0 += part; else v1 += part;
+    });
+    row_reduce_store(v0, v1, exP + half * CH, row0);
   }
   __syncthreads();
-  // Per-token scalars: dbeta, dP -> reverse cumsum -> dlog_decay; dq; floor part.
+  // Per-token scalars: dbeta, dP -> reverse cumsum -> dlog_decay.
   if (tid < CH) {
     const int s = tid;
     const float tail = expf(pl - pre[s]);
     const float ws = bet[s] * tail;
-    red[s] = rowA[s] - colA[s] - wbar[s] * ws + extra[s];
-  }
-  __syncthreads();
-  if (tid == 0) {
-    float last = 0.f;
-    for (int s = 0; s < CH; ++s) last = fmaf(wbar[s], bet[s] * expf(pl - pre[s]), last);
-    red[CH - 1] += last + expf(pl) * dot_end;
+    const float wbar = wbP[s] + wbP[CH + s];
+    const float colsum = colP[s] + colP[CH + s] + colP[2 * CH + s] + colP[3 * CH + s];
+    const float decsum = decP[s] + decP[CH + s] + decP[2 * CH + s] + decP[3 * CH + s];
+    red[s] = (rowP[s] + rowP[CH + s]) - colsum - wbar * ws + ept[s] * (exP[s] + exP[CH + s]);
+    const int t = t0 + s;
+    if (t < T) dbeta[(size_t(b) * T + t) * H + h] = decsum + wbar * tail;
+    colP[s] = wbar * ws;  // reuse: dw_s w_s for the chunk-end term
   }
   __syncthreads();
   if (tid < 32) {
-    // reverse inclusive cumsum over 64 entries: two halves
-    float hi = red[32 + (31 - tid)];
-    float shi = warp_inclusive_scan(hi, tid);   // suffix sums of upper half
+    float last = colP[tid] + colP[32 + tid];
+    last = warp_sum(last);
+    float dot_end = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) dot_end += red[CH + w];
+    const float extra_last = last + ept[CH - 1] * dot_end;
+    // reverse inclusive cumsum over 64 entries in two halves
+    const float hi = red[63 - tid] + (tid == 0 ? extra_last : 0.f);
+    const float shi = warp_inclusive_scan(hi, tid);
     const float tot_hi = __shfl_sync(0xffffffffu, shi, 31);
-    float lo = red[31 - tid];
-    float slo = warp_inclusive_scan(lo, tid) + tot_hi;
-    // write: position 32 + (31 - tid) gets shi, position 31 - tid gets slo
-    const int thi = t0 + 32 + (31 - tid), tlo = t0 + 31 - tid;
+    const float slo = warp_inclusive_scan(red[31 - tid], tid) + tot_hi;
+    const int thi = t0 + 63 - tid, tlo = t0 + 31 - tid;
     if (thi < T) dlog[(size_t(b) * T + thi) * H + h] = shi;
     if (tlo < T) dlog[(size_t(b) * T + tlo) * H + h] = slo;
   }
-  if (tid >= 64 && tid < 128) {
-    const int s = tid - 64, t = t0 + s;
-    if (t < T) dbeta[(size_t(b) * T + t) * H + h] = colB[s] + wbar[s] * expf(pl - pre[s]);
-  }
   // dq = z + dvar y ; floor partial = -sum_t z o y
-  for (int idx = tid; idx < CH * KD; idx += 256) {
+  for (int idx = tid; idx < CH * KD; idx += CT) {
     const int r = idx / KD, c = idx % KD, t = t0 + r;
     if (t < T) {
       const float dvv = d_var[(size_t(b) * T + t) * H + h];
@@ -1012,6 +1031,7 @@ __global__ void __launch_bounds__(256) grads_kernel(
   }
 }
 
+
 __global__ void floor_reduce_kernel(int rows, int H, const float* __restrict__ part, float* __restrict__ d_floor) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= H * KD) return;
@@ -1021,13 +1041,13 @@ __global__ void floor_reduce_kernel(int rows, int H, const float* __restrict__ p
 }
 
 template <int P>
-size_t output_smem() { return (3 * CH * LD + CH * (P + 1) + P * LD + 2 * CH) * sizeof(float); }
+size_t output_smem() { return (3 * CH * LD + CH * (P + 4) + P * LD + 3 * CH) * sizeof(float); }
 template <int P>
-size_t rhs_smem() { return (2 * CH * LD + 2 * CH * (P + 1) + P * LD + 2 * CH) * sizeof(float); }
+size_t rhs_smem() { return (2 * CH * LD + 2 * CH * (P + 4) + P * LD + 3 * CH) * sizeof(float); }
 template <int P>
-size_t carry_smem() { return (2 * CH * LD + CH * (P + 1) + 2 * CH) * sizeof(float); }
+size_t carry_smem() { return (2 * CH * LD + CH * (P + 4) + 3 * CH) * sizeof(float); }
 template <int P>
-size_t grads_smem() { return (6 * CH * LD + 2 * CH * (P + 1) + P * LD + 8 * CH) * sizeof(float); }
+size_t grads_smem() { return (6 * CH * LD + 2 * CH * (P + 4) + P * LD + 18 * CH + 16) * sizeof(float); }
 
 template <int P>
 int forward(const M4MemDims& d, const float* keys, const float* values, const float* queries,
@@ -1049,7 +1069,7 @@ int forward(const M4MemDims& d, const float* keys, const float* values, const fl
       z.B, z.T, z.H, keys, queries, beta, log_decay, floor_, Ss, Lst, Y, var);
   const size_t osm = output_smem<P>();
   cudaFuncSetAttribute(output_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(osm));
-  output_kernel<P><<<bh * z.nch, 256, osm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Cs, out);
+  output_kernel<P><<<bh * z.nch, CT, osm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Cs, out);
   return launch_status();
 }
 
@@ -1072,17 +1092,19 @@ int backward(const M4MemDims& d, const float* keys, const float* values, const f
   const int bh = z.B * z.H;
   const size_t rsm = rhs_smem<P>();
   cudaFuncSetAttribute(rhs_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(rsm));
-  rhs_kernel<P><<<bh * z.nch, 256, rsm, st>>>(z.B, z.T, z.H, keys, values, queries, beta, log_decay, Cs,
+  rhs_kernel<P><<<bh * z.nch, CT, rsm, st>>>(z.B, z.T, z.H, keys, values, queries, beta, log_decay, Cs,
                                               d_out, d_var, G);
   const int warps = bh * z.nsub;
-  zsolve_kernel<<<(warps + WARPS - 1) / WARPS, 32 * WARPS, 0, st>>>(z.B, z.T, z.H, Lst, G, Zb);
+  const int ssm = int(sizeof(SolveSmem) * WARPS);
+  cudaFuncSetAttribute(zsolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm);
+  zsolve_kernel<<<(warps + WARPS - 1) / WARPS, 32 * WARPS, ssm, st>>>(z.B, z.T, z.H, Lst, G, Zb);
   const size_t csm = carry_smem<P>();
   cudaFuncSetAttribute(carry_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(csm));
-  carry_kernel<P><<<bh, 256, csm, st>>>(z.B, z.T, z.H, beta, log_decay, Y, Zb, d_out, d_sfin, d_cfin, sb,
+  carry_kernel<P><<<bh, CT, csm, st>>>(z.B, z.T, z.H, beta, log_decay, Y, Zb, d_out, d_sfin, d_cfin, sb,
                                         cb, d_init_s, d_init_c);
   const size_t gsm = grads_smem<P>();
   cudaFuncSetAttribute(grads_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(gsm));
-  grads_kernel<P><<<bh * z.nch, 256, gsm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Zb, Ss,
+  grads_kernel<P><<<bh * z.nch, CT, gsm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Zb, Ss,
                                                 Cs, sb, cb, d_out, d_var, dk, dv, dq, dbeta, dlog, fl);
   floor_reduce_kernel<<<(z.H * KD + 255) / 256, 256, 0, st>>>(z.B * z.nch, z.H, fl, dfloor);
   return launch_status();
