@@ -16,7 +16,8 @@
  *     The library never allocates: the caller sizes residual and workspace
  *     buffers with the *_bytes queries and passes them in.
  *   - `stream` is a cudaStream_t passed as void*; every call is asynchronous
- *     on it and reentrant (no global mutable state).
+ *     on it and reentrant (no global mutable state; the one exception,
+ *     m4_scan_bwd_noalloc, documents its shared scratch below).
  *   - Tensors are dense, row-major, in the layouts stated per argument.
  *   - Every entry point returns an M4Status; nonzero means nothing was
  *     launched (argument errors) or a launch failed (M4_ERR_LAUNCH).
@@ -139,6 +140,28 @@ int m4_scan_bwd(const M4ScanDims* dims, const void* c, const void* b, const void
                 float* d_dt, float* d_trap_logits, float* d_angles,
                 float* d_q_bias, float* d_k_bias, void* workspace,
                 size_t workspace_bytes, void* stream);
+
+/* Backward scan that allocates nothing (no counterpart in the reference).
+ * For callers that may not allocate device memory while the operator runs:
+ * an XLA FFI custom call or other framework plugin that must not use the
+ * device allocator, work recorded into a CUDA graph, or a server that
+ * reserves all device memory up front. Same arguments and results as
+ * m4_scan_bwd, without the workspace: its scratch is a fixed 32 MiB array
+ * inside the library, held on every GPU that loads the library until exit.
+ * Limit: m4_scan_workspace_bytes(dims) must not exceed 32 MiB (batch x time
+ * x heads up to about 51,000); larger problems return M4_ERR_WORKSPACE and
+ * launch nothing. The first call on a device looks up the array's device
+ * address (with the current device) - make that first call before any
+ * stream capture. All calls share the one array: calls that overlap on the
+ * GPU (on different streams) race and must not be issued. Nothing in the
+ * array needs clearing between calls. */
+int m4_scan_bwd_noalloc(const M4ScanDims* dims, const void* c, const void* b, const void* x,
+                        const float* adt, const float* dt, const float* trap_logits,
+                        const float* angles, const float* q_bias, const float* k_bias,
+                        const void* residual, size_t residual_bytes, const void* d_y,
+                        const float* d_final, void* dc, void* db, void* dx, float* d_adt,
+                        float* d_dt, float* d_trap_logits, float* d_angles,
+                        float* d_q_bias, float* d_k_bias, void* stream);
 
 /* Name of a status code (static string). */
 const char* m4_status_string(int status);

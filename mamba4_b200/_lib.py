@@ -45,6 +45,8 @@ SIGNATURES = {
     "m4_scan_fwd": ([ctypes.POINTER(ScanDims)] + [_p] * 11 + [_p, _size, _p], _c_int),
     "m4_scan_bwd": ([ctypes.POINTER(ScanDims)] + [_p] * 10 + [_size] + [_p] * 11
                     + [_p, _size, _p], _c_int),
+    "m4_scan_bwd_noalloc": ([ctypes.POINTER(ScanDims)] + [_p] * 10 + [_size] + [_p] * 11 + [_p],
+                            _c_int),
     "m4_status_string": ([_c_int], ctypes.c_char_p),
     "m4_version": ([], ctypes.c_char_p),
 }

@@ -839,3 +839,68 @@ extern "C" int m4_scan_bwd(const M4ScanDims* s, const void* c, const void* b, co
                                dy, d_final, dc, db, dx, d_adt, d_dt, d_trap, d_angles, d_qb, d_kb,
                                static_cast<char*>(work), strm);
 }
+
+// ---------------------------------------------------------------------------
+// Backward scan for callers that cannot allocate device memory.
+//
+// Some callers may not allocate at all while they run this operator: an XLA
+// FFI custom call or other framework plugin that must not touch the device
+// allocator, code recorded into a CUDA graph, or an inference server that
+// reserves all device memory up front. This entry point takes its scratch
+// from a fixed array compiled into the library instead of a caller buffer.
+// ---------------------------------------------------------------------------
+#include <atomic>
+
+namespace {
+
+// Fixed scratch: 32 MiB, held on every GPU that loads the library until the
+// process exits. Enough for batch x time x heads up to about 51,000
+// (e.g. 2 sequences x 1,024 tokens x 16 heads).
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+__device__ __align__(256) unsigned char g_scan_bwd_scratch[kNoAllocScratchBytes];
+
+// Device address of the array per device, looked up once per device.
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_scan_bwd_scratch_ptr[kMaxDevices];
+
+}  // namespace
+
+extern "C" int m4_scan_bwd_noalloc(const M4ScanDims* s, const void* c, const void* b, const void* x,
+                                   const float* adt, const float* dt, const float* trap,
+                                   const float* angles, const float* qb, const float* kb,
+                                   const void* resid, size_t resid_bytes, const void* dy,
+                                   const float* d_final, void* dc, void* db, void* dx, float* d_adt,
+                                   float* d_dt, float* d_trap, float* d_angles, float* d_qb,
+                                   float* d_kb, void* stream) {
+  int st = scan::check(s);
+  if (st) return st;
+  if (!c || !b || !x || !adt || !dt || !trap || !resid || !dy || !dc || !db || !dx || !d_adt ||
+      !d_dt || !d_trap)
+    return M4_ERR_NULL;
+  if (s->angle_count > 0 && (!angles || !d_angles)) return M4_ERR_NULL;
+  const scan::Layout l = scan::layout(*s);
+  if (resid_bytes < l.resid) return M4_ERR_WORKSPACE;
+  // Reject problems whose scratch does not fit the fixed array; nothing is launched.
+  if (l.work > kNoAllocScratchBytes) return M4_ERR_WORKSPACE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return M4_ERR_LAUNCH;
+  void* scratch = g_scan_bwd_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (scratch == nullptr) {
+    // Host code only sees a stand-in for the __device__ array; its device
+    // address comes from the runtime, once per device, with that device current.
+    if (cudaGetSymbolAddress(&scratch, g_scan_bwd_scratch) != cudaSuccess || scratch == nullptr)
+      return M4_ERR_LAUNCH;
+    g_scan_bwd_scratch_ptr[dev].store(scratch, std::memory_order_release);
+  }
+  // Every scratch byte the backward reads is written earlier in the same
+  // call, so nothing needs clearing between calls.
+  cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  char* work = static_cast<char*>(scratch);
+  if (s->bf16)
+    return scan::backward<__nv_bfloat16>(*s, c, b, x, adt, dt, trap, angles, qb, kb,
+                                         static_cast<const char*>(resid), dy, d_final, dc, db, dx, d_adt,
+                                         d_dt, d_trap, d_angles, d_qb, d_kb, work, strm);
+  return scan::backward<float>(*s, c, b, x, adt, dt, trap, angles, qb, kb, static_cast<const char*>(resid),
+                               dy, d_final, dc, db, dx, d_adt, d_dt, d_trap, d_angles, d_qb, d_kb, work,
+                               strm);
+}
