@@ -149,7 +149,7 @@ int m4_scan_bwd(const M4ScanDims* dims, const void* c, const void* b, const void
  * m4_scan_bwd, without the workspace: its scratch is a fixed 32 MiB array
  * inside the library, held on every GPU that loads the library until exit.
  * Limit: m4_scan_workspace_bytes(dims) must not exceed 32 MiB (batch x time
- * x heads up to about 51,000); larger problems return M4_ERR_WORKSPACE and
+ * x heads up to about 36,000); larger problems return M4_ERR_WORKSPACE and
  * launch nothing. The first call on a device looks up the array's device
  * address (with the current device) - make that first call before any
  * stream capture. All calls share the one array: calls that overlap on the

@@ -684,8 +684,8 @@ __global__ void bias_kernel(Dims d, const float* __restrict__ dqb, const float* 
 }
 
 struct Layout {
-  size_t starts, phases, resid;
-  size_t dq, dk, drate, dgam, dscl, dlog, ddtp, dqb, dkb, work;
+  size_t starts, phases, deltas, resid;
+  size_t dq, dk, drate, dgam, dscl, dlog, ddtp, dqb, dkb, carries, dth, work;
 };
 
 inline Layout layout(const M4ScanDims& s) {
@@ -695,6 +695,7 @@ inline Layout layout(const M4ScanDims& s) {
   size_t off = 0;
   l.starts = off; off += align256(bh * nch * NS * HP * sizeof(float));
   l.phases = off; off += align256(bh * nch * 32 * sizeof(float));
+  l.deltas = off; off += align256(bh * nch * sizeof(float));
   l.resid = off;
   off = 0;
   l.dq = off; off += align256(bth * NS * sizeof(float));
@@ -704,8 +705,10 @@ inline Layout layout(const M4ScanDims& s) {
   l.dscl = off; off += align256(bth * sizeof(float));
   l.dlog = off; off += align256(bth * sizeof(float));
   l.ddtp = off; off += align256(bth * sizeof(float));
-  l.dqb = off; off += align256(bh * NS * sizeof(float));
-  l.dkb = off; off += align256(bh * NS * sizeof(float));
+  l.dqb = off; off += align256(bh * nch * NS * sizeof(float));
+  l.dkb = off; off += align256(bh * nch * NS * sizeof(float));
+  l.carries = s.bf16 ? off : 0; off += s.bf16 ? align256(bh * nch * NS * HP * sizeof(float)) : 0;
+  l.dth = off; off += align256(bh * nch * 32 * sizeof(float));
   l.work = off;
   return l;
 }
@@ -733,10 +736,21 @@ inline int check(const M4ScanDims* s) {
   return M4_OK;
 }
 
+inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                        const float* dt, const float* trap, const float* angles, const float* qb,
+                        const float* kb, void* y, float* fin, char* resid, cudaStream_t st);
+inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                         const float* dt, const float* trap, const float* angles, const float* qb,
+                         const float* kb, const char* resid, const void* dy, const float* d_final, void* dc,
+                         void* db, void* dx, float* d_adt, float* d_dt, float* d_trap, float* d_angles,
+                         float* d_qb, float* d_kb, char* work, cudaStream_t st);
+
 template <typename T>
 int forward(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
             const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
             void* y, float* fin, char* resid, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2)
+    return forward_bf16(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
   const Dims d = make_dims(s);
   const Layout l = layout(s);
   const size_t sm = fwd_smem();
@@ -754,6 +768,9 @@ int backward(const M4ScanDims& s, const void* c, const void* b, const void* x, c
              const char* resid, const void* dy, const float* d_final, void* dc, void* db, void* dx,
              float* d_adt, float* d_dt, float* d_trap, float* d_angles, float* d_qb, float* d_kb,
              char* work, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2)
+    return backward_bf16(s, c, b, x, adt, dt, trap, angles, qb, kb, resid, dy, d_final, dc, db, dx, d_adt,
+                         d_dt, d_trap, d_angles, d_qb, d_kb, work, st);
   const Dims d = make_dims(s);
   const Layout l = layout(s);
   BwdOut o;
@@ -783,6 +800,104 @@ int backward(const M4ScanDims& s, const void* c, const void* b, const void* x, c
                                                             o.drate, d_adt, d_dt, d_trap, d_angles);
   if (d_qb || d_kb)
     bias_kernel<<<(s.heads * NS + 255) / 256, 256, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
+  return launch_status();
+}
+
+}  // namespace scan
+}  // namespace m4
+
+#include "scan_bf16.cuh"
+
+namespace m4 {
+namespace scan {
+
+// bfloat16 operands run the chunk-parallel kernels of scan_bf16.cuh.
+inline scan2::Dims make_dims2(const M4ScanDims& s) {
+  scan2::Dims d;
+  d.B = s.batch; d.T = s.time; d.H = s.heads; d.A = s.angle_count;
+  d.nch = (s.time + C - 1) / C;
+  d.per_head = s.per_head != 0;
+  return d;
+}
+
+template <class K>
+inline void allow_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+}
+
+inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                        const float* dt, const float* trap, const float* angles, const float* qb,
+                        const float* kb, void* y, float* fin, char* resid, cudaStream_t st) {
+  using namespace scan2;
+  const scan2::Dims d = make_dims2(s);
+  const Layout l = layout(s);
+  float* starts = reinterpret_cast<float*>(resid + l.starts);
+  float* phases = reinterpret_cast<float*>(resid + l.phases);
+  float* deltas = reinterpret_cast<float*>(resid + l.deltas);
+  const bf16* cq = static_cast<const bf16*>(c);
+  const bf16* bk = static_cast<const bf16*>(b);
+  const bf16* xx = static_cast<const bf16*>(x);
+  const int bh = d.B * d.H, chunks = bh * d.nch;
+  const size_t psm = size_t(d.nch) * 32 * sizeof(float);
+  allow_smem(phase_kernel, psm);
+  phase_kernel<<<bh, 256, psm, st>>>(d, dt, angles, phases);
+  allow_smem(update_kernel, sizeof(UpdSmem));
+  update_kernel<<<chunks, CTH, sizeof(UpdSmem), st>>>(d, bk, xx, adt, dt, trap, angles, kb, phases, starts,
+                                                      deltas);
+  state_kernel<<<bh, 256, 0, st>>>(d, starts, deltas, fin);
+  allow_smem(output_kernel, sizeof(OutSmem));
+  output_kernel<<<chunks, CTH, sizeof(OutSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
+                                                      starts, static_cast<bf16*>(y));
+  return launch_status();
+}
+
+inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                         const float* dt, const float* trap, const float* angles, const float* qb,
+                         const float* kb, const char* resid, const void* dy, const float* d_final, void* dc,
+                         void* db, void* dx, float* d_adt, float* d_dt, float* d_trap, float* d_angles,
+                         float* d_qb, float* d_kb, char* work, cudaStream_t st) {
+  using namespace scan2;
+  const scan2::Dims d = make_dims2(s);
+  const scan::Dims d1 = make_dims(s);
+  const Layout l = layout(s);
+  const float* starts = reinterpret_cast<const float*>(resid + l.starts);
+  const float* phases = reinterpret_cast<const float*>(resid + l.phases);
+  const float* deltas = reinterpret_cast<const float*>(resid + l.deltas);
+  float* carries = reinterpret_cast<float*>(work + l.carries);
+  GradOut o;
+  o.dq = reinterpret_cast<float*>(work + l.dq);
+  o.dk = reinterpret_cast<float*>(work + l.dk);
+  o.drate = reinterpret_cast<float*>(work + l.drate);
+  o.dgam = reinterpret_cast<float*>(work + l.dgam);
+  o.dscl = reinterpret_cast<float*>(work + l.dscl);
+  o.dlog = reinterpret_cast<float*>(work + l.dlog);
+  o.ddtp = reinterpret_cast<float*>(work + l.ddtp);
+  o.dth = reinterpret_cast<float*>(work + l.dth);
+  o.dqb = reinterpret_cast<float*>(work + l.dqb);
+  o.dkb = reinterpret_cast<float*>(work + l.dkb);
+  const bf16* cq = static_cast<const bf16*>(c);
+  const bf16* bk = static_cast<const bf16*>(b);
+  const bf16* xx = static_cast<const bf16*>(x);
+  const bf16* g = static_cast<const bf16*>(dy);
+  const int bh = d.B * d.H, chunks = bh * d.nch;
+  allow_smem(dstart_kernel, sizeof(DsSmem));
+  dstart_kernel<<<chunks, CTH, sizeof(DsSmem), st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
+  carry_kernel<<<bh, 256, 0, st>>>(d, carries, deltas, d_final);
+  allow_smem(grads_kernel, sizeof(GradSmem));
+  grads_kernel<<<chunks, CTH, sizeof(GradSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
+                                                      starts, carries, g, static_cast<bf16*>(dx), o);
+  const size_t lsm = size_t(d.nch) * 32 * sizeof(float);
+  allow_smem(later_kernel, lsm);
+  later_kernel<<<bh, 256, lsm, st>>>(d, dt, angles, o.dth, o.drate, o.ddtp);
+  const size_t n1 = s.per_head ? size_t(s.batch) * s.time * s.heads * NS : size_t(s.batch) * s.time * NS;
+  reduce_heads_kernel<bf16><<<unsigned((n1 + 255) / 256), 256, 0, st>>>(d1, o.dq, o.dk, static_cast<bf16*>(dc),
+                                                                       static_cast<bf16*>(db));
+  size_t n2 = size_t(s.batch) * s.time * s.heads;
+  const size_t na = s.per_head ? n2 * s.angle_count : size_t(s.batch) * s.time * s.angle_count;
+  if (na > n2) n2 = na;
+  gates_kernel<<<unsigned((n2 + 255) / 256), 256, 0, st>>>(d1, dt, trap, o.dgam, o.dscl, o.dlog, o.ddtp,
+                                                            o.drate, d_adt, d_dt, d_trap, d_angles);
+  if (d_qb || d_kb) scan2::bias_kernel<<<(s.heads * NS + 255) / 256, 256, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
   return launch_status();
 }
 
@@ -854,7 +969,7 @@ extern "C" int m4_scan_bwd(const M4ScanDims* s, const void* c, const void* b, co
 namespace {
 
 // Fixed scratch: 32 MiB, held on every GPU that loads the library until the
-// process exits. Enough for batch x time x heads up to about 51,000
+// process exits. Enough for batch x time x heads up to about 36,000
 // (e.g. 2 sequences x 1,024 tokens x 16 heads).
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
 __device__ __align__(256) unsigned char g_scan_bwd_scratch[kNoAllocScratchBytes];
