@@ -442,18 +442,105 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+LM_PER_GPU = {"lm60m": 32, "lm125m": 64}
+LM_SEQ = 1024
+
+
+def lm_flops_per_token(cfg):
+    """Model FLOPs per token for one training step (fwd + bwd): 6 x matmul
+    parameters (in/out projections and the tied head) plus the two hot
+    operators' survey figures (memory read 202,581 per token-head; scan
+    1,835,008 per token at 16 heads, scaled by heads)."""
+    s_layers = cfg.layer_pattern.count("S")
+    m_layers = cfg.layer_pattern.count("M")
+    h, n = cfg.num_heads, cfg.d_state
+    angles = int(cfg.d_state * cfg.rope_fraction) // 2
+    s_proj = cfg.d_model * (2 * cfg.inner + 2 * n + 3 * h + angles) + cfg.inner * cfg.d_model
+    mh, d = cfg.memory_heads, cfg.key_dim
+    m_proj = cfg.d_model * (2 * cfg.inner + 2 * mh * d + 3 * mh) + cfg.inner * cfg.d_model
+    matmul = s_layers * s_proj + m_layers * m_proj + cfg.vocab_size * cfg.d_model
+    return 6 * matmul + m_layers * mh * (MEM_FWD_FLOPS + MEM_BWD_FLOPS) + s_layers * SCAN_FLOPS * h / 16
+
+
+def run_lm(args):
+    import torch
+
+    from mamba4_b200.model import CONFIGS, Mamba4LM
+    from mamba4_b200.train import DataParallelTrainer, TrainSettings, synthetic_batch
+
+    world, rank, local = setup_dist(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    name = args.workload[2:]
+    cfg = CONFIGS[name]
+    per_gpu = LM_PER_GPU[args.workload]
+    torch.manual_seed(1234)
+    model = Mamba4LM(cfg).to(dev)
+    trainer = DataParallelTrainer(model, TrainSettings(), world=world, device_id=local)
+    tokens, targets, mask = synthetic_batch(per_gpu, LM_SEQ, cfg.vocab_size, seed=100 + rank, device=dev)
+
+    def step():
+        trainer.step(tokens, targets, mask)
+
+    with ClockSampler(local) as clocks:
+        total_ms = time_region(step, args.steps, args.warmup, world)
+    total_ms = max_over_ranks(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    tokens_per_step = world * per_gpu * LM_SEQ
+    value = tokens_per_step / (ms_per_step / 1000.0)
+    e2e = None
+    if not args.no_e2e:
+        host = [t.cpu().pin_memory() for t in (tokens, targets, mask)]
+        loss_host = torch.empty((), dtype=torch.float32, pin_memory=True)
+
+        def e2e_step():
+            t, y, m = (h.to(dev, non_blocking=True) for h in host)
+            loss, _, _ = trainer.step(t, y, m)
+            loss_host.copy_(loss, non_blocking=True)
+
+        e_ms = max_over_ranks(time_region(e2e_step, args.steps, args.warmup, world), world) / args.steps
+        e2e = {"value": tokens_per_step / (e_ms / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": sum(h.numel() * h.element_size() for h in host),
+               "d2h_bytes_per_step": 4, "ms_per_step": e_ms}
+    pk = peaks()
+    flops = lm_flops_per_token(cfg) * per_gpu * LM_SEQ / (ms_per_step / 1000.0) / 1e12
+    line = {
+        "metric": f"Mamba 4 {name.upper()} train tokens/s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform-random token ids)",
+        "config": {"workload": "configs[3]" if name == "60m" else "configs[4]", "model": f"mamba4-{name}",
+                   "global_batch": world * per_gpu, "seq_len": LM_SEQ, "parallelism": f"dp{world}",
+                   "layer_pattern": cfg.layer_pattern, "d_model": cfg.d_model, "vocab": cfg.vocab_size,
+                   "l2": "activations and stored factors far exceed L2"},
+        "roofline": {"bound": "tensor", "kernel": "whole training step (model FLOPs utilisation)",
+                     "achieved": flops, "peak": pk["bf16_sust"], "unit": "TFLOP/s",
+                     "frac": flops / pk["bf16_sust"], "traffic": None, "peak_source": pk["source"]},
+        "e2e": e2e, "clocks": clocks.summary(),
+        "gpu_launches": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["hotpath", "small"], default="hotpath")
+    p.add_argument("--workload", choices=["hotpath", "small", "lm60m", "lm125m"], default="hotpath")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     args = p.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload.startswith("lm"):
+        run_lm(args)
     else:
         run_ours(args)
 

@@ -1,0 +1,285 @@
+"""Mamba 4 language model around the B200 operators (PyTorch modules).
+
+Restates the reference model (`lm/models/mamba4.py`, `lm/models/mamba3.py`,
+`lm/models/common.py`) with the same parameter tree, initialisation and
+forward arithmetic, using this package's CUDA operators for the two hot
+ops: the memory read (`selective_memory_fused`) and the Mamba-3 scan
+(`mamba3_fused`). Linear layers run in bfloat16 (torch autocast), norms,
+gates and the memory statistics in float32, as the reference's
+`dtype="bfloat16"`, `param_dtype="float32"` configuration does.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .flashmamba import mamba3_fused
+from .memory import selective_memory_fused
+
+
+@dataclass(frozen=True)
+class Mamba4Config:
+    """Subset of the reference `ModelConfig` (`lm/config.py:6-89`) the
+    Mamba 4 model reads. Defaults: BASELINE config 3 (60M)."""
+
+    vocab_size: int = 50304
+    d_model: int = 512
+    layer_pattern: str = "SSSM" * 4
+    expand: int = 2
+    head_dim: int = 64          # Mamba-3 head dim (16 heads at d_model 512)
+    d_state: int = 64           # Mamba-3 state dim (kernel size N = 64)
+    rope_fraction: float = 0.5  # angle pairs = d_state * rope_fraction / 2
+    key_dim: int = 64           # memory key dim
+    memory_head_dim: int = 128  # memory value dim (8 heads at d_model 512)
+    conv_kernel: int = 4
+    floor_min: float = 0.25
+    floor_init: float = 1.0
+    order_head: bool = True
+    memory_beta_max: float = 1.0
+    memory_key_shift: bool = True
+    norm_eps: float = 1e-5
+    chunk_size: int = 64
+
+    @property
+    def n_layers(self) -> int:
+        return len(self.layer_pattern)
+
+    @property
+    def inner(self) -> int:
+        return self.d_model * self.expand
+
+    @property
+    def num_heads(self) -> int:
+        return self.inner // self.head_dim
+
+    @property
+    def memory_heads(self) -> int:
+        return self.inner // self.memory_head_dim
+
+
+CONFIGS = {
+    # d_model 512, 16 blocks (12 Mamba-3 + 4 memory, one
+    # every 4th block), memory 8 heads x key 64 (value 128, forced by
+    # d_model * expand = heads * value_dim), vocab 50304.
+    "60m": Mamba4Config(),
+    # d_model 768, 17 Mamba-3 + 4 memory layers
+    # (pattern of lm/configs/mamba4-125m.json), memory 12 heads x 128.
+    "125m": Mamba4Config(d_model=768, layer_pattern="SSSMSSSSMSSSSMSSSSMSS"),
+}
+
+
+class RMSNorm(nn.Module):
+    """`lm/models/common.py:25-45`: fp32 statistics, output in the model dtype."""
+
+    def __init__(self, features: int, eps: float, out_dtype=torch.bfloat16):
+        super().__init__()
+        self.scale = nn.Parameter(torch.ones(features))
+        self.eps = eps
+        self.out_dtype = out_dtype
+
+    def forward(self, x):
+        x32 = x.float()
+        var = x32.square().mean(-1, keepdim=True)
+        return (x32 * torch.rsqrt(var + self.eps) * self.scale).to(self.out_dtype)
+
+
+def _dense(din, dout, std):
+    layer = nn.Linear(din, dout, bias=False)
+    nn.init.normal_(layer.weight, 0.0, std)
+    return layer
+
+
+def heavy_tail_activation(x):
+    """`lm/models/mamba3.py:28-29`."""
+    return torch.clamp(x, min=0) + torch.reciprocal(1 - torch.clamp(x, max=0))
+
+
+def timestep_bias_init(shape, generator=None):
+    """`lm/models/mamba3.py:32-36`: inverse softplus of log-uniform dt."""
+    u = torch.rand(shape, generator=generator)
+    dt = torch.exp(u * (math.log(0.1) - math.log(0.001)) + math.log(0.001))
+    return dt + torch.log(-torch.expm1(-dt))
+
+
+class Mamba3Mixer(nn.Module):
+    """Flash branch of `Mamba3Mixer` (`lm/models/mamba3.py:43-132`)."""
+
+    def __init__(self, cfg: Mamba4Config):
+        super().__init__()
+        self.cfg = cfg
+        h, n = cfg.num_heads, cfg.d_state
+        self.angles = int(cfg.d_state * cfg.rope_fraction) // 2
+        self.sizes = (cfg.inner, cfg.inner, n, n, h, h, h, self.angles)
+        self.in_proj = _dense(cfg.d_model, sum(self.sizes), 0.02)
+        self.B_norm = RMSNorm(n, cfg.norm_eps)
+        self.C_norm = RMSNorm(n, cfg.norm_eps)
+        self.B_bias = nn.Parameter(torch.ones(h, 1, n))
+        self.C_bias = nn.Parameter(torch.ones(h, 1, n))
+        self.dt_bias = nn.Parameter(timestep_bias_init((h,)))
+        self.D = nn.Parameter(torch.ones(h))
+        self.out_proj = _dense(cfg.inner, cfg.d_model, 0.02 / math.sqrt(2 * cfg.n_layers))
+
+    def forward(self, u):
+        cfg = self.cfg
+        proj = self.in_proj(u)
+        z, x, b, c, raw_dt, raw_a, trap, angles = torch.split(proj, self.sizes, dim=-1)
+        b = self.B_norm(b)
+        c = self.C_norm(c)
+        dt = F.softplus(raw_dt.float() + self.dt_bias)
+        a = -torch.clamp(heavy_tail_activation(raw_a.float()), min=1e-4)
+        with torch.autocast("cuda", enabled=False):
+            y, _ = mamba3_fused(c, b, x.to(torch.bfloat16).contiguous(), (a * dt).contiguous(),
+                                dt.contiguous(), trap.float().contiguous(), angles.float().contiguous(),
+                                q_bias=self.C_bias, k_bias=self.B_bias, chunk_size=cfg.chunk_size)
+            y = y.float() + x.float() * torch.repeat_interleave(self.D, cfg.head_dim)
+            y = (y * F.silu(z.float())).to(torch.bfloat16)
+        return self.out_proj(y)
+
+
+def causal_conv(x, weight, bias):
+    """Depthwise causal convolution (`lm/models/mamba4.py:98-108`), fp32 taps."""
+    taps = weight.shape[0]
+    xt = F.pad(x.float().transpose(1, 2), (taps - 1, 0))
+    w = weight.float().t().unsqueeze(1)  # [channels, 1, taps]
+    return (F.conv1d(xt, w, bias.float(), groups=x.shape[-1])).transpose(1, 2)
+
+
+def order_memory_chunked(values, log_decay, chunk_size=64):
+    """h_t = lam_t h_(t-1) + (1 - lam_t) v_t, chunked
+    (`lm/models/mamba4.py:59-95`)."""
+    x = values.float()
+    batch, time, heads, width = x.shape
+    pad = (-time) % chunk_size
+    count = (time + pad) // chunk_size
+
+    def chunks(a):
+        a = F.pad(a, [0, 0] * (a.ndim - 2) + [0, pad])
+        return a.reshape(batch, count, chunk_size, *a.shape[2:]).transpose(2, 3)
+
+    value, logs = chunks(x), chunks(log_decay.float())   # [B,n,H,c,P], [B,n,H,c]
+    inflow = -torch.expm1(logs)
+    prefix = torch.cumsum(logs, dim=-1)
+    causal = torch.tril(torch.ones(chunk_size, chunk_size, dtype=torch.bool, device=x.device))
+    diff = prefix[..., :, None] - prefix[..., None, :]
+    weights = torch.where(causal, torch.exp(torch.where(causal, diff, torch.zeros_like(diff))),
+                          torch.zeros_like(diff))
+    local = torch.einsum("bnhts,bnhsp->bnhtp", weights * inflow[..., None, :], value)
+    ends = local[..., -1, :]                               # [B,n,H,P]
+    decay = torch.exp(prefix[..., -1])                     # [B,n,H]
+    carries, state = [], torch.zeros_like(ends[:, 0])
+    for n in range(count):
+        carries.append(state)
+        state = decay[:, n, :, None] * state + ends[:, n]
+    starts = torch.stack(carries, 1)
+    out = local + torch.exp(prefix)[..., None] * starts[..., None, :]
+    return out.transpose(2, 3).reshape(batch, count * chunk_size, heads, width)[:, :time]
+
+
+def _unit(x):
+    x = x.float()
+    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + 1e-6)
+
+
+class SelectiveMemoryMixer(nn.Module):
+    """`SelectiveMemoryMixer` (`lm/models/mamba4.py:115-337`), training path."""
+
+    def __init__(self, cfg: Mamba4Config):
+        super().__init__()
+        self.cfg = cfg
+        h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
+        if h * p != cfg.inner:
+            raise ValueError("Expanded dimension must divide exactly into memory heads")
+        if cfg.floor_min <= 0 or cfg.floor_init <= cfg.floor_min:
+            raise ValueError("Selective floor must be positive and above its minimum")
+        self.sizes = (cfg.inner, cfg.inner, h * d, h * d, h, h, h)
+        self.in_proj = _dense(cfg.d_model, sum(self.sizes), 0.02)
+        channels = cfg.inner + 2 * h * d
+        bound = 1 / math.sqrt(cfg.conv_kernel)
+        self.conv_weight = nn.Parameter(torch.empty(cfg.conv_kernel, channels).uniform_(0.0, 2 * bound))
+        self.conv_bias = nn.Parameter(torch.zeros(channels))
+        self.bound = bound
+        start = 0.5 / max(cfg.memory_beta_max, 1.0)
+        self.beta_bias = nn.Parameter(torch.full((h,), math.log(start / (1 - start))))
+        self.dt_bias = nn.Parameter(timestep_bias_init((h,)))
+        self.a_log = nn.Parameter(torch.log(torch.empty(h).uniform_(1.0, 16.0)))
+        self.floor = nn.Parameter(torch.full((h, d), math.log(math.expm1(cfg.floor_init - cfg.floor_min))))
+        self.confidence_scale = nn.Parameter(torch.full((h,), 0.1))
+        self.D = nn.Parameter(torch.ones(h))
+        self.order_mix = nn.Parameter(torch.full((h,), -1.0))
+        self.read_norm = RMSNorm(p, cfg.norm_eps)
+        self.out_proj = _dense(cfg.inner, cfg.d_model, 0.02 / math.sqrt(2 * cfg.n_layers))
+
+    def forward(self, u):
+        cfg = self.cfg
+        h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
+        batch, time, _ = u.shape
+        proj = self.in_proj(u)
+        gate, value, key, query, beta_raw, dt_raw, order_raw = torch.split(proj, self.sizes, dim=-1)
+        with torch.autocast("cuda", enabled=False):
+            mixed = torch.cat((value, key, query), -1)
+            mixed = F.silu(causal_conv(mixed, self.conv_weight - self.bound, self.conv_bias))
+            value = mixed[..., : cfg.inner].reshape(batch, time, h, p)
+            key = mixed[..., cfg.inner: cfg.inner + h * d].reshape(batch, time, h, d)
+            query = mixed[..., cfg.inner + h * d:].reshape(batch, time, h, d)
+            if cfg.memory_key_shift:
+                key = torch.cat((torch.zeros_like(key[:, :1]), key[:, :-1]), 1)
+            key, query = _unit(key), _unit(query)
+            beta = cfg.memory_beta_max * torch.sigmoid(beta_raw.float() + self.beta_bias)
+            dt = F.softplus(dt_raw.float() + self.dt_bias)
+            log_decay = -torch.exp(self.a_log) * dt
+            floor = cfg.floor_min + F.softplus(self.floor)
+            res = selective_memory_fused(key, value, query, beta, log_decay, floor,
+                                         chunk_size=cfg.chunk_size)
+            read = res.output * torch.sigmoid(1 - self.confidence_scale * torch.log1p(res.variance))[..., None]
+            read = read + self.D[:, None] * value
+            if cfg.order_head:
+                logits = order_raw.float() + 2
+                ordered = order_memory_chunked(value, F.logsigmoid(logits), cfg.chunk_size)
+                read = read + torch.sigmoid(self.order_mix)[:, None] * ordered
+            read = self.read_norm(read)
+            read = (read.float() * F.silu(gate.float().reshape(read.shape))).to(torch.bfloat16)
+        return self.out_proj(read.reshape(batch, time, cfg.inner))
+
+
+class Block(nn.Module):
+    """Pre-norm residual block (`Mamba3Block`, `SelectiveMemoryBlock`)."""
+
+    def __init__(self, cfg: Mamba4Config, kind: str):
+        super().__init__()
+        self.norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self.mixer = SelectiveMemoryMixer(cfg) if kind == "M" else Mamba3Mixer(cfg)
+
+    def forward(self, x):
+        return x + self.mixer(self.norm(x)).to(x.dtype)
+
+
+class Mamba4LM(nn.Module):
+    """`Mamba4LM` (`lm/models/mamba4.py:484-504`): embedding, blocks per the
+    layer pattern, final RMSNorm, tied output head with float32 logits."""
+
+    def __init__(self, cfg: Mamba4Config):
+        super().__init__()
+        if set(cfg.layer_pattern) - {"M", "S"}:
+            raise ValueError("layer_pattern must contain n_layers M/S characters")
+        self.cfg = cfg
+        self.embedding = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        nn.init.normal_(self.embedding.weight, 0.0, 0.02)
+        self.blocks = nn.ModuleList(Block(cfg, k) for k in cfg.layer_pattern)
+        self.final_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+
+    def forward(self, tokens):
+        # bfloat16 residual stream and tied head (Embed dtype bf16, attend().astype(f32)).
+        x = self.embedding(tokens).to(torch.bfloat16)
+        for block in self.blocks:
+            x = block(x)
+        x = self.final_norm(x)
+        return F.linear(x, self.embedding.weight.to(x.dtype)).float()
+
+
+def parameter_count(model: nn.Module) -> int:
+    return sum(p.numel() for p in model.parameters())
