@@ -844,7 +844,7 @@ inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const
   allow_smem(update_kernel, sizeof(UpdSmem));
   update_kernel<<<chunks, CTH, sizeof(UpdSmem), st>>>(d, bk, xx, adt, dt, trap, angles, kb, phases, starts,
                                                       deltas);
-  state_kernel<<<bh, 256, 0, st>>>(d, starts, deltas, fin);
+  state_kernel<<<bh * SPARTS, 256, 0, st>>>(d, starts, deltas, fin);
   allow_smem(output_kernel, sizeof(OutSmem));
   output_kernel<<<chunks, CTH, sizeof(OutSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
                                                       starts, static_cast<bf16*>(y));
@@ -858,7 +858,6 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
                          float* d_qb, float* d_kb, char* work, cudaStream_t st) {
   using namespace scan2;
   const scan2::Dims d = make_dims2(s);
-  const scan::Dims d1 = make_dims(s);
   const Layout l = layout(s);
   const float* starts = reinterpret_cast<const float*>(resid + l.starts);
   const float* phases = reinterpret_cast<const float*>(resid + l.phases);
@@ -882,22 +881,15 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
   const int bh = d.B * d.H, chunks = bh * d.nch;
   allow_smem(dstart_kernel, sizeof(DsSmem));
   dstart_kernel<<<chunks, CTH, sizeof(DsSmem), st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
-  carry_kernel<<<bh, 256, 0, st>>>(d, carries, deltas, d_final);
+  carry_kernel<<<bh * SPARTS, 256, 0, st>>>(d, carries, deltas, d_final);
   allow_smem(grads_kernel, sizeof(GradSmem));
   grads_kernel<<<chunks, CTH, sizeof(GradSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
                                                       starts, carries, g, static_cast<bf16*>(dx), o);
-  const size_t lsm = size_t(d.nch) * 32 * sizeof(float);
-  allow_smem(later_kernel, lsm);
-  later_kernel<<<bh, 256, lsm, st>>>(d, dt, angles, o.dth, o.drate, o.ddtp);
-  const size_t n1 = s.per_head ? size_t(s.batch) * s.time * s.heads * NS : size_t(s.batch) * s.time * NS;
-  reduce_heads_kernel<bf16><<<unsigned((n1 + 255) / 256), 256, 0, st>>>(d1, o.dq, o.dk, static_cast<bf16*>(dc),
-                                                                       static_cast<bf16*>(db));
-  size_t n2 = size_t(s.batch) * s.time * s.heads;
-  const size_t na = s.per_head ? n2 * s.angle_count : size_t(s.batch) * s.time * s.angle_count;
-  if (na > n2) n2 = na;
-  gates_kernel<<<unsigned((n2 + 255) / 256), 256, 0, st>>>(d1, dt, trap, o.dgam, o.dscl, o.dlog, o.ddtp,
-                                                            o.drate, d_adt, d_dt, d_trap, d_angles);
-  if (d_qb || d_kb) scan2::bias_kernel<<<(s.heads * NS + 255) / 256, 256, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
+  later_kernel<<<bh, 32, 0, st>>>(d, o.dth);
+  const size_t tokens = size_t(d.B) * d.T;
+  finish_kernel<<<unsigned((tokens + 7) / 8), 256, 0, st>>>(d, dt, trap, angles, o.dth, o, static_cast<bf16*>(dc),
+                                                          static_cast<bf16*>(db), d_adt, d_dt, d_trap, d_angles);
+  if (d_qb || d_kb) scan2::bias_kernel<<<s.heads, 1024, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
   return launch_status();
 }
 

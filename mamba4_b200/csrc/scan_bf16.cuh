@@ -28,6 +28,7 @@ constexpr int P = 64;        // head dim
 constexpr int TS = 72;       // bf16 tile stride (144 B rows: ldmatrix conflict-free)
 constexpr int FS = 68;       // fp32 tile stride
 constexpr int CTH = 128;     // threads per chunk CTA (4 warps x 16 rows)
+static_assert(CTH == 128 && C == 64, "chunk_theta and the grads epilogue map 4 warps onto 4 x 16 tokens");
 
 M4_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -108,6 +109,18 @@ M4_DEV void store_bf16(bf16* T, int row0, int col0, const float (&acc)[NT][4], F
     }
 }
 
+// Store a warp's accumulator tile as fp32 rows of `ld` elements (float2 pairs).
+template <int NT>
+M4_DEV void store_f32(float* dst, int ld, int row0, const float (&acc)[NT][4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      *reinterpret_cast<float2*>(dst + (row0 + g + 8 * h) * ld + 8 * nt + 2 * c) =
+          make_float2(acc[nt][2 * h], acc[nt][2 * h + 1]);
+}
+
 struct Dims {
   int B, T, H, A, nch;
   bool per_head;
@@ -116,6 +129,7 @@ struct Dims {
 // Per-token scalars of one chunk of (b, h) (threads 0..63 + warp 0 prefix).
 struct Rows {
   float p[C], gam[C], scl[C], tail[C], dt[C], ept[C];
+  float seg[4 * 32];  // per-segment totals of the 16-token scans
 };
 
 M4_DEV void chunk_rows(const Dims& d, int b, int h, int t0, const float* adt, const float* dt,
@@ -157,65 +171,121 @@ M4_DEV float rate_at(const Dims& d, const float* angles, int b, int h, int t, in
                     : angles[(size_t(b) * d.T + t) * d.A + i];
 }
 
-// theta[t][i] = phase0[i] + sum_{s<=t} rate_s[i] dt_s within the chunk.
-M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles, const Rows& r,
-                        const float* phase0, float* theta) {
-  const int tid = threadIdx.x;
-  if (tid < d.A) {
-    float acc = phase0[tid];
-    for (int tt = 0; tt < C; ++tt) {
-      const int t = t0 + tt;
-      const float rate = t < d.T ? rate_at(d, angles, b, h, t, tid) : 0.f;
-      acc = fmaf(rate, r.dt[tt], acc);
-      theta[tt * 33 + tid] = acc;
+// theta[t][i] = phase0[i] + sum_{s<=t} rate_s[i] dt_s within the chunk,
+// returned as cos (in `cosv`) and sin. Warp w scans tokens 16w..16w+15
+// (independent loads, then a 16-step sum), the segment totals are combined
+// through `r.seg`, and the same thread takes sincos of its 16 elements in one
+// compact loop. Pairs i >= A get cos 1, sin 0. All CTH threads must call.
+M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles, Rows& r,
+                        const float* phase0, float* cosv, float* sinv) {
+  const int i = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float acc = 0.f;
+  if (i < d.A) {
+    float inc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int tt = 16 * w + j, t = t0 + tt;
+      inc[j] = t < d.T ? rate_at(d, angles, b, h, t, i) * r.dt[tt] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      acc += inc[j];
+      cosv[(16 * w + j) * 33 + i] = acc;
     }
   }
-}
-
-// Rotated, rounded queries/keys of a chunk as bf16 tiles. With `Qf`, also
-// keeps cos/sin for the backward.
-M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const bf16* bk, const float* qb,
-                     const float* kb, const float* theta, bf16* Qs, bf16* Ks, float* cosv, float* sinv) {
-  for (int idx = threadIdx.x; idx < C * (N / 2); idx += CTH) {
-    const int tt = idx / (N / 2), i = idx % (N / 2), t = t0 + tt;
-    const int n0 = 2 * i;
-    float c0 = 0.f, c1 = 0.f, b0 = 0.f, b1 = 0.f;
-    if (t < d.T) {
-      const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
-      const __nv_bfloat162 cc = *reinterpret_cast<const __nv_bfloat162*>(cq + base + n0);
-      const __nv_bfloat162 bb = *reinterpret_cast<const __nv_bfloat162*>(bk + base + n0);
-      c0 = __low2float(cc); c1 = __high2float(cc);
-      b0 = __low2float(bb); b1 = __high2float(bb);
-    }
-    const float q0 = round_to<bf16>(c0 + (qb ? qb[h * N + n0] : 0.f));
-    const float q1 = round_to<bf16>(c1 + (qb ? qb[h * N + n0 + 1] : 0.f));
-    const float k0 = round_to<bf16>(b0 + (kb ? kb[h * N + n0] : 0.f));
-    const float k1 = round_to<bf16>(b1 + (kb ? kb[h * N + n0 + 1] : 0.f));
+  r.seg[w * 32 + i] = acc;
+  __syncthreads();
+  float off = 0.f;
+  if (i < d.A) {
+    off = phase0[i];
+    for (int v = 0; v < w; ++v) off += r.seg[v * 32 + i];
+  }
+#pragma unroll 1
+  for (int j = 0; j < 16; ++j) {
+    const int e = (16 * w + j) * 33 + i;
     float cs = 1.f, sn = 0.f;
-    if (i < d.A) sincosf(theta[tt * 33 + i], &sn, &cs);
-    if (Qs) *reinterpret_cast<__nv_bfloat162*>(Qs + tt * TS + n0) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
-    if (Ks) *reinterpret_cast<__nv_bfloat162*>(Ks + tt * TS + n0) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
-    if (cosv) { cosv[tt * 33 + i] = cs; sinv[tt * 33 + i] = sn; }
+    if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
+    cosv[e] = cs;
+    sinv[e] = sn;
   }
 }
 
-// Copy a [64 tokens][64] slice of a [B,T,H*64] bf16 tensor into a tile.
-M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16* T) {
-  for (int idx = threadIdx.x; idx < C * P / 8; idx += CTH) {
-    const int tt = idx / (P / 8), c8 = idx % (P / 8), t = t0 + tt;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (t < d.T) v = *reinterpret_cast<const uint4*>(src + (size_t(b) * d.T + t) * d.H * P + h * P + 8 * c8);
-    *reinterpret_cast<uint4*>(T + tt * TS + 8 * c8) = v;
+M4_DEV uint32_t ld_u32(const bf16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+M4_DEV float lo_f(uint32_t v) { return __uint_as_float(v << 16); }
+M4_DEV float hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Rotated, rounded queries/keys of a chunk as bf16 tiles (either may be null).
+// Lane = angle pair i, warp w = tokens w, w+4, ..., w+60; all global loads are
+// issued before the rotation.
+M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const bf16* bk, const float* qb,
+                     const float* kb, const float* cosv, const float* sinv, bf16* Qs, bf16* Ks) {
+  const int i = threadIdx.x & 31, w = threadIdx.x >> 5, n0 = 2 * i;
+  const float qb0 = qb ? qb[h * N + n0] : 0.f, qb1 = qb ? qb[h * N + n0 + 1] : 0.f;
+  const float kb0 = kb ? kb[h * N + n0] : 0.f, kb1 = kb ? kb[h * N + n0 + 1] : 0.f;
+  uint32_t cr[16], br[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int t = t0 + w + 4 * k;
+    const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
+    cr[k] = (Qs && t < d.T) ? ld_u32(cq + base + n0) : 0u;
+    br[k] = (Ks && t < d.T) ? ld_u32(bk + base + n0) : 0u;
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int tt = w + 4 * k;
+    const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
+    if (Qs) {
+      const float q0 = round_to<bf16>(lo_f(cr[k]) + qb0), q1 = round_to<bf16>(hi_f(cr[k]) + qb1);
+      *reinterpret_cast<__nv_bfloat162*>(Qs + tt * TS + n0) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
+    }
+    if (Ks) {
+      const float k0 = round_to<bf16>(lo_f(br[k]) + kb0), k1 = round_to<bf16>(hi_f(br[k]) + kb1);
+      *reinterpret_cast<__nv_bfloat162*>(Ks + tt * TS + n0) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+    }
   }
 }
 
-// Load a [64][64] fp32 block (row-major) into a bf16 tile with RN rounding.
+// Copy a [64 tokens][64] slice of a [B,T,H*64] bf16 tensor into a tile, each
+// row scaled by rowscale[t] (and rounded) when given. Four 16-byte loads per
+// thread, all in flight before the stores.
+M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16* T,
+                      const float* rowscale = nullptr) {
+  uint4 v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int idx = threadIdx.x + k * CTH, tt = idx >> 3, c8 = idx & 7, t = t0 + tt;
+    v[k] = t < d.T ? *reinterpret_cast<const uint4*>(src + (size_t(b) * d.T + t) * d.H * P + h * P + 8 * c8)
+                   : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int idx = threadIdx.x + k * CTH, tt = idx >> 3, c8 = idx & 7;
+    uint4 o = v[k];
+    if (rowscale) {
+      const float f = rowscale[tt];
+      uint32_t* u = reinterpret_cast<uint32_t*>(&v[k]);
+      uint32_t* r = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __nv_bfloat162 x2 = __floats2bfloat162_rn(lo_f(u[q]) * f, hi_f(u[q]) * f);
+        r[q] = *reinterpret_cast<const uint32_t*>(&x2);
+      }
+    }
+    *reinterpret_cast<uint4*>(T + tt * TS + 8 * c8) = o;
+  }
+}
+
+// Load a [64][64] fp32 block (row-major) into a bf16 tile with RN rounding;
+// eight 16-byte loads per thread in flight.
 M4_DEV void load_state_bf16(const float* src, bf16* T) {
-  for (int idx = threadIdx.x; idx < N * P / 4; idx += CTH) {
-    const float4 v = ld4(src + 4 * idx);
-    const int r = idx / (P / 4), c4 = idx % (P / 4);
-    *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4) = __floats2bfloat162_rn(v.x, v.y);
-    *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(v.z, v.w);
+  float4 v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] = ld4(src + 4 * (threadIdx.x + k * CTH));
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int idx = threadIdx.x + k * CTH, r = idx / (P / 4), c4 = idx % (P / 4);
+    *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4) = __floats2bfloat162_rn(v[k].x, v[k].y);
+    *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(v[k].z, v[k].w);
   }
 }
 
@@ -224,6 +294,7 @@ M4_DEV void load_state_bf16(const float* src, bf16* T) {
 // ---------------------------------------------------------------------------
 
 // Phase at every chunk start: phases[b,h,n,i] = sum_{t < 64n} rate_t[i] dt_t.
+// Warp per chunk, lane per pair, loads issued 16 tokens at a time.
 __global__ void __launch_bounds__(256) phase_kernel(Dims d, const float* __restrict__ dt,
                                                     const float* __restrict__ angles,
                                                     float* __restrict__ phases) {
@@ -233,10 +304,15 @@ __global__ void __launch_bounds__(256) phase_kernel(Dims d, const float* __restr
   for (int n = warp; n < d.nch; n += 8) {
     float acc = 0.f;
     if (lane < d.A) {
-      for (int tt = 0; tt < C; ++tt) {
-        const int t = n * C + tt;
-        if (t >= d.T) break;
-        acc = fmaf(rate_at(d, angles, b, h, t, lane), dt[(size_t(b) * d.T + t) * d.H + h], acc);
+      for (int j0 = 0; j0 < C; j0 += 16) {
+        float inc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int t = n * C + j0 + j;
+          inc[j] = t < d.T ? rate_at(d, angles, b, h, t, lane) * dt[(size_t(b) * d.T + t) * d.H + h] : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc += inc[j];
       }
     }
     loc[n * 32 + lane] = acc;
@@ -254,7 +330,8 @@ __global__ void __launch_bounds__(256) phase_kernel(Dims d, const float* __restr
 struct UpdSmem {
   bf16 Ks[C * TS];
   bf16 Vw[C * TS];
-  float theta[C * 33];
+  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  float sinv[C * 33];
   float scratch[C];
   Rows r;
 };
@@ -271,51 +348,47 @@ __global__ void __launch_bounds__(CTH) update_kernel(
   const int t0 = n * C, warp = threadIdx.x >> 5;
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta);
+  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk(d, b, h, t0, bk, bk, nullptr, kb, s.theta, nullptr, s.Ks, nullptr, nullptr);
-  for (int idx = threadIdx.x; idx < C * P / 2; idx += CTH) {
-    const int tt = idx / (P / 2), c2 = idx % (P / 2), t = t0 + tt;
-    float v0 = 0.f, v1 = 0.f;
-    if (t < d.T) {
-      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(x + (size_t(b) * d.T + t) * d.H * P + h * P + 2 * c2);
-      const float src = s.r.scl[tt] * s.r.tail[tt];
-      v0 = __low2float(v) * src;
-      v1 = __high2float(v) * src;
-    }
-    *reinterpret_cast<__nv_bfloat162*>(s.Vw + tt * TS + 2 * c2) = __floats2bfloat162_rn(v0, v1);
-  }
+  if (threadIdx.x < C) s.scratch[threadIdx.x] = s.r.scl[threadIdx.x] * s.r.tail[threadIdx.x];
+  __syncthreads();
+  build_qk(d, b, h, t0, nullptr, bk, nullptr, kb, s.theta, s.sinv, nullptr, s.Ks);
+  load_tile(d, b, h, t0, x, s.Vw, s.scratch);
   __syncthreads();
   float acc[8][4];
   zero(acc);
   mma_tile<C, 8, true, true>(acc, s.Ks, warp * 16, s.Vw, 0);  // rows n (A = K^T), cols p
-  float* dst = starts + (size_t(bh) * d.nch + n) * N * P;
-  each<8>(warp * 16, 0, [&](int r, int c, int nt, int e) { dst[r * P + c] = acc[nt][e]; });
+  store_f32<8>(starts + (size_t(bh) * d.nch + n) * N * P, P, warp * 16, acc);
   if (threadIdx.x == 0) deltas[size_t(bh) * d.nch + n] = expf(s.r.p[C - 1]);
 }
 
 // In place over chunks: starts[n] <- S_n with S_0 = 0, S_(n+1) = d_n S_n + U_n.
+// Four CTAs per (b, h), one float4 column of the state per thread; the
+// chunk slots are loaded eight at a time ahead of the serial update.
+constexpr int SPARTS = 4;
 __global__ void __launch_bounds__(256) state_kernel(Dims d, float* __restrict__ starts,
                                                     const float* __restrict__ deltas,
                                                     float* __restrict__ final_state) {
-  const int bh = blockIdx.x;
-  float4 s[4];
+  const int bh = blockIdx.x / SPARTS, i = 4 * ((blockIdx.x % SPARTS) * 256 + threadIdx.x);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int n0 = 0; n0 < d.nch; n0 += 8) {
+    float4 u[8];
+    float dl[8];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) s[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int n = 0; n < d.nch; ++n) {
-    float* slot = starts + (size_t(bh) * d.nch + n) * N * P;
-    const float dl = deltas[size_t(bh) * d.nch + n];
+    for (int j = 0; j < 8; ++j)
+      if (n0 + j < d.nch) {
+        u[j] = ld4(starts + (size_t(bh) * d.nch + n0 + j) * N * P + i);
+        dl[j] = deltas[size_t(bh) * d.nch + n0 + j];
+      }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = 4 * (threadIdx.x + 256 * k);
-      const float4 u = ld4(slot + i);
-      st4(slot + i, s[k]);
-      s[k] = make_float4(fmaf(dl, s[k].x, u.x), fmaf(dl, s[k].y, u.y), fmaf(dl, s[k].z, u.z),
-                         fmaf(dl, s[k].w, u.w));
-    }
+    for (int j = 0; j < 8; ++j)
+      if (n0 + j < d.nch) {
+        st4(starts + (size_t(bh) * d.nch + n0 + j) * N * P + i, s);
+        s = make_float4(fmaf(dl[j], s.x, u[j].x), fmaf(dl[j], s.y, u[j].y), fmaf(dl[j], s.z, u[j].z),
+                        fmaf(dl[j], s.w, u[j].w));
+      }
   }
-#pragma unroll
-  for (int k = 0; k < 4; ++k) st4(final_state + size_t(bh) * N * P + 4 * (threadIdx.x + 256 * k), s[k]);
+  st4(final_state + size_t(bh) * N * P + i, s);
 }
 
 struct OutSmem {
@@ -324,7 +397,8 @@ struct OutSmem {
   bf16 Vs[C * TS];
   bf16 Ms[C * TS];
   bf16 Ss[N * TS];
-  float theta[C * 33];
+  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  float sinv[C * 33];
   float scratch[C];
   Rows r;
 };
@@ -341,9 +415,9 @@ __global__ void __launch_bounds__(CTH) output_kernel(
   const int t0 = n * C, warp = threadIdx.x >> 5, row0 = warp * 16;
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta);
+  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk(d, b, h, t0, cq, bk, qb, kb, s.theta, s.Qs, s.Ks, nullptr, nullptr);
+  build_qk(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
   load_tile(d, b, h, t0, x, s.Vs);
   load_state_bf16(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
   __syncthreads();
@@ -386,7 +460,8 @@ __global__ void __launch_bounds__(CTH) output_kernel(
 struct DsSmem {
   bf16 Qs[C * TS];
   bf16 Ds[C * TS];
-  float theta[C * 33];
+  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  float sinv[C * 33];
   float scratch[C];
   Rows r;
 };
@@ -402,49 +477,44 @@ __global__ void __launch_bounds__(CTH) dstart_kernel(
   const int t0 = n * C, warp = threadIdx.x >> 5;
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta);
+  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk(d, b, h, t0, cq, cq, qb, nullptr, s.theta, s.Qs, nullptr, nullptr, nullptr);
-  for (int idx = threadIdx.x; idx < C * P / 2; idx += CTH) {
-    const int tt = idx / (P / 2), c2 = idx % (P / 2), t = t0 + tt;
-    float v0 = 0.f, v1 = 0.f;
-    if (t < d.T) {
-      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(dy + (size_t(b) * d.T + t) * d.H * P + h * P + 2 * c2);
-      v0 = __low2float(v) * s.r.ept[tt];
-      v1 = __high2float(v) * s.r.ept[tt];
-    }
-    *reinterpret_cast<__nv_bfloat162*>(s.Ds + tt * TS + 2 * c2) = __floats2bfloat162_rn(v0, v1);
-  }
+  build_qk(d, b, h, t0, cq, nullptr, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
+  load_tile(d, b, h, t0, dy, s.Ds, s.r.ept);
   __syncthreads();
   float acc[8][4];
   zero(acc);
   mma_tile<C, 8, true, true>(acc, s.Qs, warp * 16, s.Ds, 0);  // Q^T D: rows n, cols p
-  float* dst = carries + (size_t(bh) * d.nch + n) * N * P;
-  each<8>(warp * 16, 0, [&](int r, int c, int nt, int e) { dst[r * P + c] = acc[nt][e]; });
+  store_f32<8>(carries + (size_t(bh) * d.nch + n) * N * P, P, warp * 16, acc);
 }
 
 // Reverse over chunks, in place: carries[n] <- E_n (cotangent of chunk n's end
-// state); E_(nch-1) = d_final, E_(n-1) = D_n + d_n E_n.
+// state); E_(nch-1) = d_final, E_(n-1) = D_n + d_n E_n. Same split and
+// look-ahead as state_kernel.
 __global__ void __launch_bounds__(256) carry_kernel(Dims d, float* __restrict__ carries,
                                                     const float* __restrict__ deltas,
                                                     const float* __restrict__ d_final) {
-  const int bh = blockIdx.x;
-  float4 e[4];
+  const int bh = blockIdx.x / SPARTS, i = 4 * ((blockIdx.x % SPARTS) * 256 + threadIdx.x);
+  float4 e = d_final ? ld4(d_final + size_t(bh) * N * P + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int m0 = 0; m0 < d.nch; m0 += 8) {
+    float4 u[8];
+    float dl[8];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int i = 4 * (threadIdx.x + 256 * k);
-    e[k] = d_final ? ld4(d_final + size_t(bh) * N * P + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  for (int n = d.nch - 1; n >= 0; --n) {
-    float* slot = carries + (size_t(bh) * d.nch + n) * N * P;
-    const float dl = deltas[size_t(bh) * d.nch + n];
+    for (int j = 0; j < 8; ++j) {
+      const int n = d.nch - 1 - m0 - j;
+      if (n >= 0) {
+        u[j] = ld4(carries + (size_t(bh) * d.nch + n) * N * P + i);
+        dl[j] = deltas[size_t(bh) * d.nch + n];
+      }
+    }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = 4 * (threadIdx.x + 256 * k);
-      const float4 dn = ld4(slot + i);
-      st4(slot + i, e[k]);
-      e[k] = make_float4(fmaf(dl, e[k].x, dn.x), fmaf(dl, e[k].y, dn.y), fmaf(dl, e[k].z, dn.z),
-                         fmaf(dl, e[k].w, dn.w));
+    for (int j = 0; j < 8; ++j) {
+      const int n = d.nch - 1 - m0 - j;
+      if (n >= 0) {
+        st4(carries + (size_t(bh) * d.nch + n) * N * P + i, e);
+        e = make_float4(fmaf(dl[j], e.x, u[j].x), fmaf(dl[j], e.y, u[j].y), fmaf(dl[j], e.z, u[j].z),
+                        fmaf(dl[j], e.w, u[j].w));
+      }
     }
   }
 }
@@ -467,14 +537,15 @@ struct GradSmem {
   bf16 Ks[C * TS];
   bf16 Vs[C * TS];
   bf16 Dy[C * TS];
-  bf16 Ms[C * TS];   // rd(scores o W), rd(d_mixed o W), then rd(dY o e^p)
+  bf16 Ms[C * TS];   // rd(scores o W), then rd(dY o e^p)
+  bf16 Mt[C * TS];   // rd(d_mixed o W)
   bf16 Es[N * TS];   // rd(E_n)
   bf16 Ss[N * TS];   // rd(S_n)
-  float Sc[C * FS];  // scores (fp32)
-  float Dm[C * FS];  // d_mixed (fp32)
-  float theta[C * 33];
+  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  float sinv[C * 33];
   float vec[8 * C];
-  float bq[4 * N];   // per-warp bias partials
+  float col[2][4 * C];  // per-warp column sums of d_weights o W and d_weights o decay
+  float bq[4 * N];      // per-warp bias partials
   float bk[4 * N];
   float scratch[C];
   Rows r;
@@ -493,33 +564,106 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
   const int g = lane >> 2, cc = lane & 3;
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta);
+  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk(d, b, h, t0, cq, bk, qb, kb, s.theta, s.Qs, s.Ks, nullptr, nullptr);
+  build_qk(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
   load_tile(d, b, h, t0, x, s.Vs);
   load_tile(d, b, h, t0, dy, s.Dy);
-  load_state_bf16(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
-  load_state_bf16(carries + (size_t(bh) * d.nch + n) * N * P, s.Es);
-  __syncthreads();
-  auto wgt = [&](int t, int sidx) -> float {
-    if (sidx < t) return expf(s.r.p[t] - s.r.p[sidx]) * s.r.scl[sidx];
-    return sidx == t ? s.r.gam[t] : 0.f;
-  };
-  // Scores and d_mixed (rows t, cols s), fp32.
+  // rd(S_n), rd(E_n) as tiles and <E_n, S_n> (fp32 values) for the chunk-end decay.
   {
-    float acc[8][4];
-    zero(acc);
-    mma_tile<N, 8, false, false>(acc, s.Qs, row0, s.Ks, 0);
-    each<8>(row0, 0, [&](int r, int c, int nt, int e) { s.Sc[r * FS + c] = acc[nt][e]; });
-    zero(acc);
-    mma_tile<P, 8, false, false>(acc, s.Dy, row0, s.Vs, 0);
-    each<8>(row0, 0, [&](int r, int c, int nt, int e) { s.Dm[r * FS + c] = acc[nt][e]; });
+    const float* Sg = starts + (size_t(bh) * d.nch + n) * N * P;
+    const float* Eg = carries + (size_t(bh) * d.nch + n) * N * P;
+    float part = 0.f;
+    float4 sv[8], ev[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      sv[k] = ld4(Sg + 4 * (tid + k * CTH));
+      ev[k] = ld4(Eg + 4 * (tid + k * CTH));
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int idx = tid + k * CTH;
+      const float4 a4 = sv[k], e4 = ev[k];
+      const int r = idx / (P / 4), c4 = idx % (P / 4);
+      *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4) = __floats2bfloat162_rn(a4.x, a4.y);
+      *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(a4.z, a4.w);
+      *reinterpret_cast<__nv_bfloat162*>(s.Es + r * TS + 4 * c4) = __floats2bfloat162_rn(e4.x, e4.y);
+      *reinterpret_cast<__nv_bfloat162*>(s.Es + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(e4.z, e4.w);
+      part = fmaf(a4.x, e4.x, fmaf(a4.y, e4.y, fmaf(a4.z, e4.z, fmaf(a4.w, e4.w, part))));
+    }
+    part = warp_sum(part);
+    if (lane == 0) s.scratch[warp] = part;
   }
   __syncthreads();
-  for (int idx = tid; idx < C * C / 2; idx += CTH) {
-    const int t = idx / (C / 2), s2 = 2 * (idx % (C / 2));
-    *reinterpret_cast<__nv_bfloat162*>(s.Ms + t * TS + s2) =
-        __floats2bfloat162_rn(s.Sc[t * FS + s2] * wgt(t, s2), s.Sc[t * FS + s2 + 1] * wgt(t, s2 + 1));
+  // Scores Q K^T and d_mixed dY V^T (rows t, cols s) stay in registers. Each
+  // element gives the two masked tiles rd(scores o W) and rd(d_mixed o W) and
+  // the per-token sums of d_weights = d_mixed o scores:
+  //   row t:    sum_{s<t} dw W,  column s: sum_{u>s} dw W and sum_{u>s} dw decay,
+  // with W = decay(t, s) scale_s below the diagonal and gamma_t on it.
+  {
+    float sc[8][4], dm[8][4];
+    zero(sc);
+    zero(dm);
+    mma_tile<N, 8, false, false>(sc, s.Qs, row0, s.Ks, 0);
+    mma_tile<P, 8, false, false>(dm, s.Dy, row0, s.Vs, 0);
+    float rsum[2] = {0.f, 0.f}, c1[8][2], c2[8][2];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int t = row0 + g + 8 * hf;
+      const float pt = s.r.p[t];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        float ms[2], mt[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int sidx = nt * 8 + 2 * cc + e;
+          const float vs = sc[nt][2 * hf + e], vd = dm[nt][2 * hf + e], dw = vd * vs;
+          float w = 0.f, dec = 0.f;
+          if (sidx < t) {
+            dec = expf(pt - s.r.p[sidx]);
+            w = dec * s.r.scl[sidx];
+          } else if (sidx == t) {
+            w = s.r.gam[t];
+            s.vec[3 * C + t] = dw;
+          }
+          ms[e] = vs * w;
+          mt[e] = vd * w;
+          const float dww = sidx < t ? dw * w : 0.f;
+          rsum[hf] += dww;
+          if (hf == 0) {
+            c1[nt][e] = dww;
+            c2[nt][e] = dw * dec;
+          } else {
+            c1[nt][e] += dww;
+            c2[nt][e] = fmaf(dw, dec, c2[nt][e]);
+          }
+        }
+        *reinterpret_cast<__nv_bfloat162*>(s.Ms + t * TS + nt * 8 + 2 * cc) = __floats2bfloat162_rn(ms[0], ms[1]);
+        *reinterpret_cast<__nv_bfloat162*>(s.Mt + t * TS + nt * 8 + 2 * cc) = __floats2bfloat162_rn(mt[0], mt[1]);
+      }
+    }
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      float v = rsum[hf];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (cc == 0) s.vec[7 * C + row0 + g + 8 * hf] = v;
+    }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float a = c1[nt][e], v = c2[nt][e];
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          a += __shfl_xor_sync(0xffffffffu, a, off);
+          v += __shfl_xor_sync(0xffffffffu, v, off);
+        }
+        if (g == 0) {
+          s.col[0][warp * C + nt * 8 + 2 * cc + e] = a;
+          s.col[1][warp * C + nt * 8 + 2 * cc + e] = v;
+        }
+      }
   }
   __syncthreads();
   // dV = rd(Sc o W)^T dY + src o (K rd(E)) -> dx.
@@ -543,19 +687,12 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
       }
     }
   }
-  __syncthreads();
-  for (int idx = tid; idx < C * C / 2; idx += CTH) {
-    const int t = idx / (C / 2), s2 = 2 * (idx % (C / 2));
-    *reinterpret_cast<__nv_bfloat162*>(s.Ms + t * TS + s2) =
-        __floats2bfloat162_rn(s.Dm[t * FS + s2] * wgt(t, s2), s.Dm[t * FS + s2 + 1] * wgt(t, s2 + 1));
-  }
-  __syncthreads();
   // dQ, dK (rows t / s, cols n) in registers.
   float gq[8][4], gk[8][4];
   zero(gq);
   zero(gk);
-  mma_tile<C, 8, false, true>(gq, s.Ms, row0, s.Ks, 0);   // rd(Dm o W) K
-  mma_tile<C, 8, true, true>(gk, s.Ms, row0, s.Qs, 0);    // rd(Dm o W)^T Q
+  mma_tile<C, 8, false, true>(gq, s.Mt, row0, s.Ks, 0);   // rd(Dm o W) K
+  mma_tile<C, 8, true, true>(gk, s.Mt, row0, s.Qs, 0);    // rd(Dm o W)^T Q
   __syncthreads();  // Ms is rewritten below
   for (int idx = tid; idx < C * P / 2; idx += CTH) {
     const int tt = idx / (P / 2), c2 = idx % (P / 2);
@@ -608,18 +745,6 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
       s.vec[1 * C + r] = v * s.r.ept[r];
     }
   }
-  // <E, S> for the chunk-end decay (fp32 values).
-  {
-    const float* Sg = starts + (size_t(bh) * d.nch + n) * N * P;
-    const float* Eg = carries + (size_t(bh) * d.nch + n) * N * P;
-    float part = 0.f;
-    for (int i = tid; i < N * P / 4; i += CTH) {
-      const float4 a4 = ld4(Sg + 4 * i), e4 = ld4(Eg + 4 * i);
-      part = fmaf(a4.x, e4.x, fmaf(a4.y, e4.y, fmaf(a4.z, e4.z, fmaf(a4.w, e4.w, part))));
-    }
-    part = warp_sum(part);
-    if (lane == 0) s.scratch[warp] = part;
-  }
   // Rotation backward in registers: the accumulators hold each pair (2i, 2i+1)
   // on one thread. Pre-rotation gradients to workspace, the pair phase
   // gradient into theta (same element, read then written by this thread),
@@ -628,27 +753,33 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
     float sq[8][2], sk[8][2];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) sq[nt][0] = sq[nt][1] = sk[nt][0] = sk[nt][1] = 0.f;
+    uint32_t craw[2][8], braw[2][8];
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int t = t0 + row0 + g + 8 * hf;
+      const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        craw[hf][nt] = t < d.T ? ld_u32(cq + base + 8 * nt + 2 * cc) : 0u;
+        braw[hf][nt] = t < d.T ? ld_u32(bk + base + 8 * nt + 2 * cc) : 0u;
+      }
+    }
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int tt = row0 + g + 8 * hf, t = t0 + tt;
       const bool live = t < d.T;
-      const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
       const size_t ob = ((size_t(b) * d.T + t) * d.H + h) * N;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const int i = 4 * nt + cc, n0 = 2 * i;
-        float cs = 1.f, sn = 0.f;
-        if (i < d.A) sincosf(s.theta[tt * 33 + i], &sn, &cs);
+        const float cs = s.theta[tt * 33 + i], sn = s.sinv[tt * 33 + i];
         const float gq0 = gq[nt][2 * hf], gq1 = gq[nt][2 * hf + 1];
         const float gk0 = gk[nt][2 * hf], gk1 = gk[nt][2 * hf + 1];
         const float pq0 = gq0 * cs + gq1 * sn, pq1 = gq1 * cs - gq0 * sn;
         const float pk0 = gk0 * cs + gk1 * sn, pk1 = gk1 * cs - gk0 * sn;
-        float c0 = 0.f, c1 = 0.f, b0 = 0.f, b1 = 0.f;
+        const float c0 = lo_f(craw[hf][nt]), c1 = hi_f(craw[hf][nt]);
+        const float b0 = lo_f(braw[hf][nt]), b1 = hi_f(braw[hf][nt]);
         if (live) {
-          const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162*>(cq + base + n0);
-          const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(bk + base + n0);
-          c0 = __low2float(c2); c1 = __high2float(c2);
-          b0 = __low2float(b2); b1 = __high2float(b2);
           *reinterpret_cast<float2*>(o.dq + ob + n0) = make_float2(pq0, pq1);
           *reinterpret_cast<float2*>(o.dk + ob + n0) = make_float2(pk0, pk1);
           sq[nt][0] += pq0; sq[nt][1] += pq1;
@@ -681,21 +812,13 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
       }
   }
   __syncthreads();
-  // Per-token scalar gradients from d_weights = Dm o Sc.
+  // Per-token scalar gradients.
   if (tid < C) {
     const int t = tid;
-    float rowoff = 0.f, coloff = 0.f, cdec = 0.f;
-    for (int sidx = 0; sidx < t; ++sidx)
-      rowoff = fmaf(s.Dm[t * FS + sidx] * s.Sc[t * FS + sidx], expf(s.r.p[t] - s.r.p[sidx]) * s.r.scl[sidx], rowoff);
-    for (int u = t + 1; u < C; ++u) {
-      const float dw = s.Dm[u * FS + t] * s.Sc[u * FS + t];
-      const float dec = expf(s.r.p[u] - s.r.p[t]);
-      coloff = fmaf(dw, dec * s.r.scl[t], coloff);
-      cdec = fmaf(dw, dec, cdec);
-    }
+    const float coloff = s.col[0][t] + s.col[0][C + t] + s.col[0][2 * C + t] + s.col[0][3 * C + t];
+    const float cdec = s.col[1][t] + s.col[1][C + t] + s.col[1][2 * C + t] + s.col[1][3 * C + t];
     const float flow = s.vec[0 * C + t] * s.r.scl[t] * s.r.tail[t];
-    s.vec[2 * C + t] = rowoff - coloff - flow + s.vec[1 * C + t];
-    s.vec[3 * C + t] = s.Dm[t * FS + t] * s.Sc[t * FS + t];
+    s.vec[2 * C + t] = s.vec[7 * C + t] - coloff - flow + s.vec[1 * C + t];
     s.vec[4 * C + t] = s.vec[0 * C + t] * s.r.tail[t] + cdec;
     s.vec[5 * C + t] = flow;
   } else if (tid < C + N) {
@@ -704,93 +827,165 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
     o.dkb[(size_t(bh) * d.nch + n) * N + nn] = s.bk[nn] + s.bk[N + nn] + s.bk[2 * N + nn] + s.bk[3 * N + nn];
   }
   __syncthreads();
-  if (tid < 32) {
-    float fl = s.vec[5 * C + tid] + s.vec[5 * C + 32 + tid];
-    fl = warp_sum(fl);
-    const float end = expf(s.r.p[C - 1]);
-    const float extra = fl + end * (s.scratch[0] + s.scratch[1] + s.scratch[2] + s.scratch[3]);
-    const float hi = s.vec[2 * C + 63 - tid] + (tid == 0 ? extra : 0.f);
-    const float shi = warp_inclusive_scan(hi, tid);
-    const float tot = __shfl_sync(0xffffffffu, shi, 31);
-    const float slo = warp_inclusive_scan(s.vec[2 * C + 31 - tid], tid) + tot;
-    s.vec[6 * C + 63 - tid] = shi;
-    s.vec[6 * C + 31 - tid] = slo;
-  } else if (tid >= 64 && tid - 64 < d.A) {
-    // Suffix sums of the pair phase gradient within the chunk (the carry from
-    // later chunks is added by later_kernel).
-    const int i = tid - 64;
+  // Suffix sums of the pair phase gradient: warp w over tokens 16w..16w+15,
+  // then the totals of later segments (the carry from later chunks is added
+  // by finish_kernel). Warp 0 also runs the log-decay suffix scan.
+  {
+    const int i = lane;
     float acc = 0.f;
-    for (int tt = C - 1; tt >= 0; --tt) {
-      acc += s.theta[tt * 33 + i];
-      s.theta[tt * 33 + i] = acc;
+#pragma unroll
+    for (int j = 15; j >= 0; --j) {
+      acc += s.theta[(16 * warp + j) * 33 + i];
+      s.theta[(16 * warp + j) * 33 + i] = acc;
     }
-    o.dth[(size_t(bh) * d.nch + n) * 32 + i] = acc;
+    s.r.seg[warp * 32 + i] = acc;
+    if (warp == 0) {
+      float fl = s.vec[5 * C + lane] + s.vec[5 * C + 32 + lane];
+      fl = warp_sum(fl);
+      const float end = expf(s.r.p[C - 1]);
+      const float extra = fl + end * (s.scratch[0] + s.scratch[1] + s.scratch[2] + s.scratch[3]);
+      const float hi = s.vec[2 * C + 63 - lane] + (lane == 0 ? extra : 0.f);
+      const float shi = warp_inclusive_scan(hi, lane);
+      const float tot = __shfl_sync(0xffffffffu, shi, 31);
+      const float slo = warp_inclusive_scan(s.vec[2 * C + 31 - lane], lane) + tot;
+      s.vec[6 * C + 63 - lane] = shi;
+      s.vec[6 * C + 31 - lane] = slo;
+    }
   }
   __syncthreads();
-  if (tid < C) {
-    const int tt = tid, t = t0 + tt;
-    if (t < d.T) {
-      float ddt = 0.f;
-      for (int i = 0; i < d.A; ++i) {
-        const float inc = s.theta[tt * 33 + i];
-        o.drate[((size_t(b) * d.T + t) * d.H + h) * d.A + i] = inc * s.r.dt[tt];
-        ddt = fmaf(inc, rate_at(d, angles, b, h, t, i), ddt);
-      }
+  {
+    const int i = lane;
+    float off = 0.f;
+    for (int v = warp + 1; v < 4; ++v) off += s.r.seg[v * 32 + i];
+    if (warp == 0 && i < d.A)
+      o.dth[(size_t(bh) * d.nch + n) * 32 + i] = off + s.r.seg[i];
+    // Angle-rate and dt-through-phase gradients of this warp's 16 tokens:
+    // lanes over angle pairs (coalesced rows), dt term by a warp reduction.
+    float mine = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+      const int tt = 16 * warp + j, t = t0 + tt;
+      if (t >= d.T) break;
+      const float inc = i < d.A ? s.theta[tt * 33 + i] + off : 0.f;
+      const float rate = i < d.A ? rate_at(d, angles, b, h, t, i) : 0.f;
       const size_t si = (size_t(b) * d.T + t) * d.H + h;
-      o.ddtp[si] = ddt;
-      o.dgam[si] = s.vec[3 * C + tt];
-      o.dscl[si] = s.vec[4 * C + tt];
-      o.dlog[si] = s.vec[6 * C + tt];
+      if (i < d.A) o.drate[si * d.A + i] = inc * s.r.dt[tt];
+      const float ddt = warp_sum(inc * rate);
+      if (lane == j) mine = ddt;
+    }
+    if (lane < 16) {
+      const int tt = 16 * warp + lane, t = t0 + tt;
+      if (t < d.T) {
+        const size_t si = (size_t(b) * d.T + t) * d.H + h;
+        o.ddtp[si] = mine;
+        o.dgam[si] = s.vec[3 * C + tt];
+        o.dscl[si] = s.vec[4 * C + tt];
+        o.dlog[si] = s.vec[6 * C + tt];
+      }
     }
   }
 }
 
-// Phase-gradient carry: later_n[i] = sum over chunks m > n of the chunk
-// totals; adds later * dt to the rate gradients and later . rate to the dt
-// gradient of every token of chunk n.
-__global__ void __launch_bounds__(256) later_kernel(Dims d, const float* __restrict__ dt,
-                                                    const float* __restrict__ angles,
-                                                    const float* __restrict__ dth,
-                                                    float* __restrict__ drate, float* __restrict__ ddtp) {
-  extern __shared__ float later[];  // [nch][32]
-  const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
-  if (threadIdx.x < 32) {
-    float acc = 0.f;
-    for (int n = d.nch - 1; n >= 0; --n) {
-      later[n * 32 + threadIdx.x] = acc;
-      acc += threadIdx.x < d.A ? dth[(size_t(bh) * d.nch + n) * 32 + threadIdx.x] : 0.f;
-    }
-  }
-  __syncthreads();
-  for (int t = threadIdx.x; t < d.T; t += blockDim.x) {
-    const int n = t / C;
-    const size_t si = (size_t(b) * d.T + t) * d.H + h;
-    const float dtv = dt[si];
-    float add = 0.f;
-    for (int i = 0; i < d.A; ++i) {
-      const float l = later[n * 32 + i];
-      drate[si * d.A + i] += l * dtv;
-      add = fmaf(l, rate_at(d, angles, b, h, t, i), add);
-    }
-    ddtp[si] += add;
+// In place over chunks: dth[n] <- sum over chunks m > n of the chunk totals
+// (the phase-gradient carry every token of chunk n receives).
+__global__ void later_kernel(Dims d, float* __restrict__ dth) {
+  const int bh = blockIdx.x, i = threadIdx.x;
+  float acc = 0.f;
+  for (int n = d.nch - 1; n >= 0; --n) {
+    float* slot = dth + (size_t(bh) * d.nch + n) * 32 + i;
+    const float v = i < d.A ? *slot : 0.f;
+    *slot = acc;
+    acc += v;
   }
 }
 
-// Bias gradients: sum per-chunk partials over batch and chunks (fixed order).
-__global__ void bias_kernel(Dims d, const float* __restrict__ dqb, const float* __restrict__ dkb,
-                            float* __restrict__ d_qb, float* __restrict__ d_kb) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= d.H * N) return;
-  const int h = idx / N, nn = idx % N;
+// One warp per token (b, t), lanes over angle pairs and state pairs, heads in
+// order: adds the later-chunk phase carry (rate gradient += later dt, dt
+// gradient += later . rate), applies the gate chain rule of the mamba3_fused
+// preprocessing (flashmamba.py:1142-1147) and sums the angle-rate and
+// query/key gradients over heads (shared layout) or converts them (per head).
+__global__ void __launch_bounds__(256) finish_kernel(
+    Dims d, const float* __restrict__ dt, const float* __restrict__ trap_logits,
+    const float* __restrict__ angles, const float* __restrict__ later, GradOut o, bf16* __restrict__ dc,
+    bf16* __restrict__ db, float* __restrict__ d_adt, float* __restrict__ d_dt, float* __restrict__ d_trap,
+    float* __restrict__ d_angles) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t bt = size_t(blockIdx.x) * 8 + warp;
+  if (bt >= size_t(d.B) * d.T) return;
+  const int b = int(bt / d.T), t = int(bt % d.T), n = t / C;
+  const bool pair = lane < d.A;
+  const float shared_rate = (!d.per_head && pair) ? angles[bt * d.A + lane] : 0.f;
+  float ang = 0.f, q0 = 0.f, q1 = 0.f, k0 = 0.f, k1 = 0.f;
+  for (int h0 = 0; h0 < d.H; h0 += 32) {
+    float mine = 0.f;
+    const int hn = min(32, d.H - h0);
+    for (int j = 0; j < hn; ++j) {
+      const int h = h0 + j;
+      const size_t si = bt * d.H + h;
+      const float rate = d.per_head ? (pair ? angles[si * d.A + lane] : 0.f) : shared_rate;
+      const float l = pair ? later[((size_t(b) * d.H + h) * d.nch + n) * 32 + lane] : 0.f;
+      if (pair) {
+        const float dr = fmaf(l, dt[si], o.drate[si * d.A + lane]);
+        if (d.per_head) d_angles[si * d.A + lane] = dr;
+        else ang += dr;
+      }
+      const float extra = warp_sum(l * rate);
+      if (lane == j) mine = extra;
+      const float2 gq = *reinterpret_cast<const float2*>(o.dq + si * N + 2 * lane);
+      const float2 gk = *reinterpret_cast<const float2*>(o.dk + si * N + 2 * lane);
+      if (d.per_head) {
+        *reinterpret_cast<__nv_bfloat162*>(dc + si * N + 2 * lane) = __floats2bfloat162_rn(gq.x, gq.y);
+        *reinterpret_cast<__nv_bfloat162*>(db + si * N + 2 * lane) = __floats2bfloat162_rn(gk.x, gk.y);
+      } else {
+        q0 += gq.x; q1 += gq.y; k0 += gk.x; k1 += gk.y;
+      }
+    }
+    if (lane < hn) {
+      const size_t si = bt * d.H + h0 + lane;
+      const float s = 1.f / (1.f + expf(-trap_logits[si]));
+      const float gsum = o.dgam[si] + o.dscl[si];
+      const float pv = t > 0 ? o.dscl[si - d.H] : 0.f;
+      d_dt[si] = fmaf(gsum, s, pv * (1.f - s)) + (o.ddtp[si] + mine);
+      d_trap[si] = (gsum - pv) * dt[si] * s * (1.f - s);
+      d_adt[si] = o.dlog[si];
+    }
+  }
+  if (!d.per_head) {
+    if (pair) d_angles[bt * d.A + lane] = ang;
+    *reinterpret_cast<__nv_bfloat162*>(dc + bt * N + 2 * lane) = __floats2bfloat162_rn(q0, q1);
+    *reinterpret_cast<__nv_bfloat162*>(db + bt * N + 2 * lane) = __floats2bfloat162_rn(k0, k1);
+  }
+}
+
+// Bias gradients: sum per-chunk partials over batch and chunks. Block per
+// head; 16 groups of 64 threads take interleaved (batch, chunk) slots, then
+// the groups are added in a fixed order (deterministic).
+__global__ void __launch_bounds__(1024) bias_kernel(Dims d, const float* __restrict__ dqb,
+                                                    const float* __restrict__ dkb, float* __restrict__ d_qb,
+                                                    float* __restrict__ d_kb) {
+  __shared__ float part[2][16][N];
+  const int h = blockIdx.x, nn = threadIdx.x & (N - 1), grp = threadIdx.x >> 6;
+  const int slots = d.B * d.nch;
   float sq = 0.f, sk = 0.f;
-  for (int b = 0; b < d.B; ++b)
-    for (int n = 0; n < d.nch; ++n) {
-      const size_t o = ((size_t(b) * d.H + h) * d.nch + n) * N + nn;
-      sq += dqb[o];
-      sk += dkb[o];
+#pragma unroll 4
+  for (int k = grp; k < slots; k += 16) {
+    const int b = k / d.nch, n = k % d.nch;
+    const size_t o = ((size_t(b) * d.H + h) * d.nch + n) * N + nn;
+    sq += dqb[o];
+    sk += dkb[o];
+  }
+  part[0][grp][nn] = sq;
+  part[1][grp][nn] = sk;
+  __syncthreads();
+  if (threadIdx.x < N) {
+    float q = 0.f, k = 0.f;
+    for (int gi = 0; gi < 16; ++gi) {
+      q += part[0][gi][nn];
+      k += part[1][gi][nn];
     }
-  if (d_qb) d_qb[idx] = sq;
-  if (d_kb) d_kb[idx] = sk;
+    if (d_qb) d_qb[h * N + nn] = q;
+    if (d_kb) d_kb[h * N + nn] = k;
+  }
 }
 
 }  // namespace scan2
