@@ -163,6 +163,65 @@ int m4_scan_bwd_noalloc(const M4ScanDims* dims, const void* c, const void* b, co
                         float* d_dt, float* d_trap_logits, float* d_angles,
                         float* d_q_bias, float* d_k_bias, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Model glue (PyTorch Mamba 4 LM in this repository). Fused forms of the
+ * reference's XLA elementwise code around the scan; all bf16 tensors are
+ * row-major, one row per token.
+ * ---------------------------------------------------------------------- */
+
+/* Mamba-3 mixer in-projection layout (lm/models/mamba3.py:60-73): each row of
+ * `proj` holds z [inner], x [inner], b [64], c [64], raw_dt [heads],
+ * raw_a [heads], trap [heads], angles [angles] (bfloat16). */
+typedef struct {
+  int rows;    /* B*T */
+  int inner;   /* d_model * expand, a multiple of 256, = 64 * heads */
+  int heads;   /* <= 32 */
+  int angles;  /* rotation pairs, <= 32 */
+  float eps;   /* RMSNorm epsilon of B_norm / C_norm */
+  int stride;  /* elements between rows of proj and d_proj: a multiple of 8 that
+                  is at least 2 inner + 128 + 3 heads + angles */
+} M4MixerDims;
+
+/* Rows of the per-warp partial-sum buffers the backward calls need
+ * (post: rows x heads floats; prep: rows x (128 + heads) floats). */
+size_t m4_mixer_partial_rows(const M4MixerDims* dims);
+
+/* Before the scan (lm/models/mamba3.py:76-103): c = C_norm(c), b = B_norm(b)
+ * [rows,64] bf16; x copied to [rows,inner]; dt = softplus(raw_dt + dt_bias),
+ * adt = -max(heavy_tail(raw_a), 1e-4) * dt, trap, angles as float32. */
+int m4_mixer_prep_fwd(const M4MixerDims* dims, const void* proj, const float* b_scale,
+                      const float* c_scale, const float* dt_bias, void* c_out, void* b_out,
+                      void* x_out, float* adt, float* dt, float* trap, float* angles,
+                      void* stream);
+
+/* After the scan (lm/models/mamba3.py:115-117):
+ * out = bf16((y + x * D[head]) * silu(z)), [rows, inner]. */
+int m4_mixer_post_fwd(const M4MixerDims* dims, const void* proj, const void* y, const float* D,
+                      void* out, void* stream);
+
+/* Backward of m4_mixer_post_fwd: d_y (scan cotangent, bf16 [rows,inner]), the z
+ * columns of d_proj, and dD [heads] (via dD_part). */
+int m4_mixer_post_bwd(const M4MixerDims* dims, const void* proj, const void* y, const float* D,
+                      const void* g_out, void* d_y, void* d_proj, float* dD_part, float* dD,
+                      void* stream);
+
+/* Backward of m4_mixer_prep_fwd and of the x term of the D skip: every
+ * d_proj column except z, and the B/C norm scale and dt_bias gradients. */
+int m4_mixer_prep_bwd(const M4MixerDims* dims, const void* proj, const float* b_scale,
+                      const float* c_scale, const float* dt_bias, const float* D, const void* g_out,
+                      const void* dc, const void* db, const void* dx, const float* d_adt,
+                      const float* d_dt, const float* d_trap, const float* d_angles, void* d_proj,
+                      float* part, float* d_b_scale, float* d_c_scale, float* d_dt_bias,
+                      void* stream);
+
+/* bfloat16 RMSNorm with float32 statistics (lm/models/common.py:25-45) over
+ * `features` in {256, 512, 768, 1024}; rstd [rows] is saved for backward. */
+size_t m4_rmsnorm_partial_rows(int rows);
+int m4_rmsnorm_fwd(int rows, int features, float eps, const void* x, const float* scale, void* y,
+                   float* rstd, void* stream);
+int m4_rmsnorm_bwd(int rows, int features, const void* x, const float* scale, const float* rstd,
+                   const void* gy, void* gx, float* part, float* d_scale, void* stream);
+
 /* Name of a status code (static string). */
 const char* m4_status_string(int status);
 

@@ -33,6 +33,13 @@ class ScanDims(ctypes.Structure):
                 ("chunk", _c_int), ("bf16", _c_int), ("per_head", _c_int)]
 
 
+class MixerDims(ctypes.Structure):
+    """M4MixerDims."""
+
+    _fields_ = [("rows", _c_int), ("inner", _c_int), ("heads", _c_int), ("angles", _c_int),
+                ("eps", ctypes.c_float), ("stride", _c_int)]
+
+
 # Exported symbols and their signatures (argtypes, restype).
 SIGNATURES = {
     "m4_memread_residual_bytes": ([ctypes.POINTER(MemDims)], _size),
@@ -47,6 +54,14 @@ SIGNATURES = {
                     + [_p, _size, _p], _c_int),
     "m4_scan_bwd_noalloc": ([ctypes.POINTER(ScanDims)] + [_p] * 10 + [_size] + [_p] * 11 + [_p],
                             _c_int),
+    "m4_mixer_partial_rows": ([ctypes.POINTER(MixerDims)], _size),
+    "m4_mixer_prep_fwd": ([ctypes.POINTER(MixerDims)] + [_p] * 12, _c_int),
+    "m4_mixer_post_fwd": ([ctypes.POINTER(MixerDims)] + [_p] * 5, _c_int),
+    "m4_mixer_post_bwd": ([ctypes.POINTER(MixerDims)] + [_p] * 9, _c_int),
+    "m4_mixer_prep_bwd": ([ctypes.POINTER(MixerDims)] + [_p] * 19, _c_int),
+    "m4_rmsnorm_partial_rows": ([_c_int], _size),
+    "m4_rmsnorm_fwd": ([_c_int, _c_int, ctypes.c_float] + [_p] * 5, _c_int),
+    "m4_rmsnorm_bwd": ([_c_int, _c_int] + [_p] * 8, _c_int),
     "m4_status_string": ([_c_int], ctypes.c_char_p),
     "m4_version": ([], ctypes.c_char_p),
 }

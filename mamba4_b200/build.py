@@ -16,7 +16,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 SRC = HERE / "csrc"
 LIB = HERE / "libmamba4_b200.so"
-SOURCES = ["abi.cu", "memread.cu", "scan.cu"]
+SOURCES = ["abi.cu", "memread.cu", "scan.cu", "glue.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 

@@ -26,55 +26,67 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+def scan_forward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
+    """m4_scan_fwd on padded, contiguous operands: returns y, final, residual."""
+    lib = _lib.load()
+    batch, time = c.shape[:2]
+    heads = dt.shape[-1]
+    bf16 = x.dtype == torch.bfloat16
+    dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, angles.shape[-1], CHUNK,
+                         int(bf16), int(per_head))
+    y = torch.empty_like(x)
+    final = torch.empty(batch, heads, STATE_DIM, HEAD_DIM, device=x.device)
+    nbytes = lib.m4_scan_residual_bytes(ctypes.byref(dims))
+    resid = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    _lib.check(
+        lib.m4_scan_fwd(ctypes.byref(dims), *map(_lib.ptr, (c, b, x, adt, dt, trap, angles, q_bias,
+                                                             k_bias, y, final, resid)),
+                        nbytes, _stream()),
+        "m4_scan_fwd")
+    return y, final, resid
+
+
+def scan_backward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, resid, d_y, d_final, per_head):
+    """m4_scan_bwd: returns dc, db, dx, d_adt, d_dt, d_trap, d_angles, d_q_bias, d_k_bias."""
+    lib = _lib.load()
+    batch, time = c.shape[:2]
+    heads = dt.shape[-1]
+    bf16 = x.dtype == torch.bfloat16
+    dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, angles.shape[-1], CHUNK, int(bf16),
+                         int(per_head))
+    d_y = torch.zeros_like(x) if d_y is None else d_y.to(x.dtype).contiguous()
+    d_final = None if d_final is None else d_final.float().contiguous()
+    dc, db, dx = torch.empty_like(c), torch.empty_like(b), torch.empty_like(x)
+    dadt, ddt, dtrap = torch.empty_like(adt), torch.empty_like(dt), torch.empty_like(trap)
+    dang = torch.empty_like(angles)
+    dqb = torch.empty_like(q_bias) if q_bias is not None else None
+    dkb = torch.empty_like(k_bias) if k_bias is not None else None
+    wbytes = lib.m4_scan_workspace_bytes(ctypes.byref(dims))
+    work = torch.empty(wbytes, dtype=torch.uint8, device=x.device)
+    _lib.check(
+        lib.m4_scan_bwd(ctypes.byref(dims), *map(_lib.ptr, (c, b, x, adt, dt, trap, angles, q_bias,
+                                                             k_bias, resid)),
+                        resid.numel(),
+                        *map(_lib.ptr, (d_y, d_final, dc, db, dx, dadt, ddt, dtrap, dang, dqb, dkb,
+                                        work)),
+                        wbytes, _stream()),
+        "m4_scan_bwd")
+    return dc, db, dx, dadt, ddt, dtrap, dang, dqb, dkb
+
+
 class _Scan(torch.autograd.Function):
     """Forward/backward over padded operands (N = P = 64, chunk 64)."""
 
     @staticmethod
     def forward(ctx, c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
-        lib = _lib.load()
-        batch, time = c.shape[:2]
-        heads = dt.shape[-1]
-        bf16 = x.dtype == torch.bfloat16
-        dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, angles.shape[-1], CHUNK,
-                             int(bf16), int(per_head))
-        y = torch.empty_like(x)
-        final = torch.empty(batch, heads, STATE_DIM, HEAD_DIM, device=x.device)
-        nbytes = lib.m4_scan_residual_bytes(ctypes.byref(dims))
-        resid = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
-        _lib.check(
-            lib.m4_scan_fwd(ctypes.byref(dims), *map(_lib.ptr, (c, b, x, adt, dt, trap, angles, q_bias,
-                                                                 k_bias, y, final, resid)),
-                            nbytes, _stream()),
-            "m4_scan_fwd")
+        y, final, resid = scan_forward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head)
         ctx.save_for_backward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, resid)
-        ctx.dims = (batch, time, heads, angles.shape[-1], bf16, per_head)
+        ctx.per_head = per_head
         return y, final
 
     @staticmethod
     def backward(ctx, d_y, d_final):
-        lib = _lib.load()
-        c, b, x, adt, dt, trap, angles, q_bias, k_bias, resid = ctx.saved_tensors
-        batch, time, heads, count, bf16, per_head = ctx.dims
-        dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, count, CHUNK, int(bf16),
-                             int(per_head))
-        d_y = torch.zeros_like(x) if d_y is None else d_y.to(x.dtype).contiguous()
-        d_final = None if d_final is None else d_final.float().contiguous()
-        dc, db, dx = torch.empty_like(c), torch.empty_like(b), torch.empty_like(x)
-        dadt, ddt, dtrap = torch.empty_like(adt), torch.empty_like(dt), torch.empty_like(trap)
-        dang = torch.empty_like(angles)
-        dqb = torch.empty_like(q_bias) if q_bias is not None else None
-        dkb = torch.empty_like(k_bias) if k_bias is not None else None
-        wbytes = lib.m4_scan_workspace_bytes(ctypes.byref(dims))
-        work = torch.empty(wbytes, dtype=torch.uint8, device=x.device)
-        _lib.check(
-            lib.m4_scan_bwd(ctypes.byref(dims), *map(_lib.ptr, (c, b, x, adt, dt, trap, angles, q_bias,
-                                                                 k_bias, resid)),
-                            resid.numel(),
-                            *map(_lib.ptr, (d_y, d_final, dc, db, dx, dadt, ddt, dtrap, dang, dqb, dkb,
-                                            work)),
-                            wbytes, _stream()),
-            "m4_scan_bwd")
-        return dc, db, dx, dadt, ddt, dtrap, dang, dqb, dkb, None
+        return (*scan_backward(*ctx.saved_tensors, d_y, d_final, ctx.per_head), None)
 
 
 def _prepare(c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, per_head):

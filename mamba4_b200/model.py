@@ -18,7 +18,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .flashmamba import mamba3_fused
+from .glue import mamba_mixer_core, rms_norm_bf16
 from .memory import selective_memory_fused
 
 
@@ -83,6 +83,9 @@ class RMSNorm(nn.Module):
         self.out_dtype = out_dtype
 
     def forward(self, x):
+        if (x.is_cuda and x.dtype == torch.bfloat16 and self.out_dtype == torch.bfloat16
+                and x.shape[-1] in (256, 512, 768, 1024)):
+            return rms_norm_bf16(x, self.scale, self.eps)
         x32 = x.float()
         var = x32.square().mean(-1, keepdim=True)
         return (x32 * torch.rsqrt(var + self.eps) * self.scale).to(self.out_dtype)
@@ -127,17 +130,10 @@ class Mamba3Mixer(nn.Module):
     def forward(self, u):
         cfg = self.cfg
         proj = self.in_proj(u)
-        z, x, b, c, raw_dt, raw_a, trap, angles = torch.split(proj, self.sizes, dim=-1)
-        b = self.B_norm(b)
-        c = self.C_norm(c)
-        dt = F.softplus(raw_dt.float() + self.dt_bias)
-        a = -torch.clamp(heavy_tail_activation(raw_a.float()), min=1e-4)
         with torch.autocast("cuda", enabled=False):
-            y, _ = mamba3_fused(c, b, x.to(torch.bfloat16).contiguous(), (a * dt).contiguous(),
-                                dt.contiguous(), trap.float().contiguous(), angles.float().contiguous(),
-                                q_bias=self.C_bias, k_bias=self.B_bias, chunk_size=cfg.chunk_size)
-            y = y.float() + x.float() * torch.repeat_interleave(self.D, cfg.head_dim)
-            y = (y * F.silu(z.float())).to(torch.bfloat16)
+            y = mamba_mixer_core(proj.to(torch.bfloat16), self.B_norm.scale, self.C_norm.scale, self.dt_bias,
+                                 self.D, self.C_bias, self.B_bias, inner=cfg.inner, heads=cfg.num_heads,
+                                 angles=self.angles, eps=cfg.norm_eps)
         return self.out_proj(y)
 
 
