@@ -222,6 +222,61 @@ int m4_rmsnorm_fwd(int rows, int features, float eps, const void* x, const float
 int m4_rmsnorm_bwd(int rows, int features, const void* x, const float* scale, const float* rstd,
                    const void* gy, void* gx, float* part, float* d_scale, void* stream);
 
+/* Selective-memory mixer glue (lm/models/mamba4.py:155-260): key dim 64,
+ * value dim 128, 1 to 16 heads. `rest` is the projection
+ * after the gate columns: value [128h], key [64h], query [64h],
+ * beta_raw [h], dt_raw [h], order_raw [h] per row (bf16, row stride
+ * `stride`, a multiple of 8); d_rest is contiguous with 259h columns. The
+ * gate view has row stride `gate_stride`; d_gate is contiguous [rows,128h]. */
+typedef struct {
+  int batch, time, heads;
+  int stride;       /* row stride of rest, elements */
+  int gate_stride;  /* row stride of the gate view, elements */
+  float beta_max;   /* memory_beta_max */
+} M4MemMixDims;
+
+/* Floats needed by the `part` scratch of the backward calls. */
+size_t m4_memmix_partial_floats(const M4MemMixDims* dims);
+
+/* Causal depthwise conv (weights minus `bound`, bias) + SiLU of the value/key/
+ * query channels (:98-108, :170-182); keys shifted one token (:183-194) and
+ * unit-normalised with queries (:37-39); beta = beta_max sigmoid(raw + bias),
+ * log_decay = -exp(a_log) softplus(raw + dt_bias), order logit = raw + 2. */
+int m4_memmix_prep_fwd(const M4MemMixDims* dims, const void* rest, const float* conv_w,
+                       const float* conv_b, float bound, const float* beta_bias, const float* dt_bias,
+                       const float* a_log, float* values, float* keys, float* queries, float* beta,
+                       float* log_decay, float* order_logit, void* stream);
+int m4_memmix_prep_bwd(const M4MemMixDims* dims, const void* rest, const float* conv_w,
+                       const float* conv_b, float bound, const float* beta_bias, const float* dt_bias,
+                       const float* a_log, const float* d_values, const float* d_keys,
+                       const float* d_queries, const float* d_beta, const float* d_log_decay,
+                       const float* d_order_logit, float* d_conv, void* d_rest, float* part,
+                       float* d_conv_w, float* d_conv_b, float* d_beta_bias, float* d_dt_bias,
+                       float* d_a_log, void* stream);
+
+/* Order head h_t = lam_t h_(t-1) + (1 - lam_t) v_t, lam = sigmoid(logit)
+ * (:59-95), [B,T,h,128]; backward writes d_values and four per-warp partials
+ * of d_logit per (b, t, head). */
+int m4_memmix_order_fwd(const M4MemMixDims* dims, const float* values, const float* logit,
+                        float* ordered, void* stream);
+int m4_memmix_order_bwd(const M4MemMixDims* dims, const float* values, const float* logit,
+                        const float* ordered, const float* g_ordered, float* d_values,
+                        float* d_logit4, void* stream);
+
+/* Confidence gate, D skip, order mix, read RMSNorm (eps) and SiLU gate
+ * (:238-260): y [rows, 128h] bf16, rstd [rows*h] saved for backward. */
+int m4_memmix_post_fwd(const M4MemMixDims* dims, float eps, const float* out, const float* var,
+                       const float* values, const float* ordered, const void* gate,
+                       const float* conf_scale, const float* D, const float* order_mix,
+                       const float* scale, void* y, float* rstd, void* stream);
+int m4_memmix_post_bwd(const M4MemMixDims* dims, const float* out, const float* var,
+                       const float* values, const float* ordered, const void* gate,
+                       const float* conf_scale, const float* D, const float* order_mix,
+                       const float* scale, const float* rstd, const void* g_y, float* d_out,
+                       float* d_var, float* d_values, float* d_ordered, void* d_gate, float* part,
+                       float* d_conf_scale, float* d_D, float* d_order_mix, float* d_scale,
+                       void* stream);
+
 /* Name of a status code (static string). */
 const char* m4_status_string(int status);
 

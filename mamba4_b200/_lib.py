@@ -40,6 +40,13 @@ class MixerDims(ctypes.Structure):
                 ("eps", ctypes.c_float), ("stride", _c_int)]
 
 
+class MemMixDims(ctypes.Structure):
+    """M4MemMixDims."""
+
+    _fields_ = [("batch", _c_int), ("time", _c_int), ("heads", _c_int), ("stride", _c_int),
+                ("gate_stride", _c_int), ("beta_max", ctypes.c_float)]
+
+
 # Exported symbols and their signatures (argtypes, restype).
 SIGNATURES = {
     "m4_memread_residual_bytes": ([ctypes.POINTER(MemDims)], _size),
@@ -62,6 +69,13 @@ SIGNATURES = {
     "m4_rmsnorm_partial_rows": ([_c_int], _size),
     "m4_rmsnorm_fwd": ([_c_int, _c_int, ctypes.c_float] + [_p] * 5, _c_int),
     "m4_rmsnorm_bwd": ([_c_int, _c_int] + [_p] * 8, _c_int),
+    "m4_memmix_partial_floats": ([ctypes.POINTER(MemMixDims)], _size),
+    "m4_memmix_prep_fwd": ([ctypes.POINTER(MemMixDims), _p, _p, _p, ctypes.c_float] + [_p] * 10, _c_int),
+    "m4_memmix_prep_bwd": ([ctypes.POINTER(MemMixDims), _p, _p, _p, ctypes.c_float] + [_p] * 18, _c_int),
+    "m4_memmix_order_fwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 4, _c_int),
+    "m4_memmix_order_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 7, _c_int),
+    "m4_memmix_post_fwd": ([ctypes.POINTER(MemMixDims), ctypes.c_float] + [_p] * 12, _c_int),
+    "m4_memmix_post_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 22, _c_int),
     "m4_status_string": ([_c_int], ctypes.c_char_p),
     "m4_version": ([], ctypes.c_char_p),
 }

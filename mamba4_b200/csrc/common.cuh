@@ -49,6 +49,10 @@ template <typename T> M4_DEV float round_to(float v) { return to_f<T>(from_f<T>(
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Every given pointer is 16-byte aligned (NULL counts as aligned).
+template <class... Ps>
+inline bool all_aligned16(const Ps*... ps) { return (aligned16(ps) && ...); }
+
 inline size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 inline int launch_status() {

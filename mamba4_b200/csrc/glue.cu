@@ -381,6 +381,7 @@ extern "C" int m4_mixer_prep_fwd(const M4MixerDims* m, const void* proj, const f
                                  float* trap, float* angles, void* stream) {
   const int st = check_mix(m);
   if (st != M4_OK) return st;
+  if (!all_aligned16(proj, c_out, b_out, x_out, adt, dt, trap, angles)) return M4_ERR_ALIGN;
   const Mix d = make_mix(*m);
   mixer_prep_fwd<<<row_blocks(d.rows), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
       d, static_cast<const bf16*>(proj), bscale, cscale, dt_bias, static_cast<bf16*>(c_out),
@@ -392,6 +393,7 @@ extern "C" int m4_mixer_post_fwd(const M4MixerDims* m, const void* proj, const v
                                  void* stream) {
   const int st = check_mix(m);
   if (st != M4_OK) return st;
+  if (!all_aligned16(proj, y, out)) return M4_ERR_ALIGN;
   const Mix d = make_mix(*m);
   const size_t total = size_t(d.rows) * (d.inner / 8);
   const unsigned blocks = unsigned(std::min<size_t>((total + 255) / 256, size_t(148) * 16));
@@ -405,6 +407,7 @@ extern "C" int m4_mixer_post_bwd(const M4MixerDims* m, const void* proj, const v
                                  void* stream) {
   const int st = check_mix(m);
   if (st != M4_OK) return st;
+  if (!all_aligned16(proj, y, g_out, d_y, d_proj, dD_part)) return M4_ERR_ALIGN;
   const Mix d = make_mix(*m);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int blocks = row_blocks(d.rows);
@@ -422,6 +425,7 @@ extern "C" int m4_mixer_prep_bwd(const M4MixerDims* m, const void* proj, const f
                                  float* d_bscale, float* d_cscale, float* d_dt_bias, void* stream) {
   const int st = check_mix(m);
   if (st != M4_OK) return st;
+  if (!all_aligned16(proj, g_out, dc, db, dx, d_adt, d_dt, d_trap, d_angles, d_proj, part)) return M4_ERR_ALIGN;
   const Mix d = make_mix(*m);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int blocks = row_blocks(d.rows), nw = blocks * WPB;
@@ -444,6 +448,7 @@ extern "C" int m4_rmsnorm_fwd(int rows, int features, float eps, const void* x, 
                               float* rstd, void* stream) {
   if (!x || !scale || !y || !rstd) return M4_ERR_NULL;
   if (rows <= 0) return M4_ERR_DIMS;
+  if (!all_aligned16(x, y)) return M4_ERR_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int blocks = row_blocks(rows);
   const bf16* xi = static_cast<const bf16*>(x);
@@ -462,6 +467,7 @@ extern "C" int m4_rmsnorm_bwd(int rows, int features, const void* x, const float
                               const void* gy, void* gx, float* part, float* gscale, void* stream) {
   if (!x || !scale || !rstd || !gy || !gx || !part || !gscale) return M4_ERR_NULL;
   if (rows <= 0) return M4_ERR_DIMS;
+  if (!all_aligned16(x, gy, gx)) return M4_ERR_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int blocks = row_blocks(rows);
   const bf16* xi = static_cast<const bf16*>(x);
@@ -475,5 +481,585 @@ extern "C" int m4_rmsnorm_bwd(int rows, int features, const void* x, const float
     default: return M4_ERR_UNSUPPORTED;
   }
   colsum_kernel<<<features, 256, 0, s>>>(part, blocks * WPB, features, gscale);
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Selective-memory mixer glue (lm/models/mamba4.py:155-260). Key dim 64,
+// value dim 128, up to 16 memory heads. The projection columns after
+// the gate ("rest", row stride `stride`) hold value [128h], key [64h],
+// query [64h], beta_raw [h], dt_raw [h], order_raw [h]; the depthwise causal
+// convolution runs over the 256h value/key/query channels.
+// ---------------------------------------------------------------------------
+namespace m4 {
+namespace glue {
+
+struct MemMix {
+  int B, T, heads, stride, gstride;  // gstride: row stride of the gate view
+  float beta_max;
+};
+
+M4_DEV float silu_grad(float x) {
+  const float s = sigmoid(x);
+  return s * (1.f + x * (1.f - s));
+}
+
+// Depthwise causal convolution of 8 channels at (b, t): bias + sum_j w[j] x[t-3+j].
+M4_DEV void conv8(const MemMix& d, const bf16* rest, int b, int t, int ch, const float* w_s, const float* bias_s,
+                  int C, float (&o)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = bias_s[ch + e];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int s = t - 3 + j;
+    if (s < 0) continue;
+    float x[8];
+    unpack8(ld16(rest + (size_t(b) * d.T + s) * d.stride + ch), x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = fmaf(w_s[j * C + ch + e], x[e], o[e]);
+  }
+}
+
+// Stage conv weights (minus `bound`) and bias in shared memory: [4][C] + [C].
+M4_DEV void stage_conv(const float* w, const float* bias, float bound, int C, float* w_s, float* bias_s) {
+  for (int i = threadIdx.x; i < 4 * C; i += blockDim.x) w_s[i] = w[i] - bound;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) bias_s[i] = bias[i];
+  __syncthreads();
+}
+
+// Forward: values = silu(conv) [B,T,h,128]; keys = unit(silu(conv_key)) of the
+// previous token (zero at t = 0); queries = unit(silu(conv_query)); beta,
+// log_decay, order logit [B,T,h]. One warp per token; lane owns channel
+// groups lane + 32k (8 channels each), so the 8 lanes 8j..8j+7 hold one
+// key/query head and reduce its norm with three shuffles.
+__global__ void __launch_bounds__(WPB * 32) mem_prep_fwd(
+    MemMix d, const bf16* __restrict__ rest, const float* __restrict__ conv_w, const float* __restrict__ conv_b,
+    float bound, const float* __restrict__ beta_bias, const float* __restrict__ dt_bias,
+    const float* __restrict__ a_log, float* __restrict__ values, float* __restrict__ keys,
+    float* __restrict__ queries, float* __restrict__ beta, float* __restrict__ log_decay,
+    float* __restrict__ order_logit) {
+  extern __shared__ float smem[];
+  const int h = d.heads, C = 256 * h;
+  float* w_s = smem;
+  float* bias_s = smem + 4 * C;
+  stage_conv(conv_w, conv_b, bound, C, w_s, bias_s);
+  const int lane = threadIdx.x & 31;
+  for (int row = gwarp(); row < d.B * d.T; row += nwarps()) {
+    const int b = row / d.T, t = row % d.T;
+    for (int k = 0; k < h; ++k) {
+      // Channel group lane + 32k: value below 16h, key below 24h, query above.
+      const int cg = lane + 32 * k, ch = 8 * cg;
+      const int cls = cg < 16 * h ? 0 : (cg < 24 * h ? 1 : 2);
+      float o[8];
+      if (cls == 1 && t == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = 0.f;
+      } else {
+        conv8(d, rest, b, cls == 1 ? t - 1 : t, ch, w_s, bias_s, C, o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] *= sigmoid(o[e]);
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(o[e], o[e], ss);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+      const float r = cls == 0 ? 1.f : rsqrtf(ss + 1e-6f);
+      float* dst = cls == 0 ? values + size_t(row) * 128 * h + ch
+                            : (cls == 1 ? keys + size_t(row) * 64 * h + (ch - 128 * h)
+                                        : queries + size_t(row) * 64 * h + (ch - 192 * h));
+      st4(dst, make_float4(o[0] * r, o[1] * r, o[2] * r, o[3] * r));
+      st4(dst + 4, make_float4(o[4] * r, o[5] * r, o[6] * r, o[7] * r));
+    }
+    if (lane < h) {
+      const bf16* pr = rest + size_t(row) * d.stride + C;
+      const size_t i = size_t(row) * h + lane;
+      beta[i] = d.beta_max * sigmoid(bf(pr + lane) + beta_bias[lane]);
+      log_decay[i] = -expf(a_log[lane]) * softplus(bf(pr + h + lane) + dt_bias[lane]);
+      order_logit[i] = bf(pr + 2 * h + lane) + 2.f;
+    }
+  }
+}
+
+// Backward, part 1: cotangent of the convolution output d_conv [B,T,256h]
+// (through the SiLU, the unit norms and the key shift) and the head-scalar
+// columns of d_rest, with per-warp partials of beta_bias, dt_bias, a_log.
+__global__ void __launch_bounds__(WPB * 32) mem_prep_bwd1(
+    MemMix d, const bf16* __restrict__ rest, const float* __restrict__ conv_w, const float* __restrict__ conv_b,
+    float bound, const float* __restrict__ beta_bias, const float* __restrict__ dt_bias,
+    const float* __restrict__ a_log, const float* __restrict__ d_values, const float* __restrict__ d_keys,
+    const float* __restrict__ d_queries, const float* __restrict__ d_beta, const float* __restrict__ d_log_decay,
+    const float* __restrict__ d_order, float* __restrict__ d_conv, bf16* __restrict__ d_rest,
+    float* __restrict__ part) {
+  extern __shared__ float smem[];
+  const int h = d.heads, C = 256 * h;
+  float* w_s = smem;
+  float* bias_s = smem + 4 * C;
+  stage_conv(conv_w, conv_b, bound, C, w_s, bias_s);
+  const int lane = threadIdx.x & 31;
+  float pb = 0.f, pd = 0.f, pa = 0.f;
+  for (int row = gwarp(); row < d.B * d.T; row += nwarps()) {
+    const int b = row / d.T, t = row % d.T;
+    for (int k = 0; k < h; ++k) {
+      const int cg = lane + 32 * k, ch = 8 * cg;
+      const int cls = cg < 16 * h ? 0 : (cg < 24 * h ? 1 : 2);
+      float o[8], m[8], gy[8];
+      conv8(d, rest, b, t, ch, w_s, bias_s, C, o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m[e] = o[e] * sigmoid(o[e]);
+      // The key written at token t is read by token t + 1.
+      const bool live = cls != 1 || t + 1 < d.T;
+      const float* gsrc = cls == 0 ? d_values + size_t(row) * 128 * h + ch
+                                   : (cls == 1 ? d_keys + (size_t(row) + 1) * 64 * h + (ch - 128 * h)
+                                               : d_queries + size_t(row) * 64 * h + (ch - 192 * h));
+      if (live) {
+        const float4 a0 = ld4(gsrc), a1 = ld4(gsrc + 4);
+        gy[0] = a0.x; gy[1] = a0.y; gy[2] = a0.z; gy[3] = a0.w;
+        gy[4] = a1.x; gy[5] = a1.y; gy[6] = a1.z; gy[7] = a1.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) gy[e] = 0.f;
+      }
+      float ss = 0.f, dot = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ss = fmaf(m[e], m[e], ss);
+        dot = fmaf(m[e], gy[e], dot);
+      }
+#pragma unroll
+      for (int off = 1; off < 8; off <<= 1) {
+        ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      }
+      float dc[8];
+      if (cls == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dc[e] = gy[e] * silu_grad(o[e]);
+      } else {
+        // unit(m) = m r: d m = r (g - u (u . g)), u = m r.
+        const float r = rsqrtf(ss + 1e-6f), ug = dot * r;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dc[e] = r * (gy[e] - m[e] * r * ug) * silu_grad(o[e]);
+      }
+      float* dst = d_conv + size_t(row) * C + ch;
+      st4(dst, make_float4(dc[0], dc[1], dc[2], dc[3]));
+      st4(dst + 4, make_float4(dc[4], dc[5], dc[6], dc[7]));
+    }
+    if (lane < h) {
+      const bf16* pr = rest + size_t(row) * d.stride + C;
+      bf16* gr = d_rest + size_t(row) * (C + 3 * h) + C;
+      const size_t i = size_t(row) * h + lane;
+      const float bs = sigmoid(bf(pr + lane) + beta_bias[lane]);
+      const float g_beta = d_beta[i] * d.beta_max * bs * (1.f - bs);
+      const float pre = bf(pr + h + lane) + dt_bias[lane];
+      const float rate = expf(a_log[lane]), dt = softplus(pre);
+      const float g_ld = d_log_decay[i];
+      const float g_pre = -g_ld * rate * softplus_grad(pre);
+      gr[lane] = __float2bfloat16_rn(g_beta);
+      gr[h + lane] = __float2bfloat16_rn(g_pre);
+      gr[2 * h + lane] = __float2bfloat16_rn(d_order[i]);
+      pb += g_beta;
+      pd += g_pre;
+      pa = fmaf(g_ld, -rate * dt, pa);
+    }
+  }
+  if (lane < h) {
+    const size_t w = gwarp();
+    part[w * 3 * h + lane] = pb;
+    part[w * 3 * h + h + lane] = pd;
+    part[w * 3 * h + 2 * h + lane] = pa;
+  }
+}
+
+// Backward, part 2: the depthwise causal convolution. Thread per channel pair,
+// block per (64-token tile of one sequence, 512 channels); d_x[t] =
+// sum_j w[j] d_conv[t + 3 - j] into d_rest, and per-tile partials of the
+// weight ([4][C]) and bias ([C]) gradients (tile-major rows of 5C).
+__global__ void __launch_bounds__(256) mem_prep_bwd2(MemMix d, const bf16* __restrict__ rest,
+                                                     const float* __restrict__ conv_w, float bound,
+                                                     const float* __restrict__ d_conv, bf16* __restrict__ d_rest,
+                                                     float* __restrict__ wpart) {
+  const int h = d.heads, C = 256 * h;
+  const int tiles = (d.T + 63) / 64;
+  const int tile = blockIdx.x % tiles, b = blockIdx.x / tiles;
+  const int ch = 2 * (blockIdx.y * 256 + threadIdx.x);
+  if (ch >= C) return;
+  const int t0 = tile * 64, t1 = min(d.T, t0 + 64);
+  float w[4][2];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    w[j][0] = conv_w[j * C + ch] - bound;
+    w[j][1] = conv_w[j * C + ch + 1] - bound;
+  }
+  auto dconv = [&](int t) -> float2 {
+    return t < d.T ? *reinterpret_cast<const float2*>(d_conv + (size_t(b) * d.T + t) * C + ch) : make_float2(0.f, 0.f);
+  };
+  auto xin = [&](int t) -> float2 {
+    return t >= 0 ? bf2(rest + (size_t(b) * d.T + t) * d.stride + ch) : make_float2(0.f, 0.f);
+  };
+  float2 g[4], x[4];  // g[j] = d_conv[t + j], x[j] = x[t - 3 + j]
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    g[j + 1] = dconv(t0 + j);
+    x[j + 1] = xin(t0 - 3 + j);
+  }
+  float gw[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}}, gb[2] = {0.f, 0.f};
+  for (int t = t0; t < t1; ++t) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      g[j] = g[j + 1];
+      x[j] = x[j + 1];
+    }
+    g[3] = dconv(t + 3);
+    x[3] = xin(t);
+    // d_x[t] = sum_j w[j] d_conv[t + 3 - j]
+    float dx0 = 0.f, dx1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      dx0 = fmaf(w[j][0], g[3 - j].x, dx0);
+      dx1 = fmaf(w[j][1], g[3 - j].y, dx1);
+    }
+    st_bf2(d_rest + (size_t(b) * d.T + t) * (C + 3 * h) + ch, dx0, dx1);
+    // d_w[j] += d_conv[t] x[t - 3 + j]
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      gw[j][0] = fmaf(g[0].x, x[j].x, gw[j][0]);
+      gw[j][1] = fmaf(g[0].y, x[j].y, gw[j][1]);
+    }
+    gb[0] += g[0].x;
+    gb[1] += g[0].y;
+  }
+  float* wp = wpart + size_t(b * tiles + tile) * 5 * C;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<float2*>(wp + j * C + ch) = make_float2(gw[j][0], gw[j][1]);
+  *reinterpret_cast<float2*>(wp + 4 * C + ch) = make_float2(gb[0], gb[1]);
+}
+
+// Order head h_t = lam_t h_(t-1) + (1 - lam_t) v_t, lam = sigmoid(logit)
+// (lm/models/mamba4.py:59-95, the same recurrence as its chunked form).
+// Block per (b, head), thread per value channel, 8 tokens loaded ahead.
+__global__ void __launch_bounds__(128) order_fwd(MemMix d, const float* __restrict__ values,
+                                                 const float* __restrict__ logit, float* __restrict__ ordered) {
+  const int h = d.heads, b = blockIdx.x / h, hh = blockIdx.x % h, p = threadIdx.x;
+  float state = 0.f;
+  for (int t0 = 0; t0 < d.T; t0 += 8) {
+    float v[8], l[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = t0 + j;
+      const size_t r = size_t(b) * d.T + t;
+      v[j] = t < d.T ? values[(r * h + hh) * 128 + p] : 0.f;
+      l[j] = t < d.T ? logit[r * h + hh] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = t0 + j;
+      if (t >= d.T) break;
+      state = fmaf(sigmoid(l[j]), state, sigmoid(-l[j]) * v[j]);
+      ordered[((size_t(b) * d.T + t) * h + hh) * 128 + p] = state;
+    }
+  }
+}
+
+// Reverse: G_t = g_t + lam_(t+1) G_(t+1); d v_t = (1 - lam_t) G_t;
+// d logit_t = sum_p G_t (h_(t-1) - v_t) lam_t (1 - lam_t), written as four
+// per-warp partials [B,T,h,4].
+__global__ void __launch_bounds__(128) order_bwd(MemMix d, const float* __restrict__ values,
+                                                 const float* __restrict__ logit, const float* __restrict__ ordered,
+                                                 const float* __restrict__ g_ord, float* __restrict__ d_values,
+                                                 float* __restrict__ d_logit4) {
+  const int h = d.heads, b = blockIdx.x / h, hh = blockIdx.x % h, p = threadIdx.x;
+  const int lane = p & 31, warp = p >> 5;
+  float G = 0.f, lam_next = 0.f;
+  for (int t1 = d.T; t1 > 0; t1 -= 8) {
+    float v[8], l[8], g[8], hp[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = t1 - 1 - j;
+      const size_t r = size_t(b) * d.T + t;
+      const bool live = t >= 0;
+      v[j] = live ? values[(r * h + hh) * 128 + p] : 0.f;
+      l[j] = live ? logit[r * h + hh] : 0.f;
+      g[j] = live ? g_ord[(r * h + hh) * 128 + p] : 0.f;
+      hp[j] = t >= 1 ? ordered[((r - 1) * h + hh) * 128 + p] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = t1 - 1 - j;
+      if (t < 0) break;
+      const float lam = sigmoid(l[j]), inflow = sigmoid(-l[j]);
+      G = fmaf(lam_next, G, g[j]);
+      const size_t r = size_t(b) * d.T + t;
+      d_values[(r * h + hh) * 128 + p] = inflow * G;
+      const float dl = warp_sum(G * (hp[j] - v[j])) * lam * inflow;
+      if (lane == 0) d_logit4[(r * h + hh) * 4 + warp] = dl;
+      lam_next = lam;
+    }
+  }
+}
+
+// After the read: r = out c + D v + sigmoid(order_mix) o with the confidence
+// gate c = sigmoid(1 - conf_scale log1p(var)); y = rd(rd(rmsnorm(r) s) silu(gate)).
+// One warp per (b, t, head) row of 128 values (float4 per lane).
+__global__ void __launch_bounds__(WPB * 32) mem_post_fwd(
+    MemMix d, float eps, const float* __restrict__ out, const float* __restrict__ var,
+    const float* __restrict__ values, const float* __restrict__ ordered, const bf16* __restrict__ gate,
+    const float* __restrict__ conf_scale, const float* __restrict__ Dskip, const float* __restrict__ order_mix,
+    const float* __restrict__ scale, bf16* __restrict__ y, float* __restrict__ rstd) {
+  const int lane = threadIdx.x & 31, h = d.heads;
+  for (int row = gwarp(); row < d.B * d.T * h; row += nwarps()) {
+    const int hh = row % h, tok = row / h;
+    const float cg = sigmoid(1.f - conf_scale[hh] * log1pf(var[row]));
+    const float dh = Dskip[hh], om = sigmoid(order_mix[hh]);
+    const float4 o4 = ld4(out + size_t(row) * 128 + 4 * lane), v4 = ld4(values + size_t(row) * 128 + 4 * lane);
+    const float4 q4 = ld4(ordered + size_t(row) * 128 + 4 * lane);
+    const float r[4] = {fmaf(om, q4.x, fmaf(dh, v4.x, o4.x * cg)), fmaf(om, q4.y, fmaf(dh, v4.y, o4.y * cg)),
+                        fmaf(om, q4.z, fmaf(dh, v4.z, o4.z * cg)), fmaf(om, q4.w, fmaf(dh, v4.w, o4.w * cg))};
+    const float ss = warp_sum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3]);
+    const float rs = rsqrtf(ss * (1.f / 128.f) + eps);
+    const float2 g01 = bf2(gate + size_t(tok) * d.gstride + hh * 128 + 4 * lane);
+    const float2 g23 = bf2(gate + size_t(tok) * d.gstride + hh * 128 + 4 * lane + 2);
+    const float gz[4] = {g01.x, g01.y, g23.x, g23.y};
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float n = __bfloat162float(__float2bfloat16_rn(r[e] * rs * scale[4 * lane + e]));
+      o[e] = n * (gz[e] * sigmoid(gz[e]));
+    }
+    bf16* dst = y + size_t(row) * 128 + 4 * lane;
+    st_bf2(dst, o[0], o[1]);
+    st_bf2(dst + 2, o[2], o[3]);
+    if (lane == 0) rstd[row] = rs;
+  }
+}
+
+// Partial-sum row of mem_post_bwd: scale [128], conf_scale, D, order_mix, pad
+// (132 floats keep every row 16-byte aligned for the float4 stores).
+constexpr int PROW = 132;
+
+// Backward of mem_post_fwd. Per-warp partials (a warp keeps one head because
+// the warp count is a multiple of h) in rows of PROW floats.
+__global__ void __launch_bounds__(WPB * 32) mem_post_bwd(
+    MemMix d, const float* __restrict__ out, const float* __restrict__ var, const float* __restrict__ values,
+    const float* __restrict__ ordered, const bf16* __restrict__ gate, const float* __restrict__ conf_scale,
+    const float* __restrict__ Dskip, const float* __restrict__ order_mix, const float* __restrict__ scale,
+    const float* __restrict__ rstd, const bf16* __restrict__ g_y, float* __restrict__ d_out,
+    float* __restrict__ d_var, float* __restrict__ d_values, float* __restrict__ d_ordered,
+    bf16* __restrict__ d_gate, float* __restrict__ part) {
+  const int lane = threadIdx.x & 31, h = d.heads;
+  const float4 sc = ld4(scale + 4 * lane);
+  const float s4[4] = {sc.x, sc.y, sc.z, sc.w};
+  float ps[4] = {0.f, 0.f, 0.f, 0.f}, pcs = 0.f, pD = 0.f, pom = 0.f;
+  for (int row = gwarp(); row < d.B * d.T * h; row += nwarps()) {
+    const int hh = row % h, tok = row / h;
+    const float lv = log1pf(var[row]), cs = conf_scale[hh];
+    const float u = 1.f - cs * lv, cg = sigmoid(u);
+    const float dh = Dskip[hh], om = sigmoid(order_mix[hh]);
+    const float4 o4 = ld4(out + size_t(row) * 128 + 4 * lane), v4 = ld4(values + size_t(row) * 128 + 4 * lane);
+    const float4 q4 = ld4(ordered + size_t(row) * 128 + 4 * lane);
+    const float ov[4] = {o4.x, o4.y, o4.z, o4.w}, vv[4] = {v4.x, v4.y, v4.z, v4.w}, qv[4] = {q4.x, q4.y, q4.z, q4.w};
+    const float rs = rstd[row];
+    const float2 g01 = bf2(gate + size_t(tok) * d.gstride + hh * 128 + 4 * lane);
+    const float2 g23 = bf2(gate + size_t(tok) * d.gstride + hh * 128 + 4 * lane + 2);
+    const float gz[4] = {g01.x, g01.y, g23.x, g23.y};
+    const float2 y01 = bf2(g_y + size_t(row) * 128 + 4 * lane), y23 = bf2(g_y + size_t(row) * 128 + 4 * lane + 2);
+    const float gy[4] = {y01.x, y01.y, y23.x, y23.y};
+    float rh[4], dn[4], dgz[4], dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float r = fmaf(om, qv[e], fmaf(dh, vv[e], ov[e] * cg));
+      rh[e] = r * rs;
+      const float n = __bfloat162float(__float2bfloat16_rn(rh[e] * s4[e]));
+      const float sg = sigmoid(gz[e]);
+      dn[e] = gy[e] * (gz[e] * sg);
+      dgz[e] = gy[e] * n * sg * (1.f + gz[e] * (1.f - sg));
+      ps[e] = fmaf(dn[e], rh[e], ps[e]);
+      dot = fmaf(dn[e] * s4[e], rh[e], dot);
+    }
+    const float m = warp_sum(dot) * (1.f / 128.f);
+    float dr[4], go = 0.f, gD = 0.f, gq = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      dr[e] = rs * (dn[e] * s4[e] - rh[e] * m);
+      go = fmaf(dr[e], ov[e], go);
+      gD = fmaf(dr[e], vv[e], gD);
+      gq = fmaf(dr[e], qv[e], gq);
+    }
+    st4(d_out + size_t(row) * 128 + 4 * lane, make_float4(dr[0] * cg, dr[1] * cg, dr[2] * cg, dr[3] * cg));
+    st4(d_values + size_t(row) * 128 + 4 * lane, make_float4(dr[0] * dh, dr[1] * dh, dr[2] * dh, dr[3] * dh));
+    st4(d_ordered + size_t(row) * 128 + 4 * lane, make_float4(dr[0] * om, dr[1] * om, dr[2] * om, dr[3] * om));
+    bf16* gg = d_gate + size_t(tok) * (128 * h) + hh * 128 + 4 * lane;
+    st_bf2(gg, dgz[0], dgz[1]);
+    st_bf2(gg + 2, dgz[2], dgz[3]);
+    go = warp_sum(go);
+    gD = warp_sum(gD);
+    gq = warp_sum(gq);
+    const float dsg = cg * (1.f - cg);
+    if (lane == 0) d_var[row] = go * dsg * (-cs / (1.f + var[row]));
+    pcs = fmaf(go * dsg, -lv, pcs);
+    pD += gD;
+    pom = fmaf(gq, om * (1.f - om), pom);
+  }
+  float* pw = part + size_t(gwarp()) * PROW;
+  st4(pw + 4 * lane, make_float4(ps[0], ps[1], ps[2], ps[3]));
+  if (lane == 0) {
+    pw[128] = pcs;
+    pw[129] = pD;
+    pw[130] = pom;
+    pw[131] = 0.f;
+  }
+}
+
+// Per-head sums of the mem_post_bwd partials: warp w holds head w % h.
+__global__ void head_sum_kernel(const float* __restrict__ part, int nw, int h, float* __restrict__ d_cs,
+                                float* __restrict__ d_D, float* __restrict__ d_om) {
+  const int hh = threadIdx.x;
+  if (hh >= h) return;
+  float a = 0.f, b = 0.f, c = 0.f;
+  for (int w = hh; w < nw; w += h) {
+    a += part[size_t(w) * PROW + 128];
+    b += part[size_t(w) * PROW + 129];
+    c += part[size_t(w) * PROW + 130];
+  }
+  d_cs[hh] = a;
+  d_D[hh] = b;
+  d_om[hh] = c;
+}
+
+inline int mem_blocks(int rows, int h) {
+  int blocks = row_blocks(rows);
+  blocks = ((blocks + h - 1) / h) * h;  // warp count a multiple of h
+  return blocks;
+}
+
+inline int check_mem(const M4MemMixDims* m) {
+  if (!m) return M4_ERR_NULL;
+  if (m->batch <= 0 || m->time <= 0 || m->heads <= 0) return M4_ERR_DIMS;
+  if (m->heads > 16 || m->stride % 8 != 0 || m->stride < 259 * m->heads ||
+      m->gate_stride % 2 != 0 || m->gate_stride < 128 * m->heads)
+    return M4_ERR_UNSUPPORTED;
+  return M4_OK;
+}
+
+inline MemMix make_memmix(const M4MemMixDims& m) {
+  MemMix d;
+  d.B = m.batch; d.T = m.time; d.heads = m.heads; d.stride = m.stride; d.gstride = m.gate_stride;
+  d.beta_max = m.beta_max;
+  return d;
+}
+
+}  // namespace glue
+}  // namespace m4
+
+extern "C" size_t m4_memmix_partial_floats(const M4MemMixDims* m) {
+  if (check_mem(m) != M4_OK) return 0;
+  const int h = m->heads, rows = m->batch * m->time, C = 256 * h;
+  const size_t nw_prep = size_t(row_blocks(rows)) * WPB;
+  const size_t tiles = size_t(m->batch) * ((m->time + 63) / 64);
+  const size_t nw_post = size_t(mem_blocks(rows * h, h)) * WPB;
+  const size_t a = nw_prep * 3 * h, b = tiles * 5 * C, c = nw_post * PROW;
+  return std::max(a, std::max(b, c));
+}
+
+extern "C" int m4_memmix_prep_fwd(const M4MemMixDims* m, const void* rest, const float* conv_w, const float* conv_b,
+                                  float bound, const float* beta_bias, const float* dt_bias, const float* a_log,
+                                  float* values, float* keys, float* queries, float* beta, float* log_decay,
+                                  float* order_logit, void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (!all_aligned16(rest, conv_w, values, keys, queries, beta, log_decay, order_logit)) return M4_ERR_ALIGN;
+  const MemMix d = make_memmix(*m);
+  const size_t smem = size_t(5) * 256 * d.heads * sizeof(float);
+  cudaFuncSetAttribute(mem_prep_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  mem_prep_fwd<<<row_blocks(d.B * d.T), WPB * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+      d, static_cast<const bf16*>(rest), conv_w, conv_b, bound, beta_bias, dt_bias, a_log, values, keys, queries,
+      beta, log_decay, order_logit);
+  return launch_status();
+}
+
+extern "C" int m4_memmix_prep_bwd(const M4MemMixDims* m, const void* rest, const float* conv_w, const float* conv_b,
+                                  float bound, const float* beta_bias, const float* dt_bias, const float* a_log,
+                                  const float* d_values, const float* d_keys, const float* d_queries,
+                                  const float* d_beta, const float* d_log_decay, const float* d_order,
+                                  float* d_conv, void* d_rest, float* part, float* d_conv_w, float* d_conv_b,
+                                  float* d_beta_bias, float* d_dt_bias, float* d_a_log, void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (!all_aligned16(rest, conv_w, d_values, d_keys, d_queries, d_conv, d_rest, part)) return M4_ERR_ALIGN;
+  const MemMix d = make_memmix(*m);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int h = d.heads, C = 256 * h, rows = d.B * d.T;
+  const size_t smem = size_t(5) * C * sizeof(float);
+  cudaFuncSetAttribute(mem_prep_bwd1, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const int blocks = row_blocks(rows), nw = blocks * WPB;
+  mem_prep_bwd1<<<blocks, WPB * 32, smem, s>>>(d, static_cast<const bf16*>(rest), conv_w, conv_b, bound, beta_bias,
+                                               dt_bias, a_log, d_values, d_keys, d_queries, d_beta, d_log_decay,
+                                               d_order, d_conv, static_cast<bf16*>(d_rest), part);
+  colsum_kernel<<<h, 256, 0, s>>>(part, nw, 3 * h, d_beta_bias);
+  colsum_kernel<<<h, 256, 0, s>>>(part + h, nw, 3 * h, d_dt_bias);
+  colsum_kernel<<<h, 256, 0, s>>>(part + 2 * h, nw, 3 * h, d_a_log);
+  const int tiles = (d.T + 63) / 64;
+  mem_prep_bwd2<<<dim3(d.B * tiles, (C + 511) / 512), 256, 0, s>>>(d, static_cast<const bf16*>(rest), conv_w, bound,
+                                                          d_conv, static_cast<bf16*>(d_rest), part);
+  colsum_kernel<<<4 * C, 256, 0, s>>>(part, d.B * tiles, 5 * C, d_conv_w);
+  colsum_kernel<<<C, 256, 0, s>>>(part + 4 * C, d.B * tiles, 5 * C, d_conv_b);
+  return launch_status();
+}
+
+extern "C" int m4_memmix_order_fwd(const M4MemMixDims* m, const float* values, const float* logit, float* ordered,
+                                   void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (!all_aligned16(values, logit, ordered)) return M4_ERR_ALIGN;
+  const MemMix d = make_memmix(*m);
+  order_fwd<<<d.B * d.heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(d, values, logit, ordered);
+  return launch_status();
+}
+
+extern "C" int m4_memmix_order_bwd(const M4MemMixDims* m, const float* values, const float* logit,
+                                   const float* ordered, const float* g_ordered, float* d_values, float* d_logit4,
+                                   void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (!all_aligned16(values, logit, ordered, g_ordered, d_values, d_logit4)) return M4_ERR_ALIGN;
+  const MemMix d = make_memmix(*m);
+  order_bwd<<<d.B * d.heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(d, values, logit, ordered, g_ordered,
+                                                                            d_values, d_logit4);
+  return launch_status();
+}
+
+extern "C" int m4_memmix_post_fwd(const M4MemMixDims* m, float eps, const float* out, const float* var,
+                                  const float* values, const float* ordered, const void* gate,
+                                  const float* conf_scale, const float* D, const float* order_mix,
+                                  const float* scale, void* y, float* rstd, void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (!all_aligned16(out, var, values, ordered, gate, scale, y, rstd)) return M4_ERR_ALIGN;
+  const MemMix d = make_memmix(*m);
+  const int rows = d.B * d.T * d.heads;
+  mem_post_fwd<<<mem_blocks(rows, d.heads), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      d, eps, out, var, values, ordered, static_cast<const bf16*>(gate), conf_scale, D, order_mix, scale,
+      static_cast<bf16*>(y), rstd);
+  return launch_status();
+}
+
+extern "C" int m4_memmix_post_bwd(const M4MemMixDims* m, const float* out, const float* var, const float* values,
+                                  const float* ordered, const void* gate, const float* conf_scale, const float* D,
+                                  const float* order_mix, const float* scale, const float* rstd, const void* g_y,
+                                  float* d_out, float* d_var, float* d_values, float* d_ordered, void* d_gate,
+                                  float* part, float* d_conf_scale, float* d_D, float* d_order_mix,
+                                  float* d_scale, void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (!all_aligned16(out, values, ordered, gate, scale, g_y, d_out, d_values, d_ordered, d_gate, part)) return M4_ERR_ALIGN;
+  const MemMix d = make_memmix(*m);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rows = d.B * d.T * d.heads, blocks = mem_blocks(rows, d.heads), nw = blocks * WPB;
+  mem_post_bwd<<<blocks, WPB * 32, 0, s>>>(d, out, var, values, ordered, static_cast<const bf16*>(gate), conf_scale,
+                                           D, order_mix, scale, rstd, static_cast<const bf16*>(g_y), d_out, d_var,
+                                           d_values, d_ordered, static_cast<bf16*>(d_gate), part);
+  colsum_kernel<<<128, 256, 0, s>>>(part, nw, PROW, d_scale);
+  head_sum_kernel<<<1, 32, 0, s>>>(part, nw, d.heads, d_conf_scale, d_D, d_order_mix);
   return launch_status();
 }

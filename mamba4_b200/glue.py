@@ -131,3 +131,154 @@ def rms_norm_bf16(x, scale, eps):
     if not x.is_cuda:
         raise RuntimeError("rms_norm_bf16 runs on CUDA tensors only (no CPU path)")
     return _RMSNormBF16.apply(x.to(torch.bfloat16).contiguous(), scale.float().contiguous(), eps)
+
+
+# ---------------------------------------------------------------------------
+# Selective-memory mixer glue (lm/models/mamba4.py:155-260)
+# ---------------------------------------------------------------------------
+def _row_stride(view):
+    """Row stride (elements) of a [B,T,F] view whose rows are uniformly spaced."""
+    b, t, f = view.shape
+    if view.stride(2) != 1 or (b > 1 and view.stride(0) != t * view.stride(1)):
+        raise ValueError("expected a [B,T,F] view with unit last stride and uniform row stride")
+    return view.stride(1)
+
+
+def _memmix_dims(batch, time, heads, stride, gate_stride, beta_max):
+    return _lib.MemMixDims(batch, time, heads, stride, gate_stride, beta_max)
+
+
+class _MemPrep(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, rest, conv_w, conv_b, beta_bias, dt_bias, a_log, heads, bound, beta_max):
+        lib = _lib.load()
+        batch, time, _ = rest.shape
+        dims = _memmix_dims(batch, time, heads, _row_stride(rest), 0 + 128 * heads, beta_max)
+        dev = rest.device
+        values = torch.empty(batch, time, heads, 128, device=dev)
+        keys = torch.empty(batch, time, heads, 64, device=dev)
+        queries = torch.empty_like(keys)
+        beta = torch.empty(batch, time, heads, device=dev)
+        log_decay, order_logit = torch.empty_like(beta), torch.empty_like(beta)
+        _lib.check(lib.m4_memmix_prep_fwd(ctypes.byref(dims), _lib.ptr(rest), _lib.ptr(conv_w), _lib.ptr(conv_b),
+                                          bound, *map(_lib.ptr, (beta_bias, dt_bias, a_log, values, keys, queries,
+                                                                 beta, log_decay, order_logit)), _stream()),
+                   "m4_memmix_prep_fwd")
+        ctx.save_for_backward(rest, conv_w, conv_b, beta_bias, dt_bias, a_log)
+        ctx.cfg = (heads, bound, beta_max)
+        return values, keys, queries, beta, log_decay, order_logit
+
+    @staticmethod
+    def backward(ctx, d_values, d_keys, d_queries, d_beta, d_log_decay, d_order):
+        lib = _lib.load()
+        rest, conv_w, conv_b, beta_bias, dt_bias, a_log = ctx.saved_tensors
+        heads, bound, beta_max = ctx.cfg
+        batch, time, _ = rest.shape
+        dims = _memmix_dims(batch, time, heads, _row_stride(rest), 128 * heads, beta_max)
+        dev = rest.device
+
+        def g(t, shape):
+            return torch.zeros(shape, device=dev) if t is None else t.float().contiguous()
+
+        d_values = g(d_values, (batch, time, heads, 128))
+        d_keys = g(d_keys, (batch, time, heads, 64))
+        d_queries = g(d_queries, (batch, time, heads, 64))
+        d_beta = g(d_beta, (batch, time, heads))
+        d_log_decay = g(d_log_decay, (batch, time, heads))
+        d_order = g(d_order, (batch, time, heads))
+        channels = 256 * heads
+        d_conv = torch.empty(batch, time, channels, device=dev)
+        d_rest = torch.empty(batch, time, channels + 3 * heads, dtype=torch.bfloat16, device=dev)
+        part = torch.empty(lib.m4_memmix_partial_floats(ctypes.byref(dims)), device=dev)
+        d_w, d_b = torch.empty_like(conv_w), torch.empty_like(conv_b)
+        d_bb, d_dtb, d_al = torch.empty_like(beta_bias), torch.empty_like(dt_bias), torch.empty_like(a_log)
+        _lib.check(lib.m4_memmix_prep_bwd(ctypes.byref(dims), _lib.ptr(rest), _lib.ptr(conv_w), _lib.ptr(conv_b),
+                                          bound, *map(_lib.ptr, (beta_bias, dt_bias, a_log, d_values, d_keys,
+                                                                 d_queries, d_beta, d_log_decay, d_order, d_conv,
+                                                                 d_rest, part, d_w, d_b, d_bb, d_dtb, d_al)),
+                                          _stream()), "m4_memmix_prep_bwd")
+        return d_rest, d_w, d_b, d_bb, d_dtb, d_al, None, None, None
+
+
+class _OrderScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, values, logit):
+        lib = _lib.load()
+        batch, time, heads, _ = values.shape
+        dims = _memmix_dims(batch, time, heads, 259 * heads + (-259 * heads) % 8, 128 * heads, 1.0)
+        ordered = torch.empty_like(values)
+        _lib.check(lib.m4_memmix_order_fwd(ctypes.byref(dims), *map(_lib.ptr, (values, logit, ordered)),
+                                           _stream()), "m4_memmix_order_fwd")
+        ctx.save_for_backward(values, logit, ordered)
+        return ordered
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        values, logit, ordered = ctx.saved_tensors
+        batch, time, heads, _ = values.shape
+        dims = _memmix_dims(batch, time, heads, 259 * heads + (-259 * heads) % 8, 128 * heads, 1.0)
+        d_values = torch.empty_like(values)
+        d_logit4 = torch.empty(batch, time, heads, 4, device=values.device)
+        _lib.check(lib.m4_memmix_order_bwd(ctypes.byref(dims), *map(_lib.ptr, (
+            values, logit, ordered, g.float().contiguous(), d_values, d_logit4)), _stream()),
+            "m4_memmix_order_bwd")
+        return d_values, d_logit4.sum(-1)
+
+
+class _MemPost(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, out, var, values, ordered, gate, conf_scale, D, order_mix, scale, eps):
+        lib = _lib.load()
+        batch, time, heads, _ = values.shape
+        dims = _memmix_dims(batch, time, heads, 259 * heads + (-259 * heads) % 8, _row_stride(gate), 1.0)
+        y = torch.empty(batch, time, heads * 128, dtype=torch.bfloat16, device=values.device)
+        rstd = torch.empty(batch, time, heads, device=values.device)
+        _lib.check(lib.m4_memmix_post_fwd(ctypes.byref(dims), eps, *map(_lib.ptr, (
+            out, var, values, ordered, gate, conf_scale, D, order_mix, scale, y, rstd)), _stream()),
+            "m4_memmix_post_fwd")
+        ctx.save_for_backward(out, var, values, ordered, gate, conf_scale, D, order_mix, scale, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        out, var, values, ordered, gate, conf_scale, D, order_mix, scale, rstd = ctx.saved_tensors
+        batch, time, heads, _ = values.shape
+        dims = _memmix_dims(batch, time, heads, 259 * heads + (-259 * heads) % 8, _row_stride(gate), 1.0)
+        dev = values.device
+        d_out, d_values, d_ordered = (torch.empty_like(values) for _ in range(3))
+        d_var = torch.empty_like(var)
+        d_gate = torch.empty(batch, time, heads * 128, dtype=torch.bfloat16, device=dev)
+        part = torch.empty(lib.m4_memmix_partial_floats(ctypes.byref(dims)), device=dev)
+        d_cs, d_D, d_om, d_scale = (torch.empty_like(t) for t in (conf_scale, D, order_mix, scale))
+        _lib.check(lib.m4_memmix_post_bwd(ctypes.byref(dims), *map(_lib.ptr, (
+            out, var, values, ordered, gate, conf_scale, D, order_mix, scale, rstd,
+            g.to(torch.bfloat16).contiguous(), d_out, d_var, d_values, d_ordered, d_gate, part, d_cs, d_D, d_om,
+            d_scale)), _stream()), "m4_memmix_post_bwd")
+        return d_out, d_var, d_values, d_ordered, d_gate, d_cs, d_D, d_om, d_scale, None
+
+
+def memory_mixer_prep(rest, conv_w, conv_b, beta_bias, dt_bias, a_log, *, heads, bound, beta_max):
+    """rest [B,T,259h] bf16 view (value|key|query|beta|dt|order columns) ->
+    values [B,T,h,128], unit keys (shifted one token) and queries [B,T,h,64],
+    beta, log_decay, order logit [B,T,h] (float32)."""
+    if not rest.is_cuda:
+        raise RuntimeError("memory_mixer_prep runs on CUDA tensors only (no CPU path)")
+    if rest.dtype != torch.bfloat16 or rest.shape[-1] != 259 * heads:
+        raise ValueError("memory_mixer_prep expects bf16 rows of 259 * heads columns")
+    f32 = lambda t: t.float().contiguous()  # noqa: E731
+    return _MemPrep.apply(rest, f32(conv_w), f32(conv_b), f32(beta_bias), f32(dt_bias), f32(a_log), heads,
+                          float(bound), float(beta_max))
+
+
+def order_scan(values, logit):
+    """Order head of the memory mixer: h_t = s h_(t-1) + (1 - s) v_t, s = sigmoid(logit)."""
+    return _OrderScan.apply(values.float().contiguous(), logit.float().contiguous())
+
+
+def memory_mixer_post(out, var, values, ordered, gate, conf_scale, D, order_mix, scale, eps):
+    """Confidence gate, D skip, order mix, read RMSNorm and SiLU gate -> bf16 [B,T,128h]."""
+    f32 = lambda t: t.float().contiguous()  # noqa: E731
+    return _MemPost.apply(f32(out), f32(var), f32(values), f32(ordered), gate, f32(conf_scale), f32(D),
+                          f32(order_mix), f32(scale), float(eps))

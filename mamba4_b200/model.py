@@ -18,7 +18,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .glue import mamba_mixer_core, rms_norm_bf16
+from .glue import mamba_mixer_core, memory_mixer_post, memory_mixer_prep, order_scan, rms_norm_bf16
 from .memory import selective_memory_fused
 
 
@@ -212,34 +212,26 @@ class SelectiveMemoryMixer(nn.Module):
 
     def forward(self, u):
         cfg = self.cfg
-        h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
-        batch, time, _ = u.shape
+        h = cfg.memory_heads
+        if cfg.key_dim != 64 or cfg.memory_head_dim != 128 or not cfg.memory_key_shift or cfg.conv_kernel != 4:
+            raise ValueError("the fused memory mixer supports key_dim 64, memory_head_dim 128, "
+                             "conv_kernel 4 and the key shift")
         proj = self.in_proj(u)
-        gate, value, key, query, beta_raw, dt_raw, order_raw = torch.split(proj, self.sizes, dim=-1)
         with torch.autocast("cuda", enabled=False):
-            mixed = torch.cat((value, key, query), -1)
-            mixed = F.silu(causal_conv(mixed, self.conv_weight - self.bound, self.conv_bias))
-            value = mixed[..., : cfg.inner].reshape(batch, time, h, p)
-            key = mixed[..., cfg.inner: cfg.inner + h * d].reshape(batch, time, h, d)
-            query = mixed[..., cfg.inner + h * d:].reshape(batch, time, h, d)
-            if cfg.memory_key_shift:
-                key = torch.cat((torch.zeros_like(key[:, :1]), key[:, :-1]), 1)
-            key, query = _unit(key), _unit(query)
-            beta = cfg.memory_beta_max * torch.sigmoid(beta_raw.float() + self.beta_bias)
-            dt = F.softplus(dt_raw.float() + self.dt_bias)
-            log_decay = -torch.exp(self.a_log) * dt
+            proj = proj.to(torch.bfloat16)
+            if proj.shape[-1] % 8:
+                # The fused glue reads rows with 16-byte loads.
+                proj = F.pad(proj, (0, -proj.shape[-1] % 8))
+            gate, rest = proj[..., : cfg.inner], proj[..., cfg.inner: cfg.inner + 259 * h]
+            value, key, query, beta, log_decay, order_logit = memory_mixer_prep(
+                rest, self.conv_weight, self.conv_bias, self.beta_bias, self.dt_bias, self.a_log, heads=h,
+                bound=self.bound, beta_max=cfg.memory_beta_max)
             floor = cfg.floor_min + F.softplus(self.floor)
-            res = selective_memory_fused(key, value, query, beta, log_decay, floor,
-                                         chunk_size=cfg.chunk_size)
-            read = res.output * torch.sigmoid(1 - self.confidence_scale * torch.log1p(res.variance))[..., None]
-            read = read + self.D[:, None] * value
-            if cfg.order_head:
-                logits = order_raw.float() + 2
-                ordered = order_memory_chunked(value, F.logsigmoid(logits), cfg.chunk_size)
-                read = read + torch.sigmoid(self.order_mix)[:, None] * ordered
-            read = self.read_norm(read)
-            read = (read.float() * F.silu(gate.float().reshape(read.shape))).to(torch.bfloat16)
-        return self.out_proj(read.reshape(batch, time, cfg.inner))
+            res = selective_memory_fused(key, value, query, beta, log_decay, floor, chunk_size=cfg.chunk_size)
+            ordered = order_scan(value, order_logit) if cfg.order_head else torch.zeros_like(value)
+            read = memory_mixer_post(res.output, res.variance, value, ordered, gate, self.confidence_scale,
+                                     self.D, self.order_mix, self.read_norm.scale, cfg.norm_eps)
+        return self.out_proj(read)
 
 
 class Block(nn.Module):

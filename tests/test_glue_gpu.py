@@ -87,3 +87,74 @@ def test_rms_norm_bf16_matches_composition(features):
     gb = torch.autograd.grad(yb, (xb, sb), g)
     assert rel(ga[0], gb[0]) < 1e-2
     assert rel(ga[1], gb[1]) < 1e-3
+
+
+def composite_memory_mixer(m, u):
+    """The memory mixer as plain PyTorch ops (lm/models/mamba4.py:155-260)."""
+    from mamba4_b200.memory import selective_memory_fused
+    from mamba4_b200.model import _unit, causal_conv, order_memory_chunked
+
+    cfg = m.cfg
+    h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
+    batch, time, _ = u.shape
+    proj = m.in_proj(u)
+    gate, value, key, query, beta_raw, dt_raw, order_raw = torch.split(proj, m.sizes, dim=-1)
+    mixed = torch.cat((value, key, query), -1)
+    mixed = F.silu(causal_conv(mixed, m.conv_weight - m.bound, m.conv_bias))
+    value = mixed[..., : cfg.inner].reshape(batch, time, h, p)
+    key = mixed[..., cfg.inner: cfg.inner + h * d].reshape(batch, time, h, d)
+    query = mixed[..., cfg.inner + h * d:].reshape(batch, time, h, d)
+    key = torch.cat((torch.zeros_like(key[:, :1]), key[:, :-1]), 1)
+    key, query = _unit(key), _unit(query)
+    beta = cfg.memory_beta_max * torch.sigmoid(beta_raw.float() + m.beta_bias)
+    dt = F.softplus(dt_raw.float() + m.dt_bias)
+    log_decay = -torch.exp(m.a_log) * dt
+    floor = cfg.floor_min + F.softplus(m.floor)
+    res = selective_memory_fused(key, value, query, beta, log_decay, floor)
+    read = res.output * torch.sigmoid(1 - m.confidence_scale * torch.log1p(res.variance))[..., None]
+    read = read + m.D[:, None] * value
+    ordered = order_memory_chunked(value, F.logsigmoid(order_raw.float() + 2), 64)
+    read = read + torch.sigmoid(m.order_mix)[:, None] * ordered
+    x32 = read.float()
+    read = (x32 * torch.rsqrt(x32.square().mean(-1, keepdim=True) + cfg.norm_eps) * m.read_norm.scale).to(torch.bfloat16)
+    read = (read.float() * F.silu(gate.float().reshape(read.shape))).to(torch.bfloat16)
+    return read.reshape(batch, time, cfg.inner)
+
+
+@pytest.mark.parametrize("time,d_model", [(160, 512), (64, 512), (100, 128)])
+def test_memory_mixer_glue_matches_composition(time, d_model):
+    from mamba4_b200.model import Mamba4Config, SelectiveMemoryMixer
+
+    torch.manual_seed(2)
+    cfg = Mamba4Config(d_model=d_model, layer_pattern="M")
+    m = SelectiveMemoryMixer(cfg).cuda()
+    with torch.no_grad():  # non-trivial values for the scalar parameters
+        m.confidence_scale.uniform_(0.05, 0.3)
+        m.D.uniform_(0.5, 1.5)
+        m.order_mix.uniform_(-1.5, 0.5)
+        m.read_norm.scale.uniform_(0.5, 1.5)
+        m.conv_bias.uniform_(-0.1, 0.1)
+    u = (torch.randn(2, time, d_model, device="cuda")).to(torch.bfloat16)
+    g = torch.randn(2, time, cfg.inner, device="cuda").to(torch.bfloat16)
+    out_proj = m.out_proj
+    m.out_proj = torch.nn.Identity()
+    params = [p for p in m.parameters()]
+
+    def run(fn):
+        uu = u.clone().requires_grad_()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = fn(uu)
+        grads = torch.autograd.grad(y, [uu, *params], g, allow_unused=True)
+        return y, grads
+
+    y_f, g_f = run(m)
+    y_c, g_c = run(lambda uu: composite_memory_mixer(m, uu))
+    m.out_proj = out_proj
+    assert rel(y_f, y_c) < 1e-2
+    names = ["u"] + [n for n, _ in m.named_parameters() if n != "out_proj.weight"]
+    for name, a, b in zip(names, g_f, g_c):
+        if name.startswith("out_proj"):
+            continue
+        assert a is not None and b is not None, name
+        assert torch.isfinite(a.float()).all(), name
+        assert rel(a, b) < 2e-2, (name, rel(a, b))
