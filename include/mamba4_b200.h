@@ -28,6 +28,7 @@
 #define MAMBA4_B200_H
 
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -276,6 +277,16 @@ int m4_memmix_post_bwd(const M4MemMixDims* dims, const float* out, const float* 
                        float* d_var, float* d_values, float* d_ordered, void* d_gate, float* part,
                        float* d_conf_scale, float* d_D, float* d_order_mix, float* d_scale,
                        void* stream);
+
+/* Softmax cross-entropy over bf16 logits [rows, vocab], rows `ld` elements
+ * apart (ld >= vocab, a multiple of 8; columns past vocab are ignored), with
+ * int64 targets (lm/train.py:81-87): loss and log-sum-exp [rows]; targets
+ * outside [0, vocab) give loss 0. The backward overwrites `logits` with
+ * g[r] * (softmax - onehot) in bf16 (0 past vocab). */
+int m4_cross_entropy_fwd(int rows, int vocab, int ld, const void* logits, const int64_t* targets,
+                         float* loss, float* lse, void* stream);
+int m4_cross_entropy_bwd(int rows, int vocab, int ld, void* logits, const int64_t* targets,
+                         const float* lse, const float* g, void* stream);
 
 /* Name of a status code (static string). */
 const char* m4_status_string(int status);

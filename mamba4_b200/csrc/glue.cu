@@ -1063,3 +1063,103 @@ extern "C" int m4_memmix_post_bwd(const M4MemMixDims* m, const float* out, const
   head_sum_kernel<<<1, 32, 0, s>>>(part, nw, d.heads, d_conf_scale, d_D, d_order_mix);
   return launch_status();
 }
+
+// ---------------------------------------------------------------------------
+// Cross-entropy over bf16 logits (lm/train.py:81-87: logits cast to float32,
+// optax softmax cross-entropy with integer labels). Forward: per-row loss and
+// log-sum-exp from one streaming pass; backward: the logits buffer is
+// overwritten with g_r (softmax - onehot), in bf16.
+// ---------------------------------------------------------------------------
+namespace m4 {
+namespace glue {
+
+constexpr int CE_THREADS = 512;
+
+M4_DEV void lse_merge(float& m, float& s, float m2, float s2) {
+  const float mx = fmaxf(m, m2);
+  s = (m == -INFINITY ? 0.f : s * expf(m - mx)) + (m2 == -INFINITY ? 0.f : s2 * expf(m2 - mx));
+  m = mx;
+}
+
+__global__ void __launch_bounds__(CE_THREADS) ce_fwd(int vocab, int ld, const bf16* __restrict__ logits,
+                                                     const int64_t* __restrict__ targets, float* __restrict__ loss,
+                                                     float* __restrict__ lse) {
+  __shared__ float red_m[CE_THREADS / 32], red_s[CE_THREADS / 32];
+  const int row = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bf16* lr = logits + size_t(row) * ld;
+  float m = -INFINITY, s = 0.f;
+  for (int k = threadIdx.x; k < (vocab + 7) / 8; k += CE_THREADS) {
+    float v[8];
+    unpack8(ld16(lr + 8 * k), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (8 * k + e >= vocab) v[e] = -INFINITY;
+    float bm = v[0];
+#pragma unroll
+    for (int e = 1; e < 8; ++e) bm = fmaxf(bm, v[e]);
+    float bs = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bs += expf(v[e] - bm);
+    lse_merge(m, s, bm, bs);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    lse_merge(m, s, m2, s2);
+  }
+  if (lane == 0) {
+    red_m[warp] = m;
+    red_s[warp] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = red_m[0], S = red_s[0];
+    for (int w = 1; w < CE_THREADS / 32; ++w) lse_merge(M, S, red_m[w], red_s[w]);
+    const float l = M + logf(S);
+    lse[row] = l;
+    const int64_t tg = targets[row];
+    loss[row] = (tg >= 0 && tg < vocab) ? l - __bfloat162float(lr[tg]) : 0.f;
+  }
+}
+
+__global__ void __launch_bounds__(CE_THREADS) ce_bwd(int vocab, int ld, bf16* __restrict__ logits,
+                                                     const int64_t* __restrict__ targets,
+                                                     const float* __restrict__ lse, const float* __restrict__ g) {
+  const int row = blockIdx.x;
+  bf16* lr = logits + size_t(row) * ld;
+  const float gr = g[row], l = lse[row];
+  const int64_t tg = targets[row];
+  for (int k = threadIdx.x; k < ld / 8; k += CE_THREADS) {
+    float v[8];
+    unpack8(ld16(lr + 8 * k), v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      v[e] = 8 * k + e < vocab ? gr * (expf(v[e] - l) - (8 * k + e == tg ? 1.f : 0.f)) : 0.f;
+    st16(lr + 8 * k, pack8(v));
+  }
+}
+
+}  // namespace glue
+}  // namespace m4
+
+extern "C" int m4_cross_entropy_fwd(int rows, int vocab, int ld, const void* logits, const int64_t* targets,
+                                    float* loss, float* lse, void* stream) {
+  if (!logits || !targets || !loss || !lse) return M4_ERR_NULL;
+  if (rows <= 0 || vocab <= 0 || ld < vocab) return M4_ERR_DIMS;
+  if (ld % 8 != 0) return M4_ERR_UNSUPPORTED;
+  if (!all_aligned16(logits)) return M4_ERR_ALIGN;
+  ce_fwd<<<rows, CE_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(vocab, ld, static_cast<const bf16*>(logits),
+                                                                      targets, loss, lse);
+  return launch_status();
+}
+
+extern "C" int m4_cross_entropy_bwd(int rows, int vocab, int ld, void* logits, const int64_t* targets,
+                                    const float* lse, const float* g, void* stream) {
+  if (!logits || !targets || !lse || !g) return M4_ERR_NULL;
+  if (rows <= 0 || vocab <= 0 || ld < vocab) return M4_ERR_DIMS;
+  if (ld % 8 != 0) return M4_ERR_UNSUPPORTED;
+  if (!all_aligned16(logits)) return M4_ERR_ALIGN;
+  ce_bwd<<<rows, CE_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(vocab, ld, static_cast<bf16*>(logits), targets,
+                                                                      lse, g);
+  return launch_status();
+}

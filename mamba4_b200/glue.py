@@ -282,3 +282,54 @@ def memory_mixer_post(out, var, values, ordered, gate, conf_scale, D, order_mix,
     f32 = lambda t: t.float().contiguous()  # noqa: E731
     return _MemPost.apply(f32(out), f32(var), f32(values), f32(ordered), gate, f32(conf_scale), f32(D),
                           f32(order_mix), f32(scale), float(eps))
+
+
+# ---------------------------------------------------------------------------
+# Tied output head + cross-entropy (lm/models/mamba4.py:499-504, lm/train.py:81-87)
+# ---------------------------------------------------------------------------
+class _HeadCrossEntropy(torch.autograd.Function):
+    """loss[r] = logsumexp(l_r) - l_r[target_r] with l = rd_bf16(x W^T): the
+    bf16 logits are kept (not widened to float32) and overwritten in place by
+    their gradient in the backward."""
+
+    @staticmethod
+    def forward(ctx, x, weight, targets):
+        lib = _lib.load()
+        rows, vocab = x.shape[0], weight.shape[0]
+        w16 = weight.to(torch.bfloat16)
+        if vocab % 8:
+            # Rows of 16-byte multiples: zero weight rows give ignored logits.
+            w16 = torch.nn.functional.pad(w16, (0, 0, 0, -vocab % 8))
+        ld = w16.shape[0]
+        logits = torch.matmul(x, w16.t())
+        loss = torch.empty(rows, device=x.device)
+        lse = torch.empty(rows, device=x.device)
+        _lib.check(lib.m4_cross_entropy_fwd(rows, vocab, ld, *map(_lib.ptr, (logits, targets, loss, lse)),
+                                            _stream()), "m4_cross_entropy_fwd")
+        ctx.save_for_backward(x, w16, targets, logits, lse)
+        ctx.vocab = vocab
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        lib = _lib.load()
+        x, w16, targets, logits, lse = ctx.saved_tensors
+        rows, ld = logits.shape
+        vocab = ctx.vocab
+        _lib.check(lib.m4_cross_entropy_bwd(rows, vocab, ld, *map(_lib.ptr, (logits, targets, lse,
+                                                                             g.float().contiguous())), _stream()),
+                   "m4_cross_entropy_bwd")
+        dx = torch.matmul(logits, w16)
+        dw = torch.matmul(logits.t(), x)[:vocab].float()
+        return dx, dw, None
+
+
+def head_cross_entropy(x, weight, targets):
+    """Per-token loss of the tied head: x [..., D] bf16, weight [V, D] (the
+    embedding), targets [...] int64 -> float32 loss [...]."""
+    if not x.is_cuda:
+        raise RuntimeError("head_cross_entropy runs on CUDA tensors only (no CPU path)")
+    lead = x.shape[:-1]
+    loss = _HeadCrossEntropy.apply(x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous(), weight,
+                                   targets.reshape(-1).to(torch.int64).contiguous())
+    return loss.reshape(lead)

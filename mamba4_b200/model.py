@@ -18,7 +18,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .glue import mamba_mixer_core, memory_mixer_post, memory_mixer_prep, order_scan, rms_norm_bf16
+from .glue import (head_cross_entropy, mamba_mixer_core, memory_mixer_post, memory_mixer_prep, order_scan,
+                   rms_norm_bf16)
 from .memory import selective_memory_fused
 
 
@@ -259,13 +260,21 @@ class Mamba4LM(nn.Module):
         nn.init.normal_(self.embedding.weight, 0.0, 0.02)
         self.blocks = nn.ModuleList(Block(cfg, k) for k in cfg.layer_pattern)
         self.final_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self.fused_loss = True  # forward(tokens, targets) returns per-token losses
 
-    def forward(self, tokens):
-        # bfloat16 residual stream and tied head (Embed dtype bf16, attend().astype(f32)).
+    def hidden(self, tokens):
+        # bfloat16 residual stream and final norm (Embed dtype bf16).
         x = self.embedding(tokens).to(torch.bfloat16)
         for block in self.blocks:
             x = block(x)
-        x = self.final_norm(x)
+        return self.final_norm(x)
+
+    def forward(self, tokens, targets=None):
+        """Logits [B,T,V] float32 (tied head, attend().astype(f32)); with
+        `targets`, the per-token cross-entropy [B,T] from the fused head."""
+        x = self.hidden(tokens)
+        if targets is not None:
+            return head_cross_entropy(x, self.embedding.weight, targets)
         return F.linear(x, self.embedding.weight.to(x.dtype)).float()
 
 

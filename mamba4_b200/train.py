@@ -88,9 +88,13 @@ class DataParallelTrainer:
         count = self._all_reduce(mask.sum().to(torch.float32))
         total = torch.clamp(count, min=1.0)
         with torch.autocast(tokens.device.type, dtype=torch.bfloat16, enabled=tokens.is_cuda):
-            logits = self.net(tokens)
-        losses = F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), targets.reshape(-1),
-                                 reduction="none")
+            if getattr(self.model, "fused_loss", False) and tokens.is_cuda:
+                # Per-token losses from the fused head (the model takes targets).
+                losses = self.net(tokens, targets).reshape(-1)
+            else:
+                logits = self.net(tokens)
+                losses = F.cross_entropy(logits.float().reshape(-1, logits.shape[-1]), targets.reshape(-1),
+                                         reduction="none")
         numerator = (losses * mask.reshape(-1).float()).sum()
         # DDP averages over ranks; scaling by world / global count turns the
         # average into sum-over-ranks / global count (`lm/train.py:95-99`).

@@ -158,3 +158,24 @@ def test_memory_mixer_glue_matches_composition(time, d_model):
         assert a is not None and b is not None, name
         assert torch.isfinite(a.float()).all(), name
         assert rel(a, b) < 2e-2, (name, rel(a, b))
+
+
+def test_head_cross_entropy_matches_composition():
+    from mamba4_b200.glue import head_cross_entropy
+
+    torch.manual_seed(3)
+    rows, dim, vocab = 300, 256, 997  # not a multiple of 8: padded row stride
+    x = (torch.randn(rows, dim, device="cuda")).to(torch.bfloat16)
+    w = torch.randn(vocab, dim, device="cuda") * 0.05
+    t = torch.randint(0, vocab, (rows,), device="cuda")
+    g = torch.rand(rows, device="cuda")
+    g[::7] = 0.0  # masked tokens
+    xa, wa = x.clone().requires_grad_(), w.clone().requires_grad_()
+    xb, wb = x.clone().requires_grad_(), w.clone().requires_grad_()
+    la = head_cross_entropy(xa, wa, t)
+    lb = F.cross_entropy(F.linear(xb, wb.to(torch.bfloat16)).float(), t, reduction="none")
+    torch.testing.assert_close(la, lb, rtol=1e-5, atol=1e-5)
+    ga = torch.autograd.grad(la, (xa, wa), g)
+    gb = torch.autograd.grad(lb, (xb, wb), g)
+    assert rel(ga[0], gb[0]) < 1e-2
+    assert rel(ga[1], gb[1]) < 1e-2
