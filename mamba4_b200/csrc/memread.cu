@@ -179,17 +179,49 @@ M4_DEV float2 fma2(float2 a, float b, float2 c) {
 #endif
 }
 
+// Scalar broadcast to both halves of a float2 operand, made once per column
+// step and reused by every pair update of that step (fma.rn.f32x2: two FMAs
+// per instruction on sm_100a).
+#ifndef M4_NO_FFMA2
+using dup_t = unsigned long long;
+M4_DEV dup_t dup2(float b) {
+  dup_t r;
+  asm("mov.b64 %0, {%1,%1};" : "=l"(r) : "f"(b));
+  return r;
+}
+M4_DEV float2 fma2d(float2 a, dup_t b, float2 c) {
+  unsigned long long ar, cr, dr;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(ar) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1,%2};" : "=l"(cr) : "f"(c.x), "f"(c.y));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dr) : "l"(ar), "l"(b), "l"(cr));
+  float2 d;
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dr));
+  return d;
+}
+#else
+using dup_t = float;
+M4_DEV dup_t dup2(float b) { return b; }
+M4_DEV float2 fma2d(float2 a, dup_t b, float2 c) { return make_float2(fmaf(a.x, b, c.x), fmaf(a.y, b, c.y)); }
+#endif
+
+// Shared-memory strides that keep the broadcast reads conflict-free: float2
+// rows of PS per a (the four a-rows land on disjoint banks, 16-byte aligned)
+// and float rows of KS per b (the eight b-rows of a float4 read on disjoint
+// banks).
+constexpr int PS = 10;
+constexpr int KS = 12;
+
 struct SolveSmem {
   float4 E[NPAIR / 2][32];       // running evidence (pairs 2q, 2q+1 per lane)
-  float flC[64];                 // floor[b + 8n] at b*8 + n
+  float flC[8 * KS];             // floor[b + 8n] at b*KS + n
   float w[64];                   // w = L^-1 q (forward) / u = L^-1 g (backward)
   float y[64];                   // solution
   union {
     struct {
-      float2 kP[32];             // (k[a + 8p], k[a + 4 + 8p]) at a*8 + p
-      float kC[64];              // k[b + 8n] at b*8 + n
-      float qC[64];              // q[b + 8n] at b*8 + n
-      float2 col[2][32];         // column broadcast, pairs at a*8 + p
+      float2 kP[4 * PS];         // (k[a + 8p], k[a + 4 + 8p]) at a*PS + p
+      float kC[8 * KS];          // k[b + 8n] at b*KS + n
+      float qC[8 * KS];          // q[b + 8n] at b*KS + n
+      float2 col[2][4 * PS];     // column broadcast, pairs at a*PS + p
       float colw[2][4];          // bordered-row entry per a
     } f;
     struct {
@@ -321,17 +353,17 @@ M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], Solv
   float2* cb = sm.u.f.col[J & 1];
   float* cw = sm.u.f.colw[J & 1];
   if (b == JB) {
-    store_column<JN>(cb + a * 8, A);
+    store_column<JN>(cb + a * PS, A);
     cw[a] = wr[JN];
   }
   __syncwarp();
-  const float piv = reinterpret_cast<const float*>(cb)[(JA * 8 + JN) * 2 + JH];
+  const float piv = reinterpret_cast<const float*>(cb)[(JA * PS + JN) * 2 + JH];
   const float r = rsqrtf(piv);
   const float r2 = r * r;
   rc[JN] = (b == JB) ? r : rc[JN];
   float C[8];
   {
-    const float2* cs = cb + (b & 3) * 8;
+    const float2* cs = cb + (b & 3) * PS;
     if constexpr (JN & 1) C[JN] = (b >= 4 ? cs[JN].y : cs[JN].x) * r2;
 #pragma unroll
     for (int n = (JN + 1) & ~1; n < 8; n += 2) {
@@ -342,16 +374,18 @@ M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], Solv
   }
   C[JN] = (b > JB) ? C[JN] : 0.f;
   const float rw = cw[a];
+  dup_t Cd[8];
+#pragma unroll
+  for (int n = JN; n < 8; ++n) Cd[n] = dup2(-C[n]);
 #pragma unroll
   for (int p = JN; p < 8; ++p) {
-    float2 rv = cb[a * 8 + p];
+    float2 rv = cb[a * PS + p];
     if (p == JN) {
       rv.x = (a > JB) ? rv.x : 0.f;
       rv.y = (a + 4 > JB) ? rv.y : 0.f;
     }
-    const float2 nr = make_float2(-rv.x, -rv.y);
 #pragma unroll
-    for (int n = JN; n <= p; ++n) A[pair_of(p, n)] = fma2(nr, C[n], A[pair_of(p, n)]);
+    for (int n = JN; n <= p; ++n) A[pair_of(p, n)] = fma2d(rv, Cd[n], A[pair_of(p, n)]);
   }
 #pragma unroll
   for (int n = JN; n < 8; ++n) wr[n] = fmaf(-rw, C[n], wr[n]);
@@ -392,7 +426,7 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
     }
     if (a == 0) {
 #pragma unroll
-      for (int n = 0; n < 8; ++n) sm.flC[b * 8 + n] = floor_[h * KD + b + 8 * n];
+      for (int n = 0; n < 8; ++n) sm.flC[b * KS + n] = floor_[h * KD + b + 8 * n];
     }
   }
   __syncwarp();
@@ -409,10 +443,10 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
       for (int e = 0; e < 4; ++e) {
         const int i = 4 * l + e;
         if (lane < 16) {
-          reinterpret_cast<float*>(sm.u.f.kP)[((i & 3) * 8 + (i >> 3)) * 2 + ((i >> 2) & 1)] = vv[e];
-          sm.u.f.kC[(i & 7) * 8 + (i >> 3)] = vv[e];
+          reinterpret_cast<float*>(sm.u.f.kP)[((i & 3) * PS + (i >> 3)) * 2 + ((i >> 2) & 1)] = vv[e];
+          sm.u.f.kC[(i & 7) * KS + (i >> 3)] = vv[e];
         } else {
-          sm.u.f.qC[(i & 7) * 8 + (i >> 3)] = vv[e];
+          sm.u.f.qC[(i & 7) * KS + (i >> 3)] = vv[e];
         }
       }
     }
@@ -427,13 +461,13 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
       float kc[8];
 #pragma unroll
       for (int p = 0; p < 8; p += 2) {
-        const float4 v = *reinterpret_cast<const float4*>(&sm.u.f.kP[a * 8 + p]);
+        const float4 v = *reinterpret_cast<const float4*>(&sm.u.f.kP[a * PS + p]);
         kr[p] = make_float2(bet * v.x, bet * v.y);
         kr[p + 1] = make_float2(bet * v.z, bet * v.w);
       }
 #pragma unroll
       for (int n = 0; n < 8; n += 4) {
-        const float4 k4 = ld4(&sm.u.f.kC[b * 8 + n]);
+        const float4 k4 = ld4(&sm.u.f.kC[b * KS + n]);
         kc[n] = k4.x; kc[n + 1] = k4.y; kc[n + 2] = k4.z; kc[n + 3] = k4.w;
       }
 #pragma unroll
@@ -451,10 +485,10 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
     // the query as the bordered row (rows 64.., lanes a == 0).
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
-      const float f = sm.flC[b * 8 + n];
+      const float f = sm.flC[b * KS + n];
       A[pair_of(n, n)].x += (b == a) ? f : 0.f;
       A[pair_of(n, n)].y += (b == a + 4) ? f : 0.f;
-      wr[n] = a == 0 ? sm.u.f.qC[b * 8 + n] : 0.f;
+      wr[n] = a == 0 ? sm.u.f.qC[b * KS + n] : 0.f;
     }
 
     float rc[8];
@@ -589,19 +623,31 @@ M4_DEV void chunk_gates(int tid, int b, int T, int H, int h, int t0, const float
   }
 }
 
-// Load a [64 tokens][W] chunk of a [B,T,H,W] tensor into a tile of stride ld.
+// 16-byte asynchronous global -> shared copy (cp.async, no registers); an
+// invalid source copies zeros (src-size 0; the address stays a valid one).
+M4_DEV void cp16(float* dst, const float* src, bool valid) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+// Wait for this thread's copies; a __syncthreads must follow before other
+// threads read them.
+M4_DEV void cp_wait() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Start copying a [64 tokens][W] chunk of a [B,T,H,W] tensor into a tile of
+// stride ld (tokens past T read as zero).
 template <int W>
 M4_DEV void load_tokens(float* tile, int ld, const float* src, int b, int T, int H, int h, int t0, int tid) {
+#pragma unroll
   for (int idx = tid; idx < CH * W / 4; idx += CT) {
     const int tt = idx / (W / 4), c4 = idx % (W / 4), t = t0 + tt;
-    const float4 v = t < T ? ld4(src + ((size_t(b) * T + t) * H + h) * W + 4 * c4) : make_float4(0.f, 0.f, 0.f, 0.f);
-    st4(tile + tt * ld + 4 * c4, v);
+    const bool live = t < T;
+    cp16(tile + tt * ld + 4 * c4, live ? src + ((size_t(b) * T + t) * H + h) * W + 4 * c4 : src, live);
   }
 }
 
-// Load a dense [rows][64] row-major block into a tile of stride LD.
+// Start copying a dense [rows][64] row-major block into a tile of stride LD.
 M4_DEV void load_block(float* tile, int rows, const float* src, int tid) {
-  for (int idx = tid; idx < rows * KD / 4; idx += CT) st4(tile + (idx / 16) * LD + 4 * (idx % 16), ld4(src + 4 * idx));
+  for (int idx = tid; idx < rows * KD / 4; idx += CT) cp16(tile + (idx / 16) * LD + 4 * (idx % 16), src + 4 * idx, true);
 }
 
 template <int P>
@@ -628,6 +674,7 @@ __global__ void __launch_bounds__(CT) output_kernel(
   load_tokens<P>(Vs, LP, values, b, T, H, h, t0, tid);
   load_block(C0, P, c_start + (size_t(bh) * nch + ch) * P * KD, tid);
   chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
+  cp_wait();
   __syncthreads();
   {
     float acc[4][4];
@@ -679,6 +726,7 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
   load_tokens<P>(Vs, LP, values, b, T, H, h, t0, tid);
   load_block(C0, P, c_start + (size_t(bh) * nch + ch) * P * KD, tid);
   chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
+  cp_wait();
   __syncthreads();
   {
     float acc[4][4];
@@ -787,6 +835,7 @@ __global__ void __launch_bounds__(CT) carry_kernel(
     load_block(Zs, CH, Z + (size_t(bh) * Tp + t0) * KD, tid);
     load_tokens<P>(Os, LP, d_out, b, T, H, h, t0, tid);
     chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
+    cp_wait();
     __syncthreads();
     const float end = ept[CH - 1];
     float xs[4][4], xc[NTP][4];
@@ -865,6 +914,7 @@ __global__ void __launch_bounds__(CT) grads_kernel(
   load_block(Sb, KD, sbar + (size_t(bh) * nch + ch) * KD * KD, tid);
   load_block(Cb, P, cbar + (size_t(bh) * nch + ch) * P * KD, tid);
   chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
+  cp_wait();
   __syncthreads();
   const float pl = pre[CH - 1];
   // Phase 1: GY, GZ, OV -> M1, M2 and the dW reductions.
@@ -956,15 +1006,34 @@ __global__ void __launch_bounds__(CT) grads_kernel(
   const float* s0 = s_start + (size_t(bh) * nsub + ch * (CH / SUB)) * KD * KD;
   const float* c0 = c_start + (size_t(bh) * nch + ch) * P * KD;
   {
+    // Each thread reads its own float4 slots of Sb / Cb, then overwrites the
+    // same slots with S0 / C0 (no other thread touches them in between).
+    constexpr int NS = KD * KD / 4 / CT, NC = P * KD / 4 / CT;
+    float4 sv[NS], cv[NC];
+#pragma unroll
+    for (int i = 0; i < NS; ++i) sv[i] = ld4(s0 + 4 * (tid + CT * i));
+#pragma unroll
+    for (int i = 0; i < NC; ++i) cv[i] = ld4(c0 + 4 * (tid + CT * i));
     float part = 0.f;
-    for (int idx = tid; idx < KD * KD; idx += CT) part = fmaf(Sb[(idx / KD) * LD + idx % KD], s0[idx], part);
-    for (int idx = tid; idx < P * KD; idx += CT) part = fmaf(Cb[(idx / KD) * LD + idx % KD], c0[idx], part);
+#pragma unroll
+    for (int i = 0; i < NS; ++i) {
+      const int idx = tid + CT * i;
+      float* slot = Sb + (idx / 16) * LD + 4 * (idx % 16);
+      const float4 e = ld4(slot);
+      part = fmaf(e.x, sv[i].x, fmaf(e.y, sv[i].y, fmaf(e.z, sv[i].z, fmaf(e.w, sv[i].w, part))));
+      st4(slot, sv[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int idx = tid + CT * i;
+      float* slot = Cb + (idx / 16) * LD + 4 * (idx % 16);
+      const float4 e = ld4(slot);
+      part = fmaf(e.x, cv[i].x, fmaf(e.y, cv[i].y, fmaf(e.z, cv[i].z, fmaf(e.w, cv[i].w, part))));
+      st4(slot, cv[i]);
+    }
     part = warp_sum(part);
     if (lane == 0) red[CH + warp] = part;
   }
-  __syncthreads();
-  load_block(Sb, KD, s0, tid);
-  load_block(Cb, P, c0, tid);
   __syncthreads();
   // Phase 3: extra_t = e^(P_t) (-z_t . (S0 y_t) + dO_t . (C0 y_t)).
   {
@@ -1142,7 +1211,8 @@ extern "C" int m4_memread_fwd(const M4MemDims* d, const float* keys, const float
       !c_fin || !resid)
     return M4_ERR_NULL;
   if ((init_s == nullptr) != (init_c == nullptr)) return M4_ERR_NULL;
-  if (!aligned16(keys) || !aligned16(queries) || !aligned16(resid)) return M4_ERR_ALIGN;
+  if (!all_aligned16(keys, values, queries, init_s, init_c, out, s_fin, c_fin, static_cast<const float*>(resid)))
+    return M4_ERR_ALIGN;
   if (resid_bytes < mem::sizes(*d).resid_bytes) return M4_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (d->value_dim == 64)
@@ -1168,7 +1238,9 @@ extern "C" int m4_memread_bwd(const M4MemDims* d, const float* keys, const float
   if (!keys || !values || !queries || !beta || !log_decay || !resid || !d_out || !d_var || !dk ||
       !dv || !dq || !dbeta || !dlog || !dfloor || !work)
     return M4_ERR_NULL;
-  if (!aligned16(resid) || !aligned16(work)) return M4_ERR_ALIGN;
+  if (!all_aligned16(keys, values, queries, d_out, d_sfin, d_cfin, dk, dv, dq, d_init_s, d_init_c,
+                     static_cast<const float*>(resid), static_cast<const float*>(work)))
+    return M4_ERR_ALIGN;
   const mem::Sizes z = mem::sizes(*d);
   if (resid_bytes < z.resid_bytes || work_bytes < z.work_bytes) return M4_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
