@@ -206,6 +206,27 @@ def scan_step(s):
     return y, final, grads
 
 
+def count_launches(fn):
+    """Kernels of this library (names in namespace m4::) launched by one call
+    of fn, counted by the CUDA profiler outside the timed region."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    try:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+    except RuntimeError:  # the profiler is unavailable (e.g. under another profiler)
+        return None
+    return sum(e.count for e in prof.key_averages() if "m4::" in e.key)
+
+
+def launches(fn, steps):
+    n = count_launches(fn)
+    return None if n is None else n * steps
+
+
 def time_region(fn, steps, warmup, world):
     import torch
 
@@ -428,7 +449,7 @@ def run_ours(args):
                    "tokens_per_step_per_gpu": tokens, "l2": "inputs larger than L2 (memory-read "
                    "operands 268 MB each, stored factors 9.7 GB)"},
         "roofline": roofline, "components": components, "e2e": e2e,
-        "gpu_launches": 13 * args.steps, "clocks": clocks.summary(),
+        "gpu_launches": launches(step, args.steps), "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, desc = cpu_baseline_sample(mem_cfg, SCAN_CFG, host_threads())
@@ -517,7 +538,7 @@ def run_lm(args):
                      "achieved": flops, "peak": pk["bf16_sust"], "unit": "TFLOP/s",
                      "frac": flops / pk["bf16_sust"], "traffic": None, "peak_source": pk["source"]},
         "e2e": e2e, "clocks": clocks.summary(),
-        "gpu_launches": None,
+        "gpu_launches": launches(step, args.steps),
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
