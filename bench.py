@@ -455,6 +455,13 @@ def run_ours(args):
         rate, desc = cpu_baseline_sample(mem_cfg, SCAN_CFG, host_threads())
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": host_threads(),
                                 "kind": "port", "sample": desc}
+    if not args.no_lm and args.workload == "hotpath":
+        # The second half of the metric: the data-parallel 60M LM training
+        # step on the same ranks (one NCCL gradient all-reduce per step).
+        del m, s
+        step = e2e_step = None
+        torch.cuda.empty_cache()
+        line["lm60m"] = measure_lm(args, "lm60m", world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -483,18 +490,18 @@ def lm_flops_per_token(cfg):
     return 6 * matmul + m_layers * mh * (MEM_FWD_FLOPS + MEM_BWD_FLOPS) + s_layers * SCAN_FLOPS * h / 16
 
 
-def run_lm(args):
+def measure_lm(args, workload, world, rank, local):
+    """One data-parallel LM training step per iteration on this rank's shard;
+    returns the JSON object (global tokens/s, max over ranks)."""
     import torch
 
     from mamba4_b200.model import CONFIGS, Mamba4LM
     from mamba4_b200.train import DataParallelTrainer, TrainSettings, synthetic_batch
 
-    world, rank, local = setup_dist(args.gpus)
     dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    name = args.workload[2:]
+    name = workload[2:]
     cfg = CONFIGS[name]
-    per_gpu = LM_PER_GPU[args.workload]
+    per_gpu = LM_PER_GPU[workload]
     torch.manual_seed(1234)
     model = Mamba4LM(cfg).to(dev)
     trainer = DataParallelTrainer(model, TrainSettings(), world=world, device_id=local)
@@ -540,6 +547,17 @@ def run_lm(args):
         "e2e": e2e, "clocks": clocks.summary(),
         "gpu_launches": launches(step, args.steps),
     }
+    del trainer, model
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_lm(args):
+    import torch
+
+    world, rank, local = setup_dist(args.gpus)
+    torch.cuda.set_device(local)
+    line = measure_lm(args, args.workload, world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -557,6 +575,8 @@ def main():
     p.add_argument("--workload", choices=["hotpath", "small", "lm60m", "lm125m"], default="hotpath")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-lm", action="store_true",
+                   help="hot-path workload: skip the nested data-parallel 60M LM step measurement")
     args = p.parse_args()
     if args.impl == "reference":
         run_reference(args)
