@@ -346,13 +346,16 @@ M4_DEV void store_column(float2* dst, const float2 (&A)[NPAIR]) {
   }
 }
 
-// One right-looking column step on unscaled columns U (L[:, j] = U[:, j]/sqrt(U_jj)).
-template <int J>
-M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
-  constexpr int JN = J >> 3, JB = J & 7, JH = (J >> 2) & 1, JA = J & 3;
+// One right-looking column step on unscaled columns U (L[:, j] = U[:, j]/sqrt(U_jj)),
+// column j = 8 JN + jb: the column block JN is a template parameter (register
+// indices), the column within it a runtime value, so the 64 steps compile to
+// 8 loop bodies (small enough for the instruction cache).
+template <int JN>
+M4_DEV void factor_step(int jb, float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
+  const int J = 8 * JN + jb, JH = (J >> 2) & 1, JA = J & 3;
   float2* cb = sm.u.f.col[J & 1];
   float* cw = sm.u.f.colw[J & 1];
-  if (b == JB) {
+  if (b == jb) {
     store_column<JN>(cb + a * PS, A);
     cw[a] = wr[JN];
   }
@@ -360,7 +363,7 @@ M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], Solv
   const float piv = reinterpret_cast<const float*>(cb)[(JA * PS + JN) * 2 + JH];
   const float r = rsqrtf(piv);
   const float r2 = r * r;
-  rc[JN] = (b == JB) ? r : rc[JN];
+  rc[JN] = (b == jb) ? r : rc[JN];
   float C[8];
   {
     const float2* cs = cb + (b & 3) * PS;
@@ -372,7 +375,7 @@ M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], Solv
       C[n + 1] = (b >= 4 ? v.w : v.z) * r2;
     }
   }
-  C[JN] = (b > JB) ? C[JN] : 0.f;
+  C[JN] = (b > jb) ? C[JN] : 0.f;
   const float rw = cw[a];
   dup_t Cd[8];
 #pragma unroll
@@ -381,8 +384,8 @@ M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], Solv
   for (int p = JN; p < 8; ++p) {
     float2 rv = cb[a * PS + p];
     if (p == JN) {
-      rv.x = (a > JB) ? rv.x : 0.f;
-      rv.y = (a + 4 > JB) ? rv.y : 0.f;
+      rv.x = (a > jb) ? rv.x : 0.f;
+      rv.y = (a + 4 > jb) ? rv.y : 0.f;
     }
 #pragma unroll
     for (int n = JN; n <= p; ++n) A[pair_of(p, n)] = fma2d(rv, Cd[n], A[pair_of(p, n)]);
@@ -391,10 +394,11 @@ M4_DEV void factor_step(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], Solv
   for (int n = JN; n < 8; ++n) wr[n] = fmaf(-rw, C[n], wr[n]);
 }
 
-template <int J>
+template <int JN>
 M4_DEV void factor_all(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
-  factor_step<J>(A, wr, rc, sm, a, b);
-  if constexpr (J + 1 < KD) factor_all<J + 1>(A, wr, rc, sm, a, b);
+#pragma unroll 1
+  for (int jb = 0; jb < 8; ++jb) factor_step<JN>(jb, A, wr, rc, sm, a, b);
+  if constexpr (JN + 1 < 8) factor_all<JN + 1>(A, wr, rc, sm, a, b);
 }
 
 // ---------------------------------------------------------------------------
