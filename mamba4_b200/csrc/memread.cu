@@ -71,6 +71,24 @@ inline Sizes sizes(const M4MemDims& d) {
 // ---------------------------------------------------------------------------
 // memread_states: sequential evidence/cross statistics per (batch, head).
 // ---------------------------------------------------------------------------
+// Asynchronous global -> shared copies (cp.async): 16 bytes (.cg) or 4 bytes
+// (.ca); an invalid source copies zeros (src-size 0; the address stays a
+// valid one). Groups are committed and awaited per pipeline stage.
+M4_DEV void cp16(float* dst, const float* src, bool valid) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+M4_DEV void cp4(float* dst, const float* src, bool valid) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+M4_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+M4_DEV void cp_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+// Wait for all of this thread's copies; a __syncthreads must follow before
+// other threads read them.
+M4_DEV void cp_wait() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 template <int P>
 __global__ void __launch_bounds__(256) states_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ values,
@@ -83,9 +101,34 @@ __global__ void __launch_bounds__(256) states_kernel(
   const int tid = threadIdx.x;
   const int Tp = (T + CH - 1) / CH * CH, nsub = Tp / SUB, nch = Tp / CH;
   const int i = tid >> 2, j0 = (tid & 3) * 16;
-  __shared__ __align__(16) float ks[SUB][KD];
-  __shared__ __align__(16) float vs[SUB][P];
-  __shared__ float bl[SUB], ll[SUB];
+  // Two sub-chunk buffers: the next sub-chunk's keys, values, beta and
+  // log_decay stream in (cp.async) while the current one is applied.
+  __shared__ __align__(16) float ks[2][SUB][KD];
+  __shared__ __align__(16) float vs[2][SUB][P];
+  __shared__ float bl[2][SUB], ll[2][SUB];
+  auto prefetch = [&](int buf, int sub) {
+    const int t0 = sub * SUB;
+#pragma unroll
+    for (int idx = tid; idx < SUB * KD / 4; idx += 256) {
+      const int tt = idx / (KD / 4), d4 = idx % (KD / 4), t = t0 + tt;
+      const bool live = t < T;
+      cp16(&ks[buf][tt][4 * d4], live ? keys + ((size_t(b) * T + t) * H + h) * KD + 4 * d4 : keys, live);
+    }
+#pragma unroll
+    for (int idx = tid; idx < SUB * P / 4; idx += 256) {
+      const int tt = idx / (P / 4), p4 = idx % (P / 4), t = t0 + tt;
+      const bool live = t < T;
+      cp16(&vs[buf][tt][4 * p4], live ? values + ((size_t(b) * T + t) * H + h) * P + 4 * p4 : values, live);
+    }
+    if (tid < SUB) {
+      const int t = t0 + tid;
+      const bool live = t < T;
+      const size_t o = (size_t(b) * T + t) * H + h;
+      cp4(&bl[buf][tid], live ? beta + o : beta, live);        // beta 0 past T
+      cp4(&ll[buf][tid], live ? log_decay + o : log_decay, live);  // lambda 1 past T
+    }
+    cp_commit();
+  };
   float s[16], c[CR][16];
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
@@ -94,7 +137,10 @@ __global__ void __launch_bounds__(256) states_kernel(
     for (int r = 0; r < CR; ++r)
       c[r][e] = init_c ? init_c[(size_t(bh) * P + i + 64 * r) * KD + j0 + e] : 0.f;
   }
+  prefetch(0, 0);
   for (int sub = 0; sub < nsub; ++sub) {
+    const int buf = sub & 1;
+    if (sub + 1 < nsub) prefetch(buf ^ 1, sub + 1);
     float* sd = s_start + ((size_t(bh) * nsub + sub) * KD + i) * KD + j0;
 #pragma unroll
     for (int e = 0; e < 16; e += 4) st4(sd + e, make_float4(s[e], s[e + 1], s[e + 2], s[e + 3]));
@@ -107,41 +153,28 @@ __global__ void __launch_bounds__(256) states_kernel(
           st4(cd + e, make_float4(c[r][e], c[r][e + 1], c[r][e + 2], c[r][e + 3]));
       }
     }
-    const int t0 = sub * SUB;
-    for (int idx = tid; idx < SUB * KD; idx += 256) {
-      const int tt = idx / KD, d = idx % KD, t = t0 + tt;
-      ks[tt][d] = t < T ? keys[((size_t(b) * T + t) * H + h) * KD + d] : 0.f;
-    }
-    for (int idx = tid; idx < SUB * P; idx += 256) {
-      const int tt = idx / P, p = idx % P, t = t0 + tt;
-      vs[tt][p] = t < T ? values[((size_t(b) * T + t) * H + h) * P + p] : 0.f;
-    }
-    if (tid < SUB) {
-      const int t = t0 + tid;
-      bl[tid] = t < T ? beta[(size_t(b) * T + t) * H + h] : 0.f;
-      ll[tid] = t < T ? expf(log_decay[(size_t(b) * T + t) * H + h]) : 1.f;
-    }
+    if (sub + 1 < nsub) cp_wait_group<1>(); else cp_wait_group<0>();
     __syncthreads();
 #pragma unroll 2
     for (int tt = 0; tt < SUB; ++tt) {
-      const float lam = ll[tt], bet = bl[tt];
+      const float lam = expf(ll[buf][tt]), bet = bl[buf][tt];
       float kj[16];
 #pragma unroll
       for (int e = 0; e < 16; e += 4) {
-        float4 v4 = ld4(&ks[tt][j0 + e]);
+        float4 v4 = ld4(&ks[buf][tt][j0 + e]);
         kj[e] = v4.x; kj[e + 1] = v4.y; kj[e + 2] = v4.z; kj[e + 3] = v4.w;
       }
-      const float bk = bet * ks[tt][i];
+      const float bk = bet * ks[buf][tt][i];
 #pragma unroll
       for (int e = 0; e < 16; ++e) s[e] = fmaf(bk, kj[e], lam * s[e]);
 #pragma unroll
       for (int r = 0; r < CR; ++r) {
-        const float bv = bet * vs[tt][i + 64 * r];
+        const float bv = bet * vs[buf][tt][i + 64 * r];
 #pragma unroll
         for (int e = 0; e < 16; ++e) c[r][e] = fmaf(bv, kj[e], lam * c[r][e]);
       }
     }
-    __syncthreads();
+    __syncthreads();  // this buffer is refilled two sub-chunks later
   }
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
@@ -626,16 +659,6 @@ M4_DEV void chunk_gates(int tid, int b, int T, int H, int h, int t0, const float
     }
   }
 }
-
-// 16-byte asynchronous global -> shared copy (cp.async, no registers); an
-// invalid source copies zeros (src-size 0; the address stays a valid one).
-M4_DEV void cp16(float* dst, const float* src, bool valid) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-// Wait for this thread's copies; a __syncthreads must follow before other
-// threads read them.
-M4_DEV void cp_wait() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 // Start copying a [64 tokens][W] chunk of a [B,T,H,W] tensor into a tile of
 // stride ld (tokens past T read as zero).
