@@ -35,7 +35,7 @@ constexpr int SUB = 16;        // tokens per solve warp (state stride)
 constexpr int LSTRIDE = 72 * 32;  // floats of one token's stored factor (36 float2 per lane)
 constexpr int WARPS = 4;       // solve warps per CTA
 #ifndef M4_SOLVE_MINB
-#define M4_SOLVE_MINB 3
+#define M4_SOLVE_MINB 4
 #endif
 
 
@@ -254,8 +254,8 @@ struct SolveSmem {
       float2 kP[4 * PS];         // (k[a + 8p], k[a + 4 + 8p]) at a*PS + p
       float kC[8 * KS];          // k[b + 8n] at b*KS + n
       float qC[8 * KS];          // q[b + 8n] at b*KS + n
-      float2 col[2][4 * PS];     // column broadcast, pairs at a*PS + p
-      float colw[2][4];          // bordered-row entry per a
+      float2 col[4][4 * PS];     // column broadcasts (two per step, two steps), pairs at a*PS + p
+      float colw[4][4];          // bordered-row entry per a
     } f;
     struct {
       float T[8 * 36];           // diagonal blocks, packed lower tri(r, c)
@@ -383,54 +383,75 @@ M4_DEV void store_column(float2* dst, const float2 (&A)[NPAIR]) {
 // column j = 8 JN + jb: the column block JN is a template parameter (register
 // indices), the column within it a runtime value, so the 64 steps compile to
 // 8 loop bodies (small enough for the instruction cache).
+// Two right-looking column steps at once on unscaled columns U
+// (L[:, j] = U[:, j]/sqrt(U_jj)): columns J = 8 JN + jb and J + 1 (jb even).
+// Both owners broadcast their columns; every lane forms the column J + 1
+// updated by column J from the two broadcasts (U'[:, J+1] = U[:, J+1] -
+// U[:, J] U[J+1, J] / U[J, J]) and applies the rank-2 update to its trailing
+// entries. Half the barrier / pivot chains of single-column steps.
 template <int JN>
-M4_DEV void factor_step(int jb, float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
-  const int J = 8 * JN + jb, JH = (J >> 2) & 1, JA = J & 3;
-  float2* cb = sm.u.f.col[J & 1];
-  float* cw = sm.u.f.colw[J & 1];
-  if (b == jb) {
-    store_column<JN>(cb + a * PS, A);
-    cw[a] = wr[JN];
+M4_DEV void factor_pair(int jb, float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
+  const int par = (jb >> 1) & 1;  // alternating buffer pair
+  float2* cA = sm.u.f.col[2 * par];
+  float2* cB = sm.u.f.col[2 * par + 1];
+  float* wA = sm.u.f.colw[2 * par];
+  float* wB = sm.u.f.colw[2 * par + 1];
+  if (b == jb || b == jb + 1) {
+    store_column<JN>((b == jb ? cA : cB) + a * PS, A);
+    (b == jb ? wA : wB)[a] = wr[JN];
   }
   __syncwarp();
-  const float piv = reinterpret_cast<const float*>(cb)[(JA * PS + JN) * 2 + JH];
-  const float r = rsqrtf(piv);
-  const float r2 = r * r;
-  rc[JN] = (b == jb) ? r : rc[JN];
-  float C[8];
+  const int A0 = jb & 3, H0 = (jb >> 2) & 1, A1 = (jb + 1) & 3, H1 = ((jb + 1) >> 2) & 1;
+  const float* fA = reinterpret_cast<const float*>(cA);
+  const float* fB = reinterpret_cast<const float*>(cB);
+  const float pJ = fA[(A0 * PS + JN) * 2 + H0];   // U[J][J]
+  const float u10 = fA[(A1 * PS + JN) * 2 + H1];  // U[J+1][J]
+  const float pJ1 = fB[(A1 * PS + JN) * 2 + H1];  // U[J+1][J+1]
+  const float r = rsqrtf(pJ), r2 = r * r;
+  const float sf = u10 * r2;
+  const float r1 = rsqrtf(fmaf(-u10, sf, pJ1)), r12 = r1 * r1;
+  rc[JN] = (b == jb) ? r : (b == jb + 1 ? r1 : rc[JN]);
+  dup_t DA[8], DB[8];
   {
-    const float2* cs = cb + (b & 3) * PS;
-    if constexpr (JN & 1) C[JN] = (b >= 4 ? cs[JN].y : cs[JN].x) * r2;
+    const float2* sa = cA + (b & 3) * PS;
+    const float2* sb = cB + (b & 3) * PS;
+    const float rwA = wA[a];
+    const float rwB = fmaf(-rwA, sf, wB[a]);
 #pragma unroll
-    for (int n = (JN + 1) & ~1; n < 8; n += 2) {
-      const float4 v = *reinterpret_cast<const float4*>(cs + n);
-      C[n] = (b >= 4 ? v.y : v.x) * r2;
-      C[n + 1] = (b >= 4 ? v.w : v.z) * r2;
+    for (int n = JN; n < 8; ++n) {
+      const float2 va = sa[n], vb = sb[n];
+      const float ca = b >= 4 ? va.y : va.x;
+      const float cb = b >= 4 ? vb.y : vb.x;
+      float CA = ca * r2, CB = fmaf(-ca, sf, cb) * r12;
+      if (n == JN) {
+        CA = (b > jb) ? CA : 0.f;
+        CB = (b > jb + 1) ? CB : 0.f;
+      }
+      wr[n] = fmaf(-rwB, CB, fmaf(-rwA, CA, wr[n]));
+      DA[n] = dup2(-CA);
+      DB[n] = dup2(-CB);
     }
   }
-  C[JN] = (b > jb) ? C[JN] : 0.f;
-  const float rw = cw[a];
-  dup_t Cd[8];
-#pragma unroll
-  for (int n = JN; n < 8; ++n) Cd[n] = dup2(-C[n]);
 #pragma unroll
   for (int p = JN; p < 8; ++p) {
-    float2 rv = cb[a * PS + p];
+    float2 ra = cA[a * PS + p];
+    const float2 rb0 = cB[a * PS + p];
+    float2 rb = make_float2(fmaf(-ra.x, sf, rb0.x), fmaf(-ra.y, sf, rb0.y));
     if (p == JN) {
-      rv.x = (a > jb) ? rv.x : 0.f;
-      rv.y = (a + 4 > jb) ? rv.y : 0.f;
+      ra.x = (a > jb) ? ra.x : 0.f;
+      ra.y = (a + 4 > jb) ? ra.y : 0.f;
+      rb.x = (a > jb + 1) ? rb.x : 0.f;
+      rb.y = (a + 4 > jb + 1) ? rb.y : 0.f;
     }
 #pragma unroll
-    for (int n = JN; n <= p; ++n) A[pair_of(p, n)] = fma2d(rv, Cd[n], A[pair_of(p, n)]);
+    for (int n = JN; n <= p; ++n) A[pair_of(p, n)] = fma2d(rb, DB[n], fma2d(ra, DA[n], A[pair_of(p, n)]));
   }
-#pragma unroll
-  for (int n = JN; n < 8; ++n) wr[n] = fmaf(-rw, C[n], wr[n]);
 }
 
 template <int JN>
 M4_DEV void factor_all(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
 #pragma unroll 1
-  for (int jb = 0; jb < 8; ++jb) factor_step<JN>(jb, A, wr, rc, sm, a, b);
+  for (int jb = 0; jb < 8; jb += 2) factor_pair<JN>(jb, A, wr, rc, sm, a, b);
   if constexpr (JN + 1 < 8) factor_all<JN + 1>(A, wr, rc, sm, a, b);
 }
 
