@@ -883,7 +883,7 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
   dstart_kernel<<<chunks, CTH, sizeof(DsSmem), st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
   carry_kernel<<<bh * SPARTS, 256, 0, st>>>(d, carries, deltas, d_final);
   allow_smem(grads_kernel, sizeof(GradSmem));
-  grads_kernel<<<chunks, CTH, sizeof(GradSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
+  grads_kernel<<<chunks, GW * 32, sizeof(GradSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
                                                       starts, carries, g, static_cast<bf16*>(dx), o);
   later_kernel<<<bh, 32, 0, st>>>(d, o.dth);
   const size_t tokens = size_t(d.B) * d.T;

@@ -27,8 +27,9 @@ constexpr int N = 64;        // state dim
 constexpr int P = 64;        // head dim
 constexpr int TS = 72;       // bf16 tile stride (144 B rows: ldmatrix conflict-free)
 constexpr int FS = 68;       // fp32 tile stride
-constexpr int CTH = 128;     // threads per chunk CTA (4 warps x 16 rows)
-static_assert(CTH == 128 && C == 64, "chunk_theta and the grads epilogue map 4 warps onto 4 x 16 tokens");
+constexpr int CTH = 128;     // threads per forward / dstart chunk CTA (4 warps x 16 rows)
+constexpr int GW = 8;        // warps per grads CTA (4 row blocks x 2 column halves)
+static_assert(C == 64 && (C % (4 * GW)) == 0, "warp/token maps assume 64-token chunks");
 
 M4_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -129,7 +130,7 @@ struct Dims {
 // Per-token scalars of one chunk of (b, h) (threads 0..63 + warp 0 prefix).
 struct Rows {
   float p[C], gam[C], scl[C], tail[C], dt[C], ept[C];
-  float seg[4 * 32];  // per-segment totals of the 16-token scans
+  float seg[8 * 32];  // per-segment totals of the in-chunk scans (one segment per warp)
 };
 
 M4_DEV void chunk_rows(const Dims& d, int b, int h, int t0, const float* adt, const float* dt,
@@ -172,25 +173,28 @@ M4_DEV float rate_at(const Dims& d, const float* angles, int b, int h, int t, in
 }
 
 // theta[t][i] = phase0[i] + sum_{s<=t} rate_s[i] dt_s within the chunk,
-// returned as cos (in `cosv`) and sin. Warp w scans tokens 16w..16w+15
-// (independent loads, then a 16-step sum), the segment totals are combined
-// through `r.seg`, and the same thread takes sincos of its 16 elements in one
-// compact loop. Pairs i >= A get cos 1, sin 0. All CTH threads must call.
+// returned as cos (in `cosv`) and sin. Warp w of NW scans tokens
+// SEG w .. SEG w + SEG - 1 (independent loads, then a SEG-step sum), the
+// segment totals are combined through `r.seg`, and the same thread takes
+// sincos of its SEG elements in one compact loop. Pairs i >= A get cos 1,
+// sin 0. All 32 NW threads must call.
+template <int NW = 4>
 M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles, Rows& r,
                         const float* phase0, float* cosv, float* sinv) {
+  constexpr int SEG = C / NW;
   const int i = threadIdx.x & 31, w = threadIdx.x >> 5;
   float acc = 0.f;
   if (i < d.A) {
-    float inc[16];
+    float inc[SEG];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int tt = 16 * w + j, t = t0 + tt;
+    for (int j = 0; j < SEG; ++j) {
+      const int tt = SEG * w + j, t = t0 + tt;
       inc[j] = t < d.T ? rate_at(d, angles, b, h, t, i) * r.dt[tt] : 0.f;
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < SEG; ++j) {
       acc += inc[j];
-      cosv[(16 * w + j) * 33 + i] = acc;
+      cosv[(SEG * w + j) * 33 + i] = acc;
     }
   }
   r.seg[w * 32 + i] = acc;
@@ -201,8 +205,8 @@ M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles
     for (int v = 0; v < w; ++v) off += r.seg[v * 32 + i];
   }
 #pragma unroll 1
-  for (int j = 0; j < 16; ++j) {
-    const int e = (16 * w + j) * 33 + i;
+  for (int j = 0; j < SEG; ++j) {
+    const int e = (SEG * w + j) * 33 + i;
     float cs = 1.f, sn = 0.f;
     if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
     cosv[e] = cs;
@@ -215,24 +219,26 @@ M4_DEV float lo_f(uint32_t v) { return __uint_as_float(v << 16); }
 M4_DEV float hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 
 // Rotated, rounded queries/keys of a chunk as bf16 tiles (either may be null).
-// Lane = angle pair i, warp w = tokens w, w+4, ..., w+60; all global loads are
-// issued before the rotation.
+// Lane = angle pair i, warp w of NW = tokens w, w + NW, ...; all global loads
+// are issued before the rotation.
+template <int NW = 4>
 M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const bf16* bk, const float* qb,
                      const float* kb, const float* cosv, const float* sinv, bf16* Qs, bf16* Ks) {
+  constexpr int PER = C / NW;
   const int i = threadIdx.x & 31, w = threadIdx.x >> 5, n0 = 2 * i;
   const float qb0 = qb ? qb[h * N + n0] : 0.f, qb1 = qb ? qb[h * N + n0 + 1] : 0.f;
   const float kb0 = kb ? kb[h * N + n0] : 0.f, kb1 = kb ? kb[h * N + n0 + 1] : 0.f;
-  uint32_t cr[16], br[16];
+  uint32_t cr[PER], br[PER];
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int t = t0 + w + 4 * k;
+  for (int k = 0; k < PER; ++k) {
+    const int t = t0 + w + NW * k;
     const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
     cr[k] = (Qs && t < d.T) ? ld_u32(cq + base + n0) : 0u;
     br[k] = (Ks && t < d.T) ? ld_u32(bk + base + n0) : 0u;
   }
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int tt = w + 4 * k;
+  for (int k = 0; k < PER; ++k) {
+    const int tt = w + NW * k;
     const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
     if (Qs) {
       const float q0 = round_to<bf16>(lo_f(cr[k]) + qb0), q1 = round_to<bf16>(hi_f(cr[k]) + qb1);
@@ -246,20 +252,22 @@ M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const 
 }
 
 // Copy a [64 tokens][64] slice of a [B,T,H*64] bf16 tensor into a tile, each
-// row scaled by rowscale[t] (and rounded) when given. Four 16-byte loads per
-// thread, all in flight before the stores.
+// row scaled by rowscale[t] (and rounded) when given. 16 / NW 16-byte loads
+// per thread, all in flight before the stores.
+template <int NW = 4>
 M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16* T,
                       const float* rowscale = nullptr) {
-  uint4 v[4];
+  constexpr int PER = 16 / NW, TH = 32 * NW;
+  uint4 v[PER];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int idx = threadIdx.x + k * CTH, tt = idx >> 3, c8 = idx & 7, t = t0 + tt;
+  for (int k = 0; k < PER; ++k) {
+    const int idx = threadIdx.x + k * TH, tt = idx >> 3, c8 = idx & 7, t = t0 + tt;
     v[k] = t < d.T ? *reinterpret_cast<const uint4*>(src + (size_t(b) * d.T + t) * d.H * P + h * P + 8 * c8)
                    : make_uint4(0u, 0u, 0u, 0u);
   }
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int idx = threadIdx.x + k * CTH, tt = idx >> 3, c8 = idx & 7;
+  for (int k = 0; k < PER; ++k) {
+    const int idx = threadIdx.x + k * TH, tt = idx >> 3, c8 = idx & 7;
     uint4 o = v[k];
     if (rowscale) {
       const float f = rowscale[tt];
@@ -276,14 +284,16 @@ M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16
 }
 
 // Load a [64][64] fp32 block (row-major) into a bf16 tile with RN rounding;
-// eight 16-byte loads per thread in flight.
+// 32 / NW 16-byte loads per thread in flight.
+template <int NW = 4>
 M4_DEV void load_state_bf16(const float* src, bf16* T) {
-  float4 v[8];
+  constexpr int PER = 32 / NW, TH = 32 * NW;
+  float4 v[PER];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) v[k] = ld4(src + 4 * (threadIdx.x + k * CTH));
+  for (int k = 0; k < PER; ++k) v[k] = ld4(src + 4 * (threadIdx.x + k * TH));
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int idx = threadIdx.x + k * CTH, r = idx / (P / 4), c4 = idx % (P / 4);
+  for (int k = 0; k < PER; ++k) {
+    const int idx = threadIdx.x + k * TH, r = idx / (P / 4), c4 = idx % (P / 4);
     *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4) = __floats2bfloat162_rn(v[k].x, v[k].y);
     *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(v[k].z, v[k].w);
   }
@@ -541,48 +551,59 @@ struct GradSmem {
   bf16 Mt[C * TS];   // rd(d_mixed o W)
   bf16 Es[N * TS];   // rd(E_n)
   bf16 Ss[N * TS];   // rd(S_n)
-  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  float theta[C * 33];  // cos of the pair phase, then the pair phase gradient
   float sinv[C * 33];
-  float vec[8 * C];
-  float col[2][4 * C];  // per-warp column sums of d_weights o W and d_weights o decay
-  float bq[4 * N];      // per-warp bias partials
+  // Per-token rows: 0 sum K.(V rd(E)^T), 1 e^p dY.(Q rd(S)), 2 log-decay
+  // increment, 3 d gamma, 4 d scale, 5 flow, 6 d log-decay, 7 unused;
+  // 8-9 / 10-11 / 12-13: the two column halves' partials of the row sums
+  // of d_weights o W, of row 0 and of row 1.
+  float vec[14 * C];
+  float col[2][4 * C];  // per row block: column sums of d_weights o W and of d_weights o decay
+  float bq[4 * N];      // per row block bias partials
   float bk[4 * N];
   float scratch[C];
   Rows r;
 };
 
-__global__ void __launch_bounds__(CTH) grads_kernel(
+// Every gradient of one chunk given S_n and E_n. Eight warps: warp w owns
+// rows 16 (w % 4) .. +15 and column half w / 4 (32 columns) of every chunk
+// product, so each product tile is 16 x 32 per warp; row sums over the two
+// halves and column sums over the four row blocks meet in shared memory.
+__global__ void __launch_bounds__(GW * 32) grads_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ bk, const bf16* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
     const float* __restrict__ phases, const float* __restrict__ starts, const float* __restrict__ carries,
     const bf16* __restrict__ dy, bf16* __restrict__ dx, GradOut o) {
+  constexpr int TH = GW * 32;
   extern __shared__ __align__(16) unsigned char raw[];
   GradSmem& s = *reinterpret_cast<GradSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, row0 = warp * 16;
+  const int t0 = n * C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rb = warp & 3, half = warp >> 2, row0 = 16 * rb, col0 = 32 * half;
   const int g = lane >> 2, cc = lane & 3;
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
+  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
-  load_tile(d, b, h, t0, x, s.Vs);
-  load_tile(d, b, h, t0, dy, s.Dy);
+  build_qk<GW>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+  load_tile<GW>(d, b, h, t0, x, s.Vs);
+  load_tile<GW>(d, b, h, t0, dy, s.Dy);
   // rd(S_n), rd(E_n) as tiles and <E_n, S_n> (fp32 values) for the chunk-end decay.
   {
+    constexpr int PER = 32 / GW;
     const float* Sg = starts + (size_t(bh) * d.nch + n) * N * P;
     const float* Eg = carries + (size_t(bh) * d.nch + n) * N * P;
     float part = 0.f;
-    float4 sv[8], ev[8];
+    float4 sv[PER], ev[PER];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      sv[k] = ld4(Sg + 4 * (tid + k * CTH));
-      ev[k] = ld4(Eg + 4 * (tid + k * CTH));
+    for (int k = 0; k < PER; ++k) {
+      sv[k] = ld4(Sg + 4 * (tid + k * TH));
+      ev[k] = ld4(Eg + 4 * (tid + k * TH));
     }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int idx = tid + k * CTH;
+    for (int k = 0; k < PER; ++k) {
+      const int idx = tid + k * TH;
       const float4 a4 = sv[k], e4 = ev[k];
       const int r = idx / (P / 4), c4 = idx % (P / 4);
       *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4) = __floats2bfloat162_rn(a4.x, a4.y);
@@ -595,28 +616,28 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
     if (lane == 0) s.scratch[warp] = part;
   }
   __syncthreads();
-  // Scores Q K^T and d_mixed dY V^T (rows t, cols s) stay in registers. Each
-  // element gives the two masked tiles rd(scores o W) and rd(d_mixed o W) and
-  // the per-token sums of d_weights = d_mixed o scores:
+  // Scores Q K^T and d_mixed dY V^T (rows t, this warp's 32 columns s) in
+  // registers. Each element gives the two masked tiles rd(scores o W) and
+  // rd(d_mixed o W) and the per-token sums of d_weights = d_mixed o scores:
   //   row t:    sum_{s<t} dw W,  column s: sum_{u>s} dw W and sum_{u>s} dw decay,
   // with W = decay(t, s) scale_s below the diagonal and gamma_t on it.
   {
-    float sc[8][4], dm[8][4];
+    float sc[4][4], dm[4][4];
     zero(sc);
     zero(dm);
-    mma_tile<N, 8, false, false>(sc, s.Qs, row0, s.Ks, 0);
-    mma_tile<P, 8, false, false>(dm, s.Dy, row0, s.Vs, 0);
-    float rsum[2] = {0.f, 0.f}, c1[8][2], c2[8][2];
+    mma_tile<N, 4, false, false>(sc, s.Qs, row0, s.Ks, col0);
+    mma_tile<P, 4, false, false>(dm, s.Dy, row0, s.Vs, col0);
+    float rsum[2] = {0.f, 0.f}, c1[4][2], c2[4][2];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int t = row0 + g + 8 * hf;
       const float pt = s.r.p[t];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < 4; ++nt) {
         float ms[2], mt[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int sidx = nt * 8 + 2 * cc + e;
+          const int sidx = col0 + nt * 8 + 2 * cc + e;
           const float vs = sc[nt][2 * hf + e], vd = dm[nt][2 * hf + e], dw = vd * vs;
           float w = 0.f, dec = 0.f;
           if (sidx < t) {
@@ -638,8 +659,8 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
             c2[nt][e] = fmaf(dw, dec, c2[nt][e]);
           }
         }
-        *reinterpret_cast<__nv_bfloat162*>(s.Ms + t * TS + nt * 8 + 2 * cc) = __floats2bfloat162_rn(ms[0], ms[1]);
-        *reinterpret_cast<__nv_bfloat162*>(s.Mt + t * TS + nt * 8 + 2 * cc) = __floats2bfloat162_rn(mt[0], mt[1]);
+        *reinterpret_cast<__nv_bfloat162*>(s.Ms + t * TS + col0 + nt * 8 + 2 * cc) = __floats2bfloat162_rn(ms[0], ms[1]);
+        *reinterpret_cast<__nv_bfloat162*>(s.Mt + t * TS + col0 + nt * 8 + 2 * cc) = __floats2bfloat162_rn(mt[0], mt[1]);
       }
     }
 #pragma unroll
@@ -647,10 +668,10 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
       float v = rsum[hf];
       v += __shfl_xor_sync(0xffffffffu, v, 1);
       v += __shfl_xor_sync(0xffffffffu, v, 2);
-      if (cc == 0) s.vec[7 * C + row0 + g + 8 * hf] = v;
+      if (cc == 0) s.vec[(8 + half) * C + row0 + g + 8 * hf] = v;
     }
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float a = c1[nt][e], v = c2[nt][e];
@@ -660,19 +681,19 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
           v += __shfl_xor_sync(0xffffffffu, v, off);
         }
         if (g == 0) {
-          s.col[0][warp * C + nt * 8 + 2 * cc + e] = a;
-          s.col[1][warp * C + nt * 8 + 2 * cc + e] = v;
+          s.col[0][rb * C + col0 + nt * 8 + 2 * cc + e] = a;
+          s.col[1][rb * C + col0 + nt * 8 + 2 * cc + e] = v;
         }
       }
   }
   __syncthreads();
-  // dV = rd(Sc o W)^T dY + src o (K rd(E)) -> dx.
+  // dV = rd(Sc o W)^T dY + src o (K rd(E)) -> dx (rows s, this warp's 32 columns p).
   {
-    float acc[8][4], ve[8][4];
+    float acc[4][4], ve[4][4];
     zero(acc);
     zero(ve);
-    mma_tile<C, 8, true, true>(acc, s.Ms, row0, s.Dy, 0);
-    mma_tile<N, 8, false, true>(ve, s.Ks, row0, s.Es, 0);
+    mma_tile<C, 4, true, true>(acc, s.Ms, row0, s.Dy, col0);
+    mma_tile<N, 4, false, true>(ve, s.Ks, row0, s.Es, col0);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int sr = row0 + g + 8 * hf, t = t0 + sr;
@@ -680,69 +701,70 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
       const float src = s.r.scl[sr] * s.r.tail[sr];
       bf16* row = dx + (size_t(b) * d.T + t) * d.H * P + h * P;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int col = nt * 8 + 2 * cc;
+      for (int nt = 0; nt < 4; ++nt) {
+        const int col = col0 + nt * 8 + 2 * cc;
         *reinterpret_cast<__nv_bfloat162*>(row + col) = __floats2bfloat162_rn(
             fmaf(src, ve[nt][2 * hf], acc[nt][2 * hf]), fmaf(src, ve[nt][2 * hf + 1], acc[nt][2 * hf + 1]));
       }
     }
   }
-  // dQ, dK (rows t / s, cols n) in registers.
-  float gq[8][4], gk[8][4];
+  // dQ, dK (rows t / s, this warp's 32 columns n) in registers.
+  float gq[4][4], gk[4][4];
   zero(gq);
   zero(gk);
-  mma_tile<C, 8, false, true>(gq, s.Mt, row0, s.Ks, 0);   // rd(Dm o W) K
-  mma_tile<C, 8, true, true>(gk, s.Mt, row0, s.Qs, 0);    // rd(Dm o W)^T Q
+  mma_tile<C, 4, false, true>(gq, s.Mt, row0, s.Ks, col0);   // rd(Dm o W) K
+  mma_tile<C, 4, true, true>(gk, s.Mt, row0, s.Qs, col0);    // rd(Dm o W)^T Q
   __syncthreads();  // Ms is rewritten below
-  for (int idx = tid; idx < C * P / 2; idx += CTH) {
+  for (int idx = tid; idx < C * P / 2; idx += TH) {
     const int tt = idx / (P / 2), c2 = idx % (P / 2);
     const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(s.Dy + tt * TS + 2 * c2);
     *reinterpret_cast<__nv_bfloat162*>(s.Ms + tt * TS + 2 * c2) =
         __floats2bfloat162_rn(__low2float(v) * s.r.ept[tt], __high2float(v) * s.r.ept[tt]);
   }
   __syncthreads();
-  mma_tile<P, 8, false, false>(gq, s.Ms, row0, s.Ss, 0);  // rd(dY e^p) rd(S)^T
-  float dsrc[2] = {0.f, 0.f}, inh_dot[2] = {0.f, 0.f};
+  mma_tile<P, 4, false, false>(gq, s.Ms, row0, s.Ss, col0);  // rd(dY e^p) rd(S)^T
   {
-    float ve[8][4];
+    float dsrc[2] = {0.f, 0.f}, inh_dot[2] = {0.f, 0.f};
+    float ve[4][4];
     zero(ve);
-    mma_tile<P, 8, false, false>(ve, s.Vs, row0, s.Es, 0);  // V rd(E)^T (rows s, cols n)
+    mma_tile<P, 4, false, false>(ve, s.Vs, row0, s.Es, col0);  // V rd(E)^T (rows s, cols n)
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int sr = row0 + g + 8 * hf;
       const float src = s.r.scl[sr] * s.r.tail[sr];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float kv = __bfloat162float(s.Ks[sr * TS + nt * 8 + 2 * cc + e]);
+          const float kv = __bfloat162float(s.Ks[sr * TS + col0 + nt * 8 + 2 * cc + e]);
           dsrc[hf] = fmaf(kv, ve[nt][2 * hf + e], dsrc[hf]);
           gk[nt][2 * hf + e] = fmaf(src, ve[nt][2 * hf + e], gk[nt][2 * hf + e]);
         }
     }
     zero(ve);
-    mma_tile<N, 8, false, true>(ve, s.Qs, row0, s.Ss, 0);  // Q rd(S) (rows t, cols p)
+    mma_tile<N, 4, false, true>(ve, s.Qs, row0, s.Ss, col0);  // Q rd(S) (rows t, cols p)
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int t = row0 + g + 8 * hf;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e)
-          inh_dot[hf] = fmaf(__bfloat162float(s.Dy[t * TS + nt * 8 + 2 * cc + e]), ve[nt][2 * hf + e], inh_dot[hf]);
+          inh_dot[hf] = fmaf(__bfloat162float(s.Dy[t * TS + col0 + nt * 8 + 2 * cc + e]), ve[nt][2 * hf + e],
+                             inh_dot[hf]);
     }
-  }
 #pragma unroll
-  for (int hf = 0; hf < 2; ++hf) {
-    float a = dsrc[hf], v = inh_dot[hf];
-    a += __shfl_xor_sync(0xffffffffu, a, 1);
-    a += __shfl_xor_sync(0xffffffffu, a, 2);
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    if (cc == 0) {
-      const int r = row0 + g + 8 * hf;
-      s.vec[0 * C + r] = a;
-      s.vec[1 * C + r] = v * s.r.ept[r];
+    for (int hf = 0; hf < 2; ++hf) {
+      float a = dsrc[hf], v = inh_dot[hf];
+      a += __shfl_xor_sync(0xffffffffu, a, 1);
+      a += __shfl_xor_sync(0xffffffffu, a, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (cc == 0) {
+        const int r = row0 + g + 8 * hf;
+        s.vec[(10 + half) * C + r] = a;
+        s.vec[(12 + half) * C + r] = v;
+      }
     }
   }
   // Rotation backward in registers: the accumulators hold each pair (2i, 2i+1)
@@ -750,28 +772,28 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
   // gradient into theta (same element, read then written by this thread),
   // bias partials per column.
   {
-    float sq[8][2], sk[8][2];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) sq[nt][0] = sq[nt][1] = sk[nt][0] = sk[nt][1] = 0.f;
-    uint32_t craw[2][8], braw[2][8];
+    uint32_t craw[2][4], braw[2][4];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int t = t0 + row0 + g + 8 * hf;
       const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        craw[hf][nt] = t < d.T ? ld_u32(cq + base + 8 * nt + 2 * cc) : 0u;
-        braw[hf][nt] = t < d.T ? ld_u32(bk + base + 8 * nt + 2 * cc) : 0u;
+      for (int nt = 0; nt < 4; ++nt) {
+        craw[hf][nt] = t < d.T ? ld_u32(cq + base + col0 + 8 * nt + 2 * cc) : 0u;
+        braw[hf][nt] = t < d.T ? ld_u32(bk + base + col0 + 8 * nt + 2 * cc) : 0u;
       }
     }
+    float sq[4][2], sk[4][2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) sq[nt][0] = sq[nt][1] = sk[nt][0] = sk[nt][1] = 0.f;
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int tt = row0 + g + 8 * hf, t = t0 + tt;
       const bool live = t < d.T;
       const size_t ob = ((size_t(b) * d.T + t) * d.H + h) * N;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int i = 4 * nt + cc, n0 = 2 * i;
+      for (int nt = 0; nt < 4; ++nt) {
+        const int i = (col0 >> 1) + 4 * nt + cc, n0 = 2 * i;
         const float cs = s.theta[tt * 33 + i], sn = s.sinv[tt * 33 + i];
         const float gq0 = gq[nt][2 * hf], gq1 = gq[nt][2 * hf + 1];
         const float gk0 = gk[nt][2 * hf], gk1 = gk[nt][2 * hf + 1];
@@ -792,11 +814,11 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
         const float qr0 = q0 * cs - q1 * sn, qr1 = q1 * cs + q0 * sn;
         const float kr0 = k0 * cs - k1 * sn, kr1 = k1 * cs + k0 * sn;
         const float dth = gq0 * (-qr1) + gq1 * qr0 + gk0 * (-kr1) + gk1 * kr0;
-        if (i < 32) s.theta[tt * 33 + i] = (i < d.A && live) ? dth : 0.f;
+        s.theta[tt * 33 + i] = (i < d.A && live) ? dth : 0.f;
       }
     }
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float q = sq[nt][e], kk = sk[nt][e];
@@ -806,8 +828,8 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
           kk += __shfl_xor_sync(0xffffffffu, kk, off);
         }
         if (g == 0) {
-          s.bq[warp * N + nt * 8 + 2 * cc + e] = q;
-          s.bk[warp * N + nt * 8 + 2 * cc + e] = kk;
+          s.bq[rb * N + col0 + nt * 8 + 2 * cc + e] = q;
+          s.bk[rb * N + col0 + nt * 8 + 2 * cc + e] = kk;
         }
       }
   }
@@ -815,11 +837,15 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
   // Per-token scalar gradients.
   if (tid < C) {
     const int t = tid;
+    const float dsrc = s.vec[10 * C + t] + s.vec[11 * C + t];
+    s.vec[0 * C + t] = dsrc;
+    s.vec[1 * C + t] = (s.vec[12 * C + t] + s.vec[13 * C + t]) * s.r.ept[t];
+    const float rowoff = s.vec[8 * C + t] + s.vec[9 * C + t];
     const float coloff = s.col[0][t] + s.col[0][C + t] + s.col[0][2 * C + t] + s.col[0][3 * C + t];
     const float cdec = s.col[1][t] + s.col[1][C + t] + s.col[1][2 * C + t] + s.col[1][3 * C + t];
-    const float flow = s.vec[0 * C + t] * s.r.scl[t] * s.r.tail[t];
-    s.vec[2 * C + t] = s.vec[7 * C + t] - coloff - flow + s.vec[1 * C + t];
-    s.vec[4 * C + t] = s.vec[0 * C + t] * s.r.tail[t] + cdec;
+    const float flow = dsrc * s.r.scl[t] * s.r.tail[t];
+    s.vec[2 * C + t] = rowoff - coloff - flow + s.vec[1 * C + t];
+    s.vec[4 * C + t] = dsrc * s.r.tail[t] + cdec;
     s.vec[5 * C + t] = flow;
   } else if (tid < C + N) {
     const int nn = tid - C;
@@ -827,23 +853,27 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
     o.dkb[(size_t(bh) * d.nch + n) * N + nn] = s.bk[nn] + s.bk[N + nn] + s.bk[2 * N + nn] + s.bk[3 * N + nn];
   }
   __syncthreads();
-  // Suffix sums of the pair phase gradient: warp w over tokens 16w..16w+15,
-  // then the totals of later segments (the carry from later chunks is added
-  // by finish_kernel). Warp 0 also runs the log-decay suffix scan.
+  // Suffix sums of the pair phase gradient: warp w over tokens SG w .. SG w +
+  // SG - 1, then the totals of later segments (the carry from later chunks is
+  // added by finish_kernel). Warp 0 also runs the log-decay suffix scan.
+  constexpr int SG = C / GW;
   {
     const int i = lane;
     float acc = 0.f;
 #pragma unroll
-    for (int j = 15; j >= 0; --j) {
-      acc += s.theta[(16 * warp + j) * 33 + i];
-      s.theta[(16 * warp + j) * 33 + i] = acc;
+    for (int j = SG - 1; j >= 0; --j) {
+      acc += s.theta[(SG * warp + j) * 33 + i];
+      s.theta[(SG * warp + j) * 33 + i] = acc;
     }
     s.r.seg[warp * 32 + i] = acc;
     if (warp == 0) {
       float fl = s.vec[5 * C + lane] + s.vec[5 * C + 32 + lane];
       fl = warp_sum(fl);
       const float end = expf(s.r.p[C - 1]);
-      const float extra = fl + end * (s.scratch[0] + s.scratch[1] + s.scratch[2] + s.scratch[3]);
+      float es = 0.f;
+#pragma unroll
+      for (int w = 0; w < GW; ++w) es += s.scratch[w];
+      const float extra = fl + end * es;
       const float hi = s.vec[2 * C + 63 - lane] + (lane == 0 ? extra : 0.f);
       const float shi = warp_inclusive_scan(hi, lane);
       const float tot = __shfl_sync(0xffffffffu, shi, 31);
@@ -856,15 +886,15 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
   {
     const int i = lane;
     float off = 0.f;
-    for (int v = warp + 1; v < 4; ++v) off += s.r.seg[v * 32 + i];
+    for (int v = warp + 1; v < GW; ++v) off += s.r.seg[v * 32 + i];
     if (warp == 0 && i < d.A)
       o.dth[(size_t(bh) * d.nch + n) * 32 + i] = off + s.r.seg[i];
-    // Angle-rate and dt-through-phase gradients of this warp's 16 tokens:
+    // Angle-rate and dt-through-phase gradients of this warp's SG tokens:
     // lanes over angle pairs (coalesced rows), dt term by a warp reduction.
     float mine = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < 16; ++j) {
-      const int tt = 16 * warp + j, t = t0 + tt;
+#pragma unroll
+    for (int j = 0; j < SG; ++j) {
+      const int tt = SG * warp + j, t = t0 + tt;
       if (t >= d.T) break;
       const float inc = i < d.A ? s.theta[tt * 33 + i] + off : 0.f;
       const float rate = i < d.A ? rate_at(d, angles, b, h, t, i) : 0.f;
@@ -873,8 +903,8 @@ __global__ void __launch_bounds__(CTH) grads_kernel(
       const float ddt = warp_sum(inc * rate);
       if (lane == j) mine = ddt;
     }
-    if (lane < 16) {
-      const int tt = 16 * warp + lane, t = t0 + tt;
+    if (lane < SG) {
+      const int tt = SG * warp + lane, t = t0 + tt;
       if (t < d.T) {
         const size_t si = (size_t(b) * d.T + t) * d.H + h;
         o.ddtp[si] = mine;
