@@ -842,11 +842,11 @@ inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const
   allow_smem(phase_kernel, psm);
   phase_kernel<<<bh, 256, psm, st>>>(d, dt, angles, phases);
   allow_smem(update_kernel, sizeof(UpdSmem));
-  update_kernel<<<chunks, CTH, sizeof(UpdSmem), st>>>(d, bk, xx, adt, dt, trap, angles, kb, phases, starts,
+  update_kernel<<<chunks, GW * 32, sizeof(UpdSmem), st>>>(d, bk, xx, adt, dt, trap, angles, kb, phases, starts,
                                                       deltas);
   state_kernel<<<bh * SPARTS, 256, 0, st>>>(d, starts, deltas, fin);
   allow_smem(output_kernel, sizeof(OutSmem));
-  output_kernel<<<chunks, CTH, sizeof(OutSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
+  output_kernel<<<chunks, GW * 32, sizeof(OutSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
                                                       starts, static_cast<bf16*>(y));
   return launch_status();
 }
@@ -880,7 +880,7 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
   const bf16* g = static_cast<const bf16*>(dy);
   const int bh = d.B * d.H, chunks = bh * d.nch;
   allow_smem(dstart_kernel, sizeof(DsSmem));
-  dstart_kernel<<<chunks, CTH, sizeof(DsSmem), st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
+  dstart_kernel<<<chunks, GW * 32, sizeof(DsSmem), st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
   carry_kernel<<<bh * SPARTS, 256, 0, st>>>(d, carries, deltas, d_final);
   allow_smem(grads_kernel, sizeof(GradSmem));
   grads_kernel<<<chunks, GW * 32, sizeof(GradSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,

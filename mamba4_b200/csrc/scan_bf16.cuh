@@ -27,8 +27,7 @@ constexpr int N = 64;        // state dim
 constexpr int P = 64;        // head dim
 constexpr int TS = 72;       // bf16 tile stride (144 B rows: ldmatrix conflict-free)
 constexpr int FS = 68;       // fp32 tile stride
-constexpr int CTH = 128;     // threads per forward / dstart chunk CTA (4 warps x 16 rows)
-constexpr int GW = 8;        // warps per grads CTA (4 row blocks x 2 column halves)
+constexpr int GW = 8;        // warps per chunk CTA (4 row blocks x 2 column halves)
 static_assert(C == 64 && (C % (4 * GW)) == 0, "warp/token maps assume 64-token chunks");
 
 M4_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -178,7 +177,7 @@ M4_DEV float rate_at(const Dims& d, const float* angles, int b, int h, int t, in
 // segment totals are combined through `r.seg`, and the same thread takes
 // sincos of its SEG elements in one compact loop. Pairs i >= A get cos 1,
 // sin 0. All 32 NW threads must call.
-template <int NW = 4>
+template <int NW = GW>
 M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles, Rows& r,
                         const float* phase0, float* cosv, float* sinv) {
   constexpr int SEG = C / NW;
@@ -221,7 +220,7 @@ M4_DEV float hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 // Rotated, rounded queries/keys of a chunk as bf16 tiles (either may be null).
 // Lane = angle pair i, warp w of NW = tokens w, w + NW, ...; all global loads
 // are issued before the rotation.
-template <int NW = 4>
+template <int NW = GW>
 M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const bf16* bk, const float* qb,
                      const float* kb, const float* cosv, const float* sinv, bf16* Qs, bf16* Ks) {
   constexpr int PER = C / NW;
@@ -254,7 +253,7 @@ M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const 
 // Copy a [64 tokens][64] slice of a [B,T,H*64] bf16 tensor into a tile, each
 // row scaled by rowscale[t] (and rounded) when given. 16 / NW 16-byte loads
 // per thread, all in flight before the stores.
-template <int NW = 4>
+template <int NW = GW>
 M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16* T,
                       const float* rowscale = nullptr) {
   constexpr int PER = 16 / NW, TH = 32 * NW;
@@ -285,7 +284,7 @@ M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16
 
 // Load a [64][64] fp32 block (row-major) into a bf16 tile with RN rounding;
 // 32 / NW 16-byte loads per thread in flight.
-template <int NW = 4>
+template <int NW = GW>
 M4_DEV void load_state_bf16(const float* src, bf16* T) {
   constexpr int PER = 32 / NW, TH = 32 * NW;
   float4 v[PER];
@@ -346,8 +345,9 @@ struct UpdSmem {
   Rows r;
 };
 
-// U_n = K^T rd(V o scale o tail) into starts[n]; deltas[n] = e^(p_L).
-__global__ void __launch_bounds__(CTH) update_kernel(
+// U_n = K^T rd(V o scale o tail) into starts[n]; deltas[n] = e^(p_L). Eight
+// warps: rows 16 (w % 4) .. +15 and column half w / 4 of the product.
+__global__ void __launch_bounds__(GW * 32) update_kernel(
     Dims d, const bf16* __restrict__ bk, const bf16* __restrict__ x, const float* __restrict__ adt,
     const float* __restrict__ dt, const float* __restrict__ trap_logits, const float* __restrict__ angles,
     const float* __restrict__ kb, const float* __restrict__ phases, float* __restrict__ starts,
@@ -355,20 +355,20 @@ __global__ void __launch_bounds__(CTH) update_kernel(
   extern __shared__ __align__(16) unsigned char raw[];
   UpdSmem& s = *reinterpret_cast<UpdSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5;
+  const int t0 = n * C, warp = threadIdx.x >> 5, row0 = 16 * (warp & 3), col0 = 32 * (warp >> 2);
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
+  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
   if (threadIdx.x < C) s.scratch[threadIdx.x] = s.r.scl[threadIdx.x] * s.r.tail[threadIdx.x];
   __syncthreads();
-  build_qk(d, b, h, t0, nullptr, bk, nullptr, kb, s.theta, s.sinv, nullptr, s.Ks);
-  load_tile(d, b, h, t0, x, s.Vw, s.scratch);
+  build_qk<GW>(d, b, h, t0, nullptr, bk, nullptr, kb, s.theta, s.sinv, nullptr, s.Ks);
+  load_tile<GW>(d, b, h, t0, x, s.Vw, s.scratch);
   __syncthreads();
-  float acc[8][4];
+  float acc[4][4];
   zero(acc);
-  mma_tile<C, 8, true, true>(acc, s.Ks, warp * 16, s.Vw, 0);  // rows n (A = K^T), cols p
-  store_f32<8>(starts + (size_t(bh) * d.nch + n) * N * P, P, warp * 16, acc);
+  mma_tile<C, 4, true, true>(acc, s.Ks, row0, s.Vw, col0);  // rows n (A = K^T), cols p
+  store_f32<4>(starts + (size_t(bh) * d.nch + n) * N * P + col0, P, row0, acc);
   if (threadIdx.x == 0) deltas[size_t(bh) * d.nch + n] = expf(s.r.p[C - 1]);
 }
 
@@ -413,8 +413,9 @@ struct OutSmem {
   Rows r;
 };
 
-// y = rd(rd((Q K^T) o W) V + e^p Q rd(S_n)).
-__global__ void __launch_bounds__(CTH) output_kernel(
+// y = rd(rd((Q K^T) o W) V + e^p Q rd(S_n)). Eight warps: rows
+// 16 (w % 4) .. +15 and column half w / 4 of every product.
+__global__ void __launch_bounds__(GW * 32) output_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ bk, const bf16* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
@@ -422,32 +423,32 @@ __global__ void __launch_bounds__(CTH) output_kernel(
   extern __shared__ __align__(16) unsigned char raw[];
   OutSmem& s = *reinterpret_cast<OutSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5, row0 = warp * 16;
+  const int t0 = n * C, warp = threadIdx.x >> 5, row0 = 16 * (warp & 3), col0 = 32 * (warp >> 2);
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
+  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
-  load_tile(d, b, h, t0, x, s.Vs);
-  load_state_bf16(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
+  build_qk<GW>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+  load_tile<GW>(d, b, h, t0, x, s.Vs);
+  load_state_bf16<GW>(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
   __syncthreads();
   {
-    float acc[8][4];
+    float acc[4][4];
     zero(acc);
-    mma_tile<N, 8, false, false>(acc, s.Qs, row0, s.Ks, 0);  // Q K^T: B = K as [s][n]
-    store_bf16<8>(s.Ms, row0, 0, acc, [&](int t, int sidx, float v) {
+    mma_tile<N, 4, false, false>(acc, s.Qs, row0, s.Ks, col0);  // Q K^T: B = K as [s][n]
+    store_bf16<4>(s.Ms, row0, col0, acc, [&](int t, int sidx, float v) {
       float w = 0.f;
       if (sidx < t) w = expf(s.r.p[t] - s.r.p[sidx]) * s.r.scl[sidx];
       else if (sidx == t) w = s.r.gam[t];
       return v * w;
     });
   }
-  __syncwarp();  // each warp reads back only its own 16 rows of Ms
-  float acc[8][4], inh[8][4];
+  __syncthreads();  // the other column half of each Ms row comes from the partner warp
+  float acc[4][4], inh[4][4];
   zero(acc);
   zero(inh);
-  mma_tile<C, 8, false, true>(acc, s.Ms, row0, s.Vs, 0);   // mixed V: B = V as [s][p]
-  mma_tile<N, 8, false, true>(inh, s.Qs, row0, s.Ss, 0);   // Q S: B = S as [n][p]
+  mma_tile<C, 4, false, true>(acc, s.Ms, row0, s.Vs, col0);   // mixed V: B = V as [s][p]
+  mma_tile<N, 4, false, true>(inh, s.Qs, row0, s.Ss, col0);   // Q S: B = S as [n][p]
   const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf) {
@@ -456,8 +457,8 @@ __global__ void __launch_bounds__(CTH) output_kernel(
     const float e = s.r.ept[tt];
     bf16* yrow = y + (size_t(b) * d.T + t) * d.H * P + h * P;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const int col = nt * 8 + 2 * c;
+    for (int nt = 0; nt < 4; ++nt) {
+      const int col = col0 + nt * 8 + 2 * c;
       *reinterpret_cast<__nv_bfloat162*>(yrow + col) = __floats2bfloat162_rn(
           fmaf(e, inh[nt][2 * hf], acc[nt][2 * hf]), fmaf(e, inh[nt][2 * hf + 1], acc[nt][2 * hf + 1]));
     }
@@ -476,26 +477,27 @@ struct DsSmem {
   Rows r;
 };
 
-// D_n = Q^T rd(dY o e^p) into carries[n].
-__global__ void __launch_bounds__(CTH) dstart_kernel(
+// D_n = Q^T rd(dY o e^p) into carries[n]. Eight warps: rows 16 (w % 4) ..
+// +15 and column half w / 4 of the product.
+__global__ void __launch_bounds__(GW * 32) dstart_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ dy, const float* __restrict__ adt,
     const float* __restrict__ dt, const float* __restrict__ trap_logits, const float* __restrict__ angles,
     const float* __restrict__ qb, const float* __restrict__ phases, float* __restrict__ carries) {
   extern __shared__ __align__(16) unsigned char raw[];
   DsSmem& s = *reinterpret_cast<DsSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5;
+  const int t0 = n * C, warp = threadIdx.x >> 5, row0 = 16 * (warp & 3), col0 = 32 * (warp >> 2);
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
-  chunk_theta(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
+  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk(d, b, h, t0, cq, nullptr, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
-  load_tile(d, b, h, t0, dy, s.Ds, s.r.ept);
+  build_qk<GW>(d, b, h, t0, cq, nullptr, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
+  load_tile<GW>(d, b, h, t0, dy, s.Ds, s.r.ept);
   __syncthreads();
-  float acc[8][4];
+  float acc[4][4];
   zero(acc);
-  mma_tile<C, 8, true, true>(acc, s.Qs, warp * 16, s.Ds, 0);  // Q^T D: rows n, cols p
-  store_f32<8>(carries + (size_t(bh) * d.nch + n) * N * P, P, warp * 16, acc);
+  mma_tile<C, 4, true, true>(acc, s.Qs, row0, s.Ds, col0);  // Q^T D: rows n, cols p
+  store_f32<4>(carries + (size_t(bh) * d.nch + n) * N * P + col0, P, row0, acc);
 }
 
 // Reverse over chunks, in place: carries[n] <- E_n (cotangent of chunk n's end
