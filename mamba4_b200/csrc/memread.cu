@@ -806,7 +806,9 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
 // Backward kernels.
 // ---------------------------------------------------------------------------
 // zsolve_kernel: z_t = A_t^-1 g_t from the stored factor (one warp per token
-// at a time, 16 tokens per warp).
+// at a time, 16 tokens per warp). The next token's factor and right-hand side
+// stream into shared memory (cp.async; the evidence buffer of the forward's
+// layout is free here) while the current token is solved.
 __global__ void __launch_bounds__(32 * WARPS, 4) zsolve_kernel(
     int B, int T, int H, const float* __restrict__ Lst, const float* __restrict__ G,
     float* __restrict__ Z) {
@@ -819,17 +821,29 @@ __global__ void __launch_bounds__(32 * WARPS, 4) zsolve_kernel(
   if (wid >= B * H * nsub) return;
   SolveSmem& sm = smem_all[warp];
   const int sub = wid % nsub, bh = wid / nsub;
-  for (int tt = 0; tt < SUB; ++tt) {
-    const int t = sub * SUB + tt;
-    float2 L[NPAIR];
+  auto prefetch = [&](int t) {
     const float* src = Lst + (size_t(bh) * Tp + t) * LSTRIDE;
 #pragma unroll
+    for (int q4 = 0; q4 < NPAIR / 2; ++q4)
+      cp16(reinterpret_cast<float*>(&sm.E[q4][lane]), src + (q4 * 32 + lane) * 4, true);
+    if (lane < 16) cp16(&sm.flC[4 * lane], G + (size_t(bh) * Tp + t) * KD + 4 * lane, true);
+    cp_commit();
+  };
+  prefetch(sub * SUB);
+  for (int tt = 0; tt < SUB; ++tt) {
+    const int t = sub * SUB + tt;
+    cp_wait_group<0>();
+    __syncwarp();
+    float2 L[NPAIR];
+#pragma unroll
     for (int q4 = 0; q4 < NPAIR / 2; ++q4) {
-      const float4 v4 = __ldcs(reinterpret_cast<const float4*>(src + (q4 * 32 + lane) * 4));
+      const float4 v4 = sm.E[q4][lane];
       L[2 * q4] = make_float2(v4.x, v4.y);
       L[2 * q4 + 1] = make_float2(v4.z, v4.w);
     }
-    if (lane < 16) st4(&sm.y[4 * lane], ld4(G + (size_t(bh) * Tp + t) * KD + 4 * lane));
+    if (lane < 16) st4(&sm.y[4 * lane], ld4(&sm.flC[4 * lane]));
+    __syncwarp();  // the buffers are refilled below
+    if (tt + 1 < SUB) prefetch(t + 1);
     invert_blocks(L, sm, lane, a, b);
     forward_substitute(L, sm, sm.y, sm.w, a, b);
     back_substitute(L, sm, sm.w, sm.y, a, b);
