@@ -605,6 +605,7 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
 // ---------------------------------------------------------------------------
 constexpr int LD = 68;    // tile stride in floats (conflict-free A fragments)
 constexpr int CT = 256;   // threads per chunk CTA
+constexpr int CTG = 512;  // threads per chunk-gradient CTA (16 warps: 4 row blocks x 4 column quarters)
 
 M4_DEV uint32_t to_tf32(float x) {
   uint32_t r;
@@ -683,10 +684,10 @@ M4_DEV void chunk_gates(int tid, int b, int T, int H, int h, int t0, const float
 
 // Start copying a [64 tokens][W] chunk of a [B,T,H,W] tensor into a tile of
 // stride ld (tokens past T read as zero).
-template <int W>
+template <int W, int NTH = CT>
 M4_DEV void load_tokens(float* tile, int ld, const float* src, int b, int T, int H, int h, int t0, int tid) {
 #pragma unroll
-  for (int idx = tid; idx < CH * W / 4; idx += CT) {
+  for (int idx = tid; idx < CH * W / 4; idx += NTH) {
     const int tt = idx / (W / 4), c4 = idx % (W / 4), t = t0 + tt;
     const bool live = t < T;
     cp16(tile + tt * ld + 4 * c4, live ? src + ((size_t(b) * T + t) * H + h) * W + 4 * c4 : src, live);
@@ -694,8 +695,9 @@ M4_DEV void load_tokens(float* tile, int ld, const float* src, int b, int T, int
 }
 
 // Start copying a dense [rows][64] row-major block into a tile of stride LD.
+template <int NTH = CT>
 M4_DEV void load_block(float* tile, int rows, const float* src, int tid) {
-  for (int idx = tid; idx < rows * KD / 4; idx += CT) cp16(tile + (idx / 16) * LD + 4 * (idx % 16), src + 4 * idx, true);
+  for (int idx = tid; idx < rows * KD / 4; idx += NTH) cp16(tile + (idx / 16) * LD + 4 * (idx % 16), src + 4 * idx, true);
 }
 
 template <int P>
@@ -934,7 +936,7 @@ M4_DEV void row_reduce_store(float v0, float v1, float* dst, int row0) {
 // grads_kernel: every input gradient of one chunk (chunk form; the algebra
 // is written out in oracle/memread.py:chunked_backward).
 template <int P>
-__global__ void __launch_bounds__(CT) grads_kernel(
+__global__ void __launch_bounds__(CTG) grads_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ values,
     const float* __restrict__ beta, const float* __restrict__ log_decay,
     const float* __restrict__ Y, const float* __restrict__ Z, const float* __restrict__ s_start,
@@ -943,7 +945,7 @@ __global__ void __launch_bounds__(CT) grads_kernel(
     const float* __restrict__ d_var, float* __restrict__ dk, float* __restrict__ dv,
     float* __restrict__ dq, float* __restrict__ dbeta, float* __restrict__ dlog,
     float* __restrict__ floor_part) {
-  constexpr int LP = P + 4, NTP = P / 16;
+  constexpr int LP = P + 4, NTQ = P / 32;
   extern __shared__ __align__(16) float sh[];
   float* Ys = sh;                 // [64][LD]
   float* Zs = Ys + CH * LD;       // [64][LD]
@@ -957,42 +959,42 @@ __global__ void __launch_bounds__(CT) grads_kernel(
   float* pre = Cb + P * LD;
   float* bet = pre + CH;
   float* ept = bet + CH;
-  float* rowP = ept + CH;         // [2][64] half partials of sum_s dW W [t, s]
-  float* colP = rowP + 2 * CH;    // [4][64] row-block partials of sum_t dW W [t, s]
+  float* rowP = ept + CH;         // [4][64] column-quarter partials of sum_s dW W [t, s]
+  float* colP = rowP + 4 * CH;    // [4][64] row-block partials of sum_t dW W [t, s]
   float* decP = colP + 4 * CH;    // [4][64] row-block partials of sum_t dW D [t, s]
-  float* wbP = decP + 4 * CH;     // [2][64] half partials of dw_s
-  float* exP = wbP + 2 * CH;      // [2][64] half partials of the per-token extra term
-  float* red = exP + 2 * CH;      // [64 + 16] scratch
+  float* wbP = decP + 4 * CH;     // [4][64] column-quarter partials of dw_s
+  float* exP = wbP + 4 * CH;      // [4][64] column-quarter partials of the per-token extra term
+  float* red = exP + 4 * CH;      // [64 + 16] scratch
   const int Tp = (T + CH - 1) / CH * CH, nch = Tp / CH, nsub = Tp / SUB;
   const int ch = blockIdx.x % nch, bh = blockIdx.x / nch, b = bh / H, h = bh % H;
   const int t0 = ch * CH, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row0 = 16 * (warp & 3), half = warp >> 2, rb = warp & 3;
-  const int c64 = 32 * half, cP = half * (P / 2);
-  load_block(Ys, CH, Y + (size_t(bh) * Tp + t0) * KD, tid);
-  load_block(Zs, CH, Z + (size_t(bh) * Tp + t0) * KD, tid);
-  load_tokens<KD>(Ks, LD, keys, b, T, H, h, t0, tid);
-  load_tokens<P>(Os, LP, d_out, b, T, H, h, t0, tid);
-  load_tokens<P>(Vs, LP, values, b, T, H, h, t0, tid);
-  load_block(Sb, KD, sbar + (size_t(bh) * nch + ch) * KD * KD, tid);
-  load_block(Cb, P, cbar + (size_t(bh) * nch + ch) * P * KD, tid);
+  const int row0 = 16 * (warp & 3), qt = warp >> 2, rb = warp & 3;
+  const int c64 = 16 * qt, cP = qt * (P / 4);
+  load_block<CTG>(Ys, CH, Y + (size_t(bh) * Tp + t0) * KD, tid);
+  load_block<CTG>(Zs, CH, Z + (size_t(bh) * Tp + t0) * KD, tid);
+  load_tokens<KD, CTG>(Ks, LD, keys, b, T, H, h, t0, tid);
+  load_tokens<P, CTG>(Os, LP, d_out, b, T, H, h, t0, tid);
+  load_tokens<P, CTG>(Vs, LP, values, b, T, H, h, t0, tid);
+  load_block<CTG>(Sb, KD, sbar + (size_t(bh) * nch + ch) * KD * KD, tid);
+  load_block<CTG>(Cb, P, cbar + (size_t(bh) * nch + ch) * P * KD, tid);
   chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
   cp_wait();
   __syncthreads();
   const float pl = pre[CH - 1];
   // Phase 1: GY, GZ, OV -> M1, M2 and the dW reductions.
   {
-    float gy[4][4], gz[4][4], ov[4][4];
+    float gy[2][4], gz[2][4], ov[2][4];
     zero(gy); zero(gz); zero(ov);
-    gemm3<KD, 4>(gy, row0, c64, [&](int r, int k) { return Ys[r * LD + k]; },
+    gemm3<KD, 2>(gy, row0, c64, [&](int r, int k) { return Ys[r * LD + k]; },
                  [&](int k, int s) { return Ks[s * LD + k]; });
-    gemm3<KD, 4>(gz, row0, c64, [&](int r, int k) { return Zs[r * LD + k]; },
+    gemm3<KD, 2>(gz, row0, c64, [&](int r, int k) { return Zs[r * LD + k]; },
                  [&](int k, int s) { return Ks[s * LD + k]; });
-    gemm3<P, 4>(ov, row0, c64, [&](int r, int k) { return Os[r * LP + k]; },
+    gemm3<P, 2>(ov, row0, c64, [&](int r, int k) { return Os[r * LP + k]; },
                 [&](int k, int s) { return Vs[s * LP + k]; });
-    float r0 = 0.f, r1 = 0.f, cw[4][2], cd[4][2];
+    float r0 = 0.f, r1 = 0.f, cw[2][2], cd[2][2];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) cw[nt][0] = cw[nt][1] = cd[nt][0] = cd[nt][1] = 0.f;
-    each<4>(row0, c64, [&](int t, int s, int nt, int e) {
+    for (int nt = 0; nt < 2; ++nt) cw[nt][0] = cw[nt][1] = cd[nt][0] = cd[nt][1] = 0.f;
+    each<2>(row0, c64, [&](int t, int s, int nt, int e) {
       const bool on = s <= t;
       const float dec = on ? expf(pre[t] - pre[s]) : 0.f;
       const float w = dec * bet[s];
@@ -1004,10 +1006,10 @@ __global__ void __launch_bounds__(CT) grads_kernel(
       cw[nt][e & 1] = fmaf(dw, w, cw[nt][e & 1]);
       cd[nt][e & 1] = fmaf(dw, dec, cd[nt][e & 1]);
     });
-    row_reduce_store(r0, r1, rowP + half * CH, row0);
+    row_reduce_store(r0, r1, rowP + qt * CH, row0);
     // Column partials: reduce over the 8 row groups g of this warp.
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float a = cw[nt][e], d = cd[nt][e];
@@ -1026,18 +1028,18 @@ __global__ void __launch_bounds__(CT) grads_kernel(
   __syncthreads();
   // Phase 2: dK and dV (rows s) and dw_s.
   {
-    float acc[4][4], tks[4][4], tkc[4][4];
+    float acc[2][4], tks[2][4], tkc[2][4];
     zero(acc); zero(tks); zero(tkc);
-    gemm3<CH, 4>(acc, row0, c64, [&](int s, int t) { return -M1[t * LD + s]; },
+    gemm3<CH, 2>(acc, row0, c64, [&](int s, int t) { return -M1[t * LD + s]; },
                  [&](int t, int d) { return Zs[t * LD + d]; });
-    gemm3<CH, 4>(acc, row0, c64, [&](int s, int t) { return M2[t * LD + s]; },
+    gemm3<CH, 2>(acc, row0, c64, [&](int s, int t) { return M2[t * LD + s]; },
                  [&](int t, int d) { return Ys[t * LD + d]; });
-    gemm3<KD, 4>(tks, row0, c64, [&](int s, int e) { return Ks[s * LD + e]; },
+    gemm3<KD, 2>(tks, row0, c64, [&](int s, int e) { return Ks[s * LD + e]; },
                  [&](int e, int d) { return Sb[e * LD + d] + Sb[d * LD + e]; });
-    gemm3<P, 4>(tkc, row0, c64, [&](int s, int p) { return Vs[s * LP + p]; },
+    gemm3<P, 2>(tkc, row0, c64, [&](int s, int p) { return Vs[s * LP + p]; },
                 [&](int p, int d) { return Cb[p * LD + d]; });
     float w0 = 0.f, w1 = 0.f;
-    each<4>(row0, c64, [&](int s, int d, int nt, int e) {
+    each<2>(row0, c64, [&](int s, int d, int nt, int e) {
       const float part = 0.5f * Ks[s * LD + d] * tks[nt][e];
       if (e < 2) w0 += part; else w1 += part;
       const int t = t0 + s;
@@ -1046,13 +1048,13 @@ __global__ void __launch_bounds__(CT) grads_kernel(
         dk[((size_t(b) * T + t) * H + h) * KD + d] = fmaf(ws, tks[nt][e] + tkc[nt][e], acc[nt][e]);
       }
     });
-    float accv[NTP][4], ck[NTP][4];
+    float accv[NTQ][4], ck[NTQ][4];
     zero(accv); zero(ck);
-    gemm3<CH, NTP>(accv, row0, cP, [&](int s, int t) { return M1[t * LD + s]; },
+    gemm3<CH, NTQ>(accv, row0, cP, [&](int s, int t) { return M1[t * LD + s]; },
                    [&](int t, int p) { return Os[t * LP + p]; });
-    gemm3<KD, NTP>(ck, row0, cP, [&](int s, int d) { return Ks[s * LD + d]; },
+    gemm3<KD, NTQ>(ck, row0, cP, [&](int s, int d) { return Ks[s * LD + d]; },
                    [&](int d, int p) { return Cb[p * LD + d]; });
-    each<NTP>(row0, cP, [&](int s, int p, int nt, int e) {
+    each<NTQ>(row0, cP, [&](int s, int p, int nt, int e) {
       const float part = Vs[s * LP + p] * ck[nt][e];
       if (e < 2) w0 += part; else w1 += part;
       const int t = t0 + s;
@@ -1061,7 +1063,7 @@ __global__ void __launch_bounds__(CT) grads_kernel(
         dv[((size_t(b) * T + t) * H + h) * P + p] = fmaf(ws, ck[nt][e], accv[nt][e]);
       }
     });
-    row_reduce_store(w0, w1, wbP + half * CH, row0);
+    row_reduce_store(w0, w1, wbP + qt * CH, row0);
   }
   __syncthreads();
   // <dS_end, S0> + <dC_end, C0>, then S0 and C0 replace them in the tiles.
@@ -1070,16 +1072,16 @@ __global__ void __launch_bounds__(CT) grads_kernel(
   {
     // Each thread reads its own float4 slots of Sb / Cb, then overwrites the
     // same slots with S0 / C0 (no other thread touches them in between).
-    constexpr int NS = KD * KD / 4 / CT, NC = P * KD / 4 / CT;
+    constexpr int NS = KD * KD / 4 / CTG, NC = P * KD / 4 / CTG;
     float4 sv[NS], cv[NC];
 #pragma unroll
-    for (int i = 0; i < NS; ++i) sv[i] = ld4(s0 + 4 * (tid + CT * i));
+    for (int i = 0; i < NS; ++i) sv[i] = ld4(s0 + 4 * (tid + CTG * i));
 #pragma unroll
-    for (int i = 0; i < NC; ++i) cv[i] = ld4(c0 + 4 * (tid + CT * i));
+    for (int i = 0; i < NC; ++i) cv[i] = ld4(c0 + 4 * (tid + CTG * i));
     float part = 0.f;
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
-      const int idx = tid + CT * i;
+      const int idx = tid + CTG * i;
       float* slot = Sb + (idx / 16) * LD + 4 * (idx % 16);
       const float4 e = ld4(slot);
       part = fmaf(e.x, sv[i].x, fmaf(e.y, sv[i].y, fmaf(e.z, sv[i].z, fmaf(e.w, sv[i].w, part))));
@@ -1087,7 +1089,7 @@ __global__ void __launch_bounds__(CT) grads_kernel(
     }
 #pragma unroll
     for (int i = 0; i < NC; ++i) {
-      const int idx = tid + CT * i;
+      const int idx = tid + CTG * i;
       float* slot = Cb + (idx / 16) * LD + 4 * (idx % 16);
       const float4 e = ld4(slot);
       part = fmaf(e.x, cv[i].x, fmaf(e.y, cv[i].y, fmaf(e.z, cv[i].z, fmaf(e.w, cv[i].w, part))));
@@ -1099,22 +1101,22 @@ __global__ void __launch_bounds__(CT) grads_kernel(
   __syncthreads();
   // Phase 3: extra_t = e^(P_t) (-z_t . (S0 y_t) + dO_t . (C0 y_t)).
   {
-    float sy[4][4], cy[NTP][4];
+    float sy[2][4], cy[NTQ][4];
     zero(sy); zero(cy);
-    gemm3<KD, 4>(sy, row0, c64, [&](int t, int k) { return Ys[t * LD + k]; },
+    gemm3<KD, 2>(sy, row0, c64, [&](int t, int k) { return Ys[t * LD + k]; },
                  [&](int k, int d) { return Sb[d * LD + k]; });
-    gemm3<KD, NTP>(cy, row0, cP, [&](int t, int k) { return Ys[t * LD + k]; },
+    gemm3<KD, NTQ>(cy, row0, cP, [&](int t, int k) { return Ys[t * LD + k]; },
                    [&](int k, int p) { return Cb[p * LD + k]; });
     float v0 = 0.f, v1 = 0.f;
-    each<4>(row0, c64, [&](int t, int d, int nt, int e) {
+    each<2>(row0, c64, [&](int t, int d, int nt, int e) {
       const float part = -Zs[t * LD + d] * sy[nt][e];
       if (e < 2) v0 += part; else v1 += part;
     });
-    each<NTP>(row0, cP, [&](int t, int p, int nt, int e) {
+    each<NTQ>(row0, cP, [&](int t, int p, int nt, int e) {
       const float part = Os[t * LP + p] * cy[nt][e];
       if (e < 2) v0 += part; else v1 += part;
     });
-    row_reduce_store(v0, v1, exP + half * CH, row0);
+    row_reduce_store(v0, v1, exP + qt * CH, row0);
   }
   __syncthreads();
   // Per-token scalars: dbeta, dP -> reverse cumsum -> dlog_decay.
@@ -1122,10 +1124,11 @@ __global__ void __launch_bounds__(CT) grads_kernel(
     const int s = tid;
     const float tail = expf(pl - pre[s]);
     const float ws = bet[s] * tail;
-    const float wbar = wbP[s] + wbP[CH + s];
+    const float wbar = wbP[s] + wbP[CH + s] + wbP[2 * CH + s] + wbP[3 * CH + s];
     const float colsum = colP[s] + colP[CH + s] + colP[2 * CH + s] + colP[3 * CH + s];
     const float decsum = decP[s] + decP[CH + s] + decP[2 * CH + s] + decP[3 * CH + s];
-    red[s] = (rowP[s] + rowP[CH + s]) - colsum - wbar * ws + ept[s] * (exP[s] + exP[CH + s]);
+    red[s] = (rowP[s] + rowP[CH + s] + rowP[2 * CH + s] + rowP[3 * CH + s]) - colsum - wbar * ws +
+             ept[s] * (exP[s] + exP[CH + s] + exP[2 * CH + s] + exP[3 * CH + s]);
     const int t = t0 + s;
     if (t < T) dbeta[(size_t(b) * T + t) * H + h] = decsum + wbar * tail;
     colP[s] = wbar * ws;  // reuse: dw_s w_s for the chunk-end term
@@ -1136,7 +1139,7 @@ __global__ void __launch_bounds__(CT) grads_kernel(
     last = warp_sum(last);
     float dot_end = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) dot_end += red[CH + w];
+    for (int w = 0; w < CTG / 32; ++w) dot_end += red[CH + w];
     const float extra_last = last + ept[CH - 1] * dot_end;
     // reverse inclusive cumsum over 64 entries in two halves
     const float hi = red[63 - tid] + (tid == 0 ? extra_last : 0.f);
@@ -1148,7 +1151,7 @@ __global__ void __launch_bounds__(CT) grads_kernel(
     if (tlo < T) dlog[(size_t(b) * T + tlo) * H + h] = slo;
   }
   // dq = z + dvar y ; floor partial = -sum_t z o y
-  for (int idx = tid; idx < CH * KD; idx += CT) {
+  for (int idx = tid; idx < CH * KD; idx += CTG) {
     const int r = idx / KD, c = idx % KD, t = t0 + r;
     if (t < T) {
       const float dvv = d_var[(size_t(b) * T + t) * H + h];
@@ -1178,7 +1181,7 @@ size_t rhs_smem() { return (2 * CH * LD + 2 * CH * (P + 4) + P * LD + 3 * CH) * 
 template <int P>
 size_t carry_smem() { return (2 * CH * LD + CH * (P + 4) + 3 * CH) * sizeof(float); }
 template <int P>
-size_t grads_smem() { return (6 * CH * LD + 2 * CH * (P + 4) + P * LD + 18 * CH + 16) * sizeof(float); }
+size_t grads_smem() { return (6 * CH * LD + 2 * CH * (P + 4) + P * LD + 24 * CH + 16) * sizeof(float); }
 
 template <int P>
 int forward(const M4MemDims& d, const float* keys, const float* values, const float* queries,
@@ -1235,7 +1238,7 @@ int backward(const M4MemDims& d, const float* keys, const float* values, const f
                                         cb, d_init_s, d_init_c);
   const size_t gsm = grads_smem<P>();
   cudaFuncSetAttribute(grads_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(gsm));
-  grads_kernel<P><<<bh * z.nch, CT, gsm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Zb, Ss,
+  grads_kernel<P><<<bh * z.nch, CTG, gsm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Zb, Ss,
                                                 Cs, sb, cb, d_out, d_var, dk, dv, dq, dbeta, dlog, fl);
   floor_reduce_kernel<<<(z.H * KD + 255) / 256, 256, 0, st>>>(z.B * z.nch, z.H, fl, dfloor);
   return launch_status();
