@@ -41,7 +41,8 @@ typedef enum {
   M4_ERR_NULL = 3,        /* a required pointer is NULL */
   M4_ERR_ALIGN = 4,       /* a pointer is not 16-byte aligned */
   M4_ERR_LAUNCH = 5,      /* a CUDA launch reported an error */
-  M4_ERR_WORKSPACE = 6    /* residual/workspace buffer too small */
+  M4_ERR_WORKSPACE = 6,   /* residual/workspace buffer too small */
+  M4_ERR_TIMEOUT = 7      /* a bounded device wait on the tensor cores gave up */
 } M4Status;
 
 /* Memory-read problem size. key_dim must be 64 and value_dim 64 or 128
@@ -287,6 +288,12 @@ int m4_cross_entropy_fwd(int rows, int vocab, int ld, const void* logits, const 
                          float* loss, float* lse, void* stream);
 int m4_cross_entropy_bwd(int rows, int vocab, int ld, void* logits, const int64_t* targets,
                          const float* lse, const float* g, void* stream);
+
+/* Device-side status of the tensor-core (tcgen05) kernels on the current
+ * device: M4_ERR_TIMEOUT if a bounded wait for tensor-core completion gave
+ * up since the last call (the flag is then cleared), else M4_OK.
+ * Synchronous; call after the stream work of interest has finished. */
+int m4_device_status(void);
 
 /* Name of a status code (static string). */
 const char* m4_status_string(int status);

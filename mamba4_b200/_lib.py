@@ -78,6 +78,7 @@ SIGNATURES = {
     "m4_memmix_post_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 22, _c_int),
     "m4_cross_entropy_fwd": ([_c_int, _c_int, _c_int] + [_p] * 5, _c_int),
     "m4_cross_entropy_bwd": ([_c_int, _c_int, _c_int] + [_p] * 5, _c_int),
+    "m4_device_status": ([], _c_int),
     "m4_status_string": ([_c_int], ctypes.c_char_p),
     "m4_version": ([], ctypes.c_char_p),
 }

@@ -10,6 +10,7 @@ extern "C" const char* m4_status_string(int status) {
     case M4_ERR_ALIGN: return "pointer not 16-byte aligned";
     case M4_ERR_LAUNCH: return "CUDA launch failed";
     case M4_ERR_WORKSPACE: return "residual or workspace buffer too small";
+    case M4_ERR_TIMEOUT: return "a bounded wait for the tensor cores gave up";
     default: return "unknown status";
   }
 }

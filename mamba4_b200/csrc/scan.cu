@@ -898,6 +898,17 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
 
 using namespace m4;
 
+extern "C" int m4_device_status(void) {
+  int flag = 0;
+  if (cudaMemcpyFromSymbol(&flag, m4::tc::g_timeout, sizeof(int)) != cudaSuccess) return M4_ERR_LAUNCH;
+  if (flag) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(m4::tc::g_timeout, &zero, sizeof(int));
+    return M4_ERR_TIMEOUT;
+  }
+  return M4_OK;
+}
+
 extern "C" size_t m4_scan_residual_bytes(const M4ScanDims* s) {
   return scan::check(s) == M4_OK ? scan::layout(*s).resid : 0;
 }

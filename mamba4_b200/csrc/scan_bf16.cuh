@@ -18,6 +18,8 @@
 // tensor-core MMAs with fp32 accumulation.
 #pragma once
 
+#include "tc05.cuh"
+
 namespace m4 {
 namespace scan2 {
 
@@ -78,6 +80,50 @@ M4_DEV void mma_tile(float (&acc)[NT][4], const bf16* A, int row0, const bf16* B
     }
   }
 }
+
+// Element (r, c) of a 64-column bf16 tile: padded rows of TS (mma.sync path)
+// or 8 x 8 core matrices (tcgen05 descriptors, tc::blk).
+template <bool BLK>
+M4_DEV bf16* at(bf16* T, int r, int c) {
+  if constexpr (BLK) return reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(T) + tc::blk(r, c));
+  else return T + r * TS + c;
+}
+
+// D (tensor memory) = A B over K = 64 on the tensor cores (tcgen05, 4 MMAs of
+// K = 16), issued by one thread. A is M x K, B is K x N, each a blocked tile
+// read K-major (K along its contiguous columns) or MN-major (K along its rows).
+M4_DEV void tc_product(uint32_t d, const bf16* A, bool a_mn, const bf16* B, bool b_mn) {
+  const uint32_t id = tc::idesc_bf16(64, 64, a_mn ? 1 : 0, b_mn ? 1 : 0);
+  const unsigned char* a = reinterpret_cast<const unsigned char*>(A);
+  const unsigned char* b = reinterpret_cast<const unsigned char*>(B);
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const uint64_t ad = a_mn ? tc::sdesc(a + 2048 * ks, 1024, 128) : tc::sdesc(a + 256 * ks, 128, 1024);
+    const uint64_t bd = b_mn ? tc::sdesc(b + 2048 * ks, 1024, 128) : tc::sdesc(b + 256 * ks, 128, 1024);
+    tc::mma_bf16(d, ad, bd, id, ks > 0);
+  }
+}
+
+// Everyone: wait (bounded) for the tensor-core work committed to `bar` in
+// phase `phase`; a timeout raises the device error flag.
+M4_DEV bool tc_wait(uint64_t* bar, uint32_t phase) {
+  const bool ok = tc::mbar_wait(bar, phase, tc::WAIT_LIMIT);
+  if (!ok && (threadIdx.x & 31) == 0) tc::flag_timeout();
+  tc::fence_after();
+  return ok;
+}
+
+// Shared writes -> visible to the tensor cores, then a CTA barrier.
+M4_DEV void tc_publish() {
+  tc::fence_proxy_async();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+}
+
+// Accumulator row this thread reads (lanes 0..15 of each warp) and its
+// tensor-memory lane base; warps w and w + 4 share a lane quarter.
+M4_DEV uint32_t tmem_lane_base(uint32_t tm) { return tm + (uint32_t(32 * ((threadIdx.x >> 5) & 3)) << 16); }
 
 template <int NT>
 M4_DEV void zero(float (&acc)[NT][4]) {
@@ -220,32 +266,35 @@ M4_DEV float hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 // Rotated, rounded queries/keys of a chunk as bf16 tiles (either may be null).
 // Lane = angle pair i, warp w of NW = tokens w, w + NW, ...; all global loads
 // are issued before the rotation.
-template <int NW = GW>
+template <int NW = GW, bool BLK = false>
 M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const bf16* bk, const float* qb,
                      const float* kb, const float* cosv, const float* sinv, bf16* Qs, bf16* Ks) {
   constexpr int PER = C / NW;
-  const int i = threadIdx.x & 31, w = threadIdx.x >> 5, n0 = 2 * i;
-  const float qb0 = qb ? qb[h * N + n0] : 0.f, qb1 = qb ? qb[h * N + n0 + 1] : 0.f;
-  const float kb0 = kb ? kb[h * N + n0] : 0.f, kb1 = kb ? kb[h * N + n0 + 1] : 0.f;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int tt_[PER], i_[PER];
   uint32_t cr[PER], br[PER];
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
-    const int t = t0 + w + NW * k;
+    tt_[k] = w + NW * k;
+    i_[k] = lane;
+    const int t = t0 + tt_[k], n0 = 2 * i_[k];
     const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
     cr[k] = (Qs && t < d.T) ? ld_u32(cq + base + n0) : 0u;
     br[k] = (Ks && t < d.T) ? ld_u32(bk + base + n0) : 0u;
   }
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
-    const int tt = w + NW * k;
+    const int tt = tt_[k], i = i_[k], n0 = 2 * i;
     const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
     if (Qs) {
-      const float q0 = round_to<bf16>(lo_f(cr[k]) + qb0), q1 = round_to<bf16>(hi_f(cr[k]) + qb1);
-      *reinterpret_cast<__nv_bfloat162*>(Qs + tt * TS + n0) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
+      const float q0 = round_to<bf16>(lo_f(cr[k]) + (qb ? qb[h * N + n0] : 0.f));
+      const float q1 = round_to<bf16>(hi_f(cr[k]) + (qb ? qb[h * N + n0 + 1] : 0.f));
+      *reinterpret_cast<__nv_bfloat162*>(at<BLK>(Qs, tt, n0)) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
     }
     if (Ks) {
-      const float k0 = round_to<bf16>(lo_f(br[k]) + kb0), k1 = round_to<bf16>(hi_f(br[k]) + kb1);
-      *reinterpret_cast<__nv_bfloat162*>(Ks + tt * TS + n0) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+      const float k0 = round_to<bf16>(lo_f(br[k]) + (kb ? kb[h * N + n0] : 0.f));
+      const float k1 = round_to<bf16>(hi_f(br[k]) + (kb ? kb[h * N + n0 + 1] : 0.f));
+      *reinterpret_cast<__nv_bfloat162*>(at<BLK>(Ks, tt, n0)) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
     }
   }
 }
@@ -253,23 +302,26 @@ M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const 
 // Copy a [64 tokens][64] slice of a [B,T,H*64] bf16 tensor into a tile, each
 // row scaled by rowscale[t] (and rounded) when given. 16 / NW 16-byte loads
 // per thread, all in flight before the stores.
-template <int NW = GW>
+template <int NW = GW, bool BLK = false>
 M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16* T,
                       const float* rowscale = nullptr) {
   constexpr int PER = 16 / NW, TH = 32 * NW;
   uint4 v[PER];
+  int rr[PER], cc8[PER];
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
-    const int idx = threadIdx.x + k * TH, tt = idx >> 3, c8 = idx & 7, t = t0 + tt;
-    v[k] = t < d.T ? *reinterpret_cast<const uint4*>(src + (size_t(b) * d.T + t) * d.H * P + h * P + 8 * c8)
+    const int idx = threadIdx.x + k * TH;
+    rr[k] = idx >> 3;
+    cc8[k] = idx & 7;
+    const int t = t0 + rr[k];
+    v[k] = t < d.T ? *reinterpret_cast<const uint4*>(src + (size_t(b) * d.T + t) * d.H * P + h * P + 8 * cc8[k])
                    : make_uint4(0u, 0u, 0u, 0u);
   }
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
-    const int idx = threadIdx.x + k * TH, tt = idx >> 3, c8 = idx & 7;
     uint4 o = v[k];
     if (rowscale) {
-      const float f = rowscale[tt];
+      const float f = rowscale[rr[k]];
       uint32_t* u = reinterpret_cast<uint32_t*>(&v[k]);
       uint32_t* r = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
@@ -278,23 +330,28 @@ M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16
         r[q] = *reinterpret_cast<const uint32_t*>(&x2);
       }
     }
-    *reinterpret_cast<uint4*>(T + tt * TS + 8 * c8) = o;
+    *reinterpret_cast<uint4*>(at<BLK>(T, rr[k], 8 * cc8[k])) = o;
   }
 }
 
 // Load a [64][64] fp32 block (row-major) into a bf16 tile with RN rounding;
 // 32 / NW 16-byte loads per thread in flight.
-template <int NW = GW>
+template <int NW = GW, bool BLK = false>
 M4_DEV void load_state_bf16(const float* src, bf16* T) {
   constexpr int PER = 32 / NW, TH = 32 * NW;
   float4 v[PER];
-#pragma unroll
-  for (int k = 0; k < PER; ++k) v[k] = ld4(src + 4 * (threadIdx.x + k * TH));
+  int rr[PER], cc[PER];
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
-    const int idx = threadIdx.x + k * TH, r = idx / (P / 4), c4 = idx % (P / 4);
-    *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4) = __floats2bfloat162_rn(v[k].x, v[k].y);
-    *reinterpret_cast<__nv_bfloat162*>(T + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(v[k].z, v[k].w);
+    const int idx = threadIdx.x + k * TH;
+    rr[k] = idx / (P / 4);
+    cc[k] = 4 * (idx % (P / 4));
+    v[k] = ld4(src + rr[k] * P + cc[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    *reinterpret_cast<__nv_bfloat162*>(at<BLK>(T, rr[k], cc[k])) = __floats2bfloat162_rn(v[k].x, v[k].y);
+    *reinterpret_cast<__nv_bfloat162*>(at<BLK>(T, rr[k], cc[k] + 2)) = __floats2bfloat162_rn(v[k].z, v[k].w);
   }
 }
 
@@ -337,38 +394,63 @@ __global__ void __launch_bounds__(256) phase_kernel(Dims d, const float* __restr
 }
 
 struct UpdSmem {
-  bf16 Ks[C * TS];
-  bf16 Vw[C * TS];
-  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  bf16 Ks[C * N];  // blocked tiles (tcgen05 operands)
+  bf16 Vw[C * P];
+  float theta[C * 33];
   float sinv[C * 33];
   float scratch[C];
   Rows r;
+  uint64_t bar;
+  uint32_t tmem;
 };
 
-// U_n = K^T rd(V o scale o tail) into starts[n]; deltas[n] = e^(p_L). Eight
-// warps: rows 16 (w % 4) .. +15 and column half w / 4 of the product.
+// U_n = K^T rd(V o scale o tail) into starts[n]; deltas[n] = e^(p_L). The
+// product runs on the tensor cores (tcgen05, accumulator in tensor memory).
 __global__ void __launch_bounds__(GW * 32) update_kernel(
     Dims d, const bf16* __restrict__ bk, const bf16* __restrict__ x, const float* __restrict__ adt,
     const float* __restrict__ dt, const float* __restrict__ trap_logits, const float* __restrict__ angles,
     const float* __restrict__ kb, const float* __restrict__ phases, float* __restrict__ starts,
     float* __restrict__ deltas) {
-  extern __shared__ __align__(16) unsigned char raw[];
+  extern __shared__ __align__(128) unsigned char raw[];
   UpdSmem& s = *reinterpret_cast<UpdSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5, row0 = 16 * (warp & 3), col0 = 32 * (warp >> 2);
+  const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    tc::tmem_alloc(&s.tmem, 64);
+    tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
+  }
+  if (threadIdx.x == 0) tc::mbar_init(&s.bar, 1);
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
   chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
   if (threadIdx.x < C) s.scratch[threadIdx.x] = s.r.scl[threadIdx.x] * s.r.tail[threadIdx.x];
   __syncthreads();
-  build_qk<GW>(d, b, h, t0, nullptr, bk, nullptr, kb, s.theta, s.sinv, nullptr, s.Ks);
-  load_tile<GW>(d, b, h, t0, x, s.Vw, s.scratch);
+  build_qk<GW, true>(d, b, h, t0, nullptr, bk, nullptr, kb, s.theta, s.sinv, nullptr, s.Ks);
+  load_tile<GW, true>(d, b, h, t0, x, s.Vw, s.scratch);
+  tc_publish();
+  const uint32_t tm = s.tmem;
+  if (threadIdx.x == 0) {
+    tc_product(tm, s.Ks, true, s.Vw, true);  // rows n (A = K^T), cols p
+    tc::commit(&s.bar);
+  }
+  if (tc_wait(&s.bar, 0)) {
+    const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
+    float v[2][16];
+    tc::ld16(tmem_lane_base(tm) + col0, v[0]);
+    tc::ld16(tmem_lane_base(tm) + col0 + 16, v[1]);
+    tc::wait_ld();
+    if (lane < 16) {
+      float* dst = starts + (size_t(bh) * d.nch + n) * N * P + row * P + col0;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 16; e += 4) st4(dst + 16 * j + e, make_float4(v[j][e], v[j][e + 1], v[j][e + 2], v[j][e + 3]));
+    }
+  }
+  tc::fence_before();
   __syncthreads();
-  float acc[4][4];
-  zero(acc);
-  mma_tile<C, 4, true, true>(acc, s.Ks, row0, s.Vw, col0);  // rows n (A = K^T), cols p
-  store_f32<4>(starts + (size_t(bh) * d.nch + n) * N * P + col0, P, row0, acc);
+  if (warp == 0) tc::tmem_dealloc(tm, 64);
   if (threadIdx.x == 0) deltas[size_t(bh) * d.nch + n] = expf(s.r.p[C - 1]);
 }
 
@@ -402,102 +484,172 @@ __global__ void __launch_bounds__(256) state_kernel(Dims d, float* __restrict__ 
 }
 
 struct OutSmem {
-  bf16 Qs[C * TS];
-  bf16 Ks[C * TS];
-  bf16 Vs[C * TS];
-  bf16 Ms[C * TS];
-  bf16 Ss[N * TS];
-  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  bf16 Qs[C * N];  // blocked tiles (tcgen05 operands)
+  bf16 Ks[C * N];
+  bf16 Vs[C * P];
+  bf16 Ms[C * C];
+  bf16 Ss[N * P];
+  float theta[C * 33];
   float sinv[C * 33];
   float scratch[C];
   Rows r;
+  uint64_t bar;
+  uint32_t tmem;
 };
 
-// y = rd(rd((Q K^T) o W) V + e^p Q rd(S_n)). Eight warps: rows
-// 16 (w % 4) .. +15 and column half w / 4 of every product.
+// y = rd(rd((Q K^T) o W) V + e^p Q rd(S_n)). The three chunk products run on
+// the tensor cores (tcgen05): Q K^T into tensor-memory columns 0..63 and
+// Q rd(S) into 64..127; the masked scores go back to shared memory as a bf16
+// tile and rd(...) V reuses columns 0..63.
 __global__ void __launch_bounds__(GW * 32) output_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ bk, const bf16* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
     const float* __restrict__ phases, const float* __restrict__ starts, bf16* __restrict__ y) {
-  extern __shared__ __align__(16) unsigned char raw[];
+  extern __shared__ __align__(128) unsigned char raw[];
   OutSmem& s = *reinterpret_cast<OutSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5, row0 = 16 * (warp & 3), col0 = 32 * (warp >> 2);
+  const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
+  if (warp == 0) {
+    tc::tmem_alloc(&s.tmem, 128);
+    tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
+  }
+  if (threadIdx.x == 0) tc::mbar_init(&s.bar, 1);
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
   chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk<GW>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
-  load_tile<GW>(d, b, h, t0, x, s.Vs);
-  load_state_bf16<GW>(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
-  __syncthreads();
-  {
-    float acc[4][4];
-    zero(acc);
-    mma_tile<N, 4, false, false>(acc, s.Qs, row0, s.Ks, col0);  // Q K^T: B = K as [s][n]
-    store_bf16<4>(s.Ms, row0, col0, acc, [&](int t, int sidx, float v) {
-      float w = 0.f;
-      if (sidx < t) w = expf(s.r.p[t] - s.r.p[sidx]) * s.r.scl[sidx];
-      else if (sidx == t) w = s.r.gam[t];
-      return v * w;
-    });
+  build_qk<GW, true>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+  load_tile<GW, true>(d, b, h, t0, x, s.Vs);
+  load_state_bf16<GW, true>(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
+  tc_publish();
+  const uint32_t tm = s.tmem;
+  if (threadIdx.x == 0) {
+    tc_product(tm, s.Qs, false, s.Ks, false);       // Q K^T: K = n on both
+    tc_product(tm + 64, s.Qs, false, s.Ss, true);   // Q S: B = S as [n][p]
+    tc::commit(&s.bar);
   }
-  __syncthreads();  // the other column half of each Ms row comes from the partner warp
-  float acc[4][4], inh[4][4];
-  zero(acc);
-  zero(inh);
-  mma_tile<C, 4, false, true>(acc, s.Ms, row0, s.Vs, col0);   // mixed V: B = V as [s][p]
-  mma_tile<N, 4, false, true>(inh, s.Qs, row0, s.Ss, col0);   // Q S: B = S as [n][p]
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  bool ok = tc_wait(&s.bar, 0);
+  if (ok) {
+    float v[2][16];
+    tc::ld16(tmem_lane_base(tm) + col0, v[0]);
+    tc::ld16(tmem_lane_base(tm) + col0 + 16, v[1]);
+    tc::wait_ld();
+    if (lane < 16) {
+      const float pt = s.r.p[row];
 #pragma unroll
-  for (int hf = 0; hf < 2; ++hf) {
-    const int tt = row0 + g + 8 * hf, t = t0 + tt;
-    if (t >= d.T) continue;
-    const float e = s.r.ept[tt];
-    bf16* yrow = y + (size_t(b) * d.T + t) * d.H * P + h * P;
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int col = col0 + nt * 8 + 2 * c;
-      *reinterpret_cast<__nv_bfloat162*>(yrow + col) = __floats2bfloat162_rn(
-          fmaf(e, inh[nt][2 * hf], acc[nt][2 * hf]), fmaf(e, inh[nt][2 * hf + 1], acc[nt][2 * hf + 1]));
+        for (int e = 0; e < 16; e += 2) {
+          float m2[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int sidx = col0 + 16 * j + e + q;
+            float w = 0.f;
+            if (sidx < row) w = expf(pt - s.r.p[sidx]) * s.r.scl[sidx];
+            else if (sidx == row) w = s.r.gam[row];
+            m2[q] = v[j][e + q] * w;
+          }
+          *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ms, row, col0 + 16 * j + e)) = __floats2bfloat162_rn(m2[0], m2[1]);
+        }
     }
   }
+  tc_publish();
+  if (threadIdx.x == 0 && ok) {
+    tc_product(tm, s.Ms, false, s.Vs, true);  // mixed V: A = Ms (K = s), B = V as [s][p]
+    tc::commit(&s.bar);
+  }
+  ok = ok && tc_wait(&s.bar, 1);
+  if (ok) {
+    float acc[2][16], inh[2][16];
+    tc::ld16(tmem_lane_base(tm) + col0, acc[0]);
+    tc::ld16(tmem_lane_base(tm) + col0 + 16, acc[1]);
+    tc::ld16(tmem_lane_base(tm) + 64 + col0, inh[0]);
+    tc::ld16(tmem_lane_base(tm) + 64 + col0 + 16, inh[1]);
+    tc::wait_ld();
+    const int t = t0 + row;
+    if (lane < 16 && t < d.T) {
+      const float e = s.r.ept[row];
+      bf16* yrow = y + (size_t(b) * d.T + t) * d.H * P + h * P + col0;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int q = 0; q < 16; q += 8) {
+          uint4 o;
+          uint32_t* u = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaf(e, inh[j][q + 2 * k], acc[j][q + 2 * k]),
+                                                            fmaf(e, inh[j][q + 2 * k + 1], acc[j][q + 2 * k + 1]));
+            u[k] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(yrow + 16 * j + q) = o;
+        }
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, 128);
 }
 
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
 struct DsSmem {
-  bf16 Qs[C * TS];
-  bf16 Ds[C * TS];
-  float theta[C * 33];  // cos of the pair phase (grads: then the phase gradient)
+  bf16 Qs[C * N];  // blocked tiles (tcgen05 operands)
+  bf16 Ds[C * P];
+  float theta[C * 33];
   float sinv[C * 33];
   float scratch[C];
   Rows r;
+  uint64_t bar;
+  uint32_t tmem;
 };
 
-// D_n = Q^T rd(dY o e^p) into carries[n]. Eight warps: rows 16 (w % 4) ..
-// +15 and column half w / 4 of the product.
+// D_n = Q^T rd(dY o e^p) into carries[n], on the tensor cores (tcgen05).
 __global__ void __launch_bounds__(GW * 32) dstart_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ dy, const float* __restrict__ adt,
     const float* __restrict__ dt, const float* __restrict__ trap_logits, const float* __restrict__ angles,
     const float* __restrict__ qb, const float* __restrict__ phases, float* __restrict__ carries) {
-  extern __shared__ __align__(16) unsigned char raw[];
+  extern __shared__ __align__(128) unsigned char raw[];
   DsSmem& s = *reinterpret_cast<DsSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5, row0 = 16 * (warp & 3), col0 = 32 * (warp >> 2);
+  const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    tc::tmem_alloc(&s.tmem, 64);
+    tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
+  }
+  if (threadIdx.x == 0) tc::mbar_init(&s.bar, 1);
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
   chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
-  build_qk<GW>(d, b, h, t0, cq, nullptr, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
-  load_tile<GW>(d, b, h, t0, dy, s.Ds, s.r.ept);
+  build_qk<GW, true>(d, b, h, t0, cq, nullptr, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
+  load_tile<GW, true>(d, b, h, t0, dy, s.Ds, s.r.ept);
+  tc_publish();
+  const uint32_t tm = s.tmem;
+  if (threadIdx.x == 0) {
+    tc_product(tm, s.Qs, true, s.Ds, true);  // Q^T D: rows n, cols p
+    tc::commit(&s.bar);
+  }
+  if (tc_wait(&s.bar, 0)) {
+    const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
+    float v[2][16];
+    tc::ld16(tmem_lane_base(tm) + col0, v[0]);
+    tc::ld16(tmem_lane_base(tm) + col0 + 16, v[1]);
+    tc::wait_ld();
+    if (lane < 16) {
+      float* dst = carries + (size_t(bh) * d.nch + n) * N * P + row * P + col0;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 16; e += 4) st4(dst + 16 * j + e, make_float4(v[j][e], v[j][e + 1], v[j][e + 2], v[j][e + 3]));
+    }
+  }
+  tc::fence_before();
   __syncthreads();
-  float acc[4][4];
-  zero(acc);
-  mma_tile<C, 4, true, true>(acc, s.Qs, row0, s.Ds, col0);  // Q^T D: rows n, cols p
-  store_f32<4>(carries + (size_t(bh) * d.nch + n) * N * P + col0, P, row0, acc);
+  if (warp == 0) tc::tmem_dealloc(tm, 64);
 }
 
 // Reverse over chunks, in place: carries[n] <- E_n (cotangent of chunk n's end
@@ -578,7 +730,7 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
     const float* __restrict__ phases, const float* __restrict__ starts, const float* __restrict__ carries,
     const bf16* __restrict__ dy, bf16* __restrict__ dx, GradOut o) {
   constexpr int TH = GW * 32;
-  extern __shared__ __align__(16) unsigned char raw[];
+  extern __shared__ __align__(128) unsigned char raw[];
   GradSmem& s = *reinterpret_cast<GradSmem*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
