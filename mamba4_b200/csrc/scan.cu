@@ -18,6 +18,9 @@
 // (fp32 inputs use an exact CUDA-core path with the same fragment ownership).
 #include "common.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 namespace m4 {
 namespace scan {
 
@@ -811,6 +814,28 @@ int backward(const M4ScanDims& s, const void* c, const void* b, const void* x, c
 namespace m4 {
 namespace scan {
 
+// TMA descriptor of a [B][T][H*64] bf16 tensor: box of 64 channels x 64
+// tokens x 1 batch, 128-byte swizzle (the tcgen05 tile layout); tokens past T
+// read as zeros. The driver entry point is looked up once.
+inline bool encode_tokens_map(CUtensorMap* map, const void* base, int B, int T, int HP) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+    PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&fn), cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return fn;
+  }();
+  if (!encode) return false;
+  const cuuint64_t dim[3] = {cuuint64_t(HP), cuuint64_t(T), cuuint64_t(B)};
+  const cuuint64_t stride[2] = {cuuint64_t(HP) * 2, cuuint64_t(T) * HP * 2};
+  const cuuint32_t box[3] = {64, 64, 1}, elem[3] = {1, 1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dim, stride, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // bfloat16 operands run the chunk-parallel kernels of scan_bf16.cuh.
 inline scan2::Dims make_dims2(const M4ScanDims& s) {
   scan2::Dims d;
@@ -841,13 +866,15 @@ inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const
   const size_t psm = size_t(d.nch) * 32 * sizeof(float);
   allow_smem(phase_kernel, psm);
   phase_kernel<<<bh, 256, psm, st>>>(d, dt, angles, phases);
-  allow_smem(update_kernel, sizeof(UpdSmem));
-  update_kernel<<<chunks, GW * 32, sizeof(UpdSmem), st>>>(d, bk, xx, adt, dt, trap, angles, kb, phases, starts,
+  allow_smem(update_kernel, sizeof(UpdSmem) + 1024);
+  update_kernel<<<chunks, GW * 32, sizeof(UpdSmem) + 1024, st>>>(d, bk, xx, adt, dt, trap, angles, kb, phases, starts,
                                                       deltas);
   state_kernel<<<bh * SPARTS, 256, 0, st>>>(d, starts, deltas, fin);
-  allow_smem(output_kernel, sizeof(OutSmem));
-  output_kernel<<<chunks, GW * 32, sizeof(OutSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
-                                                      starts, static_cast<bf16*>(y));
+  alignas(64) CUtensorMap xmap;
+  if (!aligned16(x) || !encode_tokens_map(&xmap, x, d.B, d.T, d.H * P)) return M4_ERR_LAUNCH;
+  allow_smem(output_kernel, sizeof(OutSmem) + 1024);
+  output_kernel<<<chunks, GW * 32, sizeof(OutSmem) + 1024, st>>>(d, xmap, cq, bk, adt, dt, trap, angles, qb, kb,
+                                                               phases, starts, static_cast<bf16*>(y));
   return launch_status();
 }
 
@@ -879,8 +906,8 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
   const bf16* xx = static_cast<const bf16*>(x);
   const bf16* g = static_cast<const bf16*>(dy);
   const int bh = d.B * d.H, chunks = bh * d.nch;
-  allow_smem(dstart_kernel, sizeof(DsSmem));
-  dstart_kernel<<<chunks, GW * 32, sizeof(DsSmem), st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
+  allow_smem(dstart_kernel, sizeof(DsSmem) + 1024);
+  dstart_kernel<<<chunks, GW * 32, sizeof(DsSmem) + 1024, st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
   carry_kernel<<<bh * SPARTS, 256, 0, st>>>(d, carries, deltas, d_final);
   allow_smem(grads_kernel, sizeof(GradSmem));
   grads_kernel<<<chunks, GW * 32, sizeof(GradSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,

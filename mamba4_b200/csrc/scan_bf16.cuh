@@ -82,15 +82,15 @@ M4_DEV void mma_tile(float (&acc)[NT][4], const bf16* A, int row0, const bf16* B
 }
 
 // Element (r, c) of a 64-column bf16 tile: padded rows of TS (mma.sync path)
-// or 8 x 8 core matrices (tcgen05 descriptors, tc::blk).
+// or 128-byte swizzled rows (tcgen05 descriptors and TMA, tc::sw).
 template <bool BLK>
 M4_DEV bf16* at(bf16* T, int r, int c) {
-  if constexpr (BLK) return reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(T) + tc::blk(r, c));
+  if constexpr (BLK) return reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(T) + tc::sw(r, c));
   else return T + r * TS + c;
 }
 
 // D (tensor memory) = A B over K = 64 on the tensor cores (tcgen05, 4 MMAs of
-// K = 16), issued by one thread. A is M x K, B is K x N, each a blocked tile
+// K = 16), issued by one thread. A is M x K, B is K x N, each a swizzled tile
 // read K-major (K along its contiguous columns) or MN-major (K along its rows).
 M4_DEV void tc_product(uint32_t d, const bf16* A, bool a_mn, const bf16* B, bool b_mn) {
   const uint32_t id = tc::idesc_bf16(64, 64, a_mn ? 1 : 0, b_mn ? 1 : 0);
@@ -98,10 +98,16 @@ M4_DEV void tc_product(uint32_t d, const bf16* A, bool a_mn, const bf16* B, bool
   const unsigned char* b = reinterpret_cast<const unsigned char*>(B);
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
-    const uint64_t ad = a_mn ? tc::sdesc(a + 2048 * ks, 1024, 128) : tc::sdesc(a + 256 * ks, 128, 1024);
-    const uint64_t bd = b_mn ? tc::sdesc(b + 2048 * ks, 1024, 128) : tc::sdesc(b + 256 * ks, 128, 1024);
+    const uint64_t ad = a_mn ? tc::sdesc_sw128(a + 2048 * ks, 8192, 1024) : tc::sdesc_sw128(a + 32 * ks, 16, 1024);
+    const uint64_t bd = b_mn ? tc::sdesc_sw128(b + 2048 * ks, 8192, 1024) : tc::sdesc_sw128(b + 32 * ks, 16, 1024);
     tc::mma_bf16(d, ad, bd, id, ks > 0);
   }
+}
+
+// Shared-memory base of a tcgen05 kernel, rounded up to the 1024-byte swizzle
+// atom (launches reserve 1024 extra bytes).
+M4_DEV unsigned char* align1024(unsigned char* p) {
+  return reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
 // Everyone: wait (bounded) for the tensor-core work committed to `bar` in
@@ -412,7 +418,7 @@ __global__ void __launch_bounds__(GW * 32) update_kernel(
     const float* __restrict__ kb, const float* __restrict__ phases, float* __restrict__ starts,
     float* __restrict__ deltas) {
   extern __shared__ __align__(128) unsigned char raw[];
-  UpdSmem& s = *reinterpret_cast<UpdSmem*>(raw);
+  UpdSmem& s = *reinterpret_cast<UpdSmem*>(align1024(raw));
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
@@ -493,21 +499,22 @@ struct OutSmem {
   float sinv[C * 33];
   float scratch[C];
   Rows r;
-  uint64_t bar;
+  uint64_t bar;    // tensor-core commits
+  uint64_t bar_x;  // TMA of the x tile
   uint32_t tmem;
 };
 
 // y = rd(rd((Q K^T) o W) V + e^p Q rd(S_n)). The three chunk products run on
 // the tensor cores (tcgen05): Q K^T into tensor-memory columns 0..63 and
 // Q rd(S) into 64..127; the masked scores go back to shared memory as a bf16
-// tile and rd(...) V reuses columns 0..63.
-__global__ void __launch_bounds__(GW * 32) output_kernel(
-    Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ bk, const bf16* __restrict__ x,
+// tile and rd(...) V reuses columns 0..63. The x tile arrives by TMA.
+__global__ void __launch_bounds__(GW * 32, 1) output_kernel(
+    Dims d, const __grid_constant__ CUtensorMap tmap_x, const bf16* __restrict__ cq, const bf16* __restrict__ bk,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
     const float* __restrict__ phases, const float* __restrict__ starts, bf16* __restrict__ y) {
   extern __shared__ __align__(128) unsigned char raw[];
-  OutSmem& s = *reinterpret_cast<OutSmem*>(raw);
+  OutSmem& s = *reinterpret_cast<OutSmem*>(align1024(raw));
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
@@ -515,13 +522,21 @@ __global__ void __launch_bounds__(GW * 32) output_kernel(
     tc::tmem_alloc(&s.tmem, 128);
     tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
   }
-  if (threadIdx.x == 0) tc::mbar_init(&s.bar, 1);
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&s.bar, 1);
+    tc::mbar_init(&s.bar_x, 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // The x tile by TMA (tokens past T read as zeros): box 64 tokens x 64 channels.
+    tc::mbar_expect_tx(&s.bar_x, C * P * sizeof(bf16));
+    tc::tma_load_3d(s.Vs, &tmap_x, h * P, t0, b, &s.bar_x);
+  }
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
   chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
   build_qk<GW, true>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
-  load_tile<GW, true>(d, b, h, t0, x, s.Vs);
   load_state_bf16<GW, true>(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
   tc_publish();
   const uint32_t tm = s.tmem;
@@ -556,6 +571,12 @@ __global__ void __launch_bounds__(GW * 32) output_kernel(
     }
   }
   tc_publish();
+  if (threadIdx.x == 0 && ok) {
+    if (!tc::mbar_wait(&s.bar_x, 0, tc::WAIT_LIMIT)) {
+      tc::flag_timeout();
+      ok = false;
+    }
+  }
   if (threadIdx.x == 0 && ok) {
     tc_product(tm, s.Ms, false, s.Vs, true);  // mixed V: A = Ms (K = s), B = V as [s][p]
     tc::commit(&s.bar);
@@ -613,7 +634,7 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
     const float* __restrict__ dt, const float* __restrict__ trap_logits, const float* __restrict__ angles,
     const float* __restrict__ qb, const float* __restrict__ phases, float* __restrict__ carries) {
   extern __shared__ __align__(128) unsigned char raw[];
-  DsSmem& s = *reinterpret_cast<DsSmem*>(raw);
+  DsSmem& s = *reinterpret_cast<DsSmem*>(align1024(raw));
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {

@@ -2,14 +2,15 @@
 // descriptors (no swizzle, 8 x 16-byte core matrices), bf16 MMA with fp32
 // accumulation in tensor memory, commit to an mbarrier, tensor-memory loads.
 //
-// Tile layout used with these descriptors: a [R][64] bf16 tile (c
-// contiguous in global memory) is stored as 8 x 8 core matrices of 128 bytes,
-// cores along c adjacent, 8-row groups 1024 bytes apart (tc::blk). As a
-// K-major operand (K = c) the descriptor has LBO 128, SBO 1024 and a K step of
-// 16 advances 256 bytes; as an MN-major operand (MN = c, K = r) it has LBO
-// 1024, SBO 128 and a K step advances 2048 bytes. An M = 64 accumulator puts
-// row m in tensor-memory lane (m % 16) + 32 (m / 16): warp w reads rows
-// 16 (w % 4) .. +15 on its lanes 0..15.
+// Tile layout used with these descriptors: a [64][64] bf16 tile (c
+// contiguous in global memory) is stored as 64 rows of 128 bytes with the
+// 128-byte swizzle (16-byte chunk index XOR row % 8, tc::sw), the layout TMA
+// writes with CU_TENSOR_MAP_SWIZZLE_128B; tiles start on 1024-byte
+// boundaries. As a K-major operand (K = c) the descriptor has SBO 1024 and a
+// K step of 16 advances 32 bytes inside the swizzled rows; as an MN-major
+// operand (MN = c, K = r) it has SBO 1024 and a K step advances 2048 bytes.
+// An M = 64 accumulator puts row m in tensor-memory lane (m % 16) +
+// 32 (m / 16): warp w reads rows 16 (w % 4) .. +15 on its lanes 0..15.
 #pragma once
 #include <cstdint>
 namespace m4 {
@@ -82,6 +83,24 @@ __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.
 __host__ __device__ constexpr uint32_t blk(int r, int c) {
   return uint32_t(((r >> 3) * 8 + (c >> 3)) * 128 + (r & 7) * 16 + (c & 7) * 2);
 }
+// Swizzled (128B) variant of sdesc.
+__device__ __forceinline__ uint64_t sdesc_sw128(const void* smem, uint32_t lbo, uint32_t sbo) {
+  return sdesc(smem, lbo, sbo) | (uint64_t(2) << 61);
+}
+// Byte offset of element (r, c) of a 128-byte-swizzled [64][64] bf16 tile.
+__host__ __device__ constexpr uint32_t sw(int r, int c) {
+  return uint32_t(r * 128 + (((c >> 3) ^ (r & 7)) << 4) + (c & 7) * 2);
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
+}
+// TMA tile load (no multicast) of a 3-D tensor map box into shared memory,
+// completing `bar`'s transaction count.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+               ::"r"(su32(dst)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(su32(bar)) : "memory");
+}
+
 // Device-side error flag: a bounded wait on the tensor cores gave up.
 __device__ int g_timeout;
 __device__ __forceinline__ void flag_timeout() { atomicExch(&g_timeout, 1); }
