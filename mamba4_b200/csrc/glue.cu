@@ -738,22 +738,25 @@ __global__ void __launch_bounds__(256) mem_prep_bwd2(MemMix d, const bf16* __res
 
 // Order head h_t = lam_t h_(t-1) + (1 - lam_t) v_t, lam = sigmoid(logit)
 // (lm/models/mamba4.py:59-95, the same recurrence as its chunked form).
-// Block per (b, head), thread per value channel, 8 tokens loaded ahead.
+// Block per (b, head), thread per value channel; OLA tokens of values and
+// logits are loaded ahead of the serial update (the loop is bound by load
+// latency, not arithmetic).
+constexpr int OLA = 32;
 __global__ void __launch_bounds__(128) order_fwd(MemMix d, const float* __restrict__ values,
                                                  const float* __restrict__ logit, float* __restrict__ ordered) {
   const int h = d.heads, b = blockIdx.x / h, hh = blockIdx.x % h, p = threadIdx.x;
   float state = 0.f;
-  for (int t0 = 0; t0 < d.T; t0 += 8) {
-    float v[8], l[8];
+  for (int t0 = 0; t0 < d.T; t0 += OLA) {
+    float v[OLA], l[OLA];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < OLA; ++j) {
       const int t = t0 + j;
       const size_t r = size_t(b) * d.T + t;
       v[j] = t < d.T ? values[(r * h + hh) * 128 + p] : 0.f;
       l[j] = t < d.T ? logit[r * h + hh] : 0.f;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < OLA; ++j) {
       const int t = t0 + j;
       if (t >= d.T) break;
       state = fmaf(sigmoid(l[j]), state, sigmoid(-l[j]) * v[j]);
@@ -769,13 +772,14 @@ __global__ void __launch_bounds__(128) order_bwd(MemMix d, const float* __restri
                                                  const float* __restrict__ logit, const float* __restrict__ ordered,
                                                  const float* __restrict__ g_ord, float* __restrict__ d_values,
                                                  float* __restrict__ d_logit4) {
+  constexpr int LA = OLA / 2;
   const int h = d.heads, b = blockIdx.x / h, hh = blockIdx.x % h, p = threadIdx.x;
   const int lane = p & 31, warp = p >> 5;
   float G = 0.f, lam_next = 0.f;
-  for (int t1 = d.T; t1 > 0; t1 -= 8) {
-    float v[8], l[8], g[8], hp[8];
+  for (int t1 = d.T; t1 > 0; t1 -= LA) {
+    float v[LA], l[LA], g[LA], hp[LA];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < LA; ++j) {
       const int t = t1 - 1 - j;
       const size_t r = size_t(b) * d.T + t;
       const bool live = t >= 0;
@@ -785,7 +789,7 @@ __global__ void __launch_bounds__(128) order_bwd(MemMix d, const float* __restri
       hp[j] = t >= 1 ? ordered[((r - 1) * h + hh) * 128 + p] : 0.f;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < LA; ++j) {
       const int t = t1 - 1 - j;
       if (t < 0) break;
       const float lam = sigmoid(l[j]), inflow = sigmoid(-l[j]);
