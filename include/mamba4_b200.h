@@ -257,13 +257,15 @@ int m4_memmix_prep_bwd(const M4MemMixDims* dims, const void* rest, const float* 
                        float* d_a_log, void* stream);
 
 /* Order head h_t = lam_t h_(t-1) + (1 - lam_t) v_t, lam = sigmoid(logit)
- * (:59-95), [B,T,h,128]; backward writes d_values and four per-warp partials
- * of d_logit per (b, t, head). */
+ * (:59-95), [B,T,h,128], segment-parallel over 64-token segments; backward
+ * writes d_values and four per-warp partials of d_logit per (b, t, head).
+ * `scratch` holds m4_memmix_order_scratch_floats(dims) floats. */
+size_t m4_memmix_order_scratch_floats(const M4MemMixDims* dims);
 int m4_memmix_order_fwd(const M4MemMixDims* dims, const float* values, const float* logit,
-                        float* ordered, void* stream);
+                        float* ordered, float* scratch, void* stream);
 int m4_memmix_order_bwd(const M4MemMixDims* dims, const float* values, const float* logit,
                         const float* ordered, const float* g_ordered, float* d_values,
-                        float* d_logit4, void* stream);
+                        float* d_logit4, float* scratch, void* stream);
 
 /* Confidence gate, D skip, order mix, read RMSNorm (eps) and SiLU gate
  * (:238-260): y [rows, 128h] bf16, rstd [rows*h] saved for backward. */

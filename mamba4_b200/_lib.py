@@ -72,8 +72,9 @@ SIGNATURES = {
     "m4_memmix_partial_floats": ([ctypes.POINTER(MemMixDims)], _size),
     "m4_memmix_prep_fwd": ([ctypes.POINTER(MemMixDims), _p, _p, _p, ctypes.c_float] + [_p] * 10, _c_int),
     "m4_memmix_prep_bwd": ([ctypes.POINTER(MemMixDims), _p, _p, _p, ctypes.c_float] + [_p] * 18, _c_int),
-    "m4_memmix_order_fwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 4, _c_int),
-    "m4_memmix_order_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 7, _c_int),
+    "m4_memmix_order_scratch_floats": ([ctypes.POINTER(MemMixDims)], _size),
+    "m4_memmix_order_fwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 5, _c_int),
+    "m4_memmix_order_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 8, _c_int),
     "m4_memmix_post_fwd": ([ctypes.POINTER(MemMixDims), ctypes.c_float] + [_p] * 12, _c_int),
     "m4_memmix_post_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 22, _c_int),
     "m4_cross_entropy_fwd": ([_c_int, _c_int, _c_int] + [_p] * 5, _c_int),

@@ -39,7 +39,9 @@ M4_DEV uint4 pack8(const float (&f)[8]) {
 M4_DEV uint4 ld16(const bf16* p) { return *reinterpret_cast<const uint4*>(p); }
 M4_DEV void st16(bf16* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 
-M4_DEV float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+// 1 / (1 + e^-x) with the correctly rounded reciprocal (the same value as the
+// IEEE division, without the division's slow path).
+M4_DEV float sigmoid(float x) { return __frcp_rn(1.f + expf(-x)); }
 // torch.nn.functional.softplus (beta 1, threshold 20) and its derivative.
 M4_DEV float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
 M4_DEV float softplus_grad(float x) { return x > 20.f ? 1.f : sigmoid(x); }
@@ -737,70 +739,157 @@ __global__ void __launch_bounds__(256) mem_prep_bwd2(MemMix d, const bf16* __res
 }
 
 // Order head h_t = lam_t h_(t-1) + (1 - lam_t) v_t, lam = sigmoid(logit)
-// (lm/models/mamba4.py:59-95, the same recurrence as its chunked form).
-// Block per (b, head), thread per value channel; OLA tokens of values and
-// logits are loaded ahead of the serial update (the loop is bound by load
-// latency, not arithmetic).
-constexpr int OLA = 32;
-__global__ void __launch_bounds__(128) order_fwd(MemMix d, const float* __restrict__ values,
-                                                 const float* __restrict__ logit, float* __restrict__ ordered) {
-  const int h = d.heads, b = blockIdx.x / h, hh = blockIdx.x % h, p = threadIdx.x;
-  float state = 0.f;
-  for (int t0 = 0; t0 < d.T; t0 += OLA) {
+// (lm/models/mamba4.py:59-95, which evaluates the same recurrence in 64-token
+// chunks). Segment-parallel: the sequence splits into OSEG-token segments;
+// pass 1 scans each segment from zero (end state, product of lam), pass 2
+// carries the segment starts across segments, pass 3 rescans each segment
+// from its true start. Blocks per (b, head, segment), thread per channel.
+// The backward runs the reverse recurrence G_t = g_t + lam_(t+1) G_(t+1) the
+// same way.
+constexpr int OSEG = 64, OLA = 16;
+
+__host__ __device__ inline int nseg_of(const MemMix& d) { return (d.T + OSEG - 1) / OSEG; }
+
+// Scan tokens [t0, t1) forward from `state`; optionally write h_t.
+M4_DEV float order_run(const MemMix& d, const float* values, const float* logit, int b, int hh, int p, int t0, int t1,
+                       float state, float* prod, float* ordered) {
+  const int h = d.heads;
+  for (int tb = t0; tb < t1; tb += OLA) {
     float v[OLA], l[OLA];
 #pragma unroll
     for (int j = 0; j < OLA; ++j) {
-      const int t = t0 + j;
+      const int t = tb + j;
       const size_t r = size_t(b) * d.T + t;
-      v[j] = t < d.T ? values[(r * h + hh) * 128 + p] : 0.f;
-      l[j] = t < d.T ? logit[r * h + hh] : 0.f;
+      v[j] = t < t1 ? values[(r * h + hh) * 128 + p] : 0.f;
+      l[j] = t < t1 ? logit[r * h + hh] : 0.f;
     }
 #pragma unroll
     for (int j = 0; j < OLA; ++j) {
-      const int t = t0 + j;
-      if (t >= d.T) break;
-      state = fmaf(sigmoid(l[j]), state, sigmoid(-l[j]) * v[j]);
-      ordered[((size_t(b) * d.T + t) * h + hh) * 128 + p] = state;
+      const int t = tb + j;
+      if (t >= t1) break;
+      const float e = expf(-l[j]), lam = __frcp_rn(1.f + e);  // 1 - lam = e lam
+      state = fmaf(lam, state, (e * lam) * v[j]);
+      if (prod) *prod *= lam;
+      if (ordered) ordered[((size_t(b) * d.T + t) * h + hh) * 128 + p] = state;
     }
+  }
+  return state;
+}
+
+__global__ void __launch_bounds__(128) order_seg_fwd(MemMix d, const float* __restrict__ values,
+                                                     const float* __restrict__ logit, float* __restrict__ ends,
+                                                     float* __restrict__ prods) {
+  const int ns = nseg_of(d), seg = blockIdx.x % ns, bh = blockIdx.x / ns, b = bh / d.heads, hh = bh % d.heads;
+  const int p = threadIdx.x, t0 = seg * OSEG, t1 = min(d.T, t0 + OSEG);
+  float prod = 1.f;
+  const float e = order_run(d, values, logit, b, hh, p, t0, t1, 0.f, &prod, nullptr);
+  ends[(size_t(bh) * ns + seg) * 128 + p] = e;
+  if (p == 0) prods[size_t(bh) * ns + seg] = prod;
+}
+
+// Pass 2 (forward): start[s] = start[s-1] prod[s-1] + end[s-1], in place over `ends`.
+__global__ void order_carry_fwd(MemMix d, float* __restrict__ ends, const float* __restrict__ prods) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x, ns = nseg_of(d);
+  if (idx >= d.B * d.heads * 128) return;
+  const int bh = idx / 128, p = idx % 128;
+  float c = 0.f;
+  for (int sg = 0; sg < ns; ++sg) {
+    float* slot = ends + (size_t(bh) * ns + sg) * 128 + p;
+    const float e = *slot;
+    *slot = c;
+    c = fmaf(prods[size_t(bh) * ns + sg], c, e);
   }
 }
 
-// Reverse: G_t = g_t + lam_(t+1) G_(t+1); d v_t = (1 - lam_t) G_t;
-// d logit_t = sum_p G_t (h_(t-1) - v_t) lam_t (1 - lam_t), written as four
-// per-warp partials [B,T,h,4].
-__global__ void __launch_bounds__(128) order_bwd(MemMix d, const float* __restrict__ values,
-                                                 const float* __restrict__ logit, const float* __restrict__ ordered,
-                                                 const float* __restrict__ g_ord, float* __restrict__ d_values,
-                                                 float* __restrict__ d_logit4) {
-  constexpr int LA = OLA / 2;
-  const int h = d.heads, b = blockIdx.x / h, hh = blockIdx.x % h, p = threadIdx.x;
-  const int lane = p & 31, warp = p >> 5;
-  float G = 0.f, lam_next = 0.f;
-  for (int t1 = d.T; t1 > 0; t1 -= LA) {
-    float v[LA], l[LA], g[LA], hp[LA];
+__global__ void __launch_bounds__(128) order_fwd(MemMix d, const float* __restrict__ values,
+                                                 const float* __restrict__ logit, const float* __restrict__ starts,
+                                                 float* __restrict__ ordered) {
+  const int ns = nseg_of(d), seg = blockIdx.x % ns, bh = blockIdx.x / ns, b = bh / d.heads, hh = bh % d.heads;
+  const int p = threadIdx.x, t0 = seg * OSEG, t1 = min(d.T, t0 + OSEG);
+  order_run(d, values, logit, b, hh, p, t0, t1, starts[(size_t(bh) * ns + seg) * 128 + p], nullptr, ordered);
+}
+
+// Reverse scan of tokens [t0, t1) from G_(t1) = G (and lam_(t1) = lam_next).
+// Pass 1 (out == false): returns the local G_(t0) and the product
+// lam_(t0+1) .. lam_(t1) in *prod. Pass 3 (out == true): writes d_values and
+// the four per-warp partials of d logit.
+template <bool OUT>
+M4_DEV float order_back(const MemMix& d, const float* values, const float* logit, const float* ordered,
+                        const float* g_ord, int b, int hh, int p, int t0, int t1, float G, float lam_next,
+                        float* prod, float* d_values, float* d_logit4) {
+  const int h = d.heads, lane = p & 31, warp = p >> 5;
+  for (int tb = t1; tb > t0; tb -= OLA) {
+    float v[OLA], l[OLA], g[OLA], hp[OLA];
 #pragma unroll
-    for (int j = 0; j < LA; ++j) {
-      const int t = t1 - 1 - j;
+    for (int j = 0; j < OLA; ++j) {
+      const int t = tb - 1 - j;
       const size_t r = size_t(b) * d.T + t;
-      const bool live = t >= 0;
-      v[j] = live ? values[(r * h + hh) * 128 + p] : 0.f;
+      const bool live = t >= t0;
       l[j] = live ? logit[r * h + hh] : 0.f;
       g[j] = live ? g_ord[(r * h + hh) * 128 + p] : 0.f;
-      hp[j] = t >= 1 ? ordered[((r - 1) * h + hh) * 128 + p] : 0.f;
+      if (OUT) {
+        v[j] = live ? values[(r * h + hh) * 128 + p] : 0.f;
+        hp[j] = (live && t >= 1) ? ordered[((r - 1) * h + hh) * 128 + p] : 0.f;
+      }
     }
 #pragma unroll
-    for (int j = 0; j < LA; ++j) {
-      const int t = t1 - 1 - j;
-      if (t < 0) break;
-      const float lam = sigmoid(l[j]), inflow = sigmoid(-l[j]);
+    for (int j = 0; j < OLA; ++j) {
+      const int t = tb - 1 - j;
+      if (t < t0) break;
+      const float e = expf(-l[j]), lam = __frcp_rn(1.f + e);
       G = fmaf(lam_next, G, g[j]);
-      const size_t r = size_t(b) * d.T + t;
-      d_values[(r * h + hh) * 128 + p] = inflow * G;
-      const float dl = warp_sum(G * (hp[j] - v[j])) * lam * inflow;
-      if (lane == 0) d_logit4[(r * h + hh) * 4 + warp] = dl;
+      if (!OUT) *prod *= lam_next;
+      if (OUT) {
+        const float inflow = e * lam;
+        const size_t r = size_t(b) * d.T + t;
+        d_values[(r * h + hh) * 128 + p] = inflow * G;
+        const float dl = warp_sum(G * (hp[j] - v[j])) * lam * inflow;
+        if (lane == 0) d_logit4[(r * h + hh) * 4 + warp] = dl;
+      }
       lam_next = lam;
     }
   }
+  return G;
+}
+
+__global__ void __launch_bounds__(128) order_seg_bwd(MemMix d, const float* __restrict__ logit,
+                                                     const float* __restrict__ g_ord, float* __restrict__ gstart,
+                                                     float* __restrict__ prods) {
+  const int ns = nseg_of(d), seg = blockIdx.x % ns, bh = blockIdx.x / ns, b = bh / d.heads, hh = bh % d.heads;
+  const int p = threadIdx.x, t0 = seg * OSEG, t1 = min(d.T, t0 + OSEG);
+  // lam of the first token of the next segment multiplies the carried G.
+  const float lam_next = t1 < d.T ? sigmoid(logit[(size_t(b) * d.T + t1) * d.heads + hh]) : 0.f;
+  float prod = 1.f;
+  const float G = order_back<false>(d, nullptr, logit, nullptr, g_ord, b, hh, p, t0, t1, 0.f, lam_next, &prod,
+                                    nullptr, nullptr);
+  gstart[(size_t(bh) * ns + seg) * 128 + p] = G;
+  if (p == 0) prods[size_t(bh) * ns + seg] = prod;
+}
+
+// Pass 2 (backward, reverse over segments): Gtrue_start[s] = local[s] +
+// prod[s] Gtrue_start[s+1]; stored in place as the carry G_(t1) of segment s.
+__global__ void order_carry_bwd(MemMix d, float* __restrict__ gstart, const float* __restrict__ prods) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x, ns = nseg_of(d);
+  if (idx >= d.B * d.heads * 128) return;
+  const int bh = idx / 128, p = idx % 128;
+  float c = 0.f;  // true G at the start of segment s + 1
+  for (int sg = ns - 1; sg >= 0; --sg) {
+    float* slot = gstart + (size_t(bh) * ns + sg) * 128 + p;
+    const float local = *slot;
+    *slot = c;
+    c = fmaf(prods[size_t(bh) * ns + sg], c, local);
+  }
+}
+
+__global__ void __launch_bounds__(128) order_bwd(MemMix d, const float* __restrict__ values,
+                                                 const float* __restrict__ logit, const float* __restrict__ ordered,
+                                                 const float* __restrict__ g_ord, const float* __restrict__ gcarry,
+                                                 float* __restrict__ d_values, float* __restrict__ d_logit4) {
+  const int ns = nseg_of(d), seg = blockIdx.x % ns, bh = blockIdx.x / ns, b = bh / d.heads, hh = bh % d.heads;
+  const int p = threadIdx.x, t0 = seg * OSEG, t1 = min(d.T, t0 + OSEG);
+  const float lam_next = t1 < d.T ? sigmoid(logit[(size_t(b) * d.T + t1) * d.heads + hh]) : 0.f;
+  order_back<true>(d, values, logit, ordered, g_ord, b, hh, p, t0, t1, gcarry[(size_t(bh) * ns + seg) * 128 + p],
+                   lam_next, nullptr, d_values, d_logit4);
 }
 
 // After the read: r = out c + D v + sigmoid(order_mix) o with the confidence
@@ -1011,25 +1100,44 @@ extern "C" int m4_memmix_prep_bwd(const M4MemMixDims* m, const void* rest, const
   return launch_status();
 }
 
+extern "C" size_t m4_memmix_order_scratch_floats(const M4MemMixDims* m) {
+  if (check_mem(m) != M4_OK) return 0;
+  const size_t segs = size_t(m->batch) * m->heads * ((m->time + OSEG - 1) / OSEG);
+  return segs * 129;
+}
+
 extern "C" int m4_memmix_order_fwd(const M4MemMixDims* m, const float* values, const float* logit, float* ordered,
-                                   void* stream) {
+                                   float* scratch, void* stream) {
   const int st = check_mem(m);
   if (st != M4_OK) return st;
+  if (!scratch) return M4_ERR_NULL;
   if (!all_aligned16(values, logit, ordered)) return M4_ERR_ALIGN;
   const MemMix d = make_memmix(*m);
-  order_fwd<<<d.B * d.heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(d, values, logit, ordered);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int ns = nseg_of(d), blocks = d.B * d.heads * ns, lanes = d.B * d.heads * 128;
+  float* ends = scratch;
+  float* prods = scratch + size_t(blocks) * 128;
+  order_seg_fwd<<<blocks, 128, 0, s>>>(d, values, logit, ends, prods);
+  order_carry_fwd<<<(lanes + 255) / 256, 256, 0, s>>>(d, ends, prods);
+  order_fwd<<<blocks, 128, 0, s>>>(d, values, logit, ends, ordered);
   return launch_status();
 }
 
 extern "C" int m4_memmix_order_bwd(const M4MemMixDims* m, const float* values, const float* logit,
                                    const float* ordered, const float* g_ordered, float* d_values, float* d_logit4,
-                                   void* stream) {
+                                   float* scratch, void* stream) {
   const int st = check_mem(m);
   if (st != M4_OK) return st;
+  if (!scratch) return M4_ERR_NULL;
   if (!all_aligned16(values, logit, ordered, g_ordered, d_values, d_logit4)) return M4_ERR_ALIGN;
   const MemMix d = make_memmix(*m);
-  order_bwd<<<d.B * d.heads, 128, 0, static_cast<cudaStream_t>(stream)>>>(d, values, logit, ordered, g_ordered,
-                                                                            d_values, d_logit4);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int ns = nseg_of(d), blocks = d.B * d.heads * ns, lanes = d.B * d.heads * 128;
+  float* gstart = scratch;
+  float* prods = scratch + size_t(blocks) * 128;
+  order_seg_bwd<<<blocks, 128, 0, s>>>(d, logit, g_ordered, gstart, prods);
+  order_carry_bwd<<<(lanes + 255) / 256, 256, 0, s>>>(d, gstart, prods);
+  order_bwd<<<blocks, 128, 0, s>>>(d, values, logit, ordered, g_ordered, gstart, d_values, d_logit4);
   return launch_status();
 }
 

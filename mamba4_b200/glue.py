@@ -207,7 +207,8 @@ class _OrderScan(torch.autograd.Function):
         batch, time, heads, _ = values.shape
         dims = _memmix_dims(batch, time, heads, 259 * heads + (-259 * heads) % 8, 128 * heads, 1.0)
         ordered = torch.empty_like(values)
-        _lib.check(lib.m4_memmix_order_fwd(ctypes.byref(dims), *map(_lib.ptr, (values, logit, ordered)),
+        scratch = torch.empty(lib.m4_memmix_order_scratch_floats(ctypes.byref(dims)), device=values.device)
+        _lib.check(lib.m4_memmix_order_fwd(ctypes.byref(dims), *map(_lib.ptr, (values, logit, ordered, scratch)),
                                            _stream()), "m4_memmix_order_fwd")
         ctx.save_for_backward(values, logit, ordered)
         return ordered
@@ -220,8 +221,9 @@ class _OrderScan(torch.autograd.Function):
         dims = _memmix_dims(batch, time, heads, 259 * heads + (-259 * heads) % 8, 128 * heads, 1.0)
         d_values = torch.empty_like(values)
         d_logit4 = torch.empty(batch, time, heads, 4, device=values.device)
+        scratch = torch.empty(lib.m4_memmix_order_scratch_floats(ctypes.byref(dims)), device=values.device)
         _lib.check(lib.m4_memmix_order_bwd(ctypes.byref(dims), *map(_lib.ptr, (
-            values, logit, ordered, g.float().contiguous(), d_values, d_logit4)), _stream()),
+            values, logit, ordered, g.float().contiguous(), d_values, d_logit4, scratch)), _stream()),
             "m4_memmix_order_bwd")
         return d_values, d_logit4.sum(-1)
 
