@@ -36,6 +36,9 @@ sys.path.insert(0, str(ROOT))
 MEM_CFG = dict(batch=128, time=1024, heads=8, dim=64, value_dim=64)      # configs[2]
 SCAN_CFG = dict(batch=16, time=1024, heads=16, head_dim=64, state_dim=64)  # configs[1]
 SMALL_MEM_CFG = dict(batch=16, time=1024, heads=8, dim=64, value_dim=64)
+# ncu-sized case of the same kernels (stored factors 302 MB, still above L2).
+PROFILE_MEM_CFG = dict(batch=4, time=1024, heads=8, dim=64, value_dim=64)
+PROFILE_SCAN_CFG = dict(batch=4, time=1024, heads=16, head_dim=64, state_dim=64)
 # Algorithmic work per unit (per token-head for the memory read, per token for
 # the scan at H = 16, P = N = 64, c = 64): the figures of the hot-path survey.
 MEM_FWD_BYTES, MEM_BWD_BYTES = 9356, 10132
@@ -339,9 +342,10 @@ def run_ours(args):
     world, rank, local = setup_dist(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    mem_cfg = SMALL_MEM_CFG if args.workload == "small" else MEM_CFG
+    mem_cfg = {"small": SMALL_MEM_CFG, "profile": PROFILE_MEM_CFG}.get(args.workload, MEM_CFG)
+    scan_cfg = PROFILE_SCAN_CFG if args.workload == "profile" else SCAN_CFG
     m = make_mem(mem_cfg, seed=1000 + rank, device=dev)
-    s = make_scan(SCAN_CFG, seed=2000 + rank, device=dev)
+    s = make_scan(scan_cfg, seed=2000 + rank, device=dev)
 
     def step():
         memread_step(m)
@@ -352,7 +356,7 @@ def run_ours(args):
     total_ms = max_over_ranks(total_ms, world)
     ms_per_step = total_ms / args.steps
     mem_tokens = mem_cfg["batch"] * mem_cfg["time"]
-    scan_tokens = SCAN_CFG["batch"] * SCAN_CFG["time"]
+    scan_tokens = scan_cfg["batch"] * scan_cfg["time"]
     tokens = mem_tokens + scan_tokens
     value = world * tokens / (ms_per_step / 1000.0)
 
@@ -443,16 +447,17 @@ def run_ours(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+bf16",
         "data": "synthetic",
-        "config": {"workload": "configs[1]+configs[2] (hotpath)" if args.workload == "hotpath"
-                   else "small memory read (16x1024x8) + configs[1] scan",
-                   "memread": mem_cfg, "scan": dict(SCAN_CFG, chunk=64, dtype="bf16"),
+        "config": {"workload": {"hotpath": "configs[1]+configs[2] (hotpath)",
+                                "small": "small memory read (16x1024x8) + configs[1] scan",
+                                "profile": "ncu-sized memory read (4x1024x8) + scan (4x1024x16)"}[args.workload],
+                   "memread": mem_cfg, "scan": dict(scan_cfg, chunk=64, dtype="bf16"),
                    "tokens_per_step_per_gpu": tokens, "l2": "inputs larger than L2 (memory-read "
                    "operands 268 MB each, stored factors 9.7 GB)"},
         "roofline": roofline, "components": components, "e2e": e2e,
         "gpu_launches": launches(step, args.steps), "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, desc = cpu_baseline_sample(mem_cfg, SCAN_CFG, host_threads())
+        rate, desc = cpu_baseline_sample(mem_cfg, scan_cfg, host_threads())
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": host_threads(),
                                 "kind": "port", "sample": desc}
     if not args.no_lm and args.workload == "hotpath":
@@ -501,7 +506,7 @@ def measure_lm(args, workload, world, rank, local):
     dev = torch.device("cuda", local)
     name = workload[2:]
     cfg = CONFIGS[name]
-    per_gpu = LM_PER_GPU[workload]
+    per_gpu = args.lm_batch or LM_PER_GPU[workload]
     torch.manual_seed(1234)
     model = Mamba4LM(cfg).to(dev)
     trainer = DataParallelTrainer(model, TrainSettings(), world=world, device_id=local)
@@ -572,7 +577,9 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["hotpath", "small", "lm60m", "lm125m"], default="hotpath")
+    p.add_argument("--workload", choices=["hotpath", "small", "profile", "lm60m", "lm125m"], default="hotpath")
+    p.add_argument("--lm-batch", type=int, default=0,
+                   help="LM workloads: sequences per GPU (default: the configuration's; smaller for ncu captures)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-lm", action="store_true",

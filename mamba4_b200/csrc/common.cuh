@@ -32,6 +32,29 @@ M4_DEV float warp_inclusive_scan(float v, int lane) {
 M4_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 M4_DEV void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
+// Paired fp32 arithmetic (fma.rn.f32x2 / mul.rn.f32x2, sm_100a): two
+// lanes of work per instruction, each rounded like fmaf / __fmul_rn.
+M4_DEV unsigned long long pk2(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+M4_DEV float2 upk2(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+M4_DEV float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
+  return upk2(d);
+}
+M4_DEV float2 fmul2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return upk2(d);
+}
+
 // Streaming (evict-first) 128-bit global store for write-once residuals.
 M4_DEV void st4_stream(float* p, float4 v) { __stcs(reinterpret_cast<float4*>(p), v); }
 

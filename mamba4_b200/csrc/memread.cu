@@ -37,6 +37,9 @@ constexpr int WARPS = 4;       // solve warps per CTA
 #ifndef M4_SOLVE_MINB
 #define M4_SOLVE_MINB 4
 #endif
+#ifndef M4_STATES_MINB
+#define M4_STATES_MINB 2
+#endif
 
 
 struct Sizes {
@@ -89,23 +92,35 @@ M4_DEV void cp_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) 
 // other threads read them.
 M4_DEV void cp_wait() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
+// Each 16-token sub-chunk is applied in one pass: with P_s the inclusive
+// prefix of log lambda inside the sub-chunk,
+//   S_end = e^(P_15) S_start + sum_s beta_s e^(P_15 - P_s) k_s k_s^T
+// (the same recurrence, every weight <= beta_s), so a token costs one paired
+// FMA per two state entries and the decay one paired multiply per sub-chunk.
+// Thread (rq, cq) = (tid / 16, tid % 16) owns the 4x4 block rows 4rq..4rq+3,
+// columns 4cq..4cq+3 of S and of each 64-row block of C, as column pairs
+// (64-bit registers). A warp's shared reads per token are sixteen distinct
+// column vectors and two row vectors (conflict-free; a layout with four
+// threads per row made every 128-bit read a 5-way bank conflict).
 template <int P>
-__global__ void __launch_bounds__(256) states_kernel(
+__global__ void __launch_bounds__(256, M4_STATES_MINB) states_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ values,
     const float* __restrict__ beta, const float* __restrict__ log_decay,
     const float* __restrict__ init_s, const float* __restrict__ init_c,
     float* __restrict__ s_start, float* __restrict__ c_start,
     float* __restrict__ s_final, float* __restrict__ c_final) {
+  using u64 = unsigned long long;
   constexpr int CR = P / 64;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int tid = threadIdx.x;
   const int Tp = (T + CH - 1) / CH * CH, nsub = Tp / SUB, nch = Tp / CH;
-  const int i = tid >> 2, j0 = (tid & 3) * 16;
+  const int r0 = 4 * (tid >> 4), c0 = 4 * (tid & 15);
   // Two sub-chunk buffers: the next sub-chunk's keys, values, beta and
   // log_decay stream in (cp.async) while the current one is applied.
   __shared__ __align__(16) float ks[2][SUB][KD];
   __shared__ __align__(16) float vs[2][SUB][P];
   __shared__ float bl[2][SUB], ll[2][SUB];
+  __shared__ float wsub[SUB], dsub;
   auto prefetch = [&](int buf, int sub) {
     const int t0 = sub * SUB;
 #pragma unroll
@@ -129,58 +144,97 @@ __global__ void __launch_bounds__(256) states_kernel(
     }
     cp_commit();
   };
-  float s[16], c[CR][16];
+  // s[a][q]: S[r0 + a][c0 + 2q .. c0 + 2q + 1]; c[r][a][q]: C[r0 + a + 64 r][...].
+  u64 s[4][2], c[CR][4][2];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    s[e] = init_s ? init_s[(size_t(bh) * KD + i) * KD + j0 + e] : 0.f;
+  for (int a = 0; a < 4; ++a) {
+    ulonglong2 v = make_ulonglong2(0ull, 0ull);
+    if (init_s) v = *reinterpret_cast<const ulonglong2*>(init_s + (size_t(bh) * KD + r0 + a) * KD + c0);
+    s[a][0] = v.x; s[a][1] = v.y;
 #pragma unroll
-    for (int r = 0; r < CR; ++r)
-      c[r][e] = init_c ? init_c[(size_t(bh) * P + i + 64 * r) * KD + j0 + e] : 0.f;
+    for (int r = 0; r < CR; ++r) {
+      ulonglong2 w = make_ulonglong2(0ull, 0ull);
+      if (init_c) w = *reinterpret_cast<const ulonglong2*>(init_c + (size_t(bh) * P + r0 + a + 64 * r) * KD + c0);
+      c[r][a][0] = w.x; c[r][a][1] = w.y;
+    }
   }
   prefetch(0, 0);
   for (int sub = 0; sub < nsub; ++sub) {
     const int buf = sub & 1;
     if (sub + 1 < nsub) prefetch(buf ^ 1, sub + 1);
-    float* sd = s_start + ((size_t(bh) * nsub + sub) * KD + i) * KD + j0;
+    float* sd = s_start + (size_t(bh) * nsub + sub) * KD * KD + c0;
 #pragma unroll
-    for (int e = 0; e < 16; e += 4) st4(sd + e, make_float4(s[e], s[e + 1], s[e + 2], s[e + 3]));
+    for (int a = 0; a < 4; ++a)
+      *reinterpret_cast<ulonglong2*>(sd + (r0 + a) * KD) = make_ulonglong2(s[a][0], s[a][1]);
     if ((sub & 3) == 0) {
+      float* cd = c_start + (size_t(bh) * nch + (sub >> 2)) * P * KD + c0;
 #pragma unroll
-      for (int r = 0; r < CR; ++r) {
-        float* cd = c_start + ((size_t(bh) * nch + (sub >> 2)) * P + i + 64 * r) * KD + j0;
+      for (int r = 0; r < CR; ++r)
 #pragma unroll
-        for (int e = 0; e < 16; e += 4)
-          st4(cd + e, make_float4(c[r][e], c[r][e + 1], c[r][e + 2], c[r][e + 3]));
-      }
+        for (int a = 0; a < 4; ++a)
+          *reinterpret_cast<ulonglong2*>(cd + (r0 + a + 64 * r) * KD) = make_ulonglong2(c[r][a][0], c[r][a][1]);
     }
     if (sub + 1 < nsub) cp_wait_group<1>(); else cp_wait_group<0>();
     __syncthreads();
-#pragma unroll 2
+    if (tid < 32) {
+      const float inc = warp_inclusive_scan(tid < SUB ? ll[buf][tid] : 0.f, tid);
+      const float pend = __shfl_sync(0xffffffffu, inc, SUB - 1);
+      if (tid < SUB) wsub[tid] = bl[buf][tid] * expf(pend - inc);
+      if (tid == 0) dsub = expf(pend);
+    }
+    __syncthreads();
+    {
+      u64 dd;
+      asm("mov.b64 %0, {%1,%1};" : "=l"(dd) : "f"(dsub));
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(s[a][q]) : "l"(dd));
+#pragma unroll
+          for (int r = 0; r < CR; ++r) asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(c[r][a][q]) : "l"(dd));
+        }
+    }
+#pragma unroll 4
     for (int tt = 0; tt < SUB; ++tt) {
-      const float lam = expf(ll[buf][tt]), bet = bl[buf][tt];
-      float kj[16];
-#pragma unroll
-      for (int e = 0; e < 16; e += 4) {
-        float4 v4 = ld4(&ks[buf][tt][j0 + e]);
-        kj[e] = v4.x; kj[e + 1] = v4.y; kj[e + 2] = v4.z; kj[e + 3] = v4.w;
+      u64 ww, wk[2];
+      asm("mov.b64 %0, {%1,%1};" : "=l"(ww) : "f"(wsub[tt]));
+      {
+        const ulonglong2 kc = *reinterpret_cast<const ulonglong2*>(&ks[buf][tt][c0]);
+        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(wk[0]) : "l"(kc.x), "l"(ww));
+        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(wk[1]) : "l"(kc.y), "l"(ww));
       }
-      const float bk = bet * ks[buf][tt][i];
+      const float4 kr = ld4(&ks[buf][tt][r0]);
+      const float krv[4] = {kr.x, kr.y, kr.z, kr.w};
 #pragma unroll
-      for (int e = 0; e < 16; ++e) s[e] = fmaf(bk, kj[e], lam * s[e]);
+      for (int a = 0; a < 4; ++a) {
+        u64 d;
+        asm("mov.b64 %0, {%1,%1};" : "=l"(d) : "f"(krv[a]));
+        asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s[a][0]) : "l"(d), "l"(wk[0]));
+        asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s[a][1]) : "l"(d), "l"(wk[1]));
+      }
 #pragma unroll
       for (int r = 0; r < CR; ++r) {
-        const float bv = bet * vs[buf][tt][i + 64 * r];
+        const float4 vr = ld4(&vs[buf][tt][r0 + 64 * r]);
+        const float vrv[4] = {vr.x, vr.y, vr.z, vr.w};
 #pragma unroll
-        for (int e = 0; e < 16; ++e) c[r][e] = fmaf(bv, kj[e], lam * c[r][e]);
+        for (int a = 0; a < 4; ++a) {
+          u64 d;
+          asm("mov.b64 %0, {%1,%1};" : "=l"(d) : "f"(vrv[a]));
+          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c[r][a][0]) : "l"(d), "l"(wk[0]));
+          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c[r][a][1]) : "l"(d), "l"(wk[1]));
+        }
       }
     }
     __syncthreads();  // this buffer is refilled two sub-chunks later
   }
 #pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    s_final[(size_t(bh) * KD + i) * KD + j0 + e] = s[e];
+  for (int a = 0; a < 4; ++a) {
+    *reinterpret_cast<ulonglong2*>(s_final + (size_t(bh) * KD + r0 + a) * KD + c0) = make_ulonglong2(s[a][0], s[a][1]);
 #pragma unroll
-    for (int r = 0; r < CR; ++r) c_final[(size_t(bh) * P + i + 64 * r) * KD + j0 + e] = c[r][e];
+    for (int r = 0; r < CR; ++r)
+      *reinterpret_cast<ulonglong2*>(c_final + (size_t(bh) * P + r0 + a + 64 * r) * KD + c0) =
+          make_ulonglong2(c[r][a][0], c[r][a][1]);
   }
 }
 
