@@ -97,6 +97,22 @@ int m4_memread_bwd(const M4MemDims* dims, const float* keys, const float* values
                    float* d_floor, float* d_init_evidence, float* d_init_cross,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* One-token read against a carried state. Replaces selective_decode
+ * (lm/kernels/mamba4.py:341-355): evidence' = lam evidence + beta k k^T,
+ * cross' = lam cross + beta v k^T, y = (evidence' + diag(floor))^-1 query,
+ * output = cross' y, variance = query . y, lam = exp(log_decay).
+ * dims: batch, heads, key_dim 64, value_dim 64 or 128 (time is ignored).
+ *   evidence [B,H,D,D], cross [B,H,P,D]; key, query [B,H,D] (16-byte aligned);
+ *   value [B,H,P]; beta, log_decay [B,H]; floor [H,D].
+ * Outputs: output [B,H,P], variance [B,H], evidence_out [B,H,D,D],
+ *   cross_out [B,H,P,D]; evidence_out / cross_out may be evidence / cross
+ *   (updated in place). */
+int m4_memread_decode(const M4MemDims* dims, const float* evidence, const float* cross,
+                      const float* key, const float* value, const float* query,
+                      const float* beta, const float* log_decay, const float* floor,
+                      float* output, float* variance, float* evidence_out, float* cross_out,
+                      void* stream);
+
 /* Scan problem size (projection layout of mamba3_fused). */
 typedef struct {
   int batch;        /* B */
@@ -142,6 +158,30 @@ int m4_scan_bwd(const M4ScanDims* dims, const void* c, const void* b, const void
                 float* d_dt, float* d_trap_logits, float* d_angles,
                 float* d_q_bias, float* d_k_bias, void* workspace,
                 size_t workspace_bytes, void* stream);
+
+/* One-token scan step against a carried cache. Replaces the scan core of
+ * _Mamba3StepMixer (lm/models/mamba4.py:412-481): phase' = phase + rate dt;
+ * Q, K = rotate(c + q_bias, phase'), rotate(b + k_bias, phase') (rounded to
+ * the model dtype after the bias and after the rotation, as the reference);
+ * state' = e^(adt) (state + dt (1 - sigmoid(trap)) k_prev v_prev^T)
+ *          + dt sigmoid(trap) K x^T;  y = Q^T state'.
+ * dims: batch, heads, head_dim 64, state_dim 64, angle_count, bf16, per_head
+ * (time and chunk are ignored).
+ *   cache: state [B,H,N,P] (16-byte aligned), prev_keys [B,H,N],
+ *   prev_values [B,H,P], phase [B,H,A], all float32;
+ *   c, b [B,N] (per_head: [B,H,N]) and x [B,H*P] in the model dtype;
+ *   adt, dt, trap_logits [B,H]; angles [B,A] (per_head [B,H,A]) rates;
+ *   q_bias, k_bias [H,N] or NULL.
+ * Outputs: y [B,H*P] (model dtype) and the new cache (K, x and phase'); the
+ * output cache pointers may equal the input ones (updated in place).
+ * Stepping a zero cache through a sequence reproduces m4_scan_fwd's y and
+ * final state. */
+int m4_scan_step(const M4ScanDims* dims, const float* state, const float* prev_keys,
+                 const float* prev_values, const float* phase, const void* c, const void* b,
+                 const void* x, const float* adt, const float* dt, const float* trap_logits,
+                 const float* angles, const float* q_bias, const float* k_bias, void* y,
+                 float* state_out, float* prev_keys_out, float* prev_values_out,
+                 float* phase_out, void* stream);
 
 /* Backward scan that allocates nothing (no counterpart in the reference).
  * For callers that may not allocate device memory while the operator runs:

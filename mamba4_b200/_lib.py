@@ -54,6 +54,7 @@ SIGNATURES = {
     "m4_memread_fwd": ([ctypes.POINTER(MemDims)] + [_p] * 12 + [_p, _size, _p], _c_int),
     "m4_memread_bwd": ([ctypes.POINTER(MemDims)] + [_p] * 9 + [_size] + [_p] * 12
                        + [_p, _size, _p], _c_int),
+    "m4_memread_decode": ([ctypes.POINTER(MemDims)] + [_p] * 12 + [_p], _c_int),
     "m4_scan_residual_bytes": ([ctypes.POINTER(ScanDims)], _size),
     "m4_scan_workspace_bytes": ([ctypes.POINTER(ScanDims)], _size),
     "m4_scan_fwd": ([ctypes.POINTER(ScanDims)] + [_p] * 11 + [_p, _size, _p], _c_int),
@@ -61,6 +62,7 @@ SIGNATURES = {
                     + [_p, _size, _p], _c_int),
     "m4_scan_bwd_noalloc": ([ctypes.POINTER(ScanDims)] + [_p] * 10 + [_size] + [_p] * 11 + [_p],
                             _c_int),
+    "m4_scan_step": ([ctypes.POINTER(ScanDims)] + [_p] * 18 + [_p], _c_int),
     "m4_mixer_partial_rows": ([ctypes.POINTER(MixerDims)], _size),
     "m4_mixer_prep_fwd": ([ctypes.POINTER(MixerDims)] + [_p] * 12, _c_int),
     "m4_mixer_post_fwd": ([ctypes.POINTER(MixerDims)] + [_p] * 5, _c_int),

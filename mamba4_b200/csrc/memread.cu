@@ -649,6 +649,149 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// memread_decode: one token per (batch, head) against a carried state
+// (selective_decode, lm/kernels/mamba4.py:341-355). One warp per (b, h):
+//   E' = lam E + beta k k^T, C' = lam C + beta v k^T,
+//   y = (E' + diag(floor))^-1 q, output = C' y, variance = q . y,
+// with the solve kernel's lane-tiled factorization (bordered query row) and
+// blocked back-substitution. E' and C' may overwrite E and C: the warp reads
+// all of E before writing E', and each row of C before writing that row.
+// ---------------------------------------------------------------------------
+template <int P>
+__global__ void __launch_bounds__(32 * WARPS) decode_kernel(
+    int B, int H, const float* evidence, const float* cross,
+    const float* __restrict__ key, const float* __restrict__ value, const float* __restrict__ query,
+    const float* __restrict__ beta, const float* __restrict__ log_decay,
+    const float* __restrict__ floor_, float* __restrict__ out, float* __restrict__ variance,
+    float* evidence_out, float* cross_out) {  // may alias evidence / cross
+  extern __shared__ __align__(16) unsigned char decode_raw[];
+  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(decode_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int a = lane >> 3, b = lane & 7;
+  const int bh = blockIdx.x * WARPS + warp;
+  if (bh >= B * H) return;
+  SolveSmem& sm = smem_all[warp];
+  const int h = bh % H;
+  const float* src = evidence + size_t(bh) * KD * KD;
+  float2 A[NPAIR];
+#pragma unroll
+  for (int q = 0; q < NPAIR; ++q) {
+    const int p = pair_p(q), n = pair_n(q);
+    A[q] = make_float2(src[(a + 8 * p) * KD + b + 8 * n], src[(a + 4 + 8 * p) * KD + b + 8 * n]);
+  }
+  if (a == 0) {
+#pragma unroll
+    for (int n = 0; n < 8; ++n) sm.flC[b * KS + n] = floor_[h * KD + b + 8 * n];
+  }
+  {
+    const int l = lane & 15;
+    const float4 v4 = ld4((lane < 16 ? key : query) + size_t(bh) * KD + 4 * l);
+    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * l + e;
+      if (lane < 16) {
+        reinterpret_cast<float*>(sm.u.f.kP)[((i & 3) * PS + (i >> 3)) * 2 + ((i >> 2) & 1)] = vv[e];
+        sm.u.f.kC[(i & 7) * KS + (i >> 3)] = vv[e];
+        sm.w[i] = vv[e];  // key, kept for the cross update
+      } else {
+        sm.u.f.qC[(i & 7) * KS + (i >> 3)] = vv[e];
+      }
+    }
+  }
+  const float bet = beta[bh];
+  const float lam = expf(log_decay[bh]);
+  __syncwarp();
+  float wr[8];
+  {
+    float2 kr[8];
+    float kc[8];
+#pragma unroll
+    for (int p = 0; p < 8; p += 2) {
+      const float4 v = *reinterpret_cast<const float4*>(&sm.u.f.kP[a * PS + p]);
+      kr[p] = make_float2(bet * v.x, bet * v.y);
+      kr[p + 1] = make_float2(bet * v.z, bet * v.w);
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) kc[n] = sm.u.f.kC[b * KS + n];
+#pragma unroll
+    for (int q = 0; q < NPAIR; ++q) A[q] = fma2(kr[pair_p(q)], kc[pair_n(q)], make_float2(lam * A[q].x, lam * A[q].y));
+  }
+  // E' to global (symmetric: off-diagonal blocks both ways).
+  {
+    float* dst = evidence_out + size_t(bh) * KD * KD;
+#pragma unroll
+    for (int q = 0; q < NPAIR; ++q) {
+      const int p = pair_p(q), n = pair_n(q);
+      const int r0 = a + 8 * p, r1 = a + 4 + 8 * p, c = b + 8 * n;
+      dst[r0 * KD + c] = A[q].x;
+      dst[r1 * KD + c] = A[q].y;
+      if (p != n) {
+        dst[c * KD + r0] = A[q].x;
+        dst[c * KD + r1] = A[q].y;
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+    const float f = sm.flC[b * KS + n];
+    A[pair_of(n, n)].x += (b == a) ? f : 0.f;
+    A[pair_of(n, n)].y += (b == a + 4) ? f : 0.f;
+    wr[n] = a == 0 ? sm.u.f.qC[b * KS + n] : 0.f;
+  }
+  float rc[8];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) rc[n] = 0.f;
+  factor_all<0>(A, wr, rc, sm, a, b);
+  float vpart = 0.f, kkeep[2];
+  kkeep[0] = sm.w[lane];
+  kkeep[1] = sm.w[lane + 32];
+  __syncwarp();
+  if (a == 0) {
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float wv = wr[n] * rc[n];
+      sm.w[b + 8 * n] = wv;
+      vpart = fmaf(wv, wv, vpart);
+    }
+  }
+  const float var = warp_sum(vpart);
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+#pragma unroll
+    for (int p = n; p < 8; ++p) {
+      A[pair_of(p, n)].x *= rc[n];
+      A[pair_of(p, n)].y *= rc[n];
+    }
+    float2& d = A[pair_of(n, n)];
+    d.x = (b == a) ? rc[n] : (a < b ? 0.f : d.x);
+    d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
+  }
+  invert_blocks(A, sm, lane, a, b);
+  back_substitute(A, sm, sm.w, sm.y, a, b);
+  __syncwarp();
+  if (lane == 0) variance[bh] = var;
+  // C' = lam C + beta v k^T row by row (lanes over key coordinates 2l, 2l+1
+  // ... as lane, lane + 32), output_p = C'[p] . y.
+  const float y0 = sm.y[lane], y1 = sm.y[lane + 32];
+  const float bk0 = bet * kkeep[0], bk1 = bet * kkeep[1];
+  const float* csrc = cross + size_t(bh) * P * KD;
+  float* cdst = cross_out + size_t(bh) * P * KD;
+  const float* vrow = value + size_t(bh) * P;
+  float* orow = out + size_t(bh) * P;
+#pragma unroll 4
+  for (int p = 0; p < P; ++p) {
+    const float vp = vrow[p];
+    const float c0 = fmaf(bk0, vp, lam * csrc[p * KD + lane]);
+    const float c1 = fmaf(bk1, vp, lam * csrc[p * KD + lane + 32]);
+    const float o = warp_sum(fmaf(c0, y0, c1 * y1));
+    cdst[p * KD + lane] = c0;
+    cdst[p * KD + lane + 32] = c1;
+    if (lane == 0) orow[p] = o;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Chunk-product kernels: one CTA of 8 warps per (batch, 64-token chunk, head)
 // (carry: one per (batch, head)). The products run on tensor cores as m16n8k8
 // TF32 MMAs on a two-term split of every fp32 operand (hi = tf32(x),
@@ -1370,4 +1513,33 @@ extern "C" int m4_memread_bwd(const M4MemDims* d, const float* keys, const float
                              dk, dv, dq, dbeta, dlog, dfloor, d_init_s, d_init_c, w, s);
   return mem::backward<128>(*d, keys, values, queries, beta, log_decay, r, d_out, d_var, d_sfin, d_cfin,
                             dk, dv, dq, dbeta, dlog, dfloor, d_init_s, d_init_c, w, s);
+}
+
+extern "C" int m4_memread_decode(const M4MemDims* d, const float* evidence, const float* cross,
+                                 const float* key, const float* value, const float* query,
+                                 const float* beta, const float* log_decay, const float* floor_,
+                                 float* output, float* variance, float* evidence_out,
+                                 float* cross_out, void* stream) {
+  int st = mem::check(d);
+  if (st) return st;
+  if (!evidence || !cross || !key || !value || !query || !beta || !log_decay || !floor_ || !output ||
+      !variance || !evidence_out || !cross_out)
+    return M4_ERR_NULL;
+  if (!all_aligned16(key, query)) return M4_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int bh = d->batch * d->heads;
+  const int smem = int(sizeof(mem::SolveSmem) * mem::WARPS);
+  const int grid = (bh + mem::WARPS - 1) / mem::WARPS;
+  if (d->value_dim == 64) {
+    cudaFuncSetAttribute(mem::decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    mem::decode_kernel<64><<<grid, 32 * mem::WARPS, smem, s>>>(d->batch, d->heads, evidence, cross, key, value,
+                                                               query, beta, log_decay, floor_, output, variance,
+                                                               evidence_out, cross_out);
+  } else {
+    cudaFuncSetAttribute(mem::decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    mem::decode_kernel<128><<<grid, 32 * mem::WARPS, smem, s>>>(d->batch, d->heads, evidence, cross, key, value,
+                                                                query, beta, log_decay, floor_, output, variance,
+                                                                evidence_out, cross_out);
+  }
+  return launch_status();
 }

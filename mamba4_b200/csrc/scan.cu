@@ -986,6 +986,144 @@ extern "C" int m4_scan_bwd(const M4ScanDims* s, const void* c, const void* b, co
 }
 
 // ---------------------------------------------------------------------------
+// One-token scan step against a carried cache: the scan core of the
+// reference's _Mamba3StepMixer (lm/models/mamba4.py:412-481).
+//   phase' = phase + rate dt; Q, K = rotate(round(c + q_bias), phase'),
+//   rotate(round(b + k_bias), phase') rounded to the model dtype;
+//   S' = e^(adt) (S + dt (1 - trap) k_prev v_prev^T) + dt trap K x^T;
+//   y = Q^T S' (model dtype); cache' = (S', K, x, phase').
+// One CTA of 256 threads per (batch, head); thread (n, p0) = (tid / 4,
+// 16 (tid % 4)) updates S'[n][p0 .. p0+15]. Outputs may alias the cache
+// inputs: every cache value is read before any is written.
+// ---------------------------------------------------------------------------
+namespace m4 {
+namespace scan {
+
+template <typename T>
+__global__ void __launch_bounds__(256) step_kernel(
+    int H, int A, int per_head, const float* state, const float* prev_k, const float* prev_v,
+    const float* phase, const T* __restrict__ c, const T* __restrict__ bk, const T* __restrict__ x,
+    const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
+    const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
+    T* __restrict__ y, float* state_out, float* prev_k_out, float* prev_v_out, float* phase_out) {
+  const int bh = blockIdx.x, bb = bh / H, h = bh % H, tid = threadIdx.x;
+  __shared__ float qr[NS], kr[NS], xv[HP], pk[NS], pv[HP], ph[NS / 2];
+  __shared__ float red[8][HP];
+  const float dtv = dt[bh];
+  const float trap = 1.f / (1.f + expf(-trap_logits[bh]));
+  const float alpha = expf(adt[bh]);
+  const int n = tid >> 2, p0 = (tid & 3) * 16;
+  float sv[16];
+  {
+    const float* srow = state + (size_t(bh) * NS + n) * HP + p0;
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      const float4 v = ld4(srow + e);
+      sv[e] = v.x; sv[e + 1] = v.y; sv[e + 2] = v.z; sv[e + 3] = v.w;
+    }
+  }
+  float phv = 0.f;
+  if (tid < NS / 2) {
+    if (tid < A) {
+      const float rate = angles[per_head ? size_t(bh) * A + tid : size_t(bb) * A + tid];
+      phv = phase[size_t(bh) * A + tid] + rate * dtv;
+    }
+    ph[tid] = phv;
+  }
+  if (tid < NS) pk[tid] = prev_k[size_t(bh) * NS + tid];
+  if (tid < HP) pv[tid] = prev_v[size_t(bh) * HP + tid];
+  __syncthreads();  // every cache value is read: outputs may now overwrite them
+  if (tid < NS / 2 && tid < A) phase_out[size_t(bh) * A + tid] = phv;
+  if (tid < NS / 2) {
+    const int i = tid, n0 = 2 * i, n1 = 2 * i + 1;
+    const size_t base = per_head ? size_t(bh) * NS : size_t(bb) * NS;
+    const float q0 = round_to<T>(to_f(c[base + n0]) + (qb ? qb[h * NS + n0] : 0.f));
+    const float q1 = round_to<T>(to_f(c[base + n1]) + (qb ? qb[h * NS + n1] : 0.f));
+    const float k0 = round_to<T>(to_f(bk[base + n0]) + (kb ? kb[h * NS + n0] : 0.f));
+    const float k1 = round_to<T>(to_f(bk[base + n1]) + (kb ? kb[h * NS + n1] : 0.f));
+    float cs = 1.f, sn = 0.f;
+    if (i < A) sincosf(ph[i], &sn, &cs);
+    qr[n0] = round_to<T>(q0 * cs - q1 * sn);
+    qr[n1] = round_to<T>(q1 * cs + q0 * sn);
+    kr[n0] = round_to<T>(k0 * cs - k1 * sn);
+    kr[n1] = round_to<T>(k1 * cs + k0 * sn);
+  }
+  if (tid < HP) xv[tid] = to_f(x[size_t(bh) * HP + tid]);
+  __syncthreads();
+  if (tid < NS) prev_k_out[size_t(bh) * NS + tid] = kr[tid];
+  if (tid < HP) prev_v_out[size_t(bh) * HP + tid] = xv[tid];
+  const float wp = dtv * (1.f - trap) * pk[n], wc = dtv * trap * kr[n], q = qr[n];
+  float part[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    sv[e] = fmaf(wc, xv[p0 + e], alpha * fmaf(wp, pv[p0 + e], sv[e]));
+    part[e] = q * sv[e];
+  }
+  {
+    float* dst = state_out + (size_t(bh) * NS + n) * HP + p0;
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) st4(dst + e, make_float4(sv[e], sv[e + 1], sv[e + 2], sv[e + 3]));
+  }
+  // y[p] = sum_n Q[n] S'[n][p]: over the warp's eight n (lanes 4 apart), then
+  // over the eight warps in a fixed order.
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    float v = part[e];
+    v += __shfl_xor_sync(0xffffffffu, v, 4);
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    part[e] = v;
+  }
+  const int warp = tid >> 5, lane = tid & 31;
+  if (lane < 4) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) red[warp][p0 + e] = part[e];
+  }
+  __syncthreads();
+  if (tid < HP) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) acc += red[w][tid];
+    y[size_t(bh) * HP + tid] = from_f<T>(acc);
+  }
+}
+
+}  // namespace scan
+}  // namespace m4
+
+extern "C" int m4_scan_step(const M4ScanDims* s, const float* state, const float* prev_keys,
+                            const float* prev_values, const float* phase, const void* c, const void* b,
+                            const void* x, const float* adt, const float* dt, const float* trap,
+                            const float* angles, const float* qb, const float* kb, void* y,
+                            float* state_out, float* prev_keys_out, float* prev_values_out,
+                            float* phase_out, void* stream) {
+  if (!s) return M4_ERR_NULL;
+  if (s->batch <= 0 || s->heads <= 0 || s->head_dim <= 0 || s->state_dim <= 0 || s->angle_count < 0)
+    return M4_ERR_DIMS;
+  if (s->head_dim != scan::HP || s->state_dim != scan::NS || s->angle_count > scan::NS / 2)
+    return M4_ERR_UNSUPPORTED;
+  if (!state || !prev_keys || !prev_values || !c || !b || !x || !adt || !dt || !trap || !y || !state_out ||
+      !prev_keys_out || !prev_values_out)
+    return M4_ERR_NULL;
+  if (s->angle_count > 0 && (!angles || !phase || !phase_out)) return M4_ERR_NULL;
+  if (!all_aligned16(state, state_out)) return M4_ERR_ALIGN;
+  cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  const int grid = s->batch * s->heads;
+  if (s->bf16)
+    scan::step_kernel<__nv_bfloat16><<<grid, 256, 0, strm>>>(
+        s->heads, s->angle_count, s->per_head, state, prev_keys, prev_values, phase,
+        static_cast<const __nv_bfloat16*>(c), static_cast<const __nv_bfloat16*>(b),
+        static_cast<const __nv_bfloat16*>(x), adt, dt, trap, angles, qb, kb, static_cast<__nv_bfloat16*>(y),
+        state_out, prev_keys_out, prev_values_out, phase_out);
+  else
+    scan::step_kernel<float><<<grid, 256, 0, strm>>>(
+        s->heads, s->angle_count, s->per_head, state, prev_keys, prev_values, phase,
+        static_cast<const float*>(c), static_cast<const float*>(b), static_cast<const float*>(x), adt, dt, trap,
+        angles, qb, kb, static_cast<float*>(y), state_out, prev_keys_out, prev_values_out, phase_out);
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------
 // Backward scan for callers that cannot allocate device memory.
 //
 // Some callers may not allocate at all while they run this operator: an XLA

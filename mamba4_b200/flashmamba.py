@@ -11,6 +11,7 @@ their derivatives are folded into those kernels. No CPU path exists.
 from __future__ import annotations
 
 import ctypes
+from typing import NamedTuple
 
 import torch
 import torch.nn.functional as F
@@ -176,3 +177,73 @@ def angle_rates(angles, state_dim):
     explicit form for callers that need it."""
     rates = torch.repeat_interleave(angles.float(), 2, dim=-1)
     return F.pad(rates, (0, state_dim - rates.shape[-1]))
+
+
+class Mamba3StepCache(NamedTuple):
+    """Constant-size decode cache of one Mamba-3 layer (the scan part of the
+    reference's layer cache, `lm/models/mamba4.py:477-481`)."""
+
+    state: torch.Tensor            # [B,H,N,P] float32
+    previous_keys: torch.Tensor    # [B,H,N] rotated key of the last token
+    previous_values: torch.Tensor  # [B,H,P] value of the last token
+    phase: torch.Tensor            # [B,H,A] accumulated rotation phase
+
+
+def mamba3_step_cache(batch, heads, state_dim, head_dim, angle_count, device=None):
+    """Zero cache (`lm/models/mamba4.py:527-560`, scan fields)."""
+    z = lambda *shape: torch.zeros(*shape, dtype=torch.float32, device=device)  # noqa: E731
+    return Mamba3StepCache(z(batch, heads, state_dim, head_dim), z(batch, heads, state_dim),
+                           z(batch, heads, head_dim), z(batch, heads, angle_count))
+
+
+def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias):
+    """One cached token of the SISO scan: the scan core of `_Mamba3StepMixer`
+    (`lm/models/mamba4.py:412-481`) through `m4_scan_step`.
+
+    cache: Mamba3StepCache; c, b [B,N] (shared by the heads, as mamba3_fused)
+    or [B,H,N]; x [B,H*P] (bfloat16 or float32); adt, dt, trap_logits [B,H];
+    angles [B,A] (or [B,H,A]) rates; q_bias, k_bias [H,1,N] or [H,N].
+    Returns y [B,H*P] (dtype of x; before the D skip and gate) and the new
+    cache. Stepping mamba3_step_cache(...) through a sequence gives
+    mamba3_fused's y and final state (`test_decode_gpu.py`).
+    """
+    if not x.is_cuda:
+        raise RuntimeError("mamba3_step runs on CUDA tensors only (no CPU path)")
+    heads = dt.shape[-1]
+    per_head = c.dim() == 3
+    batch = x.shape[0]
+    state_dim = c.shape[-1]
+    value_dim = x.shape[-1] // heads
+    angle_count = angles.shape[-1]
+    if state_dim % 2 or angle_count > state_dim // 2:
+        raise ValueError("Mamba-3 state dimension must be even and contain angles")
+    if state_dim > STATE_DIM or value_dim > HEAD_DIM:
+        raise ValueError(f"Scan supports state and head dims up to {STATE_DIM}")
+    model = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
+    pad_n = STATE_DIM - state_dim
+    c = F.pad(c.to(model), (0, pad_n)).contiguous()
+    b = F.pad(b.to(model), (0, pad_n)).contiguous()
+    xp = F.pad(x.to(model).reshape(batch, heads, value_dim), (0, HEAD_DIM - value_dim))
+    xp = xp.reshape(batch, heads * HEAD_DIM).contiguous()
+    f32 = lambda a: a.float().contiguous()  # noqa: E731
+    qb = None if q_bias is None else F.pad(f32(q_bias).reshape(heads, state_dim), (0, pad_n)).contiguous()
+    kb = None if k_bias is None else F.pad(f32(k_bias).reshape(heads, state_dim), (0, pad_n)).contiguous()
+    st = F.pad(f32(cache.state), (0, HEAD_DIM - value_dim, 0, pad_n)).contiguous()
+    pk = F.pad(f32(cache.previous_keys), (0, pad_n)).contiguous()
+    pv = F.pad(f32(cache.previous_values), (0, HEAD_DIM - value_dim)).contiguous()
+    ph = f32(cache.phase)
+    y = torch.empty_like(xp)
+    st_out, pk_out, pv_out, ph_out = (torch.empty_like(t) for t in (st, pk, pv, ph))
+    dims = _lib.ScanDims(batch, 1, heads, HEAD_DIM, STATE_DIM, angle_count, CHUNK,
+                         int(model == torch.bfloat16), int(per_head))
+    lib = _lib.load()
+    _lib.check(
+        lib.m4_scan_step(ctypes.byref(dims), *map(_lib.ptr, (st, pk, pv, ph, c, b, xp, f32(adt), f32(dt),
+                                                              f32(trap_logits), f32(angles), qb, kb, y,
+                                                              st_out, pk_out, pv_out, ph_out)),
+                         _stream()),
+        "m4_scan_step")
+    y = y.reshape(batch, heads, HEAD_DIM)[..., :value_dim].reshape(batch, heads * value_dim)
+    new = Mamba3StepCache(st_out[:, :, :state_dim, :value_dim], pk_out[..., :state_dim],
+                          pv_out[..., :value_dim], ph_out)
+    return y, new

@@ -173,6 +173,59 @@ def selective_memory_fused(
     return SelectiveResult(out[..., :value_dim], var, state)
 
 
+def selective_decode(state, key, value, query, beta, log_decay, floor, solver=None):
+    """One exact write/read against a carried state (`lm/kernels/mamba4.py:341-355`).
+
+    state: SelectiveState(evidence [B,H,D,D], cross [B,H,P,D]); key, query
+    [B,H,D]; value [B,H,P]; beta, log_decay [B,H]; floor [H,D]. Returns
+    SelectiveResult(output [B,H,P], variance [B,H], SelectiveState(evidence',
+    cross')) through `m4_memread_decode` (one warp per head: rank-one state
+    update, 64x64 Cholesky with the query as bordered row, back-substitution).
+    `solver` is accepted for signature compatibility ("cuda"/"fused"/None).
+    Key dims below 64 are padded with an identity block as in
+    `selective_memory_fused`. No gradient (the reference decodes without one).
+    """
+    if solver not in (None, *SOLVERS):
+        raise ValueError(f"Unknown SPD solve backend {solver}")
+    key, value, query = (torch.as_tensor(a).float() for a in (key, value, query))
+    if not key.is_cuda:
+        raise RuntimeError("selective_decode runs on CUDA tensors only (no CPU path)")
+    batch, heads, dim = key.shape
+    value_dim = value.shape[-1]
+    if query.shape != key.shape or value.shape[:2] != key.shape[:2]:
+        raise ValueError("Selective memory keys, values and queries disagree")
+    if dim > KEY_DIM:
+        raise ValueError(f"Selective memory key dimension {dim} exceeds {KEY_DIM}")
+    if value_dim > VALUE_DIMS[-1]:
+        raise ValueError(f"Selective memory value dimension {value_dim} exceeds {VALUE_DIMS[-1]}")
+    dev = key.device
+    pv = VALUE_DIMS[0] if value_dim <= VALUE_DIMS[0] else VALUE_DIMS[1]
+    shape = (batch, heads)
+    beta = torch.broadcast_to(torch.as_tensor(beta, dtype=torch.float32, device=dev), shape).contiguous()
+    log_decay = torch.broadcast_to(torch.as_tensor(log_decay, dtype=torch.float32, device=dev),
+                                   shape).contiguous()
+    floor = torch.broadcast_to(torch.as_tensor(floor, dtype=torch.float32, device=dev), (heads, dim))
+    ev = torch.as_tensor(state.evidence, dtype=torch.float32, device=dev)
+    cr = torch.as_tensor(state.cross, dtype=torch.float32, device=dev)
+    ev = F.pad(ev, (0, KEY_DIM - dim, 0, KEY_DIM - dim)).contiguous()
+    cr = F.pad(cr, (0, KEY_DIM - dim, 0, pv - value_dim)).contiguous()
+    k = _pad_last(key, KEY_DIM).contiguous()
+    q = _pad_last(query, KEY_DIM).contiguous()
+    v = _pad_last(value, pv).contiguous()
+    f = _pad_last(floor, KEY_DIM, 1.0).contiguous()
+    out = torch.empty(batch, heads, pv, device=dev)
+    var = torch.empty(batch, heads, device=dev)
+    ev_out, cr_out = torch.empty_like(ev), torch.empty_like(cr)
+    dims = _dims(batch, 1, heads, pv)
+    lib = _lib.load()
+    _lib.check(
+        lib.m4_memread_decode(ctypes_ref(dims), *map(_lib.ptr, (ev, cr, k, v, q, beta, log_decay, f, out,
+                                                                var, ev_out, cr_out)), _stream()),
+        "m4_memread_decode")
+    new_state = SelectiveState(ev_out[..., :dim, :dim], cr_out[..., :value_dim, :dim])
+    return SelectiveResult(out[..., :value_dim], var, new_state)
+
+
 SOLVERS = ("cuda", "fused")
 
 

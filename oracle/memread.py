@@ -399,6 +399,26 @@ def chunked_backward(
     )
 
 
+def decode_step(evidence, cross, key, value, query, beta, log_decay, floor):
+    """One exact write/read against a carried state, float64.
+
+    Follows `selective_decode` (`lm/kernels/mamba4.py:341-355`): evidence
+    [B,H,D,D], cross [B,H,P,D], key/query [B,H,D], value [B,H,P], beta and
+    log_decay [B,H], floor [H,D]. Returns (output [B,H,P], variance [B,H],
+    evidence', cross').
+    """
+    s, c = np.asarray(evidence, F64), np.asarray(cross, F64)
+    k, v, q = (np.asarray(a, F64) for a in (key, value, query))
+    lam = np.exp(np.asarray(log_decay, F64))[..., None, None]
+    b = np.asarray(beta, F64)[..., None, None]
+    s = lam * s + b * (k[..., :, None] * k[..., None, :])
+    c = lam * c + b * (v[..., :, None] * k[..., None, :])
+    dim = k.shape[-1]
+    precision = s + np.asarray(floor, F64)[None, :, :, None] * np.eye(dim)
+    y = np.linalg.solve(precision, q[..., None])[..., 0]
+    return np.einsum("bhpd,bhd->bhp", c, y), np.sum(q * y, axis=-1), s, c
+
+
 def config_inputs(batch, time, heads, dim, value_dim, seed=0):
     """Seeded inputs of BASELINE configs 0 and 2 (float32 arrays).
 

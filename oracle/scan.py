@@ -237,6 +237,54 @@ def fused_layout_grads(args, weights_y, weights_final, chunk=64):
     return [g.detach() for g in torch.autograd.grad(loss, leaves)]
 
 
+def step_decode(cache, c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, model_dtype=None):
+    """One cached token of the Mamba-3 SISO scan, float64 (rounded to
+    `model_dtype` where the reference rounds).
+
+    Restates the scan core of `_Mamba3StepMixer` (`lm/models/mamba4.py:412-481`):
+    cache = (state [B,H,N,P], previous_keys [B,H,N], previous_values [B,H,P],
+    phase [B,H,A]); c, b [B,N] shared by the heads (or [B,H,N]); x [B,H*P];
+    adt, dt, trap_logits [B,H]; angles [B,A] (or [B,H,A]); biases [H,N] or
+    [H,1,N]. Biased c/b are rounded to the model dtype (`:440-441`), rotated
+    pairwise by the advanced phase and rounded again (`rotate`,
+    `lm/kernels/mamba3.py:20-40`); the state update and the read run in
+    float (`:447-462`). Returns (y [B,H*P], new cache).
+    """
+    state, prev_k, prev_v, phase = (torch.as_tensor(a, dtype=F64) for a in cache)
+    batch, heads, n_state, head_dim = state.shape
+    rd = (lambda t: t) if model_dtype is None else (lambda t: t.to(model_dtype).to(F64))
+    c, b, x = (torch.as_tensor(a, dtype=F64) for a in (c, b, x))
+    adt, dt, trap = (torch.as_tensor(a, dtype=F64) for a in (adt, dt, trap_logits))
+    ang = torch.as_tensor(angles, dtype=F64)
+    if c.dim() == 2:
+        c, b = c[:, None, :].expand(batch, heads, n_state), b[:, None, :].expand(batch, heads, n_state)
+    if ang.dim() == 2:
+        ang = ang[:, None, :].expand(batch, heads, ang.shape[-1])
+    qb = torch.as_tensor(q_bias, dtype=F64).reshape(heads, n_state)
+    kb = torch.as_tensor(k_bias, dtype=F64).reshape(heads, n_state)
+    phase = phase + ang * dt[..., None]
+    pairs = n_state // 2
+    theta = torch.nn.functional.pad(phase, (0, pairs - phase.shape[-1]))
+    cos, sin = torch.cos(theta), torch.sin(theta)
+
+    def rotate(u):
+        left, right = u[..., 0::2], u[..., 1::2]
+        out = torch.stack((left * cos - right * sin, left * sin + right * cos), dim=-1)
+        return rd(out.reshape(u.shape))
+
+    q = rotate(rd(c + qb))
+    k = rotate(rd(b + kb))
+    v = rd(x.reshape(batch, heads, head_dim))
+    gate = 1.0 / (1.0 + torch.exp(-trap))
+    alpha = torch.exp(adt)[..., None, None]
+    previous = prev_k[..., :, None] * prev_v[..., None, :]
+    current = k[..., :, None] * v[..., None, :]
+    state = alpha * (state + (dt * (1 - gate))[..., None, None] * previous)
+    state = state + (dt * gate)[..., None, None] * current
+    y = rd(torch.einsum("bhn,bhnp->bhp", q, state))
+    return y.reshape(batch, heads * head_dim), (state, k, v, phase)
+
+
 def config_inputs(batch, time, heads, head_dim, state_dim, seed=0, per_head_angles=False):
     """Seeded inputs of BASELINE config 1 (numpy float32; c, b, x meant as bf16).
 

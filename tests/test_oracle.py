@@ -207,3 +207,42 @@ def test_scan_no_future_leakage():
     # scale_t = gamma_t + dt_(t+1)(1-trap_(t+1)): y_t depends on token t+1's dt/trap
     # only through the *source* weight of s=t, which affects outputs > t.
     np.testing.assert_allclose(y[:, :25].numpy(), y2[:, :25].numpy(), rtol=0, atol=0)
+
+
+def test_decode_oracles_step_through_the_sequence_oracles():
+    """One-token oracles (`selective_decode`, lm/kernels/mamba4.py:341-355;
+    the scan core of `_Mamba3StepMixer`, lm/models/mamba4.py:412-481)
+    stepped from a zero state reproduce the sequence oracles."""
+    import torch
+
+    from oracle import scan as S
+
+    cfg = M.config_inputs(2, 20, 3, 8, 5, seed=3)
+    names = ("keys", "values", "queries", "beta", "log_decay", "floor")
+    fwd = M.dense_forward(*[cfg[n] for n in names])
+    batch, time, heads, dim = cfg["keys"].shape
+    ev = np.zeros((batch, heads, dim, dim))
+    cr = np.zeros((batch, heads, cfg["values"].shape[-1], dim))
+    for t in range(time):
+        out, var, ev, cr = M.decode_step(ev, cr, cfg["keys"][:, t], cfg["values"][:, t],
+                                         cfg["queries"][:, t], cfg["beta"][:, t],
+                                         cfg["log_decay"][:, t], cfg["floor"])
+        np.testing.assert_allclose(out, fwd["output"][:, t], rtol=1e-12, atol=1e-14)
+        np.testing.assert_allclose(var, fwd["variance"][:, t], rtol=1e-12, atol=1e-14)
+    np.testing.assert_allclose(ev, fwd["evidence"], rtol=1e-12, atol=1e-14)
+
+    sc = S.config_inputs(2, 70, 3, 8, 8, seed=1)
+    keys = ("c", "b", "x", "adt", "dt", "trap_logits", "angles", "q_bias", "k_bias")
+    ey, ef = S.fused_layout_scan(*[torch.tensor(sc[n], dtype=torch.float64) for n in keys])
+    batch, time = sc["c"].shape[:2]
+    heads = sc["dt"].shape[-1]
+    n_state, head_dim = sc["c"].shape[-1], sc["x"].shape[-1] // heads
+    cache = (np.zeros((batch, heads, n_state, head_dim)), np.zeros((batch, heads, n_state)),
+             np.zeros((batch, heads, head_dim)), np.zeros((batch, heads, sc["angles"].shape[-1])))
+    ys = []
+    for t in range(time):
+        y, cache = S.step_decode(cache, *[sc[n][:, t] for n in keys[:7]], sc["q_bias"], sc["k_bias"])
+        ys.append(y)
+    scale = float(ey.abs().max())
+    assert float((torch.stack(ys, 1) - ey).abs().max()) < 1e-12 * scale
+    assert float((cache[0] - ef).abs().max()) < 1e-12 * float(ef.abs().max())
