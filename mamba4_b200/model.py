@@ -18,9 +18,10 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .flashmamba import Mamba3StepCache, mamba3_step, mamba3_step_cache
 from .glue import (head_cross_entropy, mamba_mixer_core, memory_mixer_post, memory_mixer_prep, order_scan,
                    rms_norm_bf16)
-from .memory import selective_memory_fused
+from .memory import selective_decode, selective_initial_state, selective_memory_fused
 
 
 @dataclass(frozen=True)
@@ -137,6 +138,33 @@ class Mamba3Mixer(nn.Module):
                                  angles=self.angles, eps=cfg.norm_eps)
         return self.out_proj(y)
 
+    def init_cache(self, batch, device=None):
+        cfg = self.cfg
+        return mamba3_step_cache(batch, cfg.num_heads, cfg.d_state, cfg.head_dim, self.angles, device=device)
+
+    def decode(self, u, cache: Mamba3StepCache):
+        """One token (`_Mamba3StepMixer`, `lm/models/mamba4.py:412-481`):
+        u [B, d_model] bf16 -> ([B, d_model], new cache). Same rounding
+        points as the training glue: B/C RMSNorm to bf16, scan output bf16,
+        out = bf16((y + x D) silu(z))."""
+        cfg = self.cfg
+        h, p = cfg.num_heads, cfg.head_dim
+        proj = self.in_proj(u)
+        with torch.autocast("cuda", enabled=False):
+            proj = proj.to(torch.bfloat16)
+            z, x, b, c, raw_dt, raw_a, trap, angles = torch.split(proj, self.sizes, dim=-1)
+            b = self.B_norm(b)
+            c = self.C_norm(c)
+            dt = F.softplus(raw_dt.float() + self.dt_bias)
+            adt = -torch.clamp(heavy_tail_activation(raw_a.float()), min=1e-4) * dt
+            y, cache = mamba3_step(cache, c, b, x.contiguous(), adt, dt, trap.float(), angles.float(),
+                                   q_bias=self.C_bias, k_bias=self.B_bias)
+            batch = u.shape[0]
+            yh = y.float().reshape(batch, h, p) + x.float().reshape(batch, h, p) * self.D[:, None]
+            zf = z.float().reshape(batch, h, p)
+            out = (yh * (zf * torch.sigmoid(zf))).to(torch.bfloat16).reshape(batch, h * p)
+        return self.out_proj(out), cache
+
 
 def causal_conv(x, weight, bias):
     """Depthwise causal convolution (`lm/models/mamba4.py:98-108`), fp32 taps."""
@@ -234,6 +262,56 @@ class SelectiveMemoryMixer(nn.Module):
                                      self.D, self.order_mix, self.read_norm.scale, cfg.norm_eps)
         return self.out_proj(read)
 
+    def init_cache(self, batch, device=None):
+        cfg = self.cfg
+        h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
+        channels = cfg.inner + 2 * h * d
+        return dict(memory=selective_initial_state(batch, h, d, p, device=device),
+                    conv=torch.zeros(batch, cfg.conv_kernel - 1, channels, dtype=torch.bfloat16, device=device),
+                    order=torch.zeros(batch, h, p, device=device),
+                    shifted=torch.zeros(batch, h, d, device=device))
+
+    def decode(self, u, cache):
+        """One token of the cached memory mixer (`lm/models/mamba4.py:127-337`
+        with `cache`): conv history, key shift, unit norms, gates, the
+        one-token read (`selective_decode`), the order-head step and the read
+        epilogue, with the rounding points of the training glue."""
+        cfg = self.cfg
+        h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
+        batch = u.shape[0]
+        proj = self.in_proj(u)
+        with torch.autocast("cuda", enabled=False):
+            proj = proj.to(torch.bfloat16)
+            gate, value, key, query, beta_raw, dt_raw, order_raw = torch.split(proj, self.sizes, dim=-1)
+            mixed = torch.cat((value, key, query), dim=-1)                    # [B, C] bf16
+            window = torch.cat((cache["conv"], mixed[:, None]), dim=1)        # [B, K, C]
+            weight = self.conv_weight.float() - self.bound
+            conv = self.conv_bias.float() + (window.float() * weight[None]).sum(1)
+            act = conv * torch.sigmoid(conv)
+            value = act[:, : cfg.inner].reshape(batch, h, p)
+            key = act[:, cfg.inner: cfg.inner + h * d].reshape(batch, h, d)
+            query = act[:, cfg.inner + h * d:].reshape(batch, h, d)
+            shifted = key
+            key, query = _unit(cache["shifted"]), _unit(query)
+            beta = cfg.memory_beta_max * torch.sigmoid(beta_raw.float() + self.beta_bias)
+            dt = F.softplus(dt_raw.float() + self.dt_bias)
+            log_decay = -torch.exp(self.a_log) * dt
+            floor = cfg.floor_min + F.softplus(self.floor)
+            res = selective_decode(cache["memory"], key, value, query, beta, log_decay, floor)
+            read = res.output * torch.sigmoid(1 - self.confidence_scale * torch.log1p(res.variance))[..., None]
+            read = read + self.D[:, None] * value
+            order = cache["order"]
+            if cfg.order_head:
+                lam = torch.sigmoid(order_raw.float() + 2)[..., None]
+                order = lam * order + (1 - lam) * value
+                read = read + torch.sigmoid(self.order_mix)[:, None] * order
+            rs = torch.rsqrt(read.square().mean(-1, keepdim=True) + cfg.norm_eps)
+            normed = (read * rs * self.read_norm.scale).to(torch.bfloat16).float()
+            g = gate.float().reshape(batch, h, p)
+            out = (normed * (g * torch.sigmoid(g))).to(torch.bfloat16).reshape(batch, h * p)
+        new = dict(memory=res.state, conv=window[:, 1:].contiguous(), order=order, shifted=shifted)
+        return self.out_proj(out), new
+
 
 class Block(nn.Module):
     """Pre-norm residual block (`Mamba3Block`, `SelectiveMemoryBlock`)."""
@@ -245,6 +323,10 @@ class Block(nn.Module):
 
     def forward(self, x):
         return x + self.mixer(self.norm(x)).to(x.dtype)
+
+    def decode(self, x, cache):
+        out, cache = self.mixer.decode(self.norm(x), cache)
+        return x + out.to(x.dtype), cache
 
 
 class Mamba4LM(nn.Module):
@@ -276,6 +358,23 @@ class Mamba4LM(nn.Module):
         if targets is not None:
             return head_cross_entropy(x, self.embedding.weight, targets)
         return F.linear(x, self.embedding.weight.to(x.dtype)).float()
+
+    def init_cache(self, batch, device=None):
+        """Constant-size decode cache of every layer (`lm/models/mamba4.py:527-560`)."""
+        return [block.mixer.init_cache(batch, device=device) for block in self.blocks]
+
+    @torch.no_grad()
+    def decode_step(self, tokens, cache):
+        """One cached decode step (`lm/models/mamba4.py:507-524`): tokens [B]
+        -> (logits [B, V] float32, new cache). Run under the same autocast as
+        the forward."""
+        x = self.embedding(tokens).to(torch.bfloat16)
+        new = []
+        for block, layer in zip(self.blocks, cache):
+            x, layer = block.decode(x, layer)
+            new.append(layer)
+        x = self.final_norm(x)
+        return F.linear(x, self.embedding.weight.to(x.dtype)).float(), new
 
 
 def parameter_count(model: nn.Module) -> int:

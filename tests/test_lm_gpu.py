@@ -50,3 +50,27 @@ def test_lm_is_causal_and_gradients_reach_memory_parameters():
         assert grad is not None and torch.isfinite(grad).all() and grad.norm() > 1e-9, name
     for p in model.parameters():
         assert p.grad is not None and torch.isfinite(p.grad).all()
+
+
+def test_cached_decode_matches_prefill_logits():
+    """Token-by-token cached decode (`Mamba4LM.decode_step`, the reference's
+    `decode_step`, lm/models/mamba4.py:507-560) reproduces the prefill
+    logits (lm/tests/test_mamba4.py:407-419). The prefill scan rounds its
+    chunk products to bfloat16 where the one-token step does not, so the bar
+    is a bfloat16-level relative error rather than the reference's float32
+    2e-5."""
+    torch.manual_seed(3)
+    model = Mamba4LM(TINY).cuda().eval()
+    tokens = (torch.arange(2 * 11, device="cuda").reshape(2, 11) * 5) % TINY.vocab_size
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        logits = model(tokens)
+        cache = model.init_cache(2, device="cuda")
+        steps = []
+        for i in range(tokens.shape[1]):
+            out, cache = model.decode_step(tokens[:, i], cache)
+            steps.append(out)
+    decoded = torch.stack(steps, 1)
+    err = (decoded - logits).norm() / logits.norm()
+    assert err < 2e-2, float(err)
+    assert (decoded - logits).abs().max() < 0.05 * logits.abs().max()
+    assert (decoded.argmax(-1) == logits.argmax(-1)).float().mean() > 0.9
