@@ -794,10 +794,13 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
 // ---------------------------------------------------------------------------
 // Chunk-product kernels: one CTA of 8 warps per (batch, 64-token chunk, head)
 // (carry: one per (batch, head)). The products run on tensor cores as m16n8k8
-// TF32 MMAs on a two-term split of every fp32 operand (hi = tf32(x),
-// lo = tf32(x - hi)) with three products per tile (lo*hi + hi*lo + hi*hi):
-// about 2^-22 relative error, inside the float32 tolerance of the reference
-// (whose einsums run at Precision.HIGHEST, lm/kernels/mamba4_fused.py:411-447).
+// TF32 MMAs on a two-term split of every fp32 operand (hi = tf32(x) rounded,
+// lo = x - hi passed as is: the tensor core reads its top 19 bits) with three
+// products per tile (lo*hi + hi*lo + hi*hi): about 2^-21 relative error per
+// product, inside the float32 tolerance of the reference (whose einsums run at
+// Precision.HIGHEST, lm/kernels/mamba4_fused.py:411-447). Skipping the second
+// rounding saves one ALU conversion per operand element, the pipe these
+// kernels saturate.
 // Warp w owns rows 16 (w % 4) .. +15 and column half w / 4 of each product.
 // ---------------------------------------------------------------------------
 constexpr int LD = 68;    // tile stride in floats (conflict-free A fragments)
@@ -831,13 +834,14 @@ M4_DEV void gemm3(float (&acc)[NT][4], int row0, int col0, FA fa, FB fb) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       ah[i] = to_tf32(av[i]);
-      al[i] = to_tf32(av[i] - __uint_as_float(ah[i]));
+      al[i] = __float_as_uint(av[i] - __uint_as_float(ah[i]));  // read as tf32 (low bits ignored)
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const float b0 = fb(k0 + c, col0 + 8 * nt + g), b1 = fb(k0 + c + 4, col0 + 8 * nt + g);
       const uint32_t bh[2] = {to_tf32(b0), to_tf32(b1)};
-      const uint32_t bl[2] = {to_tf32(b0 - __uint_as_float(bh[0])), to_tf32(b1 - __uint_as_float(bh[1]))};
+      const uint32_t bl[2] = {__float_as_uint(b0 - __uint_as_float(bh[0])),
+                              __float_as_uint(b1 - __uint_as_float(bh[1]))};
       mma_tf32(acc[nt], al, bh);
       mma_tf32(acc[nt], ah, bl);
       mma_tf32(acc[nt], ah, bh);
