@@ -16,8 +16,10 @@
 //                    4x8 cyclic lane grid with the query as a bordered row
 //                    (gives w = L^-1 q for free), a blocked back-substitution
 //                    y = L^-T w with 8x8 diagonal-block inverses, and a
-//                    coalesced 128-bit streaming store of L (reciprocal
-//                    pivots on the diagonal, as mamba4_fused.py:78-113 keeps).
+//                    coalesced 128-bit streaming store of L with those
+//                    diagonal blocks inverted (their diagonals are the
+//                    reciprocal pivots mamba4_fused.py:78-113 keeps), so the
+//                    backward's substitutions need no inversion.
 //   memread_output   per (batch, 64-token chunk, head): output =
 //                    ((Y K^T) o W) V + diag(e^P) Y C0^T (mamba4_fused.py:439-447).
 //   backward         rhs g (chunk products), z = A^-1 g from the stored
@@ -357,10 +359,18 @@ M4_DEV float xblk(const SolveSmem& sm, int J, int r, int c) {
   return r >= c ? sm.u.s.X[J * 36 + tri(r, c)] : 0.f;
 }
 
-// Blocked back-substitution y = L^-T w (w in smem). yr2[K] = (y[8K+a], y[8K+a+4]);
+// Replace each diagonal block of the lane-tiled factor by its inverse (from
+// invert_blocks): the layout the factor is stored in and the substitutions
+// read. The block diagonals stay the reciprocal pivots 1/L_rr.
+M4_DEV void diag_to_inverse(float2 (&L)[NPAIR], const SolveSmem& sm, int a, int b) {
+#pragma unroll
+  for (int J = 0; J < 8; ++J) L[pair_of(J, J)] = make_float2(xblk(sm, J, a, b), xblk(sm, J, a + 4, b));
+}
+
+// Blocked back-substitution y = L^-T w (w in smem) on a factor whose diagonal
+// blocks hold their inverses (diag_to_inverse). yr2[K] = (y[8K+a], y[8K+a+4]);
 // y also written to ysm.
-M4_DEV void back_substitute(const float2 (&L)[NPAIR], const SolveSmem& sm, const float* w, float* ysm,
-                            int a, int b) {
+M4_DEV void back_substitute(const float2 (&L)[NPAIR], const float* w, float* ysm, int a, int b) {
   float2 yr2[8];
 #pragma unroll
   for (int J = 7; J >= 0; --J) {
@@ -375,8 +385,8 @@ M4_DEV void back_substitute(const float2 (&L)[NPAIR], const SolveSmem& sm, const
     const float x = w[8 * J + b] - sp;                   // x[b] on lanes (., b)
     const float xa = __shfl_sync(0xffffffffu, x, a);       // x[a]
     const float xa4 = __shfl_sync(0xffffffffu, x, a + 4);  // x[a + 4]
-    float p = xblk(sm, J, a, b) * xa;
-    p = fmaf(xblk(sm, J, a + 4, b), xa4, p);
+    float p = L[pair_of(J, J)].x * xa;
+    p = fmaf(L[pair_of(J, J)].y, xa4, p);
     p += __shfl_xor_sync(0xffffffffu, p, 8);
     p += __shfl_xor_sync(0xffffffffu, p, 16);            // y[8J + b]
     yr2[J] = make_float2(__shfl_sync(0xffffffffu, p, a), __shfl_sync(0xffffffffu, p, a + 4));
@@ -384,9 +394,9 @@ M4_DEV void back_substitute(const float2 (&L)[NPAIR], const SolveSmem& sm, const
   }
 }
 
-// Blocked forward substitution u = L^-1 g (g in smem); u written to usm.
-M4_DEV void forward_substitute(const float2 (&L)[NPAIR], const SolveSmem& sm, const float* g, float* usm,
-                               int a, int b) {
+// Blocked forward substitution u = L^-1 g (g in smem), diagonal blocks
+// inverted as in back_substitute; u written to usm.
+M4_DEV void forward_substitute(const float2 (&L)[NPAIR], const float* g, float* usm, int a, int b) {
   float ub[8];
   const int src = (b & 3) * 8;
 #pragma unroll
@@ -407,8 +417,8 @@ M4_DEV void forward_substitute(const float2 (&L)[NPAIR], const SolveSmem& sm, co
     const float t0 = __shfl_sync(0xffffffffu, x0, src);
     const float t1 = __shfl_sync(0xffffffffu, x1, src);
     const float xb = b < 4 ? t0 : t1;         // x[b]
-    float p0 = xblk(sm, J, a, b) * xb;
-    float p1 = xblk(sm, J, a + 4, b) * xb;
+    float p0 = L[pair_of(J, J)].x * xb;
+    float p1 = L[pair_of(J, J)].y * xb;
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
       p0 += __shfl_xor_sync(0xffffffffu, p0, o);
@@ -631,6 +641,8 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
       d.x = (b == a) ? rc[n] : (a < b ? 0.f : d.x);
       d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
     }
+    invert_blocks(A, sm, lane, a, b);
+    diag_to_inverse(A, sm, a, b);
     {
       float* dst = Lst + (size_t(bh) * Tp + t) * LSTRIDE;
 #pragma unroll
@@ -638,9 +650,7 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
         st4_stream(dst + (q4 * 32 + lane) * 4,
                    make_float4(A[2 * q4].x, A[2 * q4].y, A[2 * q4 + 1].x, A[2 * q4 + 1].y));
     }
-
-    invert_blocks(A, sm, lane, a, b);
-    back_substitute(A, sm, sm.w, sm.y, a, b);
+    back_substitute(A, sm.w, sm.y, a, b);
     __syncwarp();
     if (lane < 16) st4(Y + (size_t(bh) * Tp + t) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
     if (live && lane == 0) variance[(size_t(bb) * T + t) * H + h] = var;
@@ -768,7 +778,8 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
     d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
   }
   invert_blocks(A, sm, lane, a, b);
-  back_substitute(A, sm, sm.w, sm.y, a, b);
+  diag_to_inverse(A, sm, a, b);
+  back_substitute(A, sm.w, sm.y, a, b);
   __syncwarp();
   if (lane == 0) variance[bh] = var;
   // C' = lam C + beta v k^T row by row (lanes over key coordinates 2l, 2l+1
@@ -1008,8 +1019,9 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
 // ---------------------------------------------------------------------------
 // Backward kernels.
 // ---------------------------------------------------------------------------
-// zsolve_kernel: z_t = A_t^-1 g_t from the stored factor (one warp per token
-// at a time, 16 tokens per warp). The next token's factor and right-hand side
+// zsolve_kernel: z_t = A_t^-1 g_t from the stored factor (diagonal blocks
+// already inverted; one warp per token at a time, 16 tokens per warp): two
+// blocked substitutions. The next token's factor and right-hand side
 // stream into shared memory (cp.async; the evidence buffer of the forward's
 // layout is free here) while the current token is solved.
 __global__ void __launch_bounds__(32 * WARPS, 4) zsolve_kernel(
@@ -1047,9 +1059,8 @@ __global__ void __launch_bounds__(32 * WARPS, 4) zsolve_kernel(
     if (lane < 16) st4(&sm.y[4 * lane], ld4(&sm.flC[4 * lane]));
     __syncwarp();  // the buffers are refilled below
     if (tt + 1 < SUB) prefetch(t + 1);
-    invert_blocks(L, sm, lane, a, b);
-    forward_substitute(L, sm, sm.y, sm.w, a, b);
-    back_substitute(L, sm, sm.w, sm.y, a, b);
+    forward_substitute(L, sm.y, sm.w, a, b);
+    back_substitute(L, sm.w, sm.y, a, b);
     __syncwarp();
     if (lane < 16) st4(Z + (size_t(bh) * Tp + t) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
     __syncwarp();
