@@ -137,7 +137,8 @@ size_t m4_scan_workspace_bytes(const M4ScanDims* dims);
  *   adt, dt, trap_logits [B,T,H] float32; angles [B,T,A] (per_head [B,T,H,A])
  *   float32 rates; q_bias, k_bias [H,N] float32 (may be NULL = zero).
  * Outputs: y [B,T,H*P] (dtype of x), final_state [B,H,N,P] float32;
- *   residual: chunk-start states and phases (remat name "ssd_scan"). */
+ *   residual: chunk-start states and phases (remat name "ssd_scan").
+ * bfloat16 operands: c, b and x must be 16-byte aligned (M4_ERR_ALIGN). */
 int m4_scan_fwd(const M4ScanDims* dims, const void* c, const void* b, const void* x,
                 const float* adt, const float* dt, const float* trap_logits,
                 const float* angles, const float* q_bias, const float* k_bias,

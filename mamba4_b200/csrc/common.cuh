@@ -32,6 +32,24 @@ M4_DEV float warp_inclusive_scan(float v, int lane) {
 M4_DEV float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 M4_DEV void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
+// Asynchronous global -> shared copies (cp.async): 16 bytes (.cg) or 4 bytes
+// (.ca); an invalid source copies zeros (src-size 0; the address stays a
+// valid one). Groups are committed and awaited per pipeline stage.
+M4_DEV void cp16(float* dst, const float* src, bool valid) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+M4_DEV void cp4(float* dst, const float* src, bool valid) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+M4_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+M4_DEV void cp_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+// Wait for all of this thread's copies; a __syncthreads must follow before
+// other threads read them.
+M4_DEV void cp_wait() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // Paired fp32 arithmetic (fma.rn.f32x2 / mul.rn.f32x2, sm_100a): two
 // lanes of work per instruction, each rounded like fmaf / __fmul_rn.
 M4_DEV unsigned long long pk2(float2 v) {

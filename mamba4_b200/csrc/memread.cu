@@ -76,23 +76,7 @@ inline Sizes sizes(const M4MemDims& d) {
 // ---------------------------------------------------------------------------
 // memread_states: sequential evidence/cross statistics per (batch, head).
 // ---------------------------------------------------------------------------
-// Asynchronous global -> shared copies (cp.async): 16 bytes (.cg) or 4 bytes
-// (.ca); an invalid source copies zeros (src-size 0; the address stays a
-// valid one). Groups are committed and awaited per pipeline stage.
-M4_DEV void cp16(float* dst, const float* src, bool valid) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-M4_DEV void cp4(float* dst, const float* src, bool valid) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
-}
-M4_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-M4_DEV void cp_wait_group() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-// Wait for all of this thread's copies; a __syncthreads must follow before
-// other threads read them.
-M4_DEV void cp_wait() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 
 // Each 16-token sub-chunk is applied in one pass: with P_s the inclusive
 // prefix of log lambda inside the sub-chunk,

@@ -861,20 +861,12 @@ inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const
   float* deltas = reinterpret_cast<float*>(resid + l.deltas);
   const bf16* cq = static_cast<const bf16*>(c);
   const bf16* bk = static_cast<const bf16*>(b);
-  const bf16* xx = static_cast<const bf16*>(x);
-  const int bh = d.B * d.H, chunks = bh * d.nch;
-  const size_t psm = size_t(d.nch) * 32 * sizeof(float);
-  allow_smem(phase_kernel, psm);
-  phase_kernel<<<bh, 256, psm, st>>>(d, dt, angles, phases);
-  allow_smem(update_kernel, sizeof(UpdSmem) + 1024);
-  update_kernel<<<chunks, GW * 32, sizeof(UpdSmem) + 1024, st>>>(d, bk, xx, adt, dt, trap, angles, kb, phases, starts,
-                                                      deltas);
-  state_kernel<<<bh * SPARTS, 256, 0, st>>>(d, starts, deltas, fin);
   alignas(64) CUtensorMap xmap;
-  if (!aligned16(x) || !encode_tokens_map(&xmap, x, d.B, d.T, d.H * P)) return M4_ERR_LAUNCH;
-  allow_smem(output_kernel, sizeof(OutSmem) + 1024);
-  output_kernel<<<chunks, GW * 32, sizeof(OutSmem) + 1024, st>>>(d, xmap, cq, bk, adt, dt, trap, angles, qb, kb,
-                                                               phases, starts, static_cast<bf16*>(y));
+  if (!all_aligned16(c, b, x)) return M4_ERR_ALIGN;  // 16-byte row copies and the TMA box
+  if (!encode_tokens_map(&xmap, x, d.B, d.T, d.H * P)) return M4_ERR_LAUNCH;
+  allow_smem(fused_fwd_kernel, sizeof(FusedSmem) + 1024);
+  fused_fwd_kernel<<<d.B * d.H, GW * 32, sizeof(FusedSmem) + 1024, st>>>(
+      d, xmap, cq, bk, adt, dt, trap, angles, qb, kb, static_cast<bf16*>(y), starts, phases, deltas, fin);
   return launch_status();
 }
 

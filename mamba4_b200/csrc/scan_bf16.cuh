@@ -1,21 +1,21 @@
-// Chunk-parallel bf16 Mamba-3 scan (forward and backward), sm_100a.
+// bf16 Mamba-3 scan (forward and backward), sm_100a.
 //
 // Same recurrence, rounding points and outputs as the sequential kernels in
-// scan.cu, reorganised so every (batch, head, chunk) is its own CTA:
+// scan.cu:
 //
-// forward   phase_kernel    phase at every chunk start (prefix over chunks)
-//           update_kernel   per chunk: U_n = K^T rd(V o scale o tail) and the
-//                           chunk decay, U_n written into the `starts` slot
-//           state_kernel    per (b, h): S_0 = 0, S_(n+1) = d_n S_n + U_n, in
-//                           place (starts[n] <- S_n), final state
-//           output_kernel   per chunk: y = rd(rd((Q K^T) o W) V + e^p Q rd(S_n))
+// forward   fused_fwd_kernel  one persistent CTA per (b, h) walks the chunks
+//                             with the fp32 state in registers: TMA x tiles,
+//                             prefetched (cp.async) gates/angles/C/B rows,
+//                             tcgen05 chunk products, residuals S_n, phases
+//                             and chunk decays for the backward
 // backward  dstart_kernel   per chunk: D_n = Q^T rd(dY o e^p) (into `carries`)
 //           carry_kernel    per (b, h), reverse: carries[n] <- cotangent of the
 //                           chunk-end state E_n; E_(n-1) = D_n + d_n E_n
 //           grads_kernel    per chunk: every gradient given S_n and E_n
 //           later_kernel    phase-gradient carry over chunks
-// Chunk products: bf16 tiles in shared memory, ldmatrix fragments, m16n8k16
-// tensor-core MMAs with fp32 accumulation.
+// Chunk products: tcgen05 (tensor memory accumulators, swizzled shared-memory
+// operands) in the forward and dstart; bf16 tiles with ldmatrix fragments and
+// m16n8k16 mma.sync in grads_kernel; fp32 accumulation everywhere.
 #pragma once
 
 #include "tc05.cuh"
@@ -340,278 +340,347 @@ M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16
   }
 }
 
-// Load a [64][64] fp32 block (row-major) into a bf16 tile with RN rounding;
-// 32 / NW 16-byte loads per thread in flight.
-template <int NW = GW, bool BLK = false>
-M4_DEV void load_state_bf16(const float* src, bf16* T) {
-  constexpr int PER = 32 / NW, TH = 32 * NW;
-  float4 v[PER];
-  int rr[PER], cc[PER];
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    const int idx = threadIdx.x + k * TH;
-    rr[k] = idx / (P / 4);
-    cc[k] = 4 * (idx % (P / 4));
-    v[k] = ld4(src + rr[k] * P + cc[k]);
-  }
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    *reinterpret_cast<__nv_bfloat162*>(at<BLK>(T, rr[k], cc[k])) = __floats2bfloat162_rn(v[k].x, v[k].y);
-    *reinterpret_cast<__nv_bfloat162*>(at<BLK>(T, rr[k], cc[k] + 2)) = __floats2bfloat162_rn(v[k].z, v[k].w);
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
 
-// Phase at every chunk start: phases[b,h,n,i] = sum_{t < 64n} rate_t[i] dt_t.
-// Warp per chunk, lane per pair, loads issued 16 tokens at a time.
-__global__ void __launch_bounds__(256) phase_kernel(Dims d, const float* __restrict__ dt,
-                                                    const float* __restrict__ angles,
-                                                    float* __restrict__ phases) {
-  extern __shared__ float loc[];  // [nch][32]
-  const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int n = warp; n < d.nch; n += 8) {
-    float acc = 0.f;
-    if (lane < d.A) {
-      for (int j0 = 0; j0 < C; j0 += 16) {
-        float inc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int t = n * C + j0 + j;
-          inc[j] = t < d.T ? rate_at(d, angles, b, h, t, lane) * dt[(size_t(b) * d.T + t) * d.H + h] : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc += inc[j];
-      }
-    }
-    loc[n * 32 + lane] = acc;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    float acc = 0.f;
-    for (int n = 0; n < d.nch; ++n) {
-      phases[(size_t(bh) * d.nch + n) * 32 + lane] = acc;
-      acc += loc[n * 32 + lane];
-    }
-  }
-}
-
-struct UpdSmem {
-  bf16 Ks[C * N];  // blocked tiles (tcgen05 operands)
-  bf16 Vw[C * P];
-  float theta[C * 33];
-  float sinv[C * 33];
-  float scratch[C];
-  Rows r;
-  uint64_t bar;
-  uint32_t tmem;
-};
-
-// U_n = K^T rd(V o scale o tail) into starts[n]; deltas[n] = e^(p_L). The
-// product runs on the tensor cores (tcgen05, accumulator in tensor memory).
-__global__ void __launch_bounds__(GW * 32) update_kernel(
-    Dims d, const bf16* __restrict__ bk, const bf16* __restrict__ x, const float* __restrict__ adt,
-    const float* __restrict__ dt, const float* __restrict__ trap_logits, const float* __restrict__ angles,
-    const float* __restrict__ kb, const float* __restrict__ phases, float* __restrict__ starts,
-    float* __restrict__ deltas) {
-  extern __shared__ __align__(128) unsigned char raw[];
-  UpdSmem& s = *reinterpret_cast<UpdSmem*>(align1024(raw));
-  const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) {
-    tc::tmem_alloc(&s.tmem, 64);
-    tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
-  }
-  if (threadIdx.x == 0) tc::mbar_init(&s.bar, 1);
-  chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
-  __syncthreads();
-  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
-  __syncthreads();
-  if (threadIdx.x < C) s.scratch[threadIdx.x] = s.r.scl[threadIdx.x] * s.r.tail[threadIdx.x];
-  __syncthreads();
-  build_qk<GW, true>(d, b, h, t0, nullptr, bk, nullptr, kb, s.theta, s.sinv, nullptr, s.Ks);
-  load_tile<GW, true>(d, b, h, t0, x, s.Vw, s.scratch);
-  tc_publish();
-  const uint32_t tm = s.tmem;
-  if (threadIdx.x == 0) {
-    tc_product(tm, s.Ks, true, s.Vw, true);  // rows n (A = K^T), cols p
-    tc::commit(&s.bar);
-  }
-  if (tc_wait(&s.bar, 0)) {
-    const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
-    float v[2][16];
-    tc::ld16(tmem_lane_base(tm) + col0, v[0]);
-    tc::ld16(tmem_lane_base(tm) + col0 + 16, v[1]);
-    tc::wait_ld();
-    if (lane < 16) {
-      float* dst = starts + (size_t(bh) * d.nch + n) * N * P + row * P + col0;
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 16; e += 4) st4(dst + 16 * j + e, make_float4(v[j][e], v[j][e + 1], v[j][e + 2], v[j][e + 3]));
-    }
-  }
-  tc::fence_before();
-  __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tm, 64);
-  if (threadIdx.x == 0) deltas[size_t(bh) * d.nch + n] = expf(s.r.p[C - 1]);
-}
-
-// In place over chunks: starts[n] <- S_n with S_0 = 0, S_(n+1) = d_n S_n + U_n.
-// Four CTAs per (b, h), one float4 column of the state per thread; the
-// chunk slots are loaded eight at a time ahead of the serial update.
+// Four CTAs per (b, h) in the chunk-carry pass of the backward.
 constexpr int SPARTS = 4;
-__global__ void __launch_bounds__(256) state_kernel(Dims d, float* __restrict__ starts,
-                                                    const float* __restrict__ deltas,
-                                                    float* __restrict__ final_state) {
-  const int bh = blockIdx.x / SPARTS, i = 4 * ((blockIdx.x % SPARTS) * 256 + threadIdx.x);
-  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int n0 = 0; n0 < d.nch; n0 += 8) {
-    float4 u[8];
-    float dl[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (n0 + j < d.nch) {
-        u[j] = ld4(starts + (size_t(bh) * d.nch + n0 + j) * N * P + i);
-        dl[j] = deltas[size_t(bh) * d.nch + n0 + j];
-      }
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (n0 + j < d.nch) {
-        st4(starts + (size_t(bh) * d.nch + n0 + j) * N * P + i, s);
-        s = make_float4(fmaf(dl[j], s.x, u[j].x), fmaf(dl[j], s.y, u[j].y), fmaf(dl[j], s.z, u[j].z),
-                        fmaf(dl[j], s.w, u[j].w));
-      }
-  }
-  st4(final_state + size_t(bh) * N * P + i, s);
-}
 
-struct OutSmem {
-  bf16 Qs[C * N];  // blocked tiles (tcgen05 operands)
+// ---------------------------------------------------------------------------
+// Persistent forward: one CTA (8 warps) per (batch, head) walks the chunks in
+// order with the fp32 state carried in registers (the inter-chunk carry of
+// the reference's sequential chunk grid, flashmamba.py:589-660), so no state
+// pass, phase pass or per-chunk CTA setup is left. Per chunk:
+//   TMA of the next chunk's x tile into the other buffer (zero fill past T);
+//   gates, in-chunk phases and the rotated, rounded Q / K tiles;
+//   rd(S_n) as a tile, S_n and the chunk-start phase to the residuals;
+//   tcgen05 commit 1: Q K^T, Q rd(S_n), K^T rd(V o scale o tail);
+//   masked scores rd((Q K^T) o W) -> tile; tcgen05 commit 2: scores V;
+//   S_(n+1) = e^(p_L) S_n + K^T rd(V o scale o tail) in registers;
+//   y = rd(scores V + e^p Q rd(S_n)).
+// Thread (w, lane < 16) owns state row 16 (w % 4) + lane, columns
+// 32 (w / 4) .. +31: the accumulator rows it reads from tensor memory.
+// Residuals written: starts[n] = S_n, phases[n], deltas[n] = e^(p_L).
+// ---------------------------------------------------------------------------
+// Raw inputs of one chunk, prefetched (cp.async) while the previous chunk's
+// tensor-core phases run; tokens past T arrive as zeros. dt and trap hold
+// token t0 + 64 too (the trapezoid's next-token term).
+struct FusedStage {
+  bf16 c[C * N];       // rows of c (queries) and b (keys), row-major
+  bf16 b[C * N];
+  float ang[C * 32];   // angle rates [token][pair]
+  float adt[C];
+  float dt[C + 4];
+  float trap[C + 4];
+};
+
+struct FusedSmem {
+  bf16 Qs[C * N];      // 128-byte-swizzled tiles on 1024-byte boundaries
   bf16 Ks[C * N];
-  bf16 Vs[C * P];
-  bf16 Ms[C * C];
-  bf16 Ss[N * P];
+  bf16 Vs[2][C * P];   // x tiles (TMA, double buffered)
+  bf16 Vw[C * P];      // rd(V o scale o tail)
+  bf16 Ms[C * C];      // masked scores
+  bf16 Ss[N * P];      // rd(S_n)
   float theta[C * 33];
   float sinv[C * 33];
   float scratch[C];
+  float phase[32];     // phase at the current chunk start
   Rows r;
-  uint64_t bar;    // tensor-core commits
-  uint64_t bar_x;  // TMA of the x tile
+  FusedStage in;       // the current chunk's raw inputs
+  uint64_t bar;        // tensor-core commits (two per chunk)
+  uint64_t bar_x[2];   // TMA of the x tiles
   uint32_t tmem;
 };
 
-// y = rd(rd((Q K^T) o W) V + e^p Q rd(S_n)). The three chunk products run on
-// the tensor cores (tcgen05): Q K^T into tensor-memory columns 0..63 and
-// Q rd(S) into 64..127; the masked scores go back to shared memory as a bf16
-// tile and rd(...) V reuses columns 0..63. The x tile arrives by TMA.
-__global__ void __launch_bounds__(GW * 32, 1) output_kernel(
+// Start copying chunk n's raw inputs into the stage (one commit group).
+M4_DEV void fused_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, const bf16* bk, const float* adt,
+                           const float* dt, const float* trap_logits, const float* angles, FusedStage& in) {
+  const int tid = threadIdx.x, t0 = n * C;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {  // 2 tiles x 64 rows x 8 16-byte pieces over 256 threads
+    const int idx = tid + k * GW * 32, which = idx >> 9, rr = (idx >> 3) & 63, c8 = 8 * (idx & 7);
+    const int t = t0 + rr;
+    const bool live = t < d.T;
+    const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
+    const bf16* src = which ? bk : cq;
+    cp16(reinterpret_cast<float*>((which ? in.b : in.c) + rr * N + c8),
+         reinterpret_cast<const float*>(live ? src + base + c8 : src), live);
+  }
+  for (int idx = tid; idx < C * d.A; idx += GW * 32) {
+    const int tt = idx / d.A, i = idx % d.A, t = t0 + tt;
+    const bool live = t < d.T;
+    const size_t o = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * d.A + i : (size_t(b) * d.T + t) * d.A + i;
+    cp4(&in.ang[tt * 32 + i], live ? angles + o : angles, live);
+  }
+  if (tid < 3 * (C + 1)) {
+    const int which = tid / (C + 1), tt = tid % (C + 1), t = t0 + tt;
+    const bool live = t < d.T && (which > 0 || tt < C);
+    const size_t o = (size_t(b) * d.T + t) * d.H + h;
+    const float* src = which == 0 ? adt : which == 1 ? dt : trap_logits;
+    float* dst = which == 0 ? in.adt : which == 1 ? in.dt : in.trap;
+    if (which > 0 || tt < C) cp4(dst + tt, live ? src + o : src, live);
+  }
+  cp_commit();
+}
+
+// chunk_rows from the stage.
+M4_DEV void fused_rows(const Dims& d, int t0, const FusedStage& in, Rows& r, float* scratch) {
+  const int tid = threadIdx.x;
+  if (tid < C) {
+    const bool live = t0 + tid < d.T;
+    const float dtv = in.dt[tid];
+    const float tr = live ? 1.f / (1.f + expf(-in.trap[tid])) : 0.f;
+    const float next = t0 + tid + 1 < d.T ? in.dt[tid + 1] * (1.f - 1.f / (1.f + expf(-in.trap[tid + 1]))) : 0.f;
+    r.dt[tid] = dtv;
+    r.gam[tid] = dtv * tr;
+    r.scl[tid] = dtv * tr + next;
+    scratch[tid] = in.adt[tid];
+  }
+  __syncthreads();
+  if (tid < 32) {
+    const float v0 = warp_inclusive_scan(scratch[tid], tid);
+    const float tot = __shfl_sync(0xffffffffu, v0, 31);
+    const float v1 = warp_inclusive_scan(scratch[32 + tid], tid) + tot;
+    r.p[tid] = v0;
+    r.p[32 + tid] = v1;
+  }
+  __syncthreads();
+  if (tid < C) {
+    r.tail[tid] = expf(r.p[C - 1] - r.p[tid]);
+    r.ept[tid] = expf(r.p[tid]);
+  }
+}
+
+// chunk_theta from the stage (same segment scheme).
+M4_DEV void fused_theta(const Dims& d, const FusedStage& in, Rows& r, const float* phase0, float* cosv, float* sinv) {
+  constexpr int SEG = C / GW;
+  const int i = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float acc = 0.f;
+  if (i < d.A) {
+#pragma unroll
+    for (int j = 0; j < SEG; ++j) {
+      const int tt = SEG * w + j;
+      acc = fmaf(in.ang[tt * 32 + i], r.dt[tt], acc);
+      cosv[tt * 33 + i] = acc;
+    }
+  }
+  r.seg[w * 32 + i] = acc;
+  __syncthreads();
+  float off = 0.f;
+  if (i < d.A) {
+    off = phase0[i];
+    for (int v = 0; v < w; ++v) off += r.seg[v * 32 + i];
+  }
+#pragma unroll 1
+  for (int j = 0; j < SEG; ++j) {
+    const int e = (SEG * w + j) * 33 + i;
+    float cs = 1.f, sn = 0.f;
+    if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
+    cosv[e] = cs;
+    sinv[e] = sn;
+  }
+}
+
+// build_qk from the stage.
+M4_DEV void fused_qk(int h, const FusedStage& in, const float* qb, const float* kb, const float* cosv,
+                     const float* sinv, bf16* Qs, bf16* Ks) {
+  constexpr int PER = C / GW;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, n0 = 2 * lane;
+  const float qb0 = qb ? qb[h * N + n0] : 0.f, qb1 = qb ? qb[h * N + n0 + 1] : 0.f;
+  const float kb0 = kb ? kb[h * N + n0] : 0.f, kb1 = kb ? kb[h * N + n0 + 1] : 0.f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int tt = w + GW * k;
+    const uint32_t cr = ld_u32(in.c + tt * N + n0), br = ld_u32(in.b + tt * N + n0);
+    const float cs = cosv[tt * 33 + lane], sn = sinv[tt * 33 + lane];
+    const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
+    const float k0 = round_to<bf16>(lo_f(br) + kb0), k1 = round_to<bf16>(hi_f(br) + kb1);
+    *reinterpret_cast<__nv_bfloat162*>(at<true>(Qs, tt, n0)) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
+    *reinterpret_cast<__nv_bfloat162*>(at<true>(Ks, tt, n0)) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+  }
+}
+
+__global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     Dims d, const __grid_constant__ CUtensorMap tmap_x, const bf16* __restrict__ cq, const bf16* __restrict__ bk,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
-    const float* __restrict__ phases, const float* __restrict__ starts, bf16* __restrict__ y) {
+    bf16* __restrict__ y, float* __restrict__ starts, float* __restrict__ phases, float* __restrict__ deltas,
+    float* __restrict__ final_state) {
   extern __shared__ __align__(128) unsigned char raw[];
-  OutSmem& s = *reinterpret_cast<OutSmem*>(align1024(raw));
-  const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
-  const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  FusedSmem& s = *reinterpret_cast<FusedSmem*>(align1024(raw));
+  const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
   if (warp == 0) {
-    tc::tmem_alloc(&s.tmem, 128);
-    tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
+    tc::tmem_alloc(&s.tmem, 256);
+    tc::tmem_relinquish();
   }
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     tc::mbar_init(&s.bar, 1);
-    tc::mbar_init(&s.bar_x, 1);
+    tc::mbar_init(&s.bar_x[0], 1);
+    tc::mbar_init(&s.bar_x[1], 1);
   }
+  if (tid < 32) s.phase[tid] = 0.f;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    // The x tile by TMA (tokens past T read as zeros): box 64 tokens x 64 channels.
-    tc::mbar_expect_tx(&s.bar_x, C * P * sizeof(bf16));
-    tc::tma_load_3d(s.Vs, &tmap_x, h * P, t0, b, &s.bar_x);
-  }
-  chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
-  __syncthreads();
-  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
-  __syncthreads();
-  build_qk<GW, true>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
-  load_state_bf16<GW, true>(starts + (size_t(bh) * d.nch + n) * N * P, s.Ss);
-  tc_publish();
+  tc::fence_after();
   const uint32_t tm = s.tmem;
-  if (threadIdx.x == 0) {
-    tc_product(tm, s.Qs, false, s.Ks, false);       // Q K^T: K = n on both
-    tc_product(tm + 64, s.Qs, false, s.Ss, true);   // Q S: B = S as [n][p]
-    tc::commit(&s.bar);
+  if (tid == 0) {
+    tc::mbar_expect_tx(&s.bar_x[0], C * P * sizeof(bf16));
+    tc::tma_load_3d(s.Vs[0], &tmap_x, h * P, 0, b, &s.bar_x[0]);
   }
-  bool ok = tc_wait(&s.bar, 0);
-  if (ok) {
-    float v[2][16];
-    tc::ld16(tmem_lane_base(tm) + col0, v[0]);
-    tc::ld16(tmem_lane_base(tm) + col0 + 16, v[1]);
-    tc::wait_ld();
-    if (lane < 16) {
-      const float pt = s.r.p[row];
+  fused_prefetch(d, b, h, 0, cq, bk, adt, dt, trap_logits, angles, s.in);
+  float st[32];  // fp32 state S_n: row `row`, columns col0 .. col0 + 31 (lanes < 16)
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) {
-          float m2[2];
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int sidx = col0 + 16 * j + e + q;
-            float w = 0.f;
-            if (sidx < row) w = expf(pt - s.r.p[sidx]) * s.r.scl[sidx];
-            else if (sidx == row) w = s.r.gam[row];
-            m2[q] = v[j][e + q] * w;
-          }
-          *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ms, row, col0 + 16 * j + e)) = __floats2bfloat162_rn(m2[0], m2[1]);
-        }
+  for (int j = 0; j < 32; ++j) st[j] = 0.f;
+  bool ok = true;
+  for (int n = 0; n < d.nch; ++n) {
+    const int t0 = n * C, buf = n & 1;
+    if (tid == 0 && n + 1 < d.nch) {
+      // The other buffer was last read by chunk n - 1's score product, which
+      // completed before that chunk ended.
+      tc::mbar_expect_tx(&s.bar_x[buf ^ 1], C * P * sizeof(bf16));
+      tc::tma_load_3d(s.Vs[buf ^ 1], &tmap_x, h * P, t0 + C, b, &s.bar_x[buf ^ 1]);
     }
-  }
-  tc_publish();
-  if (threadIdx.x == 0 && ok) {
-    if (!tc::mbar_wait(&s.bar_x, 0, tc::WAIT_LIMIT)) {
-      tc::flag_timeout();
+    cp_wait();
+    __syncthreads();  // this chunk's stage has landed
+    fused_rows(d, t0, s.in, s.r, s.scratch);
+    __syncthreads();
+    fused_theta(d, s.in, s.r, s.phase, s.theta, s.sinv);
+    __syncthreads();
+    if (tid < 32) {
+      float inc = 0.f;
+#pragma unroll
+      for (int w = 0; w < GW; ++w) inc += s.r.seg[w * 32 + tid];
+      phases[(size_t(bh) * d.nch + n) * 32 + tid] = s.phase[tid];
+      s.phase[tid] += tid < d.A ? inc : 0.f;
+    }
+    if (tid < C) s.scratch[tid] = s.r.scl[tid] * s.r.tail[tid];
+    fused_qk(h, s.in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+    if (lane < 16) {
+      float* dst = starts + (size_t(bh) * d.nch + n) * N * P + row * P + col0;
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[j], st[j + 1], st[j + 2], st[j + 3]));
+#pragma unroll
+      for (int j = 0; j < 32; j += 2)
+        *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ss, row, col0 + j)) = __floats2bfloat162_rn(st[j], st[j + 1]);
+    }
+    __syncthreads();  // scratch (scale o tail) visible; the stage is consumed
+    if (n + 1 < d.nch) fused_prefetch(d, b, h, n + 1, cq, bk, adt, dt, trap_logits, angles, s.in);
+    // rd(V o scale o tail) from the x tile once it has landed.
+    if (!tc::mbar_wait(&s.bar_x[buf], (n >> 1) & 1, tc::WAIT_LIMIT)) {
+      if (lane == 0) tc::flag_timeout();
       ok = false;
     }
-  }
-  if (threadIdx.x == 0 && ok) {
-    tc_product(tm, s.Ms, false, s.Vs, true);  // mixed V: A = Ms (K = s), B = V as [s][p]
-    tc::commit(&s.bar);
-  }
-  ok = ok && tc_wait(&s.bar, 1);
-  if (ok) {
-    float acc[2][16], inh[2][16];
-    tc::ld16(tmem_lane_base(tm) + col0, acc[0]);
-    tc::ld16(tmem_lane_base(tm) + col0 + 16, acc[1]);
-    tc::ld16(tmem_lane_base(tm) + 64 + col0, inh[0]);
-    tc::ld16(tmem_lane_base(tm) + 64 + col0 + 16, inh[1]);
-    tc::wait_ld();
-    const int t = t0 + row;
-    if (lane < 16 && t < d.T) {
+    if (ok) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int idx = tid + k * GW * 32, rr = idx >> 3, c8 = 8 * (idx & 7);
+        const uint4 v = *reinterpret_cast<const uint4*>(at<true>(s.Vs[buf], rr, c8));
+        const float f = s.scratch[rr];
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+        uint4 o;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const __nv_bfloat162 x2 = __floats2bfloat162_rn(lo_f(u[q]) * f, hi_f(u[q]) * f);
+          w[q] = *reinterpret_cast<const uint32_t*>(&x2);
+        }
+        *reinterpret_cast<uint4*>(at<true>(s.Vw, rr, c8)) = o;
+      }
+    }
+    tc_publish();
+    if (tid == 0 && ok) {
+      tc_product(tm, s.Qs, false, s.Ks, false);        // Q K^T
+      tc_product(tm + 64, s.Qs, false, s.Ss, true);    // Q rd(S_n)
+      tc_product(tm + 128, s.Ks, true, s.Vw, true);    // K^T rd(V o scale o tail)
+      tc::commit(&s.bar);
+    }
+    ok = ok && tc_wait(&s.bar, 0);
+    if (ok) {
+      const float pt = s.r.p[row];
+#pragma unroll 1
+      for (int j = 0; j < 2; ++j) {
+        float v[16];
+        tc::ld16(tmem_lane_base(tm) + col0 + 16 * j, v);
+        tc::wait_ld();
+        if (lane < 16) {
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            float m2[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const int sidx = col0 + 16 * j + e + q;
+              float w = 0.f;
+              if (sidx < row) w = expf(pt - s.r.p[sidx]) * s.r.scl[sidx];
+              else if (sidx == row) w = s.r.gam[row];
+              m2[q] = v[e + q] * w;
+            }
+            *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ms, row, col0 + 16 * j + e)) =
+                __floats2bfloat162_rn(m2[0], m2[1]);
+          }
+        }
+      }
+    }
+    tc_publish();
+    if (tid == 0 && ok) {
+      tc_product(tm, s.Ms, false, s.Vs[buf], true);   // scores V
+      tc::commit(&s.bar);
+    }
+    if (ok) {
+      // S_(n+1) = e^(p_L) S_n + U_n (the update finished with commit 1).
+      const float dl = expf(s.r.p[C - 1]);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float u[16];
+        tc::ld16(tmem_lane_base(tm) + 128 + col0 + 16 * j, u);
+        tc::wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) st[16 * j + e] = fmaf(dl, st[16 * j + e], u[e]);
+      }
+      if (tid == 0) deltas[size_t(bh) * d.nch + n] = dl;
+    }
+    ok = ok && tc_wait(&s.bar, 1);
+    if (ok) {
+      const int t = t0 + row;
       const float e = s.r.ept[row];
       bf16* yrow = y + (size_t(b) * d.T + t) * d.H * P + h * P + col0;
+#pragma unroll 1
+      for (int j = 0; j < 2; ++j) {
+        float acc[16], inh[16];
+        tc::ld16(tmem_lane_base(tm) + col0 + 16 * j, acc);
+        tc::ld16(tmem_lane_base(tm) + 64 + col0 + 16 * j, inh);
+        tc::wait_ld();
+        if (lane < 16 && t < d.T) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+          for (int q = 0; q < 16; q += 8) {
+            uint4 o;
+            uint32_t* u = reinterpret_cast<uint32_t*>(&o);
 #pragma unroll
-        for (int q = 0; q < 16; q += 8) {
-          uint4 o;
-          uint32_t* u = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaf(e, inh[j][q + 2 * k], acc[j][q + 2 * k]),
-                                                            fmaf(e, inh[j][q + 2 * k + 1], acc[j][q + 2 * k + 1]));
-            u[k] = *reinterpret_cast<const uint32_t*>(&h2);
+            for (int k = 0; k < 4; ++k) {
+              const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaf(e, inh[q + 2 * k], acc[q + 2 * k]),
+                                                              fmaf(e, inh[q + 2 * k + 1], acc[q + 2 * k + 1]));
+              u[k] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(yrow + 16 * j + q) = o;
           }
-          *reinterpret_cast<uint4*>(yrow + 16 * j + q) = o;
         }
+      }
     }
+    tc::fence_before();
+    __syncthreads();  // tensor memory and every tile are free for the next chunk
+    tc::fence_after();
   }
+  if (lane < 16) {
+    float* dst = final_state + size_t(bh) * N * P + row * P + col0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[j], st[j + 1], st[j + 2], st[j + 3]));
+  }
+  // A TMA the loop no longer waits for cannot be in flight: the last chunk
+  // issues none and every earlier one was awaited.
   tc::fence_before();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tm, 128);
+  if (warp == 0) tc::tmem_dealloc(tm, 256);
 }
 
 // ---------------------------------------------------------------------------
