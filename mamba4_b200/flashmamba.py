@@ -90,6 +90,11 @@ class _Scan(torch.autograd.Function):
         return (*scan_backward(*ctx.saved_tensors, d_y, d_final, ctx.per_head), None)
 
 
+def _pad(t, pads):
+    """F.pad only when something is padded (a zero pad still copies)."""
+    return F.pad(t, pads) if any(pads) else t
+
+
 def _prepare(c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, per_head):
     """Pad N and P to 64 (zero coordinates do not interact) and fix dtypes."""
     state_dim = c.shape[-1]
@@ -100,14 +105,16 @@ def _prepare(c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, per_h
     if state_dim > STATE_DIM or value_dim > HEAD_DIM:
         raise ValueError(f"Scan supports state and head dims up to {STATE_DIM}")
     model = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
-    c = F.pad(c.to(model), (0, STATE_DIM - state_dim)).contiguous()
-    b = F.pad(b.to(model), (0, STATE_DIM - state_dim)).contiguous()
+    pn = (0, STATE_DIM - state_dim)
+    c = _pad(c.to(model), pn).contiguous()
+    b = _pad(b.to(model), pn).contiguous()
     lead = x.shape[:-1]
-    x = F.pad(x.to(model).reshape(*lead, heads, value_dim), (0, HEAD_DIM - value_dim))
-    x = x.reshape(*lead, heads * HEAD_DIM).contiguous()
+    if value_dim != HEAD_DIM:
+        x = F.pad(x.to(model).reshape(*lead, heads, value_dim), (0, HEAD_DIM - value_dim))
+    x = x.to(model).reshape(*lead, heads * HEAD_DIM).contiguous()
     f32 = lambda a: a.float().contiguous()  # noqa: E731
-    qb = None if q_bias is None else F.pad(f32(q_bias).reshape(heads, state_dim), (0, STATE_DIM - state_dim)).contiguous()
-    kb = None if k_bias is None else F.pad(f32(k_bias).reshape(heads, state_dim), (0, STATE_DIM - state_dim)).contiguous()
+    qb = None if q_bias is None else _pad(f32(q_bias).reshape(heads, state_dim), pn).contiguous()
+    kb = None if k_bias is None else _pad(f32(k_bias).reshape(heads, state_dim), pn).contiguous()
     return c, b, x, f32(adt), f32(dt), f32(trap_logits), f32(angles), qb, kb, value_dim, state_dim
 
 
@@ -130,9 +137,12 @@ def mamba3_fused(
     c, b, x, adt, dt, trap, ang, qb, kb, value_dim, state_dim = _prepare(
         c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, False)
     y, final = _Scan.apply(c, b, x, adt, dt, trap, ang, qb, kb, False)
-    lead = y.shape[:-1]
-    y = y.reshape(*lead, heads, HEAD_DIM)[..., :value_dim].reshape(*lead, heads * value_dim)
-    return y, final[:, :, :state_dim, :value_dim]
+    if value_dim != HEAD_DIM:
+        lead = y.shape[:-1]
+        y = y.reshape(*lead, heads, HEAD_DIM)[..., :value_dim].reshape(*lead, heads * value_dim)
+    if state_dim != STATE_DIM or value_dim != HEAD_DIM:
+        final = final[:, :, :state_dim, :value_dim]
+    return y, final
 
 
 def mamba3_flash_heads(
