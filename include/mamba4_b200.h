@@ -150,7 +150,8 @@ int m4_scan_fwd(const M4ScanDims* dims, const void* c, const void* b, const void
  * angle_rates :1105-1111). d_final may be NULL (zero). Writes dc, db
  * (dtype of c/b; shared layouts sum over heads in a fixed order), dx,
  * d_adt, d_dt, d_trap_logits [B,T,H], d_angles (shape of angles),
- * d_q_bias, d_k_bias [H,N] (may be NULL). */
+ * d_q_bias, d_k_bias [H,N] (may be NULL). bfloat16 operands: c, b, x and
+ * d_y must be 16-byte aligned (M4_ERR_ALIGN). */
 int m4_scan_bwd(const M4ScanDims* dims, const void* c, const void* b, const void* x,
                 const float* adt, const float* dt, const float* trap_logits,
                 const float* angles, const float* q_bias, const float* k_bias,

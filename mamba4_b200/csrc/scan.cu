@@ -876,6 +876,7 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
                          void* db, void* dx, float* d_adt, float* d_dt, float* d_trap, float* d_angles,
                          float* d_qb, float* d_kb, char* work, cudaStream_t st) {
   using namespace scan2;
+  if (!all_aligned16(c, b, x, dy)) return M4_ERR_ALIGN;  // 16-byte tile copies
   const scan2::Dims d = make_dims2(s);
   const Layout l = layout(s);
   const float* starts = reinterpret_cast<const float*>(resid + l.starts);

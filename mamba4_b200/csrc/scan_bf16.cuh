@@ -826,29 +826,44 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
   const int t0 = n * C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rb = warp & 3, half = warp >> 2, row0 = 16 * rb, col0 = 32 * half;
   const int g = lane >> 2, cc = lane & 3;
+  // Every pure copy starts first and lands while the gates, phases and
+  // rotations are built: x and dY straight into their tiles, S_n (fp32) into
+  // the score tiles (free until the scores), E_n into registers.
+  constexpr int PER = 32 / GW;
+  float* Sstage = reinterpret_cast<float*>(s.Ms);  // [64][64] fp32 over Ms and Mt
+  float4 ev[PER];
+  {
+#pragma unroll
+    for (int k = 0; k < 2 * (16 / GW); ++k) {
+      const int idx = tid + (k % (16 / GW)) * TH, rr = idx >> 3, c8 = 8 * (idx & 7), t = t0 + rr;
+      const bool live = t < d.T;
+      const bf16* src = k < 16 / GW ? x : dy;
+      bf16* dst = (k < 16 / GW ? s.Vs : s.Dy) + rr * TS + c8;
+      cp16(reinterpret_cast<float*>(dst),
+           reinterpret_cast<const float*>(live ? src + (size_t(b) * d.T + t) * d.H * P + h * P + c8 : src), live);
+    }
+    const float* Sg = starts + (size_t(bh) * d.nch + n) * N * P;
+    const float* Eg = carries + (size_t(bh) * d.nch + n) * N * P;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) cp16(Sstage + 4 * (tid + k * TH), Sg + 4 * (tid + k * TH), true);
+    cp_commit();
+#pragma unroll
+    for (int k = 0; k < PER; ++k) ev[k] = ld4(Eg + 4 * (tid + k * TH));
+  }
   chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
   __syncthreads();
   chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
   __syncthreads();
   build_qk<GW>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
-  load_tile<GW>(d, b, h, t0, x, s.Vs);
-  load_tile<GW>(d, b, h, t0, dy, s.Dy);
+  cp_wait();
+  __syncthreads();  // x, dY and S_n have landed
   // rd(S_n), rd(E_n) as tiles and <E_n, S_n> (fp32 values) for the chunk-end decay.
   {
-    constexpr int PER = 32 / GW;
-    const float* Sg = starts + (size_t(bh) * d.nch + n) * N * P;
-    const float* Eg = carries + (size_t(bh) * d.nch + n) * N * P;
     float part = 0.f;
-    float4 sv[PER], ev[PER];
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      sv[k] = ld4(Sg + 4 * (tid + k * TH));
-      ev[k] = ld4(Eg + 4 * (tid + k * TH));
-    }
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int idx = tid + k * TH;
-      const float4 a4 = sv[k], e4 = ev[k];
+      const float4 a4 = ld4(Sstage + 4 * idx), e4 = ev[k];
       const int r = idx / (P / 4), c4 = idx % (P / 4);
       *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4) = __floats2bfloat162_rn(a4.x, a4.y);
       *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(a4.z, a4.w);
