@@ -184,161 +184,14 @@ struct Rows {
   float seg[8 * 32];  // per-segment totals of the in-chunk scans (one segment per warp)
 };
 
-M4_DEV void chunk_rows(const Dims& d, int b, int h, int t0, const float* adt, const float* dt,
-                       const float* trap_logits, Rows& r, float* scratch) {
-  const int tid = threadIdx.x;
-  if (tid < C) {
-    const int t = t0 + tid;
-    const bool live = t < d.T;
-    const size_t i = (size_t(b) * d.T + t) * d.H + h;
-    const float dtv = live ? dt[i] : 0.f;
-    const float tr = live ? 1.f / (1.f + expf(-trap_logits[i])) : 0.f;
-    float next = 0.f;
-    if (t + 1 < d.T) {
-      const size_t j = (size_t(b) * d.T + t + 1) * d.H + h;
-      next = dt[j] * (1.f - 1.f / (1.f + expf(-trap_logits[j])));
-    }
-    r.dt[tid] = dtv;
-    r.gam[tid] = dtv * tr;
-    r.scl[tid] = dtv * tr + next;
-    scratch[tid] = live ? adt[i] : 0.f;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    const float v0 = warp_inclusive_scan(scratch[tid], tid);
-    const float tot = __shfl_sync(0xffffffffu, v0, 31);
-    const float v1 = warp_inclusive_scan(scratch[32 + tid], tid) + tot;
-    r.p[tid] = v0;
-    r.p[32 + tid] = v1;
-  }
-  __syncthreads();
-  if (tid < C) {
-    r.tail[tid] = expf(r.p[C - 1] - r.p[tid]);
-    r.ept[tid] = expf(r.p[tid]);
-  }
-}
-
 M4_DEV float rate_at(const Dims& d, const float* angles, int b, int h, int t, int i) {
   return d.per_head ? angles[((size_t(b) * d.T + t) * d.H + h) * d.A + i]
                     : angles[(size_t(b) * d.T + t) * d.A + i];
 }
 
-// theta[t][i] = phase0[i] + sum_{s<=t} rate_s[i] dt_s within the chunk,
-// returned as cos (in `cosv`) and sin. Warp w of NW scans tokens
-// SEG w .. SEG w + SEG - 1 (independent loads, then a SEG-step sum), the
-// segment totals are combined through `r.seg`, and the same thread takes
-// sincos of its SEG elements in one compact loop. Pairs i >= A get cos 1,
-// sin 0. All 32 NW threads must call.
-template <int NW = GW>
-M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles, Rows& r,
-                        const float* phase0, float* cosv, float* sinv) {
-  constexpr int SEG = C / NW;
-  const int i = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float acc = 0.f;
-  if (i < d.A) {
-    float inc[SEG];
-#pragma unroll
-    for (int j = 0; j < SEG; ++j) {
-      const int tt = SEG * w + j, t = t0 + tt;
-      inc[j] = t < d.T ? rate_at(d, angles, b, h, t, i) * r.dt[tt] : 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < SEG; ++j) {
-      acc += inc[j];
-      cosv[(SEG * w + j) * 33 + i] = acc;
-    }
-  }
-  r.seg[w * 32 + i] = acc;
-  __syncthreads();
-  float off = 0.f;
-  if (i < d.A) {
-    off = phase0[i];
-    for (int v = 0; v < w; ++v) off += r.seg[v * 32 + i];
-  }
-#pragma unroll 1
-  for (int j = 0; j < SEG; ++j) {
-    const int e = (SEG * w + j) * 33 + i;
-    float cs = 1.f, sn = 0.f;
-    if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
-    cosv[e] = cs;
-    sinv[e] = sn;
-  }
-}
-
 M4_DEV uint32_t ld_u32(const bf16* p) { return *reinterpret_cast<const uint32_t*>(p); }
 M4_DEV float lo_f(uint32_t v) { return __uint_as_float(v << 16); }
 M4_DEV float hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
-
-// Rotated, rounded queries/keys of a chunk as bf16 tiles (either may be null).
-// Lane = angle pair i, warp w of NW = tokens w, w + NW, ...; all global loads
-// are issued before the rotation.
-template <int NW = GW, bool BLK = false>
-M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const bf16* cq, const bf16* bk, const float* qb,
-                     const float* kb, const float* cosv, const float* sinv, bf16* Qs, bf16* Ks) {
-  constexpr int PER = C / NW;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  int tt_[PER], i_[PER];
-  uint32_t cr[PER], br[PER];
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    tt_[k] = w + NW * k;
-    i_[k] = lane;
-    const int t = t0 + tt_[k], n0 = 2 * i_[k];
-    const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
-    cr[k] = (Qs && t < d.T) ? ld_u32(cq + base + n0) : 0u;
-    br[k] = (Ks && t < d.T) ? ld_u32(bk + base + n0) : 0u;
-  }
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    const int tt = tt_[k], i = i_[k], n0 = 2 * i;
-    const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
-    if (Qs) {
-      const float q0 = round_to<bf16>(lo_f(cr[k]) + (qb ? qb[h * N + n0] : 0.f));
-      const float q1 = round_to<bf16>(hi_f(cr[k]) + (qb ? qb[h * N + n0 + 1] : 0.f));
-      *reinterpret_cast<__nv_bfloat162*>(at<BLK>(Qs, tt, n0)) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
-    }
-    if (Ks) {
-      const float k0 = round_to<bf16>(lo_f(br[k]) + (kb ? kb[h * N + n0] : 0.f));
-      const float k1 = round_to<bf16>(hi_f(br[k]) + (kb ? kb[h * N + n0 + 1] : 0.f));
-      *reinterpret_cast<__nv_bfloat162*>(at<BLK>(Ks, tt, n0)) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
-    }
-  }
-}
-
-// Copy a [64 tokens][64] slice of a [B,T,H*64] bf16 tensor into a tile, each
-// row scaled by rowscale[t] (and rounded) when given. 16 / NW 16-byte loads
-// per thread, all in flight before the stores.
-template <int NW = GW, bool BLK = false>
-M4_DEV void load_tile(const Dims& d, int b, int h, int t0, const bf16* src, bf16* T,
-                      const float* rowscale = nullptr) {
-  constexpr int PER = 16 / NW, TH = 32 * NW;
-  uint4 v[PER];
-  int rr[PER], cc8[PER];
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    const int idx = threadIdx.x + k * TH;
-    rr[k] = idx >> 3;
-    cc8[k] = idx & 7;
-    const int t = t0 + rr[k];
-    v[k] = t < d.T ? *reinterpret_cast<const uint4*>(src + (size_t(b) * d.T + t) * d.H * P + h * P + 8 * cc8[k])
-                   : make_uint4(0u, 0u, 0u, 0u);
-  }
-#pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    uint4 o = v[k];
-    if (rowscale) {
-      const float f = rowscale[rr[k]];
-      uint32_t* u = reinterpret_cast<uint32_t*>(&v[k]);
-      uint32_t* r = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const __nv_bfloat162 x2 = __floats2bfloat162_rn(lo_f(u[q]) * f, hi_f(u[q]) * f);
-        r[q] = *reinterpret_cast<const uint32_t*>(&x2);
-      }
-    }
-    *reinterpret_cast<uint4*>(at<BLK>(T, rr[k], 8 * cc8[k])) = o;
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Forward
@@ -393,18 +246,41 @@ struct FusedSmem {
   uint32_t tmem;
 };
 
-// Start copying chunk n's raw inputs into the stage (one commit group).
-M4_DEV void fused_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, const bf16* bk, const float* adt,
-                           const float* dt, const float* trap_logits, const float* angles, FusedStage& in) {
+// Where a kernel stages one chunk's raw inputs (cp.async, tokens past T as
+// zeros): c / b rows (bf16, row-major with `stride` elements, or 128-byte
+// swizzled when SW), angle rates [token][32], adt [64], dt / trap [65] (token
+// t0 + 64 too, for the trapezoid's next-token term). Either c or b may be null.
+struct StageRef {
+  bf16* c;
+  bf16* b;
+  int stride;
+  float* ang;
+  float* adt;
+  float* dt;
+  float* trap;
+};
+
+template <bool SW>
+M4_DEV bf16* stage_row(bf16* base, int stride, int r, int c) {
+  if constexpr (SW) return at<true>(base, r, c);
+  else return base + r * stride + c;
+}
+
+// Start copying chunk n's raw inputs (one commit group per thread).
+template <bool SW>
+M4_DEV void stage_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, const bf16* bk, const float* adt,
+                           const float* dt, const float* trap_logits, const float* angles, const StageRef& in) {
   const int tid = threadIdx.x, t0 = n * C;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {  // 2 tiles x 64 rows x 8 16-byte pieces over 256 threads
     const int idx = tid + k * GW * 32, which = idx >> 9, rr = (idx >> 3) & 63, c8 = 8 * (idx & 7);
+    bf16* dst = which ? in.b : in.c;
+    if (dst == nullptr) continue;
     const int t = t0 + rr;
     const bool live = t < d.T;
     const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
     const bf16* src = which ? bk : cq;
-    cp16(reinterpret_cast<float*>((which ? in.b : in.c) + rr * N + c8),
+    cp16(reinterpret_cast<float*>(stage_row<SW>(dst, in.stride, rr, c8)),
          reinterpret_cast<const float*>(live ? src + base + c8 : src), live);
   }
   for (int idx = tid; idx < C * d.A; idx += GW * 32) {
@@ -425,7 +301,7 @@ M4_DEV void fused_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, c
 }
 
 // chunk_rows from the stage.
-M4_DEV void fused_rows(const Dims& d, int t0, const FusedStage& in, Rows& r, float* scratch) {
+M4_DEV void stage_rows(const Dims& d, int t0, const StageRef& in, Rows& r, float* scratch) {
   const int tid = threadIdx.x;
   if (tid < C) {
     const bool live = t0 + tid < d.T;
@@ -453,7 +329,7 @@ M4_DEV void fused_rows(const Dims& d, int t0, const FusedStage& in, Rows& r, flo
 }
 
 // chunk_theta from the stage (same segment scheme).
-M4_DEV void fused_theta(const Dims& d, const FusedStage& in, Rows& r, const float* phase0, float* cosv, float* sinv) {
+M4_DEV void stage_theta(const Dims& d, const StageRef& in, Rows& r, const float* phase0, float* cosv, float* sinv) {
   constexpr int SEG = C / GW;
   const int i = threadIdx.x & 31, w = threadIdx.x >> 5;
   float acc = 0.f;
@@ -482,8 +358,11 @@ M4_DEV void fused_theta(const Dims& d, const FusedStage& in, Rows& r, const floa
   }
 }
 
-// build_qk from the stage.
-M4_DEV void fused_qk(int h, const FusedStage& in, const float* qb, const float* kb, const float* cosv,
+// build_qk from the stage: rotated, rounded Q / K tiles (either may be null);
+// a stage may be the destination tile itself (each thread reads and writes
+// the same pair).
+template <bool SRC_SW, bool DST_SW>
+M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb, const float* cosv,
                      const float* sinv, bf16* Qs, bf16* Ks) {
   constexpr int PER = C / GW;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, n0 = 2 * lane;
@@ -492,12 +371,17 @@ M4_DEV void fused_qk(int h, const FusedStage& in, const float* qb, const float* 
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
     const int tt = w + GW * k;
-    const uint32_t cr = ld_u32(in.c + tt * N + n0), br = ld_u32(in.b + tt * N + n0);
     const float cs = cosv[tt * 33 + lane], sn = sinv[tt * 33 + lane];
-    const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
-    const float k0 = round_to<bf16>(lo_f(br) + kb0), k1 = round_to<bf16>(hi_f(br) + kb1);
-    *reinterpret_cast<__nv_bfloat162*>(at<true>(Qs, tt, n0)) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
-    *reinterpret_cast<__nv_bfloat162*>(at<true>(Ks, tt, n0)) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+    if (Qs) {
+      const uint32_t cr = ld_u32(stage_row<SRC_SW>(in.c, in.stride, tt, n0));
+      const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
+      *reinterpret_cast<__nv_bfloat162*>(at<DST_SW>(Qs, tt, n0)) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
+    }
+    if (Ks) {
+      const uint32_t br = ld_u32(stage_row<SRC_SW>(in.b, in.stride, tt, n0));
+      const float k0 = round_to<bf16>(lo_f(br) + kb0), k1 = round_to<bf16>(hi_f(br) + kb1);
+      *reinterpret_cast<__nv_bfloat162*>(at<DST_SW>(Ks, tt, n0)) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+    }
   }
 }
 
@@ -529,7 +413,8 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     tc::mbar_expect_tx(&s.bar_x[0], C * P * sizeof(bf16));
     tc::tma_load_3d(s.Vs[0], &tmap_x, h * P, 0, b, &s.bar_x[0]);
   }
-  fused_prefetch(d, b, h, 0, cq, bk, adt, dt, trap_logits, angles, s.in);
+  const StageRef in{s.in.c, s.in.b, N, s.in.ang, s.in.adt, s.in.dt, s.in.trap};
+  stage_prefetch<false>(d, b, h, 0, cq, bk, adt, dt, trap_logits, angles, in);
   float st[32];  // fp32 state S_n: row `row`, columns col0 .. col0 + 31 (lanes < 16)
 #pragma unroll
   for (int j = 0; j < 32; ++j) st[j] = 0.f;
@@ -544,9 +429,9 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     }
     cp_wait();
     __syncthreads();  // this chunk's stage has landed
-    fused_rows(d, t0, s.in, s.r, s.scratch);
+    stage_rows(d, t0, in, s.r, s.scratch);
     __syncthreads();
-    fused_theta(d, s.in, s.r, s.phase, s.theta, s.sinv);
+    stage_theta(d, in, s.r, s.phase, s.theta, s.sinv);
     __syncthreads();
     if (tid < 32) {
       float inc = 0.f;
@@ -556,7 +441,7 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
       s.phase[tid] += tid < d.A ? inc : 0.f;
     }
     if (tid < C) s.scratch[tid] = s.r.scl[tid] * s.r.tail[tid];
-    fused_qk(h, s.in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+    stage_qk<false, true>(h, in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
     if (lane < 16) {
       float* dst = starts + (size_t(bh) * d.nch + n) * N * P + row * P + col0;
 #pragma unroll
@@ -566,7 +451,7 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
         *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ss, row, col0 + j)) = __floats2bfloat162_rn(st[j], st[j + 1]);
     }
     __syncthreads();  // scratch (scale o tail) visible; the stage is consumed
-    if (n + 1 < d.nch) fused_prefetch(d, b, h, n + 1, cq, bk, adt, dt, trap_logits, angles, s.in);
+    if (n + 1 < d.nch) stage_prefetch<false>(d, b, h, n + 1, cq, bk, adt, dt, trap_logits, angles, in);
     // rd(V o scale o tail) from the x tile once it has landed.
     if (!tc::mbar_wait(&s.bar_x[buf], (n >> 1) & 1, tc::WAIT_LIMIT)) {
       if (lane == 0) tc::flag_timeout();
@@ -692,6 +577,7 @@ struct DsSmem {
   float theta[C * 33];
   float sinv[C * 33];
   float scratch[C];
+  float stg[3 * C + 8 + 32];  // staged gates and the chunk-start phase
   Rows r;
   uint64_t bar;
   uint32_t tmem;
@@ -711,12 +597,51 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
     tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
   }
   if (threadIdx.x == 0) tc::mbar_init(&s.bar, 1);
-  chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
+  // Every input starts at once: c rows in place in Qs, dY rows in Ds (both
+  // in the swizzled tile layout), angle rates in sinv, gates and the
+  // chunk-start phase in stg.
+  const StageRef in{s.Qs, nullptr, 0, s.sinv, s.stg, s.stg + C, s.stg + 2 * C + 4};
+  float* phase0 = s.stg + 3 * C + 8;
+  stage_prefetch<true>(d, b, h, n, cq, nullptr, adt, dt, trap_logits, angles, in);
+  {
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < 16 / GW; ++k) {
+      const int idx = tid + k * GW * 32, rr = idx >> 3, c8 = 8 * (idx & 7), t = t0 + rr;
+      const bool live = t < d.T;
+      cp16(reinterpret_cast<float*>(at<true>(s.Ds, rr, c8)),
+           reinterpret_cast<const float*>(live ? dy + (size_t(b) * d.T + t) * d.H * P + h * P + c8 : dy), live);
+    }
+    if (tid < 32) cp4(phase0 + tid, phases + (size_t(bh) * d.nch + n) * 32 + tid, true);
+    cp_commit();
+    cp_wait();
+  }
   __syncthreads();
-  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
+  stage_rows(d, t0, in, s.r, s.scratch);
   __syncthreads();
-  build_qk<GW, true>(d, b, h, t0, cq, nullptr, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
-  load_tile<GW, true>(d, b, h, t0, dy, s.Ds, s.r.ept);
+  stage_theta(d, in, s.r, phase0, s.theta, s.sinv);
+  __syncthreads();
+  stage_qk<true, true>(h, in, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
+  {
+    // rd(dY o e^p) in place: each thread rescales the pieces it copied.
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < 16 / GW; ++k) {
+      const int idx = tid + k * GW * 32, rr = idx >> 3, c8 = 8 * (idx & 7);
+      uint4* q = reinterpret_cast<uint4*>(at<true>(s.Ds, rr, c8));
+      const uint4 v = *q;
+      const float f = s.r.ept[rr];
+      const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+      uint4 o;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 x2 = __floats2bfloat162_rn(lo_f(u[j]) * f, hi_f(u[j]) * f);
+        w[j] = *reinterpret_cast<const uint32_t*>(&x2);
+      }
+      *q = o;
+    }
+  }
   tc_publish();
   const uint32_t tm = s.tmem;
   if (threadIdx.x == 0) {
@@ -831,6 +756,12 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
   // the score tiles (free until the scores), E_n into registers.
   constexpr int PER = 32 / GW;
   float* Sstage = reinterpret_cast<float*>(s.Ms);  // [64][64] fp32 over Ms and Mt
+  // c / b rows in place in Qs / Ks, angle rates in Es, gates and the
+  // chunk-start phase in vec (all free until later phases).
+  const StageRef in{s.Qs, s.Ks, TS, reinterpret_cast<float*>(s.Es), s.vec, s.vec + C, s.vec + 2 * C + 4};
+  float* phase0 = s.vec + 3 * C + 8;
+  stage_prefetch<false>(d, b, h, n, cq, bk, adt, dt, trap_logits, angles, in);
+  if (tid < 32) cp4(phase0 + tid, phases + (size_t(bh) * d.nch + n) * 32 + tid, true);
   float4 ev[PER];
   {
 #pragma unroll
@@ -850,13 +781,15 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
 #pragma unroll
     for (int k = 0; k < PER; ++k) ev[k] = ld4(Eg + 4 * (tid + k * TH));
   }
-  chunk_rows(d, b, h, t0, adt, dt, trap_logits, s.r, s.scratch);
-  __syncthreads();
-  chunk_theta<GW>(d, b, h, t0, angles, s.r, phases + (size_t(bh) * d.nch + n) * 32, s.theta, s.sinv);
-  __syncthreads();
-  build_qk<GW>(d, b, h, t0, cq, bk, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+  cp_commit();
   cp_wait();
-  __syncthreads();  // x, dY and S_n have landed
+  __syncthreads();  // every staged input has landed
+  stage_rows(d, t0, in, s.r, s.scratch);
+  __syncthreads();
+  stage_theta(d, in, s.r, phase0, s.theta, s.sinv);
+  __syncthreads();
+  stage_qk<false, false>(h, in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+  __syncthreads();  // the angle stage (Es) is consumed
   // rd(S_n), rd(E_n) as tiles and <E_n, S_n> (fp32 values) for the chunk-end decay.
   {
     float part = 0.f;
