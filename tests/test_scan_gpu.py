@@ -98,6 +98,68 @@ def test_scan_bf16_config1_shape_matches_oracle():
         assert rel_fro(g, e) < 5e-3, (name, rel_fro(g, e))
 
 
+@pytest.mark.parametrize("time, angle_count", [(100, 16), (7, 32), (200, 0), (130, 32)])
+def test_scan_bf16_ragged_lengths_and_angle_counts(time, angle_count):
+    # Partial last chunks (TMA and cp.async zero fill past T), 0 / 16 / 32
+    # rotation pairs, random biases; same bars as the configs[1] shape.
+    cfg = make(2, time, 3, angle_count, seed=time + angle_count)
+    y, final, grads = run_cuda(cfg, torch.bfloat16)
+    args = [torch.tensor(cfg[n], dtype=torch.float32) for n in NAMES]
+    for i in range(3):
+        args[i] = args[i].to(torch.bfloat16).float()
+    ey, ef = S.fused_layout_scan(*args, chunk=64, model_dtype=torch.bfloat16,
+                                 compute_dtype=torch.float32)
+    close(y, ey, 2e-2, "y")
+    assert rel_fro(y, ey) < 5e-3
+    close(final, ef, 2e-2, "final")
+    assert rel_fro(final, ef) < 5e-3
+    eg = S.fused_layout_grads_emulated(args, cfg["d_y"], cfg["d_final"], chunk=64,
+                                       model_dtype=torch.bfloat16)
+    for name, g, e in zip(NAMES, grads, eg):
+        if e.numel() == 0:
+            continue
+        close(g, e, 2e-2, name)
+        assert rel_fro(g, e) < 5e-3, (name, rel_fro(g, e))
+
+
+def test_scan_bf16_per_head_layout_matches_oracle():
+    # mamba3_flash_heads with bf16 q/k/v and per-head angle rates.
+    from mamba4_b200 import mamba3_flash_heads
+
+    batch, time, heads = 2, 150, 3
+    cfg = S.config_inputs(batch, time, heads, 64, 64, seed=31, per_head_angles=True)
+    rng = np.random.default_rng(32)
+    q = (rng.standard_normal((batch, time, heads, 64)) / 8).astype(np.float32)
+    k = (rng.standard_normal((batch, time, heads, 64)) / 8).astype(np.float32)
+    v = cfg["x"].reshape(batch, time, heads, 64)
+    qb = (1 + 0.1 * rng.normal(size=(heads, 64))).astype(np.float32)
+    kb = (1 + 0.1 * rng.normal(size=(heads, 64))).astype(np.float32)
+    arrays = [q, k, v, cfg["adt"], cfg["dt"], cfg["trap_logits"], cfg["angles"], qb, kb]
+    dev = "cuda:0"
+    leaves = []
+    for i, a in enumerate(arrays):
+        t = torch.tensor(a, device=dev)
+        if i < 3:
+            t = t.to(torch.bfloat16)
+        leaves.append(t.requires_grad_(True))
+    y, final = mamba3_flash_heads(*leaves[:7], q_bias=leaves[7], k_bias=leaves[8])
+    dy = torch.tensor(rng.standard_normal((batch, time, heads, 64)).astype(np.float32))
+    dfin = torch.tensor(rng.standard_normal((batch, heads, 64, 64)).astype(np.float32))
+    loss = (y.float() * dy.to(dev)).sum() + (final * dfin.to(dev)).sum()
+    grads = torch.autograd.grad(loss, leaves)
+    ref = [torch.tensor(a, dtype=torch.float32) for a in arrays]
+    for i in range(3):
+        ref[i] = ref[i].to(torch.bfloat16).float()
+    ey, ef = S.chunked_scan(*ref, chunk=64, model_dtype=torch.bfloat16, compute_dtype=torch.float32)
+    close(y, ey, 2e-2, "y")
+    assert rel_fro(y, ey) < 5e-3
+    close(final, ef, 2e-2, "final")
+    eg = S.chunked_scan_backward_emulated(*ref, dy, dfin, chunk=64, model_dtype=torch.bfloat16)
+    for i, (g, e) in enumerate(zip(grads, eg)):
+        close(g, e, 2e-2, str(i))
+        assert rel_fro(g, e) < 5e-3, (i, rel_fro(g, e))
+
+
 @pytest.mark.parametrize("length, heads_per_step", [(45, 2), (40, 4), (7, 1)])
 def test_reference_fused_test_shapes_through_padding(length, heads_per_step):
     # lm/tests/test_flashmamba.py:98-168 inputs: N = 8, P = 6, 2 angle pairs.
