@@ -971,6 +971,25 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
   load_tokens<P>(Os, LP, d_out, b, T, H, h, t0, tid);
   load_tokens<P>(Vs, LP, values, b, T, H, h, t0, tid);
   load_block(C0, P, c_start + (size_t(bh) * nch + ch) * P * KD, tid);
+  // The epilogue's dvar_t q_t term: loads start now, into registers
+  // (this thread's accumulator elements: rows row0 + g (+8), columns
+  // 32 half + 8 nt + 2 c (+1)).
+  float2 qv[4][2];
+  float dvr[2];
+  {
+    const int lane = tid & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int t = t0 + row0 + g + 8 * hf;
+      const bool live = t < T;
+      dvr[hf] = live ? d_var[(size_t(b) * T + t) * H + h] : 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+        qv[nt][hf] = live ? *reinterpret_cast<const float2*>(queries + ((size_t(b) * T + t) * H + h) * KD +
+                                                             32 * half + 8 * nt + 2 * c)
+                          : make_float2(0.f, 0.f);
+    }
+  }
   chunk_gates(tid, b, T, H, h, t0, beta, log_decay, pre, bet, ept);
   cp_wait();
   __syncthreads();
@@ -993,9 +1012,8 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
               [&](int k, int d) { return C0[k * LD + d]; });
   each<4>(row0, 32 * half, [&](int r, int d, int nt, int e) {
     const int t = t0 + r;
-    const bool live = t < T;
-    const float dv = live ? d_var[(size_t(b) * T + t) * H + h] : 0.f;
-    const float q = live ? queries[((size_t(b) * T + t) * H + h) * KD + d] : 0.f;
+    const float dv = dvr[e >> 1];
+    const float q = (e & 1) ? qv[nt][e >> 1].y : qv[nt][e >> 1].x;
     G[(size_t(bh) * Tp + t) * KD + d] = fmaf(dv, q, fmaf(ept[r], inh[nt][e], acc[nt][e]));
   });
 }
@@ -1166,6 +1184,18 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
   const int t0 = ch * CH, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = 16 * (warp & 3), qt = warp >> 2, rb = warp & 3;
   const int c64 = 16 * qt, cP = qt * (P / 4);
+  // S0 and C0 are needed only after phase 2: their loads start now, into
+  // registers, so the DRAM round trip overlaps phases 1-2.
+  constexpr int NS0 = KD * KD / 4 / CTG, NC0 = P * KD / 4 / CTG;
+  float4 sv[NS0], cv[NC0];
+  {
+    const float* s0 = s_start + (size_t(bh) * nsub + ch * (CH / SUB)) * KD * KD;
+    const float* c0 = c_start + (size_t(bh) * nch + ch) * P * KD;
+#pragma unroll
+    for (int i = 0; i < NS0; ++i) sv[i] = ld4(s0 + 4 * (tid + CTG * i));
+#pragma unroll
+    for (int i = 0; i < NC0; ++i) cv[i] = ld4(c0 + 4 * (tid + CTG * i));
+  }
   load_block<CTG>(Ys, CH, Y + (size_t(bh) * Tp + t0) * KD, tid);
   load_block<CTG>(Zs, CH, Z + (size_t(bh) * Tp + t0) * KD, tid);
   load_tokens<KD, CTG>(Ks, LD, keys, b, T, H, h, t0, tid);
@@ -1263,17 +1293,11 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
   }
   __syncthreads();
   // <dS_end, S0> + <dC_end, C0>, then S0 and C0 replace them in the tiles.
-  const float* s0 = s_start + (size_t(bh) * nsub + ch * (CH / SUB)) * KD * KD;
-  const float* c0 = c_start + (size_t(bh) * nch + ch) * P * KD;
   {
     // Each thread reads its own float4 slots of Sb / Cb, then overwrites the
     // same slots with S0 / C0 (no other thread touches them in between).
+    // (sv, cv were loaded at kernel entry.)
     constexpr int NS = KD * KD / 4 / CTG, NC = P * KD / 4 / CTG;
-    float4 sv[NS], cv[NC];
-#pragma unroll
-    for (int i = 0; i < NS; ++i) sv[i] = ld4(s0 + 4 * (tid + CTG * i));
-#pragma unroll
-    for (int i = 0; i < NC; ++i) cv[i] = ld4(c0 + 4 * (tid + CTG * i));
     float part = 0.f;
 #pragma unroll
     for (int i = 0; i < NS; ++i) {
