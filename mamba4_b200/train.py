@@ -103,7 +103,7 @@ class DataParallelTrainer:
         for group in self.optimizer.param_groups:
             group["lr"] = learning_rate(self.settings, self.step_index)
         self.optimizer.step()
-        self.optimizer.zero_grad(set_to_none=False)
+        self.optimizer.zero_grad(set_to_none=True)  # fresh gradients next step: no fill, no accumulate
         self.step_index += 1
         loss = self._all_reduce(numerator.detach().clone()) / total
         return loss, count, norm
