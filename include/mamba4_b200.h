@@ -270,8 +270,9 @@ int m4_rmsnorm_bwd(int rows, int features, const void* x, const float* scale, co
  * value dim 128, 1 to 16 heads. `rest` is the projection
  * after the gate columns: value [128h], key [64h], query [64h],
  * beta_raw [h], dt_raw [h], order_raw [h] per row (bf16, row stride
- * `stride`, a multiple of 8); d_rest is contiguous with 259h columns. The
- * gate view has row stride `gate_stride`; d_gate is contiguous [rows,128h]. */
+ * `stride`, a multiple of 8); d_rest has the same row stride. The gate view
+ * has row stride `gate_stride`, and so has d_gate [rows,128h]: the two
+ * gradients can be column slices of one projection-gradient buffer. */
 typedef struct {
   int batch, time, heads;
   int stride;       /* row stride of rest, elements */

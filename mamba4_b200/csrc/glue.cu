@@ -650,7 +650,7 @@ __global__ void __launch_bounds__(WPB * 32) mem_prep_bwd1(
     }
     if (lane < h) {
       const bf16* pr = rest + size_t(row) * d.stride + C;
-      bf16* gr = d_rest + size_t(row) * (C + 3 * h) + C;
+      bf16* gr = d_rest + size_t(row) * d.stride + C;
       const size_t i = size_t(row) * h + lane;
       const float bs = sigmoid(bf(pr + lane) + beta_bias[lane]);
       const float g_beta = d_beta[i] * d.beta_max * bs * (1.f - bs);
@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(256) mem_prep_bwd2(MemMix d, const bf16* __res
       dx0 = fmaf(w[j][0], g[3 - j].x, dx0);
       dx1 = fmaf(w[j][1], g[3 - j].y, dx1);
     }
-    st_bf2(d_rest + (size_t(b) * d.T + t) * (C + 3 * h) + ch, dx0, dx1);
+    st_bf2(d_rest + (size_t(b) * d.T + t) * d.stride + ch, dx0, dx1);
     // d_w[j] += d_conv[t] x[t - 3 + j]
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -982,7 +982,7 @@ __global__ void __launch_bounds__(WPB * 32) mem_post_bwd(
     st4(d_out + size_t(row) * 128 + 4 * lane, make_float4(dr[0] * cg, dr[1] * cg, dr[2] * cg, dr[3] * cg));
     st4(d_values + size_t(row) * 128 + 4 * lane, make_float4(dr[0] * dh, dr[1] * dh, dr[2] * dh, dr[3] * dh));
     st4(d_ordered + size_t(row) * 128 + 4 * lane, make_float4(dr[0] * om, dr[1] * om, dr[2] * om, dr[3] * om));
-    bf16* gg = d_gate + size_t(tok) * (128 * h) + hh * 128 + 4 * lane;
+    bf16* gg = d_gate + size_t(tok) * d.gstride + hh * 128 + 4 * lane;
     st_bf2(gg, dgz[0], dgz[1]);
     st_bf2(gg + 2, dgz[2], dgz[3]);
     go = warp_sum(go);

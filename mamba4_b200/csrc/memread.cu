@@ -789,23 +789,26 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
 // ---------------------------------------------------------------------------
 // Chunk-product kernels: one CTA of 8 warps per (batch, 64-token chunk, head)
 // (carry: one per (batch, head)). The products run on tensor cores as m16n8k8
-// TF32 MMAs on a two-term split of every fp32 operand (hi = tf32(x) rounded,
-// lo = x - hi passed as is: the tensor core reads its top 19 bits) with three
-// products per tile (lo*hi + hi*lo + hi*hi): about 2^-21 relative error per
-// product, inside the float32 tolerance of the reference (whose einsums run at
-// Precision.HIGHEST, lm/kernels/mamba4_fused.py:411-447). Skipping the second
-// rounding saves one ALU conversion per operand element, the pipe these
-// kernels saturate.
+// TF32 MMAs on a two-term split of every fp32 operand (hi = x rounded to 11
+// significant bits by Veltkamp splitting on the FMA pipe, lo = x - hi passed
+// as is: the tensor core reads its top 19 bits) with three products per tile
+// (lo*hi + hi*lo + hi*hi): about 2^-21 relative error per product, inside the
+// float32 tolerance of the reference (whose einsums run at
+// Precision.HIGHEST, lm/kernels/mamba4_fused.py:411-447). Neither half needs
+// an ALU conversion: the ALU pipe is the one these kernels saturate.
 // Warp w owns rows 16 (w % 4) .. +15 and column half w / 4 of each product.
 // ---------------------------------------------------------------------------
 constexpr int LD = 68;    // tile stride in floats (conflict-free A fragments)
 constexpr int CT = 256;   // threads per chunk CTA
 constexpr int CTG = 512;  // threads per chunk-gradient CTA (16 warps: 4 row blocks x 4 column quarters)
 
-M4_DEV uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+// High part of the two-term split on the FMA pipe (Veltkamp splitting with
+// the constant 2^13 + 1): x rounded to 11 significant bits, exactly a tf32
+// value, with x - hi exact. Three FP32 operations instead of one ALU
+// conversion: these kernels saturate the ALU pipe and leave the FMA pipe idle.
+M4_DEV uint32_t split_hi(float x) {
+  const float t = __fmul_rn(x, 8193.f);
+  return __float_as_uint(__fsub_rn(t, __fsub_rn(t, x)));
 }
 
 M4_DEV void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -828,13 +831,13 @@ M4_DEV void gemm3(float (&acc)[NT][4], int row0, int col0, FA fa, FB fb) {
     uint32_t ah[4], al[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      ah[i] = to_tf32(av[i]);
+      ah[i] = split_hi(av[i]);
       al[i] = __float_as_uint(av[i] - __uint_as_float(ah[i]));  // read as tf32 (low bits ignored)
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const float b0 = fb(k0 + c, col0 + 8 * nt + g), b1 = fb(k0 + c + 4, col0 + 8 * nt + g);
-      const uint32_t bh[2] = {to_tf32(b0), to_tf32(b1)};
+      const uint32_t bh[2] = {split_hi(b0), split_hi(b1)};
       const uint32_t bl[2] = {__float_as_uint(b0 - __uint_as_float(bh[0])),
                               __float_as_uint(b1 - __uint_as_float(bh[1]))};
       mma_tf32(acc[nt], al, bh);

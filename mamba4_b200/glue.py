@@ -148,9 +148,77 @@ def _memmix_dims(batch, time, heads, stride, gate_stride, beta_max):
     return _lib.MemMixDims(batch, time, heads, stride, gate_stride, beta_max)
 
 
+class GradSlab:
+    """One gradient buffer for a projection whose column slices feed several
+    glue kernels (the memory mixer's gate and rest columns): each backward
+    kernel writes its columns straight into it (the kernels store gradients
+    with the row stride of their input view), and the split returns it whole,
+    so autograd never builds the projection gradient from zero-filled
+    slice-sized pieces and an add."""
+
+    def __init__(self):
+        self.shape = None
+        self.buf = None
+
+    def attach(self, proj, used):
+        self.shape, self.dtype, self.device, self.used = proj.shape, proj.dtype, proj.device, used
+        self.buf = None
+
+    def buffer(self):
+        if self.buf is None:
+            self.buf = torch.empty(self.shape, dtype=self.dtype, device=self.device)
+            if self.used < self.shape[-1]:
+                self.buf[..., self.used:].zero_()  # columns no kernel reads get no gradient
+        return self.buf
+
+
+def _is_slice_of(base, t, col):
+    return (t is not None and t.dim() == base.dim() and t.data_ptr() == base.data_ptr() + col * base.element_size()
+            and t.stride()[:-1] == base.stride()[:-1] and t.stride(-1) == 1)
+
+
+class _SplitProjection(torch.autograd.Function):
+    """proj [B,T,W] -> (proj[..., :inner], proj[..., inner:inner + rest]) as views."""
+
+    @staticmethod
+    def forward(ctx, proj, inner, rest, slab):
+        slab.attach(proj, inner + rest)
+        ctx.slab, ctx.inner, ctx.rest = slab, inner, rest
+        return proj[..., :inner], proj[..., inner: inner + rest]
+
+    @staticmethod
+    def backward(ctx, d_gate, d_rest):
+        slab, inner, rest = ctx.slab, ctx.inner, ctx.rest
+        buf = slab.buf
+        slab.buf = None
+        if buf is not None and _is_slice_of(buf, d_gate, 0) and _is_slice_of(buf, d_rest, inner):
+            return buf, None, None, None
+        out = torch.zeros(slab.shape, dtype=slab.dtype, device=slab.device)
+        if d_gate is not None:
+            out[..., :inner] = d_gate
+        if d_rest is not None:
+            out[..., inner: inner + rest] = d_rest
+        return out, None, None, None
+
+
+def split_projection(proj, inner, rest, slab):
+    """Gate and rest column views of the memory mixer's projection that share
+    one gradient buffer (`slab`, passed on to the prep and post glue)."""
+    return _SplitProjection.apply(proj, inner, rest, slab)
+
+
+def _grad_view(slab, col, like, stride):
+    """Gradient buffer for a [B,T,F] view with row stride `stride`: a column
+    slice of the slab when there is one, else a fresh buffer of that stride."""
+    if slab is not None and slab.shape is not None:
+        return slab.buffer()[..., col: col + like.shape[-1]]
+    batch, time, width = like.shape
+    return torch.empty(batch, time, stride, dtype=torch.bfloat16, device=like.device)[..., :width]
+
+
 class _MemPrep(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, rest, conv_w, conv_b, beta_bias, dt_bias, a_log, heads, bound, beta_max):
+    def forward(ctx, rest, conv_w, conv_b, beta_bias, dt_bias, a_log, heads, bound, beta_max, slab, col):
         lib = _lib.load()
         batch, time, _ = rest.shape
         dims = _memmix_dims(batch, time, heads, _row_stride(rest), 0 + 128 * heads, beta_max)
@@ -166,6 +234,7 @@ class _MemPrep(torch.autograd.Function):
                    "m4_memmix_prep_fwd")
         ctx.save_for_backward(rest, conv_w, conv_b, beta_bias, dt_bias, a_log)
         ctx.cfg = (heads, bound, beta_max)
+        ctx.slab, ctx.col = slab, col
         return values, keys, queries, beta, log_decay, order_logit
 
     @staticmethod
@@ -188,7 +257,7 @@ class _MemPrep(torch.autograd.Function):
         d_order = g(d_order, (batch, time, heads))
         channels = 256 * heads
         d_conv = torch.empty(batch, time, channels, device=dev)
-        d_rest = torch.empty(batch, time, channels + 3 * heads, dtype=torch.bfloat16, device=dev)
+        d_rest = _grad_view(ctx.slab, ctx.col, rest, _row_stride(rest))
         part = torch.empty(lib.m4_memmix_partial_floats(ctypes.byref(dims)), device=dev)
         d_w, d_b = torch.empty_like(conv_w), torch.empty_like(conv_b)
         d_bb, d_dtb, d_al = torch.empty_like(beta_bias), torch.empty_like(dt_bias), torch.empty_like(a_log)
@@ -197,7 +266,7 @@ class _MemPrep(torch.autograd.Function):
                                                                  d_queries, d_beta, d_log_decay, d_order, d_conv,
                                                                  d_rest, part, d_w, d_b, d_bb, d_dtb, d_al)),
                                           _stream()), "m4_memmix_prep_bwd")
-        return d_rest, d_w, d_b, d_bb, d_dtb, d_al, None, None, None
+        return d_rest, d_w, d_b, d_bb, d_dtb, d_al, None, None, None, None, None
 
 
 class _OrderScan(torch.autograd.Function):
@@ -230,7 +299,7 @@ class _OrderScan(torch.autograd.Function):
 
 class _MemPost(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, out, var, values, ordered, gate, conf_scale, D, order_mix, scale, eps):
+    def forward(ctx, out, var, values, ordered, gate, conf_scale, D, order_mix, scale, eps, slab):
         lib = _lib.load()
         batch, time, heads, _ = values.shape
         dims = _memmix_dims(batch, time, heads, 259 * heads + (-259 * heads) % 8, _row_stride(gate), 1.0)
@@ -240,6 +309,7 @@ class _MemPost(torch.autograd.Function):
             out, var, values, ordered, gate, conf_scale, D, order_mix, scale, y, rstd)), _stream()),
             "m4_memmix_post_fwd")
         ctx.save_for_backward(out, var, values, ordered, gate, conf_scale, D, order_mix, scale, rstd)
+        ctx.slab = slab
         return y
 
     @staticmethod
@@ -251,27 +321,30 @@ class _MemPost(torch.autograd.Function):
         dev = values.device
         d_out, d_values, d_ordered = (torch.empty_like(values) for _ in range(3))
         d_var = torch.empty_like(var)
-        d_gate = torch.empty(batch, time, heads * 128, dtype=torch.bfloat16, device=dev)
+        d_gate = _grad_view(ctx.slab, 0, gate, _row_stride(gate))
         part = torch.empty(lib.m4_memmix_partial_floats(ctypes.byref(dims)), device=dev)
         d_cs, d_D, d_om, d_scale = (torch.empty_like(t) for t in (conf_scale, D, order_mix, scale))
         _lib.check(lib.m4_memmix_post_bwd(ctypes.byref(dims), *map(_lib.ptr, (
             out, var, values, ordered, gate, conf_scale, D, order_mix, scale, rstd,
             g.to(torch.bfloat16).contiguous(), d_out, d_var, d_values, d_ordered, d_gate, part, d_cs, d_D, d_om,
             d_scale)), _stream()), "m4_memmix_post_bwd")
-        return d_out, d_var, d_values, d_ordered, d_gate, d_cs, d_D, d_om, d_scale, None
+        return d_out, d_var, d_values, d_ordered, d_gate, d_cs, d_D, d_om, d_scale, None, None
 
 
-def memory_mixer_prep(rest, conv_w, conv_b, beta_bias, dt_bias, a_log, *, heads, bound, beta_max):
+def memory_mixer_prep(rest, conv_w, conv_b, beta_bias, dt_bias, a_log, *, heads, bound, beta_max, slab=None,
+                      col=0):
     """rest [B,T,259h] bf16 view (value|key|query|beta|dt|order columns) ->
     values [B,T,h,128], unit keys (shifted one token) and queries [B,T,h,64],
-    beta, log_decay, order logit [B,T,h] (float32)."""
+    beta, log_decay, order logit [B,T,h] (float32). With `slab` (from
+    split_projection) the gradient of `rest` is written into its columns
+    starting at `col`."""
     if not rest.is_cuda:
         raise RuntimeError("memory_mixer_prep runs on CUDA tensors only (no CPU path)")
     if rest.dtype != torch.bfloat16 or rest.shape[-1] != 259 * heads:
         raise ValueError("memory_mixer_prep expects bf16 rows of 259 * heads columns")
     f32 = lambda t: t.float().contiguous()  # noqa: E731
     return _MemPrep.apply(rest, f32(conv_w), f32(conv_b), f32(beta_bias), f32(dt_bias), f32(a_log), heads,
-                          float(bound), float(beta_max))
+                          float(bound), float(beta_max), slab, col)
 
 
 def order_scan(values, logit):
@@ -279,11 +352,13 @@ def order_scan(values, logit):
     return _OrderScan.apply(values.float().contiguous(), logit.float().contiguous())
 
 
-def memory_mixer_post(out, var, values, ordered, gate, conf_scale, D, order_mix, scale, eps):
-    """Confidence gate, D skip, order mix, read RMSNorm and SiLU gate -> bf16 [B,T,128h]."""
+def memory_mixer_post(out, var, values, ordered, gate, conf_scale, D, order_mix, scale, eps, slab=None):
+    """Confidence gate, D skip, order mix, read RMSNorm and SiLU gate -> bf16 [B,T,128h].
+    With `slab` (from split_projection) the gradient of `gate` is written into
+    its first columns."""
     f32 = lambda t: t.float().contiguous()  # noqa: E731
     return _MemPost.apply(f32(out), f32(var), f32(values), f32(ordered), gate, f32(conf_scale), f32(D),
-                          f32(order_mix), f32(scale), float(eps))
+                          f32(order_mix), f32(scale), float(eps), slab)
 
 
 # ---------------------------------------------------------------------------

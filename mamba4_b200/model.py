@@ -19,8 +19,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .flashmamba import Mamba3StepCache, mamba3_step, mamba3_step_cache
-from .glue import (head_cross_entropy, mamba_mixer_core, memory_mixer_post, memory_mixer_prep, order_scan,
-                   rms_norm_bf16)
+from .glue import (GradSlab, head_cross_entropy, mamba_mixer_core, memory_mixer_post, memory_mixer_prep,
+                   order_scan, rms_norm_bf16, split_projection)
 from .memory import selective_decode, selective_initial_state, selective_memory_fused
 
 
@@ -251,15 +251,16 @@ class SelectiveMemoryMixer(nn.Module):
             if proj.shape[-1] % 8:
                 # The fused glue reads rows with 16-byte loads.
                 proj = F.pad(proj, (0, -proj.shape[-1] % 8))
-            gate, rest = proj[..., : cfg.inner], proj[..., cfg.inner: cfg.inner + 259 * h]
+            slab = GradSlab()
+            gate, rest = split_projection(proj, cfg.inner, 259 * h, slab)
             value, key, query, beta, log_decay, order_logit = memory_mixer_prep(
                 rest, self.conv_weight, self.conv_bias, self.beta_bias, self.dt_bias, self.a_log, heads=h,
-                bound=self.bound, beta_max=cfg.memory_beta_max)
+                bound=self.bound, beta_max=cfg.memory_beta_max, slab=slab, col=cfg.inner)
             floor = cfg.floor_min + F.softplus(self.floor)
             res = selective_memory_fused(key, value, query, beta, log_decay, floor, chunk_size=cfg.chunk_size)
             ordered = order_scan(value, order_logit) if cfg.order_head else torch.zeros_like(value)
             read = memory_mixer_post(res.output, res.variance, value, ordered, gate, self.confidence_scale,
-                                     self.D, self.order_mix, self.read_norm.scale, cfg.norm_eps)
+                                     self.D, self.order_mix, self.read_norm.scale, cfg.norm_eps, slab=slab)
         return self.out_proj(read)
 
     def init_cache(self, batch, device=None):

@@ -179,3 +179,43 @@ def test_head_cross_entropy_matches_composition():
     gb = torch.autograd.grad(lb, (xb, wb), g)
     assert rel(ga[0], gb[0]) < 1e-2
     assert rel(ga[1], gb[1]) < 1e-2
+
+
+def test_memory_mixer_shared_gradient_buffer_is_exact():
+    """split_projection + GradSlab (the glue kernels write the gate / rest
+    gradients straight into one projection-gradient buffer) gives bitwise the
+    gradients of plain slicing (autograd assembling the projection gradient)."""
+    from mamba4_b200.glue import GradSlab, memory_mixer_post, memory_mixer_prep, split_projection
+
+    torch.manual_seed(5)
+    heads, inner, batch, time = 2, 256, 2, 96
+    width = inner + 259 * heads + 10  # trailing columns no kernel reads (row stride a multiple of 8)
+    proj0 = (torch.randn(batch, time, width, device="cuda") * 0.5).to(torch.bfloat16)
+    conv_w = torch.rand(4, 256 * heads, device="cuda")
+    conv_b = torch.randn(256 * heads, device="cuda") * 0.1
+    beta_bias, dt_bias, a_log = (torch.randn(heads, device="cuda") * 0.1 for _ in range(3))
+    cs, D, om = torch.full((heads,), 0.1, device="cuda"), torch.ones(heads, device="cuda"), torch.zeros(heads, device="cuda")
+    scale = torch.ones(128, device="cuda")
+    g_vals = torch.randn(batch, time, heads, 128, device="cuda")
+    g_y = torch.randn(batch, time, inner, device="cuda").to(torch.bfloat16)
+    out = torch.randn(batch, time, heads, 128, device="cuda")
+    var = torch.rand(batch, time, heads, device="cuda")
+
+    def run(use_slab):
+        proj = proj0.clone().requires_grad_()
+        if use_slab:
+            slab = GradSlab()
+            gate, rest = split_projection(proj, inner, 259 * heads, slab)
+        else:
+            slab = None
+            gate, rest = proj[..., :inner], proj[..., inner: inner + 259 * heads]
+        vals, keys, queries, beta, log_decay, order = memory_mixer_prep(
+            rest, conv_w, conv_b, beta_bias, dt_bias, a_log, heads=heads, bound=0.5, beta_max=1.0,
+            slab=slab, col=inner)
+        y = memory_mixer_post(out, var, vals, vals, gate, cs, D, om, scale, 1e-5, slab=slab)
+        loss = (vals * g_vals).sum() + (y.float() * g_y.float()).sum() + keys.sum() + beta.sum() + log_decay.sum()
+        return torch.autograd.grad(loss, proj)[0]
+
+    a, b = run(True), run(False)
+    assert torch.equal(a, b)
+    assert (a[..., inner + 259 * heads:] == 0).all()
