@@ -230,7 +230,10 @@ def launches(fn, steps):
     return None if n is None else n * steps
 
 
-def time_region(fn, steps, warmup, world):
+def time_region(fn, steps, warmup, world, streams=()):
+    """Device time (ms) of `steps` calls of fn on the current stream. Work
+    that fn issues on side `streams` (pipelined copies) is bracketed too: the
+    streams wait for the start event and the stop event waits for them."""
     import torch
 
     for _ in range(warmup):
@@ -239,9 +242,14 @@ def time_region(fn, steps, warmup, world):
     barrier(world)
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
     start.record()
+    for st in streams:
+        st.wait_stream(cur)
     for _ in range(steps):
         fn()
+    for st in streams:
+        cur.wait_stream(st)
     stop.record()
     torch.cuda.synchronize()
     barrier(world)
@@ -336,6 +344,88 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def measure_e2e_hotpath(m, s, dev, world, tokens, args):
+    import torch
+
+    pin = [{k: v.detach().cpu().pin_memory() for k, v in src.items()} for src in (m, s)]
+    h2d = sum(t.numel() * t.element_size() for d in pin for t in d.values())
+    slots = [[{k: torch.empty_like(v, device=dev) for k, v in d.items()} for d in pin] for _ in range(2)]
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    freed = [torch.cuda.Event(), torch.cuda.Event()]
+    out_host = [None, None]
+    state = {"i": 0, "d2h": 0}
+    compute = torch.cuda.current_stream(dev)
+
+    def e2e_step():
+        slot = state["i"] % 2
+        state["i"] += 1
+        dm, ds = slots[slot]
+        with torch.cuda.stream(copy_in):
+            copy_in.wait_event(freed[slot])
+            for dst, src in zip((dm, ds), pin):
+                for k, v in src.items():
+                    dst[k].copy_(v, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(copy_in)
+        compute.wait_event(ready)
+        leaves_m = {k: v.detach() for k, v in dm.items()}
+        leaves_s = {k: v.detach() for k, v in ds.items()}
+        res, mg = memread_step(leaves_m)
+        y, fin, sg = scan_step(leaves_s)
+        outs = [t.detach() for t in (res.output, res.variance, res.state.evidence, res.state.cross,
+                                     *mg, y, fin, *sg)]
+        freed[slot].record(compute)
+        if out_host[slot] is None:
+            out_host[slot] = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
+            state["d2h"] = sum(t.numel() * t.element_size() for t in outs)
+        done = torch.cuda.Event()
+        done.record(compute)
+        with torch.cuda.stream(copy_out):
+            copy_out.wait_event(done)
+            for h, t in zip(out_host[slot], outs):
+                t.record_stream(copy_out)
+                h.copy_(t, non_blocking=True)
+
+    n = max(2, args.steps // 2)
+    e2e_ms = max_over_ranks(time_region(e2e_step, n, args.warmup, world, streams=(copy_in, copy_out)),
+                            world) / n
+    return {"value": world * tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": state["d2h"], "ms_per_step": e2e_ms,
+            "pipelined": "inputs of step i+1 copied in and results of step i copied out "
+                         "while step i computes (two slots, two copy streams)"}
+
+
+def measure_decode(world, rank, local, batch=64, tokens=64, warmup=8):
+    """Cached decode of the 60M LM (`Mamba4LM.decode_step`, the reference's
+    decode_step): `batch` sequences on each rank, one token per call, eager
+    launches. Returns generated tokens/s over all ranks (max-over-ranks
+    device time) and the one-token latency."""
+    import torch
+
+    from mamba4_b200.model import CONFIGS, Mamba4LM
+
+    dev = torch.device("cuda", local)
+    cfg = CONFIGS["60m"]
+    torch.manual_seed(4321)
+    model = Mamba4LM(cfg).to(dev).eval()
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (tokens + warmup, batch), device=dev, generator=g)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        cache = model.init_cache(batch, device=dev)
+        it = iter(range(tokens + warmup))
+
+        def step():
+            nonlocal cache
+            _, cache = model.decode_step(ids[next(it)], cache)
+
+        ms = max_over_ranks(time_region(step, tokens, warmup, world), world) / tokens
+    del model, cache
+    torch.cuda.empty_cache()
+    return {"metric": "Mamba 4 60M cached decode tokens/s", "value": world * batch / (ms / 1000.0),
+            "unit": "tokens/s", "ms_per_token": ms, "batch_per_gpu": batch, "tokens": tokens,
+            "warmup": warmup, "launch": "eager (no CUDA graph)"}
+
+
 def run_ours(args):
     import torch
 
@@ -385,34 +475,14 @@ def run_ours(args):
 
     scan_fwd_ms, scan_bwd_ms = op_times(sfwd, sbwd)
 
-    # End to end through the public API with host buffers.
+    # End to end through the public API with host buffers, pipelined: step
+    # i+1's inputs cross PCIe on a copy stream while step i computes, and
+    # step i's results come back on a second copy stream (two device input
+    # slots, two pinned output slots). Every step still copies all of its
+    # inputs in and all of its results out inside the timed region.
     e2e = None
     if not args.no_e2e:
-        pin = {k: v.detach().cpu().pin_memory() for k, v in m.items()}
-        spin = {k: v.detach().cpu().pin_memory() for k, v in s.items()}
-        h2d = sum(t.numel() * t.element_size() for t in list(pin.values()) + list(spin.values()))
-        out_host = {}
-        d2h = 0
-
-        def e2e_step():
-            nonlocal d2h
-            dm = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
-            ds = {k: v.to(dev, non_blocking=True) for k, v in spin.items()}
-            res, mg = memread_step(dm)
-            y, fin, sg = scan_step(ds)
-            outs = [res.output, res.variance, res.state.evidence, res.state.cross, *mg, y, fin, *sg]
-            if not out_host:
-                for i, t in enumerate(outs):
-                    out_host[i] = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-                d2h = sum(t.numel() * t.element_size() for t in outs)
-            for i, t in enumerate(outs):
-                out_host[i].copy_(t, non_blocking=True)
-
-        e2e_ms = max_over_ranks(time_region(e2e_step, max(2, args.steps // 2), args.warmup, world), world)
-        e2e_ms /= max(2, args.steps // 2)
-        e2e = {"value": world * tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms}
-
+        e2e = measure_e2e_hotpath(m, s, dev, world, tokens, args)
     pk = peaks()
     token_heads = mem_tokens * mem_cfg["heads"]
     fwd_bytes = MEM_FWD_BYTES * token_heads
@@ -467,6 +537,8 @@ def run_ours(args):
         step = e2e_step = None
         torch.cuda.empty_cache()
         line["lm60m"] = measure_lm(args, "lm60m", world, rank, local)
+    if not args.no_decode and args.workload == "hotpath":
+        line["decode"] = measure_decode(world, rank, local)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -582,6 +654,8 @@ def main():
                    help="LM workloads: sequences per GPU (default: the configuration's; smaller for ncu captures)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-decode", action="store_true",
+                   help="hot-path workload: skip the cached-decode measurement of the 60M LM")
     p.add_argument("--no-lm", action="store_true",
                    help="hot-path workload: skip the nested data-parallel 60M LM step measurement")
     args = p.parse_args()

@@ -1389,12 +1389,35 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
 }
 
 
-__global__ void floor_reduce_kernel(int rows, int H, const float* __restrict__ part, float* __restrict__ d_floor) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= H * KD) return;
+// d_floor[c] = sum over rows of part[row][c], c < H*64. A block of 32 warps
+// owns 32 columns (lane = column: coalesced rows); warp w sums rows w, w + 32,
+// ... with eight loads in flight, and the 32 warp sums combine in a fixed
+// order (deterministic).
+__global__ void __launch_bounds__(1024) floor_reduce_kernel(int rows, int H, const float* __restrict__ part,
+                                                            float* __restrict__ d_floor) {
+  __shared__ float ws[32][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, c = blockIdx.x * 32 + lane;
+  const int cols = H * KD;
   float s = 0.f;
-  for (int r = 0; r < rows; ++r) s += part[size_t(r) * H * KD + idx];
-  d_floor[idx] = s;
+  if (c < cols) {
+    int r = warp;
+    for (; r + 7 * 32 < rows; r += 8 * 32) {
+      float a[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = part[size_t(r + 32 * j) * cols + c];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += a[j];
+    }
+    for (; r < rows; r += 32) s += part[size_t(r) * cols + c];
+  }
+  ws[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && c < cols) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 32; ++w) t += ws[w][lane];
+    d_floor[c] = t;
+  }
 }
 
 template <int P>
@@ -1463,7 +1486,7 @@ int backward(const M4MemDims& d, const float* keys, const float* values, const f
   cudaFuncSetAttribute(grads_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(gsm));
   grads_kernel<P><<<bh * z.nch, CTG, gsm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Zb, Ss,
                                                 Cs, sb, cb, d_out, d_var, dk, dv, dq, dbeta, dlog, fl);
-  floor_reduce_kernel<<<(z.H * KD + 255) / 256, 256, 0, st>>>(z.B * z.nch, z.H, fl, dfloor);
+  floor_reduce_kernel<<<(z.H * KD + 31) / 32, 1024, 0, st>>>(z.B * z.nch, z.H, fl, dfloor);
   return launch_status();
 }
 

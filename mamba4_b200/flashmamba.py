@@ -230,17 +230,17 @@ def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias)
     if state_dim > STATE_DIM or value_dim > HEAD_DIM:
         raise ValueError(f"Scan supports state and head dims up to {STATE_DIM}")
     model = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
-    pad_n = STATE_DIM - state_dim
-    c = F.pad(c.to(model), (0, pad_n)).contiguous()
-    b = F.pad(b.to(model), (0, pad_n)).contiguous()
-    xp = F.pad(x.to(model).reshape(batch, heads, value_dim), (0, HEAD_DIM - value_dim))
+    pad_n, pad_p = STATE_DIM - state_dim, HEAD_DIM - value_dim
+    c = _pad(c.to(model), (0, pad_n)).contiguous()
+    b = _pad(b.to(model), (0, pad_n)).contiguous()
+    xp = _pad(x.to(model).reshape(batch, heads, value_dim), (0, pad_p))
     xp = xp.reshape(batch, heads * HEAD_DIM).contiguous()
     f32 = lambda a: a.float().contiguous()  # noqa: E731
-    qb = None if q_bias is None else F.pad(f32(q_bias).reshape(heads, state_dim), (0, pad_n)).contiguous()
-    kb = None if k_bias is None else F.pad(f32(k_bias).reshape(heads, state_dim), (0, pad_n)).contiguous()
-    st = F.pad(f32(cache.state), (0, HEAD_DIM - value_dim, 0, pad_n)).contiguous()
-    pk = F.pad(f32(cache.previous_keys), (0, pad_n)).contiguous()
-    pv = F.pad(f32(cache.previous_values), (0, HEAD_DIM - value_dim)).contiguous()
+    qb = None if q_bias is None else _pad(f32(q_bias).reshape(heads, state_dim), (0, pad_n)).contiguous()
+    kb = None if k_bias is None else _pad(f32(k_bias).reshape(heads, state_dim), (0, pad_n)).contiguous()
+    st = _pad(f32(cache.state), (0, pad_p, 0, pad_n)).contiguous()
+    pk = _pad(f32(cache.previous_keys), (0, pad_n)).contiguous()
+    pv = _pad(f32(cache.previous_values), (0, pad_p)).contiguous()
     ph = f32(cache.phase)
     y = torch.empty_like(xp)
     st_out, pk_out, pv_out, ph_out = (torch.empty_like(t) for t in (st, pk, pv, ph))

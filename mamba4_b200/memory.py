@@ -207,8 +207,11 @@ def selective_decode(state, key, value, query, beta, log_decay, floor, solver=No
     floor = torch.broadcast_to(torch.as_tensor(floor, dtype=torch.float32, device=dev), (heads, dim))
     ev = torch.as_tensor(state.evidence, dtype=torch.float32, device=dev)
     cr = torch.as_tensor(state.cross, dtype=torch.float32, device=dev)
-    ev = F.pad(ev, (0, KEY_DIM - dim, 0, KEY_DIM - dim)).contiguous()
-    cr = F.pad(cr, (0, KEY_DIM - dim, 0, pv - value_dim)).contiguous()
+    if dim != KEY_DIM:
+        ev = F.pad(ev, (0, KEY_DIM - dim, 0, KEY_DIM - dim))
+    if dim != KEY_DIM or value_dim != pv:
+        cr = F.pad(cr, (0, KEY_DIM - dim, 0, pv - value_dim))
+    ev, cr = ev.contiguous(), cr.contiguous()
     k = _pad_last(key, KEY_DIM).contiguous()
     q = _pad_last(query, KEY_DIM).contiguous()
     v = _pad_last(value, pv).contiguous()
