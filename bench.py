@@ -397,12 +397,13 @@ def measure_e2e_hotpath(m, s, dev, world, tokens, args):
 
 def measure_decode(world, rank, local, batch=64, tokens=64, warmup=8):
     """Cached decode of the 60M LM (`Mamba4LM.decode_step`, the reference's
-    decode_step): `batch` sequences on each rank, one token per call, eager
-    launches. Returns generated tokens/s over all ranks (max-over-ranks
-    device time) and the one-token latency."""
+    decode_step): `batch` sequences on each rank, one token per call, as one
+    CUDA-graph replay (`GraphedDecoder`) and as eager launches. Returns
+    generated tokens/s over all ranks (max-over-ranks device time) and the
+    one-token latency of each."""
     import torch
 
-    from mamba4_b200.model import CONFIGS, Mamba4LM
+    from mamba4_b200.model import CONFIGS, GraphedDecoder, Mamba4LM
 
     dev = torch.device("cuda", local)
     cfg = CONFIGS["60m"]
@@ -410,20 +411,26 @@ def measure_decode(world, rank, local, batch=64, tokens=64, warmup=8):
     model = Mamba4LM(cfg).to(dev).eval()
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     ids = torch.randint(0, cfg.vocab_size, (tokens + warmup, batch), device=dev, generator=g)
+
+    dec = GraphedDecoder(model, batch, device=dev)
+    it = iter(range(tokens + warmup))
+    graph_ms = max_over_ranks(time_region(lambda: dec.step(ids[next(it)]), tokens, warmup, world),
+                              world) / tokens
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         cache = model.init_cache(batch, device=dev)
         it = iter(range(tokens + warmup))
 
-        def step():
+        def eager():
             nonlocal cache
             _, cache = model.decode_step(ids[next(it)], cache)
 
-        ms = max_over_ranks(time_region(step, tokens, warmup, world), world) / tokens
-    del model, cache
+        eager_ms = max_over_ranks(time_region(eager, tokens, warmup, world), world) / tokens
+    del model, cache, dec
     torch.cuda.empty_cache()
-    return {"metric": "Mamba 4 60M cached decode tokens/s", "value": world * batch / (ms / 1000.0),
-            "unit": "tokens/s", "ms_per_token": ms, "batch_per_gpu": batch, "tokens": tokens,
-            "warmup": warmup, "launch": "eager (no CUDA graph)"}
+    return {"metric": "Mamba 4 60M cached decode tokens/s", "value": world * batch / (graph_ms / 1000.0),
+            "unit": "tokens/s", "ms_per_token": graph_ms, "batch_per_gpu": batch, "tokens": tokens,
+            "warmup": warmup, "launch": "one CUDA graph per token (GraphedDecoder)",
+            "eager": {"value": world * batch / (eager_ms / 1000.0), "ms_per_token": eager_ms}}
 
 
 def run_ours(args):
@@ -643,13 +650,29 @@ def run_lm(args):
         dist.destroy_process_group()
 
 
+def run_decode(args):
+    import torch
+
+    world, rank, local = setup_dist(args.gpus)
+    torch.cuda.set_device(local)
+    line = measure_decode(world, rank, local, batch=args.lm_batch or 64)
+    line.update(n_gpus=world, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16",
+                data="synthetic (uniform-random token ids)", config={"workload": "60M cached decode"})
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["hotpath", "small", "profile", "lm60m", "lm125m"], default="hotpath")
+    p.add_argument("--workload", choices=["hotpath", "small", "profile", "lm60m", "lm125m", "decode"], default="hotpath")
     p.add_argument("--lm-batch", type=int, default=0,
                    help="LM workloads: sequences per GPU (default: the configuration's; smaller for ncu captures)")
     p.add_argument("--no-e2e", action="store_true")
@@ -663,6 +686,8 @@ def main():
         run_reference(args)
     elif args.workload.startswith("lm"):
         run_lm(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_ours(args)
 

@@ -378,5 +378,69 @@ class Mamba4LM(nn.Module):
         return F.linear(x, self.embedding.weight.to(x.dtype)).float(), new
 
 
+def _cache_tensors(cache):
+    """The tensors of a layer-cache tree (lists, dicts and named tuples) in a
+    fixed order."""
+    if isinstance(cache, torch.Tensor):
+        return [cache]
+    if isinstance(cache, dict):
+        return [t for k in sorted(cache) for t in _cache_tensors(cache[k])]
+    return [t for item in cache for t in _cache_tensors(item)]
+
+
+class GraphedDecoder:
+    """`Mamba4LM.decode_step` captured once as a CUDA graph (the B200
+    counterpart of the reference's jitted decode, `lm/models/mamba4.py:507-524`).
+
+    A decode step is a few hundred small launches (projections, the glue
+    arithmetic, `m4_scan_step`, `m4_memread_decode`); replaying them as one
+    graph removes the per-launch host cost. The cache lives in static buffers
+    that the graph reads and then overwrites with the next cache, so
+    `step(tokens)` returns the same logits as eager `decode_step` calls from
+    `model.init_cache(batch)` (the graph runs the same kernels on the same
+    operands). `logits` is a static buffer, overwritten by the next step.
+    Parameters are read in place at every replay, so weight updates are seen.
+    """
+
+    def __init__(self, model: Mamba4LM, batch: int, device=None, dtype=torch.bfloat16):
+        self.model, self.batch, self.dtype = model, batch, dtype
+        device = torch.device("cuda" if device is None else device)
+        self._initial = model.init_cache(batch, device=device)
+        self.cache = model.init_cache(batch, device=device)
+        self._static = _cache_tensors(self.cache)
+        self.tokens = torch.zeros(batch, dtype=torch.long, device=device)
+        current = torch.cuda.current_stream(device)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(current)
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                self._body()
+        current.wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = self._body()
+        self.reset()
+
+    @torch.no_grad()
+    def _body(self):
+        with torch.autocast("cuda", dtype=self.dtype):
+            logits, new = self.model.decode_step(self.tokens, self.cache)
+        for dst, src in zip(self._static, _cache_tensors(new)):
+            if dst.data_ptr() != src.data_ptr():
+                dst.copy_(src)
+        return logits
+
+    def reset(self):
+        """Back to the empty cache (a new batch of sequences)."""
+        for dst, src in zip(self._static, _cache_tensors(self._initial)):
+            dst.copy_(src)
+
+    def step(self, tokens: torch.Tensor) -> torch.Tensor:
+        """tokens [batch] -> logits [batch, vocab] float32 (static buffer)."""
+        self.tokens.copy_(tokens, non_blocking=True)
+        self.graph.replay()
+        return self.logits
+
+
 def parameter_count(model: nn.Module) -> int:
     return sum(p.numel() for p in model.parameters())

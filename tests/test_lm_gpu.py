@@ -74,3 +74,25 @@ def test_cached_decode_matches_prefill_logits():
     assert err < 2e-2, float(err)
     assert (decoded - logits).abs().max() < 0.05 * logits.abs().max()
     assert (decoded.argmax(-1) == logits.argmax(-1)).float().mean() > 0.9
+
+
+def test_graphed_decode_matches_eager_decode():
+    """The CUDA-graph decoder replays exactly the eager decode's kernels:
+    logits and cache agree bit for bit over a sequence, and reset() returns
+    to the empty cache."""
+    from mamba4_b200.model import GraphedDecoder, _cache_tensors
+
+    torch.manual_seed(5)
+    model = Mamba4LM(TINY).cuda().eval()
+    tokens = (torch.arange(3 * 9, device="cuda").reshape(3, 9) * 7) % TINY.vocab_size
+    dec = GraphedDecoder(model, 3)
+    for _ in range(2):
+        cache = model.init_cache(3, device="cuda")
+        for i in range(tokens.shape[1]):
+            with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+                ref, cache = model.decode_step(tokens[:, i], cache)
+            got = dec.step(tokens[:, i])
+            assert torch.equal(got, ref), i
+        for a, b in zip(_cache_tensors(dec.cache), _cache_tensors(cache)):
+            assert torch.equal(a, b)
+        dec.reset()
