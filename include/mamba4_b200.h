@@ -324,6 +324,24 @@ int m4_memmix_post_bwd(const M4MemMixDims* dims, const float* out, const float* 
                        float* d_conf_scale, float* d_D, float* d_order_mix, float* d_scale,
                        void* stream);
 
+/* One cached decode token of the mixer glue (the cache branch of
+ * lm/models/mamba4.py:127-337). prep_step: `rest` holds, per sequence,
+ * `time` rows (the conv history, oldest first, then the current token; row
+ * stride `stride`); only the current token is written ([batch, h, ...]),
+ * with its own unit key, not shifted - the caller reads with the key it
+ * carried from the previous token. post_step (time = 1): as post_fwd, with
+ * the order head advanced in place of a precomputed order output:
+ * o = s o_prev + (1 - s) v, s = sigmoid(order_logit) (order_prev and
+ * order_out [batch, h, 128] both NULL: no order head, o = 0); no rstd. */
+int m4_memmix_prep_step(const M4MemMixDims* dims, const void* rest, const float* conv_w,
+                        const float* conv_b, float bound, const float* beta_bias, const float* dt_bias,
+                        const float* a_log, float* values, float* keys, float* queries, float* beta,
+                        float* log_decay, float* order_logit, void* stream);
+int m4_memmix_post_step(const M4MemMixDims* dims, float eps, const float* out, const float* var,
+                        const float* values, const float* order_logit, const float* order_prev,
+                        float* order_out, const void* gate, const float* conf_scale, const float* D,
+                        const float* order_mix, const float* scale, void* y, void* stream);
+
 /* Softmax cross-entropy over bf16 logits [rows, vocab], rows `ld` elements
  * apart (ld >= vocab, a multiple of 8; columns past vocab are ignored), with
  * int64 targets (lm/train.py:81-87): loss and log-sum-exp [rows]; targets

@@ -499,6 +499,10 @@ namespace glue {
 struct MemMix {
   int B, T, heads, stride, gstride;  // gstride: row stride of the gate view
   float beta_max;
+  // prep, one-token step: only the last token of each row window (T rows of
+  // history + current) is written, and its key is not shifted (the caller
+  // carries the previous token's key).
+  int step;
 };
 
 M4_DEV float silu_grad(float x) {
@@ -545,19 +549,21 @@ __global__ void __launch_bounds__(WPB * 32) mem_prep_fwd(
   float* w_s = smem;
   float* bias_s = smem + 4 * C;
   stage_conv(conv_w, conv_b, bound, C, w_s, bias_s);
-  const int lane = threadIdx.x & 31;
-  for (int row = gwarp(); row < d.B * d.T; row += nwarps()) {
-    const int b = row / d.T, t = row % d.T;
+  const int lane = threadIdx.x & 31, span = d.step ? 1 : d.T;
+  for (int row = gwarp(); row < d.B * span; row += nwarps()) {
+    // Output row `row` is token (b, t); inputs are read at rows b T + s.
+    const int b = row / span, t = d.step ? d.T - 1 : row % span;
+    const int kt = d.step ? t : t - 1;  // token whose key this row writes
     for (int k = 0; k < h; ++k) {
       // Channel group lane + 32k: value below 16h, key below 24h, query above.
       const int cg = lane + 32 * k, ch = 8 * cg;
       const int cls = cg < 16 * h ? 0 : (cg < 24 * h ? 1 : 2);
       float o[8];
-      if (cls == 1 && t == 0) {
+      if (cls == 1 && kt < 0) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] = 0.f;
       } else {
-        conv8(d, rest, b, cls == 1 ? t - 1 : t, ch, w_s, bias_s, C, o);
+        conv8(d, rest, b, cls == 1 ? kt : t, ch, w_s, bias_s, C, o);
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] *= sigmoid(o[e]);
       }
@@ -575,7 +581,7 @@ __global__ void __launch_bounds__(WPB * 32) mem_prep_fwd(
       st4(dst + 4, make_float4(o[4] * r, o[5] * r, o[6] * r, o[7] * r));
     }
     if (lane < h) {
-      const bf16* pr = rest + size_t(row) * d.stride + C;
+      const bf16* pr = rest + (size_t(b) * d.T + t) * d.stride + C;
       const size_t i = size_t(row) * h + lane;
       beta[i] = d.beta_max * sigmoid(bf(pr + lane) + beta_bias[lane]);
       log_decay[i] = -expf(a_log[lane]) * softplus(bf(pr + h + lane) + dt_bias[lane]);
@@ -895,18 +901,37 @@ __global__ void __launch_bounds__(128) order_bwd(MemMix d, const float* __restri
 // After the read: r = out c + D v + sigmoid(order_mix) o with the confidence
 // gate c = sigmoid(1 - conf_scale log1p(var)); y = rd(rd(rmsnorm(r) s) silu(gate)).
 // One warp per (b, t, head) row of 128 values (float4 per lane).
+// STEP (one cached token): the order head advances here,
+// o = s o_prev + (1 - s) v with s = sigmoid(order logit) (`ordered` holds the
+// logits [rows], o_prev / order_out the carried order state; o_prev null:
+// no order head, o = 0), and rstd is not written.
+template <bool STEP>
 __global__ void __launch_bounds__(WPB * 32) mem_post_fwd(
     MemMix d, float eps, const float* __restrict__ out, const float* __restrict__ var,
     const float* __restrict__ values, const float* __restrict__ ordered, const bf16* __restrict__ gate,
     const float* __restrict__ conf_scale, const float* __restrict__ Dskip, const float* __restrict__ order_mix,
-    const float* __restrict__ scale, bf16* __restrict__ y, float* __restrict__ rstd) {
+    const float* __restrict__ scale, bf16* __restrict__ y, float* __restrict__ rstd,
+    const float* __restrict__ order_prev = nullptr, float* __restrict__ order_out = nullptr) {
   const int lane = threadIdx.x & 31, h = d.heads;
   for (int row = gwarp(); row < d.B * d.T * h; row += nwarps()) {
     const int hh = row % h, tok = row / h;
     const float cg = sigmoid(1.f - conf_scale[hh] * log1pf(var[row]));
     const float dh = Dskip[hh], om = sigmoid(order_mix[hh]);
     const float4 o4 = ld4(out + size_t(row) * 128 + 4 * lane), v4 = ld4(values + size_t(row) * 128 + 4 * lane);
-    const float4 q4 = ld4(ordered + size_t(row) * 128 + 4 * lane);
+    float4 q4;
+    if constexpr (STEP) {
+      if (order_prev != nullptr) {
+        const float sg = sigmoid(ordered[row]), fl = 1.f - sg;
+        const float4 p4 = ld4(order_prev + size_t(row) * 128 + 4 * lane);
+        q4 = make_float4(sg * p4.x + fl * v4.x, sg * p4.y + fl * v4.y, sg * p4.z + fl * v4.z,
+                         sg * p4.w + fl * v4.w);
+        st4(order_out + size_t(row) * 128 + 4 * lane, q4);
+      } else {
+        q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    } else {
+      q4 = ld4(ordered + size_t(row) * 128 + 4 * lane);
+    }
     const float r[4] = {fmaf(om, q4.x, fmaf(dh, v4.x, o4.x * cg)), fmaf(om, q4.y, fmaf(dh, v4.y, o4.y * cg)),
                         fmaf(om, q4.z, fmaf(dh, v4.z, o4.z * cg)), fmaf(om, q4.w, fmaf(dh, v4.w, o4.w * cg))};
     const float ss = warp_sum(r[0] * r[0] + r[1] * r[1] + r[2] * r[2] + r[3] * r[3]);
@@ -923,7 +948,7 @@ __global__ void __launch_bounds__(WPB * 32) mem_post_fwd(
     bf16* dst = y + size_t(row) * 128 + 4 * lane;
     st_bf2(dst, o[0], o[1]);
     st_bf2(dst + 2, o[2], o[3]);
-    if (lane == 0) rstd[row] = rs;
+    if (!STEP && lane == 0) rstd[row] = rs;
   }
 }
 
@@ -1039,6 +1064,7 @@ inline MemMix make_memmix(const M4MemMixDims& m) {
   MemMix d;
   d.B = m.batch; d.T = m.time; d.heads = m.heads; d.stride = m.stride; d.gstride = m.gate_stride;
   d.beta_max = m.beta_max;
+  d.step = 0;
   return d;
 }
 
@@ -1150,9 +1176,44 @@ extern "C" int m4_memmix_post_fwd(const M4MemMixDims* m, float eps, const float*
   if (!all_aligned16(out, var, values, ordered, gate, scale, y, rstd)) return M4_ERR_ALIGN;
   const MemMix d = make_memmix(*m);
   const int rows = d.B * d.T * d.heads;
-  mem_post_fwd<<<mem_blocks(rows, d.heads), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+  mem_post_fwd<false><<<mem_blocks(rows, d.heads), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
       d, eps, out, var, values, ordered, static_cast<const bf16*>(gate), conf_scale, D, order_mix, scale,
       static_cast<bf16*>(y), rstd);
+  return launch_status();
+}
+
+extern "C" int m4_memmix_prep_step(const M4MemMixDims* m, const void* rest, const float* conv_w,
+                                   const float* conv_b, float bound, const float* beta_bias, const float* dt_bias,
+                                   const float* a_log, float* values, float* keys, float* queries, float* beta,
+                                   float* log_decay, float* order_logit, void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (!all_aligned16(rest, conv_w, values, keys, queries, beta, log_decay, order_logit)) return M4_ERR_ALIGN;
+  MemMix d = make_memmix(*m);
+  d.step = 1;
+  const size_t smem = size_t(5) * 256 * d.heads * sizeof(float);
+  cudaFuncSetAttribute(mem_prep_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  mem_prep_fwd<<<row_blocks(d.B), WPB * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+      d, static_cast<const bf16*>(rest), conv_w, conv_b, bound, beta_bias, dt_bias, a_log, values, keys, queries,
+      beta, log_decay, order_logit);
+  return launch_status();
+}
+
+extern "C" int m4_memmix_post_step(const M4MemMixDims* m, float eps, const float* out, const float* var,
+                                   const float* values, const float* order_logit, const float* order_prev,
+                                   float* order_out, const void* gate, const float* conf_scale, const float* D,
+                                   const float* order_mix, const float* scale, void* y, void* stream) {
+  const int st = check_mem(m);
+  if (st != M4_OK) return st;
+  if (m->time != 1) return M4_ERR_DIMS;
+  if ((order_prev == nullptr) != (order_out == nullptr)) return M4_ERR_DIMS;
+  if (!all_aligned16(out, var, values, gate, scale, y)) return M4_ERR_ALIGN;
+  if (order_prev != nullptr && !all_aligned16(order_logit, order_prev, order_out)) return M4_ERR_ALIGN;
+  const MemMix d = make_memmix(*m);
+  const int rows = d.B * d.heads;
+  mem_post_fwd<true><<<mem_blocks(rows, d.heads), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      d, eps, out, var, values, order_logit, static_cast<const bf16*>(gate), conf_scale, D, order_mix, scale,
+      static_cast<bf16*>(y), nullptr, order_prev, order_out);
   return launch_status();
 }
 

@@ -738,8 +738,8 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
   for (int n = 0; n < 8; ++n) rc[n] = 0.f;
   factor_all<0>(A, wr, rc, sm, a, b);
   float vpart = 0.f, kkeep[2];
-  kkeep[0] = sm.w[lane];
-  kkeep[1] = sm.w[lane + 32];
+  kkeep[0] = sm.w[2 * lane];
+  kkeep[1] = sm.w[2 * lane + 1];
   __syncwarp();
   if (a == 0) {
 #pragma unroll
@@ -766,23 +766,45 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
   back_substitute(A, sm.w, sm.y, a, b);
   __syncwarp();
   if (lane == 0) variance[bh] = var;
-  // C' = lam C + beta v k^T row by row (lanes over key coordinates 2l, 2l+1
-  // ... as lane, lane + 32), output_p = C'[p] . y.
-  const float y0 = sm.y[lane], y1 = sm.y[lane + 32];
-  const float bk0 = bet * kkeep[0], bk1 = bet * kkeep[1];
-  const float* csrc = cross + size_t(bh) * P * KD;
-  float* cdst = cross_out + size_t(bh) * P * KD;
+  // C' = lam C + beta v k^T, lane l on key coordinates 2l, 2l+1, rows in
+  // batches of R whose loads are issued before the previous batch's stores
+  // (cross_out may alias cross: row p is always read before it is written,
+  // and a batch never reads a row an earlier batch wrote), so the DRAM
+  // round trips overlap. output_p = C'[p] . y.
+  const float2 yv = *reinterpret_cast<const float2*>(&sm.y[2 * lane]);
+  const float2 bk = make_float2(bet * kkeep[0], bet * kkeep[1]);
+  const float* csrc = cross + size_t(bh) * P * KD + 2 * lane;
+  float* cdst = cross_out + size_t(bh) * P * KD + 2 * lane;
   const float* vrow = value + size_t(bh) * P;
   float* orow = out + size_t(bh) * P;
-#pragma unroll 4
-  for (int p = 0; p < P; ++p) {
-    const float vp = vrow[p];
-    const float c0 = fmaf(bk0, vp, lam * csrc[p * KD + lane]);
-    const float c1 = fmaf(bk1, vp, lam * csrc[p * KD + lane + 32]);
-    const float o = warp_sum(fmaf(c0, y0, c1 * y1));
-    cdst[p * KD + lane] = c0;
-    cdst[p * KD + lane + 32] = c1;
-    if (lane == 0) orow[p] = o;
+  constexpr int R = 16;
+  float2 cur[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) cur[r] = *reinterpret_cast<const float2*>(csrc + r * KD);
+#pragma unroll 1
+  for (int p0 = 0; p0 < P; p0 += R) {
+    float2 nxt[R];
+    if (p0 + R < P) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) nxt[r] = *reinterpret_cast<const float2*>(csrc + (p0 + R + r) * KD);
+    }
+    float part[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float vp = vrow[p0 + r];
+      const float2 c = make_float2(fmaf(bk.x, vp, lam * cur[r].x), fmaf(bk.y, vp, lam * cur[r].y));
+      *reinterpret_cast<float2*>(cdst + (p0 + r) * KD) = c;
+      part[r] = fmaf(c.x, yv.x, c.y * yv.y);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float o = warp_sum(part[r]);
+      if (lane == 0) orow[p0 + r] = o;
+    }
+    if (p0 + R < P) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) cur[r] = nxt[r];
+    }
   }
 }
 

@@ -15,7 +15,7 @@ import ctypes
 import torch
 
 from . import _lib
-from .flashmamba import scan_backward, scan_forward
+from .flashmamba import mamba3_step, scan_backward, scan_forward
 
 
 def _stream() -> int:
@@ -96,6 +96,45 @@ def mamba_mixer_core(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, *, inne
         proj = torch.nn.functional.pad(proj, (0, -width % 8))
     return _MambaMixerCore.apply(proj.contiguous(), f32(b_scale), f32(c_scale), f32(dt_bias), f32(D),
                                  f32(q_bias), f32(k_bias), inner, heads, angles, eps)
+
+
+@torch.no_grad()
+def mamba_mixer_step(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, cache, *, inner, heads, angles, eps):
+    """One cached token of the mixer core (`_Mamba3StepMixer`,
+    `lm/models/mamba4.py:412-481`): proj [B, width] bf16 and the scan cache
+    -> (gated output [B, inner] bf16, new cache), through the training
+    glue's kernels at one row per sequence (`m4_mixer_prep_fwd`, the scan
+    step `m4_scan_step`, `m4_mixer_post_fwd`): three launches, the same
+    rounding points as `mamba_mixer_core`."""
+    if not proj.is_cuda:
+        raise RuntimeError("mamba_mixer_step runs on CUDA tensors only (no CPU path)")
+    if proj.dtype != torch.bfloat16:
+        raise ValueError("mamba_mixer_step expects a bfloat16 projection")
+    width = 2 * inner + 128 + 3 * heads + angles
+    if proj.shape[-1] != width:
+        raise ValueError(f"projection width {proj.shape[-1]} != 2 inner + 128 + 3 heads + angles = {width}")
+    if width % 8:
+        proj = torch.nn.functional.pad(proj, (0, -width % 8))
+    proj = proj.contiguous()
+    lib = _lib.load()
+    batch = proj.shape[0]
+    dims = _mix_dims(batch, inner, heads, angles, eps, proj.shape[-1])
+    dev = proj.device
+    c = torch.empty(batch, 64, dtype=torch.bfloat16, device=dev)
+    b = torch.empty_like(c)
+    x = torch.empty(batch, inner, dtype=torch.bfloat16, device=dev)
+    adt = torch.empty(batch, heads, device=dev)
+    dt, trap = torch.empty_like(adt), torch.empty_like(adt)
+    ang = torch.empty(batch, angles, device=dev)
+    f32 = lambda t: t.float().contiguous()  # noqa: E731
+    _lib.check(lib.m4_mixer_prep_fwd(ctypes.byref(dims), *map(_lib.ptr, (
+        proj, f32(b_scale), f32(c_scale), f32(dt_bias), c, b, x, adt, dt, trap, ang)), _stream()),
+        "m4_mixer_prep_fwd")
+    y, cache = mamba3_step(cache, c, b, x, adt, dt, trap, ang, q_bias=q_bias, k_bias=k_bias)
+    out = torch.empty(batch, inner, dtype=torch.bfloat16, device=dev)
+    _lib.check(lib.m4_mixer_post_fwd(ctypes.byref(dims), *map(_lib.ptr, (proj, y, f32(D), out)), _stream()),
+               "m4_mixer_post_fwd")
+    return out, cache
 
 
 class _RMSNormBF16(torch.autograd.Function):
@@ -359,6 +398,55 @@ def memory_mixer_post(out, var, values, ordered, gate, conf_scale, D, order_mix,
     f32 = lambda t: t.float().contiguous()  # noqa: E731
     return _MemPost.apply(f32(out), f32(var), f32(values), f32(ordered), gate, f32(conf_scale), f32(D),
                           f32(order_mix), f32(scale), float(eps), slab)
+
+
+@torch.no_grad()
+def memory_mixer_step(proj, cache, conv_w, conv_b, beta_bias, dt_bias, a_log, floor, conf_scale, D, order_mix,
+                      scale, *, heads, bound, beta_max, eps, order_head=True):
+    """One cached token of the memory mixer (`lm/models/mamba4.py:127-337`
+    with a cache) in three launches: `m4_memmix_prep_step` (conv over the
+    history rows and the current one, SiLU, unit key and query, gates),
+    `m4_memread_decode` (the read with the key carried from the previous
+    token: the key shift) and `m4_memmix_post_step` (order-head step,
+    confidence gate, D skip, read RMSNorm, SiLU gate).
+
+    proj [B, width] bf16: gate [128h] | rest [259h] columns (width a multiple
+    of 8). cache: dict(history [B, 3, width] bf16 (the previous three
+    projection rows, zero before the sequence start), shifted [B,h,64] (the
+    previous token's unit key, zero at the first token), memory
+    (SelectiveState), order [B,h,128]). Returns (y [B, 128h] bf16, new cache).
+    """
+    from .memory import selective_decode
+
+    if not proj.is_cuda:
+        raise RuntimeError("memory_mixer_step runs on CUDA tensors only (no CPU path)")
+    batch, width = proj.shape
+    inner = 128 * heads
+    if proj.dtype != torch.bfloat16 or width % 8 or width < inner + 259 * heads:
+        raise ValueError("memory_mixer_step expects bf16 rows of gate and rest columns, width a multiple of 8")
+    lib = _lib.load()
+    dev = proj.device
+    window = torch.cat((cache["history"], proj[:, None]), dim=1)         # [B, 4, width]
+    dims = _memmix_dims(batch, window.shape[1], heads, width, width, beta_max)
+    values = torch.empty(batch, heads, 128, device=dev)
+    keys, queries = torch.empty(batch, heads, 64, device=dev), torch.empty(batch, heads, 64, device=dev)
+    beta, log_decay, order_logit = (torch.empty(batch, heads, device=dev) for _ in range(3))
+    f32 = lambda t: t.float().contiguous()  # noqa: E731
+    _lib.check(lib.m4_memmix_prep_step(
+        ctypes.byref(dims), window[..., inner:].data_ptr(), *map(_lib.ptr, (f32(conv_w), f32(conv_b))),
+        float(bound), *map(_lib.ptr, (f32(beta_bias), f32(dt_bias), f32(a_log), values, keys, queries, beta,
+                                      log_decay, order_logit)), _stream()), "m4_memmix_prep_step")
+    res = selective_decode(cache["memory"], cache["shifted"], values, queries, beta, log_decay, floor)
+    y = torch.empty(batch, inner, dtype=torch.bfloat16, device=dev)
+    order = torch.empty_like(values) if order_head else None
+    pdims = _memmix_dims(batch, 1, heads, width, width, beta_max)
+    _lib.check(lib.m4_memmix_post_step(
+        ctypes.byref(pdims), float(eps), *map(_lib.ptr, (
+            res.output, res.variance, values, order_logit, f32(cache["order"]) if order_head else None, order,
+            proj, f32(conf_scale), f32(D), f32(order_mix), f32(scale), y)), _stream()), "m4_memmix_post_step")
+    new = dict(history=window[:, 1:], shifted=keys, memory=res.state,
+               order=order if order_head else cache["order"])
+    return y, new
 
 
 # ---------------------------------------------------------------------------

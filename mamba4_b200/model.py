@@ -18,10 +18,10 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .flashmamba import Mamba3StepCache, mamba3_step, mamba3_step_cache
-from .glue import (GradSlab, head_cross_entropy, mamba_mixer_core, memory_mixer_post, memory_mixer_prep,
-                   order_scan, rms_norm_bf16, split_projection)
-from .memory import selective_decode, selective_initial_state, selective_memory_fused
+from .flashmamba import Mamba3StepCache, mamba3_step_cache
+from .glue import (GradSlab, head_cross_entropy, mamba_mixer_core, mamba_mixer_step, memory_mixer_post,
+                   memory_mixer_prep, memory_mixer_step, order_scan, rms_norm_bf16, split_projection)
+from .memory import selective_initial_state, selective_memory_fused
 
 
 @dataclass(frozen=True)
@@ -144,25 +144,17 @@ class Mamba3Mixer(nn.Module):
 
     def decode(self, u, cache: Mamba3StepCache):
         """One token (`_Mamba3StepMixer`, `lm/models/mamba4.py:412-481`):
-        u [B, d_model] bf16 -> ([B, d_model], new cache). Same rounding
-        points as the training glue: B/C RMSNorm to bf16, scan output bf16,
-        out = bf16((y + x D) silu(z))."""
+        u [B, d_model] bf16 -> ([B, d_model], new cache) through the
+        training glue's prep and post kernels around the scan step (same
+        rounding points: B/C RMSNorm to bf16, scan output bf16,
+        out = bf16((y + x D) silu(z)))."""
         cfg = self.cfg
-        h, p = cfg.num_heads, cfg.head_dim
         proj = self.in_proj(u)
         with torch.autocast("cuda", enabled=False):
-            proj = proj.to(torch.bfloat16)
-            z, x, b, c, raw_dt, raw_a, trap, angles = torch.split(proj, self.sizes, dim=-1)
-            b = self.B_norm(b)
-            c = self.C_norm(c)
-            dt = F.softplus(raw_dt.float() + self.dt_bias)
-            adt = -torch.clamp(heavy_tail_activation(raw_a.float()), min=1e-4) * dt
-            y, cache = mamba3_step(cache, c, b, x.contiguous(), adt, dt, trap.float(), angles.float(),
-                                   q_bias=self.C_bias, k_bias=self.B_bias)
-            batch = u.shape[0]
-            yh = y.float().reshape(batch, h, p) + x.float().reshape(batch, h, p) * self.D[:, None]
-            zf = z.float().reshape(batch, h, p)
-            out = (yh * (zf * torch.sigmoid(zf))).to(torch.bfloat16).reshape(batch, h * p)
+            out, cache = mamba_mixer_step(proj.to(torch.bfloat16), self.B_norm.scale, self.C_norm.scale,
+                                          self.dt_bias, self.D, self.C_bias, self.B_bias, cache,
+                                          inner=cfg.inner, heads=cfg.num_heads, angles=self.angles,
+                                          eps=cfg.norm_eps)
         return self.out_proj(out), cache
 
 
@@ -203,11 +195,6 @@ def order_memory_chunked(values, log_decay, chunk_size=64):
     starts = torch.stack(carries, 1)
     out = local + torch.exp(prefix)[..., None] * starts[..., None, :]
     return out.transpose(2, 3).reshape(batch, count * chunk_size, heads, width)[:, :time]
-
-
-def _unit(x):
-    x = x.float()
-    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + 1e-6)
 
 
 class SelectiveMemoryMixer(nn.Module):
@@ -264,54 +251,38 @@ class SelectiveMemoryMixer(nn.Module):
         return self.out_proj(read)
 
     def init_cache(self, batch, device=None):
+        """Constant-size decode cache (`lm/models/mamba4.py:527-560`): the
+        previous three projection rows (the conv history), the previous
+        token's unit key (the key shift), the memory state and the order
+        state."""
         cfg = self.cfg
         h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
-        channels = cfg.inner + 2 * h * d
+        width = sum(self.sizes) + (-sum(self.sizes)) % 8
         return dict(memory=selective_initial_state(batch, h, d, p, device=device),
-                    conv=torch.zeros(batch, cfg.conv_kernel - 1, channels, dtype=torch.bfloat16, device=device),
+                    history=torch.zeros(batch, cfg.conv_kernel - 1, width, dtype=torch.bfloat16, device=device),
                     order=torch.zeros(batch, h, p, device=device),
                     shifted=torch.zeros(batch, h, d, device=device))
 
     def decode(self, u, cache):
         """One token of the cached memory mixer (`lm/models/mamba4.py:127-337`
-        with `cache`): conv history, key shift, unit norms, gates, the
-        one-token read (`selective_decode`), the order-head step and the read
-        epilogue, with the rounding points of the training glue."""
+        with `cache`) through `memory_mixer_step`: the training glue's
+        kernels at one token (same rounding points) around the one-token
+        read `m4_memread_decode`."""
         cfg = self.cfg
-        h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
-        batch = u.shape[0]
+        if cfg.key_dim != 64 or cfg.memory_head_dim != 128 or not cfg.memory_key_shift or cfg.conv_kernel != 4:
+            raise ValueError("the fused memory mixer supports key_dim 64, memory_head_dim 128, "
+                             "conv_kernel 4 and the key shift")
         proj = self.in_proj(u)
         with torch.autocast("cuda", enabled=False):
             proj = proj.to(torch.bfloat16)
-            gate, value, key, query, beta_raw, dt_raw, order_raw = torch.split(proj, self.sizes, dim=-1)
-            mixed = torch.cat((value, key, query), dim=-1)                    # [B, C] bf16
-            window = torch.cat((cache["conv"], mixed[:, None]), dim=1)        # [B, K, C]
-            weight = self.conv_weight.float() - self.bound
-            conv = self.conv_bias.float() + (window.float() * weight[None]).sum(1)
-            act = conv * torch.sigmoid(conv)
-            value = act[:, : cfg.inner].reshape(batch, h, p)
-            key = act[:, cfg.inner: cfg.inner + h * d].reshape(batch, h, d)
-            query = act[:, cfg.inner + h * d:].reshape(batch, h, d)
-            shifted = key
-            key, query = _unit(cache["shifted"]), _unit(query)
-            beta = cfg.memory_beta_max * torch.sigmoid(beta_raw.float() + self.beta_bias)
-            dt = F.softplus(dt_raw.float() + self.dt_bias)
-            log_decay = -torch.exp(self.a_log) * dt
+            if proj.shape[-1] % 8:
+                proj = F.pad(proj, (0, -proj.shape[-1] % 8))
             floor = cfg.floor_min + F.softplus(self.floor)
-            res = selective_decode(cache["memory"], key, value, query, beta, log_decay, floor)
-            read = res.output * torch.sigmoid(1 - self.confidence_scale * torch.log1p(res.variance))[..., None]
-            read = read + self.D[:, None] * value
-            order = cache["order"]
-            if cfg.order_head:
-                lam = torch.sigmoid(order_raw.float() + 2)[..., None]
-                order = lam * order + (1 - lam) * value
-                read = read + torch.sigmoid(self.order_mix)[:, None] * order
-            rs = torch.rsqrt(read.square().mean(-1, keepdim=True) + cfg.norm_eps)
-            normed = (read * rs * self.read_norm.scale).to(torch.bfloat16).float()
-            g = gate.float().reshape(batch, h, p)
-            out = (normed * (g * torch.sigmoid(g))).to(torch.bfloat16).reshape(batch, h * p)
-        new = dict(memory=res.state, conv=window[:, 1:].contiguous(), order=order, shifted=shifted)
-        return self.out_proj(out), new
+            out, cache = memory_mixer_step(
+                proj, cache, self.conv_weight, self.conv_bias, self.beta_bias, self.dt_bias, self.a_log, floor,
+                self.confidence_scale, self.D, self.order_mix, self.read_norm.scale, heads=cfg.memory_heads,
+                bound=self.bound, beta_max=cfg.memory_beta_max, eps=cfg.norm_eps, order_head=cfg.order_head)
+        return self.out_proj(out), cache
 
 
 class Block(nn.Module):

@@ -92,7 +92,7 @@ def test_rms_norm_bf16_matches_composition(features):
 def composite_memory_mixer(m, u):
     """The memory mixer as plain PyTorch ops (lm/models/mamba4.py:155-260)."""
     from mamba4_b200.memory import selective_memory_fused
-    from mamba4_b200.model import _unit, causal_conv, order_memory_chunked
+    from mamba4_b200.model import causal_conv, order_memory_chunked
 
     cfg = m.cfg
     h, d, p = cfg.memory_heads, cfg.key_dim, cfg.memory_head_dim
@@ -219,3 +219,76 @@ def test_memory_mixer_shared_gradient_buffer_is_exact():
     a, b = run(True), run(False)
     assert torch.equal(a, b)
     assert (a[..., inner + 259 * heads:] == 0).all()
+
+
+def _unit(x):
+    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + 1e-6)
+
+
+def composite_memory_step(proj, cache, p, heads, bound, beta_max, eps, floor):
+    """The cached memory mixer restated in PyTorch (fp32 between the bf16
+    projection and output; `lm/models/mamba4.py:127-337` with a cache)
+    around the CUDA one-token read."""
+    from mamba4_b200.memory import selective_decode
+
+    inner, d = 128 * heads, 64
+    batch = proj.shape[0]
+    gate, value, key, query, beta_raw, dt_raw, order_raw = torch.split(
+        proj[:, : inner + 259 * heads], (inner, inner, heads * d, heads * d, heads, heads, heads), -1)
+    window = torch.cat((cache["history"], proj[:, None]), 1)[..., inner: inner + 256 * heads]
+    conv = p["conv_b"] + (window.float() * (p["conv_w"] - bound)[None]).sum(1)
+    act = conv * torch.sigmoid(conv)
+    v = act[:, :inner].reshape(batch, heads, 128)
+    k = _unit(act[:, inner: inner + heads * d].reshape(batch, heads, d))
+    q = _unit(act[:, inner + heads * d:].reshape(batch, heads, d))
+    beta = beta_max * torch.sigmoid(beta_raw.float() + p["beta_bias"])
+    log_decay = -torch.exp(p["a_log"]) * F.softplus(dt_raw.float() + p["dt_bias"])
+    res = selective_decode(cache["memory"], cache["shifted"], v, q, beta, log_decay, floor)
+    read = res.output * torch.sigmoid(1 - p["conf"] * torch.log1p(res.variance))[..., None] + p["D"][:, None] * v
+    lam = torch.sigmoid(order_raw.float() + 2)[..., None]
+    order = lam * cache["order"] + (1 - lam) * v
+    read = read + torch.sigmoid(p["order_mix"])[:, None] * order
+    rs = torch.rsqrt(read.square().mean(-1, keepdim=True) + eps)
+    normed = (read * rs * p["scale"]).to(torch.bfloat16).float()
+    g = gate.float().reshape(batch, heads, 128)
+    y = (normed * (g * torch.sigmoid(g))).to(torch.bfloat16).reshape(batch, inner)
+    return y, dict(history=torch.cat((cache["history"], proj[:, None]), 1)[:, 1:], shifted=k, memory=res.state,
+                   order=order)
+
+
+def test_memory_mixer_step_matches_composite():
+    """Three-launch cached memory mixer (`memory_mixer_step`) against the
+    PyTorch composition over several tokens: same outputs up to bf16
+    rounding, same carried state."""
+    from mamba4_b200.glue import memory_mixer_step
+    from mamba4_b200.memory import selective_initial_state
+
+    torch.manual_seed(11)
+    heads, batch, steps = 4, 3, 6
+    inner = 128 * heads
+    width = inner + 259 * heads + (-(inner + 259 * heads)) % 8
+    C = 256 * heads
+    dev = "cuda"
+    p = dict(conv_w=torch.rand(4, C, device=dev), conv_b=0.1 * torch.randn(C, device=dev),
+             beta_bias=torch.randn(heads, device=dev), dt_bias=torch.randn(heads, device=dev),
+             a_log=torch.rand(heads, device=dev) * 2, conf=torch.full((heads,), 0.1, device=dev),
+             D=torch.randn(heads, device=dev), order_mix=torch.randn(heads, device=dev),
+             scale=1 + 0.1 * torch.randn(128, device=dev))
+    floor = 0.25 + F.softplus(torch.randn(heads, 64, device=dev))
+    zero = lambda: dict(history=torch.zeros(batch, 3, width, dtype=torch.bfloat16, device=dev),  # noqa: E731
+                        shifted=torch.zeros(batch, heads, 64, device=dev),
+                        memory=selective_initial_state(batch, heads, 64, 128, device=dev),
+                        order=torch.zeros(batch, heads, 128, device=dev))
+    ca, cb = zero(), zero()
+    for _ in range(steps):
+        proj = torch.randn(batch, width, device=dev).to(torch.bfloat16)
+        ya, ca = memory_mixer_step(proj, ca, p["conv_w"], p["conv_b"], p["beta_bias"], p["dt_bias"], p["a_log"],
+                                   floor, p["conf"], p["D"], p["order_mix"], p["scale"], heads=heads, bound=0.5,
+                                   beta_max=1.0, eps=1e-5)
+        yb, cb = composite_memory_step(proj, cb, p, heads, 0.5, 1.0, 1e-5, floor)
+        assert rel(ya, yb) < 1e-2
+        assert rel(ca["shifted"], cb["shifted"]) < 1e-5
+        assert rel(ca["order"], cb["order"]) < 1e-5
+        assert rel(ca["memory"].evidence, cb["memory"].evidence) < 1e-5
+        assert rel(ca["memory"].cross, cb["memory"].cross) < 1e-5
+        assert torch.equal(ca["history"], cb["history"])
