@@ -527,9 +527,27 @@ M4_DEV void conv8(const MemMix& d, const bf16* rest, int b, int t, int ch, const
 }
 
 // Stage conv weights (minus `bound`) and bias in shared memory: [4][C] + [C].
+// 16-byte loads, eight in flight per thread before their stores (C is a
+// multiple of 256; w and bias 16-byte aligned).
 M4_DEV void stage_conv(const float* w, const float* bias, float bound, int C, float* w_s, float* bias_s) {
-  for (int i = threadIdx.x; i < 4 * C; i += blockDim.x) w_s[i] = w[i] - bound;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) bias_s[i] = bias[i];
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4* ws4 = reinterpret_cast<float4*>(w_s);
+  for (int i0 = threadIdx.x; i0 < C; i0 += 8 * blockDim.x) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * blockDim.x;
+      v[u] = i < C ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < C) ws4[i] = make_float4(v[u].x - bound, v[u].y - bound, v[u].z - bound, v[u].w - bound);
+    }
+  }
+  const float4* b4 = reinterpret_cast<const float4*>(bias);
+  float4* bs4 = reinterpret_cast<float4*>(bias_s);
+  for (int i = threadIdx.x; i < C / 4; i += blockDim.x) bs4[i] = b4[i];
   __syncthreads();
 }
 
@@ -1087,7 +1105,7 @@ extern "C" int m4_memmix_prep_fwd(const M4MemMixDims* m, const void* rest, const
                                   float* order_logit, void* stream) {
   const int st = check_mem(m);
   if (st != M4_OK) return st;
-  if (!all_aligned16(rest, conv_w, values, keys, queries, beta, log_decay, order_logit)) return M4_ERR_ALIGN;
+  if (!all_aligned16(rest, conv_w, conv_b, values, keys, queries, beta, log_decay, order_logit)) return M4_ERR_ALIGN;
   const MemMix d = make_memmix(*m);
   const size_t smem = size_t(5) * 256 * d.heads * sizeof(float);
   cudaFuncSetAttribute(mem_prep_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -1105,7 +1123,7 @@ extern "C" int m4_memmix_prep_bwd(const M4MemMixDims* m, const void* rest, const
                                   float* d_beta_bias, float* d_dt_bias, float* d_a_log, void* stream) {
   const int st = check_mem(m);
   if (st != M4_OK) return st;
-  if (!all_aligned16(rest, conv_w, d_values, d_keys, d_queries, d_conv, d_rest, part)) return M4_ERR_ALIGN;
+  if (!all_aligned16(rest, conv_w, conv_b, d_values, d_keys, d_queries, d_conv, d_rest, part)) return M4_ERR_ALIGN;
   const MemMix d = make_memmix(*m);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int h = d.heads, C = 256 * h, rows = d.B * d.T;
@@ -1188,7 +1206,7 @@ extern "C" int m4_memmix_prep_step(const M4MemMixDims* m, const void* rest, cons
                                    float* log_decay, float* order_logit, void* stream) {
   const int st = check_mem(m);
   if (st != M4_OK) return st;
-  if (!all_aligned16(rest, conv_w, values, keys, queries, beta, log_decay, order_logit)) return M4_ERR_ALIGN;
+  if (!all_aligned16(rest, conv_w, conv_b, values, keys, queries, beta, log_decay, order_logit)) return M4_ERR_ALIGN;
   MemMix d = make_memmix(*m);
   d.step = 1;
   const size_t smem = size_t(5) * 256 * d.heads * sizeof(float);

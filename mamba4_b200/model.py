@@ -363,19 +363,26 @@ class GraphedDecoder:
     """`Mamba4LM.decode_step` captured once as a CUDA graph (the B200
     counterpart of the reference's jitted decode, `lm/models/mamba4.py:507-524`).
 
-    A decode step is a few hundred small launches (projections, the glue
-    arithmetic, `m4_scan_step`, `m4_memread_decode`); replaying them as one
-    graph removes the per-launch host cost. The cache lives in static buffers
-    that the graph reads and then overwrites with the next cache, so
-    `step(tokens)` returns the same logits as eager `decode_step` calls from
-    `model.init_cache(batch)` (the graph runs the same kernels on the same
-    operands). `logits` is a static buffer, overwritten by the next step.
-    Parameters are read in place at every replay, so weight updates are seen.
+    A decode step is about a hundred small launches (block norms,
+    projections, the glue kernels, `m4_scan_step`, `m4_memread_decode`);
+    replaying them as one graph removes the per-launch host cost. The cache
+    lives in static buffers that the graph reads and then overwrites with the
+    next cache, so `step(tokens)` returns the same logits as eager
+    `decode_step` calls from `model.init_cache(batch)` (the graph runs the
+    same kernels on the same operands). `logits` is a static buffer,
+    overwritten by the next step.
+
+    The linear and embedding weights enter the graph as bfloat16 copies (the
+    casts autocast would otherwise repeat at every token, one launch and a
+    full weight read each); call `refresh_weights()` after changing the
+    model's parameters. Every other parameter is read in place at each replay.
     """
 
     def __init__(self, model: Mamba4LM, batch: int, device=None, dtype=torch.bfloat16):
         self.model, self.batch, self.dtype = model, batch, dtype
         device = torch.device("cuda" if device is None else device)
+        self._shadow = [(mod, mod.weight, nn.Parameter(mod.weight.detach().to(dtype), requires_grad=False))
+                        for mod in model.modules() if isinstance(mod, (nn.Linear, nn.Embedding))]
         self._initial = model.init_cache(batch, device=device)
         self.cache = model.init_cache(batch, device=device)
         self._static = _cache_tensors(self.cache)
@@ -383,14 +390,22 @@ class GraphedDecoder:
         current = torch.cuda.current_stream(device)
         side = torch.cuda.Stream(device)
         side.wait_stream(current)
-        with torch.cuda.stream(side):
-            for _ in range(2):
-                self._body()
-        current.wait_stream(side)
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self.logits = self._body()
+        self._install(True)
+        try:
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self._body()
+            current.wait_stream(side)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self.logits = self._body()
+        finally:
+            self._install(False)
         self.reset()
+
+    def _install(self, shadow: bool):
+        for mod, full, low in self._shadow:
+            mod._parameters["weight"] = low if shadow else full
 
     @torch.no_grad()
     def _body(self):
@@ -400,6 +415,13 @@ class GraphedDecoder:
             if dst.data_ptr() != src.data_ptr():
                 dst.copy_(src)
         return logits
+
+    @torch.no_grad()
+    def refresh_weights(self):
+        """Copy the model's current linear and embedding weights into the
+        graph's bfloat16 copies."""
+        for _, full, low in self._shadow:
+            low.copy_(full)
 
     def reset(self):
         """Back to the empty cache (a new batch of sequences)."""

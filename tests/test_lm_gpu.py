@@ -96,3 +96,13 @@ def test_graphed_decode_matches_eager_decode():
         for a, b in zip(_cache_tensors(dec.cache), _cache_tensors(cache)):
             assert torch.equal(a, b)
         dec.reset()
+    # The graph's bf16 weight copies follow the model after refresh_weights().
+    with torch.no_grad():
+        for p in model.parameters():
+            p.mul_(1.01)
+    dec.refresh_weights()
+    cache = model.init_cache(3, device="cuda")
+    for i in range(3):
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            ref, cache = model.decode_step(tokens[:, i], cache)
+        assert torch.equal(dec.step(tokens[:, i]), ref), i
