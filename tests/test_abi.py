@@ -61,6 +61,33 @@ def test_entry_points_reject_bad_arguments_without_launching():
     assert lib.m4_memread_fwd(ctypes.byref(bad), *null, None, 0, None) == 2  # unsupported
 
 
+def test_one_token_glue_rejects_bad_arguments_without_launching():
+    """`m4_memmix_prep_step` / `m4_memmix_post_step` validate dimensions,
+    pointer pairing and alignment before any launch. Every call here fails
+    validation (the pointer value 8 is not 16-byte aligned), so no kernel
+    runs and no memory is touched."""
+    from mamba4_b200 import _lib
+
+    lib = _lib.load()
+    odd = 8
+    good = _lib.MemMixDims(4, 1, 8, 3096, 3096, 1.0)
+    post = [odd] * 12
+    assert lib.m4_memmix_post_step(ctypes.byref(good), 1e-5, *post, None) == 4            # M4_ERR_ALIGN
+    two = _lib.MemMixDims(4, 2, 8, 3096, 3096, 1.0)
+    assert lib.m4_memmix_post_step(ctypes.byref(two), 1e-5, *post, None) == 1             # time != 1
+    unpaired = list(post)
+    unpaired[5] = None                                                                    # order_out
+    assert lib.m4_memmix_post_step(ctypes.byref(good), 1e-5, *unpaired, None) == 1
+    wide = _lib.MemMixDims(4, 1, 17, 3096 * 3, 3096 * 3, 1.0)
+    assert lib.m4_memmix_post_step(ctypes.byref(wide), 1e-5, *post, None) == 2            # > 16 heads
+    window = _lib.MemMixDims(4, 4, 8, 3096, 3096, 1.0)
+    assert lib.m4_memmix_prep_step(ctypes.byref(window), odd, odd, odd, 0.5, *[odd] * 9, None) == 4
+    ragged = _lib.MemMixDims(4, 4, 8, 3097, 3096, 1.0)
+    assert lib.m4_memmix_prep_step(ctypes.byref(ragged), odd, odd, odd, 0.5, *[odd] * 9, None) == 2
+    empty = _lib.MemMixDims(0, 4, 8, 3096, 3096, 1.0)
+    assert lib.m4_memmix_prep_step(ctypes.byref(empty), odd, odd, odd, 0.5, *[odd] * 9, None) == 1
+
+
 def test_product_path_has_no_cpu_fallback():
     import torch
     from mamba4_b200 import mamba3_fused, selective_memory_fused
