@@ -567,12 +567,16 @@ __global__ void __launch_bounds__(WPB * 32) mem_prep_fwd(
   float* w_s = smem;
   float* bias_s = smem + 4 * C;
   stage_conv(conv_w, conv_b, bound, C, w_s, bias_s);
-  const int lane = threadIdx.x & 31, span = d.step ? 1 : d.T;
-  for (int row = gwarp(); row < d.B * span; row += nwarps()) {
+  // Work: over token rows, one warp per row and all its channel groups; in
+  // the one-token step one block per sequence, its warps over the groups.
+  const int lane = threadIdx.x & 31, rows = d.step ? d.B : d.B * d.T;
+  const int row0 = d.step ? blockIdx.x : gwarp(), rstep = d.step ? gridDim.x : nwarps();
+  const int k0 = d.step ? threadIdx.x >> 5 : 0, kstep = d.step ? WPB : 1;
+  for (int row = row0; row < rows; row += rstep) {
     // Output row `row` is token (b, t); inputs are read at rows b T + s.
-    const int b = row / span, t = d.step ? d.T - 1 : row % span;
+    const int b = d.step ? row : row / d.T, t = d.step ? d.T - 1 : row % d.T;
     const int kt = d.step ? t : t - 1;  // token whose key this row writes
-    for (int k = 0; k < h; ++k) {
+    for (int k = k0; k < h; k += kstep) {
       // Channel group lane + 32k: value below 16h, key below 24h, query above.
       const int cg = lane + 32 * k, ch = 8 * cg;
       const int cls = cg < 16 * h ? 0 : (cg < 24 * h ? 1 : 2);
@@ -598,7 +602,7 @@ __global__ void __launch_bounds__(WPB * 32) mem_prep_fwd(
       st4(dst, make_float4(o[0] * r, o[1] * r, o[2] * r, o[3] * r));
       st4(dst + 4, make_float4(o[4] * r, o[5] * r, o[6] * r, o[7] * r));
     }
-    if (lane < h) {
+    if (k0 == 0 && lane < h) {
       const bf16* pr = rest + (size_t(b) * d.T + t) * d.stride + C;
       const size_t i = size_t(row) * h + lane;
       beta[i] = d.beta_max * sigmoid(bf(pr + lane) + beta_bias[lane]);
@@ -1211,7 +1215,7 @@ extern "C" int m4_memmix_prep_step(const M4MemMixDims* m, const void* rest, cons
   d.step = 1;
   const size_t smem = size_t(5) * 256 * d.heads * sizeof(float);
   cudaFuncSetAttribute(mem_prep_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  mem_prep_fwd<<<row_blocks(d.B), WPB * 32, smem, static_cast<cudaStream_t>(stream)>>>(
+  mem_prep_fwd<<<std::min(d.B, 4 * 148), WPB * 32, smem, static_cast<cudaStream_t>(stream)>>>(
       d, static_cast<const bf16*>(rest), conv_w, conv_b, bound, beta_bias, dt_bias, a_log, values, keys, queries,
       beta, log_decay, order_logit);
   return launch_status();
