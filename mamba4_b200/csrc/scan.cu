@@ -1015,6 +1015,19 @@ __global__ void __launch_bounds__(256) step_kernel(
       sv[e] = v.x; sv[e + 1] = v.y; sv[e + 2] = v.z; sv[e + 3] = v.w;
     }
   }
+  // Inputs that no output aliases, loaded at entry with the state: the
+  // token's C/B pair (plus biases) and x, so one DRAM round trip precedes the
+  // rotations instead of two.
+  float cq[2] = {0.f, 0.f}, ck[2] = {0.f, 0.f}, xr = 0.f;
+  if (tid < NS / 2) {
+    const int n0 = 2 * tid, n1 = 2 * tid + 1;
+    const size_t base = per_head ? size_t(bh) * NS : size_t(bb) * NS;
+    cq[0] = to_f(c[base + n0]) + (qb ? qb[h * NS + n0] : 0.f);
+    cq[1] = to_f(c[base + n1]) + (qb ? qb[h * NS + n1] : 0.f);
+    ck[0] = to_f(bk[base + n0]) + (kb ? kb[h * NS + n0] : 0.f);
+    ck[1] = to_f(bk[base + n1]) + (kb ? kb[h * NS + n1] : 0.f);
+  }
+  if (tid < HP) xr = to_f(x[size_t(bh) * HP + tid]);
   float phv = 0.f;
   if (tid < NS / 2) {
     if (tid < A) {
@@ -1029,11 +1042,8 @@ __global__ void __launch_bounds__(256) step_kernel(
   if (tid < NS / 2 && tid < A) phase_out[size_t(bh) * A + tid] = phv;
   if (tid < NS / 2) {
     const int i = tid, n0 = 2 * i, n1 = 2 * i + 1;
-    const size_t base = per_head ? size_t(bh) * NS : size_t(bb) * NS;
-    const float q0 = round_to<T>(to_f(c[base + n0]) + (qb ? qb[h * NS + n0] : 0.f));
-    const float q1 = round_to<T>(to_f(c[base + n1]) + (qb ? qb[h * NS + n1] : 0.f));
-    const float k0 = round_to<T>(to_f(bk[base + n0]) + (kb ? kb[h * NS + n0] : 0.f));
-    const float k1 = round_to<T>(to_f(bk[base + n1]) + (kb ? kb[h * NS + n1] : 0.f));
+    const float q0 = round_to<T>(cq[0]), q1 = round_to<T>(cq[1]);
+    const float k0 = round_to<T>(ck[0]), k1 = round_to<T>(ck[1]);
     float cs = 1.f, sn = 0.f;
     if (i < A) sincosf(ph[i], &sn, &cs);
     qr[n0] = round_to<T>(q0 * cs - q1 * sn);
@@ -1041,7 +1051,7 @@ __global__ void __launch_bounds__(256) step_kernel(
     kr[n0] = round_to<T>(k0 * cs - k1 * sn);
     kr[n1] = round_to<T>(k1 * cs + k0 * sn);
   }
-  if (tid < HP) xv[tid] = to_f(x[size_t(bh) * HP + tid]);
+  if (tid < HP) xv[tid] = xr;
   __syncthreads();
   if (tid < NS) prev_k_out[size_t(bh) * NS + tid] = kr[tid];
   if (tid < HP) prev_v_out[size_t(bh) * HP + tid] = xv[tid];
