@@ -260,6 +260,13 @@ int m4_mixer_prep_bwd(const M4MixerDims* dims, const void* proj, const float* b_
 
 /* bfloat16 RMSNorm with float32 statistics (lm/models/common.py:25-45) over
  * `features` in {256, 512, 768, 1024}; rstd [rows] is saved for backward. */
+/* Residual add fused with the next block's RMSNorm (decode, no backward):
+ * x_out = bf16(x + delta), y = bf16(rmsnorm(x_out) * scale) over bf16 rows of
+ * `features` in {256, 512, 768, 1024}; x_out may alias x (the decode blocks'
+ * residual, lm/models/mamba4.py:358 and :404, followed by the next block's
+ * norm or the final norm, :514-522). */
+int m4_add_rmsnorm_fwd(int rows, int features, float eps, const void* x, const void* delta,
+                       const float* scale, void* x_out, void* y, void* stream);
 size_t m4_rmsnorm_partial_rows(int rows);
 int m4_rmsnorm_fwd(int rows, int features, float eps, const void* x, const float* scale, void* y,
                    float* rstd, void* stream);

@@ -79,6 +79,7 @@ SIGNATURES = {
     "m4_memmix_order_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 8, _c_int),
     "m4_memmix_post_fwd": ([ctypes.POINTER(MemMixDims), ctypes.c_float] + [_p] * 12, _c_int),
     "m4_memmix_post_bwd": ([ctypes.POINTER(MemMixDims)] + [_p] * 22, _c_int),
+    "m4_add_rmsnorm_fwd": ([_c_int, _c_int, ctypes.c_float] + [_p] * 6, _c_int),
     "m4_memmix_prep_step": ([ctypes.POINTER(MemMixDims), _p, _p, _p, ctypes.c_float] + [_p] * 10, _c_int),
     "m4_memmix_post_step": ([ctypes.POINTER(MemMixDims), ctypes.c_float] + [_p] * 13, _c_int),
     "m4_cross_entropy_fwd": ([_c_int, _c_int, _c_int] + [_p] * 5, _c_int),

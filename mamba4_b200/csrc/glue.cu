@@ -306,6 +306,43 @@ __global__ void __launch_bounds__(WPB * 32) rms_fwd(int rows, float eps, const b
   }
 }
 
+// Residual add fused with the next RMSNorm (decode): x_out = rd(x + d),
+// y = rd(rmsnorm(x_out) scale). x_out may alias x (each lane reads its own
+// columns before writing them).
+template <int NV>
+__global__ void __launch_bounds__(WPB * 32) add_rms_fwd(int rows, float eps, const bf16* x,
+                                                       const bf16* __restrict__ d,
+                                                       const float* __restrict__ scale, bf16* x_out,
+                                                       bf16* __restrict__ y) {
+  constexpr int F = 256 * NV;
+  const int lane = threadIdx.x & 31;
+  for (int row = gwarp(); row < rows; row += nwarps()) {
+    float v[NV][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const size_t at = size_t(row) * F + 8 * (lane + 32 * k);
+      float a[8], b[8];
+      unpack8(ld16(x + at), a);
+      unpack8(ld16(d + at), b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[k][e] = __bfloat162float(__float2bfloat16_rn(a[e] + b[e]));
+      st16(x_out + at, pack8(v[k]));
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(v[k][e], v[k][e], ss);
+    }
+    const float r = rsqrtf(warp_sum(ss) * (1.f / F) + eps);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int col = 8 * (lane + 32 * k);
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[k][e] * r * scale[col + e];
+      st16(y + size_t(row) * F + col, pack8(o));
+    }
+  }
+}
+
 template <int NV>
 __global__ void __launch_bounds__(WPB * 32) rms_bwd(int rows, const bf16* __restrict__ x,
                                                    const float* __restrict__ scale, const float* __restrict__ rstd,
@@ -445,6 +482,27 @@ extern "C" int m4_mixer_prep_bwd(const M4MixerDims* m, const void* proj, const f
 }
 
 extern "C" size_t m4_rmsnorm_partial_rows(int rows) { return rows > 0 ? size_t(row_blocks(rows)) * WPB : 0; }
+
+extern "C" int m4_add_rmsnorm_fwd(int rows, int features, float eps, const void* x, const void* delta,
+                                  const float* scale, void* x_out, void* y, void* stream) {
+  if (!x || !delta || !scale || !x_out || !y) return M4_ERR_NULL;
+  if (rows <= 0) return M4_ERR_DIMS;
+  if (!all_aligned16(x, delta, x_out, y)) return M4_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int blocks = row_blocks(rows);
+  const bf16* xi = static_cast<const bf16*>(x);
+  const bf16* di = static_cast<const bf16*>(delta);
+  bf16* xo = static_cast<bf16*>(x_out);
+  bf16* yo = static_cast<bf16*>(y);
+  switch (features) {
+    case 256: add_rms_fwd<1><<<blocks, WPB * 32, 0, s>>>(rows, eps, xi, di, scale, xo, yo); break;
+    case 512: add_rms_fwd<2><<<blocks, WPB * 32, 0, s>>>(rows, eps, xi, di, scale, xo, yo); break;
+    case 768: add_rms_fwd<3><<<blocks, WPB * 32, 0, s>>>(rows, eps, xi, di, scale, xo, yo); break;
+    case 1024: add_rms_fwd<4><<<blocks, WPB * 32, 0, s>>>(rows, eps, xi, di, scale, xo, yo); break;
+    default: return M4_ERR_UNSUPPORTED;
+  }
+  return launch_status();
+}
 
 extern "C" int m4_rmsnorm_fwd(int rows, int features, float eps, const void* x, const float* scale, void* y,
                               float* rstd, void* stream) {

@@ -137,6 +137,29 @@ def mamba_mixer_step(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, cache, 
     return out, cache
 
 
+ADD_RMS_FEATURES = (256, 512, 768, 1024)
+
+
+@torch.no_grad()
+def add_rms_norm_bf16(x, delta, scale, eps):
+    """Residual add fused with the next RMSNorm, for decode (no gradient):
+    returns (x + delta, rmsnorm(x + delta) * scale), both bf16 [rows, F] with
+    F in ADD_RMS_FEATURES; the same rounding as the residual add followed by
+    `rms_norm_bf16` (the decode blocks' residual, lm/models/mamba4.py:358,
+    :404, then the next block's norm)."""
+    if not x.is_cuda:
+        raise RuntimeError("add_rms_norm_bf16 runs on CUDA tensors only (no CPU path)")
+    features = x.shape[-1]
+    if x.dtype != torch.bfloat16 or delta.dtype != torch.bfloat16 or features not in ADD_RMS_FEATURES:
+        raise ValueError(f"add_rms_norm_bf16 expects bf16 rows of {ADD_RMS_FEATURES} features")
+    x, delta = x.contiguous(), delta.contiguous()
+    x_out, y = torch.empty_like(x), torch.empty_like(x)
+    lib = _lib.load()
+    _lib.check(lib.m4_add_rmsnorm_fwd(x.numel() // features, features, float(eps), *map(_lib.ptr, (
+        x, delta, scale.float().contiguous(), x_out, y)), _stream()), "m4_add_rmsnorm_fwd")
+    return x_out, y
+
+
 class _RMSNormBF16(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, scale, eps):

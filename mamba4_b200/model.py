@@ -19,8 +19,9 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .flashmamba import Mamba3StepCache, mamba3_step_cache
-from .glue import (GradSlab, head_cross_entropy, mamba_mixer_core, mamba_mixer_step, memory_mixer_post,
-                   memory_mixer_prep, memory_mixer_step, order_scan, rms_norm_bf16, split_projection)
+from .glue import (ADD_RMS_FEATURES, GradSlab, add_rms_norm_bf16, head_cross_entropy, mamba_mixer_core,
+                   mamba_mixer_step, memory_mixer_post, memory_mixer_prep, memory_mixer_step, order_scan,
+                   rms_norm_bf16, split_projection)
 from .memory import selective_initial_state, selective_memory_fused
 
 
@@ -342,11 +343,19 @@ class Mamba4LM(nn.Module):
         the forward."""
         x = self.embedding(tokens).to(torch.bfloat16)
         new = []
-        for block, layer in zip(self.blocks, cache):
-            x, layer = block.decode(x, layer)
+        fused = x.shape[-1] in ADD_RMS_FEATURES
+        h = self.blocks[0].norm(x)
+        for i, (block, layer) in enumerate(zip(self.blocks, cache)):
+            out, layer = block.mixer.decode(h, layer)
             new.append(layer)
-        x = self.final_norm(x)
-        return F.linear(x, self.embedding.weight.to(x.dtype)).float(), new
+            norm = self.blocks[i + 1].norm if i + 1 < len(self.blocks) else self.final_norm
+            if fused:
+                # The block's residual add and the next norm in one launch.
+                x, h = add_rms_norm_bf16(x, out.to(x.dtype), norm.scale, norm.eps)
+            else:
+                x = x + out.to(x.dtype)
+                h = norm(x)
+        return F.linear(h, self.embedding.weight.to(h.dtype)).float(), new
 
 
 def _cache_tensors(cache):

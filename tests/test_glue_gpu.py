@@ -292,3 +292,20 @@ def test_memory_mixer_step_matches_composite():
         assert rel(ca["memory"].evidence, cb["memory"].evidence) < 1e-5
         assert rel(ca["memory"].cross, cb["memory"].cross) < 1e-5
         assert torch.equal(ca["history"], cb["history"])
+
+
+def test_add_rms_norm_matches_add_then_norm():
+    """The decode path's fused residual add + RMSNorm gives exactly the
+    residual add followed by the RMSNorm kernel."""
+    from mamba4_b200.glue import add_rms_norm_bf16
+
+    torch.manual_seed(12)
+    for features in (256, 512, 768, 1024):
+        x = torch.randn(37, features, device="cuda").to(torch.bfloat16)
+        d = torch.randn(37, features, device="cuda").to(torch.bfloat16)
+        scale = 1 + 0.1 * torch.randn(features, device="cuda")
+        xo, y = add_rms_norm_bf16(x, d, scale, 1e-5)
+        ref = x + d
+        assert torch.equal(xo, ref)
+        assert torch.equal(y, rms_norm_bf16(ref, scale, 1e-5))
+        assert rel(y, composite_rms(ref, scale, 1e-5)) < 1e-2
