@@ -206,7 +206,7 @@ def mamba3_step_cache(batch, heads, state_dim, head_dim, angle_count, device=Non
                            z(batch, heads, head_dim), z(batch, heads, angle_count))
 
 
-def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias):
+def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias, inplace=False):
     """One cached token of the SISO scan: the scan core of `_Mamba3StepMixer`
     (`lm/models/mamba4.py:412-481`) through `m4_scan_step`.
 
@@ -215,7 +215,9 @@ def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias)
     angles [B,A] (or [B,H,A]) rates; q_bias, k_bias [H,1,N] or [H,N].
     Returns y [B,H*P] (dtype of x; before the D skip and gate) and the new
     cache. Stepping mamba3_step_cache(...) through a sequence gives
-    mamba3_fused's y and final state (`test_decode_gpu.py`).
+    mamba3_fused's y and final state (`test_decode_gpu.py`). With
+    inplace=True the new cache is written over `cache`'s tensors (float32,
+    contiguous, unpadded dims) instead of fresh ones.
     """
     if not x.is_cuda:
         raise RuntimeError("mamba3_step runs on CUDA tensors only (no CPU path)")
@@ -243,7 +245,10 @@ def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias)
     pv = _pad(f32(cache.previous_values), (0, pad_p)).contiguous()
     ph = f32(cache.phase)
     y = torch.empty_like(xp)
-    st_out, pk_out, pv_out, ph_out = (torch.empty_like(t) for t in (st, pk, pv, ph))
+    if inplace:  # the kernel reads every cache value before it writes any
+        st_out, pk_out, pv_out, ph_out = st, pk, pv, ph
+    else:
+        st_out, pk_out, pv_out, ph_out = (torch.empty_like(t) for t in (st, pk, pv, ph))
     dims = _lib.ScanDims(batch, 1, heads, HEAD_DIM, STATE_DIM, angle_count, CHUNK,
                          int(model == torch.bfloat16), int(per_head))
     lib = _lib.load()

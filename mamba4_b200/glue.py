@@ -99,13 +99,15 @@ def mamba_mixer_core(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, *, inne
 
 
 @torch.no_grad()
-def mamba_mixer_step(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, cache, *, inner, heads, angles, eps):
+def mamba_mixer_step(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, cache, *, inner, heads, angles, eps,
+                     inplace=False):
     """One cached token of the mixer core (`_Mamba3StepMixer`,
     `lm/models/mamba4.py:412-481`): proj [B, width] bf16 and the scan cache
     -> (gated output [B, inner] bf16, new cache), through the training
     glue's kernels at one row per sequence (`m4_mixer_prep_fwd`, the scan
     step `m4_scan_step`, `m4_mixer_post_fwd`): three launches, the same
-    rounding points as `mamba_mixer_core`."""
+    rounding points as `mamba_mixer_core`. inplace=True writes the new scan
+    cache over `cache`'s tensors (see `mamba3_step`)."""
     if not proj.is_cuda:
         raise RuntimeError("mamba_mixer_step runs on CUDA tensors only (no CPU path)")
     if proj.dtype != torch.bfloat16:
@@ -130,7 +132,7 @@ def mamba_mixer_step(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, cache, 
     _lib.check(lib.m4_mixer_prep_fwd(ctypes.byref(dims), *map(_lib.ptr, (
         proj, f32(b_scale), f32(c_scale), f32(dt_bias), c, b, x, adt, dt, trap, ang)), _stream()),
         "m4_mixer_prep_fwd")
-    y, cache = mamba3_step(cache, c, b, x, adt, dt, trap, ang, q_bias=q_bias, k_bias=k_bias)
+    y, cache = mamba3_step(cache, c, b, x, adt, dt, trap, ang, q_bias=q_bias, k_bias=k_bias, inplace=inplace)
     out = torch.empty(batch, inner, dtype=torch.bfloat16, device=dev)
     _lib.check(lib.m4_mixer_post_fwd(ctypes.byref(dims), *map(_lib.ptr, (proj, y, f32(D), out)), _stream()),
                "m4_mixer_post_fwd")
@@ -425,7 +427,7 @@ def memory_mixer_post(out, var, values, ordered, gate, conf_scale, D, order_mix,
 
 @torch.no_grad()
 def memory_mixer_step(proj, cache, conv_w, conv_b, beta_bias, dt_bias, a_log, floor, conf_scale, D, order_mix,
-                      scale, *, heads, bound, beta_max, eps, order_head=True):
+                      scale, *, heads, bound, beta_max, eps, order_head=True, inplace=False):
     """One cached token of the memory mixer (`lm/models/mamba4.py:127-337`
     with a cache) in three launches: `m4_memmix_prep_step` (conv over the
     history rows and the current one, SiLU, unit key and query, gates),
@@ -438,6 +440,8 @@ def memory_mixer_step(proj, cache, conv_w, conv_b, beta_bias, dt_bias, a_log, fl
     projection rows, zero before the sequence start), shifted [B,h,64] (the
     previous token's unit key, zero at the first token), memory
     (SelectiveState), order [B,h,128]). Returns (y [B, 128h] bf16, new cache).
+    inplace=True writes the new memory state over the cached one (see
+    `selective_decode`); the other cache entries are always fresh tensors.
     """
     from .memory import selective_decode
 
@@ -459,7 +463,8 @@ def memory_mixer_step(proj, cache, conv_w, conv_b, beta_bias, dt_bias, a_log, fl
         ctypes.byref(dims), window[..., inner:].data_ptr(), *map(_lib.ptr, (f32(conv_w), f32(conv_b))),
         float(bound), *map(_lib.ptr, (f32(beta_bias), f32(dt_bias), f32(a_log), values, keys, queries, beta,
                                       log_decay, order_logit)), _stream()), "m4_memmix_prep_step")
-    res = selective_decode(cache["memory"], cache["shifted"], values, queries, beta, log_decay, floor)
+    res = selective_decode(cache["memory"], cache["shifted"], values, queries, beta, log_decay, floor,
+                           inplace=inplace)
     y = torch.empty(batch, inner, dtype=torch.bfloat16, device=dev)
     order = torch.empty_like(values) if order_head else None
     pdims = _memmix_dims(batch, 1, heads, width, width, beta_max)

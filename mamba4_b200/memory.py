@@ -173,7 +173,7 @@ def selective_memory_fused(
     return SelectiveResult(out[..., :value_dim], var, state)
 
 
-def selective_decode(state, key, value, query, beta, log_decay, floor, solver=None):
+def selective_decode(state, key, value, query, beta, log_decay, floor, solver=None, inplace=False):
     """One exact write/read against a carried state (`lm/kernels/mamba4.py:341-355`).
 
     state: SelectiveState(evidence [B,H,D,D], cross [B,H,P,D]); key, query
@@ -184,6 +184,8 @@ def selective_decode(state, key, value, query, beta, log_decay, floor, solver=No
     `solver` is accepted for signature compatibility ("cuda"/"fused"/None).
     Key dims below 64 are padded with an identity block as in
     `selective_memory_fused`. No gradient (the reference decodes without one).
+    With inplace=True the new state is written over `state`'s tensors
+    (float32, contiguous, unpadded dims) instead of fresh ones.
     """
     if solver not in (None, *SOLVERS):
         raise ValueError(f"Unknown SPD solve backend {solver}")
@@ -218,7 +220,9 @@ def selective_decode(state, key, value, query, beta, log_decay, floor, solver=No
     f = _pad_last(floor, KEY_DIM, 1.0).contiguous()
     out = torch.empty(batch, heads, pv, device=dev)
     var = torch.empty(batch, heads, device=dev)
-    ev_out, cr_out = torch.empty_like(ev), torch.empty_like(cr)
+    # In place the kernel reads all of E before writing E' and each row of C
+    # before writing that row.
+    ev_out, cr_out = (ev, cr) if inplace else (torch.empty_like(ev), torch.empty_like(cr))
     dims = _dims(batch, 1, heads, pv)
     lib = _lib.load()
     _lib.check(

@@ -143,7 +143,7 @@ class Mamba3Mixer(nn.Module):
         cfg = self.cfg
         return mamba3_step_cache(batch, cfg.num_heads, cfg.d_state, cfg.head_dim, self.angles, device=device)
 
-    def decode(self, u, cache: Mamba3StepCache):
+    def decode(self, u, cache: Mamba3StepCache, inplace=False):
         """One token (`_Mamba3StepMixer`, `lm/models/mamba4.py:412-481`):
         u [B, d_model] bf16 -> ([B, d_model], new cache) through the
         training glue's prep and post kernels around the scan step (same
@@ -155,7 +155,7 @@ class Mamba3Mixer(nn.Module):
             out, cache = mamba_mixer_step(proj.to(torch.bfloat16), self.B_norm.scale, self.C_norm.scale,
                                           self.dt_bias, self.D, self.C_bias, self.B_bias, cache,
                                           inner=cfg.inner, heads=cfg.num_heads, angles=self.angles,
-                                          eps=cfg.norm_eps)
+                                          eps=cfg.norm_eps, inplace=inplace)
         return self.out_proj(out), cache
 
 
@@ -264,7 +264,7 @@ class SelectiveMemoryMixer(nn.Module):
                     order=torch.zeros(batch, h, p, device=device),
                     shifted=torch.zeros(batch, h, d, device=device))
 
-    def decode(self, u, cache):
+    def decode(self, u, cache, inplace=False):
         """One token of the cached memory mixer (`lm/models/mamba4.py:127-337`
         with `cache`) through `memory_mixer_step`: the training glue's
         kernels at one token (same rounding points) around the one-token
@@ -282,7 +282,8 @@ class SelectiveMemoryMixer(nn.Module):
             out, cache = memory_mixer_step(
                 proj, cache, self.conv_weight, self.conv_bias, self.beta_bias, self.dt_bias, self.a_log, floor,
                 self.confidence_scale, self.D, self.order_mix, self.read_norm.scale, heads=cfg.memory_heads,
-                bound=self.bound, beta_max=cfg.memory_beta_max, eps=cfg.norm_eps, order_head=cfg.order_head)
+                bound=self.bound, beta_max=cfg.memory_beta_max, eps=cfg.norm_eps, order_head=cfg.order_head,
+                inplace=inplace)
         return self.out_proj(out), cache
 
 
@@ -337,16 +338,18 @@ class Mamba4LM(nn.Module):
         return [block.mixer.init_cache(batch, device=device) for block in self.blocks]
 
     @torch.no_grad()
-    def decode_step(self, tokens, cache):
+    def decode_step(self, tokens, cache, inplace=False):
         """One cached decode step (`lm/models/mamba4.py:507-524`): tokens [B]
         -> (logits [B, V] float32, new cache). Run under the same autocast as
-        the forward."""
+        the forward. inplace=True writes the layers' scan states and memory
+        states over `cache`'s tensors (the graph decoder's static cache)
+        instead of fresh ones."""
         x = self.embedding(tokens).to(torch.bfloat16)
         new = []
         fused = x.shape[-1] in ADD_RMS_FEATURES
         h = self.blocks[0].norm(x)
         for i, (block, layer) in enumerate(zip(self.blocks, cache)):
-            out, layer = block.mixer.decode(h, layer)
+            out, layer = block.mixer.decode(h, layer, inplace=inplace)
             new.append(layer)
             norm = self.blocks[i + 1].norm if i + 1 < len(self.blocks) else self.final_norm
             if fused:
@@ -419,7 +422,7 @@ class GraphedDecoder:
     @torch.no_grad()
     def _body(self):
         with torch.autocast("cuda", dtype=self.dtype):
-            logits, new = self.model.decode_step(self.tokens, self.cache)
+            logits, new = self.model.decode_step(self.tokens, self.cache, inplace=True)
         for dst, src in zip(self._static, _cache_tensors(new)):
             if dst.data_ptr() != src.data_ptr():
                 dst.copy_(src)
