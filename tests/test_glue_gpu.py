@@ -309,3 +309,26 @@ def test_add_rms_norm_matches_add_then_norm():
         assert torch.equal(xo, ref)
         assert torch.equal(y, rms_norm_bf16(ref, scale, 1e-5))
         assert rel(y, composite_rms(ref, scale, 1e-5)) < 1e-2
+
+
+def test_single_shifted_token_leaves_only_the_floor():
+    """lm/tests/test_mamba4.py:364-376: with the key shift the first token
+    writes a zero key, so after one token the evidence is exactly zero and
+    the precision is the floor itself."""
+    from mamba4_b200.glue import memory_mixer_prep
+    from mamba4_b200.memory import selective_memory_fused
+
+    torch.manual_seed(13)
+    heads, C = 4, 256 * 4
+    rest = torch.randn(3, 1, 259 * heads + (-259 * heads) % 8, device="cuda").to(torch.bfloat16)
+    rest = rest[..., : 259 * heads]
+    value, key, query, beta, log_decay, _ = memory_mixer_prep(
+        rest, torch.rand(4, C, device="cuda"), torch.randn(C, device="cuda"), torch.randn(heads, device="cuda"),
+        torch.randn(heads, device="cuda"), torch.rand(heads, device="cuda"), heads=heads, bound=0.5, beta_max=1.0)
+    assert torch.count_nonzero(key) == 0
+    floor = 0.25 + torch.rand(heads, 64, device="cuda")
+    res = selective_memory_fused(key, value, query, beta, log_decay, floor)
+    assert torch.count_nonzero(res.state.evidence) == 0
+    precision = res.state.evidence + torch.diag_embed(floor)[None]
+    eig = torch.linalg.eigvalsh(precision.double())
+    assert torch.allclose(eig[..., -1], floor.double().max(-1).values[None].expand_as(eig[..., -1]), rtol=1e-6)

@@ -193,6 +193,23 @@ def test_scan_oracle_chunked_equals_local_frame(length, chunk):
     np.testing.assert_allclose(y.numpy(), ref[..., 0, :], rtol=1e-10, atol=1e-10)
 
 
+@pytest.mark.parametrize("chunk", [1, 4, 16])
+def test_scan_euler_limit_is_hebbian(chunk):
+    # analysis/tests/test_memory.py:105-109: with the trapezoid entirely on the
+    # current token (sigmoid(trap_logit) = 1), unit steps, no decay and no
+    # rotation, the scan read is the Hebbian read y_t = sum_{s<=t} (q_t.k_s) v_s.
+    rng = np.random.default_rng(24)
+    batch, time, heads, state, width = 2, 9, 3, 8, 5
+    q, k = rng.normal(size=(batch, time, heads, state)), rng.normal(size=(batch, time, heads, state))
+    v = rng.normal(size=(batch, time, heads, width))
+    ones = np.ones((batch, time, heads))
+    t = lambda a: torch.tensor(a, dtype=torch.float64)  # noqa: E731
+    y, _ = S.chunked_scan(t(q), t(k), t(v), t(0 * ones), t(ones), t(50 * ones),
+                          t(np.zeros((batch, time, heads, 2))), chunk=chunk)
+    scores = np.einsum("bthn,bshn->bhts", q, k) * np.tril(np.ones((time, time)))
+    np.testing.assert_allclose(y.numpy(), np.einsum("bhts,bshp->bthp", scores, v), rtol=1e-10, atol=1e-10)
+
+
 def test_scan_no_future_leakage():
     # lm/tests/test_mamba3_transformer.py:72-77: outputs before t ignore inputs after t.
     cfg = S.config_inputs(1, 40, 2, 8, 8, seed=5)
