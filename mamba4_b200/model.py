@@ -298,10 +298,6 @@ class Block(nn.Module):
     def forward(self, x):
         return x + self.mixer(self.norm(x)).to(x.dtype)
 
-    def decode(self, x, cache):
-        out, cache = self.mixer.decode(self.norm(x), cache)
-        return x + out.to(x.dtype), cache
-
 
 class Mamba4LM(nn.Module):
     """`Mamba4LM` (`lm/models/mamba4.py:484-504`): embedding, blocks per the
