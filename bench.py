@@ -386,7 +386,7 @@ def measure_e2e_hotpath(m, s, dev, world, tokens, args):
                 t.record_stream(copy_out)
                 h.copy_(t, non_blocking=True)
 
-    n = max(2, args.steps // 2)
+    n = args.steps
     e2e_ms = max_over_ranks(time_region(e2e_step, n, args.warmup, world, streams=(copy_in, copy_out)),
                             world) / n
     return {"value": world * tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
