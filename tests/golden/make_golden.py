@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the CPU oracle to the reference.
 
-Run in a checkout that has the reference tree (tasmaikeni13/mamba4) at
-$MAMBA4_REFERENCE (default /root/reference):
+Run with MAMBA4_REFERENCE set to a checkout of the reference tree
+(tasmaikeni13/mamba4):
 
-    python tests/golden/make_golden.py
+    MAMBA4_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's own NumPy operator code, which runs without JAX:
 `analysis/memory.py` (EvidenceState.write/read/confidence, mamba3_core) and
@@ -22,7 +22,9 @@ HERE = Path(__file__).resolve().parent
 
 
 def _reference():
-    root = os.environ.get("MAMBA4_REFERENCE", "/root/reference")
+    root = os.environ.get("MAMBA4_REFERENCE")
+    if not root:
+        raise SystemExit("set MAMBA4_REFERENCE to the reference checkout (tasmaikeni13/mamba4)")
     sys.path.insert(0, root)
     from analysis.gradients import terminal_stream_vjp
     from analysis.memory import EvidenceState, mamba3_core
