@@ -332,3 +332,38 @@ def test_single_shifted_token_leaves_only_the_floor():
     precision = res.state.evidence + torch.diag_embed(floor)[None]
     eig = torch.linalg.eigvalsh(precision.double())
     assert torch.allclose(eig[..., -1], floor.double().max(-1).values[None].expand_as(eig[..., -1]), rtol=1e-6)
+
+
+def test_mamba_mixer_step_matches_composite():
+    """Three-launch cached Mamba-3 mixer core (`mamba_mixer_step`) against the
+    PyTorch composition of the same token (B/C RMSNorm, dt softplus,
+    heavy-tail decay around `mamba3_step`, D skip and SiLU gate) over several
+    tokens: outputs to bf16 rounding, caches to float32 rounding."""
+    from mamba4_b200.flashmamba import mamba3_step, mamba3_step_cache
+    from mamba4_b200.glue import mamba_mixer_step
+
+    torch.manual_seed(14)
+    batch, heads, angles, eps = 3, 4, 16, 1e-5
+    inner = 64 * heads
+    width = 2 * inner + 128 + 3 * heads + angles
+    bs, cs = 1 + 0.1 * torch.randn(64, device="cuda"), 1 + 0.1 * torch.randn(64, device="cuda")
+    dtb, D = torch.randn(heads, device="cuda") - 3, torch.randn(heads, device="cuda")
+    qb, kb = torch.ones(heads, 1, 64, device="cuda"), torch.ones(heads, 1, 64, device="cuda")
+    ca = mamba3_step_cache(batch, heads, 64, 64, angles, device="cuda")
+    cb = mamba3_step_cache(batch, heads, 64, 64, angles, device="cuda")
+    for _ in range(5):
+        proj = torch.randn(batch, width, device="cuda").to(torch.bfloat16)
+        ya, ca = mamba_mixer_step(proj, bs, cs, dtb, D, qb, kb, ca, inner=inner, heads=heads, angles=angles,
+                                  eps=eps)
+        z, x, b, c, raw_dt, raw_a, trap, ang = torch.split(
+            proj, (inner, inner, 64, 64, heads, heads, heads, angles), -1)
+        dt = F.softplus(raw_dt.float() + dtb)
+        adt = -torch.clamp(heavy_tail(raw_a.float()), min=1e-4) * dt
+        y, cb = mamba3_step(cb, composite_rms(c, cs, eps), composite_rms(b, bs, eps), x.contiguous(), adt, dt,
+                            trap.float(), ang.float(), q_bias=qb, k_bias=kb)
+        yh = y.float().reshape(batch, heads, 64) + x.float().reshape(batch, heads, 64) * D[:, None]
+        zf = z.float().reshape(batch, heads, 64)
+        yb = (yh * (zf * torch.sigmoid(zf))).to(torch.bfloat16).reshape(batch, inner)
+        assert rel(ya, yb) < 1e-2
+        for ta, tb in zip(ca, cb):
+            assert rel(ta, tb) < 1e-2
