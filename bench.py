@@ -345,6 +345,12 @@ def run_reference(args):
 
 
 def measure_e2e_hotpath(m, s, dev, world, tokens, args):
+    """The hot-path step through the public operators with every input copied
+    in from pinned host memory and every output and gradient copied back,
+    pipelined over two device input slots and two pinned output slots: step
+    i+1's inputs cross on one copy stream and step i's results on another
+    while step i computes. Times the same K steps as the device-timed line
+    (max over ranks); returns the `e2e` JSON object."""
     import torch
 
     pin = [{k: v.detach().cpu().pin_memory() for k, v in src.items()} for src in (m, s)]
