@@ -196,9 +196,11 @@ int m4_scan_step(const M4ScanDims* dims, const float* state, const float* prev_k
  * x heads up to about 36,000); larger problems return M4_ERR_WORKSPACE and
  * launch nothing. The first call on a device looks up the array's device
  * address (with the current device) - make that first call before any
- * stream capture. All calls share the one array: calls that overlap on the
- * GPU (on different streams) race and must not be issued. Nothing in the
- * array needs clearing between calls. */
+ * stream capture. The address is kept for the life of the process, so the
+ * device's context must not be reset (cudaDeviceReset) between calls. All
+ * calls share the one array: calls that overlap on the GPU (on different
+ * streams) race and must not be issued. Nothing in the array needs clearing
+ * between calls: every scratch byte a call reads, it writes first. */
 int m4_scan_bwd_noalloc(const M4ScanDims* dims, const void* c, const void* b, const void* x,
                         const float* adt, const float* dt, const float* trap_logits,
                         const float* angles, const float* q_bias, const float* k_bias,
