@@ -13,9 +13,10 @@ job total. `e2e` is the same metric through the public operator API with the
 inputs copied from pinned host memory and every output and gradient copied
 back inside the timed region.
 
-`--impl reference` times the reference's CPU algorithm for the same
-workload (the float64 oracle port; the reference's JAX runtime is not
-installed) on all host cores, on a bounded sample per step.
+`--impl reference` times the reference's CPU path for the same workload
+(its XLA algorithms restated in float32 PyTorch, `oracle/cpu_path.py`; the
+reference's JAX runtime is not installed) on all host cores: K whole steps,
+each a bounded sample of whole sequences in the workload's token mix.
 """
 
 from __future__ import annotations
@@ -275,38 +276,60 @@ def op_times(fn_fwd, fn_bwd, reps=5):
     return statistics.median(fwd_ms), statistics.median(bwd_ms)
 
 
-def cpu_baseline_sample(mem_cfg, scan_cfg, threads):
-    """Oracle port on the host: a bounded sample of each layer, extrapolated
-    to the step's token counts. Returns (tokens/s, description)."""
-    import numpy as np
+CPU_SAMPLE_MEM_SEQS = 8   # memory-read sequences per CPU sample step (of configs[2])
+CPU_SAMPLE_SCAN_SEQS = 1  # scan sequences per CPU sample step (of configs[1]): the 8:1 token mix
+
+
+def cpu_sample_inputs(mem_cfg, scan_cfg):
+    """One bounded sample of the hot-path workload for the CPU baseline:
+    CPU_SAMPLE_MEM_SEQS whole sequences of the memory-read config and
+    CPU_SAMPLE_SCAN_SEQS of the scan config (full length, all heads, the
+    workload's own mix of memory-read to scan tokens), float32 host tensors
+    from the oracle's seeded generators (the scan's c, b, x rounded to bf16
+    as the GPU step's inputs are)."""
     import torch
 
     from oracle import memread as M
     from oracle import scan as S
 
+    mseq = min(CPU_SAMPLE_MEM_SEQS, mem_cfg["batch"])
+    sseq = min(CPU_SAMPLE_SCAN_SEQS, scan_cfg["batch"])
+    cfg = M.config_inputs(mseq, mem_cfg["time"], mem_cfg["heads"], mem_cfg["dim"], mem_cfg["value_dim"], seed=0)
+    mem = {n: torch.tensor(v) for n, v in cfg.items()}
+    sc = S.config_inputs(sseq, scan_cfg["time"], scan_cfg["heads"], scan_cfg["head_dim"],
+                         scan_cfg["state_dim"], seed=1)
+    scan = {n: torch.tensor(v) for n, v in sc.items()}
+    for n in ("c", "b", "x", "d_y"):
+        scan[n] = scan[n].to(torch.bfloat16).float()
+    tokens = mseq * mem_cfg["time"] + sseq * scan_cfg["time"]
+    desc = (f"reference CPU path restated in float32 PyTorch (oracle/cpu_path.py: the XLA memory read of "
+            f"selective_gaussian_memory with the spd_solve VJP, and mamba3_chunked), value and gradient of "
+            f"the projected loss; one step = {mseq} x {mem_cfg['time']} tokens x {mem_cfg['heads']} heads of "
+            f"the memory read + {sseq} x {scan_cfg['time']} tokens x {scan_cfg['heads']} heads of the scan "
+            f"({tokens} tokens, the workload's token mix)")
+    return mem, scan, tokens, desc
+
+
+def cpu_sample_step(mem, scan):
+    from oracle import cpu_path as C
+
+    C.memory_step(mem)
+    C.scan_step(scan)
+
+
+def cpu_baseline_sample(mem_cfg, scan_cfg, threads):
+    """The CPU restatement of the reference path on the host's cores: one
+    warm-up and one timed sample step (whole sequences, not extrapolated).
+    Returns (tokens/s, seconds per sample step, description)."""
+    import torch
+
     torch.set_num_threads(threads)
-    mt = 256  # memory-read sample: 1 sequence x 256 tokens x all heads
-    cfg = M.config_inputs(1, mt, mem_cfg["heads"], mem_cfg["dim"], mem_cfg["value_dim"], seed=0)
-    names = ("keys", "values", "queries", "beta", "log_decay", "floor")
+    mem, scan, tokens, desc = cpu_sample_inputs(mem_cfg, scan_cfg)
+    cpu_sample_step(mem, scan)
     t0 = time.perf_counter()
-    M.chunked_forward(*[cfg[n] for n in names])
-    M.chunked_backward(*[cfg[n] for n in names], None, cfg["d_output"], cfg["d_variance"])
-    t_mem = time.perf_counter() - t0
-    st = 1024
-    sc = S.config_inputs(1, st, scan_cfg["heads"], scan_cfg["head_dim"], scan_cfg["state_dim"], seed=1)
-    keys = ("c", "b", "x", "adt", "dt", "trap_logits", "angles", "q_bias", "k_bias")
-    t0 = time.perf_counter()
-    S.fused_layout_scan(*[torch.tensor(sc[n], dtype=torch.float64) for n in keys])
-    S.fused_layout_grads([sc[n] for n in keys], sc["d_y"], sc["d_final"])
-    t_scan = time.perf_counter() - t0
-    mem_tokens = mem_cfg["batch"] * mem_cfg["time"]
-    scan_tokens = scan_cfg["batch"] * scan_cfg["time"]
-    per_step = t_mem * mem_tokens / mt + t_scan * scan_tokens / st
-    del np
-    return (mem_tokens + scan_tokens) / per_step, (
-        f"oracle port float64: memory read fwd+bwd on 1x{mt} tokens x {mem_cfg['heads']} heads "
-        f"({t_mem:.2f} s) and scan fwd+bwd on 1x{st} tokens x {scan_cfg['heads']} heads "
-        f"({t_scan:.2f} s), extrapolated linearly to the step's token counts")
+    cpu_sample_step(mem, scan)
+    dt = time.perf_counter() - t0
+    return tokens / dt, dt, desc
 
 
 def host_threads():
@@ -316,31 +339,47 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def hotpath_config(workload, mem_cfg, scan_cfg):
+    """The `config` object of the hot-path line (both arms)."""
+    tokens = mem_cfg["batch"] * mem_cfg["time"] + scan_cfg["batch"] * scan_cfg["time"]
+    return {"workload": {"hotpath": "configs[1]+configs[2] (hotpath)",
+                         "small": "small memory read (16x1024x8) + configs[1] scan",
+                         "profile": "ncu-sized memory read (4x1024x8) + scan (4x1024x16)"}[workload],
+            "memread": mem_cfg, "scan": dict(scan_cfg, chunk=64, dtype="bf16"),
+            "tokens_per_step_per_gpu": tokens, "l2": "inputs larger than L2 (memory-read "
+            "operands 268 MB each, stored factors 9.7 GB)"}
+
+
 def run_reference(args):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    """The reference arm: rank 0 times K steps (after W warm-up steps) of the
+    reference's CPU path, restated in float32 PyTorch, on all host threads.
+    Each step is one bounded sample of the workload (see cpu_sample_inputs);
+    ms_per_step is the measured time of that sample step and value its tokens
+    per second. Other ranks exit without work."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     threads = host_threads()
-    tokens = MEM_CFG["batch"] * MEM_CFG["time"] + SCAN_CFG["batch"] * SCAN_CFG["time"]
-    rates, desc = [], ""
-    for i in range(args.warmup + args.steps):
-        rate, desc = cpu_baseline_sample(MEM_CFG, SCAN_CFG, threads)
-        if i >= args.warmup:
-            rates.append(rate)
-    value = statistics.median(rates)
+    torch.set_num_threads(threads)
+    mem, scan, tokens, desc = cpu_sample_inputs(MEM_CFG, SCAN_CFG)
+    for _ in range(args.warmup):
+        cpu_sample_step(mem, scan)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_sample_step(mem, scan)
+    ms_per_step = 1000.0 * (time.perf_counter() - t0) / args.steps
+    value = tokens / (ms_per_step / 1000.0)
     line = {
         "impl": "reference", "metric": "memory-read+scan tokens/s fwd+bwd", "value": value,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * tokens / value, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": "configs[1]+configs[2] (hotpath)", "tokens_per_step": tokens,
-                   "cpu": "reference CPU algorithm (oracle port; jax not installed)"},
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": hotpath_config("hotpath", MEM_CFG, SCAN_CFG),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    del world
     print(json.dumps(line), flush=True)
 
 
@@ -530,19 +569,14 @@ def run_ours(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+bf16",
         "data": "synthetic",
-        "config": {"workload": {"hotpath": "configs[1]+configs[2] (hotpath)",
-                                "small": "small memory read (16x1024x8) + configs[1] scan",
-                                "profile": "ncu-sized memory read (4x1024x8) + scan (4x1024x16)"}[args.workload],
-                   "memread": mem_cfg, "scan": dict(scan_cfg, chunk=64, dtype="bf16"),
-                   "tokens_per_step_per_gpu": tokens, "l2": "inputs larger than L2 (memory-read "
-                   "operands 268 MB each, stored factors 9.7 GB)"},
+        "config": hotpath_config(args.workload, mem_cfg, scan_cfg),
         "roofline": roofline, "components": components, "e2e": e2e,
         "gpu_launches": launches(step, args.steps), "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, desc = cpu_baseline_sample(mem_cfg, scan_cfg, host_threads())
+        rate, step_s, desc = cpu_baseline_sample(mem_cfg, scan_cfg, host_threads())
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": host_threads(),
-                                "kind": "port", "sample": desc}
+                                "kind": "port", "sample": f"{desc}; one timed step of {step_s:.2f} s"}
     if not args.no_lm and args.workload == "hotpath":
         # The second half of the metric: the data-parallel 60M LM training
         # step on the same ranks (one NCCL gradient all-reduce per step).

@@ -42,15 +42,19 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     obj_dir = HERE / "_build"
     obj_dir.mkdir(exist_ok=True)
-    objects = []
+    objects, procs = [], []
+    # The translation units compile in parallel (one nvcc process each).
     for name in SOURCES:
         obj = obj_dir / (Path(name).stem + ".o")
         cmd = [nvcc(), *ARCH, *FLAGS, "-c", str(SRC / name), "-o", str(obj)]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        procs.append((cmd, subprocess.Popen(cmd)))
         objects.append(str(obj))
+    failed = [cmd for cmd, proc in procs if proc.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
     tmp = LIB.with_suffix(".so.tmp")
     subprocess.run([nvcc(), *ARCH, "-shared", "-o", str(tmp), *objects], check=True)
     os.replace(tmp, LIB)

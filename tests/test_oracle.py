@@ -263,3 +263,55 @@ def test_decode_oracles_step_through_the_sequence_oracles():
     scale = float(ey.abs().max())
     assert float((torch.stack(ys, 1) - ey).abs().max()) < 1e-12 * scale
     assert float((cache[0] - ef).abs().max()) < 1e-12 * float(ef.abs().max())
+
+
+def test_spd_solve_vjp_is_the_derivative_along_symmetric_directions():
+    # lm/kernels/mamba4.py:208-215: d rhs = z and dA = -sym(z y^T) give the
+    # directional derivative of <g, y> along any symmetric perturbation of A
+    # (the only directions the lower-triangle read sees) and along rhs.
+    rng = np.random.default_rng(3)
+    m = rng.normal(size=(4, 6, 6))
+    a = m @ np.swapaxes(m, -1, -2) + 0.5 * np.eye(6)
+    rhs = rng.normal(size=(4, 6))
+    g = rng.normal(size=(4, 6))
+    da, dr = M.spd_solve_vjp(a, rhs, g)
+    e = rng.normal(size=(4, 6, 6))
+    e = e + np.swapaxes(e, -1, -2)
+    f = rng.normal(size=(4, 6))
+    h = 1e-6
+    fd = (np.sum(g * M.spd_solve(a + h * e, rhs + h * f)) - np.sum(g * M.spd_solve(a - h * e, rhs - h * f))) / (2 * h)
+    np.testing.assert_allclose(np.sum(da * e) + np.sum(dr * f), fd, rtol=1e-6)
+    # Only the lower triangle is read.
+    upper = np.triu(rng.normal(size=(4, 6, 6)), 1)
+    np.testing.assert_allclose(M.spd_solve(a + upper, rhs), M.spd_solve(a, rhs), rtol=1e-12)
+
+
+def test_cpu_timing_path_equals_the_oracle():
+    # oracle/cpu_path.py (the timed CPU baseline: the reference's XLA path
+    # restated in PyTorch) computes the same operators as the float64 oracle.
+    import torch
+
+    from oracle import cpu_path as C
+    from oracle import scan as S
+
+    cfg = M.config_inputs(2, 100, 3, 64, 64, seed=4)
+    names = ("keys", "values", "queries", "beta", "log_decay", "floor")
+    t = {n: torch.tensor(cfg[n], dtype=torch.float64) for n in cfg}
+    loss, grads = C.memory_step(t)
+    fwd = M.chunked_forward(*[cfg[n] for n in names])
+    ref_loss = np.sum(fwd["output"] * cfg["d_output"]) + np.sum(fwd["variance"] * cfg["d_variance"])
+    np.testing.assert_allclose(float(loss), ref_loss, rtol=1e-9)
+    bwd = M.chunked_backward(*[cfg[n] for n in names], None, cfg["d_output"], cfg["d_variance"])
+    for g, n in zip(grads, names):
+        np.testing.assert_allclose(g.numpy(), bwd[n], rtol=1e-7, atol=1e-9 * np.abs(bwd[n]).max())
+    sc = S.config_inputs(2, 130, 3, 64, 64, seed=5)
+    keys = ("c", "b", "x", "adt", "dt", "trap_logits", "angles", "q_bias", "k_bias")
+    st = {n: torch.tensor(sc[n], dtype=torch.float64) for n in sc}
+    y, final = C.mamba3_scan(*[st[n] for n in keys])
+    ey, ef = S.fused_layout_scan(*[st[n] for n in keys])
+    np.testing.assert_allclose(y.numpy(), ey.numpy(), rtol=1e-9, atol=1e-12)
+    np.testing.assert_allclose(final.numpy(), ef.numpy(), rtol=1e-9, atol=1e-12)
+    _, sg = C.scan_step(st)
+    eg = S.fused_layout_grads([sc[n] for n in keys], sc["d_y"], sc["d_final"])
+    for g, e, n in zip(sg, eg, keys):
+        np.testing.assert_allclose(g.numpy(), e.numpy(), rtol=1e-7, atol=1e-9 * float(e.abs().max()), err_msg=n)

@@ -54,10 +54,22 @@ def _worker(rank, world, port, out):
         tokens, targets, mask = batch()
         rows = slice(rank * 2, rank * 2 + 2)
         trainer = DataParallelTrainer(Tiny(), SETTINGS, world=world)
-        loss, count, norm = trainer.step(tokens[rows], targets[rows], mask[rows])
+        calls = []
+        plain = dist.all_reduce
+
+        def counting(*args, **kwargs):
+            calls.append(args[0].numel())
+            return plain(*args, **kwargs)
+
+        dist.all_reduce = counting
+        try:
+            loss, count, norm = trainer.step(tokens[rows], targets[rows], mask[rows])
+        finally:
+            dist.all_reduce = plain
         if rank == 0:
             out.put({"loss": float(loss), "count": float(count), "norm": float(norm),
-                     "params": [p.detach().tolist() for p in trainer.model.parameters()]})
+                     "params": [p.detach().tolist() for p in trainer.model.parameters()],
+                     "all_reduce_sizes": calls})
     finally:
         dist.destroy_process_group()
 
@@ -83,6 +95,10 @@ def test_two_rank_step_equals_single_process_with_uneven_masks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
+    # One collective per step: the tiny model's gradients fit one bucket, which
+    # also carries the target count and loss numerator (2 extra floats).
+    n_params = sum(p.numel() for p in single.model.parameters())
+    assert result["all_reduce_sizes"] == [n_params + 2]
     assert result["count"] == float(count1) == 11.0
     assert abs(result["loss"] - float(loss1)) < 1e-6
     assert abs(result["norm"] - float(norm1)) < 1e-5
