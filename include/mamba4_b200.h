@@ -113,6 +113,28 @@ int m4_memread_decode(const M4MemDims* dims, const float* evidence, const float*
                       float* output, float* variance, float* evidence_out, float* cross_out,
                       void* stream);
 
+/* Standalone SPD solve. Replaces spd_solve (lm/kernels/mamba4.py:187-218)
+ * with its factorization backends (_cholesky_loop / _cholesky_blocked /
+ * _cholesky_unrolled, :31-125, and _triangular_solves, :138-158): for each of
+ * `count` matrices, solve precision y = rhs with a Cholesky factorization.
+ *   precision [count, dim, dim] row-major, SPD, only the lower triangle read;
+ *   rhs, solution [count, dim]; dim 1..64 (orders below 64 are padded with an
+ *   identity block inside the kernel). No alignment needed for these.
+ *   factor: the stored Cholesky factor for the backward, sized by
+ *   m4_spd_solve_factor_bytes (9,216 bytes per matrix, 16-byte aligned).
+ * count 0 launches nothing and returns M4_OK. */
+size_t m4_spd_solve_factor_bytes(int count, int dim);
+int m4_spd_solve_fwd(int count, int dim, const float* precision, const float* rhs,
+                     float* solution, void* factor, size_t factor_bytes, void* stream);
+
+/* Backward of m4_spd_solve_fwd (_spd_solve_backward, lm/kernels/mamba4.py:208-215):
+ * z = precision^-1 d_solution from the stored factor, d_rhs = z [count, dim],
+ * d_precision = -(z y^T + y z^T) / 2 [count, dim, dim] (every entry, the
+ * reference's symmetric cotangent), y = the forward's solution. */
+int m4_spd_solve_bwd(int count, int dim, const void* factor, size_t factor_bytes,
+                     const float* solution, const float* d_solution, float* d_precision,
+                     float* d_rhs, void* stream);
+
 /* Scan problem size (projection layout of mamba3_fused). */
 typedef struct {
   int batch;        /* B */

@@ -3,7 +3,7 @@
 Operators (reference `lm/kernels` surface):
   memory:      selective_memory_fused, selective_gaussian_memory,
                selective_decode, SelectiveState, SelectiveResult,
-               selective_initial_state
+               selective_initial_state, spd_solve
   flashmamba:  mamba3_fused, mamba3_flash, mamba3_flash_heads, angle_rates,
                mamba3_step, mamba3_step_cache, Mamba3StepCache
 Compute runs in the in-tree CUDA library `libmamba4_b200.so` (C ABI in
@@ -17,6 +17,7 @@ from .memory import (  # noqa: F401
     selective_gaussian_memory,
     selective_initial_state,
     selective_memory_fused,
+    spd_solve,
 )
 from .flashmamba import (  # noqa: F401
     Mamba3StepCache,

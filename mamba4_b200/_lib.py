@@ -55,6 +55,9 @@ SIGNATURES = {
     "m4_memread_bwd": ([ctypes.POINTER(MemDims)] + [_p] * 9 + [_size] + [_p] * 12
                        + [_p, _size, _p], _c_int),
     "m4_memread_decode": ([ctypes.POINTER(MemDims)] + [_p] * 12 + [_p], _c_int),
+    "m4_spd_solve_factor_bytes": ([_c_int, _c_int], _size),
+    "m4_spd_solve_fwd": ([_c_int, _c_int] + [_p] * 4 + [_size, _p], _c_int),
+    "m4_spd_solve_bwd": ([_c_int, _c_int, _p, _size] + [_p] * 4 + [_p], _c_int),
     "m4_scan_residual_bytes": ([ctypes.POINTER(ScanDims)], _size),
     "m4_scan_workspace_bytes": ([ctypes.POINTER(ScanDims)], _size),
     "m4_scan_fwd": ([ctypes.POINTER(ScanDims)] + [_p] * 11 + [_p, _size, _p], _c_int),

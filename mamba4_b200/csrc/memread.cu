@@ -809,6 +809,118 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
 }
 
 // ---------------------------------------------------------------------------
+// spd_solve: standalone SPD solves precision @ y = rhs (spd_solve,
+// lm/kernels/mamba4.py:187-218) for `count` matrices of order dim <= 64.
+// One warp per matrix with the solve kernel's lane layout. Only the lower
+// triangle of each row-major [dim][dim] matrix is read (the upper entries of
+// the register tiles are mirrored from it); orders below 64 are padded with
+// an identity block and a zero right-hand side, which solves to zero. The
+// factor is stored in the memory read's layout (LSTRIDE floats per matrix,
+// 8x8 diagonal blocks inverted) for the backward.
+// ---------------------------------------------------------------------------
+M4_DEV float spd_entry(const float* M, int dim, int r, int c) {
+  if (r >= dim || c >= dim) return r == c ? 1.f : 0.f;
+  return r >= c ? M[r * dim + c] : M[c * dim + r];
+}
+
+__global__ void __launch_bounds__(32 * WARPS) spd_fwd_kernel(
+    int count, int dim, const float* __restrict__ precision, const float* __restrict__ rhs,
+    float* __restrict__ solution, float* __restrict__ Lst) {
+  extern __shared__ __align__(16) unsigned char spd_raw[];
+  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(spd_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int a = lane >> 3, b = lane & 7;
+  const int m = blockIdx.x * WARPS + warp;
+  if (m >= count) return;
+  SolveSmem& sm = smem_all[warp];
+  const float* src = precision + size_t(m) * dim * dim;
+  float2 A[NPAIR];
+#pragma unroll
+  for (int q = 0; q < NPAIR; ++q) {
+    const int p = pair_p(q), n = pair_n(q);
+    A[q] = make_float2(spd_entry(src, dim, a + 8 * p, b + 8 * n), spd_entry(src, dim, a + 4 + 8 * p, b + 8 * n));
+  }
+  float wr[8];
+  const float* g = rhs + size_t(m) * dim;
+#pragma unroll
+  for (int n = 0; n < 8; ++n) wr[n] = (a == 0 && b + 8 * n < dim) ? g[b + 8 * n] : 0.f;
+  float rc[8];
+#pragma unroll
+  for (int n = 0; n < 8; ++n) rc[n] = 0.f;
+  factor_all<0>(A, wr, rc, sm, a, b);
+  if (a == 0) {
+#pragma unroll
+    for (int n = 0; n < 8; ++n) sm.w[b + 8 * n] = wr[n] * rc[n];
+  }
+  // Scale to L; reciprocal pivot on the diagonal; zero the upper triangle.
+#pragma unroll
+  for (int n = 0; n < 8; ++n) {
+#pragma unroll
+    for (int p = n; p < 8; ++p) {
+      A[pair_of(p, n)].x *= rc[n];
+      A[pair_of(p, n)].y *= rc[n];
+    }
+    float2& d = A[pair_of(n, n)];
+    d.x = (b == a) ? rc[n] : (a < b ? 0.f : d.x);
+    d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
+  }
+  invert_blocks(A, sm, lane, a, b);
+  diag_to_inverse(A, sm, a, b);
+  {
+    float* dst = Lst + size_t(m) * LSTRIDE;
+#pragma unroll
+    for (int q4 = 0; q4 < NPAIR / 2; ++q4)
+      st4(dst + (q4 * 32 + lane) * 4, make_float4(A[2 * q4].x, A[2 * q4].y, A[2 * q4 + 1].x, A[2 * q4 + 1].y));
+  }
+  back_substitute(A, sm.w, sm.y, a, b);
+  __syncwarp();
+  float* out = solution + size_t(m) * dim;
+  for (int i = lane; i < dim; i += 32) out[i] = sm.y[i];
+}
+
+// Backward of spd_solve (lm/kernels/mamba4.py:208-215): z = A^-1 g from the
+// stored factor, d rhs = z, d precision = -(z y^T + y z^T) / 2 (all dim x dim
+// entries, as the reference's symmetric cotangent).
+__global__ void __launch_bounds__(32 * WARPS) spd_bwd_kernel(
+    int count, int dim, const float* __restrict__ Lst, const float* __restrict__ solution,
+    const float* __restrict__ d_solution, float* __restrict__ d_precision, float* __restrict__ d_rhs) {
+  extern __shared__ __align__(16) unsigned char spdb_raw[];
+  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(spdb_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int a = lane >> 3, b = lane & 7;
+  const int m = blockIdx.x * WARPS + warp;
+  if (m >= count) return;
+  SolveSmem& sm = smem_all[warp];
+  float2 L[NPAIR];
+  {
+    const float* src = Lst + size_t(m) * LSTRIDE;
+#pragma unroll
+    for (int q4 = 0; q4 < NPAIR / 2; ++q4) {
+      const float4 v4 = ld4(src + (q4 * 32 + lane) * 4);
+      L[2 * q4] = make_float2(v4.x, v4.y);
+      L[2 * q4 + 1] = make_float2(v4.z, v4.w);
+    }
+  }
+  const float* g = d_solution + size_t(m) * dim;
+  const float* y = solution + size_t(m) * dim;
+  for (int i = lane; i < 64; i += 32) {
+    sm.y[i] = i < dim ? g[i] : 0.f;
+    sm.flC[i] = i < dim ? y[i] : 0.f;  // the solution, kept for the outer product
+  }
+  __syncwarp();
+  forward_substitute(L, sm.y, sm.w, a, b);
+  back_substitute(L, sm.w, sm.y, a, b);  // z in sm.y
+  __syncwarp();
+  float* dr = d_rhs + size_t(m) * dim;
+  for (int i = lane; i < dim; i += 32) dr[i] = sm.y[i];
+  float* dp = d_precision + size_t(m) * dim * dim;
+  for (int idx = lane; idx < dim * dim; idx += 32) {
+    const int i = idx / dim, j = idx - i * dim;
+    dp[idx] = -0.5f * fmaf(sm.y[i], sm.flC[j], sm.flC[i] * sm.y[j]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Chunk-product kernels: one CTA of 8 warps per (batch, 64-token chunk, head)
 // (carry: one per (batch, head)). The products run on tensor cores as m16n8k8
 // TF32 MMAs on a two-term split of every fp32 operand (hi = x rounded to 11
@@ -1612,5 +1724,43 @@ extern "C" int m4_memread_decode(const M4MemDims* d, const float* evidence, cons
                                                                 query, beta, log_decay, floor_, output, variance,
                                                                 evidence_out, cross_out);
   }
+  return launch_status();
+}
+
+extern "C" size_t m4_spd_solve_factor_bytes(int count, int dim) {
+  if (count < 0 || dim <= 0 || dim > mem::KD) return 0;
+  return size_t(count) * mem::LSTRIDE * sizeof(float);
+}
+
+extern "C" int m4_spd_solve_fwd(int count, int dim, const float* precision, const float* rhs,
+                                float* solution, void* factor, size_t factor_bytes, void* stream) {
+  if (count < 0 || dim <= 0) return M4_ERR_DIMS;
+  if (dim > mem::KD) return M4_ERR_UNSUPPORTED;
+  if (count == 0) return M4_OK;
+  if (!precision || !rhs || !solution || !factor) return M4_ERR_NULL;
+  if (!all_aligned16(static_cast<const float*>(factor))) return M4_ERR_ALIGN;
+  if (factor_bytes < m4_spd_solve_factor_bytes(count, dim)) return M4_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int smem = int(sizeof(mem::SolveSmem) * mem::WARPS);
+  cudaFuncSetAttribute(mem::spd_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  mem::spd_fwd_kernel<<<(count + mem::WARPS - 1) / mem::WARPS, 32 * mem::WARPS, smem, s>>>(
+      count, dim, precision, rhs, solution, static_cast<float*>(factor));
+  return launch_status();
+}
+
+extern "C" int m4_spd_solve_bwd(int count, int dim, const void* factor, size_t factor_bytes,
+                                const float* solution, const float* d_solution, float* d_precision,
+                                float* d_rhs, void* stream) {
+  if (count < 0 || dim <= 0) return M4_ERR_DIMS;
+  if (dim > mem::KD) return M4_ERR_UNSUPPORTED;
+  if (count == 0) return M4_OK;
+  if (!factor || !solution || !d_solution || !d_precision || !d_rhs) return M4_ERR_NULL;
+  if (!all_aligned16(static_cast<const float*>(factor))) return M4_ERR_ALIGN;
+  if (factor_bytes < m4_spd_solve_factor_bytes(count, dim)) return M4_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int smem = int(sizeof(mem::SolveSmem) * mem::WARPS);
+  cudaFuncSetAttribute(mem::spd_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  mem::spd_bwd_kernel<<<(count + mem::WARPS - 1) / mem::WARPS, 32 * mem::WARPS, smem, s>>>(
+      count, dim, static_cast<const float*>(factor), solution, d_solution, d_precision, d_rhs);
   return launch_status();
 }

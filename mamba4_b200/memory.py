@@ -233,21 +233,82 @@ def selective_decode(state, key, value, query, beta, log_decay, floor, solver=No
     return SelectiveResult(out[..., :value_dim], var, new_state)
 
 
-SOLVERS = ("cuda", "fused")
+# Solver names the reference accepts (`lm/kernels/mamba4.py:167-184`,
+# `:249-262`) plus "cuda". Every name selects the same mathematics (an exact
+# Cholesky solve of the same system; the reference's backends differ only in
+# their arithmetic schedule), so all of them run the sm_100a kernels.
+SOLVERS = ("cuda", "fused", "loop", "blocked", "unrolled", "auto")
+
+
+class _SpdSolve(torch.autograd.Function):
+    """precision @ y = rhs over [count, dim, dim] / [count, dim] float32."""
+
+    @staticmethod
+    def forward(ctx, precision, rhs):
+        lib = _lib.load()
+        count, dim = rhs.shape
+        solution = torch.empty_like(rhs)
+        nbytes = lib.m4_spd_solve_factor_bytes(count, dim)
+        factor = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=rhs.device)
+        _lib.check(lib.m4_spd_solve_fwd(count, dim, _lib.ptr(precision), _lib.ptr(rhs), _lib.ptr(solution),
+                                        _lib.ptr(factor), nbytes, _stream()), "m4_spd_solve_fwd")
+        ctx.save_for_backward(factor, solution)
+        return solution
+
+    @staticmethod
+    def backward(ctx, gradient):
+        lib = _lib.load()
+        factor, solution = ctx.saved_tensors
+        count, dim = solution.shape
+        gradient = gradient.float().contiguous()
+        d_precision = torch.empty(count, dim, dim, dtype=torch.float32, device=solution.device)
+        d_rhs = torch.empty_like(solution)
+        nbytes = lib.m4_spd_solve_factor_bytes(count, dim)
+        _lib.check(lib.m4_spd_solve_bwd(count, dim, _lib.ptr(factor), nbytes, _lib.ptr(solution),
+                                        _lib.ptr(gradient), _lib.ptr(d_precision), _lib.ptr(d_rhs),
+                                        _stream()), "m4_spd_solve_bwd")
+        return d_precision, d_rhs
+
+
+def spd_solve(precision, rhs, backend=None):
+    """Solve precision @ y = rhs for SPD [...,d,d] precision and [...,d] rhs.
+
+    Mirrors `spd_solve` (`lm/kernels/mamba4.py:187-218`): float32, only the
+    lower triangle of `precision` is read, d <= 64; the backward reuses the
+    stored Cholesky factor, z = A^-1 g, d rhs = z and d A = -sym(z y^T)
+    (`:208-215`). `backend` takes the reference's names (None, "loop",
+    "blocked", "unrolled", "auto", "fused") and "cuda"; they change only the
+    reference's arithmetic schedule, and all run the `m4_spd_solve_*` kernels.
+    """
+    if backend not in (None, *SOLVERS):
+        raise ValueError(f"Unknown SPD solve backend {backend}")
+    precision = torch.as_tensor(precision).float()
+    rhs = torch.as_tensor(rhs).float()
+    if not rhs.is_cuda or not precision.is_cuda:
+        raise RuntimeError("spd_solve runs on CUDA tensors only (no CPU path)")
+    dim = rhs.shape[-1]
+    if precision.shape != rhs.shape + (dim,):
+        raise ValueError(f"SPD solve precision {tuple(precision.shape)} does not match rhs {tuple(rhs.shape)}")
+    if dim > KEY_DIM:
+        raise ValueError(f"SPD solve dimension {dim} exceeds {KEY_DIM}")
+    count = rhs.numel() // dim if dim else 0
+    solution = _SpdSolve.apply(precision.reshape(count, dim, dim).contiguous(),
+                               rhs.reshape(count, dim).contiguous())
+    return solution.reshape(rhs.shape)
 
 
 def selective_gaussian_memory(
-    keys, values, queries, beta, log_decay, floor, *, chunk_size=64, initial=None, solver="cuda"
+    keys, values, queries, beta, log_decay, floor, *, chunk_size=64, initial=None, solver=None
 ):
     """`lm/kernels/mamba4.py:228-338` dispatcher with the B200 solver.
 
-    `solver` "cuda" (and the reference's "fused", which this build maps to
-    the same kernel) selects the sm_100a path; the reference's XLA solvers
-    (loop, blocked, unrolled, auto) are not part of this library.
+    Every solver name the reference accepts ("fused", "loop", "blocked",
+    "unrolled", "auto", or None) and "cuda" runs the sm_100a kernels: they
+    solve the same system, so a reference config (the 60M model's "blocked",
+    `lm/configs/mamba4-60m.json:40`) runs unchanged. Unknown names raise the
+    reference's ValueError.
     """
-    if solver is None:
-        solver = "cuda"
-    if solver not in SOLVERS:
+    if solver not in (None, *SOLVERS):
         raise ValueError(f"Unknown SPD solve backend {solver}")
     return selective_memory_fused(
         keys, values, queries, beta, log_decay, floor, chunk_size=chunk_size, initial=initial

@@ -419,6 +419,28 @@ def decode_step(evidence, cross, key, value, query, beta, log_decay, floor):
     return np.einsum("bhpd,bhd->bhp", c, y), np.sum(q * y, axis=-1), s, c
 
 
+def spd_solve(precision, rhs):
+    """Float64 solve of precision @ y = rhs, reading only the lower triangle.
+
+    Restates `spd_solve` (`lm/kernels/mamba4.py:187-206`): precision
+    [...,d,d] SPD, rhs [...,d]; the Cholesky backends there read the lower
+    triangle only, so the matrix solved is tril(A) + tril(A, -1)^T.
+    """
+    a = np.asarray(precision, F64)
+    a = np.tril(a) + np.swapaxes(np.tril(a, -1), -1, -2)
+    return np.linalg.solve(a, np.asarray(rhs, F64)[..., None])[..., 0]
+
+
+def spd_solve_vjp(precision, rhs, gradient):
+    """`_spd_solve_backward` (`lm/kernels/mamba4.py:208-215`), float64:
+    z = A^-1 g, d rhs = z, d precision = -(z y^T + y z^T) / 2.
+    Returns (d_precision, d_rhs)."""
+    y = spd_solve(precision, rhs)
+    z = spd_solve(precision, gradient)
+    outer = z[..., :, None] * y[..., None, :]
+    return -0.5 * (outer + np.swapaxes(outer, -1, -2)), z
+
+
 def config_inputs(batch, time, heads, dim, value_dim, seed=0):
     """Seeded inputs of BASELINE configs 0 and 2 (float32 arrays).
 
