@@ -159,45 +159,6 @@ class Mamba3Mixer(nn.Module):
         return self.out_proj(out), cache
 
 
-def causal_conv(x, weight, bias):
-    """Depthwise causal convolution (`lm/models/mamba4.py:98-108`), fp32 taps."""
-    taps = weight.shape[0]
-    xt = F.pad(x.float().transpose(1, 2), (taps - 1, 0))
-    w = weight.float().t().unsqueeze(1)  # [channels, 1, taps]
-    return (F.conv1d(xt, w, bias.float(), groups=x.shape[-1])).transpose(1, 2)
-
-
-def order_memory_chunked(values, log_decay, chunk_size=64):
-    """h_t = lam_t h_(t-1) + (1 - lam_t) v_t, chunked
-    (`lm/models/mamba4.py:59-95`)."""
-    x = values.float()
-    batch, time, heads, width = x.shape
-    pad = (-time) % chunk_size
-    count = (time + pad) // chunk_size
-
-    def chunks(a):
-        a = F.pad(a, [0, 0] * (a.ndim - 2) + [0, pad])
-        return a.reshape(batch, count, chunk_size, *a.shape[2:]).transpose(2, 3)
-
-    value, logs = chunks(x), chunks(log_decay.float())   # [B,n,H,c,P], [B,n,H,c]
-    inflow = -torch.expm1(logs)
-    prefix = torch.cumsum(logs, dim=-1)
-    causal = torch.tril(torch.ones(chunk_size, chunk_size, dtype=torch.bool, device=x.device))
-    diff = prefix[..., :, None] - prefix[..., None, :]
-    weights = torch.where(causal, torch.exp(torch.where(causal, diff, torch.zeros_like(diff))),
-                          torch.zeros_like(diff))
-    local = torch.einsum("bnhts,bnhsp->bnhtp", weights * inflow[..., None, :], value)
-    ends = local[..., -1, :]                               # [B,n,H,P]
-    decay = torch.exp(prefix[..., -1])                     # [B,n,H]
-    carries, state = [], torch.zeros_like(ends[:, 0])
-    for n in range(count):
-        carries.append(state)
-        state = decay[:, n, :, None] * state + ends[:, n]
-    starts = torch.stack(carries, 1)
-    out = local + torch.exp(prefix)[..., None] * starts[..., None, :]
-    return out.transpose(2, 3).reshape(batch, count * chunk_size, heads, width)[:, :time]
-
-
 class SelectiveMemoryMixer(nn.Module):
     """`SelectiveMemoryMixer` (`lm/models/mamba4.py:115-337`), training path."""
 
