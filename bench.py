@@ -584,6 +584,8 @@ def run_ours(args):
         step = e2e_step = None
         torch.cuda.empty_cache()
         line["lm60m"] = measure_lm(args, "lm60m", world, rank, local)
+        # the 125M step (64 sequences per GPU) on the same ranks.
+        line["lm125m"] = measure_lm(args, "lm125m", world, rank, local)
     if not args.no_decode and args.workload == "hotpath":
         line["decode"] = measure_decode(world, rank, local)
     if rank == 0:
@@ -611,7 +613,10 @@ def lm_flops_per_token(cfg):
     mh, d = cfg.memory_heads, cfg.key_dim
     m_proj = cfg.d_model * (2 * cfg.inner + 2 * mh * d + 3 * mh) + cfg.inner * cfg.d_model
     matmul = s_layers * s_proj + m_layers * m_proj + cfg.vocab_size * cfg.d_model
-    return 6 * matmul + m_layers * mh * (MEM_FWD_FLOPS + MEM_BWD_FLOPS) + s_layers * SCAN_FLOPS * h / 16
+    # The scan's chunk products per token and head: 2 c N + 2 c P + 4 N P
+    # (c = P = 64), i.e. the survey figure (N = 64) scaled by (192 N + 4096) / 16384.
+    scan = SCAN_FLOPS * (h / 16) * (192 * n + 4096) / 16384
+    return 6 * matmul + m_layers * mh * (MEM_FWD_FLOPS + MEM_BWD_FLOPS) + s_layers * scan
 
 
 def measure_lm(args, workload, world, rank, local):
@@ -720,7 +725,7 @@ def main():
     p.add_argument("--no-decode", action="store_true",
                    help="hot-path workload: skip the cached-decode measurement of the 60M LM")
     p.add_argument("--no-lm", action="store_true",
-                   help="hot-path workload: skip the nested data-parallel 60M LM step measurement")
+                   help="hot-path workload: skip the nested data-parallel 60M and 125M LM step measurements")
     args = p.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -238,24 +238,25 @@ int m4_scan_bwd_noalloc(const M4ScanDims* dims, const void* c, const void* b, co
  * ---------------------------------------------------------------------- */
 
 /* Mamba-3 mixer in-projection layout (lm/models/mamba3.py:60-73): each row of
- * `proj` holds z [inner], x [inner], b [64], c [64], raw_dt [heads],
- * raw_a [heads], trap [heads], angles [angles] (bfloat16). */
+ * `proj` holds z [inner], x [inner], b [N], c [N], raw_dt [heads],
+ * raw_a [heads], trap [heads], angles [angles] (bfloat16), N = state_dim. */
 typedef struct {
-  int rows;    /* B*T */
-  int inner;   /* d_model * expand, a multiple of 256, = 64 * heads */
-  int heads;   /* <= 32 */
-  int angles;  /* rotation pairs, <= 32 */
-  float eps;   /* RMSNorm epsilon of B_norm / C_norm */
-  int stride;  /* elements between rows of proj and d_proj: a multiple of 8 that
-                  is at least 2 inner + 128 + 3 heads + angles */
+  int rows;       /* B*T */
+  int inner;      /* d_model * expand, a multiple of 256, = 64 * heads */
+  int heads;      /* <= 32 */
+  int angles;     /* rotation pairs, <= state_dim / 2 */
+  float eps;      /* RMSNorm epsilon of B_norm / C_norm */
+  int stride;     /* elements between rows of proj and d_proj: a multiple of 8 that
+                     is at least 2 inner + 2 state_dim + 3 heads + angles */
+  int state_dim;  /* N: 64, 96 or 128 (the width of the b and c slices) */
 } M4MixerDims;
 
 /* Rows of the per-warp partial-sum buffers the backward calls need
- * (post: rows x heads floats; prep: rows x (128 + heads) floats). */
+ * (post: rows x heads floats; prep: rows x (2 state_dim + heads) floats). */
 size_t m4_mixer_partial_rows(const M4MixerDims* dims);
 
 /* Before the scan (lm/models/mamba3.py:76-103): c = C_norm(c), b = B_norm(b)
- * [rows,64] bf16; x copied to [rows,inner]; dt = softplus(raw_dt + dt_bias),
+ * [rows,N] bf16; x copied to [rows,inner]; dt = softplus(raw_dt + dt_bias),
  * adt = -max(heavy_tail(raw_a), 1e-4) * dt, trap, angles as float32. */
 int m4_mixer_prep_fwd(const M4MixerDims* dims, const void* proj, const float* b_scale,
                       const float* c_scale, const float* dt_bias, void* c_out, void* b_out,

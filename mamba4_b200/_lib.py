@@ -37,7 +37,7 @@ class MixerDims(ctypes.Structure):
     """M4MixerDims."""
 
     _fields_ = [("rows", _c_int), ("inner", _c_int), ("heads", _c_int), ("angles", _c_int),
-                ("eps", ctypes.c_float), ("stride", _c_int)]
+                ("eps", ctypes.c_float), ("stride", _c_int), ("state_dim", _c_int)]
 
 
 class MemMixDims(ctypes.Structure):

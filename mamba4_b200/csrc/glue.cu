@@ -54,6 +54,7 @@ M4_DEV float heavy_tail_grad(float x) {
 
 struct Mix {
   int rows, inner, heads, angles, width;  // width: row stride of proj / d_proj
+  int nb;                                  // width of the B and C slices (state dim)
   float eps;
   int off_x, off_b, off_c, off_dt, off_a, off_trap, off_ang;
 };
@@ -61,10 +62,11 @@ struct Mix {
 inline Mix make_mix(const M4MixerDims& m) {
   Mix d;
   d.rows = m.rows; d.inner = m.inner; d.heads = m.heads; d.angles = m.angles; d.eps = m.eps;
+  d.nb = m.state_dim;
   d.off_x = m.inner;
   d.off_b = 2 * m.inner;
-  d.off_c = d.off_b + 64;
-  d.off_dt = d.off_c + 64;
+  d.off_c = d.off_b + d.nb;
+  d.off_dt = d.off_c + d.nb;
   d.off_a = d.off_dt + m.heads;
   d.off_trap = d.off_a + m.heads;
   d.off_ang = d.off_trap + m.heads;
@@ -77,12 +79,21 @@ constexpr int WPB = 8;  // warps per block
 M4_DEV int gwarp() { return blockIdx.x * WPB + (threadIdx.x >> 5); }
 M4_DEV int nwarps() { return gridDim.x * WPB; }
 
-// RMSNorm of a 64-wide bf16 slice held as one pair per lane; returns the
-// normalised pair and the inverse rms.
-M4_DEV float2 norm64(float2 v, float eps, float& r) {
-  const float ss = warp_sum(v.x * v.x + v.y * v.y);
-  r = rsqrtf(ss * (1.f / 64.f) + eps);
-  return make_float2(v.x * r, v.y * r);
+// RMSNorm of an nb-wide bf16 slice (nb in {64, 96, 128}): lane l holds
+// elements l + 32 j (j < nb / 32; the rest zero); returns the normalised
+// values in v and the inverse rms.
+M4_DEV float norm_slice(const bf16* p, int nb, float eps, float (&v)[4]) {
+  const int lane = threadIdx.x & 31;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[j] = 32 * j < nb ? bf(p + lane + 32 * j) : 0.f;
+    ss = fmaf(v[j], v[j], ss);
+  }
+  const float r = rsqrtf(warp_sum(ss) / float(nb) + eps);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] *= r;
+  return r;
 }
 
 // Mamba-3 mixer, before the scan: c = C_norm(c), b = B_norm(b) (bf16),
@@ -99,11 +110,17 @@ __global__ void __launch_bounds__(WPB * 32) mixer_prep_fwd(Mix d, const bf16* __
   for (int row = gwarp(); row < d.rows; row += nwarps()) {
     const bf16* pr = proj + size_t(row) * d.width;
     for (int k = lane; k < d.inner / 8; k += 32) st16(x_out + size_t(row) * d.inner + 8 * k, ld16(pr + d.off_x + 8 * k));
-    float r;
-    const float2 bn = norm64(bf2(pr + d.off_b + 2 * lane), d.eps, r);
-    st_bf2(b_out + size_t(row) * 64 + 2 * lane, bn.x * bscale[2 * lane], bn.y * bscale[2 * lane + 1]);
-    const float2 cn = norm64(bf2(pr + d.off_c + 2 * lane), d.eps, r);
-    st_bf2(c_out + size_t(row) * 64 + 2 * lane, cn.x * cscale[2 * lane], cn.y * cscale[2 * lane + 1]);
+    float bn[4], cn[4];
+    norm_slice(pr + d.off_b, d.nb, d.eps, bn);
+    norm_slice(pr + d.off_c, d.nb, d.eps, cn);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = lane + 32 * j;
+      if (n < d.nb) {
+        b_out[size_t(row) * d.nb + n] = __float2bfloat16_rn(bn[j] * bscale[n]);
+        c_out[size_t(row) * d.nb + n] = __float2bfloat16_rn(cn[j] * cscale[n]);
+      }
+    }
     if (lane < d.heads) {
       const float t = softplus(bf(pr + d.off_dt + lane) + dt_bias[lane]);
       const float a = -fmaxf(heavy_tail(bf(pr + d.off_a + lane)), 1e-4f);
@@ -111,7 +128,7 @@ __global__ void __launch_bounds__(WPB * 32) mixer_prep_fwd(Mix d, const bf16* __
       adt[size_t(row) * d.heads + lane] = a * t;
       trap[size_t(row) * d.heads + lane] = bf(pr + d.off_trap + lane);
     }
-    if (lane < d.angles) ang[size_t(row) * d.angles + lane] = bf(pr + d.off_ang + lane);
+    for (int i = lane; i < d.angles; i += 32) ang[size_t(row) * d.angles + i] = bf(pr + d.off_ang + i);
   }
 }
 
@@ -194,9 +211,14 @@ __global__ void __launch_bounds__(WPB * 32) mixer_prep_bwd(
     const float* __restrict__ d_ang, bf16* __restrict__ d_proj, float* __restrict__ bs_part,
     float* __restrict__ cs_part, float* __restrict__ dtb_part) {
   const int lane = threadIdx.x & 31, G = d.inner / 256;
-  float sb0 = 0.f, sb1 = 0.f, sc0 = 0.f, sc1 = 0.f, sdt = 0.f;
-  const float2 bsc = make_float2(bscale[2 * lane], bscale[2 * lane + 1]);
-  const float2 csc = make_float2(cscale[2 * lane], cscale[2 * lane + 1]);
+  float sb[4] = {0.f, 0.f, 0.f, 0.f}, sc[4] = {0.f, 0.f, 0.f, 0.f}, sdt = 0.f;
+  float bsc[4], csc[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int n = lane + 32 * j;
+    bsc[j] = n < d.nb ? bscale[n] : 0.f;
+    csc[j] = n < d.nb ? cscale[n] : 0.f;
+  }
   for (int row = gwarp(); row < d.rows; row += nwarps()) {
     const bf16* pr = proj + size_t(row) * d.width;
     bf16* gp = d_proj + size_t(row) * d.width;
@@ -214,25 +236,27 @@ __global__ void __launch_bounds__(WPB * 32) mixer_prep_bwd(
       st16(gp + d.off_x + col, pack8(o));
     }
     // Norm backward: dx = r (g s - xhat mean(g s xhat)).
-    {
-      float r;
-      const float2 xh = norm64(bf2(pr + d.off_b + 2 * lane), d.eps, r);
-      const float2 g = bf2(db + size_t(row) * 64 + 2 * lane);
-      const float gs0 = g.x * bsc.x, gs1 = g.y * bsc.y;
-      const float m = warp_sum(gs0 * xh.x + gs1 * xh.y) * (1.f / 64.f);
-      st_bf2(gp + d.off_b + 2 * lane, r * (gs0 - xh.x * m), r * (gs1 - xh.y * m));
-      sb0 = fmaf(g.x, xh.x, sb0);
-      sb1 = fmaf(g.y, xh.y, sb1);
-    }
-    {
-      float r;
-      const float2 xh = norm64(bf2(pr + d.off_c + 2 * lane), d.eps, r);
-      const float2 g = bf2(dc + size_t(row) * 64 + 2 * lane);
-      const float gs0 = g.x * csc.x, gs1 = g.y * csc.y;
-      const float m = warp_sum(gs0 * xh.x + gs1 * xh.y) * (1.f / 64.f);
-      st_bf2(gp + d.off_c + 2 * lane, r * (gs0 - xh.x * m), r * (gs1 - xh.y * m));
-      sc0 = fmaf(g.x, xh.x, sc0);
-      sc1 = fmaf(g.y, xh.y, sc1);
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      float xh[4], gs[4], g[4];
+      const float r = norm_slice(pr + (which ? d.off_c : d.off_b), d.nb, d.eps, xh);
+      const bf16* grow = (which ? dc : db) + size_t(row) * d.nb;
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = lane + 32 * j;
+        g[j] = n < d.nb ? bf(grow + n) : 0.f;
+        gs[j] = g[j] * (which ? csc[j] : bsc[j]);
+        dot = fmaf(gs[j], xh[j], dot);
+      }
+      const float m = warp_sum(dot) / float(d.nb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = lane + 32 * j;
+        if (n < d.nb) gp[(which ? d.off_c : d.off_b) + n] = __float2bfloat16_rn(r * (gs[j] - xh[j] * m));
+        if (which) sc[j] = fmaf(g[j], xh[j], sc[j]);
+        else sb[j] = fmaf(g[j], xh[j], sb[j]);
+      }
     }
     if (lane < d.heads) {
       const size_t i = size_t(row) * d.heads + lane;
@@ -248,13 +272,18 @@ __global__ void __launch_bounds__(WPB * 32) mixer_prep_bwd(
       gp[d.off_trap + lane] = __float2bfloat16_rn(d_trap[i]);
       sdt += g_pre;
     }
-    if (lane < d.angles) gp[d.off_ang + lane] = __float2bfloat16_rn(d_ang[size_t(row) * d.angles + lane]);
+    for (int i = lane; i < d.angles; i += 32)
+      gp[d.off_ang + i] = __float2bfloat16_rn(d_ang[size_t(row) * d.angles + i]);
   }
   const size_t w = gwarp();
-  bs_part[w * 64 + 2 * lane] = sb0;
-  bs_part[w * 64 + 2 * lane + 1] = sb1;
-  cs_part[w * 64 + 2 * lane] = sc0;
-  cs_part[w * 64 + 2 * lane + 1] = sc1;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int n = lane + 32 * j;
+    if (n < d.nb) {
+      bs_part[w * d.nb + n] = sb[j];
+      cs_part[w * d.nb + n] = sc[j];
+    }
+  }
   if (lane < d.heads) dtb_part[w * d.heads + lane] = sdt;
 }
 
@@ -399,9 +428,12 @@ inline int row_blocks(int rows) {
 inline int check_mix(const M4MixerDims* m) {
   if (!m) return M4_ERR_NULL;
   if (m->rows <= 0 || m->inner <= 0 || m->heads <= 0 || m->angles < 0) return M4_ERR_DIMS;
-  if (m->inner % 256 != 0 || m->inner > 2048 || m->heads > 32 || m->angles > 32 || m->inner != 64 * m->heads)
+  if (m->state_dim != 64 && m->state_dim != 96 && m->state_dim != 128) return M4_ERR_UNSUPPORTED;
+  if (m->inner % 256 != 0 || m->inner > 2048 || m->heads > 32 || m->angles > m->state_dim / 2 ||
+      m->inner != 64 * m->heads)
     return M4_ERR_UNSUPPORTED;
-  if (m->stride % 8 != 0 || m->stride < 2 * m->inner + 128 + 3 * m->heads + m->angles) return M4_ERR_UNSUPPORTED;
+  if (m->stride % 8 != 0 || m->stride < 2 * m->inner + 2 * m->state_dim + 3 * m->heads + m->angles)
+    return M4_ERR_UNSUPPORTED;
   return M4_OK;
 }
 
@@ -469,14 +501,14 @@ extern "C" int m4_mixer_prep_bwd(const M4MixerDims* m, const void* proj, const f
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int blocks = row_blocks(d.rows), nw = blocks * WPB;
   float* bs_part = part;
-  float* cs_part = part + size_t(nw) * 64;
-  float* dtb_part = part + size_t(nw) * 128;
+  float* cs_part = part + size_t(nw) * d.nb;
+  float* dtb_part = part + size_t(nw) * 2 * d.nb;
   mixer_prep_bwd<<<blocks, WPB * 32, 0, s>>>(
       d, static_cast<const bf16*>(proj), bscale, cscale, dt_bias, D, static_cast<const bf16*>(g_out),
       static_cast<const bf16*>(dc), static_cast<const bf16*>(db), static_cast<const bf16*>(dx), d_adt, d_dt,
       d_trap, d_angles, static_cast<bf16*>(d_proj), bs_part, cs_part, dtb_part);
-  colsum_kernel<<<64, 256, 0, s>>>(bs_part, nw, 64, d_bscale);
-  colsum_kernel<<<64, 256, 0, s>>>(cs_part, nw, 64, d_cscale);
+  colsum_kernel<<<d.nb, 256, 0, s>>>(bs_part, nw, d.nb, d_bscale);
+  colsum_kernel<<<d.nb, 256, 0, s>>>(cs_part, nw, d.nb, d_cscale);
   colsum_kernel<<<d.heads, 256, 0, s>>>(dtb_part, nw, d.heads, d_dt_bias);
   return launch_status();
 }

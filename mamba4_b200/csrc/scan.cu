@@ -25,7 +25,6 @@ namespace m4 {
 namespace scan {
 
 constexpr int C = 64;      // chunk length
-constexpr int NS = 64;     // state dim N
 constexpr int HP = 64;     // head dim P
 constexpr int LDS = 68;    // smem tile stride (floats)
 constexpr int THREADS = 128;
@@ -143,7 +142,13 @@ M4_DEV void chunk_rows(const Dims& d, int b, int h, int t0, const float* adt, co
   if (tid < C) r.tail[tid] = expf(r.p[C - 1] - r.p[tid]);
 }
 
+// Strides of the state-dim-templated tiles: [C][NS] tiles (rotated Q / K and
+// the N-wide gradient tile) and [C][pairs] tables (phases).
+template <int NS> constexpr int ldn() { return NS + 4; }
+template <int NS> constexpr int tw() { return NS / 2 + 1; }
+
 // Phase theta[t][i] = phase0[i] + sum_{s<=t} rate_s[i] dt_s for pairs i < A.
+template <int NS>
 M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles, const Rows& r,
                         const float* phase0, float* theta) {
   const int tid = threadIdx.x;
@@ -156,43 +161,42 @@ M4_DEV void chunk_theta(const Dims& d, int b, int h, int t0, const float* angles
         rate = d.per_head ? angles[((size_t(b) * d.T + t) * d.H + h) * d.A + tid]
                           : angles[(size_t(b) * d.T + t) * d.A + tid];
       acc = fmaf(rate, r.dt[tt], acc);
-      theta[tt * 33 + tid] = acc;
+      theta[tt * tw<NS>() + tid] = acc;
     }
   }
 }
 
-// Build rotated, rounded Q and K tiles (and optionally the fp32 rotated
-// values and cos/sin for the backward).
-template <typename T>
+// Biased, rounded query/key pair (2i, 2i+1) of token t0 + tt, before rotation.
+template <typename T, int NS>
+M4_DEV void load_pair(const Dims& d, int b, int h, int t, const T* cq, const T* bk, const float* qb,
+                      const float* kb, int i, float (&q)[2], float (&k)[2]) {
+  const int n0 = 2 * i, n1 = 2 * i + 1;
+  float c0 = 0.f, c1 = 0.f, b0 = 0.f, b1 = 0.f;
+  if (t < d.T) {
+    const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * NS : (size_t(b) * d.T + t) * NS;
+    c0 = to_f(cq[base + n0]); c1 = to_f(cq[base + n1]);
+    b0 = to_f(bk[base + n0]); b1 = to_f(bk[base + n1]);
+  }
+  q[0] = round_to<T>(c0 + (qb ? qb[h * NS + n0] : 0.f));
+  q[1] = round_to<T>(c1 + (qb ? qb[h * NS + n1] : 0.f));
+  k[0] = round_to<T>(b0 + (kb ? kb[h * NS + n0] : 0.f));
+  k[1] = round_to<T>(b1 + (kb ? kb[h * NS + n1] : 0.f));
+}
+
+// Rotated, rounded Q and K tiles [C][ldn<NS>()].
+template <typename T, int NS>
 M4_DEV void build_qk(const Dims& d, int b, int h, int t0, const T* cq, const T* bk, const float* qb,
-                     const float* kb, const float* theta, float* Qs, float* Ks, float* Qf, float* Kf,
-                     float* cosv, float* sinv) {
+                     const float* kb, const float* theta, float* Qs, float* Ks) {
   for (int idx = threadIdx.x; idx < C * (NS / 2); idx += THREADS) {
     const int tt = idx / (NS / 2), i = idx % (NS / 2), t = t0 + tt;
-    const int n0 = 2 * i, n1 = 2 * i + 1;
-    float c0 = 0.f, c1 = 0.f, b0 = 0.f, b1 = 0.f;
-    if (t < d.T) {
-      const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * NS : (size_t(b) * d.T + t) * NS;
-      c0 = to_f(cq[base + n0]); c1 = to_f(cq[base + n1]);
-      b0 = to_f(bk[base + n0]); b1 = to_f(bk[base + n1]);
-    }
-    const float q0 = round_to<T>(c0 + (qb ? qb[h * NS + n0] : 0.f));
-    const float q1 = round_to<T>(c1 + (qb ? qb[h * NS + n1] : 0.f));
-    const float k0 = round_to<T>(b0 + (kb ? kb[h * NS + n0] : 0.f));
-    const float k1 = round_to<T>(b1 + (kb ? kb[h * NS + n1] : 0.f));
+    float q[2], k[2];
+    load_pair<T, NS>(d, b, h, t, cq, bk, qb, kb, i, q, k);
     float cs = 1.f, sn = 0.f;
-    if (i < d.A) sincosf(theta[tt * 33 + i], &sn, &cs);
-    const float qr0 = q0 * cs - q1 * sn, qr1 = q1 * cs + q0 * sn;
-    const float kr0 = k0 * cs - k1 * sn, kr1 = k1 * cs + k0 * sn;
-    Qs[tt * LDS + n0] = round_to<T>(qr0);
-    Qs[tt * LDS + n1] = round_to<T>(qr1);
-    Ks[tt * LDS + n0] = round_to<T>(kr0);
-    Ks[tt * LDS + n1] = round_to<T>(kr1);
-    if (Qf) {
-      Qf[tt * LDS + n0] = qr0; Qf[tt * LDS + n1] = qr1;
-      Kf[tt * LDS + n0] = kr0; Kf[tt * LDS + n1] = kr1;
-      cosv[tt * 33 + i] = cs; sinv[tt * 33 + i] = sn;
-    }
+    if (i < d.A) sincosf(theta[tt * tw<NS>() + i], &sn, &cs);
+    Qs[tt * ldn<NS>() + 2 * i] = round_to<T>(q[0] * cs - q[1] * sn);
+    Qs[tt * ldn<NS>() + 2 * i + 1] = round_to<T>(q[1] * cs + q[0] * sn);
+    Ks[tt * ldn<NS>() + 2 * i] = round_to<T>(k[0] * cs - k[1] * sn);
+    Ks[tt * ldn<NS>() + 2 * i + 1] = round_to<T>(k[1] * cs + k[0] * sn);
   }
 }
 
@@ -205,9 +209,15 @@ M4_DEV void load_values(const Dims& d, int b, int h, int t0, const T* x, float* 
 }
 
 // ---------------------------------------------------------------------------
-// Forward.
+// Forward (sequential chunks per (batch, head); state dim NS in {64, 96, 128}).
 // ---------------------------------------------------------------------------
-template <typename T>
+template <int NS>
+inline size_t fwd_smem() {
+  return (2 * C * ldn<NS>() + 2 * C * LDS + NS * LDS + C * tw<NS>() + NS / 2 + C + sizeof(Rows) / 4) *
+         sizeof(float);
+}
+
+template <typename T, int NS>
 __global__ void __launch_bounds__(THREADS) fwd_kernel(
     Dims d, const T* __restrict__ cq, const T* __restrict__ bk, const T* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
@@ -215,21 +225,22 @@ __global__ void __launch_bounds__(THREADS) fwd_kernel(
     T* __restrict__ y, float* __restrict__ final_state, float* __restrict__ starts,
     float* __restrict__ phases) {
   constexpr bool BF = sizeof(T) == 2;
+  constexpr int LN = ldn<NS>(), TW = tw<NS>(), NP = NS / 2;
   extern __shared__ __align__(16) float sh[];
   float* Qs = sh;
-  float* Ks = Qs + C * LDS;
-  float* Vs = Ks + C * LDS;
+  float* Ks = Qs + C * LN;
+  float* Vs = Ks + C * LN;
   float* Ms = Vs + C * LDS;
-  float* St = Ms + C * LDS;           // [N][P] fp32 state
-  float* theta = St + NS * LDS;       // [C][33]
-  float* phase = theta + C * 33;      // [32]
-  float* scratch = phase + 32;        // [64]
+  float* St = Ms + C * LDS;           // [NS][P] fp32 state
+  float* theta = St + NS * LDS;       // [C][TW]
+  float* phase = theta + C * TW;      // [NP]
+  float* scratch = phase + NP;        // [64]
   Rows& r = *reinterpret_cast<Rows*>(scratch + C);
   const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
   const int tid = threadIdx.x, warp = tid >> 5;
   const int row0 = warp * 16;
   for (int i = tid; i < NS * LDS; i += THREADS) St[i] = 0.f;
-  if (tid < 32) phase[tid] = 0.f;
+  if (tid < NP) phase[tid] = 0.f;
   __syncthreads();
   for (int ch = 0; ch < d.nch; ++ch) {
     const int t0 = ch * C;
@@ -237,22 +248,22 @@ __global__ void __launch_bounds__(THREADS) fwd_kernel(
     {
       float* sd = starts + (size_t(bh) * d.nch + ch) * NS * HP;
       for (int i = tid; i < NS * HP; i += THREADS) sd[i] = St[(i / HP) * LDS + i % HP];
-      if (tid < 32) phases[(size_t(bh) * d.nch + ch) * 32 + tid] = phase[tid];
+      if (tid < NP) phases[(size_t(bh) * d.nch + ch) * NP + tid] = phase[tid];
     }
     chunk_rows(d, b, h, t0, adt, dt, trap_logits, r, scratch);
     __syncthreads();
-    chunk_theta(d, b, h, t0, angles, r, phase, theta);
+    chunk_theta<NS>(d, b, h, t0, angles, r, phase, theta);
     __syncthreads();
-    build_qk<T>(d, b, h, t0, cq, bk, qb, kb, theta, Qs, Ks, nullptr, nullptr, nullptr, nullptr);
+    build_qk<T, NS>(d, b, h, t0, cq, bk, qb, kb, theta, Qs, Ks);
     load_values<T>(d, b, h, t0, x, Vs);
-    if (tid < d.A) phase[tid] = theta[(C - 1) * 33 + tid];
+    if (tid < d.A) phase[tid] = theta[(C - 1) * TW + tid];
     __syncthreads();
     // Masked, weighted scores.
     {
       float acc[8][4];
       zero8(acc);
-      warp_gemm<BF, NS>(acc, row0, [&](int i, int k) { return Qs[i * LDS + k]; },
-                        [&](int k, int j) { return Ks[j * LDS + k]; });
+      warp_gemm<BF, NS>(acc, row0, [&](int i, int k) { return Qs[i * LN + k]; },
+                        [&](int k, int j) { return Ks[j * LN + k]; });
       for_tile(acc, row0, [&](int t, int s, float v) {
         float w = 0.f;
         if (s < t) w = expf(r.p[t] - r.p[s]) * r.scl[s];
@@ -268,7 +279,7 @@ __global__ void __launch_bounds__(THREADS) fwd_kernel(
       zero8(inh);
       warp_gemm<BF, C>(acc, row0, [&](int i, int k) { return Ms[i * LDS + k]; },
                        [&](int k, int j) { return Vs[k * LDS + j]; });
-      warp_gemm<BF, NS>(inh, row0, [&](int i, int k) { return Qs[i * LDS + k]; },
+      warp_gemm<BF, NS>(inh, row0, [&](int i, int k) { return Qs[i * LN + k]; },
                         [&](int k, int j) { return round_to<T>(St[k * LDS + j]); });
       const int lane = tid & 31, g = lane >> 2, c = lane & 3;
 #pragma unroll
@@ -286,14 +297,16 @@ __global__ void __launch_bounds__(THREADS) fwd_kernel(
       }
     }
     __syncthreads();
-    // state = e^(p_L) state + K^T (V o scale o tail)
+    // state = e^(p_L) state + K^T (V o scale o tail), 16 state rows per warp pass.
     {
-      float acc[8][4];
-      zero8(acc);
-      warp_gemm<BF, C>(acc, row0, [&](int n, int t) { return Ks[t * LDS + n]; },
-                       [&](int t, int p) { return round_to<T>(Vs[t * LDS + p] * (r.scl[t] * r.tail[t])); });
       const float end = expf(r.p[C - 1]);
-      for_tile(acc, row0, [&](int n, int p, float v) { St[n * LDS + p] = fmaf(end, St[n * LDS + p], v); });
+      for (int n0 = row0; n0 < NS; n0 += 4 * 16) {
+        float acc[8][4];
+        zero8(acc);
+        warp_gemm<BF, C>(acc, n0, [&](int n, int t) { return Ks[t * LN + n]; },
+                         [&](int t, int p) { return round_to<T>(Vs[t * LDS + p] * (r.scl[t] * r.tail[t])); });
+        for_tile(acc, n0, [&](int n, int p, float v) { St[n * LDS + p] = fmaf(end, St[n * LDS + p], v); });
+      }
     }
     __syncthreads();
   }
@@ -302,8 +315,10 @@ __global__ void __launch_bounds__(THREADS) fwd_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Backward: reverse chunks, state cotangent carried in shared memory.
-// Per-head partial outputs go to workspace; head/batch reductions and the
+// Backward: reverse chunks per (batch, head). The chunk-start state is read
+// from the residual and the chunk-end state cotangent (the carry) lives in
+// the workspace; both are [NS][P] fp32 slices that stay in L2. Per-head
+// partial outputs go to workspace; head/batch reductions and the
 // trapezoid/gate chain rule run in small follow-up kernels.
 // ---------------------------------------------------------------------------
 struct BwdOut {
@@ -316,9 +331,47 @@ struct BwdOut {
   float* ddtp;    // [B,T,H] d dt through the phase
   float* dqb;     // [B,H,N] bias partials
   float* dkb;     // [B,H,N]
+  float* carry;   // [B,H,N,P] cotangent of the current chunk's end state
 };
 
-template <typename T>
+template <int NS>
+inline size_t bwd_smem() {
+  return (3 * C * ldn<NS>() + 4 * C * LDS + 2 * C * tw<NS>() + NS / 2 + C + 8 * C + sizeof(Rows) / 4) *
+         sizeof(float);
+}
+
+// Rotation backward of one [C][NS] gradient tile G (rotated frame), in place
+// to the pre-rotation frame, written to `out` [B,T,H,N]; the pair-phase
+// gradient G . J rot(u) is added into dth [C][pairs] (u = the biased,
+// rounded queries (QUERY) or keys).
+template <typename T, int NS, bool QUERY>
+M4_DEV void rotate_back(const Dims& d, int b, int h, int t0, const T* cq, const T* bk, const float* qb,
+                        const float* kb, const float* theta, float* G, float* dth, float* out) {
+  constexpr int LN = ldn<NS>(), TW = tw<NS>();
+  for (int idx = threadIdx.x; idx < C * (NS / 2); idx += THREADS) {
+    const int tt = idx / (NS / 2), i = idx % (NS / 2), t = t0 + tt;
+    float q[2], k[2];
+    load_pair<T, NS>(d, b, h, t, cq, bk, qb, kb, i, q, k);
+    const float u0 = QUERY ? q[0] : k[0], u1 = QUERY ? q[1] : k[1];
+    float cs = 1.f, sn = 0.f;
+    if (i < d.A) sincosf(theta[tt * TW + i], &sn, &cs);
+    const float r0 = u0 * cs - u1 * sn, r1 = u1 * cs + u0 * sn;  // fp32 rotated, before rounding
+    const float g0 = G[tt * LN + 2 * i], g1 = G[tt * LN + 2 * i + 1];
+    const float p0 = g0 * cs + g1 * sn, p1 = g1 * cs - g0 * sn;
+    if (t < d.T) {
+      const size_t base = ((size_t(b) * d.T + t) * d.H + h) * NS;
+      out[base + 2 * i] = p0;
+      out[base + 2 * i + 1] = p1;
+    }
+    G[tt * LN + 2 * i] = p0;
+    G[tt * LN + 2 * i + 1] = p1;
+    // partner(rot) = (-r1, r0) (flashmamba.py:776)
+    const float v = i < d.A ? g0 * (-r1) + g1 * r0 : 0.f;
+    dth[tt * TW + i] = QUERY ? dth[tt * TW + i] + v : v;
+  }
+}
+
+template <typename T, int NS>
 __global__ void __launch_bounds__(THREADS) bwd_kernel(
     Dims d, const T* __restrict__ cq, const T* __restrict__ bk, const T* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
@@ -326,45 +379,37 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
     const float* __restrict__ starts, const float* __restrict__ phases, const T* __restrict__ dy,
     const float* __restrict__ d_final, T* __restrict__ dx, BwdOut o) {
   constexpr bool BF = sizeof(T) == 2;
+  constexpr int LN = ldn<NS>(), TW = tw<NS>(), NP = NS / 2;
   extern __shared__ __align__(16) float sh[];
-  float* Qs = sh;                     // rounded rotated queries
-  float* Ks = Qs + C * LDS;
-  float* Vs = Ks + C * LDS;
+  float* Qs = sh;                     // rounded rotated queries [C][LN]
+  float* Ks = Qs + C * LN;
+  float* G = Ks + C * LN;             // dK, then dQ (rotated frame, then pre-rotation) [C][LN]
+  float* Vs = G + C * LN;             // values [C][LDS]
   float* Dy = Vs + C * LDS;           // dY (model dtype values)
   float* Sc = Dy + C * LDS;           // scores  Q K^T
   float* Dm = Sc + C * LDS;           // d_mixed dY V^T
-  float* St = Dm + C * LDS;           // chunk-start state [N][P]
-  float* Cy = St + NS * LDS;          // carry: cotangent of chunk-end state [N][P]
-  float* Qf = Cy + NS * LDS;          // fp32 rotated (pre-rounding) queries
-  float* Kf = Qf + C * LDS;
-  float* theta = Kf + C * LDS;        // [C][33]
-  float* cosv = theta + C * 33;       // [C][33]
-  float* sinv = cosv + C * 33;        // [C][33]
-  float* later = sinv + C * 33;       // [32] phase-gradient carry per pair
-  float* scratch = later + 32;        // [64]
+  float* theta = Dm + C * LDS;        // [C][TW] phase
+  float* dth = theta + C * TW;        // [C][TW] pair-phase gradient, then its suffix sums
+  float* later = dth + C * TW;        // [NP] phase-gradient carry per pair
+  float* scratch = later + NP;        // [64]
   float* vec = scratch + C;           // [8][64] per-token accumulators
   Rows& r = *reinterpret_cast<Rows*>(vec + 8 * C);
-  float* dq_t = Qf;                   // reuse after use: dQ tile
-  float* dk_t = Kf;                   // dK tile
   const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row0 = warp * 16;
-  for (int i = tid; i < NS * HP; i += THREADS)
-    Cy[(i / HP) * LDS + i % HP] = d_final ? d_final[size_t(bh) * NS * HP + i] : 0.f;
-  if (tid < 32) later[tid] = 0.f;
-  float qbs = 0.f, kbs = 0.f;  // bias partial sums for column tid (tid < N)
+  float* Cy = o.carry + size_t(bh) * NS * HP;
+  for (int i = tid; i < NS * HP; i += THREADS) Cy[i] = d_final ? d_final[size_t(bh) * NS * HP + i] : 0.f;
+  if (tid < NP) later[tid] = 0.f;
+  float qbs = 0.f, kbs = 0.f;  // bias partial sums for column tid (tid < NS)
   __syncthreads();
   for (int ch = d.nch - 1; ch >= 0; --ch) {
     const int t0 = ch * C;
+    const float* St = starts + (size_t(bh) * d.nch + ch) * NS * HP;  // chunk-start state [NS][P]
     chunk_rows(d, b, h, t0, adt, dt, trap_logits, r, scratch);
     __syncthreads();
-    chunk_theta(d, b, h, t0, angles, r, phases + (size_t(bh) * d.nch + ch) * 32, theta);
-    {
-      const float* sd = starts + (size_t(bh) * d.nch + ch) * NS * HP;
-      for (int i = tid; i < NS * HP; i += THREADS) St[(i / HP) * LDS + i % HP] = sd[i];
-    }
+    chunk_theta<NS>(d, b, h, t0, angles, r, phases + (size_t(bh) * d.nch + ch) * NP, theta);
     __syncthreads();
-    build_qk<T>(d, b, h, t0, cq, bk, qb, kb, theta, Qs, Ks, Qf, Kf, cosv, sinv);
+    build_qk<T, NS>(d, b, h, t0, cq, bk, qb, kb, theta, Qs, Ks);
     load_values<T>(d, b, h, t0, x, Vs);
     load_values<T>(d, b, h, t0, dy, Dy);
     for (int i = tid; i < 8 * C; i += THREADS) vec[i] = 0.f;
@@ -373,8 +418,8 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
     {
       float acc[8][4];
       zero8(acc);
-      warp_gemm<BF, NS>(acc, row0, [&](int i, int k) { return Qs[i * LDS + k]; },
-                        [&](int k, int j) { return Ks[j * LDS + k]; });
+      warp_gemm<BF, NS>(acc, row0, [&](int i, int k) { return Qs[i * LN + k]; },
+                        [&](int k, int j) { return Ks[j * LN + k]; });
       for_tile(acc, row0, [&](int t, int s, float v) { Sc[t * LDS + s] = v; });
       zero8(acc);
       warp_gemm<BF, HP>(acc, row0, [&](int i, int k) { return Dy[i * LDS + k]; },
@@ -387,6 +432,7 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
       return s == t ? r.gam[t] : 0.f;
     };
     const float end = expf(r.p[C - 1]);
+    const int g = lane >> 2, c = lane & 3;
     // dV = rd(mixed)^T dY + src o (K rd(carry)) ; write dx.
     {
       float acc[8][4], ve[8][4];
@@ -394,9 +440,8 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
       zero8(ve);
       warp_gemm<BF, C>(acc, row0, [&](int s, int t) { return round_to<T>(Sc[t * LDS + s] * wgt(t, s)); },
                        [&](int t, int p) { return Dy[t * LDS + p]; });
-      warp_gemm<BF, NS>(ve, row0, [&](int s, int n) { return Ks[s * LDS + n]; },
-                        [&](int n, int p) { return round_to<T>(Cy[n * LDS + p]); });
-      const int g = lane >> 2, c = lane & 3;
+      warp_gemm<BF, NS>(ve, row0, [&](int s, int n) { return Ks[s * LN + n]; },
+                        [&](int n, int p) { return round_to<T>(Cy[n * HP + p]); });
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int s = row0 + g + 8 * half, t = t0 + s;
@@ -411,53 +456,48 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
         }
       }
     }
-    // dQ = rd(Dm o W) K + rd(dY e^p) rd(start)^T  ; inherited for dp.
+    // dK = rd(Dm o W)^T Q + src o (V rd(carry)^T) -> G (64 state columns per
+    // pass); d_source = sum_n K (V rd(carry)^T).
     {
-      float acc[8][4];
-      zero8(acc);
-      warp_gemm<BF, C>(acc, row0, [&](int t, int s) { return round_to<T>(Dm[t * LDS + s] * wgt(t, s)); },
-                       [&](int s, int n) { return Ks[s * LDS + n]; });
-      warp_gemm<BF, HP>(acc, row0, [&](int t, int p) { return round_to<T>(Dy[t * LDS + p] * expf(r.p[t])); },
-                        [&](int p, int n) { return round_to<T>(St[n * LDS + p]); });
-      for_tile(acc, row0, [&](int t, int n, float v) { dq_t[t * LDS + n] = v; });
-    }
-    // dK = rd(Dm o W)^T Q + src o (V rd(carry)^T)  ; d_source.
-    {
-      float acc[8][4], ve[8][4];
-      zero8(acc);
-      zero8(ve);
-      warp_gemm<BF, C>(acc, row0, [&](int s, int t) { return round_to<T>(Dm[t * LDS + s] * wgt(t, s)); },
-                       [&](int t, int n) { return Qs[t * LDS + n]; });
-      warp_gemm<BF, HP>(ve, row0, [&](int s, int p) { return Vs[s * LDS + p]; },
-                        [&](int p, int n) { return round_to<T>(Cy[n * LDS + p]); });
       float dsrc[2] = {0.f, 0.f};
-      const int g = lane >> 2, c = lane & 3;
+      for (int nb = 0; nb < NS; nb += 64) {
+        float acc[8][4], ve[8][4];
+        zero8(acc);
+        zero8(ve);
+        warp_gemm<BF, C>(acc, row0, [&](int s, int t) { return round_to<T>(Dm[t * LDS + s] * wgt(t, s)); },
+                         [&](int t, int n) { return nb + n < NS ? Qs[t * LN + nb + n] : 0.f; });
+        warp_gemm<BF, HP>(ve, row0, [&](int s, int p) { return Vs[s * LDS + p]; },
+                          [&](int p, int n) { return nb + n < NS ? round_to<T>(Cy[(nb + n) * HP + p]) : 0.f; });
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int s = row0 + g + 8 * half;
+          const float src = r.scl[s] * r.tail[s];
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int n = nb + nt * 8 + 2 * c + e;
+              if (n < NS) {
+                dsrc[half] = fmaf(Ks[s * LN + n], ve[nt][2 * half + e], dsrc[half]);
+                G[s * LN + n] = fmaf(src, ve[nt][2 * half + e], acc[nt][2 * half + e]);
+              }
+            }
+        }
+      }
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
-        const int s = row0 + g + 8 * half;
-        const float src = r.scl[s] * r.tail[s];
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int n = nt * 8 + 2 * c + e;
-            dsrc[half] = fmaf(Ks[s * LDS + n], ve[nt][2 * half + e], dsrc[half]);
-            dk_t[s * LDS + n] = fmaf(src, ve[nt][2 * half + e], acc[nt][2 * half + e]);
-          }
-        // reduce over the 4 lanes sharing the row
         float v = dsrc[half];
         v += __shfl_xor_sync(0xffffffffu, v, 1);
         v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (c == 0) vec[0 * C + s] = v;  // d_source
+        if (c == 0) vec[0 * C + row0 + g + 8 * half] = v;  // d_source
       }
     }
     // inherited . dY (dp term) : rows t, e^(p_t) sum_p dY[t,p] (Q rd(start))[t,p]
     {
       float acc[8][4];
       zero8(acc);
-      warp_gemm<BF, NS>(acc, row0, [&](int t, int n) { return Qs[t * LDS + n]; },
-                        [&](int n, int p) { return round_to<T>(St[n * LDS + p]); });
-      const int g = lane >> 2, c = lane & 3;
+      warp_gemm<BF, NS>(acc, row0, [&](int t, int n) { return Qs[t * LN + n]; },
+                        [&](int n, int p) { return round_to<T>(St[n * HP + p]); });
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int t = row0 + g + 8 * half;
@@ -495,10 +535,13 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
     // <carry, start> for the chunk-end decay.
     {
       float part = 0.f;
-      for (int i = tid; i < NS * HP; i += THREADS) part = fmaf(Cy[(i / HP) * LDS + i % HP], St[(i / HP) * LDS + i % HP], part);
+      for (int i = tid; i < NS * HP; i += THREADS) part = fmaf(Cy[i], St[i], part);
       part = warp_sum(part);
       if (lane == 0) scratch[warp] = part;
     }
+    // Rotation backward of dK (pre-rotation gradient to o.dk, its pair-phase
+    // gradient into dth).
+    rotate_back<T, NS, false>(d, b, h, t0, cq, bk, qb, kb, theta, G, dth, o.dk);
     __syncthreads();
     if (tid < 32) {
       // d_log_decay = suffix sum of dp (+ chunk-end terms at the last position)
@@ -512,68 +555,56 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
       vec[6 * C + 63 - tid] = shi;
       vec[6 * C + 31 - tid] = slo;
     }
-    __syncthreads();
-    // New carry: d_start = Q^T rd(dY e^p) + e^(p_L) carry.
+    if (tid < NS) {  // key-bias partials over this chunk's tokens (column tid)
+      float sk = 0.f;
+      for (int tt = 0; tt < C && t0 + tt < d.T; ++tt) sk += G[tt * LN + tid];
+      kbs += sk;
+    }
+    // New carry: d_start = Q^T rd(dY e^p) + e^(p_L) carry (every read of the
+    // old carry in this chunk is done: dV, dK and the dot product above).
     {
+      float acc[2][8][4];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) zero8(acc[k]);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int n0 = row0 + 64 * k;
+        if (n0 < NS)
+          warp_gemm<BF, C>(acc[k], n0, [&](int n, int t) { return Qs[t * LN + n]; },
+                           [&](int t, int p) { return round_to<T>(Dy[t * LDS + p] * expf(r.p[t])); });
+      }
+      __syncthreads();  // G's bias sums are done too: G is rewritten below
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int n0 = row0 + 64 * k;
+        if (n0 < NS) for_tile(acc[k], n0, [&](int n, int p, float v) { Cy[n * HP + p] = fmaf(end, Cy[n * HP + p], v); });
+      }
+    }
+    // dQ = rd(Dm o W) K + rd(dY e^p) rd(start)^T -> G (64 state columns per pass).
+    for (int nb = 0; nb < NS; nb += 64) {
       float acc[8][4];
       zero8(acc);
-      warp_gemm<BF, C>(acc, row0, [&](int n, int t) { return Qs[t * LDS + n]; },
-                       [&](int t, int p) { return round_to<T>(Dy[t * LDS + p] * expf(r.p[t])); });
-      __syncthreads();
-      for_tile(acc, row0, [&](int n, int p, float v) { Cy[n * LDS + p] = fmaf(end, Cy[n * LDS + p], v); });
-    }
-    // Rotation backward: dq_pre = R^T dQ, d_theta = dQ.J q_rot + dK.J k_rot.
-    // Per-token, per-pair: write dq/dk pre-rotation and d_theta per pair.
-    for (int idx = tid; idx < C * (NS / 2); idx += THREADS) {
-      const int tt = idx / (NS / 2), i = idx % (NS / 2), t = t0 + tt;
-      const int n0 = 2 * i, n1 = 2 * i + 1;
-      const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
-      const float gq0 = dq_t[tt * LDS + n0], gq1 = dq_t[tt * LDS + n1];
-      const float gk0 = dk_t[tt * LDS + n0], gk1 = dk_t[tt * LDS + n1];
-      const float pq0 = gq0 * cs + gq1 * sn, pq1 = gq1 * cs - gq0 * sn;
-      const float pk0 = gk0 * cs + gk1 * sn, pk1 = gk1 * cs - gk0 * sn;
-      if (t < d.T) {
-        const size_t base = ((size_t(b) * d.T + t) * d.H + h) * NS;
-        o.dq[base + n0] = pq0; o.dq[base + n1] = pq1;
-        o.dk[base + n0] = pk0; o.dk[base + n1] = pk1;
-      }
-      // Pre-rotation gradients kept for the bias sums.
-      Sc[tt * LDS + n0] = pq0; Sc[tt * LDS + n1] = pq1;
-      Dm[tt * LDS + n0] = pk0; Dm[tt * LDS + n1] = pk1;
+      warp_gemm<BF, C>(acc, row0, [&](int t, int s) { return round_to<T>(Dm[t * LDS + s] * wgt(t, s)); },
+                       [&](int s, int n) { return nb + n < NS ? Ks[s * LN + nb + n] : 0.f; });
+      warp_gemm<BF, HP>(acc, row0, [&](int t, int p) { return round_to<T>(Dy[t * LDS + p] * expf(r.p[t])); },
+                        [&](int p, int n) { return nb + n < NS ? round_to<T>(St[(nb + n) * HP + p]) : 0.f; });
+      for_tile(acc, row0, [&](int t, int n, float v) { if (nb + n < NS) G[t * LN + nb + n] = v; });
     }
     __syncthreads();
-    // d_theta per pair from the fp32 rotated values before rounding
-    // (flashmamba.py:776), recomputed since Qf/Kf now hold dQ/dK.
-    for (int idx = tid; idx < C * (NS / 2); idx += THREADS) {
-      const int tt = idx / (NS / 2), i = idx % (NS / 2), t = t0 + tt;
-      const int n0 = 2 * i, n1 = 2 * i + 1;
-      float c0 = 0.f, c1 = 0.f, b0 = 0.f, b1 = 0.f;
-      if (t < d.T) {
-        const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * NS : (size_t(b) * d.T + t) * NS;
-        c0 = to_f(cq[base + n0]); c1 = to_f(cq[base + n1]);
-        b0 = to_f(bk[base + n0]); b1 = to_f(bk[base + n1]);
-      }
-      const float q0 = round_to<T>(c0 + (qb ? qb[h * NS + n0] : 0.f));
-      const float q1 = round_to<T>(c1 + (qb ? qb[h * NS + n1] : 0.f));
-      const float k0 = round_to<T>(b0 + (kb ? kb[h * NS + n0] : 0.f));
-      const float k1 = round_to<T>(b1 + (kb ? kb[h * NS + n1] : 0.f));
-      const float cs = cosv[tt * 33 + i], sn = sinv[tt * 33 + i];
-      const float qr0 = q0 * cs - q1 * sn, qr1 = q1 * cs + q0 * sn;
-      const float kr0 = k0 * cs - k1 * sn, kr1 = k1 * cs + k0 * sn;
-      const float gq0 = dq_t[tt * LDS + n0], gq1 = dq_t[tt * LDS + n1];
-      const float gk0 = dk_t[tt * LDS + n0], gk1 = dk_t[tt * LDS + n1];
-      // partner(q_rot) = (-qr1, qr0)
-      const float dth = gq0 * (-qr1) + gq1 * qr0 + gk0 * (-kr1) + gk1 * kr0;
-      theta[tt * 33 + i] = i < d.A ? dth : 0.f;
-    }
+    rotate_back<T, NS, true>(d, b, h, t0, cq, bk, qb, kb, theta, G, dth, o.dq);
     __syncthreads();
-    // Suffix sums of d_theta per pair -> rate and dt gradients.
+    if (tid < NS) {  // query-bias partials
+      float sq = 0.f;
+      for (int tt = 0; tt < C && t0 + tt < d.T; ++tt) sq += G[tt * LN + tid];
+      qbs += sq;
+    }
+    // Suffix sums of the pair-phase gradient -> rate and dt gradients.
     if (tid < d.A) {
       const int i = tid;
       float acc = later[i];
       for (int tt = C - 1; tt >= 0; --tt) {
-        acc += theta[tt * 33 + i];
-        theta[tt * 33 + i] = acc;  // d_increment (pair) at tt
+        acc += dth[tt * TW + i];
+        dth[tt * TW + i] = acc;  // d_increment (pair) at tt
       }
       later[i] = acc;
     }
@@ -585,7 +616,7 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
         for (int i = 0; i < d.A; ++i) {
           const float rate = d.per_head ? angles[((size_t(b) * d.T + t) * d.H + h) * d.A + i]
                                         : angles[(size_t(b) * d.T + t) * d.A + i];
-          const float inc = theta[tt * 33 + i];
+          const float inc = dth[tt * TW + i];
           o.drate[((size_t(b) * d.T + t) * d.H + h) * d.A + i] = inc * r.dt[tt];
           ddt = fmaf(inc, rate, ddt);
         }
@@ -595,15 +626,6 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
         o.dscl[si] = vec[4 * C + tt];
         o.dlog[si] = vec[6 * C + tt];
       }
-    }
-    // Bias partial sums over this chunk's tokens (column tid).
-    if (tid < NS) {
-      float sq = 0.f, sk = 0.f;
-      for (int tt = 0; tt < C; ++tt) {
-        if (t0 + tt < d.T) { sq += Sc[tt * LDS + tid]; sk += Dm[tt * LDS + tid]; }
-      }
-      qbs += sq;
-      kbs += sk;
     }
     __syncthreads();
   }
@@ -615,7 +637,7 @@ __global__ void __launch_bounds__(THREADS) bwd_kernel(
 
 // dc/db: sum the per-head pre-rotation gradients over heads (fixed order),
 // or copy them for per-head layouts; cast to the model dtype.
-template <typename T>
+template <typename T, int NS>
 __global__ void reduce_heads_kernel(Dims d, const float* __restrict__ dq, const float* __restrict__ dk,
                                     T* __restrict__ dc, T* __restrict__ db) {
   const size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -673,6 +695,7 @@ __global__ void gates_kernel(Dims d, const float* __restrict__ dt, const float* 
   }
 }
 
+template <int NS>
 __global__ void bias_kernel(Dims d, const float* __restrict__ dqb, const float* __restrict__ dkb,
                             float* __restrict__ d_qb, float* __restrict__ d_kb) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -686,39 +709,41 @@ __global__ void bias_kernel(Dims d, const float* __restrict__ dqb, const float* 
   if (d_kb) d_kb[idx] = sk;
 }
 
+// bf16 operands at state dim 64 run the chunk-parallel tensor-core kernels of
+// scan_bf16.cuh; every other case the sequential kernels above.
+inline bool fast_path(const M4ScanDims& s) { return s.bf16 && s.state_dim == 64; }
+
 struct Layout {
   size_t starts, phases, deltas, resid;
-  size_t dq, dk, drate, dgam, dscl, dlog, ddtp, dqb, dkb, carries, dth, work;
+  size_t dq, dk, drate, dgam, dscl, dlog, ddtp, dqb, dkb, carries, dth, carry, work;
 };
 
 inline Layout layout(const M4ScanDims& s) {
   Layout l;
   const int nch = (s.time + C - 1) / C;
+  const size_t ns = size_t(s.state_dim), np = ns / 2;
   const size_t bh = size_t(s.batch) * s.heads, bth = size_t(s.batch) * s.time * s.heads;
+  const bool fast = fast_path(s);
   size_t off = 0;
-  l.starts = off; off += align256(bh * nch * NS * HP * sizeof(float));
-  l.phases = off; off += align256(bh * nch * 32 * sizeof(float));
+  l.starts = off; off += align256(bh * nch * ns * HP * sizeof(float));
+  l.phases = off; off += align256(bh * nch * np * sizeof(float));
   l.deltas = off; off += align256(bh * nch * sizeof(float));
   l.resid = off;
   off = 0;
-  l.dq = off; off += align256(bth * NS * sizeof(float));
-  l.dk = off; off += align256(bth * NS * sizeof(float));
-  l.drate = off; off += align256(bth * 32 * sizeof(float));
+  l.dq = off; off += align256(bth * ns * sizeof(float));
+  l.dk = off; off += align256(bth * ns * sizeof(float));
+  l.drate = off; off += align256(bth * np * sizeof(float));
   l.dgam = off; off += align256(bth * sizeof(float));
   l.dscl = off; off += align256(bth * sizeof(float));
   l.dlog = off; off += align256(bth * sizeof(float));
   l.ddtp = off; off += align256(bth * sizeof(float));
-  l.dqb = off; off += align256(bh * nch * NS * sizeof(float));
-  l.dkb = off; off += align256(bh * nch * NS * sizeof(float));
-  l.carries = s.bf16 ? off : 0; off += s.bf16 ? align256(bh * nch * NS * HP * sizeof(float)) : 0;
-  l.dth = off; off += align256(bh * nch * 32 * sizeof(float));
+  l.dqb = off; off += align256(bh * nch * ns * sizeof(float));
+  l.dkb = off; off += align256(bh * nch * ns * sizeof(float));
+  l.carries = fast ? off : 0; off += fast ? align256(bh * nch * ns * HP * sizeof(float)) : 0;
+  l.dth = off; off += align256(bh * nch * np * sizeof(float));
+  l.carry = fast ? 0 : off; off += fast ? 0 : align256(bh * ns * HP * sizeof(float));
   l.work = off;
   return l;
-}
-
-inline size_t fwd_smem() { return (5 * C * LDS + C * 33 + 32 + C + sizeof(Rows) / 4) * sizeof(float); }
-inline size_t bwd_smem() {
-  return (10 * C * LDS + 3 * C * 33 + 32 + C + 8 * C + sizeof(Rows) / 4) * sizeof(float);
 }
 
 inline Dims make_dims(const M4ScanDims& s) {
@@ -729,12 +754,15 @@ inline Dims make_dims(const M4ScanDims& s) {
   return d;
 }
 
+inline bool state_dim_supported(int n) { return n == 64 || n == 96 || n == 128; }
+
 inline int check(const M4ScanDims* s) {
   if (!s) return M4_ERR_NULL;
   if (s->batch <= 0 || s->time <= 0 || s->heads <= 0 || s->head_dim <= 0 || s->state_dim <= 0 ||
       s->angle_count < 0 || s->chunk <= 0)
     return M4_ERR_DIMS;
-  if (s->head_dim != HP || s->state_dim != NS || s->chunk != C || s->angle_count > NS / 2)
+  if (s->head_dim != HP || !state_dim_supported(s->state_dim) || s->chunk != C ||
+      s->angle_count > s->state_dim / 2)
     return M4_ERR_UNSUPPORTED;
   return M4_OK;
 }
@@ -748,32 +776,27 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
                          void* db, void* dx, float* d_adt, float* d_dt, float* d_trap, float* d_angles,
                          float* d_qb, float* d_kb, char* work, cudaStream_t st);
 
-template <typename T>
-int forward(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
-            const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
-            void* y, float* fin, char* resid, cudaStream_t st) {
-  if constexpr (sizeof(T) == 2)
-    return forward_bf16(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
+template <typename T, int NS>
+int forward_seq(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
+                void* y, float* fin, char* resid, cudaStream_t st) {
   const Dims d = make_dims(s);
   const Layout l = layout(s);
-  const size_t sm = fwd_smem();
-  cudaFuncSetAttribute(fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-  fwd_kernel<T><<<s.batch * s.heads, THREADS, sm, st>>>(
+  const size_t sm = fwd_smem<NS>();
+  cudaFuncSetAttribute(fwd_kernel<T, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  fwd_kernel<T, NS><<<s.batch * s.heads, THREADS, sm, st>>>(
       d, static_cast<const T*>(c), static_cast<const T*>(b), static_cast<const T*>(x), adt, dt, trap,
       angles, qb, kb, static_cast<T*>(y), fin, reinterpret_cast<float*>(resid + l.starts),
       reinterpret_cast<float*>(resid + l.phases));
   return launch_status();
 }
 
-template <typename T>
-int backward(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
-             const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
-             const char* resid, const void* dy, const float* d_final, void* dc, void* db, void* dx,
-             float* d_adt, float* d_dt, float* d_trap, float* d_angles, float* d_qb, float* d_kb,
-             char* work, cudaStream_t st) {
-  if constexpr (sizeof(T) == 2)
-    return backward_bf16(s, c, b, x, adt, dt, trap, angles, qb, kb, resid, dy, d_final, dc, db, dx, d_adt,
-                         d_dt, d_trap, d_angles, d_qb, d_kb, work, st);
+template <typename T, int NS>
+int backward_seq(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                 const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
+                 const char* resid, const void* dy, const float* d_final, void* dc, void* db, void* dx,
+                 float* d_adt, float* d_dt, float* d_trap, float* d_angles, float* d_qb, float* d_kb,
+                 char* work, cudaStream_t st) {
   const Dims d = make_dims(s);
   const Layout l = layout(s);
   BwdOut o;
@@ -786,24 +809,57 @@ int backward(const M4ScanDims& s, const void* c, const void* b, const void* x, c
   o.ddtp = reinterpret_cast<float*>(work + l.ddtp);
   o.dqb = reinterpret_cast<float*>(work + l.dqb);
   o.dkb = reinterpret_cast<float*>(work + l.dkb);
-  const size_t sm = bwd_smem();
-  cudaFuncSetAttribute(bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
-  bwd_kernel<T><<<s.batch * s.heads, THREADS, sm, st>>>(
+  o.carry = reinterpret_cast<float*>(work + l.carry);
+  const size_t sm = bwd_smem<NS>();
+  cudaFuncSetAttribute(bwd_kernel<T, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sm));
+  bwd_kernel<T, NS><<<s.batch * s.heads, THREADS, sm, st>>>(
       d, static_cast<const T*>(c), static_cast<const T*>(b), static_cast<const T*>(x), adt, dt, trap,
       angles, qb, kb, reinterpret_cast<const float*>(resid + l.starts),
       reinterpret_cast<const float*>(resid + l.phases), static_cast<const T*>(dy), d_final,
       static_cast<T*>(dx), o);
   const size_t n1 = s.per_head ? size_t(s.batch) * s.time * s.heads * NS : size_t(s.batch) * s.time * NS;
-  reduce_heads_kernel<T><<<unsigned((n1 + 255) / 256), 256, 0, st>>>(d, o.dq, o.dk, static_cast<T*>(dc),
-                                                                      static_cast<T*>(db));
+  reduce_heads_kernel<T, NS><<<unsigned((n1 + 255) / 256), 256, 0, st>>>(d, o.dq, o.dk, static_cast<T*>(dc),
+                                                                          static_cast<T*>(db));
   size_t n2 = size_t(s.batch) * s.time * s.heads;
   const size_t na = s.per_head ? n2 * s.angle_count : size_t(s.batch) * s.time * s.angle_count;
   if (na > n2) n2 = na;
   gates_kernel<<<unsigned((n2 + 255) / 256), 256, 0, st>>>(d, dt, trap, o.dgam, o.dscl, o.dlog, o.ddtp,
                                                             o.drate, d_adt, d_dt, d_trap, d_angles);
   if (d_qb || d_kb)
-    bias_kernel<<<(s.heads * NS + 255) / 256, 256, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
+    bias_kernel<NS><<<(s.heads * NS + 255) / 256, 256, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
   return launch_status();
+}
+
+template <typename T>
+int forward(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+            const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
+            void* y, float* fin, char* resid, cudaStream_t st) {
+  if (fast_path(s)) return forward_bf16(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
+  switch (s.state_dim) {
+    case 64: return forward_seq<T, 64>(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
+    case 96: return forward_seq<T, 96>(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
+    default: return forward_seq<T, 128>(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
+  }
+}
+
+template <typename T>
+int backward(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+             const float* dt, const float* trap, const float* angles, const float* qb, const float* kb,
+             const char* resid, const void* dy, const float* d_final, void* dc, void* db, void* dx,
+             float* d_adt, float* d_dt, float* d_trap, float* d_angles, float* d_qb, float* d_kb,
+             char* work, cudaStream_t st) {
+  if (fast_path(s))
+    return backward_bf16(s, c, b, x, adt, dt, trap, angles, qb, kb, resid, dy, d_final, dc, db, dx, d_adt,
+                         d_dt, d_trap, d_angles, d_qb, d_kb, work, st);
+#define M4_SEQ_BWD(NSV)                                                                                     \
+  return backward_seq<T, NSV>(s, c, b, x, adt, dt, trap, angles, qb, kb, resid, dy, d_final, dc, db, dx, \
+                              d_adt, d_dt, d_trap, d_angles, d_qb, d_kb, work, st)
+  switch (s.state_dim) {
+    case 64: M4_SEQ_BWD(64);
+    case 96: M4_SEQ_BWD(96);
+    default: M4_SEQ_BWD(128);
+  }
+#undef M4_SEQ_BWD
 }
 
 }  // namespace scan
@@ -985,15 +1041,15 @@ extern "C" int m4_scan_bwd(const M4ScanDims* s, const void* c, const void* b, co
 //   rotate(round(b + k_bias), phase') rounded to the model dtype;
 //   S' = e^(adt) (S + dt (1 - trap) k_prev v_prev^T) + dt trap K x^T;
 //   y = Q^T S' (model dtype); cache' = (S', K, x, phase').
-// One CTA of 256 threads per (batch, head); thread (n, p0) = (tid / 4,
-// 16 (tid % 4)) updates S'[n][p0 .. p0+15]. Outputs may alias the cache
+// One CTA of 4 N threads per (batch, head) (state dim N in {64, 96, 128});
+// thread (n, p0) = (tid / 4, 16 (tid % 4)) updates S'[n][p0 .. p0+15]. Outputs may alias the cache
 // inputs: every cache value is read before any is written.
 // ---------------------------------------------------------------------------
 namespace m4 {
 namespace scan {
 
-template <typename T>
-__global__ void __launch_bounds__(256) step_kernel(
+template <typename T, int NS>
+__global__ void __launch_bounds__(4 * NS) step_kernel(
     int H, int A, int per_head, const float* state, const float* prev_k, const float* prev_v,
     const float* phase, const T* __restrict__ c, const T* __restrict__ bk, const T* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
@@ -1001,7 +1057,7 @@ __global__ void __launch_bounds__(256) step_kernel(
     T* __restrict__ y, float* state_out, float* prev_k_out, float* prev_v_out, float* phase_out) {
   const int bh = blockIdx.x, bb = bh / H, h = bh % H, tid = threadIdx.x;
   __shared__ float qr[NS], kr[NS], xv[HP], pk[NS], pv[HP], ph[NS / 2];
-  __shared__ float red[8][HP];
+  __shared__ float red[NS / 8][HP];
   const float dtv = dt[bh];
   const float trap = 1.f / (1.f + expf(-trap_logits[bh]));
   const float alpha = expf(adt[bh]);
@@ -1086,7 +1142,7 @@ __global__ void __launch_bounds__(256) step_kernel(
   if (tid < HP) {
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) acc += red[w][tid];
+    for (int w = 0; w < NS / 8; ++w) acc += red[w][tid];
     y[size_t(bh) * HP + tid] = from_f<T>(acc);
   }
 }
@@ -1103,7 +1159,7 @@ extern "C" int m4_scan_step(const M4ScanDims* s, const float* state, const float
   if (!s) return M4_ERR_NULL;
   if (s->batch <= 0 || s->heads <= 0 || s->head_dim <= 0 || s->state_dim <= 0 || s->angle_count < 0)
     return M4_ERR_DIMS;
-  if (s->head_dim != scan::HP || s->state_dim != scan::NS || s->angle_count > scan::NS / 2)
+  if (s->head_dim != scan::HP || !scan::state_dim_supported(s->state_dim) || s->angle_count > s->state_dim / 2)
     return M4_ERR_UNSUPPORTED;
   if (!state || !prev_keys || !prev_values || !c || !b || !x || !adt || !dt || !trap || !y || !state_out ||
       !prev_keys_out || !prev_values_out)
@@ -1112,17 +1168,21 @@ extern "C" int m4_scan_step(const M4ScanDims* s, const float* state, const float
   if (!all_aligned16(state, state_out)) return M4_ERR_ALIGN;
   cudaStream_t strm = static_cast<cudaStream_t>(stream);
   const int grid = s->batch * s->heads;
-  if (s->bf16)
-    scan::step_kernel<__nv_bfloat16><<<grid, 256, 0, strm>>>(
-        s->heads, s->angle_count, s->per_head, state, prev_keys, prev_values, phase,
-        static_cast<const __nv_bfloat16*>(c), static_cast<const __nv_bfloat16*>(b),
-        static_cast<const __nv_bfloat16*>(x), adt, dt, trap, angles, qb, kb, static_cast<__nv_bfloat16*>(y),
-        state_out, prev_keys_out, prev_values_out, phase_out);
-  else
-    scan::step_kernel<float><<<grid, 256, 0, strm>>>(
-        s->heads, s->angle_count, s->per_head, state, prev_keys, prev_values, phase,
-        static_cast<const float*>(c), static_cast<const float*>(b), static_cast<const float*>(x), adt, dt, trap,
-        angles, qb, kb, static_cast<float*>(y), state_out, prev_keys_out, prev_values_out, phase_out);
+#define M4_STEP(T, NSV)                                                                                         \
+  scan::step_kernel<T, NSV><<<grid, 4 * NSV, 0, strm>>>(                                                       \
+      s->heads, s->angle_count, s->per_head, state, prev_keys, prev_values, phase, static_cast<const T*>(c),  \
+      static_cast<const T*>(b), static_cast<const T*>(x), adt, dt, trap, angles, qb, kb, static_cast<T*>(y),  \
+      state_out, prev_keys_out, prev_values_out, phase_out)
+  if (s->bf16) {
+    if (s->state_dim == 64) M4_STEP(__nv_bfloat16, 64);
+    else if (s->state_dim == 96) M4_STEP(__nv_bfloat16, 96);
+    else M4_STEP(__nv_bfloat16, 128);
+  } else {
+    if (s->state_dim == 64) M4_STEP(float, 64);
+    else if (s->state_dim == 96) M4_STEP(float, 96);
+    else M4_STEP(float, 128);
+  }
+#undef M4_STEP
   return launch_status();
 }
 

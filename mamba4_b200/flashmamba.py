@@ -18,7 +18,8 @@ import torch.nn.functional as F
 
 from . import _lib
 
-STATE_DIM = 64
+STATE_DIMS = (64, 96, 128)   # state dims the kernels implement (smaller ones are padded)
+STATE_DIM = STATE_DIMS[-1]
 HEAD_DIM = 64
 CHUNK = 64
 
@@ -27,16 +28,26 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+def kernel_state_dim(state_dim: int) -> int:
+    """Smallest state dim the kernels implement that holds `state_dim`
+    (zero-padded coordinates never interact)."""
+    for n in STATE_DIMS:
+        if state_dim <= n:
+            return n
+    raise ValueError(f"Scan supports state dims up to {STATE_DIM}")
+
+
 def scan_forward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
     """m4_scan_fwd on padded, contiguous operands: returns y, final, residual."""
     lib = _lib.load()
     batch, time = c.shape[:2]
     heads = dt.shape[-1]
     bf16 = x.dtype == torch.bfloat16
-    dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, angles.shape[-1], CHUNK,
+    n = c.shape[-1]
+    dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, n, angles.shape[-1], CHUNK,
                          int(bf16), int(per_head))
     y = torch.empty_like(x)
-    final = torch.empty(batch, heads, STATE_DIM, HEAD_DIM, device=x.device)
+    final = torch.empty(batch, heads, n, HEAD_DIM, device=x.device)
     nbytes = lib.m4_scan_residual_bytes(ctypes.byref(dims))
     resid = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
     _lib.check(
@@ -53,7 +64,7 @@ def scan_backward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, resid, d_y, d_
     batch, time = c.shape[:2]
     heads = dt.shape[-1]
     bf16 = x.dtype == torch.bfloat16
-    dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, STATE_DIM, angles.shape[-1], CHUNK, int(bf16),
+    dims = _lib.ScanDims(batch, time, heads, HEAD_DIM, c.shape[-1], angles.shape[-1], CHUNK, int(bf16),
                          int(per_head))
     d_y = torch.zeros_like(x) if d_y is None else d_y.to(x.dtype).contiguous()
     d_final = None if d_final is None else d_final.float().contiguous()
@@ -76,7 +87,7 @@ def scan_backward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, resid, d_y, d_
 
 
 class _Scan(torch.autograd.Function):
-    """Forward/backward over padded operands (N = P = 64, chunk 64)."""
+    """Forward/backward over padded operands (N in {64, 96, 128}, P = 64, chunk 64)."""
 
     @staticmethod
     def forward(ctx, c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
@@ -96,16 +107,17 @@ def _pad(t, pads):
 
 
 def _prepare(c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, per_head):
-    """Pad N and P to 64 (zero coordinates do not interact) and fix dtypes."""
+    """Pad N to the next kernel state dim (64, 96 or 128) and P to 64 (zero
+    coordinates do not interact) and fix dtypes."""
     state_dim = c.shape[-1]
     value_dim = x.shape[-1] // heads
     if state_dim % 2 or angles.shape[-1] > state_dim // 2:
         # Message of lm/kernels/mamba3.py:23-24.
         raise ValueError("Mamba-3 state dimension must be even and contain angles")
     if state_dim > STATE_DIM or value_dim > HEAD_DIM:
-        raise ValueError(f"Scan supports state and head dims up to {STATE_DIM}")
+        raise ValueError(f"Scan supports state dims up to {STATE_DIM} and head dims up to {HEAD_DIM}")
     model = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
-    pn = (0, STATE_DIM - state_dim)
+    pn = (0, kernel_state_dim(state_dim) - state_dim)
     c = _pad(c.to(model), pn).contiguous()
     b = _pad(b.to(model), pn).contiguous()
     lead = x.shape[:-1]
@@ -140,7 +152,7 @@ def mamba3_fused(
     if value_dim != HEAD_DIM:
         lead = y.shape[:-1]
         y = y.reshape(*lead, heads, HEAD_DIM)[..., :value_dim].reshape(*lead, heads * value_dim)
-    if state_dim != STATE_DIM or value_dim != HEAD_DIM:
+    if state_dim != final.shape[2] or value_dim != HEAD_DIM:
         final = final[:, :, :state_dim, :value_dim]
     return y, final
 
@@ -230,9 +242,10 @@ def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias,
     if state_dim % 2 or angle_count > state_dim // 2:
         raise ValueError("Mamba-3 state dimension must be even and contain angles")
     if state_dim > STATE_DIM or value_dim > HEAD_DIM:
-        raise ValueError(f"Scan supports state and head dims up to {STATE_DIM}")
+        raise ValueError(f"Scan supports state dims up to {STATE_DIM} and head dims up to {HEAD_DIM}")
     model = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
-    pad_n, pad_p = STATE_DIM - state_dim, HEAD_DIM - value_dim
+    kn = kernel_state_dim(state_dim)
+    pad_n, pad_p = kn - state_dim, HEAD_DIM - value_dim
     c = _pad(c.to(model), (0, pad_n)).contiguous()
     b = _pad(b.to(model), (0, pad_n)).contiguous()
     xp = _pad(x.to(model).reshape(batch, heads, value_dim), (0, pad_p))
@@ -249,7 +262,7 @@ def mamba3_step(cache, c, b, x, adt, dt, trap_logits, angles, *, q_bias, k_bias,
         st_out, pk_out, pv_out, ph_out = st, pk, pv, ph
     else:
         st_out, pk_out, pv_out, ph_out = (torch.empty_like(t) for t in (st, pk, pv, ph))
-    dims = _lib.ScanDims(batch, 1, heads, HEAD_DIM, STATE_DIM, angle_count, CHUNK,
+    dims = _lib.ScanDims(batch, 1, heads, HEAD_DIM, kn, angle_count, CHUNK,
                          int(model == torch.bfloat16), int(per_head))
     lib = _lib.load()
     _lib.check(

@@ -22,19 +22,19 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
-def _mix_dims(rows, inner, heads, angles, eps, stride):
-    return _lib.MixerDims(rows, inner, heads, angles, eps, stride)
+def _mix_dims(rows, inner, heads, angles, eps, stride, state):
+    return _lib.MixerDims(rows, inner, heads, angles, eps, stride, state)
 
 
 class _MambaMixerCore(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, inner, heads, angles, eps):
+    def forward(ctx, proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, inner, heads, angles, eps, state):
         lib = _lib.load()
         batch, time, width = proj.shape
         rows = batch * time
-        dims = _mix_dims(rows, inner, heads, angles, eps, width)
+        dims = _mix_dims(rows, inner, heads, angles, eps, width, state)
         dev = proj.device
-        c = torch.empty(batch, time, 64, dtype=torch.bfloat16, device=dev)
+        c = torch.empty(batch, time, state, dtype=torch.bfloat16, device=dev)
         b = torch.empty_like(c)
         x = torch.empty(batch, time, inner, dtype=torch.bfloat16, device=dev)
         adt = torch.empty(batch, time, heads, device=dev)
@@ -43,15 +43,15 @@ class _MambaMixerCore(torch.autograd.Function):
         _lib.check(lib.m4_mixer_prep_fwd(ctypes.byref(dims), *map(_lib.ptr, (
             proj, b_scale, c_scale, dt_bias, c, b, x, adt, dt, trap, ang)), _stream()),
             "m4_mixer_prep_fwd")
-        qb = q_bias.reshape(heads, 64)
-        kb = k_bias.reshape(heads, 64)
+        qb = q_bias.reshape(heads, state)
+        kb = k_bias.reshape(heads, state)
         y, _, resid = scan_forward(c, b, x, adt, dt, trap, ang, qb, kb, False)
         out = torch.empty(batch, time, inner, dtype=torch.bfloat16, device=dev)
         _lib.check(lib.m4_mixer_post_fwd(ctypes.byref(dims), *map(_lib.ptr, (proj, y, D, out)), _stream()),
                    "m4_mixer_post_fwd")
         ctx.save_for_backward(proj, b_scale, c_scale, dt_bias, D, c, b, x, adt, dt, trap, ang, qb, kb,
                               resid, y)
-        ctx.cfg = (inner, heads, angles, eps)
+        ctx.cfg = (inner, heads, angles, eps, state)
         return out
 
     @staticmethod
@@ -59,12 +59,12 @@ class _MambaMixerCore(torch.autograd.Function):
         lib = _lib.load()
         (proj, b_scale, c_scale, dt_bias, D, c, b, x, adt, dt, trap, ang, qb, kb, resid,
          y) = ctx.saved_tensors
-        inner, heads, angles, eps = ctx.cfg
+        inner, heads, angles, eps, state = ctx.cfg
         batch, time, width = proj.shape
-        dims = _mix_dims(batch * time, inner, heads, angles, eps, width)
+        dims = _mix_dims(batch * time, inner, heads, angles, eps, width, state)
         g_out = g_out.to(torch.bfloat16).contiguous()
         nw = lib.m4_mixer_partial_rows(ctypes.byref(dims))
-        part = torch.empty(nw * (128 + heads), device=proj.device)
+        part = torch.empty(nw * (2 * state + heads), device=proj.device)
         d_proj = torch.empty_like(proj)
         d_y = torch.empty_like(y)
         dD = torch.empty_like(D)
@@ -76,31 +76,33 @@ class _MambaMixerCore(torch.autograd.Function):
         _lib.check(lib.m4_mixer_prep_bwd(ctypes.byref(dims), *map(_lib.ptr, (
             proj, b_scale, c_scale, dt_bias, D, g_out, dc, db, dx, dadt, ddt, dtrap, dang, d_proj, part,
             d_bs, d_cs, d_dtb)), _stream()), "m4_mixer_prep_bwd")
-        return (d_proj, d_bs, d_cs, d_dtb, dD, dqb.reshape(heads, 1, 64), dkb.reshape(heads, 1, 64),
-                None, None, None, None)
+        return (d_proj, d_bs, d_cs, d_dtb, dD, dqb.reshape(heads, 1, state), dkb.reshape(heads, 1, state),
+                None, None, None, None, None)
 
 
-def mamba_mixer_core(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, *, inner, heads, angles, eps):
-    """proj [B,T,2 inner + 128 + 3 heads + angles] bf16 -> gated scan output
-    [B,T,inner] bf16 (input of the mixer's out projection)."""
+def mamba_mixer_core(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, *, inner, heads, angles, eps,
+                     state=64):
+    """proj [B,T,2 inner + 2 state + 3 heads + angles] bf16 -> gated scan
+    output [B,T,inner] bf16 (input of the mixer's out projection); `state`
+    is the scan state dim N (64, 96 or 128), the width of the B and C slices."""
     if not proj.is_cuda:
         raise RuntimeError("mamba_mixer_core runs on CUDA tensors only (no CPU path)")
     if proj.dtype != torch.bfloat16:
         raise ValueError("mamba_mixer_core expects a bfloat16 projection")
     f32 = lambda t: t.float().contiguous()  # noqa: E731
-    width = 2 * inner + 128 + 3 * heads + angles
+    width = 2 * inner + 2 * state + 3 * heads + angles
     if proj.shape[-1] != width:
-        raise ValueError(f"projection width {proj.shape[-1]} != 2 inner + 128 + 3 heads + angles = {width}")
+        raise ValueError(f"projection width {proj.shape[-1]} != 2 inner + 2 state + 3 heads + angles = {width}")
     if width % 8:
         # Rows are read with 16-byte loads: pad the row stride to a multiple of 8.
         proj = torch.nn.functional.pad(proj, (0, -width % 8))
     return _MambaMixerCore.apply(proj.contiguous(), f32(b_scale), f32(c_scale), f32(dt_bias), f32(D),
-                                 f32(q_bias), f32(k_bias), inner, heads, angles, eps)
+                                 f32(q_bias), f32(k_bias), inner, heads, angles, eps, state)
 
 
 @torch.no_grad()
 def mamba_mixer_step(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, cache, *, inner, heads, angles, eps,
-                     inplace=False):
+                     inplace=False, state=64):
     """One cached token of the mixer core (`_Mamba3StepMixer`,
     `lm/models/mamba4.py:412-481`): proj [B, width] bf16 and the scan cache
     -> (gated output [B, inner] bf16, new cache), through the training
@@ -112,17 +114,17 @@ def mamba_mixer_step(proj, b_scale, c_scale, dt_bias, D, q_bias, k_bias, cache, 
         raise RuntimeError("mamba_mixer_step runs on CUDA tensors only (no CPU path)")
     if proj.dtype != torch.bfloat16:
         raise ValueError("mamba_mixer_step expects a bfloat16 projection")
-    width = 2 * inner + 128 + 3 * heads + angles
+    width = 2 * inner + 2 * state + 3 * heads + angles
     if proj.shape[-1] != width:
-        raise ValueError(f"projection width {proj.shape[-1]} != 2 inner + 128 + 3 heads + angles = {width}")
+        raise ValueError(f"projection width {proj.shape[-1]} != 2 inner + 2 state + 3 heads + angles = {width}")
     if width % 8:
         proj = torch.nn.functional.pad(proj, (0, -width % 8))
     proj = proj.contiguous()
     lib = _lib.load()
     batch = proj.shape[0]
-    dims = _mix_dims(batch, inner, heads, angles, eps, proj.shape[-1])
+    dims = _mix_dims(batch, inner, heads, angles, eps, proj.shape[-1], state)
     dev = proj.device
-    c = torch.empty(batch, 64, dtype=torch.bfloat16, device=dev)
+    c = torch.empty(batch, state, dtype=torch.bfloat16, device=dev)
     b = torch.empty_like(c)
     x = torch.empty(batch, inner, dtype=torch.bfloat16, device=dev)
     adt = torch.empty(batch, heads, device=dev)

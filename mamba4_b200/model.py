@@ -35,7 +35,7 @@ class Mamba4Config:
     layer_pattern: str = "SSSM" * 4
     expand: int = 2
     head_dim: int = 64          # Mamba-3 head dim (16 heads at d_model 512)
-    d_state: int = 64           # Mamba-3 state dim (kernel size N = 64)
+    d_state: int = 96           # Mamba-3 state dim N (the kernels run 64, 96 and 128)
     rope_fraction: float = 0.5  # angle pairs = d_state * rope_fraction / 2
     key_dim: int = 64           # memory key dim
     memory_head_dim: int = 128  # memory value dim (8 heads at d_model 512)
@@ -68,11 +68,13 @@ class Mamba4Config:
 CONFIGS = {
     # d_model 512, 16 blocks (12 Mamba-3 + 4 memory, one
     # every 4th block), memory 8 heads x key 64 (value 128, forced by
-    # d_model * expand = heads * value_dim), vocab 50304.
-    "60m": Mamba4Config(),
+    # d_model * expand = heads * value_dim), vocab 50304; Mamba-3 state 96
+    # as the reference 60M model (lm/configs/mamba4-60m.json:10).
+    "60m": Mamba4Config(d_state=96),
     # d_model 768, 17 Mamba-3 + 4 memory layers
-    # (pattern of lm/configs/mamba4-125m.json), memory 12 heads x 128.
-    "125m": Mamba4Config(d_model=768, layer_pattern="SSSMSSSSMSSSSMSSSSMSS"),
+    # (pattern of lm/configs/mamba4-125m.json), memory 12 heads x 128,
+    # Mamba-3 state 128 (lm/configs/mamba4-125m.json:10).
+    "125m": Mamba4Config(d_model=768, layer_pattern="SSSMSSSSMSSSSMSSSSMSS", d_state=128),
 }
 
 
@@ -136,7 +138,7 @@ class Mamba3Mixer(nn.Module):
         with torch.autocast("cuda", enabled=False):
             y = mamba_mixer_core(proj.to(torch.bfloat16), self.B_norm.scale, self.C_norm.scale, self.dt_bias,
                                  self.D, self.C_bias, self.B_bias, inner=cfg.inner, heads=cfg.num_heads,
-                                 angles=self.angles, eps=cfg.norm_eps)
+                                 angles=self.angles, eps=cfg.norm_eps, state=cfg.d_state)
         return self.out_proj(y)
 
     def init_cache(self, batch, device=None):
@@ -155,7 +157,7 @@ class Mamba3Mixer(nn.Module):
             out, cache = mamba_mixer_step(proj.to(torch.bfloat16), self.B_norm.scale, self.C_norm.scale,
                                           self.dt_bias, self.D, self.C_bias, self.B_bias, cache,
                                           inner=cfg.inner, heads=cfg.num_heads, angles=self.angles,
-                                          eps=cfg.norm_eps, inplace=inplace)
+                                          eps=cfg.norm_eps, inplace=inplace, state=cfg.d_state)
         return self.out_proj(out), cache
 
 

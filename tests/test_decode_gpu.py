@@ -120,16 +120,17 @@ def _scan_inputs(batch, time, heads, state_dim, head_dim, seed):
 KEYS = ("c", "b", "x", "adt", "dt", "trap_logits", "angles")
 
 
-def test_scan_step_float32_reproduces_mamba3_fused():
+@pytest.mark.parametrize("state_dim", [64, 128])
+def test_scan_step_float32_reproduces_mamba3_fused(state_dim):
     from mamba4_b200 import mamba3_fused, mamba3_step, mamba3_step_cache
 
     batch, time, heads = 2, 70, 3
-    sc = _scan_inputs(batch, time, heads, 64, 64, seed=5)
+    sc = _scan_inputs(batch, time, heads, 64, state_dim, seed=5)
     t = lambda a: torch.tensor(a, device=DEV)  # noqa: E731
     args = [t(sc[n]) for n in KEYS]
     qb, kb = t(sc["q_bias"]), t(sc["k_bias"])
     y_full, final = mamba3_fused(*args, q_bias=qb, k_bias=kb)
-    cache = mamba3_step_cache(batch, heads, 64, 64, sc["angles"].shape[-1], device=DEV)
+    cache = mamba3_step_cache(batch, heads, state_dim, 64, sc["angles"].shape[-1], device=DEV)
     ys = []
     for i in range(time):
         y, cache = mamba3_step(cache, *[a[:, i] for a in args], q_bias=qb, k_bias=kb)
@@ -140,7 +141,7 @@ def test_scan_step_float32_reproduces_mamba3_fused():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("state_dim,head_dim", [(64, 64), (16, 8)])
+@pytest.mark.parametrize("state_dim,head_dim", [(64, 64), (16, 8), (96, 64), (128, 64)])
 def test_scan_step_matches_oracle(dtype, state_dim, head_dim):
     from mamba4_b200 import Mamba3StepCache, mamba3_step
 

@@ -53,7 +53,8 @@ def heavy_tail(x):
 def composite_core64(proj, bs, cs, dtb, D, qb, kb, inner, heads, angles, eps):
     """Mamba-3 mixer glue (`lm/models/mamba3.py:74-117`) in float64 around the
     rounding-point scan oracle; bf16 rounding at the B/C norms and output."""
-    z, x, b, c, raw_dt, raw_a, trap, ang = torch.split(proj, (inner, inner, 64, 64, heads, heads, heads, angles), -1)
+    n = bs.shape[0]
+    z, x, b, c, raw_dt, raw_a, trap, ang = torch.split(proj, (inner, inner, n, n, heads, heads, heads, angles), -1)
 
     def rms(v, scale):
         return bf16_round(v * torch.rsqrt(v.square().mean(-1, keepdim=True) + eps) * scale)
@@ -66,22 +67,23 @@ def composite_core64(proj, bs, cs, dtb, D, qb, kb, inner, heads, angles, eps):
     return bf16_round(y * F.silu(z))
 
 
-@pytest.mark.parametrize("batch,time", [(2, 160), (1, 64)])
-def test_mixer_core_matches_composition(batch, time):
+@pytest.mark.parametrize("batch,time,state", [(2, 160, 64), (1, 64, 64), (2, 100, 96), (1, 130, 128)])
+def test_mixer_core_matches_composition(batch, time, state):
     torch.manual_seed(0)
-    inner, heads, angles, eps = 256, 4, 16, 1e-5  # row width 668: padded to 672 by the wrapper
-    width = 2 * inner + 128 + 3 * heads + angles
+    inner, heads, angles, eps = 256, 4, state // 4, 1e-5  # row width 668 at N = 64: padded to 672
+    width = 2 * inner + 2 * state + 3 * heads + angles
     dev = "cuda"
     proj = torch.randn(batch, time, width, device=dev)
-    proj[..., 2 * inner + 128: 2 * inner + 128 + heads] -= 3.0  # dt around softplus(-3)
+    proj[..., 2 * inner + 2 * state: 2 * inner + 2 * state + heads] -= 3.0  # dt around softplus(-3)
     proj = proj.to(torch.bfloat16)
-    params = [torch.rand(64, device=dev) + 0.5, torch.rand(64, device=dev) + 0.5,
+    params = [torch.rand(state, device=dev) + 0.5, torch.rand(state, device=dev) + 0.5,
               torch.randn(heads, device=dev) - 2.0, torch.randn(heads, device=dev),
-              torch.randn(heads, 1, 64, device=dev) * 0.5 + 1.0, torch.randn(heads, 1, 64, device=dev) * 0.5 + 1.0]
+              torch.randn(heads, 1, state, device=dev) * 0.5 + 1.0,
+              torch.randn(heads, 1, state, device=dev) * 0.5 + 1.0]
     g = torch.randn(batch, time, inner, device=dev).to(torch.bfloat16)
     p = proj.clone().requires_grad_()
     ps = [t.clone().requires_grad_() for t in params]
-    out_f = mamba_mixer_core(p, *ps, inner=inner, heads=heads, angles=angles, eps=eps)
+    out_f = mamba_mixer_core(p, *ps, inner=inner, heads=heads, angles=angles, eps=eps, state=state)
     g_f = torch.autograd.grad(out_f, [p, *ps], g)
     p64 = proj.to(F64).cpu().requires_grad_()
     ps64 = [t.to(F64).cpu().requires_grad_() for t in params]

@@ -38,8 +38,8 @@ def rel_fro(actual, expected):
     return float((a - e).norm() / max(float(e.norm()), 1e-30))
 
 
-def make(batch, time, heads, angle_count, seed, random_bias=True):
-    cfg = S.config_inputs(batch, time, heads, 64, 64, seed=seed)
+def make(batch, time, heads, angle_count, seed, random_bias=True, state_dim=64):
+    cfg = S.config_inputs(batch, time, heads, 64, state_dim, seed=seed)
     cfg["angles"] = cfg["angles"][..., :angle_count].copy()
     rng = np.random.default_rng(seed + 7)
     if random_bias:
@@ -118,6 +118,42 @@ def test_scan_bf16_ragged_lengths_and_angle_counts(time, angle_count):
     for name, g, e in zip(NAMES, grads, eg):
         if e.numel() == 0:
             continue
+        close(g, e, 2e-2, name)
+        assert rel_fro(g, e) < 5e-3, (name, rel_fro(g, e))
+
+
+@pytest.mark.parametrize("state_dim, time, angle_count", [(96, 130, 24), (128, 100, 64), (128, 64, 32)])
+def test_scan_fp32_reference_state_dims_match_oracle(state_dim, time, angle_count):
+    # The reference models' state dims: 96 (lm/configs/mamba4-60m.json:10) and
+    # 128 (lm/configs/mamba4-125m.json:10); same bars as N = 64.
+    cfg = make(2, time, 3, angle_count, seed=state_dim + time, state_dim=state_dim)
+    y, final, grads = run_cuda(cfg, torch.float32)
+    args = [torch.tensor(cfg[n], dtype=torch.float64) for n in NAMES]
+    ey, ef = S.fused_layout_scan(*args, chunk=64)
+    close(y, ey, 1e-4, "y")
+    close(final, ef, 1e-4, "final")
+    eg = S.fused_layout_grads([cfg[n] for n in NAMES], cfg["d_y"], cfg["d_final"], chunk=64)
+    for name, g, e in zip(NAMES, grads, eg):
+        close(g, e, 1e-3, name)
+
+
+@pytest.mark.parametrize("state_dim, time, angle_count", [(96, 200, 24), (128, 130, 32), (128, 64, 64)])
+def test_scan_bf16_reference_state_dims_match_oracle(state_dim, time, angle_count):
+    # bf16 at N = 96 / 128 against the rounding-point oracle, same bars as N = 64.
+    cfg = make(2, time, 4, angle_count, seed=state_dim + time + 1, state_dim=state_dim)
+    y, final, grads = run_cuda(cfg, torch.bfloat16)
+    args = [torch.tensor(cfg[n], dtype=torch.float32) for n in NAMES]
+    for i in range(3):
+        args[i] = args[i].to(torch.bfloat16).float()
+    ey, ef = S.fused_layout_scan(*args, chunk=64, model_dtype=torch.bfloat16,
+                                 compute_dtype=torch.float32)
+    close(y, ey, 2e-2, "y")
+    assert rel_fro(y, ey) < 5e-3
+    close(final, ef, 2e-2, "final")
+    assert rel_fro(final, ef) < 5e-3
+    eg = S.fused_layout_grads_emulated(args, cfg["d_y"], cfg["d_final"], chunk=64,
+                                       model_dtype=torch.bfloat16)
+    for name, g, e in zip(NAMES, grads, eg):
         close(g, e, 2e-2, name)
         assert rel_fro(g, e) < 5e-3, (name, rel_fro(g, e))
 
