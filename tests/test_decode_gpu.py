@@ -125,7 +125,7 @@ def test_scan_step_float32_reproduces_mamba3_fused(state_dim):
     from mamba4_b200 import mamba3_fused, mamba3_step, mamba3_step_cache
 
     batch, time, heads = 2, 70, 3
-    sc = _scan_inputs(batch, time, heads, 64, state_dim, seed=5)
+    sc = _scan_inputs(batch, time, heads, state_dim, 64, seed=5)
     t = lambda a: torch.tensor(a, device=DEV)  # noqa: E731
     args = [t(sc[n]) for n in KEYS]
     qb, kb = t(sc["q_bias"]), t(sc["k_bias"])
