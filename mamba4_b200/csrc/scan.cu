@@ -709,9 +709,9 @@ __global__ void bias_kernel(Dims d, const float* __restrict__ dqb, const float* 
   if (d_kb) d_kb[idx] = sk;
 }
 
-// bf16 operands at state dim 64 run the chunk-parallel tensor-core kernels of
-// scan_bf16.cuh; every other case the sequential kernels above.
-inline bool fast_path(const M4ScanDims& s) { return s.bf16 && s.state_dim == 64; }
+// bf16 operands at state dim 64 or 128 run the chunk-parallel tensor-core
+// kernels of scan_bf16.cuh; every other case the sequential kernels above.
+inline bool fast_path(const M4ScanDims& s) { return s.bf16 && (s.state_dim == 64 || s.state_dim == 128); }
 
 struct Layout {
   size_t starts, phases, deltas, resid;
@@ -892,7 +892,8 @@ inline bool encode_tokens_map(CUtensorMap* map, const void* base, int B, int T, 
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// bfloat16 operands run the chunk-parallel kernels of scan_bf16.cuh.
+// bfloat16 operands at state dim 64 or 128 run the chunk-parallel kernels of
+// scan_bf16.cuh (templated on the number of 64-row state halves).
 inline scan2::Dims make_dims2(const M4ScanDims& s) {
   scan2::Dims d;
   d.B = s.batch; d.T = s.time; d.H = s.heads; d.A = s.angle_count;
@@ -906,9 +907,10 @@ inline void allow_smem(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
 }
 
-inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
-                        const float* dt, const float* trap, const float* angles, const float* qb,
-                        const float* kb, void* y, float* fin, char* resid, cudaStream_t st) {
+template <int NH>
+inline int forward_bf16_nh(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                           const float* dt, const float* trap, const float* angles, const float* qb,
+                           const float* kb, void* y, float* fin, char* resid, cudaStream_t st) {
   using namespace scan2;
   const scan2::Dims d = make_dims2(s);
   const Layout l = layout(s);
@@ -920,17 +922,25 @@ inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const
   alignas(64) CUtensorMap xmap;
   if (!all_aligned16(c, b, x)) return M4_ERR_ALIGN;  // 16-byte row copies and the TMA box
   if (!encode_tokens_map(&xmap, x, d.B, d.T, d.H * P)) return M4_ERR_LAUNCH;
-  allow_smem(fused_fwd_kernel, sizeof(FusedSmem) + 1024);
-  fused_fwd_kernel<<<d.B * d.H, GW * 32, sizeof(FusedSmem) + 1024, st>>>(
+  allow_smem(fused_fwd_kernel<NH>, sizeof(FusedSmem<NH>) + 1024);
+  fused_fwd_kernel<NH><<<d.B * d.H, GW * 32, sizeof(FusedSmem<NH>) + 1024, st>>>(
       d, xmap, cq, bk, adt, dt, trap, angles, qb, kb, static_cast<bf16*>(y), starts, phases, deltas, fin);
   return launch_status();
 }
 
-inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
-                         const float* dt, const float* trap, const float* angles, const float* qb,
-                         const float* kb, const char* resid, const void* dy, const float* d_final, void* dc,
-                         void* db, void* dx, float* d_adt, float* d_dt, float* d_trap, float* d_angles,
-                         float* d_qb, float* d_kb, char* work, cudaStream_t st) {
+inline int forward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                        const float* dt, const float* trap, const float* angles, const float* qb,
+                        const float* kb, void* y, float* fin, char* resid, cudaStream_t st) {
+  if (s.state_dim == 128) return forward_bf16_nh<2>(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
+  return forward_bf16_nh<1>(s, c, b, x, adt, dt, trap, angles, qb, kb, y, fin, resid, st);
+}
+
+template <int NH>
+inline int backward_bf16_nh(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                            const float* dt, const float* trap, const float* angles, const float* qb,
+                            const float* kb, const char* resid, const void* dy, const float* d_final, void* dc,
+                            void* db, void* dx, float* d_adt, float* d_dt, float* d_trap, float* d_angles,
+                            float* d_qb, float* d_kb, char* work, cudaStream_t st) {
   using namespace scan2;
   if (!all_aligned16(c, b, x, dy)) return M4_ERR_ALIGN;  // 16-byte tile copies
   const scan2::Dims d = make_dims2(s);
@@ -955,18 +965,33 @@ inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, cons
   const bf16* xx = static_cast<const bf16*>(x);
   const bf16* g = static_cast<const bf16*>(dy);
   const int bh = d.B * d.H, chunks = bh * d.nch;
-  allow_smem(dstart_kernel, sizeof(DsSmem) + 1024);
-  dstart_kernel<<<chunks, GW * 32, sizeof(DsSmem) + 1024, st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
-  carry_kernel<<<bh * SPARTS, 256, 0, st>>>(d, carries, deltas, d_final);
-  allow_smem(grads_kernel, sizeof(GradSmem));
-  grads_kernel<<<chunks, GW * 32, sizeof(GradSmem), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb, phases,
-                                                      starts, carries, g, static_cast<bf16*>(dx), o);
-  later_kernel<<<bh, 32, 0, st>>>(d, o.dth);
+  allow_smem(dstart_kernel<NH>, sizeof(DsSmem<NH>) + 1024);
+  dstart_kernel<NH><<<chunks, GW * 32, sizeof(DsSmem<NH>) + 1024, st>>>(d, cq, g, adt, dt, trap, angles, qb, phases,
+                                                                        carries);
+  carry_kernel<NH><<<bh * sparts<NH>(), 256, 0, st>>>(d, carries, deltas, d_final);
+  allow_smem(grads_kernel<NH>, sizeof(GradSmem<NH>));
+  grads_kernel<NH><<<chunks, GW * 32, sizeof(GradSmem<NH>), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb,
+                                                                  phases, starts, carries, g,
+                                                                  static_cast<bf16*>(dx), o);
+  later_kernel<NH><<<bh, Geo<NH>::NP, 0, st>>>(d, o.dth);
   const size_t tokens = size_t(d.B) * d.T;
-  finish_kernel<<<unsigned((tokens + 7) / 8), 256, 0, st>>>(d, dt, trap, angles, o.dth, o, static_cast<bf16*>(dc),
-                                                          static_cast<bf16*>(db), d_adt, d_dt, d_trap, d_angles);
-  if (d_qb || d_kb) scan2::bias_kernel<<<s.heads, 1024, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
+  finish_kernel<NH><<<unsigned((tokens + 7) / 8), 256, 0, st>>>(d, dt, trap, angles, o.dth, o,
+                                                                static_cast<bf16*>(dc), static_cast<bf16*>(db),
+                                                                d_adt, d_dt, d_trap, d_angles);
+  if (d_qb || d_kb) scan2::bias_kernel<NH><<<s.heads, 1024, 0, st>>>(d, o.dqb, o.dkb, d_qb, d_kb);
   return launch_status();
+}
+
+inline int backward_bf16(const M4ScanDims& s, const void* c, const void* b, const void* x, const float* adt,
+                         const float* dt, const float* trap, const float* angles, const float* qb,
+                         const float* kb, const char* resid, const void* dy, const float* d_final, void* dc,
+                         void* db, void* dx, float* d_adt, float* d_dt, float* d_trap, float* d_angles,
+                         float* d_qb, float* d_kb, char* work, cudaStream_t st) {
+  if (s.state_dim == 128)
+    return backward_bf16_nh<2>(s, c, b, x, adt, dt, trap, angles, qb, kb, resid, dy, d_final, dc, db, dx, d_adt,
+                               d_dt, d_trap, d_angles, d_qb, d_kb, work, st);
+  return backward_bf16_nh<1>(s, c, b, x, adt, dt, trap, angles, qb, kb, resid, dy, d_final, dc, db, dx, d_adt,
+                             d_dt, d_trap, d_angles, d_qb, d_kb, work, st);
 }
 
 }  // namespace scan

@@ -16,6 +16,10 @@
 // Chunk products: tcgen05 (tensor memory accumulators, swizzled shared-memory
 // operands) in the forward and dstart; bf16 tiles with ldmatrix fragments and
 // m16n8k16 mma.sync in grads_kernel; fp32 accumulation everywhere.
+// Every kernel is templated on NH, the number of 64-row halves of the state
+// (N = 64 or 128): contractions over the state accumulate the halves' products
+// in one accumulator, products with state-row outputs get one M = 64
+// accumulator per half.
 #pragma once
 
 #include "tc05.cuh"
@@ -25,9 +29,15 @@ namespace scan2 {
 
 using bf16 = __nv_bfloat16;
 constexpr int C = 64;        // chunk
-constexpr int N = 64;        // state dim
 constexpr int P = 64;        // head dim
 constexpr int TS = 72;       // bf16 tile stride (144 B rows: ldmatrix conflict-free)
+// State dim N = 64 NH (NH = 1 or 2 halves of 64 state rows): pairs NP = N / 2,
+// [C][N] bf16 tiles of the chunk-gradient kernel with row stride TSN
+// (272-byte rows at N = 128: ldmatrix conflict-free), [C][pairs] fp32 tables
+// with row stride TW.
+template <int NH> struct Geo {
+  static constexpr int N = 64 * NH, NP = 32 * NH, TSN = N + 8, TW = NP + 1;
+};
 constexpr int FS = 68;       // fp32 tile stride
 constexpr int GW = 8;        // warps per chunk CTA (4 row blocks x 2 column halves)
 static_assert(C == 64 && (C % (4 * GW)) == 0, "warp/token maps assume 64-token chunks");
@@ -58,23 +68,23 @@ M4_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_
 // (g = lane/4, c = lane%4) over K (multiple of 16), NT (even) n-tiles.
 // A is row-major [m][k] (AT = false) or stored transposed [k][m] (AT = true);
 // B is [n][k] (BT = false) or [k][n] (BT = true). Strides in elements.
-template <int K, int NT, bool AT, bool BT>
+template <int K, int NT, bool AT, bool BT, int SA = TS, int SB = TS>
 M4_DEV void mma_tile(float (&acc)[NT][4], const bf16* A, int row0, const bf16* B, int col0) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k0 = 0; k0 < K; k0 += 16) {
     uint32_t a[4];
     if constexpr (!AT)
-      ldsm_x4(a, A + (row0 + (lane & 15)) * TS + k0 + 8 * (lane >> 4));
+      ldsm_x4(a, A + (row0 + (lane & 15)) * SA + k0 + 8 * (lane >> 4));
     else
-      ldsm_x4_t(a, A + (k0 + (lane & 7) + 8 * (lane >> 4)) * TS + row0 + 8 * ((lane >> 3) & 1));
+      ldsm_x4_t(a, A + (k0 + (lane & 7) + 8 * (lane >> 4)) * SA + row0 + 8 * ((lane >> 3) & 1));
 #pragma unroll
     for (int nt = 0; nt < NT; nt += 2) {
       uint32_t b[4];
       if constexpr (!BT)
-        ldsm_x4(b, B + (col0 + nt * 8 + (lane & 7) + 8 * (lane >> 4)) * TS + k0 + 8 * ((lane >> 3) & 1));
+        ldsm_x4(b, B + (col0 + nt * 8 + (lane & 7) + 8 * (lane >> 4)) * SB + k0 + 8 * ((lane >> 3) & 1));
       else
-        ldsm_x4_t(b, B + (k0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * TS + col0 + nt * 8 + 8 * (lane >> 4));
+        ldsm_x4_t(b, B + (k0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * SB + col0 + nt * 8 + 8 * (lane >> 4));
       mma_bf16(acc[nt], a, b[0], b[1]);
       mma_bf16(acc[nt + 1], a, b[2], b[3]);
     }
@@ -89,10 +99,11 @@ M4_DEV bf16* at(bf16* T, int r, int c) {
   else return T + r * TS + c;
 }
 
-// D (tensor memory) = A B over K = 64 on the tensor cores (tcgen05, 4 MMAs of
-// K = 16), issued by one thread. A is M x K, B is K x N, each a swizzled tile
-// read K-major (K along its contiguous columns) or MN-major (K along its rows).
-M4_DEV void tc_product(uint32_t d, const bf16* A, bool a_mn, const bf16* B, bool b_mn) {
+// D (tensor memory) = A B (+ D when `accumulate`) over K = 64 on the tensor
+// cores (tcgen05, 4 MMAs of K = 16), issued by one thread. A is M x K, B is
+// K x N, each a swizzled tile read K-major (K along its contiguous columns)
+// or MN-major (K along its rows).
+M4_DEV void tc_product(uint32_t d, const bf16* A, bool a_mn, const bf16* B, bool b_mn, bool accumulate = false) {
   const uint32_t id = tc::idesc_bf16(64, 64, a_mn ? 1 : 0, b_mn ? 1 : 0);
   const unsigned char* a = reinterpret_cast<const unsigned char*>(A);
   const unsigned char* b = reinterpret_cast<const unsigned char*>(B);
@@ -100,7 +111,7 @@ M4_DEV void tc_product(uint32_t d, const bf16* A, bool a_mn, const bf16* B, bool
   for (int ks = 0; ks < 4; ++ks) {
     const uint64_t ad = a_mn ? tc::sdesc_sw128(a + 2048 * ks, 8192, 1024) : tc::sdesc_sw128(a + 32 * ks, 16, 1024);
     const uint64_t bd = b_mn ? tc::sdesc_sw128(b + 2048 * ks, 8192, 1024) : tc::sdesc_sw128(b + 32 * ks, 16, 1024);
-    tc::mma_bf16(d, ad, bd, id, ks > 0);
+    tc::mma_bf16(d, ad, bd, id, accumulate || ks > 0);
   }
 }
 
@@ -181,7 +192,7 @@ struct Dims {
 // Per-token scalars of one chunk of (b, h) (threads 0..63 + warp 0 prefix).
 struct Rows {
   float p[C], gam[C], scl[C], tail[C], dt[C], ept[C];
-  float seg[8 * 32];  // per-segment totals of the in-chunk scans (one segment per warp)
+  float seg[8 * 64];  // per-segment totals of the in-chunk scans (one segment per warp, NP pairs)
 };
 
 M4_DEV float rate_at(const Dims& d, const float* angles, int b, int h, int t, int i) {
@@ -197,8 +208,8 @@ M4_DEV float hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 // Forward
 // ---------------------------------------------------------------------------
 
-// Four CTAs per (b, h) in the chunk-carry pass of the backward.
-constexpr int SPARTS = 4;
+// CTAs per (b, h) in the chunk-carry pass of the backward (1,024 floats each).
+template <int NH> constexpr int sparts() { return 4 * NH; }
 
 // ---------------------------------------------------------------------------
 // Persistent forward: one CTA (8 warps) per (batch, head) walks the chunks in
@@ -219,37 +230,42 @@ constexpr int SPARTS = 4;
 // Raw inputs of one chunk, prefetched (cp.async) while the previous chunk's
 // tensor-core phases run; tokens past T arrive as zeros. dt and trap hold
 // token t0 + 64 too (the trapezoid's next-token term).
+template <int NH>
 struct FusedStage {
+  static constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP;
   bf16 c[C * N];       // rows of c (queries) and b (keys), row-major
   bf16 b[C * N];
-  float ang[C * 32];   // angle rates [token][pair]
+  float ang[C * NP];   // angle rates [token][pair]
   float adt[C];
   float dt[C + 4];
   float trap[C + 4];
 };
 
+template <int NH>
 struct FusedSmem {
-  bf16 Qs[C * N];      // 128-byte-swizzled tiles on 1024-byte boundaries
-  bf16 Ks[C * N];
+  static constexpr int TW = Geo<NH>::TW, NP = Geo<NH>::NP;
+  bf16 Qs[NH][C * 64]; // 128-byte-swizzled 64-column tiles on 1024-byte boundaries
+  bf16 Ks[NH][C * 64];
   bf16 Vs[2][C * P];   // x tiles (TMA, double buffered)
   bf16 Vw[C * P];      // rd(V o scale o tail)
   bf16 Ms[C * C];      // masked scores
-  bf16 Ss[N * P];      // rd(S_n)
-  float theta[C * 33];
-  float sinv[C * 33];
+  bf16 Ss[NH][64 * P]; // rd(S_n), 64 state rows per tile
+  float theta[C * TW];
+  float sinv[C * TW];
   float scratch[C];
-  float phase[32];     // phase at the current chunk start
+  float phase[NP];     // phase at the current chunk start
   Rows r;
-  FusedStage in;       // the current chunk's raw inputs
+  FusedStage<NH> in;   // the current chunk's raw inputs
   uint64_t bar;        // tensor-core commits (two per chunk)
   uint64_t bar_x[2];   // TMA of the x tiles
   uint32_t tmem;
 };
 
 // Where a kernel stages one chunk's raw inputs (cp.async, tokens past T as
-// zeros): c / b rows (bf16, row-major with `stride` elements, or 128-byte
-// swizzled when SW), angle rates [token][32], adt [64], dt / trap [65] (token
-// t0 + 64 too, for the trapezoid's next-token term). Either c or b may be null.
+// zeros): c / b rows (bf16, row-major with `stride` elements, or in 128-byte
+// swizzled 64-column tiles when SW), angle rates [token][NP], adt [64],
+// dt / trap [65] (token t0 + 64 too, for the trapezoid's next-token term).
+// Either c or b may be null.
 struct StageRef {
   bf16* c;
   bf16* b;
@@ -260,20 +276,24 @@ struct StageRef {
   float* trap;
 };
 
+// Element (r, c) of a staged [C][N] row block: row-major with `stride`, or
+// column c of the swizzled 64-column tile c / 64.
 template <bool SW>
 M4_DEV bf16* stage_row(bf16* base, int stride, int r, int c) {
-  if constexpr (SW) return at<true>(base, r, c);
+  if constexpr (SW) return at<true>(base + (c >> 6) * (C * 64), r, c & 63);
   else return base + r * stride + c;
 }
 
 // Start copying chunk n's raw inputs (one commit group per thread).
-template <bool SW>
+template <bool SW, int NH>
 M4_DEV void stage_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, const bf16* bk, const float* adt,
                            const float* dt, const float* trap_logits, const float* angles, const StageRef& in) {
+  constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP, PIECES = N / 8;
   const int tid = threadIdx.x, t0 = n * C;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {  // 2 tiles x 64 rows x 8 16-byte pieces over 256 threads
-    const int idx = tid + k * GW * 32, which = idx >> 9, rr = (idx >> 3) & 63, c8 = 8 * (idx & 7);
+  for (int k = 0; k < 4 * NH; ++k) {  // 2 tiles x 64 rows x N/8 16-byte pieces over 256 threads
+    const int idx = tid + k * GW * 32, which = idx / (C * PIECES), rr = (idx / PIECES) % C;
+    const int c8 = 8 * (idx % PIECES);
     bf16* dst = which ? in.b : in.c;
     if (dst == nullptr) continue;
     const int t = t0 + rr;
@@ -287,7 +307,7 @@ M4_DEV void stage_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, c
     const int tt = idx / d.A, i = idx % d.A, t = t0 + tt;
     const bool live = t < d.T;
     const size_t o = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * d.A + i : (size_t(b) * d.T + t) * d.A + i;
-    cp4(&in.ang[tt * 32 + i], live ? angles + o : angles, live);
+    cp4(&in.ang[tt * NP + i], live ? angles + o : angles, live);
   }
   if (tid < 3 * (C + 1)) {
     const int which = tid / (C + 1), tt = tid % (C + 1), t = t0 + tt;
@@ -328,71 +348,97 @@ M4_DEV void stage_rows(const Dims& d, int t0, const StageRef& in, Rows& r, float
   }
 }
 
-// chunk_theta from the stage (same segment scheme).
+// chunk_theta from the stage (same segment scheme): lanes over the pairs
+// lane + 32 q (q < NH).
+template <int NH>
 M4_DEV void stage_theta(const Dims& d, const StageRef& in, Rows& r, const float* phase0, float* cosv, float* sinv) {
-  constexpr int SEG = C / GW;
-  const int i = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float acc = 0.f;
-  if (i < d.A) {
+  constexpr int SEG = C / GW, NP = Geo<NH>::NP, TW = Geo<NH>::TW;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
+  for (int q = 0; q < NH; ++q) {
+    const int i = lane + 32 * q;
+    float acc = 0.f;
+    if (i < d.A) {
+#pragma unroll
+      for (int j = 0; j < SEG; ++j) {
+        const int tt = SEG * w + j;
+        acc = fmaf(in.ang[tt * NP + i], r.dt[tt], acc);
+        cosv[tt * TW + i] = acc;
+      }
+    }
+    r.seg[w * NP + i] = acc;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < NH; ++q) {
+    const int i = lane + 32 * q;
+    float off = 0.f;
+    if (i < d.A) {
+      off = phase0[i];
+      for (int v = 0; v < w; ++v) off += r.seg[v * NP + i];
+    }
+#pragma unroll 1
     for (int j = 0; j < SEG; ++j) {
-      const int tt = SEG * w + j;
-      acc = fmaf(in.ang[tt * 32 + i], r.dt[tt], acc);
-      cosv[tt * 33 + i] = acc;
+      const int e = (SEG * w + j) * TW + i;
+      float cs = 1.f, sn = 0.f;
+      if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
+      cosv[e] = cs;
+      sinv[e] = sn;
     }
   }
-  r.seg[w * 32 + i] = acc;
-  __syncthreads();
-  float off = 0.f;
-  if (i < d.A) {
-    off = phase0[i];
-    for (int v = 0; v < w; ++v) off += r.seg[v * 32 + i];
-  }
-#pragma unroll 1
-  for (int j = 0; j < SEG; ++j) {
-    const int e = (SEG * w + j) * 33 + i;
-    float cs = 1.f, sn = 0.f;
-    if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
-    cosv[e] = cs;
-    sinv[e] = sn;
-  }
+}
+
+// Destination element (r, c) of a rotated Q / K tile: 128-byte-swizzled
+// 64-column tiles (DST_SW) or row-major rows of `stride` elements.
+template <bool SW>
+M4_DEV bf16* qk_at(bf16* T, int stride, int r, int c) {
+  if constexpr (SW) return at<true>(T + (c >> 6) * (C * 64), r, c & 63);
+  else return T + r * stride + c;
 }
 
 // build_qk from the stage: rotated, rounded Q / K tiles (either may be null);
 // a stage may be the destination tile itself (each thread reads and writes
-// the same pair).
-template <bool SRC_SW, bool DST_SW>
+// the same pair). Lane l handles the pairs l + 32 q (columns 2 l + 64 q).
+template <bool SRC_SW, bool DST_SW, int NH>
 M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb, const float* cosv,
-                     const float* sinv, bf16* Qs, bf16* Ks) {
-  constexpr int PER = C / GW;
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, n0 = 2 * lane;
-  const float qb0 = qb ? qb[h * N + n0] : 0.f, qb1 = qb ? qb[h * N + n0 + 1] : 0.f;
-  const float kb0 = kb ? kb[h * N + n0] : 0.f, kb1 = kb ? kb[h * N + n0 + 1] : 0.f;
+                     const float* sinv, bf16* Qs, bf16* Ks, int dst_stride = 0) {
+  constexpr int PER = C / GW, N = Geo<NH>::N, TW = Geo<NH>::TW;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
-  for (int k = 0; k < PER; ++k) {
-    const int tt = w + GW * k;
-    const float cs = cosv[tt * 33 + lane], sn = sinv[tt * 33 + lane];
-    if (Qs) {
-      const uint32_t cr = ld_u32(stage_row<SRC_SW>(in.c, in.stride, tt, n0));
-      const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
-      *reinterpret_cast<__nv_bfloat162*>(at<DST_SW>(Qs, tt, n0)) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
-    }
-    if (Ks) {
-      const uint32_t br = ld_u32(stage_row<SRC_SW>(in.b, in.stride, tt, n0));
-      const float k0 = round_to<bf16>(lo_f(br) + kb0), k1 = round_to<bf16>(hi_f(br) + kb1);
-      *reinterpret_cast<__nv_bfloat162*>(at<DST_SW>(Ks, tt, n0)) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+  for (int q = 0; q < NH; ++q) {
+    const int n0 = 2 * lane + 64 * q, i = lane + 32 * q;
+    const float qb0 = qb ? qb[h * N + n0] : 0.f, qb1 = qb ? qb[h * N + n0 + 1] : 0.f;
+    const float kb0 = kb ? kb[h * N + n0] : 0.f, kb1 = kb ? kb[h * N + n0 + 1] : 0.f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int tt = w + GW * k;
+      const float cs = cosv[tt * TW + i], sn = sinv[tt * TW + i];
+      if (Qs) {
+        const uint32_t cr = ld_u32(stage_row<SRC_SW>(in.c, in.stride, tt, n0));
+        const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
+        *reinterpret_cast<__nv_bfloat162*>(qk_at<DST_SW>(Qs, dst_stride, tt, n0)) =
+            __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
+      }
+      if (Ks) {
+        const uint32_t br = ld_u32(stage_row<SRC_SW>(in.b, in.stride, tt, n0));
+        const float k0 = round_to<bf16>(lo_f(br) + kb0), k1 = round_to<bf16>(hi_f(br) + kb1);
+        *reinterpret_cast<__nv_bfloat162*>(qk_at<DST_SW>(Ks, dst_stride, tt, n0)) =
+            __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+      }
     }
   }
 }
 
-__global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
+template <int NH>
+__global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
     Dims d, const __grid_constant__ CUtensorMap tmap_x, const bf16* __restrict__ cq, const bf16* __restrict__ bk,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
     bf16* __restrict__ y, float* __restrict__ starts, float* __restrict__ phases, float* __restrict__ deltas,
     float* __restrict__ final_state) {
+  constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP;
   extern __shared__ __align__(128) unsigned char raw[];
-  FusedSmem& s = *reinterpret_cast<FusedSmem*>(align1024(raw));
+  FusedSmem<NH>& s = *reinterpret_cast<FusedSmem<NH>*>(align1024(raw));
   const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
@@ -405,7 +451,7 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     tc::mbar_init(&s.bar_x[0], 1);
     tc::mbar_init(&s.bar_x[1], 1);
   }
-  if (tid < 32) s.phase[tid] = 0.f;
+  if (tid < NP) s.phase[tid] = 0.f;
   __syncthreads();
   tc::fence_after();
   const uint32_t tm = s.tmem;
@@ -414,10 +460,13 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     tc::tma_load_3d(s.Vs[0], &tmap_x, h * P, 0, b, &s.bar_x[0]);
   }
   const StageRef in{s.in.c, s.in.b, N, s.in.ang, s.in.adt, s.in.dt, s.in.trap};
-  stage_prefetch<false>(d, b, h, 0, cq, bk, adt, dt, trap_logits, angles, in);
-  float st[32];  // fp32 state S_n: row `row`, columns col0 .. col0 + 31 (lanes < 16)
+  stage_prefetch<false, NH>(d, b, h, 0, cq, bk, adt, dt, trap_logits, angles, in);
+  // fp32 state S_n: rows 64 q + `row` (q < NH), columns col0 .. col0 + 31 (lanes < 16)
+  float st[NH][32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) st[j] = 0.f;
+  for (int q = 0; q < NH; ++q)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) st[q][j] = 0.f;
   bool ok = true;
   for (int n = 0; n < d.nch; ++n) {
     const int t0 = n * C, buf = n & 1;
@@ -431,27 +480,31 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     __syncthreads();  // this chunk's stage has landed
     stage_rows(d, t0, in, s.r, s.scratch);
     __syncthreads();
-    stage_theta(d, in, s.r, s.phase, s.theta, s.sinv);
+    stage_theta<NH>(d, in, s.r, s.phase, s.theta, s.sinv);
     __syncthreads();
-    if (tid < 32) {
+    if (tid < NP) {
       float inc = 0.f;
 #pragma unroll
-      for (int w = 0; w < GW; ++w) inc += s.r.seg[w * 32 + tid];
-      phases[(size_t(bh) * d.nch + n) * 32 + tid] = s.phase[tid];
+      for (int w = 0; w < GW; ++w) inc += s.r.seg[w * NP + tid];
+      phases[(size_t(bh) * d.nch + n) * NP + tid] = s.phase[tid];
       s.phase[tid] += tid < d.A ? inc : 0.f;
     }
     if (tid < C) s.scratch[tid] = s.r.scl[tid] * s.r.tail[tid];
-    stage_qk<false, true>(h, in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+    stage_qk<false, true, NH>(h, in, qb, kb, s.theta, s.sinv, s.Qs[0], s.Ks[0]);
     if (lane < 16) {
-      float* dst = starts + (size_t(bh) * d.nch + n) * N * P + row * P + col0;
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[j], st[j + 1], st[j + 2], st[j + 3]));
+      for (int q = 0; q < NH; ++q) {
+        float* dst = starts + (size_t(bh) * d.nch + n) * N * P + (64 * q + row) * P + col0;
 #pragma unroll
-      for (int j = 0; j < 32; j += 2)
-        *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ss, row, col0 + j)) = __floats2bfloat162_rn(st[j], st[j + 1]);
+        for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[q][j], st[q][j + 1], st[q][j + 2], st[q][j + 3]));
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+          *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ss[q], row, col0 + j)) =
+              __floats2bfloat162_rn(st[q][j], st[q][j + 1]);
+      }
     }
     __syncthreads();  // scratch (scale o tail) visible; the stage is consumed
-    if (n + 1 < d.nch) stage_prefetch<false>(d, b, h, n + 1, cq, bk, adt, dt, trap_logits, angles, in);
+    if (n + 1 < d.nch) stage_prefetch<false, NH>(d, b, h, n + 1, cq, bk, adt, dt, trap_logits, angles, in);
     // rd(V o scale o tail) from the x tile once it has landed.
     if (!tc::mbar_wait(&s.bar_x[buf], (n >> 1) & 1, tc::WAIT_LIMIT)) {
       if (lane == 0) tc::flag_timeout();
@@ -476,9 +529,15 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     }
     tc_publish();
     if (tid == 0 && ok) {
-      tc_product(tm, s.Qs, false, s.Ks, false);        // Q K^T
-      tc_product(tm + 64, s.Qs, false, s.Ss, true);    // Q rd(S_n)
-      tc_product(tm + 128, s.Ks, true, s.Vw, true);    // K^T rd(V o scale o tail)
+      // The state-dim contractions accumulate over the halves; the update
+      // K^T rd(V o scale o tail) gets one accumulator per half (columns
+      // 128 + 64 q).
+#pragma unroll
+      for (int q = 0; q < NH; ++q) tc_product(tm, s.Qs[q], false, s.Ks[q], false, q > 0);       // Q K^T
+#pragma unroll
+      for (int q = 0; q < NH; ++q) tc_product(tm + 64, s.Qs[q], false, s.Ss[q], true, q > 0);   // Q rd(S_n)
+#pragma unroll
+      for (int q = 0; q < NH; ++q) tc_product(tm + 128 + 64 * q, s.Ks[q], true, s.Vw, true);    // K^T rd(V w)
       tc::commit(&s.bar);
     }
     ok = ok && tc_wait(&s.bar, 0);
@@ -516,13 +575,15 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
       // S_(n+1) = e^(p_L) S_n + U_n (the update finished with commit 1).
       const float dl = expf(s.r.p[C - 1]);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        float u[16];
-        tc::ld16(tmem_lane_base(tm) + 128 + col0 + 16 * j, u);
-        tc::wait_ld();
+      for (int q = 0; q < NH; ++q)
 #pragma unroll
-        for (int e = 0; e < 16; ++e) st[16 * j + e] = fmaf(dl, st[16 * j + e], u[e]);
-      }
+        for (int j = 0; j < 2; ++j) {
+          float u[16];
+          tc::ld16(tmem_lane_base(tm) + 128 + 64 * q + col0 + 16 * j, u);
+          tc::wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) st[q][16 * j + e] = fmaf(dl, st[q][16 * j + e], u[e]);
+        }
       if (tid == 0) deltas[size_t(bh) * d.nch + n] = dl;
     }
     ok = ok && tc_wait(&s.bar, 1);
@@ -557,9 +618,12 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     tc::fence_after();
   }
   if (lane < 16) {
-    float* dst = final_state + size_t(bh) * N * P + row * P + col0;
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[j], st[j + 1], st[j + 2], st[j + 3]));
+    for (int q = 0; q < NH; ++q) {
+      float* dst = final_state + size_t(bh) * N * P + (64 * q + row) * P + col0;
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[q][j], st[q][j + 1], st[q][j + 2], st[q][j + 3]));
+    }
   }
   // A TMA the loop no longer waits for cannot be in flight: the last chunk
   // issues none and every earlier one was awaited.
@@ -571,38 +635,43 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
+template <int NH>
 struct DsSmem {
-  bf16 Qs[C * N];  // blocked tiles (tcgen05 operands)
+  static constexpr int TW = Geo<NH>::TW, NP = Geo<NH>::NP;
+  bf16 Qs[NH][C * 64];  // blocked tiles (tcgen05 operands)
   bf16 Ds[C * P];
-  float theta[C * 33];
-  float sinv[C * 33];
+  float theta[C * TW];
+  float sinv[C * TW];
   float scratch[C];
-  float stg[3 * C + 8 + 32];  // staged gates and the chunk-start phase
+  float stg[3 * C + 8 + NP];  // staged gates and the chunk-start phase
   Rows r;
   uint64_t bar;
   uint32_t tmem;
 };
 
-// D_n = Q^T rd(dY o e^p) into carries[n], on the tensor cores (tcgen05).
+// D_n = Q^T rd(dY o e^p) into carries[n], on the tensor cores (tcgen05):
+// one M = 64 product per half of the state rows.
+template <int NH>
 __global__ void __launch_bounds__(GW * 32) dstart_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ dy, const float* __restrict__ adt,
     const float* __restrict__ dt, const float* __restrict__ trap_logits, const float* __restrict__ angles,
     const float* __restrict__ qb, const float* __restrict__ phases, float* __restrict__ carries) {
+  constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP;
   extern __shared__ __align__(128) unsigned char raw[];
-  DsSmem& s = *reinterpret_cast<DsSmem*>(align1024(raw));
+  DsSmem<NH>& s = *reinterpret_cast<DsSmem<NH>*>(align1024(raw));
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
-    tc::tmem_alloc(&s.tmem, 64);
+    tc::tmem_alloc(&s.tmem, 64 * NH);
     tc::tmem_relinquish();  // this CTA allocates once; others on the SM may proceed
   }
   if (threadIdx.x == 0) tc::mbar_init(&s.bar, 1);
   // Every input starts at once: c rows in place in Qs, dY rows in Ds (both
   // in the swizzled tile layout), angle rates in sinv, gates and the
   // chunk-start phase in stg.
-  const StageRef in{s.Qs, nullptr, 0, s.sinv, s.stg, s.stg + C, s.stg + 2 * C + 4};
+  const StageRef in{s.Qs[0], nullptr, 0, s.sinv, s.stg, s.stg + C, s.stg + 2 * C + 4};
   float* phase0 = s.stg + 3 * C + 8;
-  stage_prefetch<true>(d, b, h, n, cq, nullptr, adt, dt, trap_logits, angles, in);
+  stage_prefetch<true, NH>(d, b, h, n, cq, nullptr, adt, dt, trap_logits, angles, in);
   {
     const int tid = threadIdx.x;
 #pragma unroll
@@ -612,16 +681,16 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
       cp16(reinterpret_cast<float*>(at<true>(s.Ds, rr, c8)),
            reinterpret_cast<const float*>(live ? dy + (size_t(b) * d.T + t) * d.H * P + h * P + c8 : dy), live);
     }
-    if (tid < 32) cp4(phase0 + tid, phases + (size_t(bh) * d.nch + n) * 32 + tid, true);
+    if (tid < NP) cp4(phase0 + tid, phases + (size_t(bh) * d.nch + n) * NP + tid, true);
     cp_commit();
     cp_wait();
   }
   __syncthreads();
   stage_rows(d, t0, in, s.r, s.scratch);
   __syncthreads();
-  stage_theta(d, in, s.r, phase0, s.theta, s.sinv);
+  stage_theta<NH>(d, in, s.r, phase0, s.theta, s.sinv);
   __syncthreads();
-  stage_qk<true, true>(h, in, qb, nullptr, s.theta, s.sinv, s.Qs, nullptr);
+  stage_qk<true, true, NH>(h, in, qb, nullptr, s.theta, s.sinv, s.Qs[0], nullptr);
   {
     // rd(dY o e^p) in place: each thread rescales the pieces it copied.
     const int tid = threadIdx.x;
@@ -645,35 +714,42 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
   tc_publish();
   const uint32_t tm = s.tmem;
   if (threadIdx.x == 0) {
-    tc_product(tm, s.Qs, true, s.Ds, true);  // Q^T D: rows n, cols p
+#pragma unroll
+    for (int q = 0; q < NH; ++q) tc_product(tm + 64 * q, s.Qs[q], true, s.Ds, true);  // Q^T D: rows n, cols p
     tc::commit(&s.bar);
   }
   if (tc_wait(&s.bar, 0)) {
     const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
-    float v[2][16];
-    tc::ld16(tmem_lane_base(tm) + col0, v[0]);
-    tc::ld16(tmem_lane_base(tm) + col0 + 16, v[1]);
-    tc::wait_ld();
-    if (lane < 16) {
-      float* dst = carries + (size_t(bh) * d.nch + n) * N * P + row * P + col0;
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
+    for (int q = 0; q < NH; ++q) {
+      float v[2][16];
+      tc::ld16(tmem_lane_base(tm) + 64 * q + col0, v[0]);
+      tc::ld16(tmem_lane_base(tm) + 64 * q + col0 + 16, v[1]);
+      tc::wait_ld();
+      if (lane < 16) {
+        float* dst = carries + (size_t(bh) * d.nch + n) * N * P + (64 * q + row) * P + col0;
 #pragma unroll
-        for (int e = 0; e < 16; e += 4) st4(dst + 16 * j + e, make_float4(v[j][e], v[j][e + 1], v[j][e + 2], v[j][e + 3]));
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            st4(dst + 16 * j + e, make_float4(v[j][e], v[j][e + 1], v[j][e + 2], v[j][e + 3]));
+      }
     }
   }
   tc::fence_before();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tm, 64);
+  if (warp == 0) tc::tmem_dealloc(tm, 64 * NH);
 }
 
 // Reverse over chunks, in place: carries[n] <- E_n (cotangent of chunk n's end
 // state); E_(nch-1) = d_final, E_(n-1) = D_n + d_n E_n. Same split and
 // look-ahead as state_kernel.
+template <int NH>
 __global__ void __launch_bounds__(256) carry_kernel(Dims d, float* __restrict__ carries,
                                                     const float* __restrict__ deltas,
                                                     const float* __restrict__ d_final) {
-  const int bh = blockIdx.x / SPARTS, i = 4 * ((blockIdx.x % SPARTS) * 256 + threadIdx.x);
+  constexpr int N = Geo<NH>::N, SP = sparts<NH>();
+  const int bh = blockIdx.x / SP, i = 4 * ((blockIdx.x % SP) * 256 + threadIdx.x);
   float4 e = d_final ? ld4(d_final + size_t(bh) * N * P + i) : make_float4(0.f, 0.f, 0.f, 0.f);
   for (int m0 = 0; m0 < d.nch; m0 += 8) {
     float4 u[8];
@@ -706,22 +782,24 @@ struct GradOut {
   float* dscl;    // [B,T,H]
   float* dlog;    // [B,T,H]
   float* ddtp;    // [B,T,H] dt gradient through the phase, without the carry
-  float* dth;     // [B,H,nch,32] per-chunk totals of the pair phase gradient
+  float* dth;     // [B,H,nch,NP] per-chunk totals of the pair phase gradient
   float* dqb;     // [B,H,nch,N] per-chunk bias partials
   float* dkb;     // [B,H,nch,N]
 };
 
+template <int NH>
 struct GradSmem {
-  bf16 Qs[C * TS];
-  bf16 Ks[C * TS];
+  static constexpr int N = Geo<NH>::N, TSN = Geo<NH>::TSN, TW = Geo<NH>::TW;
+  bf16 Qs[C * TSN];
+  bf16 Ks[C * TSN];
   bf16 Vs[C * TS];
   bf16 Dy[C * TS];
   bf16 Ms[C * TS];   // rd(scores o W), then rd(dY o e^p)
   bf16 Mt[C * TS];   // rd(d_mixed o W)
   bf16 Es[N * TS];   // rd(E_n)
   bf16 Ss[N * TS];   // rd(S_n)
-  float theta[C * 33];  // cos of the pair phase, then the pair phase gradient
-  float sinv[C * 33];
+  float theta[C * TW];  // cos of the pair phase, then the pair phase gradient
+  float sinv[C * TW];
   // Per-token rows: 0 sum K.(V rd(E)^T), 1 e^p dY.(Q rd(S)), 2 log-decay
   // increment, 3 d gamma, 4 d scale, 5 flow, 6 d log-decay, 7 unused;
   // 8-9 / 10-11 / 12-13: the two column halves' partials of the row sums
@@ -735,34 +813,38 @@ struct GradSmem {
 };
 
 // Every gradient of one chunk given S_n and E_n. Eight warps: warp w owns
-// rows 16 (w % 4) .. +15 and column half w / 4 (32 columns) of every chunk
-// product, so each product tile is 16 x 32 per warp; row sums over the two
-// halves and column sums over the four row blocks meet in shared memory.
+// rows 16 (w % 4) .. +15 and column half w / 4 of every chunk product (32
+// token columns, or N / 2 state columns), so each product tile is 16 x 32 (or
+// 16 x N / 2) per warp; row sums over the two halves and column sums over the
+// four row blocks meet in shared memory.
+template <int NH>
 __global__ void __launch_bounds__(GW * 32) grads_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ bk, const bf16* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
     const float* __restrict__ phases, const float* __restrict__ starts, const float* __restrict__ carries,
     const bf16* __restrict__ dy, bf16* __restrict__ dx, GradOut o) {
-  constexpr int TH = GW * 32;
+  constexpr int TH = GW * 32, N = Geo<NH>::N, NP = Geo<NH>::NP, TSN = Geo<NH>::TSN, TW = Geo<NH>::TW;
+  constexpr int NTN = 4 * NH;  // 8-column n-tiles of a warp's state-column half
   extern __shared__ __align__(128) unsigned char raw[];
-  GradSmem& s = *reinterpret_cast<GradSmem*>(raw);
+  GradSmem<NH>& s = *reinterpret_cast<GradSmem<NH>*>(raw);
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rb = warp & 3, half = warp >> 2, row0 = 16 * rb, col0 = 32 * half;
+  const int rb = warp & 3, half = warp >> 2, row0 = 16 * rb, col0 = 32 * half, colN = (N / 2) * half;
   const int g = lane >> 2, cc = lane & 3;
   // Every pure copy starts first and lands while the gates, phases and
   // rotations are built: x and dY straight into their tiles, S_n (fp32) into
-  // the score tiles (free until the scores), E_n into registers.
-  constexpr int PER = 32 / GW;
-  float* Sstage = reinterpret_cast<float*>(s.Ms);  // [64][64] fp32 over Ms and Mt
+  // the score tiles (free until the scores; at N = 128 into registers), E_n
+  // into registers.
+  constexpr int PER = N * P / 4 / TH;
+  float* Sstage = reinterpret_cast<float*>(s.Ms);  // [64][64] fp32 over Ms and Mt (N = 64)
   // c / b rows in place in Qs / Ks, angle rates in Es, gates and the
   // chunk-start phase in vec (all free until later phases).
-  const StageRef in{s.Qs, s.Ks, TS, reinterpret_cast<float*>(s.Es), s.vec, s.vec + C, s.vec + 2 * C + 4};
+  const StageRef in{s.Qs, s.Ks, TSN, reinterpret_cast<float*>(s.Es), s.vec, s.vec + C, s.vec + 2 * C + 4};
   float* phase0 = s.vec + 3 * C + 8;
-  stage_prefetch<false>(d, b, h, n, cq, bk, adt, dt, trap_logits, angles, in);
-  if (tid < 32) cp4(phase0 + tid, phases + (size_t(bh) * d.nch + n) * 32 + tid, true);
-  float4 ev[PER];
+  stage_prefetch<false, NH>(d, b, h, n, cq, bk, adt, dt, trap_logits, angles, in);
+  if (tid < NP) cp4(phase0 + tid, phases + (size_t(bh) * d.nch + n) * NP + tid, true);
+  float4 ev[PER], sv[NH == 1 ? 1 : PER];
   {
 #pragma unroll
     for (int k = 0; k < 2 * (16 / GW); ++k) {
@@ -775,8 +857,13 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
     }
     const float* Sg = starts + (size_t(bh) * d.nch + n) * N * P;
     const float* Eg = carries + (size_t(bh) * d.nch + n) * N * P;
+    if constexpr (NH == 1) {
 #pragma unroll
-    for (int k = 0; k < PER; ++k) cp16(Sstage + 4 * (tid + k * TH), Sg + 4 * (tid + k * TH), true);
+      for (int k = 0; k < PER; ++k) cp16(Sstage + 4 * (tid + k * TH), Sg + 4 * (tid + k * TH), true);
+    } else {
+#pragma unroll
+      for (int k = 0; k < PER; ++k) sv[k] = ld4(Sg + 4 * (tid + k * TH));
+    }
     cp_commit();
 #pragma unroll
     for (int k = 0; k < PER; ++k) ev[k] = ld4(Eg + 4 * (tid + k * TH));
@@ -786,9 +873,9 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
   __syncthreads();  // every staged input has landed
   stage_rows(d, t0, in, s.r, s.scratch);
   __syncthreads();
-  stage_theta(d, in, s.r, phase0, s.theta, s.sinv);
+  stage_theta<NH>(d, in, s.r, phase0, s.theta, s.sinv);
   __syncthreads();
-  stage_qk<false, false>(h, in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks);
+  stage_qk<false, false, NH>(h, in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks, TSN);
   __syncthreads();  // the angle stage (Es) is consumed
   // rd(S_n), rd(E_n) as tiles and <E_n, S_n> (fp32 values) for the chunk-end decay.
   {
@@ -796,7 +883,10 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int idx = tid + k * TH;
-      const float4 a4 = ld4(Sstage + 4 * idx), e4 = ev[k];
+      float4 a4;
+      if constexpr (NH == 1) a4 = ld4(Sstage + 4 * idx);
+      else a4 = sv[k];
+      const float4 e4 = ev[k];
       const int r = idx / (P / 4), c4 = idx % (P / 4);
       *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4) = __floats2bfloat162_rn(a4.x, a4.y);
       *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(a4.z, a4.w);
@@ -817,7 +907,7 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
     float sc[4][4], dm[4][4];
     zero(sc);
     zero(dm);
-    mma_tile<N, 4, false, false>(sc, s.Qs, row0, s.Ks, col0);
+    mma_tile<N, 4, false, false, TSN, TSN>(sc, s.Qs, row0, s.Ks, col0);
     mma_tile<P, 4, false, false>(dm, s.Dy, row0, s.Vs, col0);
     float rsum[2] = {0.f, 0.f}, c1[4][2], c2[4][2];
 #pragma unroll
@@ -885,7 +975,7 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
     zero(acc);
     zero(ve);
     mma_tile<C, 4, true, true>(acc, s.Ms, row0, s.Dy, col0);
-    mma_tile<N, 4, false, true>(ve, s.Ks, row0, s.Es, col0);
+    mma_tile<N, 4, false, true, TSN, TS>(ve, s.Ks, row0, s.Es, col0);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int sr = row0 + g + 8 * hf, t = t0 + sr;
@@ -900,12 +990,12 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
       }
     }
   }
-  // dQ, dK (rows t / s, this warp's 32 columns n) in registers.
-  float gq[4][4], gk[4][4];
+  // dQ, dK (rows t / s, this warp's N / 2 columns n) in registers.
+  float gq[NTN][4], gk[NTN][4];
   zero(gq);
   zero(gk);
-  mma_tile<C, 4, false, true>(gq, s.Mt, row0, s.Ks, col0);   // rd(Dm o W) K
-  mma_tile<C, 4, true, true>(gk, s.Mt, row0, s.Qs, col0);    // rd(Dm o W)^T Q
+  mma_tile<C, NTN, false, true, TS, TSN>(gq, s.Mt, row0, s.Ks, colN);   // rd(Dm o W) K
+  mma_tile<C, NTN, true, true, TS, TSN>(gk, s.Mt, row0, s.Qs, colN);    // rd(Dm o W)^T Q
   __syncthreads();  // Ms is rewritten below
   for (int idx = tid; idx < C * P / 2; idx += TH) {
     const int tt = idx / (P / 2), c2 = idx % (P / 2);
@@ -914,27 +1004,30 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
         __floats2bfloat162_rn(__low2float(v) * s.r.ept[tt], __high2float(v) * s.r.ept[tt]);
   }
   __syncthreads();
-  mma_tile<P, 4, false, false>(gq, s.Ms, row0, s.Ss, col0);  // rd(dY e^p) rd(S)^T
+  mma_tile<P, NTN, false, false>(gq, s.Ms, row0, s.Ss, colN);  // rd(dY e^p) rd(S)^T
   {
     float dsrc[2] = {0.f, 0.f}, inh_dot[2] = {0.f, 0.f};
+    {
+      float vn[NTN][4];
+      zero(vn);
+      mma_tile<P, NTN, false, false>(vn, s.Vs, row0, s.Es, colN);  // V rd(E)^T (rows s, cols n)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int sr = row0 + g + 8 * hf;
+        const float src = s.r.scl[sr] * s.r.tail[sr];
+#pragma unroll
+        for (int nt = 0; nt < NTN; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float kv = __bfloat162float(s.Ks[sr * TSN + colN + nt * 8 + 2 * cc + e]);
+            dsrc[hf] = fmaf(kv, vn[nt][2 * hf + e], dsrc[hf]);
+            gk[nt][2 * hf + e] = fmaf(src, vn[nt][2 * hf + e], gk[nt][2 * hf + e]);
+          }
+      }
+    }
     float ve[4][4];
     zero(ve);
-    mma_tile<P, 4, false, false>(ve, s.Vs, row0, s.Es, col0);  // V rd(E)^T (rows s, cols n)
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int sr = row0 + g + 8 * hf;
-      const float src = s.r.scl[sr] * s.r.tail[sr];
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float kv = __bfloat162float(s.Ks[sr * TS + col0 + nt * 8 + 2 * cc + e]);
-          dsrc[hf] = fmaf(kv, ve[nt][2 * hf + e], dsrc[hf]);
-          gk[nt][2 * hf + e] = fmaf(src, ve[nt][2 * hf + e], gk[nt][2 * hf + e]);
-        }
-    }
-    zero(ve);
-    mma_tile<N, 4, false, true>(ve, s.Qs, row0, s.Ss, col0);  // Q rd(S) (rows t, cols p)
+    mma_tile<N, 4, false, true, TSN, TS>(ve, s.Qs, row0, s.Ss, col0);  // Q rd(S) (rows t, cols p)
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int t = row0 + g + 8 * hf;
@@ -964,29 +1057,29 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
   // gradient into theta (same element, read then written by this thread),
   // bias partials per column.
   {
-    uint32_t craw[2][4], braw[2][4];
+    uint32_t craw[2][NTN], braw[2][NTN];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int t = t0 + row0 + g + 8 * hf;
       const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        craw[hf][nt] = t < d.T ? ld_u32(cq + base + col0 + 8 * nt + 2 * cc) : 0u;
-        braw[hf][nt] = t < d.T ? ld_u32(bk + base + col0 + 8 * nt + 2 * cc) : 0u;
+      for (int nt = 0; nt < NTN; ++nt) {
+        craw[hf][nt] = t < d.T ? ld_u32(cq + base + colN + 8 * nt + 2 * cc) : 0u;
+        braw[hf][nt] = t < d.T ? ld_u32(bk + base + colN + 8 * nt + 2 * cc) : 0u;
       }
     }
-    float sq[4][2], sk[4][2];
+    float sq[NTN][2], sk[NTN][2];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) sq[nt][0] = sq[nt][1] = sk[nt][0] = sk[nt][1] = 0.f;
+    for (int nt = 0; nt < NTN; ++nt) sq[nt][0] = sq[nt][1] = sk[nt][0] = sk[nt][1] = 0.f;
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int tt = row0 + g + 8 * hf, t = t0 + tt;
       const bool live = t < d.T;
       const size_t ob = ((size_t(b) * d.T + t) * d.H + h) * N;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const int i = (col0 >> 1) + 4 * nt + cc, n0 = 2 * i;
-        const float cs = s.theta[tt * 33 + i], sn = s.sinv[tt * 33 + i];
+      for (int nt = 0; nt < NTN; ++nt) {
+        const int i = (colN >> 1) + 4 * nt + cc, n0 = 2 * i;
+        const float cs = s.theta[tt * TW + i], sn = s.sinv[tt * TW + i];
         const float gq0 = gq[nt][2 * hf], gq1 = gq[nt][2 * hf + 1];
         const float gk0 = gk[nt][2 * hf], gk1 = gk[nt][2 * hf + 1];
         const float pq0 = gq0 * cs + gq1 * sn, pq1 = gq1 * cs - gq0 * sn;
@@ -1006,11 +1099,11 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
         const float qr0 = q0 * cs - q1 * sn, qr1 = q1 * cs + q0 * sn;
         const float kr0 = k0 * cs - k1 * sn, kr1 = k1 * cs + k0 * sn;
         const float dth = gq0 * (-qr1) + gq1 * qr0 + gk0 * (-kr1) + gk1 * kr0;
-        s.theta[tt * 33 + i] = (i < d.A && live) ? dth : 0.f;
+        s.theta[tt * TW + i] = (i < d.A && live) ? dth : 0.f;
       }
     }
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < NTN; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float q = sq[nt][e], kk = sk[nt][e];
@@ -1020,8 +1113,8 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
           kk += __shfl_xor_sync(0xffffffffu, kk, off);
         }
         if (g == 0) {
-          s.bq[rb * N + col0 + nt * 8 + 2 * cc + e] = q;
-          s.bk[rb * N + col0 + nt * 8 + 2 * cc + e] = kk;
+          s.bq[rb * N + colN + nt * 8 + 2 * cc + e] = q;
+          s.bk[rb * N + colN + nt * 8 + 2 * cc + e] = kk;
         }
       }
   }
@@ -1050,14 +1143,17 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
   // added by finish_kernel). Warp 0 also runs the log-decay suffix scan.
   constexpr int SG = C / GW;
   {
-    const int i = lane;
-    float acc = 0.f;
 #pragma unroll
-    for (int j = SG - 1; j >= 0; --j) {
-      acc += s.theta[(SG * warp + j) * 33 + i];
-      s.theta[(SG * warp + j) * 33 + i] = acc;
+    for (int q = 0; q < NH; ++q) {
+      const int i = lane + 32 * q;
+      float acc = 0.f;
+#pragma unroll
+      for (int j = SG - 1; j >= 0; --j) {
+        acc += s.theta[(SG * warp + j) * TW + i];
+        s.theta[(SG * warp + j) * TW + i] = acc;
+      }
+      s.r.seg[warp * NP + i] = acc;
     }
-    s.r.seg[warp * 32 + i] = acc;
     if (warp == 0) {
       float fl = s.vec[5 * C + lane] + s.vec[5 * C + 32 + lane];
       fl = warp_sum(fl);
@@ -1076,11 +1172,15 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
   }
   __syncthreads();
   {
-    const int i = lane;
-    float off = 0.f;
-    for (int v = warp + 1; v < GW; ++v) off += s.r.seg[v * 32 + i];
-    if (warp == 0 && i < d.A)
-      o.dth[(size_t(bh) * d.nch + n) * 32 + i] = off + s.r.seg[i];
+    float off[NH];
+#pragma unroll
+    for (int q = 0; q < NH; ++q) {
+      const int i = lane + 32 * q;
+      off[q] = 0.f;
+      for (int v = warp + 1; v < GW; ++v) off[q] += s.r.seg[v * NP + i];
+      if (warp == 0 && i < d.A)
+        o.dth[(size_t(bh) * d.nch + n) * NP + i] = off[q] + s.r.seg[i];
+    }
     // Angle-rate and dt-through-phase gradients of this warp's SG tokens:
     // lanes over angle pairs (coalesced rows), dt term by a warp reduction.
     float mine = 0.f;
@@ -1088,11 +1188,17 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
     for (int j = 0; j < SG; ++j) {
       const int tt = SG * warp + j, t = t0 + tt;
       if (t >= d.T) break;
-      const float inc = i < d.A ? s.theta[tt * 33 + i] + off : 0.f;
-      const float rate = i < d.A ? rate_at(d, angles, b, h, t, i) : 0.f;
       const size_t si = (size_t(b) * d.T + t) * d.H + h;
-      if (i < d.A) o.drate[si * d.A + i] = inc * s.r.dt[tt];
-      const float ddt = warp_sum(inc * rate);
+      float part = 0.f;
+#pragma unroll
+      for (int q = 0; q < NH; ++q) {
+        const int i = lane + 32 * q;
+        const float inc = i < d.A ? s.theta[tt * TW + i] + off[q] : 0.f;
+        const float rate = i < d.A ? rate_at(d, angles, b, h, t, i) : 0.f;
+        if (i < d.A) o.drate[si * d.A + i] = inc * s.r.dt[tt];
+        part = fmaf(inc, rate, part);
+      }
+      const float ddt = warp_sum(part);
       if (lane == j) mine = ddt;
     }
     if (lane < SG) {
@@ -1110,11 +1216,13 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
 
 // In place over chunks: dth[n] <- sum over chunks m > n of the chunk totals
 // (the phase-gradient carry every token of chunk n receives).
+template <int NH>
 __global__ void later_kernel(Dims d, float* __restrict__ dth) {
-  const int bh = blockIdx.x, i = threadIdx.x;
+  constexpr int NP = Geo<NH>::NP;
+  const int bh = blockIdx.x, i = threadIdx.x;  // NP threads
   float acc = 0.f;
   for (int n = d.nch - 1; n >= 0; --n) {
-    float* slot = dth + (size_t(bh) * d.nch + n) * 32 + i;
+    float* slot = dth + (size_t(bh) * d.nch + n) * NP + i;
     const float v = i < d.A ? *slot : 0.f;
     *slot = acc;
     acc += v;
@@ -1126,41 +1234,56 @@ __global__ void later_kernel(Dims d, float* __restrict__ dth) {
 // gradient += later . rate), applies the gate chain rule of the mamba3_fused
 // preprocessing (flashmamba.py:1142-1147) and sums the angle-rate and
 // query/key gradients over heads (shared layout) or converts them (per head).
+template <int NH>
 __global__ void __launch_bounds__(256) finish_kernel(
     Dims d, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ later, GradOut o, bf16* __restrict__ dc,
     bf16* __restrict__ db, float* __restrict__ d_adt, float* __restrict__ d_dt, float* __restrict__ d_trap,
     float* __restrict__ d_angles) {
+  constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t bt = size_t(blockIdx.x) * 8 + warp;
   if (bt >= size_t(d.B) * d.T) return;
   const int b = int(bt / d.T), t = int(bt % d.T), n = t / C;
-  const bool pair = lane < d.A;
-  const float shared_rate = (!d.per_head && pair) ? angles[bt * d.A + lane] : 0.f;
-  float ang = 0.f, q0 = 0.f, q1 = 0.f, k0 = 0.f, k1 = 0.f;
+  // Lane l handles angle pairs and state pairs l + 32 q (q < NH).
+  bool pair[NH];
+  float shared_rate[NH], ang[NH], q0[NH], q1[NH], k0[NH], k1[NH];
+#pragma unroll
+  for (int q = 0; q < NH; ++q) {
+    const int i = lane + 32 * q;
+    pair[q] = i < d.A;
+    shared_rate[q] = (!d.per_head && pair[q]) ? angles[bt * d.A + i] : 0.f;
+    ang[q] = q0[q] = q1[q] = k0[q] = k1[q] = 0.f;
+  }
   for (int h0 = 0; h0 < d.H; h0 += 32) {
     float mine = 0.f;
     const int hn = min(32, d.H - h0);
     for (int j = 0; j < hn; ++j) {
       const int h = h0 + j;
       const size_t si = bt * d.H + h;
-      const float rate = d.per_head ? (pair ? angles[si * d.A + lane] : 0.f) : shared_rate;
-      const float l = pair ? later[((size_t(b) * d.H + h) * d.nch + n) * 32 + lane] : 0.f;
-      if (pair) {
-        const float dr = fmaf(l, dt[si], o.drate[si * d.A + lane]);
-        if (d.per_head) d_angles[si * d.A + lane] = dr;
-        else ang += dr;
+      float part = 0.f;
+#pragma unroll
+      for (int q = 0; q < NH; ++q) {
+        const int i = lane + 32 * q;
+        const float rate = d.per_head ? (pair[q] ? angles[si * d.A + i] : 0.f) : shared_rate[q];
+        const float l = pair[q] ? later[((size_t(b) * d.H + h) * d.nch + n) * NP + i] : 0.f;
+        if (pair[q]) {
+          const float dr = fmaf(l, dt[si], o.drate[si * d.A + i]);
+          if (d.per_head) d_angles[si * d.A + i] = dr;
+          else ang[q] += dr;
+        }
+        part = fmaf(l, rate, part);
+        const float2 gq = *reinterpret_cast<const float2*>(o.dq + si * N + 2 * i);
+        const float2 gk = *reinterpret_cast<const float2*>(o.dk + si * N + 2 * i);
+        if (d.per_head) {
+          *reinterpret_cast<__nv_bfloat162*>(dc + si * N + 2 * i) = __floats2bfloat162_rn(gq.x, gq.y);
+          *reinterpret_cast<__nv_bfloat162*>(db + si * N + 2 * i) = __floats2bfloat162_rn(gk.x, gk.y);
+        } else {
+          q0[q] += gq.x; q1[q] += gq.y; k0[q] += gk.x; k1[q] += gk.y;
+        }
       }
-      const float extra = warp_sum(l * rate);
+      const float extra = warp_sum(part);
       if (lane == j) mine = extra;
-      const float2 gq = *reinterpret_cast<const float2*>(o.dq + si * N + 2 * lane);
-      const float2 gk = *reinterpret_cast<const float2*>(o.dk + si * N + 2 * lane);
-      if (d.per_head) {
-        *reinterpret_cast<__nv_bfloat162*>(dc + si * N + 2 * lane) = __floats2bfloat162_rn(gq.x, gq.y);
-        *reinterpret_cast<__nv_bfloat162*>(db + si * N + 2 * lane) = __floats2bfloat162_rn(gk.x, gk.y);
-      } else {
-        q0 += gq.x; q1 += gq.y; k0 += gk.x; k1 += gk.y;
-      }
     }
     if (lane < hn) {
       const size_t si = bt * d.H + h0 + lane;
@@ -1173,24 +1296,30 @@ __global__ void __launch_bounds__(256) finish_kernel(
     }
   }
   if (!d.per_head) {
-    if (pair) d_angles[bt * d.A + lane] = ang;
-    *reinterpret_cast<__nv_bfloat162*>(dc + bt * N + 2 * lane) = __floats2bfloat162_rn(q0, q1);
-    *reinterpret_cast<__nv_bfloat162*>(db + bt * N + 2 * lane) = __floats2bfloat162_rn(k0, k1);
+#pragma unroll
+    for (int q = 0; q < NH; ++q) {
+      const int i = lane + 32 * q;
+      if (pair[q]) d_angles[bt * d.A + i] = ang[q];
+      *reinterpret_cast<__nv_bfloat162*>(dc + bt * N + 2 * i) = __floats2bfloat162_rn(q0[q], q1[q]);
+      *reinterpret_cast<__nv_bfloat162*>(db + bt * N + 2 * i) = __floats2bfloat162_rn(k0[q], k1[q]);
+    }
   }
 }
 
 // Bias gradients: sum per-chunk partials over batch and chunks. Block per
-// head; 16 groups of 64 threads take interleaved (batch, chunk) slots, then
-// the groups are added in a fixed order (deterministic).
+// head; 1024 / N groups of N threads take interleaved (batch, chunk) slots,
+// then the groups are added in a fixed order (deterministic).
+template <int NH>
 __global__ void __launch_bounds__(1024) bias_kernel(Dims d, const float* __restrict__ dqb,
                                                     const float* __restrict__ dkb, float* __restrict__ d_qb,
                                                     float* __restrict__ d_kb) {
-  __shared__ float part[2][16][N];
-  const int h = blockIdx.x, nn = threadIdx.x & (N - 1), grp = threadIdx.x >> 6;
+  constexpr int N = Geo<NH>::N, GR = 1024 / N;
+  __shared__ float part[2][GR][N];
+  const int h = blockIdx.x, nn = threadIdx.x & (N - 1), grp = threadIdx.x / N;
   const int slots = d.B * d.nch;
   float sq = 0.f, sk = 0.f;
 #pragma unroll 4
-  for (int k = grp; k < slots; k += 16) {
+  for (int k = grp; k < slots; k += GR) {
     const int b = k / d.nch, n = k % d.nch;
     const size_t o = ((size_t(b) * d.H + h) * d.nch + n) * N + nn;
     sq += dqb[o];
@@ -1201,7 +1330,7 @@ __global__ void __launch_bounds__(1024) bias_kernel(Dims d, const float* __restr
   __syncthreads();
   if (threadIdx.x < N) {
     float q = 0.f, k = 0.f;
-    for (int gi = 0; gi < 16; ++gi) {
+    for (int gi = 0; gi < GR; ++gi) {
       q += part[0][gi][nn];
       k += part[1][gi][nn];
     }

@@ -37,6 +37,15 @@ def kernel_state_dim(state_dim: int) -> int:
     raise ValueError(f"Scan supports state dims up to {STATE_DIM}")
 
 
+def sequence_state_dim(state_dim: int, bf16: bool) -> int:
+    """State dim a whole-sequence scan runs at: bfloat16 scans above 64 run
+    the tensor-core kernels at 128 (96 is zero-padded: the padded state rows
+    stay zero and every product with them is zero, so outputs and gradients
+    are those of the unpadded scan); float32 runs 64, 96 or 128 natively."""
+    n = kernel_state_dim(state_dim)
+    return 128 if bf16 and n > 64 else n
+
+
 def scan_forward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
     """m4_scan_fwd on padded, contiguous operands: returns y, final, residual."""
     lib = _lib.load()
@@ -117,7 +126,7 @@ def _prepare(c, b, x, adt, dt, trap_logits, angles, q_bias, k_bias, heads, per_h
     if state_dim > STATE_DIM or value_dim > HEAD_DIM:
         raise ValueError(f"Scan supports state dims up to {STATE_DIM} and head dims up to {HEAD_DIM}")
     model = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
-    pn = (0, kernel_state_dim(state_dim) - state_dim)
+    pn = (0, sequence_state_dim(state_dim, model == torch.bfloat16) - state_dim)
     c = _pad(c.to(model), pn).contiguous()
     b = _pad(b.to(model), pn).contiguous()
     lead = x.shape[:-1]

@@ -13,9 +13,10 @@ from __future__ import annotations
 import ctypes
 
 import torch
+import torch.nn.functional as F
 
 from . import _lib
-from .flashmamba import mamba3_step, scan_backward, scan_forward
+from .flashmamba import mamba3_step, scan_backward, scan_forward, sequence_state_dim
 
 
 def _stream() -> int:
@@ -45,6 +46,11 @@ class _MambaMixerCore(torch.autograd.Function):
             "m4_mixer_prep_fwd")
         qb = q_bias.reshape(heads, state)
         kb = k_bias.reshape(heads, state)
+        # The scan's state dim (96 runs the tensor-core kernels zero-padded to 128).
+        pad = sequence_state_dim(state, True) - state
+        if pad:
+            c, b = F.pad(c, (0, pad)), F.pad(b, (0, pad))
+            qb, kb = F.pad(qb, (0, pad)), F.pad(kb, (0, pad))
         y, _, resid = scan_forward(c, b, x, adt, dt, trap, ang, qb, kb, False)
         out = torch.empty(batch, time, inner, dtype=torch.bfloat16, device=dev)
         _lib.check(lib.m4_mixer_post_fwd(ctypes.byref(dims), *map(_lib.ptr, (proj, y, D, out)), _stream()),
@@ -72,6 +78,9 @@ class _MambaMixerCore(torch.autograd.Function):
             proj, y, D, g_out, d_y, d_proj, part, dD)), _stream()), "m4_mixer_post_bwd")
         dc, db, dx, dadt, ddt, dtrap, dang, dqb, dkb = scan_backward(
             c, b, x, adt, dt, trap, ang, qb, kb, resid, d_y, None, False)
+        if c.shape[-1] != state:  # drop the zero-padded state coordinates
+            dc, db = dc[..., :state].contiguous(), db[..., :state].contiguous()
+            dqb, dkb = dqb[..., :state].contiguous(), dkb[..., :state].contiguous()
         d_bs, d_cs, d_dtb = torch.empty_like(b_scale), torch.empty_like(c_scale), torch.empty_like(dt_bias)
         _lib.check(lib.m4_mixer_prep_bwd(ctypes.byref(dims), *map(_lib.ptr, (
             proj, b_scale, c_scale, dt_bias, D, g_out, dc, db, dx, dadt, ddt, dtrap, dang, d_proj, part,
