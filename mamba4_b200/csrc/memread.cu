@@ -291,11 +291,12 @@ struct SolveSmem {
   float y[64];                   // solution
   union {
     struct {
+      float4 col[2][4 * PS];     // column pair broadcasts (two steps): at a*PS + p the row
+                                 // pair (a + 8p, a + 4 + 8p) of column J, then of column J + 1
+      float2 colw[2][4];         // bordered-row entries of columns J, J + 1 per a
       float2 kP[4 * PS];         // (k[a + 8p], k[a + 4 + 8p]) at a*PS + p
       float kC[8 * KS];          // k[b + 8n] at b*KS + n
       float qC[8 * KS];          // q[b + 8n] at b*KS + n
-      float2 col[4][4 * PS];     // column broadcasts (two per step, two steps), pairs at a*PS + p
-      float colw[4][4];          // bordered-row entry per a
     } f;
     struct {
       float T[8 * 36];           // diagonal blocks, packed lower tri(r, c)
@@ -416,60 +417,48 @@ M4_DEV void forward_substitute(const float2 (&L)[NPAIR], const float* g, float* 
   __syncwarp();
 }
 
-template <int JN>
-M4_DEV void store_column(float2* dst, const float2 (&A)[NPAIR]) {
-  if constexpr (JN & 1) dst[JN] = A[pair_of(JN, JN)];
-  constexpr int S = (JN + 1) & ~1;
-#pragma unroll
-  for (int p = S; p < 8; p += 2) {
-    const float2 u = A[pair_of(p, JN)], v = A[pair_of(p + 1, JN)];
-    *reinterpret_cast<float4*>(dst + p) = make_float4(u.x, u.y, v.x, v.y);
-  }
-}
-
-// One right-looking column step on unscaled columns U (L[:, j] = U[:, j]/sqrt(U_jj)),
-// column j = 8 JN + jb: the column block JN is a template parameter (register
-// indices), the column within it a runtime value, so the 64 steps compile to
-// 8 loop bodies (small enough for the instruction cache).
 // Two right-looking column steps at once on unscaled columns U
 // (L[:, j] = U[:, j]/sqrt(U_jj)): columns J = 8 JN + jb and J + 1 (jb even).
-// Both owners broadcast their columns; every lane forms the column J + 1
-// updated by column J from the two broadcasts (U'[:, J+1] = U[:, J+1] -
-// U[:, J] U[J+1, J] / U[J, J]) and applies the rank-2 update to its trailing
-// entries. Half the barrier / pivot chains of single-column steps.
+// Both owners broadcast their columns into one interleaved buffer (a lane
+// reads both columns' entries of a row pair with one 128-bit load); every
+// lane forms the column J + 1 updated by column J from the two broadcasts
+// (U'[:, J+1] = U[:, J+1] - U[:, J] U[J+1, J] / U[J, J]) and applies the
+// rank-2 update to its trailing entries. The column block JN is a template
+// parameter (register indices), the column within it a runtime value, so the
+// 32 steps compile to 8 loop bodies (small enough for the instruction cache).
 template <int JN>
 M4_DEV void factor_pair(int jb, float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
-  const int par = (jb >> 1) & 1;  // alternating buffer pair
-  float2* cA = sm.u.f.col[2 * par];
-  float2* cB = sm.u.f.col[2 * par + 1];
-  float* wA = sm.u.f.colw[2 * par];
-  float* wB = sm.u.f.colw[2 * par + 1];
+  const int par = (jb >> 1) & 1;  // alternating buffer
+  float4* col = sm.u.f.col[par];
+  float2* colw = sm.u.f.colw[par];
   if (b == jb || b == jb + 1) {
-    store_column<JN>((b == jb ? cA : cB) + a * PS, A);
-    (b == jb ? wA : wB)[a] = wr[JN];
+    const int o = b - jb;  // 0: column J into .xy, 1: column J + 1 into .zw
+    float2* dst = reinterpret_cast<float2*>(col + a * PS) + o;
+#pragma unroll
+    for (int p = JN; p < 8; ++p) dst[2 * p] = A[pair_of(p, JN)];
+    reinterpret_cast<float*>(colw + a)[o] = wr[JN];
   }
   __syncwarp();
   const int A0 = jb & 3, H0 = (jb >> 2) & 1, A1 = (jb + 1) & 3, H1 = ((jb + 1) >> 2) & 1;
-  const float* fA = reinterpret_cast<const float*>(cA);
-  const float* fB = reinterpret_cast<const float*>(cB);
-  const float pJ = fA[(A0 * PS + JN) * 2 + H0];   // U[J][J]
-  const float u10 = fA[(A1 * PS + JN) * 2 + H1];  // U[J+1][J]
-  const float pJ1 = fB[(A1 * PS + JN) * 2 + H1];  // U[J+1][J+1]
+  const float* fc = reinterpret_cast<const float*>(col);
+  const float pJ = fc[(A0 * PS + JN) * 4 + H0];       // U[J][J]
+  const float u10 = fc[(A1 * PS + JN) * 4 + H1];      // U[J+1][J]
+  const float pJ1 = fc[(A1 * PS + JN) * 4 + 2 + H1];  // U[J+1][J+1]
   const float r = rsqrtf(pJ), r2 = r * r;
   const float sf = u10 * r2;
   const float r1 = rsqrtf(fmaf(-u10, sf, pJ1)), r12 = r1 * r1;
   rc[JN] = (b == jb) ? r : (b == jb + 1 ? r1 : rc[JN]);
   dup_t DA[8], DB[8];
   {
-    const float2* sa = cA + (b & 3) * PS;
-    const float2* sb = cB + (b & 3) * PS;
-    const float rwA = wA[a];
-    const float rwB = fmaf(-rwA, sf, wB[a]);
+    const float4* sc = col + (b & 3) * PS;
+    const float2 rw = colw[a];
+    const float rwA = rw.x;
+    const float rwB = fmaf(-rwA, sf, rw.y);
 #pragma unroll
     for (int n = JN; n < 8; ++n) {
-      const float2 va = sa[n], vb = sb[n];
-      const float ca = b >= 4 ? va.y : va.x;
-      const float cb = b >= 4 ? vb.y : vb.x;
+      const float4 v = sc[n];
+      const float ca = b >= 4 ? v.y : v.x;
+      const float cb = b >= 4 ? v.w : v.z;
       float CA = ca * r2, CB = fmaf(-ca, sf, cb) * r12;
       if (n == JN) {
         CA = (b > jb) ? CA : 0.f;
@@ -482,9 +471,9 @@ M4_DEV void factor_pair(int jb, float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[
   }
 #pragma unroll
   for (int p = JN; p < 8; ++p) {
-    float2 ra = cA[a * PS + p];
-    const float2 rb0 = cB[a * PS + p];
-    float2 rb = make_float2(fmaf(-ra.x, sf, rb0.x), fmaf(-ra.y, sf, rb0.y));
+    const float4 v = col[a * PS + p];
+    float2 ra = make_float2(v.x, v.y);
+    float2 rb = make_float2(fmaf(-v.x, sf, v.z), fmaf(-v.y, sf, v.w));
     if (p == JN) {
       ra.x = (a > jb) ? ra.x : 0.f;
       ra.y = (a + 4 > jb) ? ra.y : 0.f;
