@@ -922,8 +922,9 @@ inline int forward_bf16_nh(const M4ScanDims& s, const void* c, const void* b, co
   alignas(64) CUtensorMap xmap;
   if (!all_aligned16(c, b, x)) return M4_ERR_ALIGN;  // 16-byte row copies and the TMA box
   if (!encode_tokens_map(&xmap, x, d.B, d.T, d.H * P)) return M4_ERR_LAUNCH;
-  allow_smem(fused_fwd_kernel<NH>, sizeof(FusedSmem<NH>) + 1024);
-  fused_fwd_kernel<NH><<<d.B * d.H, GW * 32, sizeof(FusedSmem<NH>) + 1024, st>>>(
+  const size_t fsm = fused_smem_bytes<NH>(d.A) + 1024;
+  allow_smem(fused_fwd_kernel<NH>, fsm);
+  fused_fwd_kernel<NH><<<d.B * d.H, GW * 32, fsm, st>>>(
       d, xmap, cq, bk, adt, dt, trap, angles, qb, kb, static_cast<bf16*>(y), starts, phases, deltas, fin);
   return launch_status();
 }

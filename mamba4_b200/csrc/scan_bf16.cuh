@@ -142,6 +142,19 @@ M4_DEV void tc_publish() {
 // tensor-memory lane base; warps w and w + 4 share a lane quarter.
 M4_DEV uint32_t tmem_lane_base(uint32_t tm) { return tm + (uint32_t(32 * ((threadIdx.x >> 5) & 3)) << 16); }
 
+// 16 rows x 32 columns of an M = 64 accumulator (the warp's lane quarter from
+// `taddr`) over all 32 threads: v[4 k + 2 hh + j] is row t / 4 + 8 hh,
+// column 8 k + 2 (t % 4) + j (tcgen05.ld 16x256b, four repetitions).
+M4_DEV void ld_16x256b_x4(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 template <int NT>
 M4_DEV void zero(float (&acc)[NT][4]) {
 #pragma unroll
@@ -217,49 +230,46 @@ template <int NH> constexpr int sparts() { return 4 * NH; }
 // the reference's sequential chunk grid, flashmamba.py:589-660), so no state
 // pass, phase pass or per-chunk CTA setup is left. Per chunk:
 //   TMA of the next chunk's x tile into the other buffer (zero fill past T);
-//   gates, in-chunk phases and the rotated, rounded Q / K tiles;
+//   gates, in-chunk phases and the rotated, rounded Q / K tiles (rotated in
+//   place: the raw c / b rows land in the swizzled tiles);
 //   rd(S_n) as a tile, S_n and the chunk-start phase to the residuals;
-//   tcgen05 commit 1: Q K^T, Q rd(S_n), K^T rd(V o scale o tail);
+//   tcgen05 commit 1: Q K^T, Q rd(S_n), K^T rd(V o scale o tail); once it
+//   completes the Q / K tiles take the next chunk's raw rows (cp.async);
 //   masked scores rd((Q K^T) o W) -> tile; tcgen05 commit 2: scores V;
 //   S_(n+1) = e^(p_L) S_n + K^T rd(V o scale o tail) in registers;
 //   y = rd(scores V + e^p Q rd(S_n)).
-// Thread (w, lane < 16) owns state row 16 (w % 4) + lane, columns
-// 32 (w / 4) .. +31: the accumulator rows it reads from tensor memory.
+// Accumulators are read with the 16-lane tensor-memory loads (16x256b), which
+// spread the 16 rows an M = 64 accumulator keeps in a warp's lane quarter
+// over all 32 threads: thread t of warp w holds rows 16 (w % 4) + t / 4 and
+// + 8, columns 32 (w / 4) + 8 k + 2 (t % 4) + {0, 1} (k < 4) of each product
+// and of the state.
 // Residuals written: starts[n] = S_n, phases[n], deltas[n] = e^(p_L).
 // ---------------------------------------------------------------------------
-// Raw inputs of one chunk, prefetched (cp.async) while the previous chunk's
-// tensor-core phases run; tokens past T arrive as zeros. dt and trap hold
-// token t0 + 64 too (the trapezoid's next-token term).
-template <int NH>
-struct FusedStage {
-  static constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP;
-  bf16 c[C * N];       // rows of c (queries) and b (keys), row-major
-  bf16 b[C * N];
-  float ang[C * NP];   // angle rates [token][pair]
-  float adt[C];
-  float dt[C + 4];
-  float trap[C + 4];
-};
-
 template <int NH>
 struct FusedSmem {
-  static constexpr int TW = Geo<NH>::TW, NP = Geo<NH>::NP;
+  static constexpr int NP = Geo<NH>::NP;
   bf16 Qs[NH][C * 64]; // 128-byte-swizzled 64-column tiles on 1024-byte boundaries
   bf16 Ks[NH][C * 64];
   bf16 Vs[2][C * P];   // x tiles (TMA, double buffered)
   bf16 Vw[C * P];      // rd(V o scale o tail)
   bf16 Ms[C * C];      // masked scores
   bf16 Ss[NH][64 * P]; // rd(S_n), 64 state rows per tile
-  float theta[C * TW];
-  float sinv[C * TW];
   float scratch[C];
   float phase[NP];     // phase at the current chunk start
+  float adt[C];        // the current chunk's gates (dt and trap with token t0 + 64)
+  float dt[C + 4];
+  float trap[C + 4];
   Rows r;
-  FusedStage<NH> in;   // the current chunk's raw inputs
   uint64_t bar;        // tensor-core commits (two per chunk)
   uint64_t bar_x[2];   // TMA of the x tiles
   uint32_t tmem;
+  // Followed by three [C][fwd_ta(A)] fp32 tables: angle rates, cos and sin
+  // of the pair phases (only the A rotated pairs).
 };
+// Row stride of the forward's angle tables.
+__host__ __device__ constexpr int fwd_ta(int A) { return A > 0 ? A : 1; }
+template <int NH>
+constexpr size_t fused_smem_bytes(int A) { return sizeof(FusedSmem<NH>) + 3 * size_t(C) * fwd_ta(A) * sizeof(float); }
 
 // Where a kernel stages one chunk's raw inputs (cp.async, tokens past T as
 // zeros): c / b rows (bf16, row-major with `stride` elements, or in 128-byte
@@ -284,10 +294,12 @@ M4_DEV bf16* stage_row(bf16* base, int stride, int r, int c) {
   else return base + r * stride + c;
 }
 
-// Start copying chunk n's raw inputs (one commit group per thread).
+// Start copying chunk n's raw inputs (one commit group per thread); the
+// angle rates land at in.ang[token * as + pair].
 template <bool SW, int NH>
 M4_DEV void stage_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, const bf16* bk, const float* adt,
-                           const float* dt, const float* trap_logits, const float* angles, const StageRef& in) {
+                           const float* dt, const float* trap_logits, const float* angles, const StageRef& in,
+                           int as = Geo<NH>::NP) {
   constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP, PIECES = N / 8;
   const int tid = threadIdx.x, t0 = n * C;
 #pragma unroll
@@ -307,7 +319,7 @@ M4_DEV void stage_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, c
     const int tt = idx / d.A, i = idx % d.A, t = t0 + tt;
     const bool live = t < d.T;
     const size_t o = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * d.A + i : (size_t(b) * d.T + t) * d.A + i;
-    cp4(&in.ang[tt * NP + i], live ? angles + o : angles, live);
+    cp4(&in.ang[tt * as + i], live ? angles + o : angles, live);
   }
   if (tid < 3 * (C + 1)) {
     const int which = tid / (C + 1), tt = tid % (C + 1), t = t0 + tt;
@@ -349,10 +361,13 @@ M4_DEV void stage_rows(const Dims& d, int t0, const StageRef& in, Rows& r, float
 }
 
 // chunk_theta from the stage (same segment scheme): lanes over the pairs
-// lane + 32 q (q < NH).
+// lane + 32 q (q < NH). Angle rates at in.ang[token * as + pair]; cos / sin
+// tables [token][tw] (pairs past the angle count hold 1 / 0 where tw has
+// room for them).
 template <int NH>
-M4_DEV void stage_theta(const Dims& d, const StageRef& in, Rows& r, const float* phase0, float* cosv, float* sinv) {
-  constexpr int SEG = C / GW, NP = Geo<NH>::NP, TW = Geo<NH>::TW;
+M4_DEV void stage_theta(const Dims& d, const StageRef& in, Rows& r, const float* phase0, float* cosv, float* sinv,
+                        int as = Geo<NH>::NP, int tw = Geo<NH>::TW) {
+  constexpr int SEG = C / GW, NP = Geo<NH>::NP;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
   for (int q = 0; q < NH; ++q) {
@@ -362,8 +377,8 @@ M4_DEV void stage_theta(const Dims& d, const StageRef& in, Rows& r, const float*
 #pragma unroll
       for (int j = 0; j < SEG; ++j) {
         const int tt = SEG * w + j;
-        acc = fmaf(in.ang[tt * NP + i], r.dt[tt], acc);
-        cosv[tt * TW + i] = acc;
+        acc = fmaf(in.ang[tt * as + i], r.dt[tt], acc);
+        cosv[tt * tw + i] = acc;
       }
     }
     r.seg[w * NP + i] = acc;
@@ -377,13 +392,15 @@ M4_DEV void stage_theta(const Dims& d, const StageRef& in, Rows& r, const float*
       off = phase0[i];
       for (int v = 0; v < w; ++v) off += r.seg[v * NP + i];
     }
+    if (i < tw) {
 #pragma unroll 1
-    for (int j = 0; j < SEG; ++j) {
-      const int e = (SEG * w + j) * TW + i;
-      float cs = 1.f, sn = 0.f;
-      if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
-      cosv[e] = cs;
-      sinv[e] = sn;
+      for (int j = 0; j < SEG; ++j) {
+        const int e = (SEG * w + j) * tw + i;
+        float cs = 1.f, sn = 0.f;
+        if (i < d.A) sincosf(cosv[e] + off, &sn, &cs);
+        cosv[e] = cs;
+        sinv[e] = sn;
+      }
     }
   }
 }
@@ -398,11 +415,13 @@ M4_DEV bf16* qk_at(bf16* T, int stride, int r, int c) {
 
 // build_qk from the stage: rotated, rounded Q / K tiles (either may be null);
 // a stage may be the destination tile itself (each thread reads and writes
-// the same pair). Lane l handles the pairs l + 32 q (columns 2 l + 64 q).
+// the same pair). Lane l handles the pairs l + 32 q (columns 2 l + 64 q);
+// pairs from `na` on are not rotated (cos / sin tables [token][tw]).
 template <bool SRC_SW, bool DST_SW, int NH>
 M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb, const float* cosv,
-                     const float* sinv, bf16* Qs, bf16* Ks, int dst_stride = 0) {
-  constexpr int PER = C / GW, N = Geo<NH>::N, TW = Geo<NH>::TW;
+                     const float* sinv, bf16* Qs, bf16* Ks, int dst_stride = 0, int na = Geo<NH>::NP,
+                     int tw = Geo<NH>::TW) {
+  constexpr int PER = C / GW, N = Geo<NH>::N;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
   for (int q = 0; q < NH; ++q) {
@@ -412,7 +431,7 @@ M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
       const int tt = w + GW * k;
-      const float cs = cosv[tt * TW + i], sn = sinv[tt * TW + i];
+      const float cs = i < na ? cosv[tt * tw + i] : 1.f, sn = i < na ? sinv[tt * tw + i] : 0.f;
       if (Qs) {
         const uint32_t cr = ld_u32(stage_row<SRC_SW>(in.c, in.stride, tt, n0));
         const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
@@ -430,7 +449,7 @@ M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb
 }
 
 template <int NH>
-__global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
+__global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
     Dims d, const __grid_constant__ CUtensorMap tmap_x, const bf16* __restrict__ cq, const bf16* __restrict__ bk,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
@@ -439,9 +458,14 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
   constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP;
   extern __shared__ __align__(128) unsigned char raw[];
   FusedSmem<NH>& s = *reinterpret_cast<FusedSmem<NH>*>(align1024(raw));
+  const int ta = fwd_ta(d.A);
+  float* angt = reinterpret_cast<float*>(&s + 1);
+  float* cosv = angt + C * ta;
+  float* sinv = cosv + C * ta;
   const int bh = blockIdx.x, b = bh / d.H, h = bh % d.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
+  // Accumulator fragment of this thread: rows r0 + 8 hh, columns col0 + 8 k + cq + j.
+  const int r0 = 16 * (warp & 3) + (lane >> 2), cq2 = 2 * (lane & 3), col0 = 32 * (warp >> 2);
   if (warp == 0) {
     tc::tmem_alloc(&s.tmem, 256);
     tc::tmem_relinquish();
@@ -455,18 +479,29 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
   __syncthreads();
   tc::fence_after();
   const uint32_t tm = s.tmem;
+  const uint32_t tl = tmem_lane_base(tm);
   if (tid == 0) {
     tc::mbar_expect_tx(&s.bar_x[0], C * P * sizeof(bf16));
     tc::tma_load_3d(s.Vs[0], &tmap_x, h * P, 0, b, &s.bar_x[0]);
   }
-  const StageRef in{s.in.c, s.in.b, N, s.in.ang, s.in.adt, s.in.dt, s.in.trap};
-  stage_prefetch<false, NH>(d, b, h, 0, cq, bk, adt, dt, trap_logits, angles, in);
-  // fp32 state S_n: rows 64 q + `row` (q < NH), columns col0 .. col0 + 31 (lanes < 16)
-  float st[NH][32];
+  const StageRef in{s.Qs[0], s.Ks[0], 0, angt, s.adt, s.dt, s.trap};
+  stage_prefetch<true, NH>(d, b, h, 0, cq, bk, adt, dt, trap_logits, angles, in, ta);
+  // fp32 state S_n: rows 64 q + r0 + 8 hh, columns col0 + 8 k + cq2 + j at st[q][4 k + 2 hh + j]
+  float st[NH][16];
 #pragma unroll
   for (int q = 0; q < NH; ++q)
 #pragma unroll
-    for (int j = 0; j < 32; ++j) st[q][j] = 0.f;
+    for (int j = 0; j < 16; ++j) st[q][j] = 0.f;
+  auto put_state = [&](float* dst) {
+#pragma unroll
+    for (int q = 0; q < NH; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          *reinterpret_cast<float2*>(dst + (64 * q + r0 + 8 * hh) * P + col0 + 8 * k + cq2) =
+              make_float2(st[q][4 * k + 2 * hh], st[q][4 * k + 2 * hh + 1]);
+  };
   bool ok = true;
   for (int n = 0; n < d.nch; ++n) {
     const int t0 = n * C, buf = n & 1;
@@ -480,7 +515,7 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
     __syncthreads();  // this chunk's stage has landed
     stage_rows(d, t0, in, s.r, s.scratch);
     __syncthreads();
-    stage_theta<NH>(d, in, s.r, s.phase, s.theta, s.sinv);
+    stage_theta<NH>(d, in, s.r, s.phase, cosv, sinv, ta, ta);
     __syncthreads();
     if (tid < NP) {
       float inc = 0.f;
@@ -490,21 +525,17 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
       s.phase[tid] += tid < d.A ? inc : 0.f;
     }
     if (tid < C) s.scratch[tid] = s.r.scl[tid] * s.r.tail[tid];
-    stage_qk<false, true, NH>(h, in, qb, kb, s.theta, s.sinv, s.Qs[0], s.Ks[0]);
-    if (lane < 16) {
+    stage_qk<true, true, NH>(h, in, qb, kb, cosv, sinv, s.Qs[0], s.Ks[0], 0, d.A, ta);
+    put_state(starts + (size_t(bh) * d.nch + n) * N * P);
 #pragma unroll
-      for (int q = 0; q < NH; ++q) {
-        float* dst = starts + (size_t(bh) * d.nch + n) * N * P + (64 * q + row) * P + col0;
+    for (int q = 0; q < NH; ++q)
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[q][j], st[q][j + 1], st[q][j + 2], st[q][j + 3]));
+      for (int k = 0; k < 4; ++k)
 #pragma unroll
-        for (int j = 0; j < 32; j += 2)
-          *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ss[q], row, col0 + j)) =
-              __floats2bfloat162_rn(st[q][j], st[q][j + 1]);
-      }
-    }
-    __syncthreads();  // scratch (scale o tail) visible; the stage is consumed
-    if (n + 1 < d.nch) stage_prefetch<false, NH>(d, b, h, n + 1, cq, bk, adt, dt, trap_logits, angles, in);
+        for (int hh = 0; hh < 2; ++hh)
+          *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ss[q], r0 + 8 * hh, col0 + 8 * k + cq2)) =
+              __floats2bfloat162_rn(st[q][4 * k + 2 * hh], st[q][4 * k + 2 * hh + 1]);
+    __syncthreads();  // scratch (scale o tail) visible
     // rd(V o scale o tail) from the x tile once it has landed.
     if (!tc::mbar_wait(&s.bar_x[buf], (n >> 1) & 1, tc::WAIT_LIMIT)) {
       if (lane == 0) tc::flag_timeout();
@@ -541,28 +572,29 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
       tc::commit(&s.bar);
     }
     ok = ok && tc_wait(&s.bar, 0);
+    // The Q / K tiles are free: the next chunk's raw rows land in them.
+    if (n + 1 < d.nch) stage_prefetch<true, NH>(d, b, h, n + 1, cq, bk, adt, dt, trap_logits, angles, in, ta);
     if (ok) {
-      const float pt = s.r.p[row];
-#pragma unroll 1
-      for (int j = 0; j < 2; ++j) {
-        float v[16];
-        tc::ld16(tmem_lane_base(tm) + col0 + 16 * j, v);
-        tc::wait_ld();
-        if (lane < 16) {
+      float v[16];
+      ld_16x256b_x4(tl + col0, v);
+      tc::wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            float m2[2];
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = r0 + 8 * hh;
+        const float pt = s.r.p[row];
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const int sidx = col0 + 16 * j + e + q;
-              float w = 0.f;
-              if (sidx < row) w = expf(pt - s.r.p[sidx]) * s.r.scl[sidx];
-              else if (sidx == row) w = s.r.gam[row];
-              m2[q] = v[e + q] * w;
-            }
-            *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ms, row, col0 + 16 * j + e)) =
-                __floats2bfloat162_rn(m2[0], m2[1]);
+        for (int k = 0; k < 4; ++k) {
+          float m2[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int sidx = col0 + 8 * k + cq2 + j;
+            float w = 0.f;
+            if (sidx < row) w = expf(pt - s.r.p[sidx]) * s.r.scl[sidx];
+            else if (sidx == row) w = s.r.gam[row];
+            m2[j] = v[4 * k + 2 * hh + j] * w;
           }
+          *reinterpret_cast<__nv_bfloat162*>(at<true>(s.Ms, row, col0 + 8 * k + cq2)) =
+              __floats2bfloat162_rn(m2[0], m2[1]);
         }
       }
     }
@@ -575,40 +607,32 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
       // S_(n+1) = e^(p_L) S_n + U_n (the update finished with commit 1).
       const float dl = expf(s.r.p[C - 1]);
 #pragma unroll
-      for (int q = 0; q < NH; ++q)
+      for (int q = 0; q < NH; ++q) {
+        float u[16];
+        ld_16x256b_x4(tl + 128 + 64 * q + col0, u);
+        tc::wait_ld();
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          float u[16];
-          tc::ld16(tmem_lane_base(tm) + 128 + 64 * q + col0 + 16 * j, u);
-          tc::wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) st[q][16 * j + e] = fmaf(dl, st[q][16 * j + e], u[e]);
-        }
+        for (int e = 0; e < 16; ++e) st[q][e] = fmaf(dl, st[q][e], u[e]);
+      }
       if (tid == 0) deltas[size_t(bh) * d.nch + n] = dl;
     }
     ok = ok && tc_wait(&s.bar, 1);
     if (ok) {
-      const int t = t0 + row;
-      const float e = s.r.ept[row];
-      bf16* yrow = y + (size_t(b) * d.T + t) * d.H * P + h * P + col0;
-#pragma unroll 1
-      for (int j = 0; j < 2; ++j) {
-        float acc[16], inh[16];
-        tc::ld16(tmem_lane_base(tm) + col0 + 16 * j, acc);
-        tc::ld16(tmem_lane_base(tm) + 64 + col0 + 16 * j, inh);
-        tc::wait_ld();
-        if (lane < 16 && t < d.T) {
+      float acc[16], inh[16];
+      ld_16x256b_x4(tl + col0, acc);
+      ld_16x256b_x4(tl + 64 + col0, inh);
+      tc::wait_ld();
 #pragma unroll
-          for (int q = 0; q < 16; q += 8) {
-            uint4 o;
-            uint32_t* u = reinterpret_cast<uint32_t*>(&o);
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = r0 + 8 * hh, t = t0 + row;
+        const float e = s.r.ept[row];
+        if (t < d.T) {
+          bf16* yrow = y + (size_t(b) * d.T + t) * d.H * P + h * P + col0 + cq2;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaf(e, inh[q + 2 * k], acc[q + 2 * k]),
-                                                              fmaf(e, inh[q + 2 * k + 1], acc[q + 2 * k + 1]));
-              u[k] = *reinterpret_cast<const uint32_t*>(&h2);
-            }
-            *reinterpret_cast<uint4*>(yrow + 16 * j + q) = o;
+          for (int k = 0; k < 4; ++k) {
+            const int i = 4 * k + 2 * hh;
+            *reinterpret_cast<__nv_bfloat162*>(yrow + 8 * k) =
+                __floats2bfloat162_rn(fmaf(e, inh[i], acc[i]), fmaf(e, inh[i + 1], acc[i + 1]));
           }
         }
       }
@@ -617,14 +641,7 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) fused_fwd_kernel(
     __syncthreads();  // tensor memory and every tile are free for the next chunk
     tc::fence_after();
   }
-  if (lane < 16) {
-#pragma unroll
-    for (int q = 0; q < NH; ++q) {
-      float* dst = final_state + size_t(bh) * N * P + (64 * q + row) * P + col0;
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) st4(dst + j, make_float4(st[q][j], st[q][j + 1], st[q][j + 2], st[q][j + 3]));
-    }
-  }
+  put_state(final_state + size_t(bh) * N * P);
   // A TMA the loop no longer waits for cannot be in flight: the last chunk
   // issues none and every earlier one was awaited.
   tc::fence_before();
