@@ -155,6 +155,29 @@ M4_DEV void ld_16x256b_x4(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Reduce-scatter over the lanes that differ in bits LO .. LO + L - 1 of the
+// lane index: V values per lane in, V >> L sums per lane out, in place at
+// v[0 .. V >> L). Level l halves the array; the lane with that bit clear keeps
+// the lower half. A lane ends with the sums of the values
+// [(V >> L) j, (V >> L) (j + 1)) of its group, j = its bits LO .. LO + L - 1
+// read as a binary number with bit LO + L - 1 most significant.
+template <int V, int L, int LO>
+M4_DEV void reduce_scatter(float (&v)[V], int lane) {
+  static_assert((V >> L) << L == V, "V must be divisible by 2^L");
+#pragma unroll
+  for (int l = L - 1; l >= 0; --l) {
+    const int bit = LO + l;
+    const int width = V >> (L - 1 - l);  // live values before this level
+    const bool up = (lane >> bit) & 1;
+#pragma unroll
+    for (int i = 0; i < width / 2; ++i) {
+      const float keep = up ? v[width / 2 + i] : v[i];
+      const float give = up ? v[i] : v[width / 2 + i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, give, 1 << bit);
+    }
+  }
+}
+
 template <int NT>
 M4_DEV void zero(float (&acc)[NT][4]) {
 #pragma unroll
@@ -835,7 +858,7 @@ struct GradSmem {
 // 16 x N / 2) per warp; row sums over the two halves and column sums over the
 // four row blocks meet in shared memory.
 template <int NH>
-__global__ void __launch_bounds__(GW * 32) grads_kernel(
+__global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ bk, const bf16* __restrict__ x,
     const float* __restrict__ adt, const float* __restrict__ dt, const float* __restrict__ trap_logits,
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
@@ -1021,6 +1044,24 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
         __floats2bfloat162_rn(__low2float(v) * s.r.ept[tt], __high2float(v) * s.r.ept[tt]);
   }
   __syncthreads();
+  // The raw c / b pairs of this thread's accumulator rows for the rotation
+  // backward: at N = 128 loaded before the next products so their latency
+  // hides (the kernel runs one CTA per SM there; registers are free), at
+  // N = 64 just before use (two CTAs per SM need <= 128 registers).
+  uint32_t craw[2][NTN], braw[2][NTN];
+  auto load_raw = [&]() {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int t = t0 + row0 + g + 8 * hf;
+      const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
+#pragma unroll
+      for (int nt = 0; nt < NTN; ++nt) {
+        craw[hf][nt] = t < d.T ? ld_u32(cq + base + colN + 8 * nt + 2 * cc) : 0u;
+        braw[hf][nt] = t < d.T ? ld_u32(bk + base + colN + 8 * nt + 2 * cc) : 0u;
+      }
+    }
+  };
+  if constexpr (NH == 2) load_raw();
   mma_tile<P, NTN, false, false>(gq, s.Ms, row0, s.Ss, colN);  // rd(dY e^p) rd(S)^T
   {
     float dsrc[2] = {0.f, 0.f}, inh_dot[2] = {0.f, 0.f};
@@ -1069,22 +1110,25 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
       }
     }
   }
+  constexpr int SG = C / GW;
+  // Angle rates of this warp's tokens (last phase), loaded ahead likewise.
+  float rates[SG][NH];
+  auto load_rates = [&]() {
+#pragma unroll
+    for (int j = 0; j < SG; ++j)
+#pragma unroll
+      for (int q = 0; q < NH; ++q) {
+        const int i = lane + 32 * q, t = t0 + SG * warp + j;
+        rates[j][q] = (i < d.A && t < d.T) ? rate_at(d, angles, b, h, t, i) : 0.f;
+      }
+  };
+  if constexpr (NH == 2) load_rates();
+  if constexpr (NH == 1) load_raw();
   // Rotation backward in registers: the accumulators hold each pair (2i, 2i+1)
   // on one thread. Pre-rotation gradients to workspace, the pair phase
   // gradient into theta (same element, read then written by this thread),
   // bias partials per column.
   {
-    uint32_t craw[2][NTN], braw[2][NTN];
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const int t = t0 + row0 + g + 8 * hf;
-      const size_t base = d.per_head ? ((size_t(b) * d.T + t) * d.H + h) * N : (size_t(b) * d.T + t) * N;
-#pragma unroll
-      for (int nt = 0; nt < NTN; ++nt) {
-        craw[hf][nt] = t < d.T ? ld_u32(cq + base + colN + 8 * nt + 2 * cc) : 0u;
-        braw[hf][nt] = t < d.T ? ld_u32(bk + base + colN + 8 * nt + 2 * cc) : 0u;
-      }
-    }
     float sq[NTN][2], sk[NTN][2];
 #pragma unroll
     for (int nt = 0; nt < NTN; ++nt) sq[nt][0] = sq[nt][1] = sk[nt][0] = sk[nt][1] = 0.f;
@@ -1119,21 +1163,24 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
         s.theta[tt * TW + i] = (i < d.A && live) ? dth : 0.f;
       }
     }
+    // Column sums over the warp's 16 rows (the eight lanes of one cc, two
+    // rows each): reduce-scatter, lane g ends with values [R g, R g + R).
+    constexpr int V = 4 * NTN, R = V / 8;
+    float v[V];
 #pragma unroll
     for (int nt = 0; nt < NTN; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        float q = sq[nt][e], kk = sk[nt][e];
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-          q += __shfl_xor_sync(0xffffffffu, q, off);
-          kk += __shfl_xor_sync(0xffffffffu, kk, off);
-        }
-        if (g == 0) {
-          s.bq[rb * N + colN + nt * 8 + 2 * cc + e] = q;
-          s.bk[rb * N + colN + nt * 8 + 2 * cc + e] = kk;
-        }
+        v[2 * nt + e] = sq[nt][e];
+        v[2 * NTN + 2 * nt + e] = sk[nt][e];
       }
+    reduce_scatter<V, 3, 2>(v, lane);
+#pragma unroll
+    for (int m = 0; m < R; ++m) {
+      const int idx = R * g + m, j = idx % (2 * NTN), nt = j >> 1, e = j & 1;
+      float* dst = idx < 2 * NTN ? s.bq : s.bk;
+      dst[rb * N + colN + nt * 8 + 2 * cc + e] = v[m];
+    }
   }
   __syncthreads();
   // Per-token scalar gradients.
@@ -1158,7 +1205,6 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
   // Suffix sums of the pair phase gradient: warp w over tokens SG w .. SG w +
   // SG - 1, then the totals of later segments (the carry from later chunks is
   // added by finish_kernel). Warp 0 also runs the log-decay suffix scan.
-  constexpr int SG = C / GW;
   {
 #pragma unroll
     for (int q = 0; q < NH; ++q) {
@@ -1199,30 +1245,34 @@ __global__ void __launch_bounds__(GW * 32) grads_kernel(
         o.dth[(size_t(bh) * d.nch + n) * NP + i] = off[q] + s.r.seg[i];
     }
     // Angle-rate and dt-through-phase gradients of this warp's SG tokens:
-    // lanes over angle pairs (coalesced rows), dt term by a warp reduction.
-    float mine = 0.f;
+    // lanes over angle pairs (coalesced rows); the dt terms of the SG tokens
+    // reduced together (reduce-scatter: lane l ends with token l / 4).
+    if constexpr (NH == 1) load_rates();
+    float part[SG];
 #pragma unroll
     for (int j = 0; j < SG; ++j) {
       const int tt = SG * warp + j, t = t0 + tt;
-      if (t >= d.T) break;
-      const size_t si = (size_t(b) * d.T + t) * d.H + h;
-      float part = 0.f;
-#pragma unroll
-      for (int q = 0; q < NH; ++q) {
-        const int i = lane + 32 * q;
-        const float inc = i < d.A ? s.theta[tt * TW + i] + off[q] : 0.f;
-        const float rate = i < d.A ? rate_at(d, angles, b, h, t, i) : 0.f;
-        if (i < d.A) o.drate[si * d.A + i] = inc * s.r.dt[tt];
-        part = fmaf(inc, rate, part);
-      }
-      const float ddt = warp_sum(part);
-      if (lane == j) mine = ddt;
-    }
-    if (lane < SG) {
-      const int tt = SG * warp + lane, t = t0 + tt;
+      part[j] = 0.f;
       if (t < d.T) {
         const size_t si = (size_t(b) * d.T + t) * d.H + h;
-        o.ddtp[si] = mine;
+#pragma unroll
+        for (int q = 0; q < NH; ++q) {
+          const int i = lane + 32 * q;
+          const float inc = i < d.A ? s.theta[tt * TW + i] + off[q] : 0.f;
+          if (i < d.A) o.drate[si * d.A + i] = inc * s.r.dt[tt];
+          part[j] = fmaf(inc, rates[j][q], part[j]);
+        }
+      }
+    }
+    static_assert(SG == 8, "one token per group of four lanes");
+    reduce_scatter<SG, 3, 2>(part, lane);
+    part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
+    part[0] += __shfl_xor_sync(0xffffffffu, part[0], 2);
+    if ((lane & 3) == 0) {
+      const int tt = SG * warp + (lane >> 2), t = t0 + tt;
+      if (t < d.T) {
+        const size_t si = (size_t(b) * d.T + t) * d.H + h;
+        o.ddtp[si] = part[0];
         o.dgam[si] = s.vec[3 * C + tt];
         o.dscl[si] = s.vec[4 * C + tt];
         o.dlog[si] = s.vec[6 * C + tt];
