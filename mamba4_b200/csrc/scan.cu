@@ -966,9 +966,9 @@ inline int backward_bf16_nh(const M4ScanDims& s, const void* c, const void* b, c
   const bf16* xx = static_cast<const bf16*>(x);
   const bf16* g = static_cast<const bf16*>(dy);
   const int bh = d.B * d.H, chunks = bh * d.nch;
-  allow_smem(dstart_kernel<NH>, sizeof(DsSmem<NH>) + 1024);
-  dstart_kernel<NH><<<chunks, GW * 32, sizeof(DsSmem<NH>) + 1024, st>>>(d, cq, g, adt, dt, trap, angles, qb, phases,
-                                                                        carries);
+  const size_t dsm = dstart_smem_bytes<NH>(d.A) + 1024;
+  allow_smem(dstart_kernel<NH>, dsm);
+  dstart_kernel<NH><<<chunks, GW * 32, dsm, st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
   carry_kernel<NH><<<bh * sparts<NH>(), 256, 0, st>>>(d, carries, deltas, d_final);
   allow_smem(grads_kernel<NH>, sizeof(GradSmem<NH>));
   grads_kernel<NH><<<chunks, GW * 32, sizeof(GradSmem<NH>), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb,

@@ -677,17 +677,19 @@ __global__ void __launch_bounds__(GW * 32, 2) fused_fwd_kernel(
 // ---------------------------------------------------------------------------
 template <int NH>
 struct DsSmem {
-  static constexpr int TW = Geo<NH>::TW, NP = Geo<NH>::NP;
+  static constexpr int NP = Geo<NH>::NP;
   bf16 Qs[NH][C * 64];  // blocked tiles (tcgen05 operands)
   bf16 Ds[C * P];
-  float theta[C * TW];
-  float sinv[C * TW];
   float scratch[C];
   float stg[3 * C + 8 + NP];  // staged gates and the chunk-start phase
   Rows r;
   uint64_t bar;
   uint32_t tmem;
+  // Followed by two [C][fwd_ta(A)] fp32 tables: cos (the phases first) and
+  // sin (the angle rates first) of the rotated pairs.
 };
+template <int NH>
+constexpr size_t dstart_smem_bytes(int A) { return sizeof(DsSmem<NH>) + 2 * size_t(C) * fwd_ta(A) * sizeof(float); }
 
 // D_n = Q^T rd(dY o e^p) into carries[n], on the tensor cores (tcgen05):
 // one M = 64 product per half of the state rows.
@@ -699,6 +701,9 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
   constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP;
   extern __shared__ __align__(128) unsigned char raw[];
   DsSmem<NH>& s = *reinterpret_cast<DsSmem<NH>*>(align1024(raw));
+  const int ta = fwd_ta(d.A);
+  float* cosv = reinterpret_cast<float*>(&s + 1);
+  float* sinv = cosv + C * ta;
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
@@ -709,9 +714,9 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
   // Every input starts at once: c rows in place in Qs, dY rows in Ds (both
   // in the swizzled tile layout), angle rates in sinv, gates and the
   // chunk-start phase in stg.
-  const StageRef in{s.Qs[0], nullptr, 0, s.sinv, s.stg, s.stg + C, s.stg + 2 * C + 4};
+  const StageRef in{s.Qs[0], nullptr, 0, sinv, s.stg, s.stg + C, s.stg + 2 * C + 4};
   float* phase0 = s.stg + 3 * C + 8;
-  stage_prefetch<true, NH>(d, b, h, n, cq, nullptr, adt, dt, trap_logits, angles, in);
+  stage_prefetch<true, NH>(d, b, h, n, cq, nullptr, adt, dt, trap_logits, angles, in, ta);
   {
     const int tid = threadIdx.x;
 #pragma unroll
@@ -728,9 +733,9 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
   __syncthreads();
   stage_rows(d, t0, in, s.r, s.scratch);
   __syncthreads();
-  stage_theta<NH>(d, in, s.r, phase0, s.theta, s.sinv);
+  stage_theta<NH>(d, in, s.r, phase0, cosv, sinv, ta, ta);
   __syncthreads();
-  stage_qk<true, true, NH>(h, in, qb, nullptr, s.theta, s.sinv, s.Qs[0], nullptr);
+  stage_qk<true, true, NH>(h, in, qb, nullptr, cosv, sinv, s.Qs[0], nullptr, 0, d.A, ta);
   {
     // rd(dY o e^p) in place: each thread rescales the pieces it copied.
     const int tid = threadIdx.x;
@@ -759,21 +764,19 @@ __global__ void __launch_bounds__(GW * 32) dstart_kernel(
     tc::commit(&s.bar);
   }
   if (tc_wait(&s.bar, 0)) {
-    const int row = 16 * (warp & 3) + lane, col0 = 32 * (warp >> 2);
+    // 16-lane loads: rows r0 + 8 hh, columns col0 + 8 k + cq2 + {0, 1}.
+    const int r0 = 16 * (warp & 3) + (lane >> 2), cq2 = 2 * (lane & 3), col0 = 32 * (warp >> 2);
 #pragma unroll
     for (int q = 0; q < NH; ++q) {
-      float v[2][16];
-      tc::ld16(tmem_lane_base(tm) + 64 * q + col0, v[0]);
-      tc::ld16(tmem_lane_base(tm) + 64 * q + col0 + 16, v[1]);
+      float v[16];
+      ld_16x256b_x4(tmem_lane_base(tm) + 64 * q + col0, v);
       tc::wait_ld();
-      if (lane < 16) {
-        float* dst = carries + (size_t(bh) * d.nch + n) * N * P + (64 * q + row) * P + col0;
+      float* dst = carries + (size_t(bh) * d.nch + n) * N * P + (64 * q + r0) * P + col0 + cq2;
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
+      for (int k = 0; k < 4; ++k)
 #pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            st4(dst + 16 * j + e, make_float4(v[j][e], v[j][e + 1], v[j][e + 2], v[j][e + 3]));
-      }
+        for (int hh = 0; hh < 2; ++hh)
+          *reinterpret_cast<float2*>(dst + 8 * hh * P + 8 * k) = make_float2(v[4 * k + 2 * hh], v[4 * k + 2 * hh + 1]);
     }
   }
   tc::fence_before();
