@@ -437,7 +437,11 @@ def measure_e2e_hotpath(m, s, dev, world, tokens, args):
     return {"value": world * tokens / (e2e_ms / 1000.0), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": state["d2h"], "ms_per_step": e2e_ms,
             "pipelined": "inputs of step i+1 copied in and results of step i copied out "
-                         "while step i computes (two slots, two copy streams)"}
+                         "while step i computes (two slots, two copy streams)",
+            "host_link": f"bound by PCIe / host memory, shared by the {world} rank(s) of this node "
+                         "(about 50 GB/s per direction for one GPU, about 130 GB/s aggregate measured "
+                         "with 8): per-GPU e2e falls as ranks are added; the device-timed value is the "
+                         "kernels' claim"}
 
 
 def measure_decode(world, rank, local, batch=64, tokens=64, warmup=8):

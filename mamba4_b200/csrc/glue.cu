@@ -1141,20 +1141,40 @@ __global__ void __launch_bounds__(WPB * 32) mem_post_bwd(
   }
 }
 
-// Per-head sums of the mem_post_bwd partials: warp w holds head w % h.
-__global__ void head_sum_kernel(const float* __restrict__ part, int nw, int h, float* __restrict__ d_cs,
-                                float* __restrict__ d_D, float* __restrict__ d_om) {
-  const int hh = threadIdx.x;
-  if (hh >= h) return;
+// Per-head sums of the mem_post_bwd partials: warp w holds head w % h. One
+// block per head; thread i sums the head's warps i, i + 256, ... and a fixed
+// tree (warp sums, then warp 0 over the eight warp totals) finishes, so the
+// order of the additions does not depend on scheduling.
+__global__ void __launch_bounds__(256) head_sum_kernel(const float* __restrict__ part, int nw, int h,
+                                                       float* __restrict__ d_cs, float* __restrict__ d_D,
+                                                       float* __restrict__ d_om) {
+  __shared__ float red[3][8];
+  const int hh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float a = 0.f, b = 0.f, c = 0.f;
-  for (int w = hh; w < nw; w += h) {
+  for (int w = hh + h * tid; w < nw; w += h * 256) {
     a += part[size_t(w) * PROW + 128];
     b += part[size_t(w) * PROW + 129];
     c += part[size_t(w) * PROW + 130];
   }
-  d_cs[hh] = a;
-  d_D[hh] = b;
-  d_om[hh] = c;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  c = warp_sum(c);
+  if (lane == 0) {
+    red[0][warp] = a;
+    red[1][warp] = b;
+    red[2][warp] = c;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    a = warp_sum(lane < 8 ? red[0][lane] : 0.f);
+    b = warp_sum(lane < 8 ? red[1][lane] : 0.f);
+    c = warp_sum(lane < 8 ? red[2][lane] : 0.f);
+    if (lane == 0) {
+      d_cs[hh] = a;
+      d_D[hh] = b;
+      d_om[hh] = c;
+    }
+  }
 }
 
 inline int mem_blocks(int rows, int h) {
@@ -1345,7 +1365,7 @@ extern "C" int m4_memmix_post_bwd(const M4MemMixDims* m, const float* out, const
                                            D, order_mix, scale, rstd, static_cast<const bf16*>(g_y), d_out, d_var,
                                            d_values, d_ordered, static_cast<bf16*>(d_gate), part);
   colsum_kernel<<<128, 256, 0, s>>>(part, nw, PROW, d_scale);
-  head_sum_kernel<<<1, 32, 0, s>>>(part, nw, d.heads, d_conf_scale, d_D, d_order_mix);
+  head_sum_kernel<<<d.heads, 256, 0, s>>>(part, nw, d.heads, d_conf_scale, d_D, d_order_mix);
   return launch_status();
 }
 
