@@ -17,6 +17,7 @@ import torch
 import torch.nn.functional as F
 
 from . import _lib
+from .remat import operator_results
 
 STATE_DIMS = (64, 96, 128)   # state dims the kernels implement (smaller ones are padded)
 STATE_DIM = STATE_DIMS[-1]
@@ -47,7 +48,14 @@ def sequence_state_dim(state_dim: int, bf16: bool) -> int:
 
 
 def scan_forward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
-    """m4_scan_fwd on padded, contiguous operands: returns y, final, residual."""
+    """m4_scan_fwd on padded, contiguous operands: returns y, final, residual
+    (inside a block rematerialized under the "kernels" policy, the recompute
+    returns the forward's results instead of relaunching: the reference's
+    "ssd_scan" checkpoint name)."""
+    return operator_results(lambda: _scan_forward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head))
+
+
+def _scan_forward(c, b, x, adt, dt, trap, angles, q_bias, k_bias, per_head):
     lib = _lib.load()
     batch, time = c.shape[:2]
     heads = dt.shape[-1]

@@ -23,6 +23,7 @@ from .glue import (ADD_RMS_FEATURES, GradSlab, add_rms_norm_bf16, head_cross_ent
                    mamba_mixer_step, memory_mixer_post, memory_mixer_prep, memory_mixer_step, order_scan,
                    rms_norm_bf16, split_projection)
 from .memory import selective_initial_state, selective_memory_fused
+from .remat import block_modes, run_block
 
 
 @dataclass(frozen=True)
@@ -47,6 +48,12 @@ class Mamba4Config:
     memory_key_shift: bool = True
     norm_eps: float = 1e-5
     chunk_size: int = 64
+    # Activation rematerialization (`lm/config.py:26-34`, `remat_block` in
+    # lm/models/common.py:97-122): off by default here (a B200 holds the
+    # configs' activations: 180 GB of HBM); the reference's policy names are
+    # accepted ("full", "kernels", "mixers", "mixers-N").
+    remat: bool = False
+    remat_policy: str = "full"
 
     @property
     def n_layers(self) -> int:
@@ -74,7 +81,8 @@ CONFIGS = {
     # d_model 768, 17 Mamba-3 + 4 memory layers
     # (pattern of lm/configs/mamba4-125m.json), memory 12 heads x 128,
     # Mamba-3 state 128 (lm/configs/mamba4-125m.json:10).
-    "125m": Mamba4Config(d_model=768, layer_pattern="SSSMSSSSMSSSSMSSSSMSS", d_state=128),
+    "125m": Mamba4Config(d_model=768, layer_pattern="SSSMSSSSMSSSSMSSSSMSS", d_state=128,
+                         remat_policy="mixers-3"),
 }
 
 
@@ -275,13 +283,15 @@ class Mamba4LM(nn.Module):
         nn.init.normal_(self.embedding.weight, 0.0, 0.02)
         self.blocks = nn.ModuleList(Block(cfg, k) for k in cfg.layer_pattern)
         self.final_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self.remat_modes = block_modes(cfg.layer_pattern, cfg.remat_policy)  # validates the name
         self.fused_loss = True  # forward(tokens, targets) returns per-token losses
 
     def hidden(self, tokens):
         # bfloat16 residual stream and final norm (Embed dtype bf16).
         x = self.embedding(tokens).to(torch.bfloat16)
-        for block in self.blocks:
-            x = block(x)
+        remat = self.cfg.remat and torch.is_grad_enabled()
+        for block, mode in zip(self.blocks, self.remat_modes):
+            x = run_block(block, x, mode) if remat else block(x)
         return self.final_norm(x)
 
     def forward(self, tokens, targets=None):

@@ -106,3 +106,44 @@ def test_graphed_decode_matches_eager_decode():
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
             ref, cache = model.decode_step(tokens[:, i], cache)
         assert torch.equal(dec.step(tokens[:, i]), ref), i
+
+
+@pytest.mark.parametrize("policy", ["full", "kernels", "mixers", "mixers-1"])
+def test_remat_policies_reproduce_the_gradients(policy, monkeypatch):
+    """Every rematerialization policy of the reference (`remat_block`,
+    lm/models/common.py:97-122) gives the loss and gradients of the model
+    without remat (the recomputed forward is deterministic); "kernels"
+    recomputes the blocks without relaunching the scan."""
+    import dataclasses
+
+    from mamba4_b200 import flashmamba
+
+    torch.manual_seed(3)
+    base = Mamba4LM(TINY).cuda()
+    model = Mamba4LM(dataclasses.replace(TINY, remat=True, remat_policy=policy)).cuda()
+    model.load_state_dict(base.state_dict())
+    ids = (torch.arange(2 * 201, device="cuda").reshape(2, 201) * 5) % TINY.vocab_size
+    tokens, targets = ids[:, :-1].contiguous(), ids[:, 1:].contiguous()
+    calls = [0]
+    inner = flashmamba._scan_forward
+
+    def counted(*args):
+        calls[0] += 1
+        return inner(*args)
+
+    monkeypatch.setattr(flashmamba, "_scan_forward", counted)
+    results = []
+    for m in (base, model):
+        calls[0] = 0
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = m(tokens, targets).sum()
+        loss.backward()
+        results.append((loss.detach(), [p.grad.clone() for p in m.parameters()], calls[0]))
+    (l0, g0, n0), (l1, g1, n1) = results
+    torch.testing.assert_close(l1, l0, rtol=0, atol=0)
+    for a, b in zip(g1, g0):
+        torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-7)
+    scans = TINY.layer_pattern.count("S")
+    assert n0 == scans
+    expected = {"full": 2 * scans, "kernels": scans, "mixers": 2 * scans, "mixers-1": scans + 1}[policy]
+    assert n1 == expected
