@@ -323,7 +323,7 @@ template <bool SW, int NH>
 M4_DEV void stage_prefetch(const Dims& d, int b, int h, int n, const bf16* cq, const bf16* bk, const float* adt,
                            const float* dt, const float* trap_logits, const float* angles, const StageRef& in,
                            int as = Geo<NH>::NP) {
-  constexpr int N = Geo<NH>::N, NP = Geo<NH>::NP, PIECES = N / 8;
+  constexpr int N = Geo<NH>::N, PIECES = N / 8;
   const int tid = threadIdx.x, t0 = n * C;
 #pragma unroll
   for (int k = 0; k < 4 * NH; ++k) {  // 2 tiles x 64 rows x N/8 16-byte pieces over 256 threads
