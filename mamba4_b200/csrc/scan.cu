@@ -970,8 +970,8 @@ inline int backward_bf16_nh(const M4ScanDims& s, const void* c, const void* b, c
   allow_smem(dstart_kernel<NH>, dsm);
   dstart_kernel<NH><<<chunks, GW * 32, dsm, st>>>(d, cq, g, adt, dt, trap, angles, qb, phases, carries);
   carry_kernel<NH><<<bh * sparts<NH>(), 256, 0, st>>>(d, carries, deltas, d_final);
-  allow_smem(grads_kernel<NH>, sizeof(GradSmem<NH>));
-  grads_kernel<NH><<<chunks, GW * 32, sizeof(GradSmem<NH>), st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb,
+  allow_smem(grads_kernel<NH>, sizeof(GradSmem<NH>) + 1024);
+  grads_kernel<NH><<<chunks, GW * 32, sizeof(GradSmem<NH>) + 1024, st>>>(d, cq, bk, xx, adt, dt, trap, angles, qb, kb,
                                                                   phases, starts, carries, g,
                                                                   static_cast<bf16*>(dx), o);
   later_kernel<NH><<<bh, Geo<NH>::NP, 0, st>>>(d, o.dth);

@@ -13,9 +13,9 @@
 //                           chunk-end state E_n; E_(n-1) = D_n + d_n E_n
 //           grads_kernel    per chunk: every gradient given S_n and E_n
 //           later_kernel    phase-gradient carry over chunks
-// Chunk products: tcgen05 (tensor memory accumulators, swizzled shared-memory
-// operands) in the forward and dstart; bf16 tiles with ldmatrix fragments and
-// m16n8k16 mma.sync in grads_kernel; fp32 accumulation everywhere.
+// Chunk products: tcgen05 (tensor memory accumulators, 128-byte-swizzled
+// shared-memory operands, one issuing thread, mbarrier commits) in every
+// kernel; fp32 accumulation everywhere.
 // Every kernel is templated on NH, the number of 64-row halves of the state
 // (N = 64 or 128): contractions over the state accumulate the halves' products
 // in one accumulator, products with state-row outputs get one M = 64
@@ -30,73 +30,20 @@ namespace scan2 {
 using bf16 = __nv_bfloat16;
 constexpr int C = 64;        // chunk
 constexpr int P = 64;        // head dim
-constexpr int TS = 72;       // bf16 tile stride (144 B rows: ldmatrix conflict-free)
 // State dim N = 64 NH (NH = 1 or 2 halves of 64 state rows): pairs NP = N / 2,
-// [C][N] bf16 tiles of the chunk-gradient kernel with row stride TSN
-// (272-byte rows at N = 128: ldmatrix conflict-free), [C][pairs] fp32 tables
-// with row stride TW.
+// [C][pairs] fp32 tables with row stride TW.
 template <int NH> struct Geo {
-  static constexpr int N = 64 * NH, NP = 32 * NH, TSN = N + 8, TW = NP + 1;
+  static constexpr int N = 64 * NH, NP = 32 * NH, TW = NP + 1;
 };
-constexpr int FS = 68;       // fp32 tile stride
 constexpr int GW = 8;        // warps per chunk CTA (4 row blocks x 2 column halves)
 static_assert(C == 64 && (C % (4 * GW)) == 0, "warp/token maps assume 64-token chunks");
 
-M4_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-M4_DEV void ldsm_x4(uint32_t (&r)[4], const bf16* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-
-M4_DEV void ldsm_x4_t(uint32_t (&r)[4], const bf16* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-
-M4_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// acc[nt][e] += sum_k A[row0 + g + 8(e>>1)][k] B[k][col0 + 8nt + 2c + (e&1)]
-// (g = lane/4, c = lane%4) over K (multiple of 16), NT (even) n-tiles.
-// A is row-major [m][k] (AT = false) or stored transposed [k][m] (AT = true);
-// B is [n][k] (BT = false) or [k][n] (BT = true). Strides in elements.
-template <int K, int NT, bool AT, bool BT, int SA = TS, int SB = TS>
-M4_DEV void mma_tile(float (&acc)[NT][4], const bf16* A, int row0, const bf16* B, int col0) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k0 = 0; k0 < K; k0 += 16) {
-    uint32_t a[4];
-    if constexpr (!AT)
-      ldsm_x4(a, A + (row0 + (lane & 15)) * SA + k0 + 8 * (lane >> 4));
-    else
-      ldsm_x4_t(a, A + (k0 + (lane & 7) + 8 * (lane >> 4)) * SA + row0 + 8 * ((lane >> 3) & 1));
-#pragma unroll
-    for (int nt = 0; nt < NT; nt += 2) {
-      uint32_t b[4];
-      if constexpr (!BT)
-        ldsm_x4(b, B + (col0 + nt * 8 + (lane & 7) + 8 * (lane >> 4)) * SB + k0 + 8 * ((lane >> 3) & 1));
-      else
-        ldsm_x4_t(b, B + (k0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * SB + col0 + nt * 8 + 8 * (lane >> 4));
-      mma_bf16(acc[nt], a, b[0], b[1]);
-      mma_bf16(acc[nt + 1], a, b[2], b[3]);
-    }
-  }
-}
-
-// Element (r, c) of a 64-column bf16 tile: padded rows of TS (mma.sync path)
-// or 128-byte swizzled rows (tcgen05 descriptors and TMA, tc::sw).
+// Element (r, c) of a 64-column bf16 tile in 128-byte swizzled rows (tcgen05
+// descriptors and TMA, tc::sw).
 template <bool BLK>
 M4_DEV bf16* at(bf16* T, int r, int c) {
-  if constexpr (BLK) return reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(T) + tc::sw(r, c));
-  else return T + r * TS + c;
+  static_assert(BLK, "every tile is swizzled");
+  return reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(T) + tc::sw(r, c));
 }
 
 // D (tensor memory) = A B (+ D when `accumulate`) over K = 64 on the tensor
@@ -107,7 +54,7 @@ M4_DEV void tc_product(uint32_t d, const bf16* A, bool a_mn, const bf16* B, bool
   const uint32_t id = tc::idesc_bf16(64, 64, a_mn ? 1 : 0, b_mn ? 1 : 0);
   const unsigned char* a = reinterpret_cast<const unsigned char*>(A);
   const unsigned char* b = reinterpret_cast<const unsigned char*>(B);
-#pragma unroll
+#pragma unroll 1  // one issuing thread: code size matters more than the loop overhead
   for (int ks = 0; ks < 4; ++ks) {
     const uint64_t ad = a_mn ? tc::sdesc_sw128(a + 2048 * ks, 8192, 1024) : tc::sdesc_sw128(a + 32 * ks, 16, 1024);
     const uint64_t bd = b_mn ? tc::sdesc_sw128(b + 2048 * ks, 8192, 1024) : tc::sdesc_sw128(b + 32 * ks, 16, 1024);
@@ -176,48 +123,6 @@ M4_DEV void reduce_scatter(float (&v)[V], int lane) {
       v[i] = keep + __shfl_xor_sync(0xffffffffu, give, 1 << bit);
     }
   }
-}
-
-template <int NT>
-M4_DEV void zero(float (&acc)[NT][4]) {
-#pragma unroll
-  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-}
-
-// f(row, col, nt, e) over a warp's accumulator tile.
-template <int NT, class F>
-M4_DEV void each(int row0, int col0, F f) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) f(row0 + g + 8 * (e >> 1), col0 + 8 * nt + 2 * c + (e & 1), nt, e);
-}
-
-// Store a warp's accumulator tile, transformed by f(row, col, value), as bf16.
-template <int NT, class F>
-M4_DEV void store_bf16(bf16* T, int row0, int col0, const float (&acc)[NT][4], F f) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = row0 + g + 8 * h, col = col0 + 8 * nt + 2 * c;
-      const __nv_bfloat162 v = __floats2bfloat162_rn(f(r, col, acc[nt][2 * h]), f(r, col + 1, acc[nt][2 * h + 1]));
-      *reinterpret_cast<__nv_bfloat162*>(T + r * TS + col) = v;
-    }
-}
-
-// Store a warp's accumulator tile as fp32 rows of `ld` elements (float2 pairs).
-template <int NT>
-M4_DEV void store_f32(float* dst, int ld, int row0, const float (&acc)[NT][4]) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-      *reinterpret_cast<float2*>(dst + (row0 + g + 8 * h) * ld + 8 * nt + 2 * c) =
-          make_float2(acc[nt][2 * h], acc[nt][2 * h + 1]);
 }
 
 struct Dims {
@@ -407,7 +312,7 @@ M4_DEV void stage_theta(const Dims& d, const StageRef& in, Rows& r, const float*
     r.seg[w * NP + i] = acc;
   }
   __syncthreads();
-#pragma unroll
+#pragma unroll 1  // one inline copy of sincosf
   for (int q = 0; q < NH; ++q) {
     const int i = lane + 32 * q;
     float off = 0.f;
@@ -438,7 +343,7 @@ M4_DEV bf16* qk_at(bf16* T, int stride, int r, int c) {
 
 // build_qk from the stage: rotated, rounded Q / K tiles (either may be null);
 // a stage may be the destination tile itself (each thread reads and writes
-// the same pair). Lane l handles the pairs l + 32 q (columns 2 l + 64 q);
+// the same pair); with both swizzled it must be (in place). Lane l handles the pairs l + 32 q (columns 2 l + 64 q);
 // pairs from `na` on are not rotated (cos / sin tables [token][tw]).
 template <bool SRC_SW, bool DST_SW, int NH>
 M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb, const float* cosv,
@@ -446,6 +351,10 @@ M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb
                      int tw = Geo<NH>::TW) {
   constexpr int PER = C / GW, N = Geo<NH>::N;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  // In place in swizzled tiles: the rows this thread visits (w + 8 k) share
+  // row % 8 = w, so the swizzled byte offset is one per-thread constant plus
+  // 1024 k.
+  const uint32_t swz = uint32_t(w * 128 + (((lane >> 2) ^ w) << 4) + 4 * (lane & 3));
 #pragma unroll
   for (int q = 0; q < NH; ++q) {
     const int n0 = 2 * lane + 64 * q, i = lane + 32 * q;
@@ -455,6 +364,22 @@ M4_DEV void stage_qk(int h, const StageRef& in, const float* qb, const float* kb
     for (int k = 0; k < PER; ++k) {
       const int tt = w + GW * k;
       const float cs = i < na ? cosv[tt * tw + i] : 1.f, sn = i < na ? sinv[tt * tw + i] : 0.f;
+      if constexpr (SRC_SW && DST_SW) {
+        const uint32_t off = swz + 1024u * k;
+        if (Qs) {
+          uint32_t* pq = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(Qs + q * C * 64) + off);
+          const uint32_t cr = *pq;
+          const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
+          *reinterpret_cast<__nv_bfloat162*>(pq) = __floats2bfloat162_rn(q0 * cs - q1 * sn, q1 * cs + q0 * sn);
+        }
+        if (Ks) {
+          uint32_t* pk = reinterpret_cast<uint32_t*>(reinterpret_cast<unsigned char*>(Ks + q * C * 64) + off);
+          const uint32_t br = *pk;
+          const float k0 = round_to<bf16>(lo_f(br) + kb0), k1 = round_to<bf16>(hi_f(br) + kb1);
+          *reinterpret_cast<__nv_bfloat162*>(pk) = __floats2bfloat162_rn(k0 * cs - k1 * sn, k1 * cs + k0 * sn);
+        }
+        continue;
+      }
       if (Qs) {
         const uint32_t cr = ld_u32(stage_row<SRC_SW>(in.c, in.stride, tt, n0));
         const float q0 = round_to<bf16>(lo_f(cr) + qb0), q1 = round_to<bf16>(hi_f(cr) + qb1);
@@ -832,15 +757,17 @@ struct GradOut {
 
 template <int NH>
 struct GradSmem {
-  static constexpr int N = Geo<NH>::N, TSN = Geo<NH>::TSN, TW = Geo<NH>::TW;
-  bf16 Qs[C * TSN];
-  bf16 Ks[C * TSN];
-  bf16 Vs[C * TS];
-  bf16 Dy[C * TS];
-  bf16 Ms[C * TS];   // rd(scores o W), then rd(dY o e^p)
-  bf16 Mt[C * TS];   // rd(d_mixed o W)
-  bf16 Es[N * TS];   // rd(E_n)
-  bf16 Ss[N * TS];   // rd(S_n)
+  static constexpr int N = Geo<NH>::N, TW = Geo<NH>::TW;
+  // tcgen05 operands: 128-byte-swizzled 64-column bf16 tiles on 1024-byte
+  // boundaries (tc::sw); Ms and Mt adjacent (16 KB, the fp32 S_n stage at N = 64).
+  bf16 Qs[NH][C * 64];  // rotated queries, state columns 64 q .. 64 q + 63
+  bf16 Ks[NH][C * 64];
+  bf16 Vs[C * 64];
+  bf16 Dy[C * 64];
+  bf16 Ms[C * 64];      // rd(scores o W), then rd(dY o e^p)
+  bf16 Mt[C * 64];      // rd(d_mixed o W)
+  bf16 Es[NH][64 * 64]; // rd(E_n), state rows 64 q .. 64 q + 63
+  bf16 Ss[NH][64 * 64]; // rd(S_n)
   float theta[C * TW];  // cos of the pair phase, then the pair phase gradient
   float sinv[C * TW];
   // Per-token rows: 0 sum K.(V rd(E)^T), 1 e^p dY.(Q rd(S)), 2 log-decay
@@ -853,13 +780,46 @@ struct GradSmem {
   float bk[4 * N];
   float scratch[C];
   Rows r;
+  uint64_t bar;         // tensor-core commits (three per chunk)
+  uint32_t tmem;
 };
 
-// Every gradient of one chunk given S_n and E_n. Eight warps: warp w owns
-// rows 16 (w % 4) .. +15 and column half w / 4 of every chunk product (32
-// token columns, or N / 2 state columns), so each product tile is 16 x 32 (or
-// 16 x N / 2) per warp; row sums over the two halves and column sums over the
-// four row blocks meet in shared memory.
+// Tensor-memory columns of the chunk-gradient products (M = 64 accumulators).
+template <int NH> struct GradCols {
+  static constexpr int SC = 0, DM = 64;             // commit 1: scores, d_mixed
+  static constexpr int DV = 0, VE = 64;             // commit 2: dV, K rd(E)
+  static constexpr int VN = 0, QS = 64 * NH;        // commit 3: V rd(E)^T (N cols), Q rd(S)
+  static constexpr int GQ = NH == 1 ? 128 : 256;    //           dQ (N cols)
+  static constexpr int GK = GQ + 64 * NH;           //           dK (N cols)
+  static constexpr int ALLOC = NH == 1 ? 256 : 512;
+};
+
+// The m16n8 accumulator fragments of NT 8-column tiles from tensor memory:
+// acc[nt][e] is row t / 4 + 8 (e / 2), column 8 nt + 2 (t % 4) + e % 2 of
+// the warp's lane quarter from column `taddr` (16x256b loads, which place an
+// M = 64 accumulator's values exactly as mma.sync places them).
+template <int NT>
+M4_DEV void tm_frag(uint32_t taddr, float (&acc)[NT][4]) {
+  static_assert(NT % 4 == 0, "whole 32-column loads");
+#pragma unroll
+  for (int g4 = 0; g4 < NT / 4; ++g4) {
+    float v[16];
+    ld_16x256b_x4(taddr + 32 * g4, v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[4 * g4 + k][e] = v[4 * k + e];
+  }
+  tc::wait_ld();
+}
+
+// Every gradient of one chunk given S_n and E_n. The nine chunk products run
+// on the tensor cores (tcgen05, one thread issuing, three commits to an
+// mbarrier; operands are 128-byte-swizzled tiles, accumulators in tensor
+// memory). Eight warps read the accumulators: warp w owns rows 16 (w % 4) ..
+// +15 and column half w / 4 of every product (32 token columns, or N / 2
+// state columns); row sums over the two halves and column sums over the four
+// row blocks meet in shared memory.
 template <int NH>
 __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
     Dims d, const bf16* __restrict__ cq, const bf16* __restrict__ bk, const bf16* __restrict__ x,
@@ -867,14 +827,23 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
     const float* __restrict__ angles, const float* __restrict__ qb, const float* __restrict__ kb,
     const float* __restrict__ phases, const float* __restrict__ starts, const float* __restrict__ carries,
     const bf16* __restrict__ dy, bf16* __restrict__ dx, GradOut o) {
-  constexpr int TH = GW * 32, N = Geo<NH>::N, NP = Geo<NH>::NP, TSN = Geo<NH>::TSN, TW = Geo<NH>::TW;
+  constexpr int TH = GW * 32, N = Geo<NH>::N, NP = Geo<NH>::NP, TW = Geo<NH>::TW;
   constexpr int NTN = 4 * NH;  // 8-column n-tiles of a warp's state-column half
+  using TC = GradCols<NH>;
   extern __shared__ __align__(128) unsigned char raw[];
-  GradSmem<NH>& s = *reinterpret_cast<GradSmem<NH>*>(raw);
+  GradSmem<NH>& s = *reinterpret_cast<GradSmem<NH>*>(align1024(raw));
   const int n = blockIdx.x % d.nch, bh = blockIdx.x / d.nch, b = bh / d.H, h = bh % d.H;
   const int t0 = n * C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rb = warp & 3, half = warp >> 2, row0 = 16 * rb, col0 = 32 * half, colN = (N / 2) * half;
   const int g = lane >> 2, cc = lane & 3;
+  // Byte offset in a swizzled tile of (row, column 8 chunk + 2 cc) for this
+  // thread's fragment rows (row % 8 == g).
+  auto frag_off = [&](int row, int chunk) { return row * 128 + ((chunk ^ g) << 4) + 4 * cc; };
+  if (warp == 0) {
+    tc::tmem_alloc(&s.tmem, TC::ALLOC);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) tc::mbar_init(&s.bar, 1);
   // Every pure copy starts first and lands while the gates, phases and
   // rotations are built: x and dY straight into their tiles, S_n (fp32) into
   // the score tiles (free until the scores; at N = 128 into registers), E_n
@@ -883,9 +852,9 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
   float* Sstage = reinterpret_cast<float*>(s.Ms);  // [64][64] fp32 over Ms and Mt (N = 64)
   // c / b rows in place in Qs / Ks, angle rates in Es, gates and the
   // chunk-start phase in vec (all free until later phases).
-  const StageRef in{s.Qs, s.Ks, TSN, reinterpret_cast<float*>(s.Es), s.vec, s.vec + C, s.vec + 2 * C + 4};
+  const StageRef in{s.Qs[0], s.Ks[0], 0, reinterpret_cast<float*>(s.Es[0]), s.vec, s.vec + C, s.vec + 2 * C + 4};
   float* phase0 = s.vec + 3 * C + 8;
-  stage_prefetch<false, NH>(d, b, h, n, cq, bk, adt, dt, trap_logits, angles, in);
+  stage_prefetch<true, NH>(d, b, h, n, cq, bk, adt, dt, trap_logits, angles, in);
   if (tid < NP) cp4(phase0 + tid, phases + (size_t(bh) * d.nch + n) * NP + tid, true);
   float4 ev[PER], sv[NH == 1 ? 1 : PER];
   {
@@ -894,7 +863,7 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
       const int idx = tid + (k % (16 / GW)) * TH, rr = idx >> 3, c8 = 8 * (idx & 7), t = t0 + rr;
       const bool live = t < d.T;
       const bf16* src = k < 16 / GW ? x : dy;
-      bf16* dst = (k < 16 / GW ? s.Vs : s.Dy) + rr * TS + c8;
+      bf16* dst = at<true>(k < 16 / GW ? s.Vs : s.Dy, rr, c8);
       cp16(reinterpret_cast<float*>(dst),
            reinterpret_cast<const float*>(live ? src + (size_t(b) * d.T + t) * d.H * P + h * P + c8 : src), live);
     }
@@ -918,7 +887,7 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
   __syncthreads();
   stage_theta<NH>(d, in, s.r, phase0, s.theta, s.sinv);
   __syncthreads();
-  stage_qk<false, false, NH>(h, in, qb, kb, s.theta, s.sinv, s.Qs, s.Ks, TSN);
+  stage_qk<true, true, NH>(h, in, qb, kb, s.theta, s.sinv, s.Qs[0], s.Ks[0]);
   __syncthreads();  // the angle stage (Es) is consumed
   // rd(S_n), rd(E_n) as tiles and <E_n, S_n> (fp32 values) for the chunk-end decay.
   {
@@ -931,27 +900,37 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
       else a4 = sv[k];
       const float4 e4 = ev[k];
       const int r = idx / (P / 4), c4 = idx % (P / 4);
-      *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4) = __floats2bfloat162_rn(a4.x, a4.y);
-      *reinterpret_cast<__nv_bfloat162*>(s.Ss + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(a4.z, a4.w);
-      *reinterpret_cast<__nv_bfloat162*>(s.Es + r * TS + 4 * c4) = __floats2bfloat162_rn(e4.x, e4.y);
-      *reinterpret_cast<__nv_bfloat162*>(s.Es + r * TS + 4 * c4 + 2) = __floats2bfloat162_rn(e4.z, e4.w);
+      // r % 8 is the same for every k of this thread; 4 columns = half a chunk.
+      const int off = (r & 63) * 128 + (((c4 >> 1) ^ (r & 7)) << 4) + 8 * (c4 & 1);
+      unsigned char* ss = reinterpret_cast<unsigned char*>(s.Ss[r >> 6]) + off;
+      unsigned char* es = reinterpret_cast<unsigned char*>(s.Es[r >> 6]) + off;
+      *reinterpret_cast<__nv_bfloat162*>(ss) = __floats2bfloat162_rn(a4.x, a4.y);
+      *reinterpret_cast<__nv_bfloat162*>(ss + 4) = __floats2bfloat162_rn(a4.z, a4.w);
+      *reinterpret_cast<__nv_bfloat162*>(es) = __floats2bfloat162_rn(e4.x, e4.y);
+      *reinterpret_cast<__nv_bfloat162*>(es + 4) = __floats2bfloat162_rn(e4.z, e4.w);
       part = fmaf(a4.x, e4.x, fmaf(a4.y, e4.y, fmaf(a4.z, e4.z, fmaf(a4.w, e4.w, part))));
     }
     part = warp_sum(part);
     if (lane == 0) s.scratch[warp] = part;
   }
-  __syncthreads();
-  // Scores Q K^T and d_mixed dY V^T (rows t, this warp's 32 columns s) in
-  // registers. Each element gives the two masked tiles rd(scores o W) and
+  tc_publish();
+  const uint32_t tm = s.tmem, tl = tmem_lane_base(tm);
+  if (tid == 0) {
+#pragma unroll
+    for (int q = 0; q < NH; ++q) tc_product(tm + TC::SC, s.Qs[q], false, s.Ks[q], false, q > 0);  // Q K^T
+    tc_product(tm + TC::DM, s.Dy, false, s.Vs, false);                                          // dY V^T
+    tc::commit(&s.bar);
+  }
+  bool ok = tc_wait(&s.bar, 0);
+  // Scores Q K^T and d_mixed dY V^T (rows t, this warp's 32 columns s) from
+  // tensor memory. Each element gives the two masked tiles rd(scores o W) and
   // rd(d_mixed o W) and the per-token sums of d_weights = d_mixed o scores:
   //   row t:    sum_{s<t} dw W,  column s: sum_{u>s} dw W and sum_{u>s} dw decay,
   // with W = decay(t, s) scale_s below the diagonal and gamma_t on it.
   {
     float sc[4][4], dm[4][4];
-    zero(sc);
-    zero(dm);
-    mma_tile<N, 4, false, false, TSN, TSN>(sc, s.Qs, row0, s.Ks, col0);
-    mma_tile<P, 4, false, false>(dm, s.Dy, row0, s.Vs, col0);
+    tm_frag<4>(tl + TC::SC + col0, sc);
+    tm_frag<4>(tl + TC::DM + col0, dm);
     float rsum[2] = {0.f, 0.f}, c1[4][2], c2[4][2];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
@@ -984,8 +963,11 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
             c2[nt][e] = fmaf(dw, dec, c2[nt][e]);
           }
         }
-        *reinterpret_cast<__nv_bfloat162*>(s.Ms + t * TS + col0 + nt * 8 + 2 * cc) = __floats2bfloat162_rn(ms[0], ms[1]);
-        *reinterpret_cast<__nv_bfloat162*>(s.Mt + t * TS + col0 + nt * 8 + 2 * cc) = __floats2bfloat162_rn(mt[0], mt[1]);
+        const int off = frag_off(t, (col0 >> 3) + nt);
+        *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<unsigned char*>(s.Ms) + off) =
+            __floats2bfloat162_rn(ms[0], ms[1]);
+        *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<unsigned char*>(s.Mt) + off) =
+            __floats2bfloat162_rn(mt[0], mt[1]);
       }
     }
 #pragma unroll
@@ -1011,14 +993,19 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
         }
       }
   }
-  __syncthreads();
+  tc_publish();
+  if (tid == 0 && ok) {
+    tc_product(tm + TC::DV, s.Ms, true, s.Dy, true);                                          // rd(Sc o W)^T dY
+#pragma unroll
+    for (int q = 0; q < NH; ++q) tc_product(tm + TC::VE, s.Ks[q], false, s.Es[q], true, q > 0);  // K rd(E)
+    tc::commit(&s.bar);
+  }
+  ok = ok && tc_wait(&s.bar, 1);
   // dV = rd(Sc o W)^T dY + src o (K rd(E)) -> dx (rows s, this warp's 32 columns p).
   {
     float acc[4][4], ve[4][4];
-    zero(acc);
-    zero(ve);
-    mma_tile<C, 4, true, true>(acc, s.Ms, row0, s.Dy, col0);
-    mma_tile<N, 4, false, true, TSN, TS>(ve, s.Ks, row0, s.Es, col0);
+    tm_frag<4>(tl + TC::DV + col0, acc);
+    tm_frag<4>(tl + TC::VE + col0, ve);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int sr = row0 + g + 8 * hf, t = t0 + sr;
@@ -1033,20 +1020,31 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
       }
     }
   }
-  // dQ, dK (rows t / s, this warp's N / 2 columns n) in registers.
-  float gq[NTN][4], gk[NTN][4];
-  zero(gq);
-  zero(gk);
-  mma_tile<C, NTN, false, true, TS, TSN>(gq, s.Mt, row0, s.Ks, colN);   // rd(Dm o W) K
-  mma_tile<C, NTN, true, true, TS, TSN>(gk, s.Mt, row0, s.Qs, colN);    // rd(Dm o W)^T Q
-  __syncthreads();  // Ms is rewritten below
-  for (int idx = tid; idx < C * P / 2; idx += TH) {
-    const int tt = idx / (P / 2), c2 = idx % (P / 2);
-    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(s.Dy + tt * TS + 2 * c2);
-    *reinterpret_cast<__nv_bfloat162*>(s.Ms + tt * TS + 2 * c2) =
-        __floats2bfloat162_rn(__low2float(v) * s.r.ept[tt], __high2float(v) * s.r.ept[tt]);
+  // rd(dY o e^p) over Ms (its product has completed): thread (warp w, lane)
+  // visits rows w + 8 k (row % 8 == w), columns 2 lane, 2 lane + 1.
+  {
+    const int swz = warp * 128 + (((lane >> 2) ^ warp) << 4) + 4 * (lane & 3);
+#pragma unroll
+    for (int k = 0; k < C / GW; ++k) {
+      const int tt = warp + GW * k, off = swz + 1024 * k;
+      const __nv_bfloat162 v =
+          *reinterpret_cast<const __nv_bfloat162*>(reinterpret_cast<const unsigned char*>(s.Dy) + off);
+      *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<unsigned char*>(s.Ms) + off) =
+          __floats2bfloat162_rn(__low2float(v) * s.r.ept[tt], __high2float(v) * s.r.ept[tt]);
+    }
   }
-  __syncthreads();
+  tc_publish();
+  if (tid == 0 && ok) {
+#pragma unroll
+    for (int q = 0; q < NH; ++q) {
+      tc_product(tm + TC::GQ + 64 * q, s.Mt, false, s.Ks[q], true);         // rd(Dm o W) K
+      tc_product(tm + TC::GQ + 64 * q, s.Ms, false, s.Ss[q], false, true);  // + rd(dY e^p) rd(S)^T
+      tc_product(tm + TC::GK + 64 * q, s.Mt, true, s.Qs[q], true);          // rd(Dm o W)^T Q
+      tc_product(tm + TC::VN + 64 * q, s.Vs, false, s.Es[q], false);        // V rd(E)^T
+      tc_product(tm + TC::QS, s.Qs[q], false, s.Ss[q], true, q > 0);        // Q rd(S)
+    }
+    tc::commit(&s.bar);
+  }
   // The raw c / b pairs of this thread's accumulator rows for the rotation
   // backward: at N = 128 loaded before the next products so their latency
   // hides (the kernel runs one CTA per SM there; registers are free), at
@@ -1065,13 +1063,16 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
     }
   };
   if constexpr (NH == 2) load_raw();
-  mma_tile<P, NTN, false, false>(gq, s.Ms, row0, s.Ss, colN);  // rd(dY e^p) rd(S)^T
+  ok = ok && tc_wait(&s.bar, 0);
+  // dK (rows s, this warp's N / 2 columns n) from tensor memory; dQ is read
+  // just before the rotation backward (fewer fragments live at once).
+  float gk[NTN][4];
+  tm_frag<NTN>(tl + TC::GK + colN, gk);
   {
     float dsrc[2] = {0.f, 0.f}, inh_dot[2] = {0.f, 0.f};
     {
       float vn[NTN][4];
-      zero(vn);
-      mma_tile<P, NTN, false, false>(vn, s.Vs, row0, s.Es, colN);  // V rd(E)^T (rows s, cols n)
+      tm_frag<NTN>(tl + TC::VN + colN, vn);  // V rd(E)^T (rows s, cols n)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int sr = row0 + g + 8 * hf;
@@ -1080,15 +1081,17 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
         for (int nt = 0; nt < NTN; ++nt)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const float kv = __bfloat162float(s.Ks[sr * TSN + colN + nt * 8 + 2 * cc + e]);
+            const int ncol = colN + nt * 8;  // + 2 cc + e
+            const bf16* kt = s.Ks[ncol >> 6];
+            const float kv = __bfloat162float(*reinterpret_cast<const bf16*>(
+                reinterpret_cast<const unsigned char*>(kt) + frag_off(sr, (ncol & 63) >> 3) + 2 * e));
             dsrc[hf] = fmaf(kv, vn[nt][2 * hf + e], dsrc[hf]);
             gk[nt][2 * hf + e] = fmaf(src, vn[nt][2 * hf + e], gk[nt][2 * hf + e]);
           }
       }
     }
     float ve[4][4];
-    zero(ve);
-    mma_tile<N, 4, false, true, TSN, TS>(ve, s.Qs, row0, s.Ss, col0);  // Q rd(S) (rows t, cols p)
+    tm_frag<4>(tl + TC::QS + col0, ve);  // Q rd(S) (rows t, cols p)
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int t = row0 + g + 8 * hf;
@@ -1096,8 +1099,9 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
       for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e)
-          inh_dot[hf] = fmaf(__bfloat162float(s.Dy[t * TS + col0 + nt * 8 + 2 * cc + e]), ve[nt][2 * hf + e],
-                             inh_dot[hf]);
+          inh_dot[hf] = fmaf(__bfloat162float(*reinterpret_cast<const bf16*>(
+                                 reinterpret_cast<const unsigned char*>(s.Dy) + frag_off(t, (col0 >> 3) + nt) + 2 * e)),
+                             ve[nt][2 * hf + e], inh_dot[hf]);
     }
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
@@ -1127,6 +1131,8 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
   };
   if constexpr (NH == 2) load_rates();
   if constexpr (NH == 1) load_raw();
+  float gq[NTN][4];
+  tm_frag<NTN>(tl + TC::GQ + colN, gq);
   // Rotation backward in registers: the accumulators hold each pair (2i, 2i+1)
   // on one thread. Pre-rotation gradients to workspace, the pair phase
   // gradient into theta (same element, read then written by this thread),
@@ -1282,6 +1288,9 @@ __global__ void __launch_bounds__(GW * 32, NH == 1 ? 2 : 1) grads_kernel(
       }
     }
   }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tm, TC::ALLOC);
 }
 
 // In place over chunks: dth[n] <- sum over chunks m > n of the chunk totals
