@@ -11,15 +11,19 @@
 //                    updates; writes S at every 16-token sub-chunk start and
 //                    C at every 64-token chunk start, and the final state.
 //   memread_solve    one warp per (batch, head, 16-token sub-chunk): per token
-//                    E <- lam E + beta k k^T in shared memory, then a
-//                    register-blocked 64x64 Cholesky of E + diag(floor) on a
-//                    4x8 cyclic lane grid with the query as a bordered row
-//                    (gives w = L^-1 q for free), a blocked back-substitution
-//                    y = L^-T w with 8x8 diagonal-block inverses, and a
-//                    coalesced 128-bit streaming store of L with those
-//                    diagonal blocks inverted (their diagonals are the
-//                    reciprocal pivots mamba4_fused.py:78-113 keeps), so the
-//                    backward's substitutions need no inversion.
+//                    E <- lam E + beta k k^T in shared memory, then a block
+//                    LDL^T of E + diag(floor) with 8x8 diagonal blocks, held
+//                    in m16n8k8 accumulator fragments: the panel and trailing
+//                    products on the tensor cores (three-term TF32), the
+//                    diagonal blocks inverted by a Gauss-Jordan sweep with
+//                    2x2 pivots (ldl_tiles.cuh); the forward substitution
+//                    u = L^-1 q interleaved with the column blocks, the back
+//                    substitution y = L^-T D^-1 u after them, and a coalesced
+//                    128-bit streaming store of the factor (unit L, D^-1
+//                    blocks) for the backward, whose substitutions need no
+//                    inversion. The reference factorises the same matrix by
+//                    Cholesky (mamba4_fused.py:78-113); both give A^-1 q to
+//                    float32 rounding.
 //   memread_output   per (batch, 64-token chunk, head): output =
 //                    ((Y K^T) o W) V + diag(e^P) Y C0^T (mamba4_fused.py:439-447).
 //   backward         rhs g (chunk products), z = A^-1 g from the stored
@@ -27,6 +31,8 @@
 //                    and every input gradient in chunk form; the algebra is
 //                    written out in oracle/memread.py:chunked_backward.
 #include "common.cuh"
+#include "tf32.cuh"
+#include "ldl_tiles.cuh"
 
 namespace m4 {
 namespace mem {
@@ -34,11 +40,8 @@ namespace mem {
 constexpr int KD = 64;         // key dimension
 constexpr int CH = 64;         // chunk (epilogue / backward products)
 constexpr int SUB = 16;        // tokens per solve warp (state stride)
-constexpr int LSTRIDE = 72 * 32;  // floats of one token's stored factor (36 float2 per lane)
+constexpr int LSTRIDE = 72 * 32;  // floats of one stored factor (18 float4 per lane)
 constexpr int WARPS = 4;       // solve warps per CTA
-#ifndef M4_SOLVE_MINB
-#define M4_SOLVE_MINB 4
-#endif
 #ifndef M4_STATES_MINB
 #define M4_STATES_MINB 2
 #endif
@@ -225,7 +228,8 @@ __global__ void __launch_bounds__(256, M4_STATES_MINB) states_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Per-token solve warps: lane-tile layout of the 64x64 lower factor.
+// Scalar solve warps (memread_decode, spd_solve): lane-tile layout of the
+// 64x64 lower Cholesky factor.
 // Lane l = a*8 + b (a in 0..3, b in 0..7) owns rows a + 4m and columns b + 8n,
 // stored as row pairs (a + 8p, a + 4 + 8p) x column b + 8n for n <= p <= 7:
 // 36 float2 per lane, index pair_of(p, n). The 8x8 diagonal block J is the
@@ -493,140 +497,120 @@ M4_DEV void factor_all(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], Solve
 }
 
 // ---------------------------------------------------------------------------
-// memread_solve: per-token Cholesky factor + solve, L stored for backward.
+// memread_solve with the factorisation on the tensor cores: a block LDL^T of
+// each token's matrix in MMA accumulator fragments (ldl_tiles.cuh). One warp
+// per 16-token sub-chunk as above; the running evidence is kept in shared
+// memory in the stored factor's fragment layout, so the per-token update
+// E = lam E + beta k k^T touches each lane's own entries.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
+struct TileSmem {
+  float4 E[ldl::NQ][32];  // running evidence (stored-factor layout)
+  float k[KD], q[KD], fl[KD], v[KD], y[KD];
+};
+
+M4_DEV float2 ld2f(const float* p) { return *reinterpret_cast<const float2*>(p); }
+
+// One warp per CTA, 168 registers (twelve warps per SM): more warps per SM
+// force spills of the fragment registers and run slower.
+__global__ void __launch_bounds__(32, 12) solve_kernel(
     int B, int T, int H, const float* __restrict__ keys, const float* __restrict__ queries,
     const float* __restrict__ beta, const float* __restrict__ log_decay,
     const float* __restrict__ floor_, const float* __restrict__ s_start,
     float* __restrict__ Lst, float* __restrict__ Y, float* __restrict__ variance) {
-  extern __shared__ __align__(16) unsigned char solve_raw[];
-  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(solve_raw);
+  extern __shared__ __align__(16) unsigned char tsolve_raw[];
+  TileSmem* smem_all = reinterpret_cast<TileSmem*>(tsolve_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int a = lane >> 3, b = lane & 7;
+  const int g = lane >> 2, t = lane & 3;
   const int Tp = (T + CH - 1) / CH * CH, nsub = Tp / SUB;
-  const int wid = blockIdx.x * WARPS + warp;
+  const int wid = blockIdx.x;
   if (wid >= B * H * nsub) return;
-  SolveSmem& sm = smem_all[warp];
+  TileSmem& sm = smem_all[warp];
   const int sub = wid % nsub, bh = wid / nsub, bb = bh / H, h = bh % H;
-
   {
     const float* src = s_start + (size_t(bh) * nsub + sub) * KD * KD;
 #pragma unroll
-    for (int q = 0; q < NPAIR; ++q) {
-      const int p = pair_p(q), n = pair_n(q);
-      float* e = reinterpret_cast<float*>(&sm.E[q >> 1][lane]) + 2 * (q & 1);
-      e[0] = src[(a + 8 * p) * KD + b + 8 * n];
-      e[1] = src[(a + 4 + 8 * p) * KD + b + 8 * n];
+    for (int q = 0; q < 16; ++q) {
+      const int r0 = 16 * ldl::slot_R(q) + g, c0 = 8 * ldl::slot_c(q) + 2 * t;
+      const float2 lo = ld2f(src + r0 * KD + c0), hi = ld2f(src + (r0 + 8) * KD + c0);
+      sm.E[q][lane] = make_float4(lo.x, lo.y, hi.x, hi.y);
     }
-    if (a == 0) {
 #pragma unroll
-      for (int n = 0; n < 8; ++n) sm.flC[b * KS + n] = floor_[h * KD + b + 8 * n];
+    for (int q = 16; q < ldl::NQ; ++q) {
+      const int R0 = 2 * (q - 16), R1 = R0 + 1;
+      const float2 e0 = ld2f(src + (16 * R0 + 8 + g) * KD + 8 * (2 * R0 + 1) + 2 * t);
+      const float2 e1 = ld2f(src + (16 * R1 + 8 + g) * KD + 8 * (2 * R1 + 1) + 2 * t);
+      sm.E[q][lane] = make_float4(e0.x, e0.y, e1.x, e1.y);
     }
+    sm.fl[lane] = floor_[h * KD + lane];
+    sm.fl[lane + 32] = floor_[h * KD + lane + 32];
   }
   __syncwarp();
 
   for (int tt = 0; tt < SUB; ++tt) {
-    const int t = sub * SUB + tt;
-    const bool live = t < T;
+    const int tok = sub * SUB + tt;
+    const bool live = tok < T;
     {
       const int l = lane & 15;
-      const float* src = (lane < 16 ? keys : queries) + ((size_t(bb) * T + t) * H + h) * KD + 4 * l;
-      const float4 v4 = live ? ld4(src) : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+      const float* src = (lane < 16 ? keys : queries) + ((size_t(bb) * T + tok) * H + h) * KD + 4 * l;
+      st4((lane < 16 ? sm.k : sm.q) + 4 * l, live ? ld4(src) : make_float4(0.f, 0.f, 0.f, 0.f));
+    }
+    const float bet = live ? beta[(size_t(bb) * T + tok) * H + h] : 0.f;
+    const float lam = live ? expf(log_decay[(size_t(bb) * T + tok) * H + h]) : 1.f;
+    __syncwarp();
+
+    ldl::Tiles F;
+    {
+      float kr[4][2];
+      float2 kc[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = 4 * l + e;
-        if (lane < 16) {
-          reinterpret_cast<float*>(sm.u.f.kP)[((i & 3) * PS + (i >> 3)) * 2 + ((i >> 2) & 1)] = vv[e];
-          sm.u.f.kC[(i & 7) * KS + (i >> 3)] = vv[e];
+      for (int R = 0; R < 4; ++R) {
+        kr[R][0] = bet * sm.k[16 * R + g];
+        kr[R][1] = bet * sm.k[16 * R + 8 + g];
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) kc[c] = ld2f(&sm.k[8 * c + 2 * t]);
+#pragma unroll
+      for (int q = 0; q < ldl::NQ; ++q) {
+        float4 e = sm.E[q][lane];
+        if (q < 16) {
+          const int R = ldl::slot_R(q), c = ldl::slot_c(q);
+          e = make_float4(fmaf(kr[R][0], kc[c].x, lam * e.x), fmaf(kr[R][0], kc[c].y, lam * e.y),
+                          fmaf(kr[R][1], kc[c].x, lam * e.z), fmaf(kr[R][1], kc[c].y, lam * e.w));
         } else {
-          sm.u.f.qC[(i & 7) * KS + (i >> 3)] = vv[e];
+          const int R0 = 2 * (q - 16), R1 = R0 + 1;
+          e = make_float4(fmaf(kr[R0][1], kc[2 * R0 + 1].x, lam * e.x), fmaf(kr[R0][1], kc[2 * R0 + 1].y, lam * e.y),
+                          fmaf(kr[R1][1], kc[2 * R1 + 1].x, lam * e.z), fmaf(kr[R1][1], kc[2 * R1 + 1].y, lam * e.w));
         }
+        sm.E[q][lane] = e;
+        ldl::set4(F, q, e);
       }
     }
-    const float bet = live ? beta[(size_t(bb) * T + t) * H + h] : 0.f;
-    const float lam = live ? expf(log_decay[(size_t(bb) * T + t) * H + h]) : 1.f;
-    __syncwarp();
-
-    float2 A[NPAIR];
-    float wr[8];
+    // Floor on the diagonal: entries (16R + g, 16R + g) of tile (R, 2R) and
+    // (16R + 8 + g, ...) of tile (R, 2R + 1), on the lanes with 2t or 2t + 1 = g.
+#pragma unroll
+    for (int R = 0; R < 4; ++R) {
+      const float f0 = sm.fl[16 * R + g], f1 = sm.fl[16 * R + 8 + g];
+      F[ldl::ti(R, 2 * R)][0] += g == 2 * t ? f0 : 0.f;
+      F[ldl::ti(R, 2 * R)][1] += g == 2 * t + 1 ? f0 : 0.f;
+      F[ldl::ti(R, 2 * R + 1)][2] += g == 2 * t ? f1 : 0.f;
+      F[ldl::ti(R, 2 * R + 1)][3] += g == 2 * t + 1 ? f1 : 0.f;
+    }
+    ldl::Forward fw;
+    fw.uv = 0.f;
+    fw.r = sm.q;
+    fw.vsm = sm.v;
+    ldl::factor_forward(F, fw, g, t);
+    const float var = warp_sum(fw.uv);
     {
-      float2 kr[8];
-      float kc[8];
+      float* dst = Lst + (size_t(bh) * Tp + tok) * LSTRIDE;
 #pragma unroll
-      for (int p = 0; p < 8; p += 2) {
-        const float4 v = *reinterpret_cast<const float4*>(&sm.u.f.kP[a * PS + p]);
-        kr[p] = make_float2(bet * v.x, bet * v.y);
-        kr[p + 1] = make_float2(bet * v.z, bet * v.w);
-      }
-#pragma unroll
-      for (int n = 0; n < 8; n += 4) {
-        const float4 k4 = ld4(&sm.u.f.kC[b * KS + n]);
-        kc[n] = k4.x; kc[n + 1] = k4.y; kc[n + 2] = k4.z; kc[n + 3] = k4.w;
-      }
-#pragma unroll
-      for (int q4 = 0; q4 < NPAIR / 2; ++q4) {
-        const float4 e = sm.E[q4][lane];
-        const int q0 = 2 * q4, q1 = 2 * q4 + 1;
-        const float2 e0 = fma2(kr[pair_p(q0)], kc[pair_n(q0)], make_float2(lam * e.x, lam * e.y));
-        const float2 e1 = fma2(kr[pair_p(q1)], kc[pair_n(q1)], make_float2(lam * e.z, lam * e.w));
-        sm.E[q4][lane] = make_float4(e0.x, e0.y, e1.x, e1.y);
-        A[q0] = e0;
-        A[q1] = e1;
-      }
+      for (int q = 0; q < ldl::NQ; ++q) st4_stream(dst + (q * 32 + lane) * 4, ldl::get4(F, q));
     }
-    // Floor on the diagonal (pair (n, n): .x if b == a, .y if b == a + 4) and
-    // the query as the bordered row (rows 64.., lanes a == 0).
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const float f = sm.flC[b * KS + n];
-      A[pair_of(n, n)].x += (b == a) ? f : 0.f;
-      A[pair_of(n, n)].y += (b == a + 4) ? f : 0.f;
-      wr[n] = a == 0 ? sm.u.f.qC[b * KS + n] : 0.f;
-    }
-
-    float rc[8];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) rc[n] = 0.f;
-    factor_all<0>(A, wr, rc, sm, a, b);
-
-    float vpart = 0.f;
-    if (a == 0) {
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        const float wv = wr[n] * rc[n];
-        sm.w[b + 8 * n] = wv;
-        vpart = fmaf(wv, wv, vpart);
-      }
-    }
-    const float var = warp_sum(vpart);
-
-    // Scale to L; reciprocal pivot on the diagonal; zero the upper triangle.
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-#pragma unroll
-      for (int p = n; p < 8; ++p) {
-        A[pair_of(p, n)].x *= rc[n];
-        A[pair_of(p, n)].y *= rc[n];
-      }
-      float2& d = A[pair_of(n, n)];
-      d.x = (b == a) ? rc[n] : (a < b ? 0.f : d.x);
-      d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
-    }
-    invert_blocks(A, sm, lane, a, b);
-    diag_to_inverse(A, sm, a, b);
-    {
-      float* dst = Lst + (size_t(bh) * Tp + t) * LSTRIDE;
-#pragma unroll
-      for (int q4 = 0; q4 < NPAIR / 2; ++q4)
-        st4_stream(dst + (q4 * 32 + lane) * 4,
-                   make_float4(A[2 * q4].x, A[2 * q4].y, A[2 * q4 + 1].x, A[2 * q4 + 1].y));
-    }
-    back_substitute(A, sm.w, sm.y, a, b);
     __syncwarp();
-    if (lane < 16) st4(Y + (size_t(bh) * Tp + t) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
-    if (live && lane == 0) variance[(size_t(bb) * T + t) * H + h] = var;
+    ldl::back_solve(F, sm.v, sm.y, g, t);
+    __syncwarp();
+    if (lane < 16) st4(Y + (size_t(bh) * Tp + tok) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
+    if (live && lane == 0) variance[(size_t(bb) * T + tok) * H + h] = var;
     __syncwarp();
   }
 }
@@ -636,7 +620,7 @@ __global__ void __launch_bounds__(32 * WARPS, M4_SOLVE_MINB) solve_kernel(
 // (selective_decode, lm/kernels/mamba4.py:341-355). One warp per (b, h):
 //   E' = lam E + beta k k^T, C' = lam C + beta v k^T,
 //   y = (E' + diag(floor))^-1 q, output = C' y, variance = q . y,
-// with the solve kernel's lane-tiled factorization (bordered query row) and
+// with the scalar lane-tiled Cholesky factorization (bordered query row) and
 // blocked back-substitution. E' and C' may overwrite E and C: the warp reads
 // all of E before writing E', and each row of C before writing that row.
 // ---------------------------------------------------------------------------
@@ -800,12 +784,12 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
 // ---------------------------------------------------------------------------
 // spd_solve: standalone SPD solves precision @ y = rhs (spd_solve,
 // lm/kernels/mamba4.py:187-218) for `count` matrices of order dim <= 64.
-// One warp per matrix with the solve kernel's lane layout. Only the lower
+// One warp per matrix with the scalar lane-tile layout. Only the lower
 // triangle of each row-major [dim][dim] matrix is read (the upper entries of
 // the register tiles are mirrored from it); orders below 64 are padded with
 // an identity block and a zero right-hand side, which solves to zero. The
-// factor is stored in the memory read's layout (LSTRIDE floats per matrix,
-// 8x8 diagonal blocks inverted) for the backward.
+// factor is stored in the lane-tile layout (LSTRIDE floats per matrix, 8x8
+// diagonal blocks inverted) for the backward.
 // ---------------------------------------------------------------------------
 M4_DEV float spd_entry(const float* M, int dim, int r, int c) {
   if (r >= dim || c >= dim) return r == c ? 1.f : 0.f;
@@ -924,23 +908,6 @@ __global__ void __launch_bounds__(32 * WARPS) spd_bwd_kernel(
 constexpr int LD = 68;    // tile stride in floats (conflict-free A fragments)
 constexpr int CT = 256;   // threads per chunk CTA
 constexpr int CTG = 512;  // threads per chunk-gradient CTA (16 warps: 4 row blocks x 4 column quarters)
-
-// High part of the two-term split on the FMA pipe (Veltkamp splitting with
-// the constant 2^13 + 1): x rounded to 11 significant bits, exactly a tf32
-// value, with x - hi exact. Three FP32 operations instead of one ALU
-// conversion: these kernels saturate the ALU pipe and leave the FMA pipe idle.
-M4_DEV uint32_t split_hi(float x) {
-  const float t = __fmul_rn(x, 8193.f);
-  return __float_as_uint(__fsub_rn(t, __fsub_rn(t, x)));
-}
-
-M4_DEV void mma_tf32(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
 
 // acc[nt][e] += sum_k A(row0 + g + 8(e>>1), k) B(k, col0 + 8nt + 2c + (e&1)),
 // g = lane/4, c = lane%4, through element accessors fa(row, k), fb(k, col).
@@ -1147,54 +1114,48 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
 // ---------------------------------------------------------------------------
 // Backward kernels.
 // ---------------------------------------------------------------------------
-// zsolve_kernel: z_t = A_t^-1 g_t from the stored factor (diagonal blocks
-// already inverted; one warp per token at a time, 16 tokens per warp): two
-// blocked substitutions. The next token's factor and right-hand side
-// stream into shared memory (cp.async; the evidence buffer of the forward's
-// layout is free here) while the current token is solved.
+// zsolve_kernel: z_t = A_t^-1 g_t from the tensor-core solve's stored
+// factor (unit lower L, D^-1 blocks), the factor and right-hand side of the
+// next token streaming into shared memory while the current one is solved.
 __global__ void __launch_bounds__(32 * WARPS, 4) zsolve_kernel(
     int B, int T, int H, const float* __restrict__ Lst, const float* __restrict__ G,
     float* __restrict__ Z) {
-  extern __shared__ __align__(16) unsigned char zsolve_raw[];
-  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(zsolve_raw);
+  extern __shared__ __align__(16) unsigned char tzsolve_raw[];
+  TileSmem* smem_all = reinterpret_cast<TileSmem*>(tzsolve_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int a = lane >> 3, b = lane & 7;
+  const int g = lane >> 2, t = lane & 3;
   const int Tp = (T + CH - 1) / CH * CH, nsub = Tp / SUB;
   const int wid = blockIdx.x * WARPS + warp;
   if (wid >= B * H * nsub) return;
-  SolveSmem& sm = smem_all[warp];
+  TileSmem& sm = smem_all[warp];
   const int sub = wid % nsub, bh = wid / nsub;
-  auto prefetch = [&](int t) {
-    const float* src = Lst + (size_t(bh) * Tp + t) * LSTRIDE;
+  auto prefetch = [&](int tok) {
+    const float* src = Lst + (size_t(bh) * Tp + tok) * LSTRIDE;
 #pragma unroll
-    for (int q4 = 0; q4 < NPAIR / 2; ++q4)
-      cp16(reinterpret_cast<float*>(&sm.E[q4][lane]), src + (q4 * 32 + lane) * 4, true);
-    if (lane < 16) cp16(&sm.flC[4 * lane], G + (size_t(bh) * Tp + t) * KD + 4 * lane, true);
+    for (int q = 0; q < ldl::NQ; ++q)
+      cp16(reinterpret_cast<float*>(&sm.E[q][lane]), src + (q * 32 + lane) * 4, true);
+    if (lane < 16) cp16(&sm.k[4 * lane], G + (size_t(bh) * Tp + tok) * KD + 4 * lane, true);
     cp_commit();
   };
   prefetch(sub * SUB);
   for (int tt = 0; tt < SUB; ++tt) {
-    const int t = sub * SUB + tt;
+    const int tok = sub * SUB + tt;
     cp_wait_group<0>();
     __syncwarp();
-    float2 L[NPAIR];
+    ldl::Tiles F;
 #pragma unroll
-    for (int q4 = 0; q4 < NPAIR / 2; ++q4) {
-      const float4 v4 = sm.E[q4][lane];
-      L[2 * q4] = make_float2(v4.x, v4.y);
-      L[2 * q4 + 1] = make_float2(v4.z, v4.w);
-    }
-    if (lane < 16) st4(&sm.y[4 * lane], ld4(&sm.flC[4 * lane]));
+    for (int q = 0; q < ldl::NQ; ++q) ldl::set4(F, q, sm.E[q][lane]);
+    if (lane < 16) st4(&sm.q[4 * lane], ld4(&sm.k[4 * lane]));
     __syncwarp();  // the buffers are refilled below
-    if (tt + 1 < SUB) prefetch(t + 1);
-    forward_substitute(L, sm.y, sm.w, a, b);
-    back_substitute(L, sm.w, sm.y, a, b);
+    if (tt + 1 < SUB) prefetch(tok + 1);
+    ldl::forward_solve(F, sm.q, sm.v, g, t);
     __syncwarp();
-    if (lane < 16) st4(Z + (size_t(bh) * Tp + t) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
+    ldl::back_solve(F, sm.v, sm.y, g, t);
+    __syncwarp();
+    if (lane < 16) st4(Z + (size_t(bh) * Tp + tok) * KD + 4 * lane, ld4(&sm.y[4 * lane]));
     __syncwarp();
   }
 }
-
 
 // carry_kernel: per (batch, head), reverse over chunks:
 //   X_S = -sum_t e^(P_t) z_t y_t^T, X_C = sum_t e^(P_t) dO_t y_t^T,
@@ -1566,10 +1527,10 @@ int forward(const M4MemDims& d, const float* keys, const float* values, const fl
   states_kernel<P><<<bh, 256, 0, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, init_s, init_c,
                                        Ss, Cs, s_fin, c_fin);
   const int warps = bh * z.nsub;
-  const int ssm = int(sizeof(SolveSmem) * WARPS);
+  const int ssm = int(sizeof(TileSmem));
   cudaFuncSetAttribute(solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm);
-  solve_kernel<<<(warps + WARPS - 1) / WARPS, 32 * WARPS, ssm, st>>>(
-      z.B, z.T, z.H, keys, queries, beta, log_decay, floor_, Ss, Lst, Y, var);
+  solve_kernel<<<warps, 32, ssm, st>>>(z.B, z.T, z.H, keys, queries, beta, log_decay, floor_, Ss, Lst, Y,
+                                            var);
   const size_t osm = output_smem<P>();
   cudaFuncSetAttribute(output_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(osm));
   output_kernel<P><<<bh * z.nch, CT, osm, st>>>(z.B, z.T, z.H, keys, values, beta, log_decay, Y, Cs, out);
@@ -1598,7 +1559,7 @@ int backward(const M4MemDims& d, const float* keys, const float* values, const f
   rhs_kernel<P><<<bh * z.nch, CT, rsm, st>>>(z.B, z.T, z.H, keys, values, queries, beta, log_decay, Cs,
                                               d_out, d_var, G);
   const int warps = bh * z.nsub;
-  const int ssm = int(sizeof(SolveSmem) * WARPS);
+  const int ssm = int(sizeof(TileSmem) * WARPS);
   cudaFuncSetAttribute(zsolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm);
   zsolve_kernel<<<(warps + WARPS - 1) / WARPS, 32 * WARPS, ssm, st>>>(z.B, z.T, z.H, Lst, G, Zb);
   const size_t csm = carry_smem<P>();
