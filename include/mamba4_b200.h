@@ -56,7 +56,7 @@ typedef struct {
   int value_dim;  /* P = 64 or 128 */
 } M4MemDims;
 
-/* Bytes of the forward residual (stored Cholesky factors, solutions and
+/* Bytes of the forward residual (stored LDL^T factors, solutions and
  * chunk-start statistics) that m4_memread_bwd consumes. The reference keeps
  * the same residuals under the remat name "memory_solve"
  * (lm/kernels/mamba4_fused.py:329-337). */

@@ -546,16 +546,25 @@ __global__ void __launch_bounds__(32, 12) solve_kernel(
   }
   __syncwarp();
 
+  // Key / query (lanes 0..15 / 16..31, four entries each), beta and
+  // log-decay of a token, loaded one token ahead of its use.
+  const float* kq = (lane < 16 ? keys : queries) + (size_t(bb) * T * H + h) * KD + 4 * (lane & 15);
+  const float* bl = (lane < 16 ? beta : log_decay) + size_t(bb) * T * H + h;
+  auto fetch = [&](int tok, float4& v, float& s) {
+    const bool live = tok < T;
+    v = live ? ld4(kq + size_t(tok) * H * KD) : make_float4(0.f, 0.f, 0.f, 0.f);
+    s = live ? bl[size_t(tok) * H] : 0.f;
+  };
+  float4 nkq;
+  float nbl;
+  fetch(sub * SUB, nkq, nbl);
   for (int tt = 0; tt < SUB; ++tt) {
     const int tok = sub * SUB + tt;
     const bool live = tok < T;
-    {
-      const int l = lane & 15;
-      const float* src = (lane < 16 ? keys : queries) + ((size_t(bb) * T + tok) * H + h) * KD + 4 * l;
-      st4((lane < 16 ? sm.k : sm.q) + 4 * l, live ? ld4(src) : make_float4(0.f, 0.f, 0.f, 0.f));
-    }
-    const float bet = live ? beta[(size_t(bb) * T + tok) * H + h] : 0.f;
-    const float lam = live ? expf(log_decay[(size_t(bb) * T + tok) * H + h]) : 1.f;
+    st4((lane < 16 ? sm.k : sm.q) + 4 * (lane & 15), nkq);
+    const float bet = __shfl_sync(0xffffffffu, nbl, 0);
+    const float lam = expf(__shfl_sync(0xffffffffu, nbl, 16));  // 1 past the end (log-decay 0)
+    if (tt + 1 < SUB) fetch(tok + 1, nkq, nbl);
     __syncwarp();
 
     ldl::Tiles F;

@@ -244,8 +244,9 @@ def selective_decode(state, key, value, query, beta, log_decay, floor, solver=No
 
 # Solver names the reference accepts (`lm/kernels/mamba4.py:167-184`,
 # `:249-262`) plus "cuda". Every name selects the same mathematics (an exact
-# Cholesky solve of the same system; the reference's backends differ only in
-# their arithmetic schedule), so all of them run the sm_100a kernels.
+# solve of the same SPD system: Cholesky in the reference, a block LDL^T in
+# this library's memory read; the reference's backends differ only in their
+# arithmetic schedule), so all of them run the sm_100a kernels.
 SOLVERS = ("cuda", "fused", "loop", "blocked", "unrolled", "auto")
 
 
