@@ -228,278 +228,9 @@ __global__ void __launch_bounds__(256, M4_STATES_MINB) states_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Scalar solve warps (memread_decode, spd_solve): lane-tile layout of the
-// 64x64 lower Cholesky factor.
-// Lane l = a*8 + b (a in 0..3, b in 0..7) owns rows a + 4m and columns b + 8n,
-// stored as row pairs (a + 8p, a + 4 + 8p) x column b + 8n for n <= p <= 7:
-// 36 float2 per lane, index pair_of(p, n). The 8x8 diagonal block J is the
-// pair (J, J) on every lane; off-diagonal block (K, J) is pair (K, J).
-// ---------------------------------------------------------------------------
-constexpr int NPAIR = 36;
-__host__ __device__ constexpr int pair_of(int p, int n) { return 8 * n - n * (n - 1) / 2 + (p - n); }
-__host__ __device__ constexpr int tri(int r, int c) { return r * (r + 1) / 2 + c; }
-constexpr int pair_n(int q) { return q < 8 ? 0 : q < 15 ? 1 : q < 21 ? 2 : q < 26 ? 3 : q < 30 ? 4 : q < 33 ? 5 : q < 35 ? 6 : 7; }
-constexpr int pair_p(int q) { return q - pair_of(pair_n(q), pair_n(q)) + pair_n(q); }
-
-M4_DEV float2 fma2(float2 a, float b, float2 c) {
-#ifdef M4_FFMA2
-  unsigned long long ar, br, cr, dr;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(ar) : "f"(a.x), "f"(a.y));
-  asm("mov.b64 %0, {%1,%1};" : "=l"(br) : "f"(b));
-  asm("mov.b64 %0, {%1,%2};" : "=l"(cr) : "f"(c.x), "f"(c.y));
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dr) : "l"(ar), "l"(br), "l"(cr));
-  float2 d;
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dr));
-  return d;
-#else
-  return make_float2(fmaf(a.x, b, c.x), fmaf(a.y, b, c.y));
-#endif
-}
-
-// Scalar broadcast to both halves of a float2 operand, made once per column
-// step and reused by every pair update of that step (fma.rn.f32x2: two FMAs
-// per instruction on sm_100a).
-#ifndef M4_NO_FFMA2
-using dup_t = unsigned long long;
-M4_DEV dup_t dup2(float b) {
-  dup_t r;
-  asm("mov.b64 %0, {%1,%1};" : "=l"(r) : "f"(b));
-  return r;
-}
-M4_DEV float2 fma2d(float2 a, dup_t b, float2 c) {
-  unsigned long long ar, cr, dr;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(ar) : "f"(a.x), "f"(a.y));
-  asm("mov.b64 %0, {%1,%2};" : "=l"(cr) : "f"(c.x), "f"(c.y));
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(dr) : "l"(ar), "l"(b), "l"(cr));
-  float2 d;
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(dr));
-  return d;
-}
-#else
-using dup_t = float;
-M4_DEV dup_t dup2(float b) { return b; }
-M4_DEV float2 fma2d(float2 a, dup_t b, float2 c) { return make_float2(fmaf(a.x, b, c.x), fmaf(a.y, b, c.y)); }
-#endif
-
-// Shared-memory strides that keep the broadcast reads conflict-free: float2
-// rows of PS per a (the four a-rows land on disjoint banks, 16-byte aligned)
-// and float rows of KS per b (the eight b-rows of a float4 read on disjoint
-// banks).
-constexpr int PS = 10;
-constexpr int KS = 12;
-
-struct SolveSmem {
-  float4 E[NPAIR / 2][32];       // running evidence (pairs 2q, 2q+1 per lane)
-  float flC[8 * KS];             // floor[b + 8n] at b*KS + n
-  float w[64];                   // w = L^-1 q (forward) / u = L^-1 g (backward)
-  float y[64];                   // solution
-  union {
-    struct {
-      float4 col[2][4 * PS];     // column pair broadcasts (two steps): at a*PS + p the row
-                                 // pair (a + 8p, a + 4 + 8p) of column J, then of column J + 1
-      float2 colw[2][4];         // bordered-row entries of columns J, J + 1 per a
-      float2 kP[4 * PS];         // (k[a + 8p], k[a + 4 + 8p]) at a*PS + p
-      float kC[8 * KS];          // k[b + 8n] at b*KS + n
-      float qC[8 * KS];          // q[b + 8n] at b*KS + n
-    } f;
-    struct {
-      float T[8 * 36];           // diagonal blocks, packed lower tri(r, c)
-      float X[8 * 36];           // their inverses
-    } s;
-  } u;
-};
-
-// Stage the diagonal blocks and invert them (lanes 0..7, one block each).
-// Diagonal entries hold reciprocal pivots 1/L_rr; X = L_block^-1.
-M4_DEV void invert_blocks(const float2 (&L)[NPAIR], SolveSmem& sm, int lane, int a, int b) {
-  __syncwarp();
-#pragma unroll
-  for (int J = 0; J < 8; ++J) {
-    const float2 d = L[pair_of(J, J)];
-    if (a >= b) sm.u.s.T[J * 36 + tri(a, b)] = d.x;
-    if (a + 4 >= b) sm.u.s.T[J * 36 + tri(a + 4, b)] = d.y;
-  }
-  __syncwarp();
-  if (lane < 8) {
-    const float* T = sm.u.s.T + lane * 36;
-    float* X = sm.u.s.X + lane * 36;
-    // In place, column by column: column c of X only overwrites entries that
-    // later columns (k > c) never read; the diagonal is unchanged.
-    float t[36];
-#pragma unroll
-    for (int i = 0; i < 36; ++i) t[i] = T[i];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-#pragma unroll
-      for (int r = c + 1; r < 8; ++r) {
-        float acc = 0.f;
-#pragma unroll
-        for (int k = c; k < r; ++k) acc = fmaf(t[tri(r, k)], t[tri(k, c)], acc);
-        t[tri(r, c)] = -t[tri(r, r)] * acc;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 36; ++i) X[i] = t[i];
-  }
-  __syncwarp();
-}
-
-M4_DEV float xblk(const SolveSmem& sm, int J, int r, int c) {
-  return r >= c ? sm.u.s.X[J * 36 + tri(r, c)] : 0.f;
-}
-
-// Replace each diagonal block of the lane-tiled factor by its inverse (from
-// invert_blocks): the layout the factor is stored in and the substitutions
-// read. The block diagonals stay the reciprocal pivots 1/L_rr.
-M4_DEV void diag_to_inverse(float2 (&L)[NPAIR], const SolveSmem& sm, int a, int b) {
-#pragma unroll
-  for (int J = 0; J < 8; ++J) L[pair_of(J, J)] = make_float2(xblk(sm, J, a, b), xblk(sm, J, a + 4, b));
-}
-
-// Blocked back-substitution y = L^-T w (w in smem) on a factor whose diagonal
-// blocks hold their inverses (diag_to_inverse). yr2[K] = (y[8K+a], y[8K+a+4]);
-// y also written to ysm.
-M4_DEV void back_substitute(const float2 (&L)[NPAIR], const float* w, float* ysm, int a, int b) {
-  float2 yr2[8];
-#pragma unroll
-  for (int J = 7; J >= 0; --J) {
-    float sp = 0.f;
-#pragma unroll
-    for (int K = J + 1; K < 8; ++K) {
-      sp = fmaf(L[pair_of(K, J)].x, yr2[K].x, sp);
-      sp = fmaf(L[pair_of(K, J)].y, yr2[K].y, sp);
-    }
-    sp += __shfl_xor_sync(0xffffffffu, sp, 8);
-    sp += __shfl_xor_sync(0xffffffffu, sp, 16);
-    const float x = w[8 * J + b] - sp;                   // x[b] on lanes (., b)
-    const float xa = __shfl_sync(0xffffffffu, x, a);       // x[a]
-    const float xa4 = __shfl_sync(0xffffffffu, x, a + 4);  // x[a + 4]
-    float p = L[pair_of(J, J)].x * xa;
-    p = fmaf(L[pair_of(J, J)].y, xa4, p);
-    p += __shfl_xor_sync(0xffffffffu, p, 8);
-    p += __shfl_xor_sync(0xffffffffu, p, 16);            // y[8J + b]
-    yr2[J] = make_float2(__shfl_sync(0xffffffffu, p, a), __shfl_sync(0xffffffffu, p, a + 4));
-    if (a == 0) ysm[8 * J + b] = p;
-  }
-}
-
-// Blocked forward substitution u = L^-1 g (g in smem), diagonal blocks
-// inverted as in back_substitute; u written to usm.
-M4_DEV void forward_substitute(const float2 (&L)[NPAIR], const float* g, float* usm, int a, int b) {
-  float ub[8];
-  const int src = (b & 3) * 8;
-#pragma unroll
-  for (int J = 0; J < 8; ++J) {
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int K = 0; K < J; ++K) {
-      s0 = fmaf(L[pair_of(J, K)].x, ub[K], s0);
-      s1 = fmaf(L[pair_of(J, K)].y, ub[K], s1);
-    }
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-    }
-    const float x0 = g[8 * J + a] - s0;       // x[a]
-    const float x1 = g[8 * J + a + 4] - s1;   // x[a + 4]
-    const float t0 = __shfl_sync(0xffffffffu, x0, src);
-    const float t1 = __shfl_sync(0xffffffffu, x1, src);
-    const float xb = b < 4 ? t0 : t1;         // x[b]
-    float p0 = L[pair_of(J, J)].x * xb;
-    float p1 = L[pair_of(J, J)].y * xb;
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      p0 += __shfl_xor_sync(0xffffffffu, p0, o);
-      p1 += __shfl_xor_sync(0xffffffffu, p1, o);
-    }
-    const float u0 = __shfl_sync(0xffffffffu, p0, src);
-    const float u1 = __shfl_sync(0xffffffffu, p1, src);
-    ub[J] = b < 4 ? u0 : u1;                  // u[8J + b]
-    if (b == 0) { usm[8 * J + a] = p0; usm[8 * J + a + 4] = p1; }
-  }
-  __syncwarp();
-}
-
-// Two right-looking column steps at once on unscaled columns U
-// (L[:, j] = U[:, j]/sqrt(U_jj)): columns J = 8 JN + jb and J + 1 (jb even).
-// Both owners broadcast their columns into one interleaved buffer (a lane
-// reads both columns' entries of a row pair with one 128-bit load); every
-// lane forms the column J + 1 updated by column J from the two broadcasts
-// (U'[:, J+1] = U[:, J+1] - U[:, J] U[J+1, J] / U[J, J]) and applies the
-// rank-2 update to its trailing entries. The column block JN is a template
-// parameter (register indices), the column within it a runtime value, so the
-// 32 steps compile to 8 loop bodies (small enough for the instruction cache).
-template <int JN>
-M4_DEV void factor_pair(int jb, float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
-  const int par = (jb >> 1) & 1;  // alternating buffer
-  float4* col = sm.u.f.col[par];
-  float2* colw = sm.u.f.colw[par];
-  if (b == jb || b == jb + 1) {
-    const int o = b - jb;  // 0: column J into .xy, 1: column J + 1 into .zw
-    float2* dst = reinterpret_cast<float2*>(col + a * PS) + o;
-#pragma unroll
-    for (int p = JN; p < 8; ++p) dst[2 * p] = A[pair_of(p, JN)];
-    reinterpret_cast<float*>(colw + a)[o] = wr[JN];
-  }
-  __syncwarp();
-  const int A0 = jb & 3, H0 = (jb >> 2) & 1, A1 = (jb + 1) & 3, H1 = ((jb + 1) >> 2) & 1;
-  const float* fc = reinterpret_cast<const float*>(col);
-  const float pJ = fc[(A0 * PS + JN) * 4 + H0];       // U[J][J]
-  const float u10 = fc[(A1 * PS + JN) * 4 + H1];      // U[J+1][J]
-  const float pJ1 = fc[(A1 * PS + JN) * 4 + 2 + H1];  // U[J+1][J+1]
-  const float r = rsqrtf(pJ), r2 = r * r;
-  const float sf = u10 * r2;
-  const float r1 = rsqrtf(fmaf(-u10, sf, pJ1)), r12 = r1 * r1;
-  rc[JN] = (b == jb) ? r : (b == jb + 1 ? r1 : rc[JN]);
-  dup_t DA[8], DB[8];
-  {
-    const float4* sc = col + (b & 3) * PS;
-    const float2 rw = colw[a];
-    const float rwA = rw.x;
-    const float rwB = fmaf(-rwA, sf, rw.y);
-#pragma unroll
-    for (int n = JN; n < 8; ++n) {
-      const float4 v = sc[n];
-      const float ca = b >= 4 ? v.y : v.x;
-      const float cb = b >= 4 ? v.w : v.z;
-      float CA = ca * r2, CB = fmaf(-ca, sf, cb) * r12;
-      if (n == JN) {
-        CA = (b > jb) ? CA : 0.f;
-        CB = (b > jb + 1) ? CB : 0.f;
-      }
-      wr[n] = fmaf(-rwB, CB, fmaf(-rwA, CA, wr[n]));
-      DA[n] = dup2(-CA);
-      DB[n] = dup2(-CB);
-    }
-  }
-#pragma unroll
-  for (int p = JN; p < 8; ++p) {
-    const float4 v = col[a * PS + p];
-    float2 ra = make_float2(v.x, v.y);
-    float2 rb = make_float2(fmaf(-v.x, sf, v.z), fmaf(-v.y, sf, v.w));
-    if (p == JN) {
-      ra.x = (a > jb) ? ra.x : 0.f;
-      ra.y = (a + 4 > jb) ? ra.y : 0.f;
-      rb.x = (a > jb + 1) ? rb.x : 0.f;
-      rb.y = (a + 4 > jb + 1) ? rb.y : 0.f;
-    }
-#pragma unroll
-    for (int n = JN; n <= p; ++n) A[pair_of(p, n)] = fma2d(rb, DB[n], fma2d(ra, DA[n], A[pair_of(p, n)]));
-  }
-}
-
-template <int JN>
-M4_DEV void factor_all(float2 (&A)[NPAIR], float (&wr)[8], float (&rc)[8], SolveSmem& sm, int a, int b) {
-#pragma unroll 1
-  for (int jb = 0; jb < 8; jb += 2) factor_pair<JN>(jb, A, wr, rc, sm, a, b);
-  if constexpr (JN + 1 < 8) factor_all<JN + 1>(A, wr, rc, sm, a, b);
-}
-
-// ---------------------------------------------------------------------------
 // memread_solve with the factorisation on the tensor cores: a block LDL^T of
 // each token's matrix in MMA accumulator fragments (ldl_tiles.cuh). One warp
-// per 16-token sub-chunk as above; the running evidence is kept in shared
+// per 16-token sub-chunk; the running evidence is kept in shared
 // memory in the stored factor's fragment layout, so the per-token update
 // E = lam E + beta k k^T touches each lane's own entries.
 // ---------------------------------------------------------------------------
@@ -629,10 +360,14 @@ __global__ void __launch_bounds__(32, 12) solve_kernel(
 // (selective_decode, lm/kernels/mamba4.py:341-355). One warp per (b, h):
 //   E' = lam E + beta k k^T, C' = lam C + beta v k^T,
 //   y = (E' + diag(floor))^-1 q, output = C' y, variance = q . y,
-// with the scalar lane-tiled Cholesky factorization (bordered query row) and
-// blocked back-substitution. E' and C' may overwrite E and C: the warp reads
-// all of E before writing E', and each row of C before writing that row.
+// with the memory read's block LDL^T in tensor-core fragments (ldl_tiles.cuh).
+// E' and C' may overwrite E and C: the warp reads all of E before writing
+// E', and each row of C before writing that row.
 // ---------------------------------------------------------------------------
+struct DecodeSmem {
+  float k[KD], q[KD], v[KD], y[KD];
+};
+
 template <int P>
 __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
     int B, int H, const float* evidence, const float* cross,
@@ -641,113 +376,92 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
     const float* __restrict__ floor_, float* __restrict__ out, float* __restrict__ variance,
     float* evidence_out, float* cross_out) {  // may alias evidence / cross
   extern __shared__ __align__(16) unsigned char decode_raw[];
-  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(decode_raw);
+  DecodeSmem* smem_all = reinterpret_cast<DecodeSmem*>(decode_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int a = lane >> 3, b = lane & 7;
+  const int g = lane >> 2, t = lane & 3;
   const int bh = blockIdx.x * WARPS + warp;
   if (bh >= B * H) return;
-  SolveSmem& sm = smem_all[warp];
+  DecodeSmem& sm = smem_all[warp];
   const int h = bh % H;
+  // E (symmetric, row-major) into the lower tiles; every load before any store.
   const float* src = evidence + size_t(bh) * KD * KD;
-  float2 A[NPAIR];
+  ldl::Tiles F;
 #pragma unroll
-  for (int q = 0; q < NPAIR; ++q) {
-    const int p = pair_p(q), n = pair_n(q);
-    A[q] = make_float2(src[(a + 8 * p) * KD + b + 8 * n], src[(a + 4 + 8 * p) * KD + b + 8 * n]);
+  for (int q = 0; q < 16; ++q) {
+    const int r0 = 16 * ldl::slot_R(q) + g, c0 = 8 * ldl::slot_c(q) + 2 * t;
+    const float2 lo = ld2f(src + r0 * KD + c0), hi = ld2f(src + (r0 + 8) * KD + c0);
+    F[q][0] = lo.x; F[q][1] = lo.y; F[q][2] = hi.x; F[q][3] = hi.y;
   }
-  if (a == 0) {
 #pragma unroll
-    for (int n = 0; n < 8; ++n) sm.flC[b * KS + n] = floor_[h * KD + b + 8 * n];
+  for (int R = 0; R < 4; ++R) {
+    const float2 e = ld2f(src + (16 * R + 8 + g) * KD + 8 * (2 * R + 1) + 2 * t);
+    F[16 + R][2] = e.x; F[16 + R][3] = e.y;
   }
   {
     const int l = lane & 15;
-    const float4 v4 = ld4((lane < 16 ? key : query) + size_t(bh) * KD + 4 * l);
-    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int i = 4 * l + e;
-      if (lane < 16) {
-        reinterpret_cast<float*>(sm.u.f.kP)[((i & 3) * PS + (i >> 3)) * 2 + ((i >> 2) & 1)] = vv[e];
-        sm.u.f.kC[(i & 7) * KS + (i >> 3)] = vv[e];
-        sm.w[i] = vv[e];  // key, kept for the cross update
-      } else {
-        sm.u.f.qC[(i & 7) * KS + (i >> 3)] = vv[e];
-      }
-    }
+    st4((lane < 16 ? sm.k : sm.q) + 4 * l, ld4((lane < 16 ? key : query) + size_t(bh) * KD + 4 * l));
   }
   const float bet = beta[bh];
   const float lam = expf(log_decay[bh]);
   __syncwarp();
-  float wr[8];
+  // E' = lam E + beta k k^T, written back whole: the kept entries in place,
+  // the strictly lower ones mirrored.
   {
-    float2 kr[8];
-    float kc[8];
+    float kr[4][2];
+    float2 kc[8];
 #pragma unroll
-    for (int p = 0; p < 8; p += 2) {
-      const float4 v = *reinterpret_cast<const float4*>(&sm.u.f.kP[a * PS + p]);
-      kr[p] = make_float2(bet * v.x, bet * v.y);
-      kr[p + 1] = make_float2(bet * v.z, bet * v.w);
+    for (int R = 0; R < 4; ++R) {
+      kr[R][0] = bet * sm.k[16 * R + g];
+      kr[R][1] = bet * sm.k[16 * R + 8 + g];
     }
 #pragma unroll
-    for (int n = 0; n < 8; ++n) kc[n] = sm.u.f.kC[b * KS + n];
-#pragma unroll
-    for (int q = 0; q < NPAIR; ++q) A[q] = fma2(kr[pair_p(q)], kc[pair_n(q)], make_float2(lam * A[q].x, lam * A[q].y));
-  }
-  // E' to global (symmetric: off-diagonal blocks both ways).
-  {
+    for (int c = 0; c < 8; ++c) kc[c] = ld2f(&sm.k[8 * c + 2 * t]);
     float* dst = evidence_out + size_t(bh) * KD * KD;
 #pragma unroll
-    for (int q = 0; q < NPAIR; ++q) {
-      const int p = pair_p(q), n = pair_n(q);
-      const int r0 = a + 8 * p, r1 = a + 4 + 8 * p, c = b + 8 * n;
-      dst[r0 * KD + c] = A[q].x;
-      dst[r1 * KD + c] = A[q].y;
-      if (p != n) {
-        dst[c * KD + r0] = A[q].x;
-        dst[c * KD + r1] = A[q].y;
+    for (int q = 0; q < 16; ++q) {
+      const int R = ldl::slot_R(q), c = ldl::slot_c(q);
+      float* e = F[q];
+      e[0] = fmaf(kr[R][0], kc[c].x, lam * e[0]);
+      e[1] = fmaf(kr[R][0], kc[c].y, lam * e[1]);
+      e[2] = fmaf(kr[R][1], kc[c].x, lam * e[2]);
+      e[3] = fmaf(kr[R][1], kc[c].y, lam * e[3]);
+      const int r0 = 16 * R + g, c0 = 8 * c + 2 * t;
+      *reinterpret_cast<float2*>(dst + r0 * KD + c0) = make_float2(e[0], e[1]);
+      *reinterpret_cast<float2*>(dst + (r0 + 8) * KD + c0) = make_float2(e[2], e[3]);
+      if (c < 2 * R) {  // rows 16R.. below the diagonal block
+        dst[c0 * KD + r0] = e[0];
+        dst[(c0 + 1) * KD + r0] = e[1];
       }
+      dst[c0 * KD + r0 + 8] = e[2];  // rows 16R + 8.. are below every column of the tile
+      dst[(c0 + 1) * KD + r0 + 8] = e[3];
+    }
+#pragma unroll
+    for (int R = 0; R < 4; ++R) {
+      float* e = F[16 + R];
+      e[2] = fmaf(kr[R][1], kc[2 * R + 1].x, lam * e[2]);
+      e[3] = fmaf(kr[R][1], kc[2 * R + 1].y, lam * e[3]);
+      *reinterpret_cast<float2*>(dst + (16 * R + 8 + g) * KD + 8 * (2 * R + 1) + 2 * t) = make_float2(e[2], e[3]);
     }
   }
 #pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const float f = sm.flC[b * KS + n];
-    A[pair_of(n, n)].x += (b == a) ? f : 0.f;
-    A[pair_of(n, n)].y += (b == a + 4) ? f : 0.f;
-    wr[n] = a == 0 ? sm.u.f.qC[b * KS + n] : 0.f;
+  for (int R = 0; R < 4; ++R) {
+    const float f0 = floor_[h * KD + 16 * R + g], f1 = floor_[h * KD + 16 * R + 8 + g];
+    F[ldl::ti(R, 2 * R)][0] += g == 2 * t ? f0 : 0.f;
+    F[ldl::ti(R, 2 * R)][1] += g == 2 * t + 1 ? f0 : 0.f;
+    F[ldl::ti(R, 2 * R + 1)][2] += g == 2 * t ? f1 : 0.f;
+    F[ldl::ti(R, 2 * R + 1)][3] += g == 2 * t + 1 ? f1 : 0.f;
   }
-  float rc[8];
-#pragma unroll
-  for (int n = 0; n < 8; ++n) rc[n] = 0.f;
-  factor_all<0>(A, wr, rc, sm, a, b);
-  float vpart = 0.f, kkeep[2];
-  kkeep[0] = sm.w[2 * lane];
-  kkeep[1] = sm.w[2 * lane + 1];
+  ldl::Forward fw;
+  fw.uv = 0.f;
+  fw.r = sm.q;
+  fw.vsm = sm.v;
+  ldl::factor_forward(F, fw, g, t);
+  const float var = warp_sum(fw.uv);
   __syncwarp();
-  if (a == 0) {
-#pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const float wv = wr[n] * rc[n];
-      sm.w[b + 8 * n] = wv;
-      vpart = fmaf(wv, wv, vpart);
-    }
-  }
-  const float var = warp_sum(vpart);
-#pragma unroll
-  for (int n = 0; n < 8; ++n) {
-#pragma unroll
-    for (int p = n; p < 8; ++p) {
-      A[pair_of(p, n)].x *= rc[n];
-      A[pair_of(p, n)].y *= rc[n];
-    }
-    float2& d = A[pair_of(n, n)];
-    d.x = (b == a) ? rc[n] : (a < b ? 0.f : d.x);
-    d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
-  }
-  invert_blocks(A, sm, lane, a, b);
-  diag_to_inverse(A, sm, a, b);
-  back_substitute(A, sm.w, sm.y, a, b);
+  ldl::back_solve(F, sm.v, sm.y, g, t);
   __syncwarp();
   if (lane == 0) variance[bh] = var;
+  float kkeep[2] = {sm.k[2 * lane], sm.k[2 * lane + 1]};
   // C' = lam C + beta v k^T, lane l on key coordinates 2l, 2l+1, rows in
   // batches of R whose loads are issued before the previous batch's stores
   // (cross_out may alias cross: row p is always read before it is written,
@@ -793,68 +507,63 @@ __global__ void __launch_bounds__(32 * WARPS) decode_kernel(
 // ---------------------------------------------------------------------------
 // spd_solve: standalone SPD solves precision @ y = rhs (spd_solve,
 // lm/kernels/mamba4.py:187-218) for `count` matrices of order dim <= 64.
-// One warp per matrix with the scalar lane-tile layout. Only the lower
-// triangle of each row-major [dim][dim] matrix is read (the upper entries of
-// the register tiles are mirrored from it); orders below 64 are padded with
-// an identity block and a zero right-hand side, which solves to zero. The
-// factor is stored in the lane-tile layout (LSTRIDE floats per matrix, 8x8
-// diagonal blocks inverted) for the backward.
+// One warp per matrix with the memory read's block LDL^T (ldl_tiles.cuh).
+// Only the lower triangle of each row-major [dim][dim] matrix is read (the
+// diagonal blocks' upper entries are mirrored from it); orders below 64 are
+// padded with an identity block and a zero right-hand side, which solves to
+// zero. The factor is stored in the memory read's fragment layout (LSTRIDE
+// floats per matrix: unit L, D^-1 blocks) for the backward.
 // ---------------------------------------------------------------------------
 M4_DEV float spd_entry(const float* M, int dim, int r, int c) {
   if (r >= dim || c >= dim) return r == c ? 1.f : 0.f;
   return r >= c ? M[r * dim + c] : M[c * dim + r];
 }
 
+struct SpdSmem {
+  float r[KD], v[KD], y[KD], s[KD];
+};
+
 __global__ void __launch_bounds__(32 * WARPS) spd_fwd_kernel(
     int count, int dim, const float* __restrict__ precision, const float* __restrict__ rhs,
     float* __restrict__ solution, float* __restrict__ Lst) {
   extern __shared__ __align__(16) unsigned char spd_raw[];
-  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(spd_raw);
+  SpdSmem* smem_all = reinterpret_cast<SpdSmem*>(spd_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int a = lane >> 3, b = lane & 7;
+  const int g = lane >> 2, t = lane & 3;
   const int m = blockIdx.x * WARPS + warp;
   if (m >= count) return;
-  SolveSmem& sm = smem_all[warp];
+  SpdSmem& sm = smem_all[warp];
   const float* src = precision + size_t(m) * dim * dim;
-  float2 A[NPAIR];
+  ldl::Tiles F;
 #pragma unroll
-  for (int q = 0; q < NPAIR; ++q) {
-    const int p = pair_p(q), n = pair_n(q);
-    A[q] = make_float2(spd_entry(src, dim, a + 8 * p, b + 8 * n), spd_entry(src, dim, a + 4 + 8 * p, b + 8 * n));
+  for (int q = 0; q < 16; ++q) {
+    const int r0 = 16 * ldl::slot_R(q) + g, c0 = 8 * ldl::slot_c(q) + 2 * t;
+    F[q][0] = spd_entry(src, dim, r0, c0);
+    F[q][1] = spd_entry(src, dim, r0, c0 + 1);
+    F[q][2] = spd_entry(src, dim, r0 + 8, c0);
+    F[q][3] = spd_entry(src, dim, r0 + 8, c0 + 1);
   }
-  float wr[8];
-  const float* g = rhs + size_t(m) * dim;
 #pragma unroll
-  for (int n = 0; n < 8; ++n) wr[n] = (a == 0 && b + 8 * n < dim) ? g[b + 8 * n] : 0.f;
-  float rc[8];
-#pragma unroll
-  for (int n = 0; n < 8; ++n) rc[n] = 0.f;
-  factor_all<0>(A, wr, rc, sm, a, b);
-  if (a == 0) {
-#pragma unroll
-    for (int n = 0; n < 8; ++n) sm.w[b + 8 * n] = wr[n] * rc[n];
+  for (int R = 0; R < 4; ++R) {
+    const int r = 16 * R + 8 + g, c = 8 * (2 * R + 1) + 2 * t;
+    F[16 + R][2] = spd_entry(src, dim, r, c);
+    F[16 + R][3] = spd_entry(src, dim, r, c + 1);
   }
-  // Scale to L; reciprocal pivot on the diagonal; zero the upper triangle.
-#pragma unroll
-  for (int n = 0; n < 8; ++n) {
-#pragma unroll
-    for (int p = n; p < 8; ++p) {
-      A[pair_of(p, n)].x *= rc[n];
-      A[pair_of(p, n)].y *= rc[n];
-    }
-    float2& d = A[pair_of(n, n)];
-    d.x = (b == a) ? rc[n] : (a < b ? 0.f : d.x);
-    d.y = (b == a + 4) ? rc[n] : (a + 4 < b ? 0.f : d.y);
-  }
-  invert_blocks(A, sm, lane, a, b);
-  diag_to_inverse(A, sm, a, b);
+  const float* g_ = rhs + size_t(m) * dim;
+  for (int i = lane; i < KD; i += 32) sm.r[i] = i < dim ? g_[i] : 0.f;
+  __syncwarp();
+  ldl::Forward fw;
+  fw.uv = 0.f;
+  fw.r = sm.r;
+  fw.vsm = sm.v;
+  ldl::factor_forward(F, fw, g, t);
   {
     float* dst = Lst + size_t(m) * LSTRIDE;
 #pragma unroll
-    for (int q4 = 0; q4 < NPAIR / 2; ++q4)
-      st4(dst + (q4 * 32 + lane) * 4, make_float4(A[2 * q4].x, A[2 * q4].y, A[2 * q4 + 1].x, A[2 * q4 + 1].y));
+    for (int q = 0; q < ldl::NQ; ++q) st4(dst + (q * 32 + lane) * 4, ldl::get4(F, q));
   }
-  back_substitute(A, sm.w, sm.y, a, b);
+  __syncwarp();
+  ldl::back_solve(F, sm.v, sm.y, g, t);
   __syncwarp();
   float* out = solution + size_t(m) * dim;
   for (int i = lane; i < dim; i += 32) out[i] = sm.y[i];
@@ -867,38 +576,35 @@ __global__ void __launch_bounds__(32 * WARPS) spd_bwd_kernel(
     int count, int dim, const float* __restrict__ Lst, const float* __restrict__ solution,
     const float* __restrict__ d_solution, float* __restrict__ d_precision, float* __restrict__ d_rhs) {
   extern __shared__ __align__(16) unsigned char spdb_raw[];
-  SolveSmem* smem_all = reinterpret_cast<SolveSmem*>(spdb_raw);
+  SpdSmem* smem_all = reinterpret_cast<SpdSmem*>(spdb_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int a = lane >> 3, b = lane & 7;
+  const int g = lane >> 2, t = lane & 3;
   const int m = blockIdx.x * WARPS + warp;
   if (m >= count) return;
-  SolveSmem& sm = smem_all[warp];
-  float2 L[NPAIR];
+  SpdSmem& sm = smem_all[warp];
+  ldl::Tiles F;
   {
     const float* src = Lst + size_t(m) * LSTRIDE;
 #pragma unroll
-    for (int q4 = 0; q4 < NPAIR / 2; ++q4) {
-      const float4 v4 = ld4(src + (q4 * 32 + lane) * 4);
-      L[2 * q4] = make_float2(v4.x, v4.y);
-      L[2 * q4 + 1] = make_float2(v4.z, v4.w);
-    }
+    for (int q = 0; q < ldl::NQ; ++q) ldl::set4(F, q, ld4(src + (q * 32 + lane) * 4));
   }
-  const float* g = d_solution + size_t(m) * dim;
+  const float* gs = d_solution + size_t(m) * dim;
   const float* y = solution + size_t(m) * dim;
-  for (int i = lane; i < 64; i += 32) {
-    sm.y[i] = i < dim ? g[i] : 0.f;
-    sm.flC[i] = i < dim ? y[i] : 0.f;  // the solution, kept for the outer product
+  for (int i = lane; i < KD; i += 32) {
+    sm.r[i] = i < dim ? gs[i] : 0.f;
+    sm.s[i] = i < dim ? y[i] : 0.f;  // the solution, kept for the outer product
   }
   __syncwarp();
-  forward_substitute(L, sm.y, sm.w, a, b);
-  back_substitute(L, sm.w, sm.y, a, b);  // z in sm.y
+  ldl::forward_solve(F, sm.r, sm.v, g, t);
+  __syncwarp();
+  ldl::back_solve(F, sm.v, sm.y, g, t);  // z in sm.y
   __syncwarp();
   float* dr = d_rhs + size_t(m) * dim;
   for (int i = lane; i < dim; i += 32) dr[i] = sm.y[i];
   float* dp = d_precision + size_t(m) * dim * dim;
   for (int idx = lane; idx < dim * dim; idx += 32) {
     const int i = idx / dim, j = idx - i * dim;
-    dp[idx] = -0.5f * fmaf(sm.y[i], sm.flC[j], sm.flC[i] * sm.y[j]);
+    dp[idx] = -0.5f * fmaf(sm.y[i], sm.s[j], sm.s[i] * sm.y[j]);
   }
 }
 
@@ -1670,7 +1376,7 @@ extern "C" int m4_memread_decode(const M4MemDims* d, const float* evidence, cons
   if (!all_aligned16(key, query)) return M4_ERR_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bh = d->batch * d->heads;
-  const int smem = int(sizeof(mem::SolveSmem) * mem::WARPS);
+  const int smem = int(sizeof(mem::DecodeSmem) * mem::WARPS);
   const int grid = (bh + mem::WARPS - 1) / mem::WARPS;
   if (d->value_dim == 64) {
     cudaFuncSetAttribute(mem::decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1700,7 +1406,7 @@ extern "C" int m4_spd_solve_fwd(int count, int dim, const float* precision, cons
   if (!all_aligned16(static_cast<const float*>(factor))) return M4_ERR_ALIGN;
   if (factor_bytes < m4_spd_solve_factor_bytes(count, dim)) return M4_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int smem = int(sizeof(mem::SolveSmem) * mem::WARPS);
+  const int smem = int(sizeof(mem::SpdSmem) * mem::WARPS);
   cudaFuncSetAttribute(mem::spd_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   mem::spd_fwd_kernel<<<(count + mem::WARPS - 1) / mem::WARPS, 32 * mem::WARPS, smem, s>>>(
       count, dim, precision, rhs, solution, static_cast<float*>(factor));
@@ -1717,7 +1423,7 @@ extern "C" int m4_spd_solve_bwd(int count, int dim, const void* factor, size_t f
   if (!all_aligned16(static_cast<const float*>(factor))) return M4_ERR_ALIGN;
   if (factor_bytes < m4_spd_solve_factor_bytes(count, dim)) return M4_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int smem = int(sizeof(mem::SolveSmem) * mem::WARPS);
+  const int smem = int(sizeof(mem::SpdSmem) * mem::WARPS);
   cudaFuncSetAttribute(mem::spd_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   mem::spd_bwd_kernel<<<(count + mem::WARPS - 1) / mem::WARPS, 32 * mem::WARPS, smem, s>>>(
       count, dim, static_cast<const float*>(factor), solution, d_solution, d_precision, d_rhs);
