@@ -74,17 +74,15 @@ M4_DEV void sweep(float& x, float& y, int g, int t) {
   }
 }
 
-// Column block J of the factorisation.
+// Column block J of the factorisation, in two parts. panel_part: the
+// unscaled panel tiles (R', J), R' >= R, split once (the A operands of the
+// panel products and the B operands of the trailing products; rows of the
+// diagonal block itself enter neither, their products are discarded), the
+// panel L = A D^-1, and the diagonal block replaced by D^-1 (ix, iy).
 template <int J>
-M4_DEV void factor_step(Tiles& F, int g, int t) {
+M4_DEV void panel_part(Tiles& F, SplitA (&po)[4], float ix, float iy) {
   constexpr int R = J / 2, H = 2 * (J & 1);
-  float ix = F[ti(R, J)][H], iy = F[ti(R, J)][H + 1];
-  sweep(ix, iy, g, t);
   const SplitB dinv = split_b(ix, iy);
-  // Unscaled panel tiles (R', J), R' >= R, split once: the A operands of
-  // the panel products and the B operands of the trailing products. Rows of
-  // the diagonal block itself enter neither (their products are discarded).
-  SplitA po[4];
 #pragma unroll
   for (int Rp = R; Rp < 4; ++Rp) {
     const float* v = F[ti(Rp, J)];
@@ -93,7 +91,6 @@ M4_DEV void factor_step(Tiles& F, int g, int t) {
     else
       po[Rp] = split_a(v[0], v[2], v[1], v[3]);  // k order: columns 2t, 2t + 1 at k = t, t + 4
   }
-  // Panel: L = A D^-1; the diagonal block becomes D^-1.
 #pragma unroll
   for (int Rp = R; Rp < 4; ++Rp) {
     if ((J & 1) && Rp == R) continue;
@@ -104,14 +101,23 @@ M4_DEV void factor_step(Tiles& F, int g, int t) {
   }
   F[ti(R, J)][H] = ix;
   F[ti(R, J)][H + 1] = iy;
-  // Trailing update of tiles (R', c'), J < c' <= 2R' + 1.
+}
+
+// trailing_part: the trailing update A -= L A_panel^T of tiles (R', c'),
+// J < c' <= 2R' + 1: with CRIT only the tile holding the next diagonal block
+// (c' = J + 1), otherwise all the others.
+template <int J, bool CRIT>
+M4_DEV void trailing_part(Tiles& F, const SplitA (&po)[4]) {
+  constexpr int R = J / 2;
 #pragma unroll
   for (int Rp = R; Rp < 4; ++Rp) {
     if (J + 1 > 2 * Rp + 1) continue;
+    if (CRIT && Rp != (J + 1) / 2) continue;
     const float* l = F[ti(Rp, J)];
     const SplitA la = split_a(-l[0], -l[2], -l[1], -l[3]);
 #pragma unroll
     for (int cp = J + 1; cp <= 2 * Rp + 1; ++cp) {
+      if ((cp == J + 1 && Rp == (J + 1) / 2) != CRIT) continue;
       // Panel rows 8c'.. (unscaled): tile (c'/2, J), row half c' % 2. As a
       // B operand b0 = A[8c' + g][8J + 2t], b1 = A[8c' + g][8J + 2t + 1]:
       // in the split's A-operand order, entries 0, 2 (half 0) or 1, 3.
@@ -162,13 +168,33 @@ M4_DEV void forward_step(const Tiles& F, Forward& f, int g, int t) {
   }
 }
 
-// The factorisation with the forward substitution of one right-hand side
-// interleaved (block J of the substitution right after column block J).
+// The factorisation with the forward substitution of one right-hand side,
+// software-pipelined: column block J's pivot sweep is followed by block
+// J - 1's trailing updates (all but the one that produced D_J) and forward
+// substitution, which do not depend on it, then by block J's panel and the
+// trailing update of the tile holding D_(J+1). The independent tensor-core
+// and substitution work is in flight while the next sweep starts.
 template <int J = 0>
+M4_DEV void factor_forward(Tiles& F, Forward& f, SplitA (&po)[4], int g, int t) {
+  constexpr int R = J / 2, H = 2 * (J & 1);
+  float ix = F[ti(R, J)][H], iy = F[ti(R, J)][H + 1];
+  sweep(ix, iy, g, t);
+  if constexpr (J > 0) {
+    trailing_part<J - 1, false>(F, po);
+    forward_step<J - 1>(F, f, g, t);
+  }
+  panel_part<J>(F, po, ix, iy);
+  if constexpr (J + 1 < 8) {
+    trailing_part<J, true>(F, po);
+    factor_forward<J + 1>(F, f, po, g, t);
+  } else {
+    forward_step<7>(F, f, g, t);
+  }
+}
+
 M4_DEV void factor_forward(Tiles& F, Forward& f, int g, int t) {
-  factor_step<J>(F, g, t);
-  forward_step<J>(F, f, g, t);
-  if constexpr (J + 1 < 8) factor_forward<J + 1>(F, f, g, t);
+  SplitA po[4];
+  factor_forward<0>(F, f, po, g, t);
 }
 
 template <int J = 0>
