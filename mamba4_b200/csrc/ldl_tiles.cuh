@@ -59,16 +59,18 @@ M4_DEV void sweep(float& x, float& y, int g, int t) {
     const float p11 = __shfl_sync(FULL, y, 4 * k1 + m);
     float rd;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(rd) : "f"(fmaf(p00, p11, -p01 * p01)));
-    const float i00 = p11 * rd, i01 = -p01 * rd, i11 = p00 * rd;
     const bool pc = t == m;  // this lane's columns are the pivot columns
-    // Pivot rows with the identity in the pivot columns, times the 2x2 inverse.
+    // Pivot rows with the identity in the pivot columns, times the adjugate
+    // of the 2x2 pivot block; the reciprocal determinant rd multiplies last,
+    // so its latency overlaps this arithmetic.
     const float s00 = pc ? 1.f : r00, s01 = pc ? 0.f : r01, s10 = pc ? 0.f : r10, s11 = pc ? 1.f : r11;
-    const float n00 = fmaf(i00, s00, i01 * s10), n01 = fmaf(i00, s01, i01 * s11);
-    const float n10 = fmaf(i01, s00, i11 * s10), n11 = fmaf(i01, s01, i11 * s11);
-    float nx = fmaf(-c0, n00, fmaf(-c1, n10, pc ? 0.f : x));
-    float ny = fmaf(-c0, n01, fmaf(-c1, n11, pc ? 0.f : y));
-    nx = g == k0 ? n00 : (g == k1 ? n10 : nx);
-    ny = g == k0 ? n01 : (g == k1 ? n11 : ny);
+    const float u00 = fmaf(p11, s00, -p01 * s10), u01 = fmaf(p11, s01, -p01 * s11);
+    const float u10 = fmaf(p00, s10, -p01 * s00), u11 = fmaf(p00, s11, -p01 * s01);
+    const float bx = fmaf(c0, u00, c1 * u10), by = fmaf(c0, u01, c1 * u11);
+    float nx = fmaf(-rd, bx, pc ? 0.f : x);
+    float ny = fmaf(-rd, by, pc ? 0.f : y);
+    nx = g == k0 ? rd * u00 : (g == k1 ? rd * u10 : nx);
+    ny = g == k0 ? rd * u01 : (g == k1 ? rd * u11 : ny);
     x = nx;
     y = ny;
   }
