@@ -981,6 +981,7 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
   float* wbP = decP + 4 * CH;     // [4][64] column-quarter partials of dw_s
   float* exP = wbP + 4 * CH;      // [4][64] column-quarter partials of the per-token extra term
   float* red = exP + 4 * CH;      // [64 + 16] scratch
+  float* wsv = red + CH + 16;     // [64] beta_s e^(P_L - P_s)
   const int Tp = (T + CH - 1) / CH * CH, nch = Tp / CH, nsub = Tp / SUB;
   const int ch = blockIdx.x % nch, bh = blockIdx.x / nch, b = bh / H, h = bh % H;
   const int t0 = ch * CH, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1009,6 +1010,7 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
   cp_wait();
   __syncthreads();
   const float pl = pre[CH - 1];
+  if (tid < CH) wsv[tid] = bet[tid] * expf(pl - pre[tid]);  // read after the phase-1 barrier
   // Phase 1: GY, GZ, OV -> M1, M2 and the dW reductions.
   {
     float gy[2][4], gz[2][4], ov[2][4];
@@ -1072,7 +1074,7 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
       if (e < 2) w0 += part; else w1 += part;
       const int t = t0 + s;
       if (t < T) {
-        const float ws = bet[s] * expf(pl - pre[s]);
+        const float ws = wsv[s];
         dk[((size_t(b) * T + t) * H + h) * KD + d] = fmaf(ws, tks[nt][e] + tkc[nt][e], acc[nt][e]);
       }
     });
@@ -1087,7 +1089,7 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
       if (e < 2) w0 += part; else w1 += part;
       const int t = t0 + s;
       if (t < T) {
-        const float ws = bet[s] * expf(pl - pre[s]);
+        const float ws = wsv[s];
         dv[((size_t(b) * T + t) * H + h) * P + p] = fmaf(ws, ck[nt][e], accv[nt][e]);
       }
     });
@@ -1226,7 +1228,7 @@ size_t rhs_smem() { return (2 * CH * LD + 2 * CH * (P + 4) + P * LD + 3 * CH) * 
 template <int P>
 size_t carry_smem() { return (2 * CH * LD + CH * (P + 4) + 3 * CH) * sizeof(float); }
 template <int P>
-size_t grads_smem() { return (6 * CH * LD + 2 * CH * (P + 4) + P * LD + 24 * CH + 16) * sizeof(float); }
+size_t grads_smem() { return (6 * CH * LD + 2 * CH * (P + 4) + P * LD + 25 * CH + 16) * sizeof(float); }
 
 template <int P>
 int forward(const M4MemDims& d, const float* keys, const float* values, const float* queries,
