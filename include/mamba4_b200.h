@@ -116,11 +116,13 @@ int m4_memread_decode(const M4MemDims* dims, const float* evidence, const float*
 /* Standalone SPD solve. Replaces spd_solve (lm/kernels/mamba4.py:187-218)
  * with its factorization backends (_cholesky_loop / _cholesky_blocked /
  * _cholesky_unrolled, :31-125, and _triangular_solves, :138-158): for each of
- * `count` matrices, solve precision y = rhs with a Cholesky factorization.
+ * `count` matrices, solve precision y = rhs with a block LDL^T factorization
+ * (8x8 pivot blocks; the same exact solve as the reference's Cholesky to
+ * float32 rounding).
  *   precision [count, dim, dim] row-major, SPD, only the lower triangle read;
  *   rhs, solution [count, dim]; dim 1..64 (orders below 64 are padded with an
  *   identity block inside the kernel). No alignment needed for these.
- *   factor: the stored Cholesky factor for the backward, sized by
+ *   factor: the stored LDL^T factor for the backward, sized by
  *   m4_spd_solve_factor_bytes (9,216 bytes per matrix, 16-byte aligned).
  * count 0 launches nothing and returns M4_OK. */
 size_t m4_spd_solve_factor_bytes(int count, int dim);

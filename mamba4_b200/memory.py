@@ -189,7 +189,8 @@ def selective_decode(state, key, value, query, beta, log_decay, floor, solver=No
     [B,H,D]; value [B,H,P]; beta, log_decay [B,H]; floor [H,D]. Returns
     SelectiveResult(output [B,H,P], variance [B,H], SelectiveState(evidence',
     cross')) through `m4_memread_decode` (one warp per head: rank-one state
-    update, 64x64 Cholesky with the query as bordered row, back-substitution).
+    update, 64x64 block LDL^T with the forward substitution interleaved,
+    back-substitution).
     `solver` is accepted for signature compatibility ("cuda"/"fused"/None).
     Key dims below 64 are padded with an identity block as in
     `selective_memory_fused`. No gradient (the reference decodes without one).
@@ -285,7 +286,7 @@ def spd_solve(precision, rhs, backend=None):
 
     Mirrors `spd_solve` (`lm/kernels/mamba4.py:187-218`): float32, only the
     lower triangle of `precision` is read, d <= 64; the backward reuses the
-    stored Cholesky factor, z = A^-1 g, d rhs = z and d A = -sym(z y^T)
+    stored LDL^T factor, z = A^-1 g, d rhs = z and d A = -sym(z y^T)
     (`:208-215`). `backend` takes the reference's names (None, "loop",
     "blocked", "unrolled", "auto", "fused") and "cuda"; they change only the
     reference's arithmetic schedule, and all run the `m4_spd_solve_*` kernels.
