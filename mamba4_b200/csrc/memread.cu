@@ -713,8 +713,8 @@ __global__ void __launch_bounds__(CT) output_kernel(
   extern __shared__ __align__(16) float sh[];
   float* Ys = sh;                 // [64][LD]
   float* Ks = Ys + CH * LD;       // [64][LD]
-  float* Ms = Ks + CH * LD;       // [64][LD]
-  float* Vs = Ms + CH * LD;       // [64][LP]
+  float* Ms = Ks;                 // [64][LD] over K once the scores are in registers
+  float* Vs = Ks + CH * LD;       // [64][LP]
   float* C0 = Vs + CH * LP;       // [P][LD]
   float* pre = C0 + P * LD;
   float* bet = pre + CH;
@@ -735,6 +735,7 @@ __global__ void __launch_bounds__(CT) output_kernel(
     zero(acc);
     gemm3<KD, 4>(acc, row0, 32 * half, [&](int r, int k) { return Ys[r * LD + k]; },
                  [&](int k, int n) { return Ks[n * LD + k]; });
+    __syncthreads();  // every warp is done with K
     each<4>(row0, 32 * half, [&](int r, int n, int nt, int e) {
       Ms[r * LD + n] = n <= r ? acc[nt][e] * bet[n] * expf(pre[r] - pre[n]) : 0.f;
     });
@@ -764,9 +765,9 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
   constexpr int LP = P + 4;
   extern __shared__ __align__(16) float sh[];
   float* Ks = sh;                 // [64][LD]
-  float* Ms = Ks + CH * LD;       // [64][LD]
-  float* Os = Ms + CH * LD;       // [64][LP]
+  float* Os = Ks + CH * LD;       // [64][LP]
   float* Vs = Os + CH * LP;       // [64][LP]
+  float* Ms = Vs;                 // [64][LD] over V once dO V^T is in registers
   float* C0 = Vs + CH * LP;       // [P][LD]
   float* pre = C0 + P * LD;
   float* bet = pre + CH;
@@ -806,6 +807,7 @@ __global__ void __launch_bounds__(CT) rhs_kernel(
     zero(acc);
     gemm3<P, 4>(acc, row0, 32 * half, [&](int r, int k) { return Os[r * LP + k]; },
                 [&](int k, int s) { return Vs[s * LP + k]; });
+    __syncthreads();  // every warp is done with V
     each<4>(row0, 32 * half, [&](int r, int s, int nt, int e) {
       Ms[r * LD + s] = s <= r ? acc[nt][e] * bet[s] * expf(pre[r] - pre[s]) : 0.f;
     });
@@ -1222,9 +1224,9 @@ __global__ void __launch_bounds__(1024) floor_reduce_kernel(int rows, int H, con
 }
 
 template <int P>
-size_t output_smem() { return (3 * CH * LD + CH * (P + 4) + P * LD + 3 * CH) * sizeof(float); }
+size_t output_smem() { return (2 * CH * LD + CH * (P + 4) + P * LD + 3 * CH) * sizeof(float); }
 template <int P>
-size_t rhs_smem() { return (2 * CH * LD + 2 * CH * (P + 4) + P * LD + 3 * CH) * sizeof(float); }
+size_t rhs_smem() { return (CH * LD + 2 * CH * (P + 4) + P * LD + 3 * CH) * sizeof(float); }
 template <int P>
 size_t carry_smem() { return (2 * CH * LD + CH * (P + 4) + 3 * CH) * sizeof(float); }
 template <int P>
