@@ -45,7 +45,7 @@ using Tiles = float[NT][4];
 // m = 0..3 (a column pair is one lane's x, y). On return x, y hold M^-1.
 // The pivot block's off-diagonal entries are taken as equal (the block is
 // symmetric); its determinant is inverted by the hardware reciprocal
-// (rcp.approx: relative error within 2^-23). The step loop stays rolled: the
+// (rcp.approx: at most one unit in the last place). The step loop stays rolled: the
 // eight sweeps of a factorisation are most of its code, and an unrolled body
 // overflows the instruction cache of warps at different steps.
 M4_DEV void sweep(float& x, float& y, int g, int t) {
