@@ -652,6 +652,76 @@ M4_DEV void gemm3(float (&acc)[NT][4], int row0, int col0, FA fa, FB fb) {
   }
 }
 
+// Two products with the same B operand (acc1 += A1 B, acc2 += A2 B): each B
+// fragment is loaded and split once.
+template <int K, int NT, class FA1, class FA2, class FB>
+M4_DEV void gemm3_shared_b(float (&acc1)[NT][4], float (&acc2)[NT][4], int row0, int col0, FA1 fa1, FA2 fa2, FB fb) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll 2
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    uint32_t ah[2][4], al[2][4];
+    {
+      const float av[2][4] = {{fa1(row0 + g, k0 + c), fa1(row0 + g + 8, k0 + c), fa1(row0 + g, k0 + c + 4),
+                               fa1(row0 + g + 8, k0 + c + 4)},
+                              {fa2(row0 + g, k0 + c), fa2(row0 + g + 8, k0 + c), fa2(row0 + g, k0 + c + 4),
+                               fa2(row0 + g + 8, k0 + c + 4)}};
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          ah[m][i] = split_hi(av[m][i]);
+          al[m][i] = __float_as_uint(av[m][i] - __uint_as_float(ah[m][i]));
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float b0 = fb(k0 + c, col0 + 8 * nt + g), b1 = fb(k0 + c + 4, col0 + 8 * nt + g);
+      const uint32_t bh[2] = {split_hi(b0), split_hi(b1)};
+      const uint32_t bl[2] = {__float_as_uint(b0 - __uint_as_float(bh[0])),
+                              __float_as_uint(b1 - __uint_as_float(bh[1]))};
+      mma_tf32(acc1[nt], al[0], bh);
+      mma_tf32(acc2[nt], al[1], bh);
+      mma_tf32(acc1[nt], ah[0], bl);
+      mma_tf32(acc2[nt], ah[1], bl);
+      mma_tf32(acc1[nt], ah[0], bh);
+      mma_tf32(acc2[nt], ah[1], bh);
+    }
+  }
+}
+
+// Two products with the same A operand (acc1 += A B1 at columns col1..,
+// acc2 += A B2 at columns col2..): each A fragment is loaded and split once.
+template <int K, int NT1, int NT2, class FA, class FB1, class FB2>
+M4_DEV void gemm3_shared_a(float (&acc1)[NT1][4], float (&acc2)[NT2][4], int row0, int col1, int col2, FA fa,
+                           FB1 fb1, FB2 fb2) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+#pragma unroll 2
+  for (int k0 = 0; k0 < K; k0 += 8) {
+    const float av[4] = {fa(row0 + g, k0 + c), fa(row0 + g + 8, k0 + c), fa(row0 + g, k0 + c + 4),
+                         fa(row0 + g + 8, k0 + c + 4)};
+    uint32_t ah[4], al[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ah[i] = split_hi(av[i]);
+      al[i] = __float_as_uint(av[i] - __uint_as_float(ah[i]));
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT1 + NT2; ++nt) {
+      const bool first = nt < NT1;
+      const int col = first ? col1 + 8 * nt : col2 + 8 * (nt - NT1);
+      const float b0 = first ? fb1(k0 + c, col + g) : fb2(k0 + c, col + g);
+      const float b1 = first ? fb1(k0 + c + 4, col + g) : fb2(k0 + c + 4, col + g);
+      const uint32_t bh[2] = {split_hi(b0), split_hi(b1)};
+      const uint32_t bl[2] = {__float_as_uint(b0 - __uint_as_float(bh[0])),
+                              __float_as_uint(b1 - __uint_as_float(bh[1]))};
+      float(&d)[4] = first ? acc1[nt < NT1 ? nt : 0] : acc2[nt < NT1 ? 0 : nt - NT1];
+      mma_tf32(d, al, bh);
+      mma_tf32(d, ah, bl);
+      mma_tf32(d, ah, bh);
+    }
+  }
+}
+
 template <int NT>
 M4_DEV void zero(float (&acc)[NT][4]) {
 #pragma unroll
@@ -1017,10 +1087,9 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
   {
     float gy[2][4], gz[2][4], ov[2][4];
     zero(gy); zero(gz); zero(ov);
-    gemm3<KD, 2>(gy, row0, c64, [&](int r, int k) { return Ys[r * LD + k]; },
-                 [&](int k, int s) { return Ks[s * LD + k]; });
-    gemm3<KD, 2>(gz, row0, c64, [&](int r, int k) { return Zs[r * LD + k]; },
-                 [&](int k, int s) { return Ks[s * LD + k]; });
+    gemm3_shared_b<KD, 2>(gy, gz, row0, c64, [&](int r, int k) { return Ys[r * LD + k]; },
+                          [&](int r, int k) { return Zs[r * LD + k]; },
+                          [&](int k, int s) { return Ks[s * LD + k]; });
     gemm3<P, 2>(ov, row0, c64, [&](int r, int k) { return Os[r * LP + k]; },
                 [&](int k, int s) { return Vs[s * LP + k]; });
     float r0 = 0.f, r1 = 0.f, cw[2][2], cd[2][2];
@@ -1060,14 +1129,18 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
   __syncthreads();
   // Phase 2: dK and dV (rows s) and dw_s.
   {
-    float acc[2][4], tks[2][4], tkc[2][4];
-    zero(acc); zero(tks); zero(tkc);
-    gemm3<CH, 2>(acc, row0, c64, [&](int s, int t) { return -M1[t * LD + s]; },
-                 [&](int t, int d) { return Zs[t * LD + d]; });
+    float acc[2][4], tks[2][4], tkc[2][4], accv[NTQ][4], ck[NTQ][4];
+    zero(acc); zero(tks); zero(tkc); zero(accv); zero(ck);
+    // M1^T with -Z (dK) and with dO (dV); K with Sbar + Sbar^T (dK) and
+    // with Cbar^T (dV): each shared operand split once.
+    gemm3_shared_a<CH, 2, NTQ>(acc, accv, row0, c64, cP, [&](int s, int t) { return M1[t * LD + s]; },
+                               [&](int t, int d) { return -Zs[t * LD + d]; },
+                               [&](int t, int p) { return Os[t * LP + p]; });
     gemm3<CH, 2>(acc, row0, c64, [&](int s, int t) { return M2[t * LD + s]; },
                  [&](int t, int d) { return Ys[t * LD + d]; });
-    gemm3<KD, 2>(tks, row0, c64, [&](int s, int e) { return Ks[s * LD + e]; },
-                 [&](int e, int d) { return Sb[e * LD + d] + Sb[d * LD + e]; });
+    gemm3_shared_a<KD, 2, NTQ>(tks, ck, row0, c64, cP, [&](int s, int e) { return Ks[s * LD + e]; },
+                               [&](int e, int d) { return Sb[e * LD + d] + Sb[d * LD + e]; },
+                               [&](int d, int p) { return Cb[p * LD + d]; });
     gemm3<P, 2>(tkc, row0, c64, [&](int s, int p) { return Vs[s * LP + p]; },
                 [&](int p, int d) { return Cb[p * LD + d]; });
     float w0 = 0.f, w1 = 0.f;
@@ -1080,12 +1153,6 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
         dk[((size_t(b) * T + t) * H + h) * KD + d] = fmaf(ws, tks[nt][e] + tkc[nt][e], acc[nt][e]);
       }
     });
-    float accv[NTQ][4], ck[NTQ][4];
-    zero(accv); zero(ck);
-    gemm3<CH, NTQ>(accv, row0, cP, [&](int s, int t) { return M1[t * LD + s]; },
-                   [&](int t, int p) { return Os[t * LP + p]; });
-    gemm3<KD, NTQ>(ck, row0, cP, [&](int s, int d) { return Ks[s * LD + d]; },
-                   [&](int d, int p) { return Cb[p * LD + d]; });
     each<NTQ>(row0, cP, [&](int s, int p, int nt, int e) {
       const float part = Vs[s * LP + p] * ck[nt][e];
       if (e < 2) w0 += part; else w1 += part;
@@ -1129,10 +1196,9 @@ __global__ void __launch_bounds__(CTG) grads_kernel(
   {
     float sy[2][4], cy[NTQ][4];
     zero(sy); zero(cy);
-    gemm3<KD, 2>(sy, row0, c64, [&](int t, int k) { return Ys[t * LD + k]; },
-                 [&](int k, int d) { return Sb[d * LD + k]; });
-    gemm3<KD, NTQ>(cy, row0, cP, [&](int t, int k) { return Ys[t * LD + k]; },
-                   [&](int k, int p) { return Cb[p * LD + k]; });
+    gemm3_shared_a<KD, 2, NTQ>(sy, cy, row0, c64, cP, [&](int t, int k) { return Ys[t * LD + k]; },
+                               [&](int k, int d) { return Sb[d * LD + k]; },
+                               [&](int k, int p) { return Cb[p * LD + k]; });
     float v0 = 0.f, v1 = 0.f;
     each<2>(row0, c64, [&](int t, int d, int nt, int e) {
       const float part = -Zs[t * LD + d] * sy[nt][e];
