@@ -153,3 +153,38 @@ def test_shape_errors_mirror_reference():
         selective_gaussian_memory(k, torch.zeros(1, 4, 2, 5, device="cuda"), k,
                                   torch.ones(1, 4, 2, device="cuda"), torch.zeros(1, 4, 2, device="cuda"),
                                   torch.ones(2, 8, device="cuda"), solver="nope")
+
+
+def test_ill_conditioned_evidence_stays_within_the_float32_bound():
+    # The block LDL^T factors without pivoting (every diagonal block of an SPD
+    # matrix's Schur complements is SPD). Keys near an 8-dimensional subspace,
+    # a tiny floor, no decay and beta 1 give evidence with condition numbers
+    # about 2e4 by the last token; a backward-stable float32 solve keeps the
+    # forward error within a small multiple of kappa * 2^-24, and the
+    # backward must stay finite.
+    from mamba4_b200 import selective_memory_fused
+
+    rng = np.random.default_rng(7)
+    B, T, H, D, P = 1, 256, 2, 64, 64
+    basis = np.linalg.qr(rng.normal(size=(D, 8)))[0]
+    k = rng.normal(size=(B, T, H, 8)) @ basis.T + 1e-2 * rng.normal(size=(B, T, H, D))
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    q = rng.normal(size=(B, T, H, D))
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    v = rng.normal(size=(B, T, H, P))
+    beta, log_decay = np.ones((B, T, H)), np.zeros((B, T, H))
+    floor = np.full((H, D), 1e-3)
+    k, q, v, beta, log_decay, floor = (a.astype(np.float32) for a in (k, q, v, beta, log_decay, floor))
+    kappa = max(np.linalg.cond(np.einsum("td,te->de", k[0, :, h].astype(np.float64), k[0, :, h].astype(np.float64))
+                               + np.diag(floor[h].astype(np.float64))) for h in range(H))
+    assert kappa > 1e4
+    tol = 20 * kappa * 2.0**-24
+    ref = M.dense_forward(k, v, q, beta, log_decay, floor)
+    dev = torch.device("cuda:0")
+    leaves = [torch.tensor(a, device=dev, requires_grad=True) for a in (k, v, q, beta, log_decay, floor)]
+    res = selective_memory_fused(*leaves)
+    close(res.output, ref["output"], tol, "output")
+    close(res.variance, ref["variance"], tol, "variance")
+    grads = torch.autograd.grad((res.output.square().sum() + res.variance.sum()), leaves)
+    for g in grads:
+        assert torch.isfinite(g).all()
