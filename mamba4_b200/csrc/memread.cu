@@ -309,20 +309,24 @@ __global__ void __launch_bounds__(32, 12) solve_kernel(
       }
 #pragma unroll
       for (int c = 0; c < 8; ++c) kc[c] = ld2f(&sm.k[8 * c + 2 * t]);
+      // Paired FMAs (fma.rn.f32x2): the same roundings as two scalar FMAs.
+      const float2 l2 = make_float2(lam, lam);
 #pragma unroll
       for (int q = 0; q < ldl::NQ; ++q) {
-        float4 e = sm.E[q][lane];
+        const float4 e = sm.E[q][lane];
+        float2 lo, hi;
         if (q < 16) {
           const int R = ldl::slot_R(q), c = ldl::slot_c(q);
-          e = make_float4(fmaf(kr[R][0], kc[c].x, lam * e.x), fmaf(kr[R][0], kc[c].y, lam * e.y),
-                          fmaf(kr[R][1], kc[c].x, lam * e.z), fmaf(kr[R][1], kc[c].y, lam * e.w));
+          lo = ffma2(make_float2(kr[R][0], kr[R][0]), kc[c], fmul2(l2, make_float2(e.x, e.y)));
+          hi = ffma2(make_float2(kr[R][1], kr[R][1]), kc[c], fmul2(l2, make_float2(e.z, e.w)));
         } else {
           const int R0 = 2 * (q - 16), R1 = R0 + 1;
-          e = make_float4(fmaf(kr[R0][1], kc[2 * R0 + 1].x, lam * e.x), fmaf(kr[R0][1], kc[2 * R0 + 1].y, lam * e.y),
-                          fmaf(kr[R1][1], kc[2 * R1 + 1].x, lam * e.z), fmaf(kr[R1][1], kc[2 * R1 + 1].y, lam * e.w));
+          lo = ffma2(make_float2(kr[R0][1], kr[R0][1]), kc[2 * R0 + 1], fmul2(l2, make_float2(e.x, e.y)));
+          hi = ffma2(make_float2(kr[R1][1], kr[R1][1]), kc[2 * R1 + 1], fmul2(l2, make_float2(e.z, e.w)));
         }
-        sm.E[q][lane] = e;
-        ldl::set4(F, q, e);
+        const float4 en = make_float4(lo.x, lo.y, hi.x, hi.y);
+        sm.E[q][lane] = en;
+        ldl::set4(F, q, en);
       }
     }
     // Floor on the diagonal: entries (16R + g, 16R + g) of tile (R, 2R) and
